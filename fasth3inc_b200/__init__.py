@@ -1,0 +1,214 @@
+"""fasth3inc_b200 -- B200-native Q4_K dequantise-and-multiply for fh3.
+
+Host-side mirror of the reference's matmul interface (include/fh3/fh3.h:82-109):
+
+    row_bytes(type, n)                     fh3_row_bytes   (src/core/fh3_quant.c:14-34)
+    dequant(type, src, n, rows)            fh3_dequant     (src/core/fh3_quant.c:284-318)
+    matmul(w, x, bias)                     fh3_matmul      (src/core/fh3_ops.c:317-404)
+    matmul_host(w, x, bias)                fh3_matmul on host buffers through the C drop-in
+
+Every call goes through libfh3cuda.so (the C ABI in include/fh3cuda.h) on
+device memory owned by torch tensors; torch is only the allocator and stream
+provider here.  There is no CPU path: without the CUDA library or a GPU these
+functions raise.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import (EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, F32, Q4_K, Fh3CudaError, Fh3CudaW,
+                   check, load)
+
+__all__ = [
+    "Q4_K", "F32", "EPI_F32", "EPI_BF16", "EPI_SWIGLU", "EPI_RESID", "Fh3CudaError", "Q4KWeight",
+    "init", "row_bytes", "dequant", "matmul", "gemv", "gemm", "matmul_host", "rmsnorm_modulate",
+    "to_bf16", "swiglu", "make_weights", "device_status",
+]
+
+_inited: set[int] = set()
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def init(device: int = 0) -> None:
+    """Set up libfh3cuda on `device` (fh3cuda_init)."""
+    torch = _torch()
+    torch.cuda.set_device(device)
+    L = load()
+    check(L.fh3cuda_init(device))
+    _inited.add(device)
+
+
+def _ensure(t) -> None:
+    dev = t.device.index if t.device.index is not None else _torch().cuda.current_device()
+    if dev not in _inited:
+        init(dev)
+
+
+def _stream(stream=None) -> int:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def row_bytes(type_: int, n: int) -> int:
+    """Bytes of one row of `n` weights (fh3_row_bytes)."""
+    return int(load().fh3cuda_row_bytes(type_, n))
+
+
+@dataclass
+class Q4KWeight:
+    """A Q4_K weight matrix resident in HBM: `out` rows of `in_` weights (Fh3W)."""
+    data: object  # torch.uint8 tensor on the device, out * row_bytes(Q4_K, in_) bytes
+    in_: int
+    out: int
+
+    @property
+    def desc(self) -> Fh3CudaW:
+        return Fh3CudaW(Q4_K, self.in_, self.out, self.data.data_ptr())
+
+    @property
+    def nbytes(self) -> int:
+        return self.out * row_bytes(Q4_K, self.in_)
+
+    @classmethod
+    def from_bytes(cls, raw: np.ndarray, in_: int, out: int, device: int | str = "cuda") -> "Q4KWeight":
+        torch = _torch()
+        raw = np.ascontiguousarray(raw, dtype=np.uint8)
+        if raw.size != out * row_bytes(Q4_K, in_):
+            raise ValueError("byte count does not match out * row_bytes(Q4_K, in)")
+        return cls(torch.from_numpy(raw).to(device), in_, out)
+
+
+def dequant(type_: int, src, n: int, rows: int = 1, out=None, stream=None):
+    """Dequantise `rows` rows of `n` weights to fp32 (fh3_dequant, bit-exact)."""
+    torch = _torch()
+    _ensure(src)
+    if out is None:
+        out = torch.zeros((rows, n), dtype=torch.float32, device=src.device)
+    check(load().fh3cuda_dequant_dev(type_, _ptr(src), _ptr(out), rows, n, _stream(stream)))
+    return out
+
+
+def matmul(w: Q4KWeight, x, bias=None, out=None, stream=None):
+    """y = x . W^T (+ bias) on device tensors (fh3_matmul semantics)."""
+    torch = _torch()
+    _ensure(x)
+    x = x.contiguous()
+    n_tok = x.shape[0]
+    if out is None:
+        out = torch.empty((n_tok, w.out), dtype=torch.float32, device=x.device)
+    d = w.desc
+    check(load().fh3cuda_matmul_dev(ctypes.byref(d), _ptr(x), _ptr(out), n_tok, _ptr(bias), _stream(stream)))
+    return out
+
+
+def gemv(w: Q4KWeight, x, bias=None, out=None, stream=None):
+    """The fp32 CUDA-core GEMV (1..16 tokens)."""
+    torch = _torch()
+    _ensure(x)
+    n_tok = x.shape[0]
+    if out is None:
+        out = torch.empty((n_tok, w.out), dtype=torch.float32, device=x.device)
+    d = w.desc
+    check(load().fh3cuda_gemv_q4k_dev(ctypes.byref(d), _ptr(x), _ptr(out), n_tok, _ptr(bias), _stream(stream)))
+    return out
+
+
+def gemm(w: Q4KWeight, x_bf16, epi: int = EPI_F32, bias=None, gate=None, out=None, stream=None):
+    """The tcgen05 GEMM on bf16 activations with the chosen epilogue."""
+    torch = _torch()
+    _ensure(x_bf16)
+    n_tok = x_bf16.shape[0]
+    n_out = w.out // 2 if epi == EPI_SWIGLU else w.out
+    if out is None:
+        dt = torch.bfloat16 if epi in (EPI_BF16, EPI_SWIGLU) else torch.float32
+        out = torch.empty((n_tok, n_out), dtype=dt, device=x_bf16.device)
+    if x_bf16.stride(-1) != 1:
+        raise ValueError("x_bf16 rows must be contiguous")
+    d = w.desc
+    check(load().fh3cuda_gemm_q4k_dev(ctypes.byref(d), _ptr(x_bf16), x_bf16.stride(0), _ptr(out),
+                                      out.stride(0), n_tok, _ptr(bias), _ptr(gate), epi, _stream(stream)))
+    return out
+
+
+def to_bf16(x, out=None, stream=None):
+    torch = _torch()
+    _ensure(x)
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    check(load().fh3cuda_f32_to_bf16_dev(_ptr(x), _ptr(out), x.numel(), _stream(stream)))
+    return out
+
+
+def rmsnorm_modulate(x, shift, scale, norm_w=None, eps: float = 1e-6, out=None, stream=None):
+    """bf16(modulate(rmsnorm(x))) per row (fh3_rmsnorm + fh3_modulate, fused)."""
+    torch = _torch()
+    _ensure(x)
+    n, dim = x.shape
+    if out is None:
+        out = torch.empty((n, dim), dtype=torch.bfloat16, device=x.device)
+    check(load().fh3cuda_rmsnorm_modulate_dev(_ptr(x), _ptr(norm_w), _ptr(shift), _ptr(scale), _ptr(out),
+                                              n, dim, eps, _stream(stream)))
+    return out
+
+
+def swiglu(h, out=None, stream=None):
+    """fh3_swiglu on a [n, 2F] fp32 device tensor (value-first halves)."""
+    torch = _torch()
+    _ensure(h)
+    n, two_f = h.shape
+    if out is None:
+        out = torch.empty((n, two_f // 2), dtype=torch.float32, device=h.device)
+    check(load().fh3cuda_swiglu_dev(_ptr(h), _ptr(out), n, two_f // 2, _stream(stream)))
+    return out
+
+
+def make_weights(rows: int, n: int, seed: int, stream_id: int, scale: float = 0.02, device="cuda",
+                 stream=None) -> Q4KWeight:
+    """Seeded synthetic Q4_K weights generated in HBM (benchmark inputs)."""
+    torch = _torch()
+    data = torch.empty(rows * row_bytes(Q4_K, n), dtype=torch.uint8, device=device)
+    _ensure(data)
+    check(load().fh3cuda_make_q4k_weights_dev(seed, stream_id, scale, rows, n, _ptr(data), _stream(stream)))
+    return Q4KWeight(data, n, rows)
+
+
+def device_status(stream=None) -> int:
+    """Synchronise and read the device status word (FH3_OK or FH3CUDA_E_TIMEOUT)."""
+    return int(load().fh3cuda_device_status(_stream(stream)))
+
+
+def matmul_host(w_raw: np.ndarray, in_: int, out: int, x: np.ndarray, bias: np.ndarray | None = None,
+                y: np.ndarray | None = None) -> np.ndarray:
+    """fh3_matmul on HOST buffers through the C drop-in (fh3cuda_matmul).
+
+    Raises Fh3CudaError with the drop-in's recorded status on failure.
+    """
+    L = load()
+    if not _inited:
+        init(_torch().cuda.current_device())
+    w_raw = np.ascontiguousarray(w_raw, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n_tok = x.shape[0] if x.ndim == 2 else 1
+    if y is None:
+        y = np.empty((n_tok, out), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    d = Fh3CudaW(Q4_K, in_, out, w_raw.ctypes.data)
+    L.fh3cuda_matmul(ctypes.byref(d), x.ctypes.data, y.ctypes.data, n_tok,
+                     None if b is None else b.ctypes.data)
+    rc = L.fh3cuda_take_status()
+    if rc != 0:
+        raise Fh3CudaError(rc, _lib.last_error())
+    return y

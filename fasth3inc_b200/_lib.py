@@ -1,0 +1,105 @@
+"""ctypes binding of libfh3cuda (include/fh3cuda.h).
+
+Loads the in-tree fasth3inc_b200/libfh3cuda.so.  There is no fallback: if the
+library is missing or fails to load, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import build as _build
+
+Q4_K = 12
+F32 = 0
+
+FH3_OK = 0
+FH3_ERR = -1
+FH3_E_NOMEM = -7
+FH3_E_INVALID = -8
+FH3CUDA_E_CUDA = -20
+FH3CUDA_E_TIMEOUT = -21
+FH3CUDA_E_NODEV = -22
+
+EPI_F32, EPI_BF16, EPI_SWIGLU, EPI_RESID = 0, 1, 2, 3
+
+EXPORTED = [
+    "fh3cuda_init", "fh3cuda_last_error", "fh3cuda_take_status", "fh3cuda_device_status",
+    "fh3cuda_sm_count", "fh3cuda_row_bytes", "fh3cuda_dequant_dev", "fh3cuda_matmul_dev",
+    "fh3cuda_matmul", "__wrap_fh3_matmul", "fh3cuda_register_weights", "fh3cuda_unregister_weights",
+    "fh3cuda_upload_weights", "fh3cuda_release_weights", "fh3cuda_gemv_q4k_dev",
+    "fh3cuda_gemm_q4k_dev", "fh3cuda_f32_to_bf16_dev", "fh3cuda_rmsnorm_modulate_dev",
+    "fh3cuda_swiglu_dev", "fh3cuda_make_q4k_weights_dev",
+]
+
+
+class Fh3CudaW(ctypes.Structure):
+    """Same layout as fh3's Fh3W (include/fh3/fh3.h:82-87)."""
+    _fields_ = [("type", ctypes.c_int), ("in_", ctypes.c_int64), ("out", ctypes.c_int64),
+                ("data", ctypes.c_void_p)]
+
+
+class Fh3CudaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{msg} (status {code})")
+        self.code = code
+
+
+_lib = None
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def load(build_if_missing: bool = True) -> ctypes.CDLL:
+    """Load libfh3cuda.so (compiling it first if it is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = _build.LIB
+    if not os.path.exists(path):
+        if not build_if_missing:
+            raise FileNotFoundError(f"{path} not built; run python -m fasth3inc_b200.build")
+        _build.build()
+    L = ctypes.CDLL(path)
+    vp, i64, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    Wp = ctypes.POINTER(Fh3CudaW)
+    sig = {
+        "fh3cuda_init": (c_int, [c_int]),
+        "fh3cuda_last_error": (ctypes.c_char_p, []),
+        "fh3cuda_take_status": (c_int, []),
+        "fh3cuda_device_status": (c_int, [vp]),
+        "fh3cuda_sm_count": (c_int, []),
+        "fh3cuda_row_bytes": (ctypes.c_size_t, [c_int, i64]),
+        "fh3cuda_dequant_dev": (c_int, [c_int, vp, vp, i64, i64, vp]),
+        "fh3cuda_matmul_dev": (c_int, [Wp, vp, vp, c_int, vp, vp]),
+        "fh3cuda_matmul": (None, [Wp, vp, vp, c_int, vp]),
+        "__wrap_fh3_matmul": (None, [Wp, vp, vp, c_int, vp]),
+        "fh3cuda_register_weights": (c_int, [vp, ctypes.c_size_t, vp]),
+        "fh3cuda_unregister_weights": (c_int, [vp]),
+        "fh3cuda_upload_weights": (c_int, [vp, ctypes.c_size_t, ctypes.POINTER(vp)]),
+        "fh3cuda_release_weights": (c_int, [vp]),
+        "fh3cuda_gemv_q4k_dev": (c_int, [Wp, vp, vp, c_int, vp, vp]),
+        "fh3cuda_gemm_q4k_dev": (c_int, [Wp, vp, i64, vp, i64, i64, vp, vp, c_int, vp]),
+        "fh3cuda_f32_to_bf16_dev": (c_int, [vp, vp, i64, vp]),
+        "fh3cuda_rmsnorm_modulate_dev": (c_int, [vp, vp, vp, vp, vp, c_int, c_int, ctypes.c_float, vp]),
+        "fh3cuda_swiglu_dev": (c_int, [vp, vp, c_int, c_int, vp]),
+        "fh3cuda_make_q4k_weights_dev": (c_int, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, i64, i64,
+                                                 vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    return load().fh3cuda_last_error().decode(errors="replace")
+
+
+def check(rc: int) -> None:
+    if rc != FH3_OK:
+        raise Fh3CudaError(rc, last_error())

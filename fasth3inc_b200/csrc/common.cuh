@@ -1,0 +1,256 @@
+// common.cuh -- shared device helpers of libfh3cuda (sm_100a only).
+//
+// Q4_K format helpers, bounded mbarrier waits, TMA and tcgen05 wrappers in
+// inline PTX.  Every spin-wait here has a time limit: on expiry it records
+// FH3CUDA_E_TIMEOUT in the caller's device status word and returns false, so
+// a kernel never hangs its GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/fh3cuda.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libfh3cuda targets sm_100a only"
+#endif
+
+namespace fh3 {
+
+constexpr int kQ4KBlock = 256;  // weights per super-block
+constexpr int kQ4KBytes = 144;  // bytes per super-block
+
+// ---------------------------------------------------------------------------
+// Q4_K super-block: bytes 0-1 d (fp16), 2-3 dmin (fp16), 4-15 packed 6-bit
+// scales/mins of the eight 32-weight sub-blocks, 16-143 nibbles.  32-byte
+// chunk c of the nibbles holds sub-block 2c in its low nibbles and 2c+1 in its
+// high nibbles (src/core/fh3_quant.c:154-196).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, int& sc, int& m) {
+    if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+// Same unpacking from the 12 scale bytes held in three 32-bit words
+// (w0 = bytes 4-7, w1 = bytes 8-11, w2 = bytes 12-15 of the block).
+__device__ __forceinline__ void q4k_scale_min_words(uint32_t w0, uint32_t w1, uint32_t w2, int j,
+                                                    int& sc, int& m) {
+    if (j < 4) {
+        sc = (w0 >> (8 * j)) & 63;
+        m = (w1 >> (8 * j)) & 63;
+    } else {
+        const int jj = j - 4;
+        const uint32_t b8 = (w2 >> (8 * jj)) & 0xFF;       // byte j+4
+        sc = (b8 & 0x0F) | (((w0 >> (8 * jj + 6)) & 3) << 4);
+        m = (b8 >> 4) | (((w1 >> (8 * jj + 6)) & 3) << 4);
+    }
+}
+
+__device__ __forceinline__ float h2f_bits(uint32_t h) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFF)));
+}
+
+// Four nibbles (bytes of `v`, each 0x80|q) -> floats 1 + q/128, exact.
+// byte_perm picks {0x00, 0x00, 0x80|q, 0x3F}: the fp32 pattern 0x3F80_0000 | q<<16.
+__device__ __forceinline__ float nib_f(uint32_t v, uint32_t sel) {
+    return __uint_as_float(__byte_perm(v, 0x3F000000u, sel));
+}
+constexpr uint32_t kSel0 = 0x7044, kSel1 = 0x7144, kSel2 = 0x7244, kSel3 = 0x7344;
+
+// ---------------------------------------------------------------------------
+// timing / status
+// ---------------------------------------------------------------------------
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far above any legitimate wait
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void record_status(int* status, int code) {
+    if (status) atomicCAS(status, 0, code);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+            smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete.  Gives up when `abort` (a
+// shared flag other roles raise on their own timeout) is set, or after
+// kWaitLimitNs; then records FH3CUDA_E_TIMEOUT and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          int* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63) == 0) {
+            if (*abort) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                *abort = 1;
+                record_status(status, FH3CUDA_E_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// TMA (no multicast anywhere in this library)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                            int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// generic-proxy smem writes -> visible to the async proxy (tcgen05.mma reads)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (cta_group::1)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (bf16 here), one thread.
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive (once) on `bar` when all tcgen05.mma issued so far by this thread finish.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns (one row per thread).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
+// layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 B (64 bf16),
+// 8-row atoms of 1024 B (stride-byte-offset), version 1, layout 2 (SW128).
+// The tile base must be 1024-byte aligned; a K offset inside the 128-byte row
+// is applied by adding bytes>>4 to the start-address field.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
+    d |= static_cast<uint64_t>(1) << 16;           // leading-byte-offset (unused for SW128 K-major)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;   // stride-byte-offset: 8 rows x 128 B
+    d |= static_cast<uint64_t>(1) << 46;           // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(2) << 61;           // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: kind::f16 with bf16 A and B, fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+    return (1u << 4)                                  // D format: f32
+           | (1u << 7)                                // A format: bf16
+           | (1u << 10)                               // B format: bf16
+           | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+           | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+}  // namespace fh3
+
+// Host-side helpers shared by the translation units (defined in api.cu).
+namespace fh3host {
+struct DevCtx;
+DevCtx* ctx();                       // context of the current device (nullptr if not initialised)
+int* ctx_status(DevCtx* c);          // device status word
+int ctx_sms(DevCtx* c);
+int set_error(int code, const char* fmt, ...);
+int check_cuda(cudaError_t e, const char* what);
+// cuTensorMapEncodeTiled through the runtime's driver entry point
+CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* gaddr,
+                      const cuuint64_t* gdim, const cuuint64_t* gstride, const cuuint32_t* box,
+                      const cuuint32_t* estride, CUtensorMapSwizzle swz);
+// scratch of at least `bytes` for slot `slot` (cached, grows)
+void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
+}  // namespace fh3host

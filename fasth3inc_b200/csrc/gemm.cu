@@ -1,0 +1,489 @@
+// gemm.cu -- large-M Q4_K GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Replaces fh3_matmul's large-M regime (src/core/fh3_ops.c:317-404: per 64-row
+// tile, dequantise to fp32 scratch, then AVX2 dots against every token).
+//
+//   y[m][n] = epi( sum_k A[m][k] * W[n][k] ),  A = activations (bf16, M x K),
+//   W = Q4_K rows (N x K), fp32 accumulation in tensor memory.
+//
+// One persistent CTA per SM walks 128 x 256 output tiles (grouped raster so
+// that concurrently running CTAs share weight tiles in L2).  Warp roles:
+//   warp 0      TMA producer: A tiles (128 x 64 bf16, 128-byte swizzle) and raw
+//               Q4_K tiles (256 rows x one 144-byte super-block = K 256).
+//   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma 128x256x16 per
+//               K-64 stage into one of two 256-column fp32 accumulators.
+//   warps 2-5   epilogue: tcgen05.ld accumulator rows -> bias / SwiGLU /
+//               gated residual -> global memory.
+//   warps 6-13  dequantisers: raw Q4_K in shared memory -> bf16 B operand
+//               in the UMMA K-major 128-byte-swizzle layout, one weight row
+//               per thread, fp32 FMA w = (d*sc)*q - dmin*m then one rounding
+//               to bf16 (the fp32 value equals fh3's dequant_q4_k output).
+// Every mbarrier wait is bounded (common.cuh); on a timeout the kernel flags
+// FH3CUDA_E_TIMEOUT, drains its own copies/MMAs, frees TMEM and returns.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128;            // tokens per tile (UMMA M)
+constexpr int BN = 256;            // weight rows per tile (UMMA N)
+constexpr int BK = 64;             // K per MMA stage: one 128-byte swizzle row of bf16
+constexpr int SA = 3;              // A stages
+constexpr int SB = 3;              // dequantised B stages
+constexpr int SR = 2;              // raw Q4_K stages
+constexpr int A_BYTES = BM * BK * 2;           // 16384
+constexpr int B_BYTES = BN * BK * 2;           // 32768
+constexpr int R_HALF = 128 * fh3::kQ4KBytes;   // 18432: one TMA box (128 rows x 144 B)
+constexpr int R_BYTES = 2 * R_HALF;            // 36864
+constexpr int kNumEpiWarps = 4;
+constexpr int kNumDqWarps = 8;
+constexpr int kEpiWarp0 = 2;
+constexpr int kDqWarp0 = kEpiWarp0 + kNumEpiWarps;
+constexpr int kThreads = 32 * (kDqWarp0 + kNumDqWarps);  // 448
+constexpr int kTmemCols = 512;                           // two 256-column accumulators
+constexpr int kGroupM = 16;
+
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + SA * A_BYTES;
+constexpr int OFF_R = OFF_B + SB * B_BYTES;
+constexpr int OFF_BAR = OFF_R + SR * R_BYTES;
+// barriers: a_full[SA] a_empty[SA] b_full[SB] b_empty[SB] r_full[SR] r_empty[SR]
+//           acc_full[2] acc_empty[2] drain[1]
+constexpr int kNumBars = 2 * SA + 2 * SB + 2 * SR + 4 + 1;
+constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;  // + tmem slot/abort flag + alignment slack
+
+static_assert(OFF_B % 1024 == 0 && OFF_R % 1024 == 0, "operand stages must be 1024-byte aligned");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+struct Params {
+    int64_t M, N, K;       // N = weight rows; for SwiGLU N = 2F
+    int64_t n_out;         // output columns (N, or F for SwiGLU)
+    int64_t ldy;
+    const float* bias;
+    const float* gate;
+    void* y;
+    int epi;
+    int* status;
+};
+
+struct Ring {
+    int idx = 0;
+    uint32_t phase = 0;
+    template <int S>
+    __device__ __forceinline__ void next() {
+        if (++idx == S) {
+            idx = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
+__device__ __forceinline__ void tile_coords(int64_t tile, int64_t num_m, int64_t num_n, int64_t& mb,
+                                            int64_t& nb) {
+    const int64_t per_group = static_cast<int64_t>(kGroupM) * num_n;
+    const int64_t group = tile / per_group;
+    const int64_t first_m = group * kGroupM;
+    const int64_t gsize = (num_m - first_m) < kGroupM ? (num_m - first_m) : kGroupM;
+    const int64_t in_group = tile - group * per_group;
+    mb = first_m + in_group % gsize;
+    nb = in_group / gsize;
+}
+
+__device__ __forceinline__ float silu_ref(float g) {
+    // fh3_swiglu: g / (1 + expf(-g)), and 0 below -80 (src/core/fh3_ops.c:517-523)
+    return g < -80.0f ? 0.0f : g / (1.0f + expf(-g));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                       const Params p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = a_full + SA;
+    uint64_t* b_full = a_empty + SA;
+    uint64_t* b_empty = b_full + SB;
+    uint64_t* r_full = b_empty + SB;
+    uint64_t* r_empty = r_full + SR;
+    uint64_t* acc_full = r_empty + SR;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const bool swiglu = p.epi == FH3CUDA_EPI_SWIGLU;
+    const int64_t num_m = (p.M + BM - 1) / BM;
+    const int64_t num_n = swiglu ? (p.n_out + 127) / 128 : (p.N + BN - 1) / BN;
+    const int64_t num_tiles = num_m * num_n;
+    const int ksteps = static_cast<int>(p.K / BK);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < SA; ++i) { fh3::mbar_init(&a_full[i], 1); fh3::mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < SB; ++i) { fh3::mbar_init(&b_full[i], kNumDqWarps); fh3::mbar_init(&b_empty[i], 1); }
+        for (int i = 0; i < SR; ++i) { fh3::mbar_init(&r_full[i], 1); fh3::mbar_init(&r_empty[i], kNumDqWarps); }
+        for (int i = 0; i < 2; ++i) { fh3::mbar_init(&acc_full[i], 1); fh3::mbar_init(&acc_empty[i], kNumEpiWarps); }
+        fh3::mbar_init(drain, 1);
+        *abort_flag = 0;
+        fh3::fence_mbar_init();
+    }
+    if (warp == 1) {
+        fh3::tmem_alloc(tmem_slot, kTmemCols);
+        fh3::tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        fh3::tma_prefetch_desc(&tmA);
+        fh3::tma_prefetch_desc(&tmW);
+    }
+    fh3::tc_fence_before();
+    __syncthreads();
+    fh3::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            Ring ra, rr;
+            uint32_t a_filled = 0, r_filled = 0;  // bit i: stage i has been filled at least once
+            uint32_t a_par = 0, r_par = 0;        // parity of the last fill of each stage
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                int64_t mb, nb;
+                tile_coords(tile, num_m, num_n, mb, nb);
+                const int m0 = static_cast<int>(mb * BM);
+                int row0, row1;
+                if (swiglu) {
+                    row0 = static_cast<int>(nb * 128);
+                    row1 = static_cast<int>(p.n_out + nb * 128);
+                } else {
+                    row0 = static_cast<int>(nb * BN);
+                    row1 = row0 + 128;
+                }
+                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                    if ((ks & 3) == 0) {
+                        if (!(ok = fh3::mbar_wait(&r_empty[rr.idx], rr.phase ^ 1u, abort_flag, p.status))) break;
+                        uint8_t* dst = smem + OFF_R + rr.idx * R_BYTES;
+                        fh3::mbar_arrive_expect_tx(&r_full[rr.idx], R_BYTES);
+                        const int xb = (ks >> 2) * fh3::kQ4KBytes;
+                        fh3::tma_load_2d(dst, &tmW, &r_full[rr.idx], xb, row0);
+                        fh3::tma_load_2d(dst + R_HALF, &tmW, &r_full[rr.idx], xb, row1);
+                        r_filled |= 1u << rr.idx;
+                        r_par = (r_par & ~(1u << rr.idx)) | (rr.phase << rr.idx);
+                        rr.next<SR>();
+                    }
+                    if (!(ok = fh3::mbar_wait(&a_empty[ra.idx], ra.phase ^ 1u, abort_flag, p.status))) break;
+                    fh3::mbar_arrive_expect_tx(&a_full[ra.idx], A_BYTES);
+                    fh3::tma_load_2d(smem + OFF_A + ra.idx * A_BYTES, &tmA, &a_full[ra.idx], ks * BK, m0);
+                    a_filled |= 1u << ra.idx;
+                    a_par = (a_par & ~(1u << ra.idx)) | (ra.phase << ra.idx);
+                    ra.next<SA>();
+                }
+            }
+            if (!ok) {
+                // drain: wait (bounded, ignoring the abort flag) for our own copies in flight
+                volatile int no_abort = 0;
+                for (int i = 0; i < SA; ++i)
+                    if (a_filled & (1u << i)) fh3::mbar_wait(&a_full[i], (a_par >> i) & 1u, &no_abort, nullptr);
+                for (int i = 0; i < SR; ++i)
+                    if (r_filled & (1u << i)) fh3::mbar_wait(&r_full[i], (r_par >> i) & 1u, &no_abort, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = fh3::idesc_bf16_f32(BM, BN);
+            Ring ra, rb, racc;
+            bool ok = true;
+            bool issued = false;
+            for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                if (!(ok = fh3::mbar_wait(&acc_empty[racc.idx], racc.phase ^ 1u, abort_flag, p.status))) break;
+                fh3::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(racc.idx * BN);
+                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                    if (!(ok = fh3::mbar_wait(&a_full[ra.idx], ra.phase, abort_flag, p.status))) break;
+                    if (!(ok = fh3::mbar_wait(&b_full[rb.idx], rb.phase, abort_flag, p.status))) break;
+                    fh3::tc_fence_after();
+                    const uint64_t ad = fh3::sdesc_sw128(fh3::smem_u32(smem + OFF_A + ra.idx * A_BYTES));
+                    const uint64_t bd = fh3::sdesc_sw128(fh3::smem_u32(smem + OFF_B + rb.idx * B_BYTES));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        // +32 bytes of K per step inside the 128-byte swizzle row
+                        fh3::umma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0 ? 1u : 0u);
+                    }
+                    issued = true;
+                    fh3::umma_commit(&a_empty[ra.idx]);
+                    fh3::umma_commit(&b_empty[rb.idx]);
+                    ra.next<SA>();
+                    rb.next<SB>();
+                }
+                if (ok) fh3::umma_commit(&acc_full[racc.idx]);
+                racc.next<2>();
+            }
+            if (issued) {
+                // all MMAs retired before TMEM is released
+                fh3::umma_commit(drain);
+                volatile int no_abort = 0;
+                fh3::mbar_wait(drain, 0, &no_abort, nullptr);
+            }
+        }
+    } else if (warp < kDqWarp0) {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int row_in_tile = q * 32 + lane;
+        Ring racc;
+        for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            int64_t mb, nb;
+            tile_coords(tile, num_m, num_n, mb, nb);
+            if (!fh3::mbar_wait(&acc_full[racc.idx], racc.phase, abort_flag, p.status)) break;
+            fh3::tc_fence_after();
+            const int64_t m = mb * BM + row_in_tile;
+            const bool row_ok = m < p.M;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(racc.idx * BN);
+            if (swiglu) {
+                for (int cc = 0; cc < 4; ++cc) {
+                    uint32_t v[32], g[32];
+                    fh3::tmem_ld32(tbase + cc * 32, v);
+                    fh3::tmem_ld32(tbase + 128 + cc * 32, g);
+                    fh3::tmem_ld_wait();
+                    const int64_t f0 = nb * 128 + cc * 32;
+                    if (!row_ok) continue;
+                    __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy;
+                    float o[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float vv = __uint_as_float(v[j]), gg = __uint_as_float(g[j]);
+                        if (p.bias) {
+                            const int64_t fj = f0 + j < p.n_out ? f0 + j : p.n_out - 1;
+                            vv += p.bias[fj];
+                            gg += p.bias[p.n_out + fj];
+                        }
+                        o[j] = vv * silu_ref(gg);
+                    }
+                    if (f0 + 32 <= p.n_out && (p.ldy & 7) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            uint4 pk;
+                            __nv_bfloat162 b0 = __floats2bfloat162_rn(o[j], o[j + 1]);
+                            __nv_bfloat162 b1 = __floats2bfloat162_rn(o[j + 2], o[j + 3]);
+                            __nv_bfloat162 b2 = __floats2bfloat162_rn(o[j + 4], o[j + 5]);
+                            __nv_bfloat162 b3 = __floats2bfloat162_rn(o[j + 6], o[j + 7]);
+                            pk.x = *reinterpret_cast<uint32_t*>(&b0);
+                            pk.y = *reinterpret_cast<uint32_t*>(&b1);
+                            pk.z = *reinterpret_cast<uint32_t*>(&b2);
+                            pk.w = *reinterpret_cast<uint32_t*>(&b3);
+                            *reinterpret_cast<uint4*>(yr + f0 + j) = pk;
+                        }
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (f0 + j < p.n_out) yr[f0 + j] = __float2bfloat16_rn(o[j]);
+                    }
+                }
+            } else {
+                for (int cc = 0; cc < BN / 32; ++cc) {
+                    uint32_t v[32];
+                    fh3::tmem_ld32(tbase + cc * 32, v);
+                    fh3::tmem_ld_wait();
+                    const int64_t n0 = nb * BN + cc * 32;
+                    if (!row_ok || n0 >= p.N) continue;
+                    float o[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        o[j] = __uint_as_float(v[j]);
+                        if (p.bias) o[j] += p.bias[n0 + j < p.N ? n0 + j : p.N - 1];
+                    }
+                    const bool full = n0 + 32 <= p.N;
+                    if (p.epi == FH3CUDA_EPI_BF16) {
+                        __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n0;
+                        if (full && (p.ldy & 7) == 0) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 8) {
+                                uint4 pk;
+                                __nv_bfloat162 b0 = __floats2bfloat162_rn(o[j], o[j + 1]);
+                                __nv_bfloat162 b1 = __floats2bfloat162_rn(o[j + 2], o[j + 3]);
+                                __nv_bfloat162 b2 = __floats2bfloat162_rn(o[j + 4], o[j + 5]);
+                                __nv_bfloat162 b3 = __floats2bfloat162_rn(o[j + 6], o[j + 7]);
+                                pk.x = *reinterpret_cast<uint32_t*>(&b0);
+                                pk.y = *reinterpret_cast<uint32_t*>(&b1);
+                                pk.z = *reinterpret_cast<uint32_t*>(&b2);
+                                pk.w = *reinterpret_cast<uint32_t*>(&b3);
+                                *reinterpret_cast<uint4*>(yr + j) = pk;
+                            }
+                        } else {
+                            for (int j = 0; j < 32; ++j)
+                                if (n0 + j < p.N) yr[j] = __float2bfloat16_rn(o[j]);
+                        }
+                    } else {
+                        float* yr = static_cast<float*>(p.y) + m * p.ldy + n0;
+                        if (p.epi == FH3CUDA_EPI_RESID) {
+                            for (int j = 0; j < 32; ++j)
+                                if (n0 + j < p.N) yr[j] = fmaf(p.gate[n0 + j], o[j], yr[j]);
+                        } else if (full && (p.ldy & 3) == 0) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(yr + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+                        } else {
+                            for (int j = 0; j < 32; ++j)
+                                if (n0 + j < p.N) yr[j] = o[j];
+                        }
+                    }
+                }
+            }
+            fh3::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) fh3::mbar_arrive(&acc_empty[racc.idx]);
+            racc.next<2>();
+        }
+    } else {
+        // ------------------------------------------------------------ dequantisers
+        const int i = threadIdx.x - kDqWarp0 * 32;  // weight row of the tile (0..255)
+        const uint32_t swz = static_cast<uint32_t>(i & 7);
+        Ring rr, rb;
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            for (int rs = 0; rs < ksteps / 4 && ok; ++rs) {
+                if (!(ok = fh3::mbar_wait(&r_full[rr.idx], rr.phase, abort_flag, p.status))) break;
+                const uint8_t* raw = smem + OFF_R + rr.idx * R_BYTES + i * fh3::kQ4KBytes;
+                const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
+                const float d = fh3::h2f_bits(hdr.x), dmin = fh3::h2f_bits(hdr.x >> 16);
+                for (int sub = 0; sub < 4 && ok; ++sub) {
+                    // sub-blocks 2*sub (low nibbles) and 2*sub+1 (high nibbles)
+                    float s[2], nm[2];
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        int sc, m;
+                        fh3::q4k_scale_min_words(hdr.y, hdr.z, hdr.w, 2 * sub + hh, sc, m);
+                        s[hh] = __fmul_rn(d, static_cast<float>(sc)) * 128.0f;
+                        nm[hh] = -__fmul_rn(dmin, static_cast<float>(m));
+                    }
+                    const uint4 q0 = *reinterpret_cast<const uint4*>(raw + 16 + sub * 32);
+                    const uint4 q1 = *reinterpret_cast<const uint4*>(raw + 32 + sub * 32);
+                    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                    if (!(ok = fh3::mbar_wait(&b_empty[rb.idx], rb.phase ^ 1u, abort_flag, p.status))) break;
+                    uint8_t* brow = smem + OFF_B + rb.idx * B_BYTES + i * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int hh = j >> 2;                 // 0: low nibbles, 1: high
+                        const uint32_t wa = qw[2 * (j & 3)], wb = qw[2 * (j & 3) + 1];
+                        const uint32_t va = ((hh ? (wa >> 4) : wa) & 0x0F0F0F0Fu) | 0x80808080u;
+                        const uint32_t vb = ((hh ? (wb >> 4) : wb) & 0x0F0F0F0Fu) | 0x80808080u;
+                        const float sj = s[hh], nj = nm[hh];
+                        float w[8];
+                        w[0] = fmaf(sj, fh3::nib_f(va, fh3::kSel0) - 1.0f, nj);
+                        w[1] = fmaf(sj, fh3::nib_f(va, fh3::kSel1) - 1.0f, nj);
+                        w[2] = fmaf(sj, fh3::nib_f(va, fh3::kSel2) - 1.0f, nj);
+                        w[3] = fmaf(sj, fh3::nib_f(va, fh3::kSel3) - 1.0f, nj);
+                        w[4] = fmaf(sj, fh3::nib_f(vb, fh3::kSel0) - 1.0f, nj);
+                        w[5] = fmaf(sj, fh3::nib_f(vb, fh3::kSel1) - 1.0f, nj);
+                        w[6] = fmaf(sj, fh3::nib_f(vb, fh3::kSel2) - 1.0f, nj);
+                        w[7] = fmaf(sj, fh3::nib_f(vb, fh3::kSel3) - 1.0f, nj);
+                        __nv_bfloat162 p0 = __floats2bfloat162_rn(w[0], w[1]);
+                        __nv_bfloat162 p1 = __floats2bfloat162_rn(w[2], w[3]);
+                        __nv_bfloat162 p2 = __floats2bfloat162_rn(w[4], w[5]);
+                        __nv_bfloat162 p3 = __floats2bfloat162_rn(w[6], w[7]);
+                        uint4 pk;
+                        pk.x = *reinterpret_cast<uint32_t*>(&p0);
+                        pk.y = *reinterpret_cast<uint32_t*>(&p1);
+                        pk.z = *reinterpret_cast<uint32_t*>(&p2);
+                        pk.w = *reinterpret_cast<uint32_t*>(&p3);
+                        // 16-byte chunk j of this 128-byte row, XOR-swizzled by row % 8
+                        *reinterpret_cast<uint4*>(brow + ((static_cast<uint32_t>(j) ^ swz) << 4)) = pk;
+                    }
+                    fh3::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) fh3::mbar_arrive(&b_full[rb.idx]);
+                    rb.next<SB>();
+                }
+                __syncwarp();
+                if (ok && lane == 0) fh3::mbar_arrive(&r_empty[rr.idx]);
+                rr.next<SR>();
+            }
+        }
+    }
+
+    fh3::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fh3::tc_fence_after();
+        fh3::tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+std::once_flag g_attr_once;
+cudaError_t g_attr_err = cudaSuccess;
+
+}  // namespace
+
+extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y,
+                                    int64_t ldy, int64_t n_tok, const float* bias, const float* gate,
+                                    int epi, void* stream) {
+    using namespace fh3host;
+    DevCtx* c = ctx();
+    if (!c) return set_error(FH3CUDA_E_NODEV, "fh3cuda_gemm_q4k_dev: call fh3cuda_init first");
+    if (!w || !w->data || !x_bf16 || !y || n_tok <= 0 || w->in <= 0 || w->out <= 0)
+        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: bad arguments");
+    if (w->type != FH3CUDA_TYPE_Q4_K || (w->in % fh3::kQ4KBlock) != 0)
+        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: Q4_K weights with in %% 256 == 0 required");
+    if (epi < FH3CUDA_EPI_F32 || epi > FH3CUDA_EPI_RESID)
+        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: unknown epilogue %d", epi);
+    if (epi == FH3CUDA_EPI_RESID && !gate)
+        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: the residual epilogue needs a gate");
+    if (epi == FH3CUDA_EPI_SWIGLU && (w->out % 2) != 0)
+        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: SwiGLU needs an even number of rows");
+    if ((reinterpret_cast<uintptr_t>(w->data) & 15) || (reinterpret_cast<uintptr_t>(x_bf16) & 15))
+        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: weights and x must be 16-byte aligned");
+    if (n_tok > 0x7FFFFFFF || w->out > 0x7FFFFFFF)
+        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: dimensions exceed the TMA coordinate range");
+    const int64_t n_out = epi == FH3CUDA_EPI_SWIGLU ? w->out / 2 : w->out;
+    if (ldy < n_out) return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: ldy < output columns");
+    if (ldx < w->in || (ldx % 8) != 0)
+        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: ldx must be >= K and a multiple of 8");
+
+    std::call_once(g_attr_once, [] {
+        g_attr_err = cudaFuncSetAttribute(gemm_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          SMEM_BYTES);
+    });
+    if (g_attr_err != cudaSuccess) return check_cuda(g_attr_err, "cudaFuncSetAttribute(gemm)");
+
+    const size_t rb = fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, w->in);
+    CUtensorMap tmA, tmW;
+    {
+        const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(w->in), static_cast<cuuint64_t>(n_tok)};
+        const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(ldx) * 2};
+        const cuuint32_t box[2] = {BK, BM};
+        const cuuint32_t es[2] = {1, 1};
+        CUresult r = encode_tiled(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x_bf16), gdim,
+                                  gstr, box, es, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(A) failed: %d", (int)r);
+    }
+    {
+        const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(rb), static_cast<cuuint64_t>(w->out)};
+        const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(rb)};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(fh3::kQ4KBytes), 128};
+        const cuuint32_t es[2] = {1, 1};
+        CUresult r = encode_tiled(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w->data), gdim,
+                                  gstr, box, es, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(W) failed: %d", (int)r);
+    }
+    Params p;
+    p.M = n_tok;
+    p.N = w->out;
+    p.K = w->in;
+    p.n_out = n_out;
+    p.ldy = ldy;
+    p.bias = bias;
+    p.gate = gate;
+    p.y = y;
+    p.epi = epi;
+    p.status = ctx_status(c);
+    const int64_t num_m = (n_tok + BM - 1) / BM;
+    const int64_t num_n = epi == FH3CUDA_EPI_SWIGLU ? (n_out + 127) / 128 : (w->out + BN - 1) / BN;
+    const int64_t tiles = num_m * num_n;
+    const int grid = static_cast<int>(tiles < ctx_sms(c) ? tiles : ctx_sms(c));
+    gemm_q4k_tc_kernel<<<grid, kThreads, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tmA, tmW, p);
+    return check_cuda(cudaGetLastError(), "gemm_q4k_tc_kernel launch");
+}

@@ -1,0 +1,187 @@
+/*
+ * fh3cuda.h -- C ABI of libfh3cuda, the sm_100a (B200) implementation of fh3's
+ * Q4_K dequantise-and-multiply path.
+ *
+ * The reference engine (fh3, C99, CPU only) sends every DiT projection through
+ *     void fh3_matmul(const Fh3W *w, const float *x, float *y, int n_tok,
+ *                     const float *bias_or_null);          (include/fh3/fh3.h:107)
+ * which dequantises Q4_K weight tiles (src/core/fh3_quant.c:154-196) and runs
+ * AVX2/FMA dot products under OpenMP (src/core/fh3_ops.c:317-404).  This
+ * library replaces that function.  Plain pointers and sizes only: no C++ or
+ * torch types cross this boundary.
+ *
+ * Conventions
+ *   - Every entry point except the void drop-in returns an int status:
+ *     FH3_OK (0) or a negative code.  The codes reuse fh3's values
+ *     (include/fh3/fh3.h:218-226) and add three of their own.
+ *   - "_dev" entry points take device pointers and a cudaStream_t passed as
+ *     void* (NULL = the legacy default stream); they are asynchronous.
+ *   - Weights are fh3 rows: row o of a Q4_K matrix with `in` columns starts at
+ *     data + o * fh3cuda_row_bytes(12, in); `in` must be a multiple of 256.
+ *   - Device-side waits inside the kernels are bounded; a wait that gives up
+ *     records FH3CUDA_E_TIMEOUT in the device status word, read by
+ *     fh3cuda_device_status().
+ */
+#ifndef FH3CUDA_H
+#define FH3CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FH3CUDA_API __attribute__((visibility("default")))
+#else
+#define FH3CUDA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (values of include/fh3/fh3.h:218-226, plus three). */
+#define FH3_OK              0
+#define FH3_ERR           (-1)
+#define FH3_E_NOMEM       (-7)
+#define FH3_E_INVALID     (-8)
+#define FH3CUDA_E_CUDA    (-20)  /* a CUDA runtime/driver call failed        */
+#define FH3CUDA_E_TIMEOUT (-21)  /* a bounded device-side wait gave up       */
+#define FH3CUDA_E_NODEV   (-22)  /* no usable sm_100 device / not initialised */
+
+/* Weight types this path accepts (GGML ids, include/fh3/fh3.h:63-79). */
+#define FH3CUDA_TYPE_F32  0
+#define FH3CUDA_TYPE_Q4_K 12
+
+/* Same layout as the reference's weight descriptor Fh3W
+ * (include/fh3/fh3.h:82-87), so a pointer to one may be passed as the other. */
+typedef struct Fh3CudaW {
+    int type;
+    int64_t in;
+    int64_t out;
+    const uint8_t *data;
+} Fh3CudaW;
+
+/* ---- library state --------------------------------------------------- */
+
+/* Select `device` for the calling thread and set up its context (streams,
+ * status word, tensor-map entry point).  Replaces nothing in fh3 (it has no
+ * device); must precede the other calls on that device. */
+FH3CUDA_API int fh3cuda_init(int device);
+
+/* Message of the most recent failure on the calling thread ("" if none). */
+FH3CUDA_API const char *fh3cuda_last_error(void);
+
+/* Sticky status of the void drop-in (fh3cuda_matmul / __wrap_fh3_matmul),
+ * which cannot return one: the first failure since the last call, then
+ * cleared.  fh3_matmul itself returns silently on bad arguments
+ * (src/core/fh3_ops.c:318-321); the drop-in records FH3_E_INVALID instead. */
+FH3CUDA_API int fh3cuda_take_status(void);
+
+/* Synchronise `stream` and read (then clear) the device status word that
+ * bounded device-side waits write.  FH3_OK, FH3CUDA_E_TIMEOUT or
+ * FH3CUDA_E_CUDA. */
+FH3CUDA_API int fh3cuda_device_status(void *stream);
+
+/* Number of SMs of the current device (0 before fh3cuda_init). */
+FH3CUDA_API int fh3cuda_sm_count(void);
+
+/* ---- format ------------------------------------------------------------ */
+
+/* Bytes of one weight row: replaces fh3_row_bytes (include/fh3/fh3.h:103,
+ * src/core/fh3_quant.c:14-34) for F32 and Q4_K; 0 for other types. */
+FH3CUDA_API size_t fh3cuda_row_bytes(int type, int64_t n);
+
+/* Dequantise `rows` Q4_K rows of `n` weights to fp32, bit-exact with
+ * fh3_dequant (include/fh3/fh3.h:104, src/core/fh3_quant.c:154-196,284-318):
+ * dst[r*n + k].  Like the reference, only whole 256-weight blocks are
+ * written; a partial trailing block of a row is left untouched. */
+FH3CUDA_API int fh3cuda_dequant_dev(int type, const void *src, float *dst, int64_t rows, int64_t n,
+                        void *stream);
+
+/* ---- the matmul ------------------------------------------------------------ */
+
+/* y[t][o] = sum_k x[t][k] * W[o][k] (+ bias[o]), all pointers on the device.
+ * Replaces fh3_matmul (include/fh3/fh3.h:107, src/core/fh3_ops.c:317-404) on
+ * device buffers.  n_tok <= 16 runs the fp32 CUDA-core GEMV (relative
+ * Frobenius error <= 1e-5 against fh3_matmul); larger n_tok runs the tcgen05
+ * GEMM on bf16 operands with fp32 accumulation (<= 5e-3).  Internal scratch
+ * (bf16 activations) is cached per device and grows on demand. */
+FH3CUDA_API int fh3cuda_matmul_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
+                       const float *bias_or_null, void *stream);
+
+/* The drop-in: same signature and meaning as fh3_matmul
+ * (include/fh3/fh3.h:107) on HOST buffers.  w->data is looked up in the
+ * registered weight ranges (fh3cuda_register_weights); an unregistered
+ * pointer is staged to the device for this call.  x is copied in, y copied
+ * out; the call returns when y is written.  Failures are recorded for
+ * fh3cuda_take_status() and printed to stderr once. */
+FH3CUDA_API void fh3cuda_matmul(const Fh3CudaW *w, const float *x, float *y, int n_tok,
+                    const float *bias_or_null);
+
+/* Link-time interposer for the unmodified reference objects: link the fh3
+ * application with -Wl,--wrap=fh3_matmul and this library, and every call of
+ * fh3_matmul (src/model/fh3_dit.c:388-461, src/model/fh3_te.c:455-487) lands
+ * here.  Identical to fh3cuda_matmul. */
+FH3CUDA_API void __wrap_fh3_matmul(const Fh3CudaW *w, const float *x, float *y, int n_tok,
+                       const float *bias_or_null);
+
+/* Map the host range [host, host+bytes) to the device range starting at
+ * `dev` for the drop-in's weight lookup.  This stands in for the reference's
+ * trunk ring (src/io/fh3_trunk.c:409-501): weights are uploaded once and
+ * stay resident in HBM. */
+FH3CUDA_API int fh3cuda_register_weights(const void *host, size_t bytes, const void *dev);
+FH3CUDA_API int fh3cuda_unregister_weights(const void *host);
+
+/* cudaMalloc + copy + register in one call; *dev_out receives the device
+ * copy, owned by the library until fh3cuda_release_weights(host). */
+FH3CUDA_API int fh3cuda_upload_weights(const void *host, size_t bytes, void **dev_out);
+FH3CUDA_API int fh3cuda_release_weights(const void *host);
+
+/* ---- explicit kernels (tests, benchmarks, fused trunk) ----------------- */
+
+/* fp32 CUDA-core GEMV, 1 <= n_tok <= 16; same contract as fh3cuda_matmul_dev. */
+FH3CUDA_API int fh3cuda_gemv_q4k_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
+                         const float *bias_or_null, void *stream);
+
+/* Epilogues of the tcgen05 GEMM. */
+#define FH3CUDA_EPI_F32      0  /* y (fp32)  = acc + bias                              */
+#define FH3CUDA_EPI_BF16     1  /* y (bf16)  = acc + bias                              */
+#define FH3CUDA_EPI_SWIGLU   2  /* y (bf16)[t][f] = v * silu(g) of the fused [up;gate]
+                                   weight, value-first halves (src/core/fh3_ops.c:507-527) */
+#define FH3CUDA_EPI_RESID    3  /* y (fp32) += gate[o] * (acc + bias), as fh3_gate_residual
+                                   (src/core/fh3_ops.c:559-585)                         */
+
+/* tcgen05 GEMM on bf16 activations: y = epi(x_bf16 . W^T), x_bf16 holding
+ * n_tok rows of K = w->in values with row stride ldx elements (ldx >= K, a
+ * multiple of 8).  W is Q4_K, dequantised to bf16 in shared memory.  ldy is
+ * the row stride of y in elements.  gate is used by FH3CUDA_EPI_RESID only.
+ * For FH3CUDA_EPI_SWIGLU, W holds 2F rows ([up; gate]) and y has F columns. */
+FH3CUDA_API int fh3cuda_gemm_q4k_dev(const Fh3CudaW *w, const void *x_bf16, int64_t ldx, void *y,
+                                     int64_t ldy, int64_t n_tok, const float *bias_or_null,
+                                     const float *gate, int epilogue, void *stream);
+
+/* fp32 -> bf16 (round to nearest even), n elements. */
+FH3CUDA_API int fh3cuda_f32_to_bf16_dev(const float *x, void *y_bf16, int64_t n, void *stream);
+
+/* Fused GEMM prologue: y_bf16 = bf16(modulate(rmsnorm(x, w, eps), shift, scale))
+ * per row, as fh3_rmsnorm (src/core/fh3_ops.c:410-456) then fh3_modulate
+ * (:529-557) with shift/scale broadcast from [dim] vectors.  norm_w may be
+ * NULL (all ones). */
+FH3CUDA_API int fh3cuda_rmsnorm_modulate_dev(const float *x, const float *norm_w, const float *shift,
+                                 const float *scale, void *y_bf16, int n, int dim, float eps,
+                                 void *stream);
+
+/* fh3_swiglu (src/core/fh3_ops.c:507-527) on device fp32 buffers. */
+FH3CUDA_API int fh3cuda_swiglu_dev(const float *in, float *out, int n, int F, void *stream);
+
+/* Seeded synthetic Q4_K weights on the device: rows x n weights drawn from
+ * scale * N(0,1) (Philox4x32-10 + Box-Muller), quantised with the same
+ * per-block rule as the project's CPU quantiser.  Benchmark input generator;
+ * values need not match the CPU generator bit for bit. */
+FH3CUDA_API int fh3cuda_make_q4k_weights_dev(uint64_t seed, uint64_t stream_id, float scale, int64_t rows,
+                                 int64_t n, void *dst, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FH3CUDA_H */

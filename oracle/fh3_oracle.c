@@ -1,0 +1,413 @@
+/*
+ * fh3_oracle.c -- CPU restatement of fh3's Q4_K dequantise-and-multiply path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity oracle for libfh3cuda: the
+ * pytest suite, __graft_entry__.smoke() and bench.py's cpu_baseline leg may load
+ * it, as the checker.  The product path (libfh3cuda, fasth3inc_b200) never links,
+ * loads or calls it, and there is no CPU fallback to it.
+ *
+ * Each function restates one reference function in plain C99 and names the
+ * reference file:line it follows (paths are relative to the fh3 project root).
+ * Parity is pinned two ways (tests/test_oracle.py):
+ *   - against the reference's own golden vectors (tests/fixtures/quant/Q4_K.bin,
+ *     tests/fixtures/quant/matmul_ref.bin, copied into tests/golden/), and
+ *   - bit-for-bit against the reference functions themselves, compiled from the
+ *     reference sources into oracle/_ref/ by oracle/Makefile (when present).
+ *
+ * The Q4_K quantiser at the bottom has no counterpart in fh3 (fh3 only
+ * dequantises; gguf-py 0.19.0 raises NotImplementedError for Q4_K quantise).
+ * It is this project's input generator, pinned by round-trip bounds only.
+ *
+ * Build flags must keep -ffp-contract=off so that a*b-c stays two roundings,
+ * as in the reference build (CMakeLists.txt:15-26).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define Q4K_TYPE 12
+#define Q4K_BLOCK 256
+#define Q4K_BYTES 144
+
+/* fp16 -> fp32, exact.  Restates fh3_f16_to_f32 (src/core/fh3_quant.h:20-41)
+ * from the IEEE-754 binary16 definition (normal, subnormal, inf/nan). */
+static float h2f(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t expo = (h >> 10) & 0x1Fu;
+    uint32_t mant = h & 0x3FFu;
+    uint32_t bits;
+    if (expo == 0) {
+        if (mant == 0) {
+            bits = sign;
+        } else {
+            /* subnormal: value = mant * 2^-24; normalise */
+            int e = -1;
+            do { mant <<= 1; e++; } while ((mant & 0x400u) == 0);
+            mant &= 0x3FFu;
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | (mant << 13);
+        }
+    } else if (expo == 31) {
+        bits = sign | 0x7F800000u | (mant << 13);
+    } else {
+        bits = sign | ((expo + 112u) << 23) | (mant << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+float oracle_f16_to_f32(uint16_t h) { return h2f(h); }
+
+/* fp32 -> fp16, round to nearest even (for the quantiser's d/dmin fields). */
+static uint16_t f2h(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    int32_t expo = (int32_t)((x >> 23) & 0xFF) - 127 + 15;
+    uint32_t mant = x & 0x7FFFFFu;
+    if (((x >> 23) & 0xFF) == 0xFF) return (uint16_t)(sign | 0x7C00u | (mant ? 0x200u : 0));
+    if (expo >= 31) return (uint16_t)(sign | 0x7C00u);
+    if (expo <= 0) {
+        if (expo < -10) return (uint16_t)sign;
+        mant |= 0x800000u;
+        uint32_t shift = (uint32_t)(14 - expo);
+        uint32_t half = 1u << (shift - 1);
+        uint32_t rem = mant & ((1u << shift) - 1);
+        uint32_t r = mant >> shift;
+        if (rem > half || (rem == half && (r & 1u))) r++;
+        return (uint16_t)(sign | r);
+    }
+    uint32_t r = mant >> 13;
+    uint32_t rem = mant & 0x1FFFu;
+    uint32_t out = ((uint32_t)expo << 10) | r;
+    if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) out++;
+    return (uint16_t)(sign | out);
+}
+
+/* Restates fh3_row_bytes (src/core/fh3_quant.c:14-34) for the two types this
+ * path uses: F32 (:17) and Q4_K (:27). */
+size_t oracle_row_bytes(int type, int64_t n) {
+    if (n <= 0) return 0;
+    if (type == 0) return (size_t)n * 4;
+    if (type == Q4K_TYPE) return (size_t)((n + 255) / 256) * Q4K_BYTES;
+    return 0;
+}
+
+/* Unpack the 6-bit scale and min of sub-block j (0..7) from the 12 packed
+ * bytes at block offset 4.  Layout per src/core/fh3_quant.c:167-177. */
+static void q4k_scale_min(const uint8_t *s, int j, int *sc, int *m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+        *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+/* Restates dequant_q4_k (src/core/fh3_quant.c:154-196): per 256-weight
+ * super-block, dl = d*sc and ml = dmin*m in fp32, then w = dl*q - ml as a
+ * multiply and a separate subtract.  Only whole blocks are written (n/256,
+ * :155): a partial trailing block is ignored, as in the reference. */
+void oracle_dequant_q4k(const uint8_t *src, float *dst, int64_t n) {
+    if (!src || !dst || n <= 0) return;
+    int64_t nb = n / Q4K_BLOCK;
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t *blk = src + b * Q4K_BYTES;
+        uint16_t dh, mh;
+        memcpy(&dh, blk, 2);
+        memcpy(&mh, blk + 2, 2);
+        float d = h2f(dh), dmin = h2f(mh);
+        const uint8_t *qs = blk + 16;
+        float *out = dst + b * Q4K_BLOCK;
+        for (int j = 0; j < 8; j++) {
+            int sc, m;
+            q4k_scale_min(blk + 4, j, &sc, &m);
+            float dl = d * (float)sc;
+            float ml = dmin * (float)m;
+            const uint8_t *chunk = qs + (j >> 1) * 32;
+            for (int l = 0; l < 32; l++) {
+                int q = (j & 1) ? (chunk[l] >> 4) : (chunk[l] & 0x0F);
+                float prod = dl * (float)q;
+                out[j * 32 + l] = prod - ml;
+            }
+        }
+    }
+}
+
+/* fixed 8-lane tree of src/core/fh3_ops.c:19-27 */
+static float tree8(const float a[8]) {
+    float s01 = a[0] + a[1], s23 = a[2] + a[3];
+    float s45 = a[4] + a[5], s67 = a[6] + a[7];
+    return (s01 + s23) + (s45 + s67);
+}
+
+/* Dot product with the reference's summation order: 8 strided fp32 FMA lanes
+ * over k, the fixed tree, then an fmaf tail (src/core/fh3_ops.c:29-47; the
+ * AVX2 kernels :50-207 use the same lanes and tree, which is why the reference
+ * asserts scalar == AVX2 == OpenMP bitwise, tests/unit/test_matmul.c:107-139). */
+static float dot_ref_order(const float *x, const float *w, int64_t n) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int64_t n8 = n - (n % 8);
+    for (int64_t k = 0; k < n8; k += 8)
+        for (int l = 0; l < 8; l++) acc[l] = fmaf(x[k + l], w[k + l], acc[l]);
+    float dot = tree8(acc);
+    for (int64_t k = n8; k < n; k++) dot = fmaf(x[k], w[k], dot);
+    return dot;
+}
+
+/* Restates fh3_matmul (src/core/fh3_ops.c:317-404) for Q4_K and F32 weights:
+ * y[t][o] = dot(x[t], dequant(W[o])) (+ bias[o]); y is overwritten.  Returns 0,
+ * or -8 (FH3_E_INVALID) where the reference returns silently (:318-321). */
+int oracle_matmul(int type, const uint8_t *wdata, int64_t in, int64_t out,
+                  const float *x, float *y, int n_tok, const float *bias) {
+    if (!wdata || !x || !y || n_tok <= 0 || in <= 0 || out <= 0) return -8;
+    size_t rb = oracle_row_bytes(type, in);
+    if (rb == 0) return -8;
+    int64_t o;
+#pragma omp parallel for schedule(dynamic, 16)
+    for (o = 0; o < out; o++) {
+        float *wrow = (float *)malloc((size_t)in * sizeof(float));
+        if (!wrow) continue;
+        if (type == Q4K_TYPE) {
+            memset(wrow, 0, (size_t)in * sizeof(float));
+            oracle_dequant_q4k(wdata + (size_t)o * rb, wrow, in);
+        } else {
+            memcpy(wrow, wdata + (size_t)o * rb, (size_t)in * 4);
+        }
+        for (int t = 0; t < n_tok; t++) {
+            float d = dot_ref_order(x + (size_t)t * in, wrow, in);
+            if (bias) d += bias[o];
+            y[(size_t)t * out + o] = d;
+        }
+        free(wrow);
+    }
+    return 0;
+}
+
+/* Restates fh3_swiglu (src/core/fh3_ops.c:507-527): value-first halves,
+ * out = val * g / (1 + expf(-g)), and 0 for g < -80. */
+void oracle_swiglu(const float *in, float *out, int n, int F) {
+    int i;
+#pragma omp parallel for schedule(static)
+    for (i = 0; i < n; i++) {
+        const float *val = in + (size_t)i * 2 * F;
+        const float *gate = val + F;
+        for (int j = 0; j < F; j++) {
+            float g = gate[j];
+            float s = (g < -80.0f) ? 0.0f : g / (1.0f + expf(-g));
+            out[(size_t)i * F + j] = val[j] * s;
+        }
+    }
+}
+
+/* Restates fh3_rmsnorm (src/core/fh3_ops.c:410-456): 8-lane FMA sum of
+ * squares + tree, variance = sum/dim, inv = 1/sqrtf(var+eps), row*inv*w. */
+void oracle_rmsnorm(float *x, const float *w, int n, int dim, float eps) {
+    int i;
+#pragma omp parallel for schedule(static)
+    for (i = 0; i < n; i++) {
+        float *row = x + (size_t)i * dim;
+        float sum = dot_ref_order(row, row, dim);
+        float var = sum / (float)dim;
+        float inv = 1.0f / sqrtf(var + eps);
+        for (int d = 0; d < dim; d++) {
+            float t = row[d] * inv;
+            row[d] = t * w[d];
+        }
+    }
+}
+
+/* Restates fh3_modulate (src/core/fh3_ops.c:529-557): x = fma(x, 1+scale,
+ * shift) on whole 8-wide vectors of each 1024-element chunk, and the unfused
+ * x*(1+scale)+shift on a chunk's tail. shift/scale span the whole n*dim
+ * array, as in the reference. */
+void oracle_modulate(float *x, const float *shift, const float *scale, int n, int dim) {
+    int64_t total = (int64_t)n * dim;
+    for (int64_t k0 = 0; k0 < total; k0 += 1024) {
+        int64_t k1 = (k0 + 1024 <= total) ? k0 + 1024 : total;
+        int64_t k = k0;
+        for (; k + 8 <= k1; k += 8)
+            for (int l = 0; l < 8; l++) x[k + l] = fmaf(x[k + l], 1.0f + scale[k + l], shift[k + l]);
+        for (; k < k1; k++) {
+            float t = x[k] * (1.0f + scale[k]);
+            x[k] = t + shift[k];
+        }
+    }
+}
+
+/* Restates fh3_gate_residual (src/core/fh3_ops.c:559-585): h = fma(g, y, h). */
+void oracle_gate_residual(float *h, const float *gate, const float *y, int n, int dim) {
+    int64_t total = (int64_t)n * dim;
+    for (int64_t k = 0; k < total; k++) h[k] = fmaf(gate[k], y[k], h[k]);
+}
+
+/* Philox4x32-10 (Salmon et al., SC'11, "Parallel random numbers: as easy as
+ * 1, 2, 3") followed by Box-Muller in double, as fh3_rng_normal
+ * (src/model/fh3_sched.c:84-159) uses it: counter = {block lo, block hi,
+ * stream lo, stream hi}, key = {seed lo, seed hi}; each 128-bit output gives
+ * four normals, u = (c + 1) / (2^32 + 2). */
+static void philox10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+    for (int r = 0; r < 10; r++) {
+        uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+        uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+        uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+        uint32_t n1 = (uint32_t)p1;
+        uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+        uint32_t n3 = (uint32_t)p0;
+        c[0] = n0; c[1] = n1; c[2] = n2; c[3] = n3;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+}
+
+void oracle_rng_normal(uint64_t seed, uint64_t stream, float *out, size_t n) {
+    if (!out || n == 0) return;
+    size_t nb = (n + 3) / 4;
+    long long b;
+#pragma omp parallel for schedule(static)
+    for (b = 0; b < (long long)nb; b++) {
+        uint32_t c[4] = {(uint32_t)((uint64_t)b & 0xFFFFFFFFu), (uint32_t)((uint64_t)b >> 32),
+                         (uint32_t)(stream & 0xFFFFFFFFu), (uint32_t)(stream >> 32)};
+        philox10(c, (uint32_t)(seed & 0xFFFFFFFFu), (uint32_t)(seed >> 32));
+        float z[4];
+        for (int p = 0; p < 2; p++) {
+            double u0 = ((double)c[2 * p] + 1.0) / 4294967298.0;
+            double u1 = ((double)c[2 * p + 1] + 1.0) / 4294967298.0;
+            double r = sqrt(-2.0 * log(u0));
+            double th = 6.28318530717958647692 * u1;
+            z[2 * p] = (float)(r * cos(th));
+            z[2 * p + 1] = (float)(r * sin(th));
+        }
+        size_t base = (size_t)b * 4;
+        for (int i = 0; i < 4; i++)
+            if (base + i < n) out[base + i] = z[i];
+    }
+}
+
+/* ------------------------------------------------------------------------
+ * Q4_K quantiser (this project's input generator; no fh3 counterpart).
+ *
+ * Per 32-weight sub-block j: lo_j = min(0, min x), hi_j = max x; the sub-block
+ * is represented as w = (d*sc_j)*q - (dmin*m_j) with q in [0,15].  d and dmin
+ * are the fp16-rounded maxima of (hi-lo)/15 and -lo over the eight sub-blocks,
+ * divided by 63; sc_j = round(((hi-lo)/15)/d) and m_j = round(-lo/dmin) in
+ * [0,63]; q = round((x + dmin*m_j)/(d*sc_j)) clamped to [0,15].  The packing
+ * is the exact inverse of dequant_q4_k's unpacking (src/core/fh3_quant.c:167-193).
+ * ------------------------------------------------------------------------ */
+static void quantize_block(const float *x, uint8_t *blk) {
+    float scale[8], mn[8];
+    float max_scale = 0.0f, max_mn = 0.0f;
+    for (int j = 0; j < 8; j++) {
+        float lo = 0.0f, hi = -INFINITY;
+        for (int l = 0; l < 32; l++) {
+            float v = x[j * 32 + l];
+            if (v < lo) lo = v;
+            if (v > hi) hi = v;
+        }
+        if (hi < lo) hi = lo;
+        scale[j] = (hi - lo) / 15.0f;
+        mn[j] = -lo;
+        if (scale[j] > max_scale) max_scale = scale[j];
+        if (mn[j] > max_mn) max_mn = mn[j];
+    }
+    uint16_t dh = f2h(max_scale / 63.0f);
+    uint16_t mh = f2h(max_mn / 63.0f);
+    float d = h2f(dh), dmin = h2f(mh);
+    int sc[8], m[8];
+    for (int j = 0; j < 8; j++) {
+        sc[j] = d > 0.0f ? (int)lrintf(scale[j] / d) : 0;
+        m[j] = dmin > 0.0f ? (int)lrintf(mn[j] / dmin) : 0;
+        if (sc[j] < 0) sc[j] = 0;
+        if (sc[j] > 63) sc[j] = 63;
+        if (m[j] < 0) m[j] = 0;
+        if (m[j] > 63) m[j] = 63;
+    }
+    memset(blk, 0, Q4K_BYTES);
+    memcpy(blk, &dh, 2);
+    memcpy(blk + 2, &mh, 2);
+    uint8_t *s = blk + 4;
+    for (int j = 0; j < 4; j++) {
+        s[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        s[j + 4] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+        s[j + 8] = (uint8_t)((sc[j + 4] & 15) | ((m[j + 4] & 15) << 4));
+    }
+    uint8_t *qs = blk + 16;
+    for (int j = 0; j < 8; j++) {
+        float dl = d * (float)sc[j];
+        float ml = dmin * (float)m[j];
+        for (int l = 0; l < 32; l++) {
+            int q = 0;
+            if (dl > 0.0f) {
+                q = (int)lrintf((x[j * 32 + l] + ml) / dl);
+                if (q < 0) q = 0;
+                if (q > 15) q = 15;
+            }
+            uint8_t *byte = qs + (j >> 1) * 32 + l;
+            if (j & 1) *byte = (uint8_t)((*byte & 0x0F) | (q << 4));
+            else *byte = (uint8_t)((*byte & 0xF0) | q);
+        }
+    }
+}
+
+/* Quantise rows x [rows][n] (n a multiple of 256) to Q4_K rows. */
+int oracle_quantize_q4k(const float *x, uint8_t *dst, int64_t rows, int64_t n) {
+    if (!x || !dst || rows <= 0 || n <= 0 || (n % Q4K_BLOCK) != 0) return -8;
+    int64_t nb = rows * (n / Q4K_BLOCK);
+    int64_t b;
+#pragma omp parallel for schedule(static)
+    for (b = 0; b < nb; b++) quantize_block(x + b * Q4K_BLOCK, dst + b * Q4K_BYTES);
+    return 0;
+}
+
+/* Seeded Q4_K weight generator: W = scale * N(0,1) from oracle_rng_normal
+ * (seed, stream), quantised row by row.  Streams the normals through a
+ * bounded buffer so that multi-GB weights need no multi-GB fp32 copy. */
+int oracle_make_q4k_weights(uint64_t seed, uint64_t stream, float scale,
+                            int64_t rows, int64_t n, uint8_t *dst) {
+    if (!dst || rows <= 0 || n <= 0 || (n % Q4K_BLOCK) != 0) return -8;
+    const int64_t chunk_rows = (int64_t)((64ll << 20) / (n * 4)) > 0 ? (int64_t)((64ll << 20) / (n * 4)) : 1;
+    float *buf = (float *)malloc((size_t)chunk_rows * n * sizeof(float));
+    if (!buf) return -7;
+    size_t rb = oracle_row_bytes(Q4K_TYPE, n);
+    for (int64_t r0 = 0; r0 < rows; r0 += chunk_rows) {
+        int64_t nr = rows - r0 < chunk_rows ? rows - r0 : chunk_rows;
+        /* element index e = r*n + k of the whole matrix maps to normal number e */
+        size_t first = (size_t)(r0 * n);
+        size_t cnt = (size_t)(nr * n);
+        /* generate normals [first, first+cnt): first is a multiple of 4 since n%256==0 */
+        size_t nb = cnt / 4;
+        long long b;
+#pragma omp parallel for schedule(static)
+        for (b = 0; b < (long long)nb; b++) {
+            uint64_t gb = (uint64_t)(first / 4) + (uint64_t)b;
+            uint32_t c[4] = {(uint32_t)(gb & 0xFFFFFFFFu), (uint32_t)(gb >> 32),
+                             (uint32_t)(stream & 0xFFFFFFFFu), (uint32_t)(stream >> 32)};
+            philox10(c, (uint32_t)(seed & 0xFFFFFFFFu), (uint32_t)(seed >> 32));
+            for (int p = 0; p < 2; p++) {
+                double u0 = ((double)c[2 * p] + 1.0) / 4294967298.0;
+                double u1 = ((double)c[2 * p + 1] + 1.0) / 4294967298.0;
+                double r = sqrt(-2.0 * log(u0));
+                double th = 6.28318530717958647692 * u1;
+                buf[b * 4 + 2 * p] = (float)(r * cos(th)) * scale;
+                buf[b * 4 + 2 * p + 1] = (float)(r * sin(th)) * scale;
+            }
+        }
+        int rc = oracle_quantize_q4k(buf, dst + (size_t)r0 * rb, nr, n);
+        if (rc) { free(buf); return rc; }
+    }
+    free(buf);
+    return 0;
+}
+
+int oracle_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

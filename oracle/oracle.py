@@ -1,0 +1,256 @@
+"""ctypes front end of the CPU parity oracle (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+legs import this module, as the checker or as the timed CPU baseline.  The
+product (fasth3inc_b200, libfh3cuda) never imports it.
+
+Two libraries sit behind it:
+  * ``liboracle.so``       -- this project's C restatement (oracle/fh3_oracle.c),
+                              built by ``make -C oracle``; always available.
+  * ``_ref/libfh3ref.so``  -- the reference's own fh3_quant.c / fh3_ops.c /
+                              fh3_sched.c compiled from its sources by the same
+                              Makefile, where the reference tree exists.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libfh3ref.so")
+
+Q4K = 12
+F32 = 0
+Q4K_BLOCK = 256
+Q4K_BYTES = 144
+
+_c_f32p = ctypes.POINTER(ctypes.c_float)
+_c_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+
+def build(quiet: bool = True) -> None:
+    """Compile liboracle.so (and _ref/libfh3ref.so where the reference exists)."""
+    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
+    if not quiet:
+        print(out.stdout)
+
+
+def _ptr(a: np.ndarray, ct):
+    return a.ctypes.data_as(ct) if a is not None else None
+
+
+class _Fh3W(ctypes.Structure):
+    """Mirror of the reference's Fh3W (include/fh3/fh3.h:82-87)."""
+    _fields_ = [("type", ctypes.c_int), ("in_", ctypes.c_int64),
+                ("out", ctypes.c_int64), ("data", _c_u8p)]
+
+
+class Oracle:
+    """This project's C restatement of the reference path."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build()
+        lib = ctypes.CDLL(path)
+        lib.oracle_row_bytes.restype = ctypes.c_size_t
+        lib.oracle_row_bytes.argtypes = [ctypes.c_int, ctypes.c_int64]
+        lib.oracle_dequant_q4k.argtypes = [_c_u8p, _c_f32p, ctypes.c_int64]
+        lib.oracle_matmul.restype = ctypes.c_int
+        lib.oracle_matmul.argtypes = [ctypes.c_int, _c_u8p, ctypes.c_int64, ctypes.c_int64,
+                                      _c_f32p, _c_f32p, ctypes.c_int, _c_f32p]
+        lib.oracle_swiglu.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
+        lib.oracle_rmsnorm.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
+        lib.oracle_modulate.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
+        lib.oracle_gate_residual.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
+        lib.oracle_rng_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _c_f32p, ctypes.c_size_t]
+        lib.oracle_quantize_q4k.restype = ctypes.c_int
+        lib.oracle_quantize_q4k.argtypes = [_c_f32p, _c_u8p, ctypes.c_int64, ctypes.c_int64]
+        lib.oracle_make_q4k_weights.restype = ctypes.c_int
+        lib.oracle_make_q4k_weights.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
+                                                ctypes.c_int64, ctypes.c_int64, _c_u8p]
+        lib.oracle_num_threads.restype = ctypes.c_int
+        self.lib = lib
+
+    def row_bytes(self, type_: int, n: int) -> int:
+        return int(self.lib.oracle_row_bytes(type_, n))
+
+    def dequant_q4k(self, raw: np.ndarray, n: int) -> np.ndarray:
+        raw = np.ascontiguousarray(raw, dtype=np.uint8)
+        out = np.zeros(n, dtype=np.float32)
+        self.lib.oracle_dequant_q4k(_ptr(raw, _c_u8p), _ptr(out, _c_f32p), n)
+        return out
+
+    def dequant_rows(self, raw: np.ndarray, rows: int, n: int) -> np.ndarray:
+        rb = self.row_bytes(Q4K, n)
+        raw = np.ascontiguousarray(raw, dtype=np.uint8).reshape(rows, rb)
+        return np.stack([self.dequant_q4k(raw[r], n) for r in range(rows)])
+
+    def matmul(self, type_: int, w: np.ndarray, in_: int, out: int, x: np.ndarray,
+               bias: np.ndarray | None = None) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n_tok = x.shape[0]
+        y = np.empty((n_tok, out), dtype=np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        rc = self.lib.oracle_matmul(type_, _ptr(w, _c_u8p), in_, out, _ptr(x, _c_f32p),
+                                    _ptr(y, _c_f32p), n_tok, _ptr(b, _c_f32p))
+        if rc != 0:
+            raise ValueError(f"oracle_matmul rejected its arguments (rc={rc})")
+        return y
+
+    def swiglu(self, h: np.ndarray) -> np.ndarray:
+        h = np.ascontiguousarray(h, dtype=np.float32)
+        n, two_f = h.shape
+        out = np.empty((n, two_f // 2), dtype=np.float32)
+        self.lib.oracle_swiglu(_ptr(h, _c_f32p), _ptr(out, _c_f32p), n, two_f // 2)
+        return out
+
+    def rmsnorm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        self.lib.oracle_rmsnorm(_ptr(x, _c_f32p), _ptr(w, _c_f32p), x.shape[0], x.shape[1], eps)
+        return x
+
+    def modulate(self, x: np.ndarray, shift: np.ndarray, scale: np.ndarray) -> np.ndarray:
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        sh = np.ascontiguousarray(np.broadcast_to(shift, x.shape), dtype=np.float32)
+        sc = np.ascontiguousarray(np.broadcast_to(scale, x.shape), dtype=np.float32)
+        self.lib.oracle_modulate(_ptr(x, _c_f32p), _ptr(sh, _c_f32p), _ptr(sc, _c_f32p),
+                                 x.shape[0], x.shape[1])
+        return x
+
+    def gate_residual(self, h: np.ndarray, gate: np.ndarray, y: np.ndarray) -> np.ndarray:
+        h = np.array(h, dtype=np.float32, copy=True, order="C")
+        g = np.ascontiguousarray(np.broadcast_to(gate, h.shape), dtype=np.float32)
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        self.lib.oracle_gate_residual(_ptr(h, _c_f32p), _ptr(g, _c_f32p), _ptr(y, _c_f32p),
+                                      h.shape[0], h.shape[1])
+        return h
+
+    def rng_normal(self, seed: int, stream: int, n: int) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        self.lib.oracle_rng_normal(seed, stream, _ptr(out, _c_f32p), n)
+        return out
+
+    def quantize_q4k(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, n = x.shape
+        out = np.empty(rows * self.row_bytes(Q4K, n), dtype=np.uint8)
+        rc = self.lib.oracle_quantize_q4k(_ptr(x, _c_f32p), _ptr(out, _c_u8p), rows, n)
+        if rc != 0:
+            raise ValueError("oracle_quantize_q4k: n must be a positive multiple of 256")
+        return out
+
+    def make_weights(self, seed: int, stream: int, rows: int, n: int, scale: float = 0.02,
+                     out: np.ndarray | None = None) -> np.ndarray:
+        """Seeded Q4_K weights: quantise(scale * fh3_rng_normal(seed, stream))."""
+        nbytes = rows * self.row_bytes(Q4K, n)
+        if out is None:
+            out = np.empty(nbytes, dtype=np.uint8)
+        assert out.nbytes >= nbytes and out.dtype == np.uint8 and out.flags.c_contiguous
+        rc = self.lib.oracle_make_q4k_weights(seed, stream, scale, rows, n, _ptr(out, _c_u8p))
+        if rc != 0:
+            raise ValueError(f"oracle_make_q4k_weights failed (rc={rc})")
+        return out
+
+    def num_threads(self) -> int:
+        return int(self.lib.oracle_num_threads())
+
+
+class Reference:
+    """The reference's own functions, compiled from its sources into _ref/."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        lib = ctypes.CDLL(path)
+        lib.fh3_row_bytes.restype = ctypes.c_size_t
+        lib.fh3_row_bytes.argtypes = [ctypes.c_int, ctypes.c_int64]
+        lib.fh3_dequant.argtypes = [ctypes.c_int, ctypes.c_void_p, _c_f32p, ctypes.c_int64]
+        for name in ("fh3_matmul", "fh3_matmul_scalar", "fh3_matmul_avx2"):
+            f = getattr(lib, name)
+            f.argtypes = [ctypes.POINTER(_Fh3W), _c_f32p, _c_f32p, ctypes.c_int, _c_f32p]
+        lib.fh3_swiglu.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
+        lib.fh3_rmsnorm.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
+        lib.fh3_modulate.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
+        lib.fh3_gate_residual.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
+        lib.fh3_rng_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _c_f32p, ctypes.c_size_t]
+        self.lib = lib
+
+    @staticmethod
+    def available(path: str = REF_SO) -> bool:
+        return os.path.exists(path)
+
+    def row_bytes(self, type_: int, n: int) -> int:
+        return int(self.lib.fh3_row_bytes(type_, n))
+
+    def dequant(self, type_: int, raw: np.ndarray, n: int) -> np.ndarray:
+        raw = np.ascontiguousarray(raw, dtype=np.uint8)
+        out = np.zeros(n, dtype=np.float32)
+        self.lib.fh3_dequant(type_, raw.ctypes.data, _ptr(out, _c_f32p), n)
+        return out
+
+    def matmul(self, type_: int, w: np.ndarray, in_: int, out: int, x: np.ndarray,
+               bias: np.ndarray | None = None, variant: str = "fh3_matmul") -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros((x.shape[0], out), dtype=np.float32)
+        desc = _Fh3W(type_, in_, out, _ptr(w, _c_u8p))
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        getattr(self.lib, variant)(ctypes.byref(desc), _ptr(x, _c_f32p), _ptr(y, _c_f32p),
+                                   x.shape[0], _ptr(b, _c_f32p))
+        return y
+
+    def matmul_into(self, desc: "_Fh3W", x: np.ndarray, y: np.ndarray, n_tok: int,
+                    bias: np.ndarray | None = None) -> None:
+        """Unchecked call used by the timed CPU baseline (buffers preallocated)."""
+        self.lib.fh3_matmul(ctypes.byref(desc), _ptr(x, _c_f32p), _ptr(y, _c_f32p), n_tok,
+                            _ptr(bias, _c_f32p) if bias is not None else None)
+
+    def swiglu(self, h: np.ndarray) -> np.ndarray:
+        h = np.ascontiguousarray(h, dtype=np.float32)
+        n, two_f = h.shape
+        out = np.empty((n, two_f // 2), dtype=np.float32)
+        self.lib.fh3_swiglu(_ptr(h, _c_f32p), _ptr(out, _c_f32p), n, two_f // 2)
+        return out
+
+    def rmsnorm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        self.lib.fh3_rmsnorm(_ptr(x, _c_f32p), _ptr(w, _c_f32p), x.shape[0], x.shape[1], eps)
+        return x
+
+    def modulate(self, x, shift, scale):
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        sh = np.ascontiguousarray(np.broadcast_to(shift, x.shape), dtype=np.float32)
+        sc = np.ascontiguousarray(np.broadcast_to(scale, x.shape), dtype=np.float32)
+        self.lib.fh3_modulate(_ptr(x, _c_f32p), _ptr(sh, _c_f32p), _ptr(sc, _c_f32p),
+                              x.shape[0], x.shape[1])
+        return x
+
+    def gate_residual(self, h, gate, y):
+        h = np.array(h, dtype=np.float32, copy=True, order="C")
+        g = np.ascontiguousarray(np.broadcast_to(gate, h.shape), dtype=np.float32)
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        self.lib.fh3_gate_residual(_ptr(h, _c_f32p), _ptr(g, _c_f32p), _ptr(y, _c_f32p),
+                                   h.shape[0], h.shape[1])
+        return h
+
+    def rng_normal(self, seed: int, stream: int, n: int) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        self.lib.fh3_rng_normal(seed, stream, _ptr(out, _c_f32p), n)
+        return out
+
+
+def rel_fro(a: np.ndarray, b: np.ndarray) -> float:
+    """Relative Frobenius error ||a-b|| / ||b|| in float64."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    den = np.linalg.norm(b)
+    return float(np.linalg.norm(a - b) / (den if den > 0 else 1.0))

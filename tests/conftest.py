@@ -1,0 +1,91 @@
+"""Shared fixtures.  GPU tests carry @pytest.mark.gpu; everything else runs on CPU."""
+from __future__ import annotations
+
+import os
+import struct
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs an sm_100 (B200) GPU; runs through libfh3cuda")
+
+
+def _has_gpu() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+HAS_GPU = _has_gpu()
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    from oracle.oracle import Oracle, build
+    build()
+    return Oracle()
+
+
+@pytest.fixture(scope="session")
+def reference():
+    from oracle.oracle import Reference
+    if not Reference.available():
+        pytest.skip("reference objects (oracle/_ref) not built in this tree")
+    return Reference()
+
+
+@pytest.fixture(scope="session")
+def golden_cases():
+    return dict(np.load(os.path.join(GOLDEN, "ref_cases.npz")))
+
+
+def read_q4k_golden():
+    """tests/fixtures/quant/Q4_K.bin of the reference: <IIII> type, rows, cols, nbytes; raw; fp32."""
+    with open(os.path.join(GOLDEN, "Q4_K.bin"), "rb") as f:
+        b = f.read()
+    t, rows, cols, nb = struct.unpack("<IIII", b[:16])
+    raw = np.frombuffer(b[16:16 + nb], np.uint8).copy()
+    ref = np.frombuffer(b[16 + nb:], np.float32).reshape(rows, cols).copy()
+    return t, rows, cols, raw, ref
+
+
+def read_matmul_golden():
+    """tests/fixtures/quant/matmul_ref.bin: <IIIII> type, K, N, M, wbytes; W; x; bias; y (fp64 numpy)."""
+    with open(os.path.join(GOLDEN, "matmul_ref.bin"), "rb") as f:
+        b = f.read()
+    t, K, N, M, wb = struct.unpack("<IIIII", b[:20])
+    off = 20
+    w = np.frombuffer(b[off:off + wb], np.uint8).copy(); off += wb
+    x = np.frombuffer(b[off:off + 4 * M * K], np.float32).reshape(M, K).copy(); off += 4 * M * K
+    bias = np.frombuffer(b[off:off + 4 * N], np.float32).copy(); off += 4 * N
+    y = np.frombuffer(b[off:off + 4 * M * N], np.float32).reshape(M, N).copy()
+    return t, K, N, M, w, x, bias, y
+
+
+@pytest.fixture(scope="session")
+def fh3():
+    """The product package on cuda:0; the CUDA library must load (no fallback)."""
+    if not HAS_GPU:
+        pytest.skip("no CUDA device")
+    import fasth3inc_b200 as f
+    from fasth3inc_b200 import build
+    build.build()
+    f.init(0)
+    return f
+
+
+def rel_fro(a, b) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    den = np.linalg.norm(b)
+    return float(np.linalg.norm(a - b) / (den if den > 0 else 1.0))

@@ -1,0 +1,81 @@
+"""Regenerate the golden vectors under tests/golden/ (run in a tree that has the reference).
+
+1. Copies the reference's own Q4_K golden vectors (data files, not sources):
+     tests/fixtures/quant/Q4_K.bin        -> Q4_K.bin        (gguf-py dequantize output)
+     tests/fixtures/quant/matmul_ref.bin  -> matmul_ref.bin  (fp64 numpy matmul output)
+   Their layouts are documented in the reference's tools/emit_quant_fixtures.py:75-81,134-141
+   and read by tests/unit/test_quant.c:54-81 and tests/unit/test_matmul.c:196-231.
+2. Writes ref_cases.npz: seeded inputs (this project's Q4_K quantiser + fh3_rng_normal)
+   with outputs computed by the REFERENCE'S OWN fh3_matmul / fh3_dequant / fh3_swiglu,
+   compiled from its sources into oracle/_ref/libfh3ref.so (oracle/Makefile).  These pin
+   the oracle and the CUDA path on shapes the reference's goldens do not cover
+   (odd N, tiny K, GEMV token counts, a GEMM-sized M).
+
+    python tests/golden/make_golden.py [--ref /path/to/fh3]
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from oracle.oracle import Q4K, Oracle, Reference, build  # noqa: E402
+
+# (name, K, N, M, bias?)  -- seeds are derived from the index
+CASES = [
+    ("k256_n1_m1", 256, 1, 1, False),
+    ("k512_n70_m1", 512, 70, 1, True),
+    ("k512_n70_m3", 512, 70, 3, False),
+    ("k1024_n130_m16", 1024, 130, 16, True),
+    ("k768_n200_m5", 768, 200, 5, False),
+    ("k1024_n192_m37", 1024, 192, 37, True),
+    ("k512_n264_m130", 512, 264, 130, True),
+]
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    fx = os.path.join(args.ref, "tests", "fixtures", "quant")
+    for name in ("Q4_K.bin", "matmul_ref.bin"):
+        shutil.copyfile(os.path.join(fx, name), os.path.join(HERE, name))
+    build()
+    o = Oracle()
+    r = Reference()
+    out = {}
+    for i, (name, K, N, M, has_bias) in enumerate(CASES):
+        w = o.make_weights(seed=1000 + i, stream=1, rows=N, n=K)
+        x = o.rng_normal(1000 + i, 2, M * K).reshape(M, K)
+        b = o.rng_normal(1000 + i, 3, N) if has_bias else None
+        y = r.matmul(Q4K, w, K, N, x, b)
+        out[f"{name}/w"] = w
+        out[f"{name}/x"] = x
+        if b is not None:
+            out[f"{name}/bias"] = b
+        out[f"{name}/y"] = y
+        out[f"{name}/dims"] = np.array([K, N, M], dtype=np.int64)
+    # dequant of one generated matrix, by the reference
+    w = o.make_weights(seed=77, stream=5, rows=3, n=1024)
+    out["dequant/w"] = w
+    out["dequant/y"] = np.stack([r.dequant(Q4K, w[i * 576:(i + 1) * 576], 1024) for i in range(3)])
+    # swiglu by the reference
+    h = (o.rng_normal(78, 1, 4 * 2 * 96) * 4.0).reshape(4, 192)
+    h[0, 96:100] = [-100.0, -80.5, -79.5, 90.0]
+    out["swiglu/h"] = h
+    out["swiglu/y"] = r.swiglu(h)
+    # fh3_rng_normal itself
+    out["rng/seed7_stream3"] = r.rng_normal(7, 3, 1001)
+    np.savez_compressed(os.path.join(HERE, "ref_cases.npz"), **out)
+    print("wrote", sorted(os.listdir(HERE)))
+
+
+if __name__ == "__main__":
+    main()

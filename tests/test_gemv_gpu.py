@@ -1,0 +1,84 @@
+"""The fp32 CUDA-core GEMV (1..16 tokens) against fh3_matmul.
+
+Tolerance: relative Frobenius error <= 1e-5 for the fp32
+GEMV path, checked against the reference's own outputs (tests/golden) and the
+oracle (bitwise equal to fh3_matmul, tests/test_oracle.py) at the BASELINE shapes.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import read_matmul_golden, rel_fro
+
+pytestmark = pytest.mark.gpu
+Q4K = 12
+TOL = 1e-5
+
+
+def _run(fh3, w_raw, K, N, x, bias=None):
+    import torch
+    w = fh3.Q4KWeight.from_bytes(w_raw, K, N)
+    xt = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+    bt = None if bias is None else torch.from_numpy(np.ascontiguousarray(bias, dtype=np.float32)).cuda()
+    y = fh3.gemv(w, xt, bt)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+def test_reference_cases(fh3, golden_cases):
+    seen = 0
+    for name in sorted({k.split("/")[0] for k in golden_cases if k.startswith("k")}):
+        K, N, M = (int(v) for v in golden_cases[f"{name}/dims"])
+        if M > 16:
+            continue
+        y = _run(fh3, golden_cases[f"{name}/w"], K, N, golden_cases[f"{name}/x"],
+                 golden_cases.get(f"{name}/bias"))
+        assert rel_fro(y, golden_cases[f"{name}/y"]) <= TOL, name
+        seen += 1
+    assert seen >= 5
+
+
+def test_reference_fp64_golden_first_16_tokens(fh3):
+    t, K, N, M, w, x, bias, y = read_matmul_golden()
+    got = _run(fh3, w, K, N, x[:16], bias)
+    assert rel_fro(got, y[:16]) <= TOL
+
+
+@pytest.mark.parametrize("K,N", [(5120, 5120), (5120, 13824), (13824, 5120)])
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_baseline_shapes_vs_oracle(fh3, oracle, K, N, M):
+    w = oracle.make_weights(seed=K + N, stream=1, rows=N, n=K)
+    x = oracle.rng_normal(M, 2, M * K).reshape(M, K)
+    ref = oracle.matmul(Q4K, w, K, N, x)
+    got = _run(fh3, w, K, N, x)
+    assert rel_fro(got, ref) <= TOL
+
+
+def test_every_token_count_and_row_tail(fh3, oracle):
+    K, N = 1280, 37  # N not a multiple of the rows-per-warp
+    w = oracle.make_weights(seed=5, stream=1, rows=N, n=K)
+    b = oracle.rng_normal(5, 9, N)
+    for M in range(1, 17):
+        x = oracle.rng_normal(5, 10 + M, M * K).reshape(M, K)
+        for bias in (None, b):
+            ref = oracle.matmul(Q4K, w, K, N, x, bias)
+            got = _run(fh3, w, K, N, x, bias)
+            assert rel_fro(got, ref) <= TOL, (M, bias is None)
+
+
+def test_single_row_single_block(fh3, oracle):
+    w = oracle.make_weights(seed=6, stream=1, rows=1, n=256)
+    x = oracle.rng_normal(6, 2, 256).reshape(1, 256)
+    assert rel_fro(_run(fh3, w, 256, 1, x), oracle.matmul(Q4K, w, 256, 1, x)) <= TOL
+
+
+def test_rejects_bad_arguments(fh3, oracle):
+    import torch
+    w = fh3.Q4KWeight.from_bytes(oracle.make_weights(1, 1, 4, 256), 256, 4)
+    x = torch.zeros((17, 256), dtype=torch.float32, device="cuda")
+    with pytest.raises(fh3.Fh3CudaError):
+        fh3.gemv(w, x)  # more than 16 tokens is the GEMM's job
+    bad = fh3.Q4KWeight(w.data, 300, 4)  # in not a multiple of 256
+    with pytest.raises(fh3.Fh3CudaError):
+        fh3.gemv(bad, x[:1, :256])

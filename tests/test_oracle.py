@@ -1,0 +1,126 @@
+"""The CPU oracle, pinned against the reference's golden vectors and the reference itself.
+
+Mirrors the reference's own checks: tests/unit/test_quant.c (dequant bit-exact vs
+gguf-py) and tests/unit/test_matmul.c (matmul rel-L2 <= 1e-6 vs fp64 numpy), plus
+bitwise equality with fh3_matmul (whose scalar/AVX2/OpenMP variants agree bitwise,
+test_matmul.c:107-139) on the reference-generated cases in tests/golden/ref_cases.npz.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import read_matmul_golden, read_q4k_golden, rel_fro
+
+Q4K = 12
+
+
+def test_dequant_matches_reference_golden_bitexact(oracle):
+    t, rows, cols, raw, ref = read_q4k_golden()
+    assert (t, rows, cols) == (12, 4, 512)
+    got = oracle.dequant_rows(raw, rows, cols)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_matmul_matches_reference_golden(oracle):
+    t, K, N, M, w, x, bias, y = read_matmul_golden()
+    assert (t, K, N, M) == (12, 5376, 192, 37)
+    got = oracle.matmul(Q4K, w, K, N, x, bias)
+    # tests/unit/test_matmul.c:287-300: rel-L2 vs the fp64 reference <= 1e-6
+    assert rel_fro(got, y) <= 1e-6
+
+
+def test_matmul_bitwise_equals_reference_cases(oracle, golden_cases):
+    names = sorted({k.split("/")[0] for k in golden_cases if k.startswith("k")})
+    assert len(names) >= 6
+    for name in names:
+        K, N, M = (int(v) for v in golden_cases[f"{name}/dims"])
+        bias = golden_cases.get(f"{name}/bias")
+        got = oracle.matmul(Q4K, golden_cases[f"{name}/w"], K, N, golden_cases[f"{name}/x"], bias)
+        ref = golden_cases[f"{name}/y"]
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), name
+
+
+def test_dequant_and_swiglu_bitwise_equal_reference_cases(oracle, golden_cases):
+    got = oracle.dequant_rows(golden_cases["dequant/w"], 3, 1024)
+    assert np.array_equal(got.view(np.uint32), golden_cases["dequant/y"].view(np.uint32))
+    sw = oracle.swiglu(golden_cases["swiglu/h"])
+    assert np.array_equal(sw.view(np.uint32), golden_cases["swiglu/y"].view(np.uint32))
+    assert sw[0, 0] == 0.0 and sw[0, 1] == 0.0  # gates -100 and -80.5: the g < -80 cut
+
+
+def test_rng_matches_reference_fh3_rng_normal(oracle, golden_cases):
+    got = oracle.rng_normal(7, 3, 1001)
+    assert np.array_equal(got.view(np.uint32), golden_cases["rng/seed7_stream3"].view(np.uint32))
+
+
+def test_oracle_bitwise_equals_live_reference(oracle, reference):
+    rng = np.random.default_rng(5)
+    for K, N, M in [(256, 3, 2), (512, 65, 9), (1280, 129, 33), (5120, 64, 3)]:
+        w = oracle.make_weights(seed=int(rng.integers(1 << 30)), stream=1, rows=N, n=K)
+        x = oracle.rng_normal(int(rng.integers(1 << 30)), 2, M * K).reshape(M, K)
+        b = oracle.rng_normal(3, 4, N)
+        for bias in (None, b):
+            a = oracle.matmul(Q4K, w, K, N, x, bias)
+            r = reference.matmul(Q4K, w, K, N, x, bias)
+            assert np.array_equal(a.view(np.uint32), r.view(np.uint32)), (K, N, M)
+    x = oracle.rng_normal(1, 3, 8 * 5120).reshape(8, 5120)
+    nw = oracle.rng_normal(1, 4, 5120)
+    sh = oracle.rng_normal(1, 5, 8 * 5120).reshape(8, 5120)
+    sc = oracle.rng_normal(1, 6, 8 * 5120).reshape(8, 5120)
+    for a, r in [(oracle.rmsnorm(x, nw, 1e-6), reference.rmsnorm(x, nw, 1e-6)),
+                 (oracle.modulate(x, sh, sc), reference.modulate(x, sh, sc)),
+                 (oracle.gate_residual(x, sh, sc), reference.gate_residual(x, sh, sc))]:
+        assert np.array_equal(a.view(np.uint32), r.view(np.uint32))
+
+
+def _subblock_bound(raw: np.ndarray, rows: int, n: int, oracle) -> np.ndarray:
+    """Per-weight round-trip bound of the quantiser: dl/2 + 7.5 d + dmin/2 (+ fp32 slack)."""
+    blocks = raw.reshape(rows * n // 256, 144)
+    d = blocks[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    dmin = blocks[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
+    s = blocks[:, 4:16].astype(np.int32)
+    sc = np.zeros((blocks.shape[0], 8), np.float32)
+    for j in range(8):
+        if j < 4:
+            sc[:, j] = s[:, j] & 63
+        else:
+            sc[:, j] = (s[:, j + 4] & 15) | ((s[:, j - 4] >> 6) << 4)
+    dl = d[:, None] * sc
+    bound = 0.5 * dl + 7.5 * d[:, None] + 0.5 * dmin[:, None] + 1e-6
+    return np.repeat(bound, 32, axis=1).reshape(rows, n)
+
+
+@pytest.mark.parametrize("scale", [0.02, 1.0, 37.0])
+def test_quantiser_round_trip_bounds(oracle, scale):
+    rows, n = 16, 1024
+    x = (scale * oracle.rng_normal(11, 12, rows * n)).reshape(rows, n)
+    raw = oracle.quantize_q4k(x)
+    dq = oracle.dequant_rows(raw, rows, n)
+    err = np.abs(dq - x)
+    assert np.all(err <= _subblock_bound(raw, rows, n, oracle))
+    assert rel_fro(dq, x) < 0.12  # 4.5-bit quantisation of a normal
+
+
+def test_quantiser_edge_blocks(oracle):
+    n = 256
+    cases = [np.zeros(n), np.full(n, 0.5), np.full(n, -0.25), np.linspace(0.0, 1.0, n),
+             np.linspace(-2.0, -1.0, n), np.where(np.arange(n) % 2 == 0, 3.0, -3.0)]
+    x = np.stack(cases).astype(np.float32)
+    raw = oracle.quantize_q4k(x)
+    dq = oracle.dequant_rows(raw, x.shape[0], n)
+    assert np.all(np.abs(dq - x) <= _subblock_bound(raw, x.shape[0], n, oracle))
+    assert np.all(dq[0] == 0.0)
+
+
+def test_make_weights_equals_quantise_of_rng(oracle):
+    w = oracle.make_weights(seed=3, stream=9, rows=5, n=512, scale=0.02)
+    x = 0.02 * oracle.rng_normal(3, 9, 5 * 512)
+    assert np.array_equal(w, oracle.quantize_q4k(x.reshape(5, 512)))
+
+
+def test_oracle_rejects_bad_arguments(oracle):
+    with pytest.raises(ValueError):
+        oracle.matmul(99, np.zeros(144, np.uint8), 256, 1, np.zeros((1, 256), np.float32))
+    with pytest.raises(ValueError):
+        oracle.quantize_q4k(np.zeros((1, 100), np.float32))
