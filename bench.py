@@ -1,0 +1,382 @@
+"""Benchmark: one synthetic 50-block DiT denoising step of Q4_K projections on B200.
+
+Workload (the headline "DiT step" of its metric): d = 5120,
+40 heads x 128, FFN 13824, M = 32760 video + 1024 audio = 33784 latent rows, 512 text
+rows, 50 blocks of Q4_K weights (11.87 GB) resident in HBM.  Rows are sharded across
+N GPUs (strong scaling: total rows fixed) and gathered with an NCCL all-gather at the
+end of the step.  The other BASELINE configs are parity-test cases (tests/).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Prints one JSON line on rank 0.  `value` = GEMM TFLOP/s of the whole step (useful
+FLOPs of all 33784 rows, text K/V counted once) / device time, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4_K DiT step ms & dequant-GEMM TFLOP/s (GEMV GB/s) at 1/2/4/8 B200 vs host CPU"
+UNIT = "TFLOP/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemm_q4k_tc_kernel launch (fc1 shape,
+# scaled to the bench's rows) from profiles/gemm_q4k_tc_fc1.md; None until captured.
+GEMM_TRAFFIC_BYTES_PER_FLOP = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--blocks", type=int, default=50)
+    ap.add_argument("--rows", type=int, default=32760 + 1024)
+    ap.add_argument("--text-rows", type=int, default=512)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU baseline sample time")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler for the timed region (SM clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_sample(trunk_block_raw, rows_s: int, text_s: int, threads: int, use_ref: bool, reps: int = 1):
+    """Time the reference's fh3_matmul (or the oracle port) on one block's projections.
+
+    Returns (flops, best seconds, kind)."""
+    import numpy as np
+
+    from fasth3inc_b200.trunk import D_MODEL, FFN, block_shapes
+    from oracle import oracle as orc
+    if use_ref and orc.Reference.available():
+        impl, kind = orc.Reference(), "reference"
+    else:
+        impl, kind = orc.Oracle(), "port"
+    rng = np.random.default_rng(0)
+    xs = {D_MODEL: rng.standard_normal((rows_s, D_MODEL), dtype=np.float32),
+          FFN: rng.standard_normal((rows_s, FFN), dtype=np.float32)}
+    xt = rng.standard_normal((text_s, D_MODEL), dtype=np.float32)
+    flops = 0
+    for name, out, inn in block_shapes():
+        r = text_s if name == "ckv" else rows_s
+        flops += 2 * r * inn * out
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for name, out, inn in block_shapes():
+            x = xt if name == "ckv" else xs[inn]
+            impl.matmul(12, trunk_block_raw[name], inn, out, x)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return flops, best, kind
+
+
+def host_block_weights(trunk, b: int = 0) -> dict:
+    """Download block b's Q4_K bytes (the same weights the GPU uses) for the CPU legs."""
+    return {k: w.data.cpu().numpy() for k, w in trunk.blocks[b].w.items()}
+
+
+def size_cpu_sample(raw, threads, use_ref, target_s):
+    rows = 16
+    flops, dt, kind = cpu_sample(raw, rows, rows, threads, use_ref)
+    rows = int(max(16, min(4096, rows * target_s / max(dt, 1e-3))))
+    return rows
+
+
+# ----------------------------------------------------------------------------- ours
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import fasth3inc_b200 as fh3
+    from fasth3inc_b200.trunk import (Runner, Trunk, Workspace, block_flops, rows_for_rank, D_MODEL, FFN)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    fh3.init(local)
+    M, T = args.rows, args.text_rows
+    r0, r1 = rows_for_rank(M, rank, world)
+    m_loc = r1 - r0
+    t_build = time.time()
+    trunk = Trunk(n_blocks=args.blocks, seed=0, device=local).build()
+    t_build = time.time() - t_build
+    ws = Workspace(m_loc, T, device=local)
+    dev = f"cuda:{local}"
+    g = torch.Generator(device=dev).manual_seed(1234)
+    h_full = torch.randn((M, D_MODEL), device=dev, generator=g)          # seeded N(0,1) latent rows
+    text = torch.randn((T, D_MODEL), device=dev, generator=g)
+    text_bf = fh3.to_bf16(text)
+    h0 = h_full[r0:r1].clone()
+    h = h0.clone()
+    stream = torch.cuda.current_stream(local)
+    runner = Runner(trunk, ws, stream)
+    # gather target: padded equal shards for all_gather_into_tensor
+    shard = (M + world - 1) // world
+    gather_out = torch.empty((shard * world, D_MODEL), device=dev) if world > 1 else None
+    send = torch.empty((shard, D_MODEL), device=dev) if world > 1 else None
+
+    def step():
+        h.copy_(h0)  # every step starts from the same latents
+        runner.step(h, text_bf)
+        if world > 1:
+            send[:m_loc].copy_(h)
+            dist.all_gather_into_tensor(gather_out, send)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    status = fh3.device_status()
+    if status != 0:
+        raise SystemExit(f"device status {status} after warm-up")
+
+    # timed region
+    clocks = Clocks(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    runner.gemm_events = []
+    runner.launches = 0
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in runner.gemm_events)
+    gemm_flops = sum(f for _, _, f in runner.gemm_events)
+    launches = runner.launches
+    runner.gemm_events = None
+    stat = torch.tensor([ms_local, gemm_ms, float(gemm_flops), float(launches)], device=dev, dtype=torch.float64)
+    if world > 1:
+        mx = stat.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stat.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    else:
+        mx = sm = stat
+    ms = float(mx[0])
+    total_flops = args.blocks * block_flops(M, T)   # useful FLOPs of the whole step
+    value = total_flops / (ms * 1e-3) / 1e12
+    # roofline of the dominant kernel: rank-local GEMM events (max over ranks of time)
+    gemm_tflops = float(sm[2]) / world / (float(mx[1]) * 1e-3) / 1e12 if float(mx[1]) > 0 else None
+
+    # ---- end to end through the public API with host buffers
+    e2e_val = None
+    h_host = torch.empty((m_loc, D_MODEL), dtype=torch.float32, pin_memory=True)
+    h_host.copy_(h0.cpu())
+    t_host = text.cpu().pin_memory()
+    out_host = torch.empty((M if world > 1 else m_loc, D_MODEL), dtype=torch.float32, pin_memory=True)
+    h2d = h_host.numel() * 4 + t_host.numel() * 4
+    d2h = out_host.numel() * 4 if rank == 0 else 0
+    text_dev = torch.empty_like(text)
+
+    def e2e_step():
+        h.copy_(h_host, non_blocking=True)
+        text_dev.copy_(t_host, non_blocking=True)
+        fh3.to_bf16(text_dev, out=text_bf)
+        runner.step(h, text_bf)
+        if world > 1:
+            send[:m_loc].copy_(h)
+            dist.all_gather_into_tensor(gather_out, send)
+            if rank == 0:
+                out_host.copy_(gather_out[:M], non_blocking=True)
+        else:
+            out_host.copy_(h, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    a1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([a0.elapsed_time(a1) / args.e2e_steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_val = total_flops / (float(e2e_ms[0]) * 1e-3) / 1e12
+    status = fh3.device_status()
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        raw = host_block_weights(trunk, 0)
+        rows_s = size_cpu_sample(raw, threads, True, args.cpu_seconds)
+        f, dt, kind = cpu_sample(raw, rows_s, min(rows_s, T), threads, True, reps=1)
+        cpu = {"value": round(f / dt / 1e12, 5), "unit": UNIT, "cores": threads, "kind": kind,
+               "sample": f"block 0's 7 Q4_K projections (fh3_matmul, OpenMP) on {rows_s} latent rows and "
+                         f"{min(rows_s, T)} text rows = {f / 1e9:.1f} GFLOP in {dt:.2f} s; same weights as the GPU"}
+
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
+    roof = None
+    if gemm_tflops:
+        traffic = None
+        if GEMM_TRAFFIC_BYTES_PER_FLOP is not None:   # bytes per launch of the fc1 GEMM at this rank's rows
+            traffic = int(GEMM_TRAFFIC_BYTES_PER_FLOP * 2 * m_loc * D_MODEL * 2 * FFN)
+        roof = {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(gemm_tflops / peak, 4), "traffic": traffic,
+                "kernel": "gemm_q4k_tc_kernel", "peak_source": f"{src} bf16_tflops_sustained",
+                "gemm_share_of_step": round(float(mx[1]) / (ms * args.steps), 4)}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_K on the device, N(0,1) fp32 latent rows",
+            "config": {"workload": "BASELINE config 5: 50-block synthetic DiT trunk step (Q4_K GEMMs, AdaLN "
+                                   "rmsnorm+modulate, SwiGLU and gated-residual epilogues)",
+                       "blocks": args.blocks, "rows": M, "text_rows": T, "d_model": D_MODEL, "heads": 40,
+                       "head_dim": 128, "ffn": FFN, "weights_gb": round(trunk.weight_bytes / 1e9, 3),
+                       "step_gflop": round(total_flops / 1e9, 1), "parallelism": f"rows{world}",
+                       "l2": "inputs larger than L2 (11.87 GB of Q4_K weights streamed every step)",
+                       "trunk_build_s": round(t_build, 1)},
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(float(mx[3])), "clocks": clk, "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    """The reference's own CPU fh3_matmul (oracle/_ref, else the oracle port) on a bounded sample."""
+    import numpy as np
+
+    from fasth3inc_b200.trunk import D_MODEL, FFN, block_flops, block_shapes
+    from oracle import oracle as orc
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    o = orc.Oracle()
+    raw = {}
+    for i, (name, out, inn) in enumerate(block_shapes()):
+        raw[name] = o.make_weights(seed=0, stream=i + 1, rows=out, n=inn)
+    use_ref = orc.Reference.available()
+    rows_s = size_cpu_sample(raw, threads, use_ref, 5.0)
+    T = min(rows_s, args.text_rows)
+    for _ in range(args.warmup):
+        cpu_sample(raw, 16, 16, threads, use_ref)
+    times = []
+    kind = "reference" if use_ref else "port"
+    f = 0
+    for _ in range(args.steps):
+        f, dt, kind = cpu_sample(raw, rows_s, T, threads, use_ref)
+        times.append(dt)
+    dt = sum(times) / len(times)
+    value = f / dt / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_K on the host, N(0,1) fp32 rows",
+        "config": {"workload": "BASELINE config 5: 50-block synthetic DiT trunk step (bounded sample: one block's "
+                               "7 projections)", "blocks": args.blocks, "rows": args.rows,
+                   "text_rows": args.text_rows, "sample_rows": rows_s, "sample_text_rows": T,
+                   "full_step_gflop": round(args.blocks * block_flops(args.rows, args.text_rows) / 1e9, 1)},
+        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"fh3_matmul (OpenMP, {threads} threads) over block 0's 7 Q4_K projections on "
+                                   f"{rows_s} latent + {T} text rows, {f / 1e9:.1f} GFLOP per step"},
+        "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
