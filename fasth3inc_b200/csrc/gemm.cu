@@ -320,8 +320,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                     } else {
                         float* yr = static_cast<float*>(p.y) + m * p.ldy + n0;
                         if (p.epi == FH3CUDA_EPI_RESID) {
-                            for (int j = 0; j < 32; ++j)
-                                if (n0 + j < p.N) yr[j] = fmaf(p.gate[n0 + j], o[j], yr[j]);
+                            if (full && (p.ldy & 3) == 0) {
+                                // issue all 16 loads before the first store: y and gate may not
+                                // alias in a valid call, and batching them hides the latency
+                                const float4* g4 = reinterpret_cast<const float4*>(p.gate + n0);
+                                float4* y4 = reinterpret_cast<float4*>(yr);
+                                float4 hv[8], gv[8];
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) {
+                                    hv[j] = y4[j];
+                                    gv[j] = __ldg(g4 + j);
+                                }
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) {
+                                    hv[j].x = fmaf(gv[j].x, o[4 * j + 0], hv[j].x);
+                                    hv[j].y = fmaf(gv[j].y, o[4 * j + 1], hv[j].y);
+                                    hv[j].z = fmaf(gv[j].z, o[4 * j + 2], hv[j].z);
+                                    hv[j].w = fmaf(gv[j].w, o[4 * j + 3], hv[j].w);
+                                }
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) y4[j] = hv[j];
+                            } else {
+                                for (int j = 0; j < 32; ++j)
+                                    if (n0 + j < p.N) yr[j] = fmaf(p.gate[n0 + j], o[j], yr[j]);
+                            }
                         } else if (full && (p.ldy & 3) == 0) {
 #pragma unroll
                             for (int j = 0; j < 32; j += 4)
