@@ -29,7 +29,7 @@ EXPORTED = [
     "fh3cuda_matmul", "__wrap_fh3_matmul", "fh3cuda_register_weights", "fh3cuda_unregister_weights",
     "fh3cuda_upload_weights", "fh3cuda_release_weights", "fh3cuda_gemv_q4k_dev",
     "fh3cuda_gemm_q4k_dev", "fh3cuda_f32_to_bf16_dev", "fh3cuda_rmsnorm_modulate_dev",
-    "fh3cuda_swiglu_dev", "fh3cuda_make_q4k_weights_dev",
+    "fh3cuda_swiglu_dev", "fh3cuda_make_q4k_weights_dev", "fh3cuda_matmul_noalloc_dev",
 ]
 
 
@@ -74,6 +74,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         "fh3cuda_row_bytes": (ctypes.c_size_t, [c_int, i64]),
         "fh3cuda_dequant_dev": (c_int, [c_int, vp, vp, i64, i64, vp]),
         "fh3cuda_matmul_dev": (c_int, [Wp, vp, vp, c_int, vp, vp]),
+        "fh3cuda_matmul_noalloc_dev": (c_int, [Wp, vp, vp, c_int, vp, vp]),
         "fh3cuda_matmul": (None, [Wp, vp, vp, c_int, vp]),
         "__wrap_fh3_matmul": (None, [Wp, vp, vp, c_int, vp]),
         "fh3cuda_register_weights": (c_int, [vp, ctypes.c_size_t, vp]),

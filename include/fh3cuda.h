@@ -108,6 +108,19 @@ FH3CUDA_API int fh3cuda_dequant_dev(int type, const void *src, float *dst, int64
 FH3CUDA_API int fh3cuda_matmul_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
                        const float *bias_or_null, void *stream);
 
+/* fh3cuda_matmul_dev without device allocation on the call path: no counterpart in
+ * the reference.  For callers that cannot let a library call cudaMalloc while they
+ * run: hosts that budget device memory once up front, processes whose device memory
+ * belongs to another allocator, and latency-critical loops that cannot afford the
+ * device synchronisation cudaMalloc/cudaFree may cause.  The bf16 activation scratch
+ * is a fixed 8 MiB static device array (n_tok * in <= 4,194,304 when n_tok > 16;
+ * larger calls return FH3_E_INVALID), held by every GPU that loads the library.
+ * Set-up: fh3cuda_init(device), then the first call on a device resolves the array's
+ * address (make that first call before any stream capture).  All calls share the
+ * array: calls that overlap on the GPU race and must be serialised. */
+FH3CUDA_API int fh3cuda_matmul_noalloc_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
+                                           const float *bias_or_null, void *stream);
+
 /* The drop-in: same signature and meaning as fh3_matmul
  * (include/fh3/fh3.h:107) on HOST buffers.  w->data is looked up in the
  * registered weight ranges (fh3cuda_register_weights); an unregistered
