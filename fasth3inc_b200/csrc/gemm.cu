@@ -6,36 +6,45 @@
 //   y[m][n] = epi( sum_k A[m][k] * W[n][k] ),  A = activations (bf16, M x K),
 //   W = Q4_K rows (N x K), fp32 accumulation in tensor memory.
 //
-// One persistent CTA per SM walks 128 x 256 output tiles (grouped raster so
-// that concurrently running CTAs share weight tiles in L2).  Warp roles:
-//   warp 0      TMA producer: A tiles (128 x 64 bf16, 128-byte swizzle) and raw
-//               Q4_K tiles (256 rows x one 144-byte super-block = K 256).
-//   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma 128x256x16 per
-//               K-64 stage into one of two 256-column fp32 accumulators.
-//   warps 2-5   epilogue: tcgen05.ld accumulator rows -> bias / SwiGLU /
+// Two kernels share the dequantiser and the epilogue:
+//
+// gemm_q4k_pair_kernel (default for M > 128) -- a 2-CTA cluster on two SMs
+//   computes 256 x 256 tiles with tcgen05.mma.cta_group::2 (M = 256): each CTA
+//   holds 128 activation rows and dequantises only its 128 weight rows of the
+//   tile, so dequantisation and B-operand shared-memory traffic per SM are half
+//   of a one-SM 128 x 256 tile with the same tensor work.  The leader CTA (rank
+//   0) issues the MMAs; both CTAs' TMA activation loads count their bytes on the
+//   leader's barrier; the leader's commits arrive on both CTAs' barriers.
+// gemm_q4k_tc_kernel (M <= 128) -- one CTA per SM, 128 x 256 tiles.
+//
+// Warp roles (both kernels, one persistent CTA per SM, grouped tile raster so
+// concurrently running CTAs share weight tiles in L2):
+//   warp 0      TMA producer: bf16 activation tiles (128-byte swizzle) and raw
+//               Q4_K tiles (weight rows x one 144-byte super-block = K 256).
+//   warp 1      TMEM owner; MMA issuer (4 x K-16 MMAs per K-64 stage) into one
+//               of two 256-column fp32 accumulators.
+//   warps 2-5   epilogue: tcgen05.ld accumulator rows -> bias / bf16 / SwiGLU /
 //               gated residual -> global memory.
-//   warps 6-13  dequantisers: raw Q4_K in shared memory -> bf16 B operand
-//               in the UMMA K-major 128-byte-swizzle layout, one weight row
-//               per thread, fp32 FMA w = (d*sc)*q - dmin*m then one rounding
-//               to bf16 (the fp32 value equals fh3's dequant_q4_k output).
-// Every mbarrier wait is bounded (common.cuh); on a timeout the kernel flags
-// FH3CUDA_E_TIMEOUT, drains its own copies/MMAs, frees TMEM and returns.
+//   warps 6-13  dequantisers: raw Q4_K in shared memory -> bf16 B operand in the
+//               UMMA K-major 128-byte-swizzle layout.  byte_perm builds the fp32
+//               pattern 1 + q/128, an exact subtraction gives q/128, and one FMA
+//               with the exact scale 128*d*sc and offset -dmin*m gives fh3's fp32
+//               weight (dequant_q4_k, src/core/fh3_quant.c:154-196), then one
+//               rounding to bf16.
+// No TMA multicast anywhere.  Every mbarrier wait is bounded (common.cuh); on a
+// timeout the kernel flags FH3CUDA_E_TIMEOUT, drains its own copies/MMAs, frees
+// TMEM and returns.
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
 
 namespace {
 
-constexpr int BM = 128;            // tokens per tile (UMMA M)
-constexpr int BN = 256;            // weight rows per tile (UMMA N)
-constexpr int BK = 64;             // K per MMA stage: one 128-byte swizzle row of bf16
-constexpr int SA = 3;              // A stages
-constexpr int SB = 3;              // dequantised B stages
-constexpr int SR = 2;              // raw Q4_K stages
-constexpr int A_BYTES = BM * BK * 2;           // 16384
-constexpr int B_BYTES = BN * BK * 2;           // 32768
-constexpr int R_HALF = 128 * fh3::kQ4KBytes;   // 18432: one TMA box (128 rows x 144 B)
-constexpr int R_BYTES = 2 * R_HALF;            // 36864
+constexpr int BK = 64;                        // K per MMA stage: one 128-byte swizzle row of bf16
+constexpr int A_BYTES = 128 * BK * 2;         // 16384: 128 activation rows
+constexpr int R_HALF = 128 * fh3::kQ4KBytes;  // 18432: one TMA box (128 weight rows x 144 B)
 constexpr int kNumEpiWarps = 4;
 constexpr int kNumDqWarps = 8;
 constexpr int kEpiWarp0 = 2;
@@ -44,22 +53,9 @@ constexpr int kThreads = 32 * (kDqWarp0 + kNumDqWarps);  // 448
 constexpr int kTmemCols = 512;                           // two 256-column accumulators
 constexpr int kGroupM = 16;
 
-constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + SA * A_BYTES;
-constexpr int OFF_R = OFF_B + SB * B_BYTES;
-constexpr int OFF_BAR = OFF_R + SR * R_BYTES;
-// barriers: a_full[SA] a_empty[SA] b_full[SB] b_empty[SB] r_full[SR] r_empty[SR]
-//           acc_full[2] acc_empty[2] drain[1]
-constexpr int kNumBars = 2 * SA + 2 * SB + 2 * SR + 4 + 1;
-constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
-constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;  // + tmem slot/abort flag + alignment slack
-
-static_assert(OFF_B % 1024 == 0 && OFF_R % 1024 == 0, "operand stages must be 1024-byte aligned");
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-
 struct Params {
-    int64_t M, N, K;       // N = weight rows; for SwiGLU N = 2F
-    int64_t n_out;         // output columns (N, or F for SwiGLU)
+    int64_t M, N, K;  // N = weight rows; for SwiGLU N = 2F
+    int64_t n_out;    // output columns (N, or F for SwiGLU)
     int64_t ldy;
     const float* bias;
     const float* gate;
@@ -96,9 +92,176 @@ __device__ __forceinline__ float silu_ref(float g) {
     return g < -80.0f ? 0.0f : g / (1.0f + expf(-g));
 }
 
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Dequantise output chunks [j0, j0 + nj) of one weight row for K-64 stage `sub`
+// of a raw super-block into a 128-byte swizzled B row.  Chunk j holds k = 8j..8j+7;
+// chunks 0-3 come from the low nibbles (sub-block 2*sub), 4-7 from the high nibbles
+// (sub-block 2*sub+1).
+template <int J0, int NJ>
+__device__ __forceinline__ void dequant_row_stage(const uint8_t* raw, const uint4& hdr, int sub, uint8_t* brow,
+                                                  uint32_t swz) {
+    const float d = fh3::h2f_bits(hdr.x), dmin = fh3::h2f_bits(hdr.x >> 16);
+    float s[2], nm[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        if ((hh == 0 && J0 >= 4) || (hh == 1 && J0 + NJ <= 4)) continue;
+        int sc, m;
+        fh3::q4k_scale_min_words(hdr.y, hdr.z, hdr.w, 2 * sub + hh, sc, m);
+        s[hh] = __fmul_rn(d, static_cast<float>(sc)) * 128.0f;
+        nm[hh] = -__fmul_rn(dmin, static_cast<float>(m));
+    }
+    const uint4 q0 = *reinterpret_cast<const uint4*>(raw + 16 + sub * 32);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(raw + 32 + sub * 32);
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int j = J0; j < J0 + NJ; ++j) {
+        const int hh = j >> 2;
+        const uint32_t wa = qw[2 * (j & 3)], wb = qw[2 * (j & 3) + 1];
+        const uint32_t va = ((hh ? (wa >> 4) : wa) & 0x0F0F0F0Fu) | 0x80808080u;
+        const uint32_t vb = ((hh ? (wb >> 4) : wb) & 0x0F0F0F0Fu) | 0x80808080u;
+        const float sj = s[hh], nj = nm[hh];
+        uint4 pk;
+        pk.x = pack_bf16(fmaf(sj, fh3::nib_f(va, fh3::kSel0) - 1.0f, nj), fmaf(sj, fh3::nib_f(va, fh3::kSel1) - 1.0f, nj));
+        pk.y = pack_bf16(fmaf(sj, fh3::nib_f(va, fh3::kSel2) - 1.0f, nj), fmaf(sj, fh3::nib_f(va, fh3::kSel3) - 1.0f, nj));
+        pk.z = pack_bf16(fmaf(sj, fh3::nib_f(vb, fh3::kSel0) - 1.0f, nj), fmaf(sj, fh3::nib_f(vb, fh3::kSel1) - 1.0f, nj));
+        pk.w = pack_bf16(fmaf(sj, fh3::nib_f(vb, fh3::kSel2) - 1.0f, nj), fmaf(sj, fh3::nib_f(vb, fh3::kSel3) - 1.0f, nj));
+        // 16-byte chunk j of this 128-byte row, XOR-swizzled by row % 8
+        *reinterpret_cast<uint4*>(brow + ((static_cast<uint32_t>(j) ^ swz) << 4)) = pk;
+    }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* yr, const float* o) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        uint4 pk;
+        pk.x = pack_bf16(o[j], o[j + 1]);
+        pk.y = pack_bf16(o[j + 2], o[j + 3]);
+        pk.z = pack_bf16(o[j + 4], o[j + 5]);
+        pk.w = pack_bf16(o[j + 6], o[j + 7]);
+        *reinterpret_cast<uint4*>(yr + j) = pk;
+    }
+}
+
+// Drain one 256-column accumulator (this thread's TMEM lane = one output row) and apply
+// the epilogue.  `nb` is the tile's column block (256 weight rows, or 128 SwiGLU features).
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tbase, int64_t m, int64_t nb) {
+    const bool row_ok = m < p.M;
+    if (p.epi == FH3CUDA_EPI_SWIGLU) {
+        for (int cc = 0; cc < 4; ++cc) {
+            uint32_t v[32], g[32];
+            fh3::tmem_ld32(tbase + cc * 32, v);
+            fh3::tmem_ld32(tbase + 128 + cc * 32, g);
+            fh3::tmem_ld_wait();
+            const int64_t f0 = nb * 128 + cc * 32;
+            if (!row_ok || f0 >= p.n_out) continue;
+            __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy;
+            float o[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                float vv = __uint_as_float(v[j]), gg = __uint_as_float(g[j]);
+                if (p.bias) {
+                    const int64_t fj = f0 + j < p.n_out ? f0 + j : p.n_out - 1;
+                    vv += p.bias[fj];
+                    gg += p.bias[p.n_out + fj];
+                }
+                o[j] = vv * silu_ref(gg);
+            }
+            if (f0 + 32 <= p.n_out && (p.ldy & 7) == 0) {
+                store_bf16x32(yr + f0, o);
+            } else {
+                for (int j = 0; j < 32; ++j)
+                    if (f0 + j < p.n_out) yr[f0 + j] = __float2bfloat16_rn(o[j]);
+            }
+        }
+        return;
+    }
+    for (int cc = 0; cc < 8; ++cc) {
+        uint32_t v[32];
+        fh3::tmem_ld32(tbase + cc * 32, v);
+        fh3::tmem_ld_wait();
+        const int64_t n0 = nb * 256 + cc * 32;
+        if (!row_ok || n0 >= p.N) continue;
+        float o[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            o[j] = __uint_as_float(v[j]);
+            if (p.bias) o[j] += p.bias[n0 + j < p.N ? n0 + j : p.N - 1];
+        }
+        const bool full = n0 + 32 <= p.N;
+        if (p.epi == FH3CUDA_EPI_BF16) {
+            __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n0;
+            if (full && (p.ldy & 7) == 0) {
+                store_bf16x32(yr, o);
+            } else {
+                for (int j = 0; j < 32; ++j)
+                    if (n0 + j < p.N) yr[j] = __float2bfloat16_rn(o[j]);
+            }
+        } else {
+            float* yr = static_cast<float*>(p.y) + m * p.ldy + n0;
+            if (p.epi == FH3CUDA_EPI_RESID) {
+                if (full && (p.ldy & 3) == 0) {
+                    // issue all 16 loads before the first store: y and gate may not
+                    // alias in a valid call, and batching them hides the latency
+                    const float4* g4 = reinterpret_cast<const float4*>(p.gate + n0);
+                    float4* y4 = reinterpret_cast<float4*>(yr);
+                    float4 hv[8], gv[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        hv[j] = y4[j];
+                        gv[j] = __ldg(g4 + j);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        hv[j].x = fmaf(gv[j].x, o[4 * j + 0], hv[j].x);
+                        hv[j].y = fmaf(gv[j].y, o[4 * j + 1], hv[j].y);
+                        hv[j].z = fmaf(gv[j].z, o[4 * j + 2], hv[j].z);
+                        hv[j].w = fmaf(gv[j].w, o[4 * j + 3], hv[j].w);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) y4[j] = hv[j];
+                } else {
+                    for (int j = 0; j < 32; ++j)
+                        if (n0 + j < p.N) yr[j] = fmaf(p.gate[n0 + j], o[j], yr[j]);
+                }
+            } else if (full && (p.ldy & 3) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(yr + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+            } else {
+                for (int j = 0; j < 32; ++j)
+                    if (n0 + j < p.N) yr[j] = o[j];
+            }
+        }
+    }
+}
+
+// =============================================================================
+// one-SM kernel: 128 x 256 tiles
+// =============================================================================
+namespace one {
+constexpr int BM = 128, BN = 256;
+constexpr int SA = 3, SB = 3, SR = 2;
+constexpr int B_BYTES = BN * BK * 2;  // 32768
+constexpr int R_BYTES = 2 * R_HALF;   // 36864
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + SA * A_BYTES;
+constexpr int OFF_R = OFF_B + SB * B_BYTES;
+constexpr int OFF_BAR = OFF_R + SR * R_BYTES;
+constexpr int kNumBars = 2 * SA + 2 * SB + 2 * SR + 4 + 1;
+constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+static_assert(OFF_B % 1024 == 0 && OFF_R % 1024 == 0, "operand stages must be 1024-byte aligned");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+}  // namespace one
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                        const Params p) {
+    using namespace one;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -232,129 +395,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp < kDqWarp0) {
         // ------------------------------------------------------------ epilogue
-        const int q = warp & 3;                 // TMEM lane quarter this warp may access
-        const int row_in_tile = q * 32 + lane;
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
         Ring racc;
         for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             int64_t mb, nb;
             tile_coords(tile, num_m, num_n, mb, nb);
-            if (!fh3::mbar_wait(&acc_full[racc.idx], racc.phase, abort_flag, p.status)) break;
+            int ok = 1;
+            if (lane == 0) ok = fh3::mbar_wait(&acc_full[racc.idx], racc.phase, abort_flag, p.status);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
             fh3::tc_fence_after();
-            const int64_t m = mb * BM + row_in_tile;
-            const bool row_ok = m < p.M;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(racc.idx * BN);
-            if (swiglu) {
-                for (int cc = 0; cc < 4; ++cc) {
-                    uint32_t v[32], g[32];
-                    fh3::tmem_ld32(tbase + cc * 32, v);
-                    fh3::tmem_ld32(tbase + 128 + cc * 32, g);
-                    fh3::tmem_ld_wait();
-                    const int64_t f0 = nb * 128 + cc * 32;
-                    if (!row_ok) continue;
-                    __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy;
-                    float o[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        float vv = __uint_as_float(v[j]), gg = __uint_as_float(g[j]);
-                        if (p.bias) {
-                            const int64_t fj = f0 + j < p.n_out ? f0 + j : p.n_out - 1;
-                            vv += p.bias[fj];
-                            gg += p.bias[p.n_out + fj];
-                        }
-                        o[j] = vv * silu_ref(gg);
-                    }
-                    if (f0 + 32 <= p.n_out && (p.ldy & 7) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 8) {
-                            uint4 pk;
-                            __nv_bfloat162 b0 = __floats2bfloat162_rn(o[j], o[j + 1]);
-                            __nv_bfloat162 b1 = __floats2bfloat162_rn(o[j + 2], o[j + 3]);
-                            __nv_bfloat162 b2 = __floats2bfloat162_rn(o[j + 4], o[j + 5]);
-                            __nv_bfloat162 b3 = __floats2bfloat162_rn(o[j + 6], o[j + 7]);
-                            pk.x = *reinterpret_cast<uint32_t*>(&b0);
-                            pk.y = *reinterpret_cast<uint32_t*>(&b1);
-                            pk.z = *reinterpret_cast<uint32_t*>(&b2);
-                            pk.w = *reinterpret_cast<uint32_t*>(&b3);
-                            *reinterpret_cast<uint4*>(yr + f0 + j) = pk;
-                        }
-                    } else {
-                        for (int j = 0; j < 32; ++j)
-                            if (f0 + j < p.n_out) yr[f0 + j] = __float2bfloat16_rn(o[j]);
-                    }
-                }
-            } else {
-                for (int cc = 0; cc < BN / 32; ++cc) {
-                    uint32_t v[32];
-                    fh3::tmem_ld32(tbase + cc * 32, v);
-                    fh3::tmem_ld_wait();
-                    const int64_t n0 = nb * BN + cc * 32;
-                    if (!row_ok || n0 >= p.N) continue;
-                    float o[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        o[j] = __uint_as_float(v[j]);
-                        if (p.bias) o[j] += p.bias[n0 + j < p.N ? n0 + j : p.N - 1];
-                    }
-                    const bool full = n0 + 32 <= p.N;
-                    if (p.epi == FH3CUDA_EPI_BF16) {
-                        __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n0;
-                        if (full && (p.ldy & 7) == 0) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 8) {
-                                uint4 pk;
-                                __nv_bfloat162 b0 = __floats2bfloat162_rn(o[j], o[j + 1]);
-                                __nv_bfloat162 b1 = __floats2bfloat162_rn(o[j + 2], o[j + 3]);
-                                __nv_bfloat162 b2 = __floats2bfloat162_rn(o[j + 4], o[j + 5]);
-                                __nv_bfloat162 b3 = __floats2bfloat162_rn(o[j + 6], o[j + 7]);
-                                pk.x = *reinterpret_cast<uint32_t*>(&b0);
-                                pk.y = *reinterpret_cast<uint32_t*>(&b1);
-                                pk.z = *reinterpret_cast<uint32_t*>(&b2);
-                                pk.w = *reinterpret_cast<uint32_t*>(&b3);
-                                *reinterpret_cast<uint4*>(yr + j) = pk;
-                            }
-                        } else {
-                            for (int j = 0; j < 32; ++j)
-                                if (n0 + j < p.N) yr[j] = __float2bfloat16_rn(o[j]);
-                        }
-                    } else {
-                        float* yr = static_cast<float*>(p.y) + m * p.ldy + n0;
-                        if (p.epi == FH3CUDA_EPI_RESID) {
-                            if (full && (p.ldy & 3) == 0) {
-                                // issue all 16 loads before the first store: y and gate may not
-                                // alias in a valid call, and batching them hides the latency
-                                const float4* g4 = reinterpret_cast<const float4*>(p.gate + n0);
-                                float4* y4 = reinterpret_cast<float4*>(yr);
-                                float4 hv[8], gv[8];
-#pragma unroll
-                                for (int j = 0; j < 8; ++j) {
-                                    hv[j] = y4[j];
-                                    gv[j] = __ldg(g4 + j);
-                                }
-#pragma unroll
-                                for (int j = 0; j < 8; ++j) {
-                                    hv[j].x = fmaf(gv[j].x, o[4 * j + 0], hv[j].x);
-                                    hv[j].y = fmaf(gv[j].y, o[4 * j + 1], hv[j].y);
-                                    hv[j].z = fmaf(gv[j].z, o[4 * j + 2], hv[j].z);
-                                    hv[j].w = fmaf(gv[j].w, o[4 * j + 3], hv[j].w);
-                                }
-#pragma unroll
-                                for (int j = 0; j < 8; ++j) y4[j] = hv[j];
-                            } else {
-                                for (int j = 0; j < 32; ++j)
-                                    if (n0 + j < p.N) yr[j] = fmaf(p.gate[n0 + j], o[j], yr[j]);
-                            }
-                        } else if (full && (p.ldy & 3) == 0) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(yr + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-                        } else {
-                            for (int j = 0; j < 32; ++j)
-                                if (n0 + j < p.N) yr[j] = o[j];
-                        }
-                    }
-                }
-            }
+            epilogue_tile(p, tbase, mb * BM + q * 32 + lane, nb);
             fh3::tc_fence_before();
             __syncwarp();
             if (lane == 0) fh3::mbar_arrive(&acc_empty[racc.idx]);
@@ -368,53 +420,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
             for (int rs = 0; rs < ksteps / 4 && ok; ++rs) {
-                if (!(ok = fh3::mbar_wait(&r_full[rr.idx], rr.phase, abort_flag, p.status))) break;
+                int w = 1;
+                if (lane == 0) w = fh3::mbar_wait(&r_full[rr.idx], rr.phase, abort_flag, p.status);
+                if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
                 const uint8_t* raw = smem + OFF_R + rr.idx * R_BYTES + i * fh3::kQ4KBytes;
                 const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
-                const float d = fh3::h2f_bits(hdr.x), dmin = fh3::h2f_bits(hdr.x >> 16);
                 for (int sub = 0; sub < 4 && ok; ++sub) {
-                    // sub-blocks 2*sub (low nibbles) and 2*sub+1 (high nibbles)
-                    float s[2], nm[2];
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        int sc, m;
-                        fh3::q4k_scale_min_words(hdr.y, hdr.z, hdr.w, 2 * sub + hh, sc, m);
-                        s[hh] = __fmul_rn(d, static_cast<float>(sc)) * 128.0f;
-                        nm[hh] = -__fmul_rn(dmin, static_cast<float>(m));
-                    }
-                    const uint4 q0 = *reinterpret_cast<const uint4*>(raw + 16 + sub * 32);
-                    const uint4 q1 = *reinterpret_cast<const uint4*>(raw + 32 + sub * 32);
-                    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-                    if (!(ok = fh3::mbar_wait(&b_empty[rb.idx], rb.phase ^ 1u, abort_flag, p.status))) break;
-                    uint8_t* brow = smem + OFF_B + rb.idx * B_BYTES + i * 128;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int hh = j >> 2;                 // 0: low nibbles, 1: high
-                        const uint32_t wa = qw[2 * (j & 3)], wb = qw[2 * (j & 3) + 1];
-                        const uint32_t va = ((hh ? (wa >> 4) : wa) & 0x0F0F0F0Fu) | 0x80808080u;
-                        const uint32_t vb = ((hh ? (wb >> 4) : wb) & 0x0F0F0F0Fu) | 0x80808080u;
-                        const float sj = s[hh], nj = nm[hh];
-                        float w[8];
-                        w[0] = fmaf(sj, fh3::nib_f(va, fh3::kSel0) - 1.0f, nj);
-                        w[1] = fmaf(sj, fh3::nib_f(va, fh3::kSel1) - 1.0f, nj);
-                        w[2] = fmaf(sj, fh3::nib_f(va, fh3::kSel2) - 1.0f, nj);
-                        w[3] = fmaf(sj, fh3::nib_f(va, fh3::kSel3) - 1.0f, nj);
-                        w[4] = fmaf(sj, fh3::nib_f(vb, fh3::kSel0) - 1.0f, nj);
-                        w[5] = fmaf(sj, fh3::nib_f(vb, fh3::kSel1) - 1.0f, nj);
-                        w[6] = fmaf(sj, fh3::nib_f(vb, fh3::kSel2) - 1.0f, nj);
-                        w[7] = fmaf(sj, fh3::nib_f(vb, fh3::kSel3) - 1.0f, nj);
-                        __nv_bfloat162 p0 = __floats2bfloat162_rn(w[0], w[1]);
-                        __nv_bfloat162 p1 = __floats2bfloat162_rn(w[2], w[3]);
-                        __nv_bfloat162 p2 = __floats2bfloat162_rn(w[4], w[5]);
-                        __nv_bfloat162 p3 = __floats2bfloat162_rn(w[6], w[7]);
-                        uint4 pk;
-                        pk.x = *reinterpret_cast<uint32_t*>(&p0);
-                        pk.y = *reinterpret_cast<uint32_t*>(&p1);
-                        pk.z = *reinterpret_cast<uint32_t*>(&p2);
-                        pk.w = *reinterpret_cast<uint32_t*>(&p3);
-                        // 16-byte chunk j of this 128-byte row, XOR-swizzled by row % 8
-                        *reinterpret_cast<uint4*>(brow + ((static_cast<uint32_t>(j) ^ swz) << 4)) = pk;
-                    }
+                    if (lane == 0) w = fh3::mbar_wait(&b_empty[rb.idx], rb.phase ^ 1u, abort_flag, p.status);
+                    if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+                    dequant_row_stage<0, 8>(raw, hdr, sub, smem + OFF_B + rb.idx * B_BYTES + i * 128, swz);
                     fh3::fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) fh3::mbar_arrive(&b_full[rb.idx]);
@@ -435,8 +449,240 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// =============================================================================
+// two-SM kernel: 256 x 256 tiles over a CTA pair (tcgen05 cta_group::2)
+// =============================================================================
+namespace two {
+constexpr int BN = 256;                 // pair tile: 256 weight rows, 128 per CTA
+constexpr int SA = 5, SB = 5, SR = 3;
+constexpr int B_BYTES = 128 * BK * 2;   // 16384: this CTA's 128 weight rows
+constexpr int R_BYTES = R_HALF;         // 18432
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + SA * A_BYTES;
+constexpr int OFF_R = OFF_B + SB * B_BYTES;
+constexpr int OFF_BAR = OFF_R + SR * R_BYTES;
+constexpr int kNumBars = 2 * SA + 2 * SB + 2 * SR + 4 + 1;
+constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+static_assert(OFF_B % 1024 == 0 && OFF_R % 1024 == 0, "operand stages must be 1024-byte aligned");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+}  // namespace two
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_q4k_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                         const Params p) {
+    using namespace two;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* a_full = bars;             // leader: 1 arrival + both CTAs' A bytes
+    uint64_t* a_empty = a_full + SA;     // both: 1 (leader's commit)
+    uint64_t* b_full = a_empty + SA;     // leader: kNumDqWarps from each CTA
+    uint64_t* b_empty = b_full + SB;     // both: 1 (leader's commit)
+    uint64_t* r_full = b_empty + SB;     // local: 1 arrival + raw bytes
+    uint64_t* r_empty = r_full + SR;     // local: kNumDqWarps
+    uint64_t* acc_full = r_empty + SR;   // both: 1 (leader's commit)
+    uint64_t* acc_empty = acc_full + 2;  // leader: 2 x kNumEpiWarps
+    uint64_t* drain = acc_empty + 2;     // both: 1 (leader's commit)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t cr = fh3::cluster_ctarank();  // 0 = leader
+    const bool leader = cr == 0;
+    const bool swiglu = p.epi == FH3CUDA_EPI_SWIGLU;
+    const int64_t num_m = (p.M + 255) / 256;
+    const int64_t num_n = swiglu ? (p.n_out + 127) / 128 : (p.N + BN - 1) / BN;
+    const int64_t num_tiles = num_m * num_n;
+    const int ksteps = static_cast<int>(p.K / BK);
+    const int64_t pair = blockIdx.x >> 1;
+    const int64_t npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < SA; ++i) { fh3::mbar_init(&a_full[i], 1); fh3::mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < SB; ++i) {
+            fh3::mbar_init(&b_full[i], 2 * kNumDqWarps);
+            fh3::mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < SR; ++i) { fh3::mbar_init(&r_full[i], 1); fh3::mbar_init(&r_empty[i], kNumDqWarps); }
+        for (int i = 0; i < 2; ++i) { fh3::mbar_init(&acc_full[i], 1); fh3::mbar_init(&acc_empty[i], 2 * kNumEpiWarps); }
+        fh3::mbar_init(drain, 1);
+        *abort_flag = 0;
+        fh3::fence_mbar_init();
+    }
+    if (warp == 1) {
+        fh3::tmem_alloc_pair(tmem_slot, kTmemCols);
+        fh3::tmem_relinquish_pair();
+    }
+    if (warp == 0 && lane == 0) {
+        fh3::tma_prefetch_desc(&tmA);
+        fh3::tma_prefetch_desc(&tmW);
+    }
+    fh3::tc_fence_before();
+    fh3::cluster_sync_all();  // both CTAs' barriers initialised before any remote arrival
+    fh3::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer (both CTAs)
+        if (lane == 0) {
+            Ring ra, rr;
+            uint32_t r_filled = 0, r_par = 0, a_filled = 0, a_par = 0;
+            bool ok = true;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                int64_t mb, nb;
+                tile_coords(tile, num_m, num_n, mb, nb);
+                const int m0 = static_cast<int>(mb * 256 + cr * 128);
+                const int wrow = swiglu ? static_cast<int>(cr ? p.n_out + nb * 128 : nb * 128)
+                                        : static_cast<int>(nb * BN + cr * 128);
+                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                    if ((ks & 3) == 0) {
+                        if (!(ok = fh3::mbar_wait(&r_empty[rr.idx], rr.phase ^ 1u, abort_flag, p.status))) break;
+                        fh3::mbar_arrive_expect_tx(&r_full[rr.idx], R_BYTES);
+                        fh3::tma_load_2d(smem + OFF_R + rr.idx * R_BYTES, &tmW, &r_full[rr.idx],
+                                         (ks >> 2) * fh3::kQ4KBytes, wrow);
+                        r_filled |= 1u << rr.idx;
+                        r_par = (r_par & ~(1u << rr.idx)) | (rr.phase << rr.idx);
+                        rr.next<SR>();
+                    }
+                    if (!(ok = fh3::mbar_wait(&a_empty[ra.idx], ra.phase ^ 1u, abort_flag, p.status))) break;
+                    // both CTAs' activation bytes are counted on the leader's a_full
+                    if (leader) fh3::mbar_arrive_expect_tx(&a_full[ra.idx], 2 * A_BYTES);
+                    fh3::tma_load_2d_pair(smem + OFF_A + ra.idx * A_BYTES, &tmA,
+                                          fh3::mapa_shared(fh3::smem_u32(&a_full[ra.idx]), 0), ks * BK, m0);
+                    a_filled |= 1u << ra.idx;
+                    a_par = (a_par & ~(1u << ra.idx)) | (ra.phase << ra.idx);
+                    ra.next<SA>();
+                }
+            }
+            if (!ok) {
+                volatile int no_abort = 0;
+                for (int i = 0; i < SR; ++i)
+                    if (r_filled & (1u << i)) fh3::mbar_wait(&r_full[i], (r_par >> i) & 1u, &no_abort, nullptr);
+                // both CTAs' activation copies count on the leader's a_full: the leader waits
+                // for them, and the final cluster barrier keeps the peer resident until then
+                if (leader)
+                    for (int i = 0; i < SA; ++i)
+                        if (a_filled & (1u << i))
+                            fh3::mbar_wait_cluster(&a_full[i], (a_par >> i) & 1u, &no_abort, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (leader)
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = fh3::idesc_bf16_f32(256, BN);
+            Ring ra, rb, racc;
+            bool ok = true;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                if (!(ok = fh3::mbar_wait(&acc_empty[racc.idx], racc.phase ^ 1u, abort_flag, p.status))) break;
+                fh3::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(racc.idx * BN);
+                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                    if (!(ok = fh3::mbar_wait(&a_full[ra.idx], ra.phase, abort_flag, p.status))) break;
+                    if (!(ok = fh3::mbar_wait(&b_full[rb.idx], rb.phase, abort_flag, p.status))) break;
+                    fh3::tc_fence_after();
+                    const uint64_t ad = fh3::sdesc_sw128(fh3::smem_u32(smem + OFF_A + ra.idx * A_BYTES));
+                    const uint64_t bd = fh3::sdesc_sw128(fh3::smem_u32(smem + OFF_B + rb.idx * B_BYTES));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        fh3::umma_f16_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0 ? 1u : 0u);
+                    fh3::umma_commit_pair(&a_empty[ra.idx], 0x3);
+                    fh3::umma_commit_pair(&b_empty[rb.idx], 0x3);
+                    ra.next<SA>();
+                    rb.next<SB>();
+                }
+                if (ok) fh3::umma_commit_pair(&acc_full[racc.idx], 0x3);
+                racc.next<2>();
+            }
+            // every MMA of the pair retires before either CTA releases its TMEM
+            fh3::umma_commit_pair(drain, 0x3);
+        }
+        if (lane == 0) {
+            volatile int no_abort = 0;
+            fh3::mbar_wait_cluster(drain, 0, &no_abort, nullptr);
+        }
+    } else if (warp < kDqWarp0) {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int q = warp & 3;
+        const uint32_t acc_empty_leader = fh3::mapa_shared(fh3::smem_u32(acc_empty), 0);
+        Ring racc;
+        for (int64_t tile = pair; tile < num_tiles; tile += npairs) {
+            int64_t mb, nb;
+            tile_coords(tile, num_m, num_n, mb, nb);
+            int ok = 1;
+            if (lane == 0) ok = fh3::mbar_wait(&acc_full[racc.idx], racc.phase, abort_flag, p.status);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            fh3::tc_fence_after();
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(racc.idx * BN);
+            epilogue_tile(p, tbase, mb * 256 + cr * 128 + q * 32 + lane, nb);
+            fh3::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (leader) fh3::mbar_arrive(&acc_empty[racc.idx]);
+                else fh3::mbar_arrive_remote(acc_empty_leader + 8u * racc.idx);
+            }
+            racc.next<2>();
+        }
+    } else {
+        // ------------------------------------------------------------ dequantisers (both CTAs)
+        // 256 threads over this CTA's 128 weight rows: thread t takes row t % 128 and the
+        // low-nibble (t < 128) or high-nibble half of each K-64 stage.
+        const int t = threadIdx.x - kDqWarp0 * 32;
+        const int i = t & 127;
+        const bool high = t >= 128;
+        const uint32_t swz = static_cast<uint32_t>(i & 7);
+        const uint32_t b_full_leader = fh3::mapa_shared(fh3::smem_u32(b_full), 0);
+        Ring rr, rb;
+        bool ok = true;
+        for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+            for (int rs = 0; rs < ksteps / 4 && ok; ++rs) {
+                int w = 1;
+                if (lane == 0) w = fh3::mbar_wait(&r_full[rr.idx], rr.phase, abort_flag, p.status);
+                if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+                const uint8_t* raw = smem + OFF_R + rr.idx * R_BYTES + i * fh3::kQ4KBytes;
+                const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
+                for (int sub = 0; sub < 4 && ok; ++sub) {
+                    if (lane == 0) w = fh3::mbar_wait(&b_empty[rb.idx], rb.phase ^ 1u, abort_flag, p.status);
+                    if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+                    uint8_t* brow = smem + OFF_B + rb.idx * B_BYTES + i * 128;
+                    if (high) dequant_row_stage<4, 4>(raw, hdr, sub, brow, swz);
+                    else dequant_row_stage<0, 4>(raw, hdr, sub, brow, swz);
+                    fh3::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (leader) fh3::mbar_arrive(&b_full[rb.idx]);
+                        else fh3::mbar_arrive_remote(b_full_leader + 8u * rb.idx);
+                    }
+                    rb.next<SB>();
+                }
+                __syncwarp();
+                if (ok && lane == 0) fh3::mbar_arrive(&r_empty[rr.idx]);
+                rr.next<SR>();
+            }
+        }
+    }
+
+    fh3::tc_fence_before();
+    __syncthreads();
+    fh3::cluster_sync_all();  // the peer is done with our barriers and the pair's MMAs have retired
+    if (warp == 1) {
+        fh3::tc_fence_after();
+        fh3::tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+}
+
 std::once_flag g_attr_once;
 cudaError_t g_attr_err = cudaSuccess;
+int g_pair_clusters = 0;  // co-resident CTA pairs on device 0's layout (queried once)
+
+bool use_pair_kernel(int64_t n_tok) {
+    const char* e = getenv("FH3CUDA_GEMM_KERNEL");
+    if (e && strcmp(e, "1sm") == 0) return false;
+    if (e && strcmp(e, "2sm") == 0) return true;
+    return n_tok > 128;
+}
 
 }  // namespace
 
@@ -467,16 +713,34 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
 
     std::call_once(g_attr_once, [] {
         g_attr_err = cudaFuncSetAttribute(gemm_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          SMEM_BYTES);
+                                          one::SMEM_BYTES);
+        if (g_attr_err == cudaSuccess)
+            g_attr_err = cudaFuncSetAttribute(gemm_q4k_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              two::SMEM_BYTES);
+        if (g_attr_err == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = 2;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            cfg.gridDim = dim3(2, 1, 1);
+            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.dynamicSmemBytes = two::SMEM_BYTES;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            g_attr_err = cudaOccupancyMaxActiveClusters(&g_pair_clusters, gemm_q4k_pair_kernel, &cfg);
+        }
     });
-    if (g_attr_err != cudaSuccess) return check_cuda(g_attr_err, "cudaFuncSetAttribute(gemm)");
+    if (g_attr_err != cudaSuccess) return check_cuda(g_attr_err, "gemm kernel attributes");
 
+    const bool pair = use_pair_kernel(n_tok) && g_pair_clusters > 0;
     const size_t rb = fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, w->in);
     CUtensorMap tmA, tmW;
     {
         const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(w->in), static_cast<cuuint64_t>(n_tok)};
         const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(ldx) * 2};
-        const cuuint32_t box[2] = {BK, BM};
+        const cuuint32_t box[2] = {BK, 128};
         const cuuint32_t es[2] = {1, 1};
         CUresult r = encode_tiled(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x_bf16), gdim,
                                   gstr, box, es, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -502,10 +766,27 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
     p.y = y;
     p.epi = epi;
     p.status = ctx_status(c);
-    const int64_t num_m = (n_tok + BM - 1) / BM;
-    const int64_t num_n = epi == FH3CUDA_EPI_SWIGLU ? (n_out + 127) / 128 : (w->out + BN - 1) / BN;
-    const int64_t tiles = num_m * num_n;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t num_n = epi == FH3CUDA_EPI_SWIGLU ? (n_out + 127) / 128 : (w->out + 255) / 256;
+    if (pair) {
+        const int64_t tiles = ((n_tok + 255) / 256) * num_n;
+        const int64_t pairs = tiles < g_pair_clusters ? tiles : g_pair_clusters;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = two::SMEM_BYTES;
+        cfg.stream = s;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        return check_cuda(cudaLaunchKernelEx(&cfg, gemm_q4k_pair_kernel, tmA, tmW, p), "gemm_q4k_pair_kernel launch");
+    }
+    const int64_t tiles = ((n_tok + 127) / 128) * num_n;
     const int grid = static_cast<int>(tiles < ctx_sms(c) ? tiles : ctx_sms(c));
-    gemm_q4k_tc_kernel<<<grid, kThreads, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tmA, tmW, p);
+    gemm_q4k_tc_kernel<<<grid, kThreads, one::SMEM_BYTES, s>>>(tmA, tmW, p);
     return check_cuda(cudaGetLastError(), "gemm_q4k_tc_kernel launch");
 }

@@ -17,6 +17,14 @@ Q4K = 12
 TOL = 5e-3
 
 
+@pytest.fixture(autouse=True, params=["2sm", "1sm"])
+def gemm_kernel(request, monkeypatch):
+    """Run every test on both GEMM kernels: the CTA-pair (cta_group::2) kernel that serves
+    M > 128 by default, and the one-SM kernel that serves M <= 128."""
+    monkeypatch.setenv("FH3CUDA_GEMM_KERNEL", request.param)
+    return request.param
+
+
 def _w(fh3, raw, K, N):
     return fh3.Q4KWeight.from_bytes(raw, K, N)
 
