@@ -297,7 +297,7 @@ def run_ours(args):
             traffic = int(GEMM_TRAFFIC_BYTES_PER_FLOP * 2 * m_loc * D_MODEL * 2 * FFN)
         roof = {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(gemm_tflops / peak, 4), "traffic": traffic,
-                "kernel": "gemm_q4k_tc_kernel", "peak_source": f"{src} bf16_tflops_sustained",
+                "kernel": "gemm_q4k_pair_kernel", "peak_source": f"{src} bf16_tflops_sustained",
                 "gemm_share_of_step": round(float(mx[1]) / (ms * args.steps), 4)}
     if rank == 0:
         line = {

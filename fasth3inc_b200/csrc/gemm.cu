@@ -49,7 +49,9 @@ constexpr int kNumEpiWarps = 4;
 constexpr int kNumDqWarps = 8;
 constexpr int kEpiWarp0 = 2;
 constexpr int kDqWarp0 = kEpiWarp0 + kNumEpiWarps;
-constexpr int kThreads = 32 * (kDqWarp0 + kNumDqWarps);  // 448
+constexpr int kThreads = 32 * (kDqWarp0 + kNumDqWarps);  // 448 (one-SM kernel)
+constexpr int kRawWarp = kDqWarp0 + kNumDqWarps;         // pair kernel: raw-weight producer
+constexpr int kThreadsPair = 32 * (kRawWarp + 1);        // 480
 constexpr int kTmemCols = 512;                           // two 256-column accumulators
 constexpr int kGroupM = 16;
 
@@ -468,7 +470,7 @@ static_assert(OFF_B % 1024 == 0 && OFF_R % 1024 == 0, "operand stages must be 10
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 }  // namespace two
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsPair, 1)
     gemm_q4k_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                          const Params p) {
     using namespace two;
@@ -477,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* a_full = bars;             // leader: 1 arrival + both CTAs' A bytes
     uint64_t* a_empty = a_full + SA;     // both: 1 (leader's commit)
-    uint64_t* b_full = a_empty + SA;     // leader: kNumDqWarps from each CTA
+    uint64_t* b_full = a_empty + SA;     // leader: kNumDqWarps / 2 from each CTA
     uint64_t* b_empty = b_full + SB;     // both: 1 (leader's commit)
     uint64_t* r_full = b_empty + SB;     // local: 1 arrival + raw bytes
     uint64_t* r_empty = r_full + SR;     // local: kNumDqWarps
@@ -502,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < SA; ++i) { fh3::mbar_init(&a_full[i], 1); fh3::mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < SB; ++i) {
-            fh3::mbar_init(&b_full[i], 2 * kNumDqWarps);
+            fh3::mbar_init(&b_full[i], kNumDqWarps);  // one 4-warp group from each CTA
             fh3::mbar_init(&b_empty[i], 1);
         }
         for (int i = 0; i < SR; ++i) { fh3::mbar_init(&r_full[i], 1); fh3::mbar_init(&r_empty[i], kNumDqWarps); }
@@ -525,27 +527,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ producer (both CTAs)
+        // ------------------------------------------------------------ activation producer (both CTAs)
         if (lane == 0) {
-            Ring ra, rr;
-            uint32_t r_filled = 0, r_par = 0, a_filled = 0, a_par = 0;
+            Ring ra;
+            uint32_t a_filled = 0, a_par = 0;
             bool ok = true;
             for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
                 int64_t mb, nb;
                 tile_coords(tile, num_m, num_n, mb, nb);
                 const int m0 = static_cast<int>(mb * 256 + cr * 128);
-                const int wrow = swiglu ? static_cast<int>(cr ? p.n_out + nb * 128 : nb * 128)
-                                        : static_cast<int>(nb * BN + cr * 128);
                 for (int ks = 0; ks < ksteps && ok; ++ks) {
-                    if ((ks & 3) == 0) {
-                        if (!(ok = fh3::mbar_wait(&r_empty[rr.idx], rr.phase ^ 1u, abort_flag, p.status))) break;
-                        fh3::mbar_arrive_expect_tx(&r_full[rr.idx], R_BYTES);
-                        fh3::tma_load_2d(smem + OFF_R + rr.idx * R_BYTES, &tmW, &r_full[rr.idx],
-                                         (ks >> 2) * fh3::kQ4KBytes, wrow);
-                        r_filled |= 1u << rr.idx;
-                        r_par = (r_par & ~(1u << rr.idx)) | (rr.phase << rr.idx);
-                        rr.next<SR>();
-                    }
                     if (!(ok = fh3::mbar_wait(&a_empty[ra.idx], ra.phase ^ 1u, abort_flag, p.status))) break;
                     // both CTAs' activation bytes are counted on the leader's a_full
                     if (leader) fh3::mbar_arrive_expect_tx(&a_full[ra.idx], 2 * A_BYTES);
@@ -558,14 +549,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok) {
                 volatile int no_abort = 0;
-                for (int i = 0; i < SR; ++i)
-                    if (r_filled & (1u << i)) fh3::mbar_wait(&r_full[i], (r_par >> i) & 1u, &no_abort, nullptr);
                 // both CTAs' activation copies count on the leader's a_full: the leader waits
                 // for them, and the final cluster barrier keeps the peer resident until then
                 if (leader)
                     for (int i = 0; i < SA; ++i)
                         if (a_filled & (1u << i))
                             fh3::mbar_wait_cluster(&a_full[i], (a_par >> i) & 1u, &no_abort, nullptr);
+            }
+        }
+    } else if (warp == kRawWarp) {
+        // ------------------------------------------------------------ raw-weight producer (both CTAs)
+        // Runs ahead of the activation loads by up to SR super-blocks, so the dequantisers
+        // never wait behind a full activation ring.
+        if (lane == 0) {
+            Ring rr;
+            uint32_t r_filled = 0, r_par = 0;
+            bool ok = true;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                int64_t mb, nb;
+                tile_coords(tile, num_m, num_n, mb, nb);
+                const int wrow = swiglu ? static_cast<int>(cr ? p.n_out + nb * 128 : nb * 128)
+                                        : static_cast<int>(nb * BN + cr * 128);
+                for (int rs = 0; rs < ksteps / 4 && ok; ++rs) {
+                    if (!(ok = fh3::mbar_wait(&r_empty[rr.idx], rr.phase ^ 1u, abort_flag, p.status))) break;
+                    fh3::mbar_arrive_expect_tx(&r_full[rr.idx], R_BYTES);
+                    fh3::tma_load_2d(smem + OFF_R + rr.idx * R_BYTES, &tmW, &r_full[rr.idx],
+                                     rs * fh3::kQ4KBytes, wrow);
+                    r_filled |= 1u << rr.idx;
+                    r_par = (r_par & ~(1u << rr.idx)) | (rr.phase << rr.idx);
+                    rr.next<SR>();
+                }
+            }
+            if (!ok) {
+                volatile int no_abort = 0;
+                for (int i = 0; i < SR; ++i)
+                    if (r_filled & (1u << i)) fh3::mbar_wait(&r_full[i], (r_par >> i) & 1u, &no_abort, nullptr);
             }
         }
     } else if (warp == 1) {
@@ -627,35 +645,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ dequantisers (both CTAs)
-        // 256 threads over this CTA's 128 weight rows: thread t takes row t % 128 and the
-        // low-nibble (t < 128) or high-nibble half of each K-64 stage.
+        // Two groups of 4 warps over this CTA's 128 weight rows, one row per thread: group g
+        // dequantises the K-64 stages with index % 2 == g (two stages in flight, a whole
+        // 128-byte row of work per thread per stage).
         const int t = threadIdx.x - kDqWarp0 * 32;
+        const int grp = t >> 7;
         const int i = t & 127;
-        const bool high = t >= 128;
         const uint32_t swz = static_cast<uint32_t>(i & 7);
         const uint32_t b_full_leader = fh3::mapa_shared(fh3::smem_u32(b_full), 0);
-        Ring rr, rb;
+        Ring rr;
+        uint32_t s_base = 0;  // index of the first K-64 stage of the current raw stage
         bool ok = true;
         for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
-            for (int rs = 0; rs < ksteps / 4 && ok; ++rs) {
+            for (int rs = 0; rs < ksteps / 4 && ok; ++rs, s_base += 4) {
                 int w = 1;
                 if (lane == 0) w = fh3::mbar_wait(&r_full[rr.idx], rr.phase, abort_flag, p.status);
                 if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
                 const uint8_t* raw = smem + OFF_R + rr.idx * R_BYTES + i * fh3::kQ4KBytes;
                 const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
-                for (int sub = 0; sub < 4 && ok; ++sub) {
-                    if (lane == 0) w = fh3::mbar_wait(&b_empty[rb.idx], rb.phase ^ 1u, abort_flag, p.status);
+                for (int sub = grp; sub < 4 && ok; sub += 2) {
+                    const uint32_t s = s_base + static_cast<uint32_t>(sub);
+                    const uint32_t bi = s % SB;
+                    const uint32_t bph = (s / SB) & 1u;
+                    if (lane == 0) w = fh3::mbar_wait(&b_empty[bi], bph ^ 1u, abort_flag, p.status);
                     if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
-                    uint8_t* brow = smem + OFF_B + rb.idx * B_BYTES + i * 128;
-                    if (high) dequant_row_stage<4, 4>(raw, hdr, sub, brow, swz);
-                    else dequant_row_stage<0, 4>(raw, hdr, sub, brow, swz);
+                    dequant_row_stage<0, 8>(raw, hdr, sub, smem + OFF_B + bi * B_BYTES + i * 128, swz);
                     fh3::fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        if (leader) fh3::mbar_arrive(&b_full[rb.idx]);
-                        else fh3::mbar_arrive_remote(b_full_leader + 8u * rb.idx);
+                        if (leader) fh3::mbar_arrive(&b_full[bi]);
+                        else fh3::mbar_arrive_remote(b_full_leader + 8u * bi);
                     }
-                    rb.next<SB>();
                 }
                 __syncwarp();
                 if (ok && lane == 0) fh3::mbar_arrive(&r_empty[rr.idx]);
@@ -725,7 +745,7 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
             at[0].val.clusterDim.y = 1;
             at[0].val.clusterDim.z = 1;
             cfg.gridDim = dim3(2, 1, 1);
-            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.blockDim = dim3(kThreadsPair, 1, 1);
             cfg.dynamicSmemBytes = two::SMEM_BYTES;
             cfg.attrs = at;
             cfg.numAttrs = 1;
@@ -778,7 +798,7 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
         at[0].val.clusterDim.y = 1;
         at[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.blockDim = dim3(kThreadsPair, 1, 1);
         cfg.dynamicSmemBytes = two::SMEM_BYTES;
         cfg.stream = s;
         cfg.attrs = at;
