@@ -66,6 +66,30 @@ __device__ __forceinline__ float nib_f(uint32_t v, uint32_t sel) {
 constexpr uint32_t kSel0 = 0x7044, kSel1 = 0x7144, kSel2 = 0x7244, kSel3 = 0x7344;
 
 // ---------------------------------------------------------------------------
+// packed fp32x2 arithmetic (sm_100): two IEEE fp32 operations per instruction
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// ---------------------------------------------------------------------------
 // timing / status
 // ---------------------------------------------------------------------------
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far above any legitimate wait
