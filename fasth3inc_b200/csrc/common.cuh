@@ -171,6 +171,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16),
+// completion bytes counted on `bar`.  No multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -371,5 +380,4 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
                       const cuuint64_t* gdim, const cuuint64_t* gstride, const cuuint32_t* box,
                       const cuuint32_t* estride, CUtensorMapSwizzle swz);
 // scratch of at least `bytes` for slot `slot` (cached, grows)
-void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
-}  // namespace fh3host
+void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s);}  // namespace fh3host

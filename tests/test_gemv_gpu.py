@@ -14,6 +14,15 @@ from conftest import read_matmul_golden, rel_fro
 pytestmark = pytest.mark.gpu
 Q4K = 12
 TOL = 1e-5
+_PATH = {"kernel": "fp32"}
+
+
+@pytest.fixture(autouse=True, params=["matmul", "gemv"])
+def gemv_path(request):
+    """Every test runs through both entry points that reach the small-M kernel: the
+    dispatcher (fh3cuda_matmul_dev, 1..16 tokens) and fh3cuda_gemv_q4k_dev."""
+    _PATH["kernel"] = request.param
+    return request.param
 
 
 def _run(fh3, w_raw, K, N, x, bias=None):
@@ -21,7 +30,7 @@ def _run(fh3, w_raw, K, N, x, bias=None):
     w = fh3.Q4KWeight.from_bytes(w_raw, K, N)
     xt = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
     bt = None if bias is None else torch.from_numpy(np.ascontiguousarray(bias, dtype=np.float32)).cuda()
-    y = fh3.gemv(w, xt, bt)
+    y = fh3.matmul(w, xt, bt) if _PATH["kernel"] == "matmul" else fh3.gemv(w, xt, bt)
     torch.cuda.synchronize()
     return y.cpu().numpy()
 
@@ -82,3 +91,18 @@ def test_rejects_bad_arguments(fh3, oracle):
     bad = fh3.Q4KWeight(w.data, 300, 4)  # in not a multiple of 256
     with pytest.raises(fh3.Fh3CudaError):
         fh3.gemv(bad, x[:1, :256])
+
+
+def test_activation_ranges_and_zero_groups(fh3, oracle):
+    """Per-16-element scales of the integer path: huge, tiny, zero and mixed-magnitude rows."""
+    K, N, M = 1024, 70, 4
+    w = oracle.make_weights(seed=9, stream=1, rows=N, n=K)
+    x = oracle.rng_normal(9, 2, M * K).reshape(M, K).astype(np.float32)
+    x[0] *= 3.0e4          # large activations
+    x[1] *= 1.0e-6         # tiny activations
+    x[2, :512] = 0.0       # whole zero groups
+    x[3, ::7] *= 1000.0    # mixed magnitudes inside groups
+    ref = oracle.matmul(Q4K, w, K, N, x)
+    got = _run(fh3, w, K, N, x)
+    for t in range(M):
+        assert rel_fro(got[t], ref[t]) <= TOL, t
