@@ -40,6 +40,17 @@ __device__ __forceinline__ void dot_piece(const uint4 (&hdr)[R], const uint4 (&q
             s2[r] = fh3::f2_pack(s, s);
             nm2[r] = fh3::f2_pack(nm, nm);
         }
+        // activations of this half-piece, loaded before the arithmetic (one L1 round trip
+        // per half instead of one per 4 weights); M <= 4 keeps them in registers
+        constexpr int XP = M <= 4 ? M : 1;
+        float4 xpre[XP][4];
+        if (M <= 4) {
+#pragma unroll
+            for (int t = 0; t < XP; ++t)
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                    xpre[t][g] = __ldg(reinterpret_cast<const float4*>(xk + half * 32 + t * K + 4 * g));
+        }
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
             uint64_t w01[R], w23[R];
@@ -54,7 +65,8 @@ __device__ __forceinline__ void dot_piece(const uint4 (&hdr)[R], const uint4 (&q
             }
 #pragma unroll
             for (int t = 0; t < M; ++t) {
-                const float4 xv = __ldg(reinterpret_cast<const float4*>(xk + half * 32 + t * K + 4 * g));
+                const float4 xv = M <= 4 ? xpre[M <= 4 ? t : 0][g]
+                                         : __ldg(reinterpret_cast<const float4*>(xk + half * 32 + t * K + 4 * g));
                 const uint64_t x01 = fh3::f2_pack(xv.x, xv.y);
                 const uint64_t x23 = fh3::f2_pack(xv.z, xv.w);
 #pragma unroll
