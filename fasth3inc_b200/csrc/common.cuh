@@ -380,4 +380,8 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
                       const cuuint64_t* gdim, const cuuint64_t* gstride, const cuuint32_t* box,
                       const cuuint32_t* estride, CUtensorMapSwizzle swz);
 // scratch of at least `bytes` for slot `slot` (cached, grows)
-void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s);}  // namespace fh3host
+void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
+// 1..16-token Q4_K GEMV on warp-level tensor-core MMAs (gemv_mma.cu); arguments
+// already validated by the caller
+int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
+}  // namespace fh3host

@@ -16,6 +16,9 @@
 // since d*sc*q is exact) and the dot-product FMAs, two weights per instruction.
 // Lane partial sums are reduced by shuffles, warp partials through shared memory
 // in a fixed order, so the result is deterministic.
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 
 namespace {
@@ -173,6 +176,10 @@ extern "C" int fh3cuda_gemv_q4k_dev(const Fh3CudaW* w, const float* x, float* y,
     if ((reinterpret_cast<uintptr_t>(w->data) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
         return set_error(FH3_E_INVALID, "fh3cuda_gemv_q4k_dev: weights and x must be 16-byte aligned");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // FH3CUDA_GEMV_KERNEL=fp32 selects the CUDA-core kernel below; the default is the
+    // tensor-core kernel of gemv_mma.cu
+    const char* kernel = getenv("FH3CUDA_GEMV_KERNEL");
+    if (!(kernel && strcmp(kernel, "fp32") == 0)) return gemv_mma(w, x, y, n_tok, bias, s);
     switch (n_tok) {
         case 1: return launch<1, 4>(w, x, y, bias, s);
         case 2: return launch<2, 4>(w, x, y, bias, s);

@@ -1,0 +1,591 @@
+// gemv_mma.cu -- Q4_K GEMV (1..16 tokens) on warp-level tensor-core MMAs with
+// exact operands.
+//
+// The small-M regime of fh3_matmul (src/core/fh3_ops.c:317-404) streams 4.5-bit
+// weights; at B200's HBM rate that leaves under three warp instructions per 32
+// weights, which a float dequantisation plus dot product exceeds.  Here:
+//
+//   y[t][n] = sum_j ( dl_nj * P_tnj - ml_nj * X_tj ),  P = sum_{k in j} q_nk x_tk,
+//   X_tj = sum_{k in j} x_tk  (32-weight sub-blocks j; w = dl*q - ml as in
+//   dequant_q4_k, src/core/fh3_quant.c:154-196)
+//
+// * A operand = the nibbles themselves: (word & 0x000F000F) is a pair of fp16
+//   subnormals q * 2^-24, exact; high nibbles (word & 0x00F000F0) are 16 q * 2^-24.
+//   Eight weights cost one shift and four ANDs.
+// * B operand = x split into two fp16 planes x*2^s = h0 + h1 (22 significant bits)
+//   under a per-token power of two 2^s that puts max|x| just below 2^14.
+// * mma.sync.m16n8k16 (fp16 x fp16 -> fp32): a product of a 4-bit integer and an
+//   11-bit significand is exact; per sub-block two MMAs (k = 32) into a zeroed
+//   accumulator give the plane sums of P in fp32.  acc += dl*(P0 + P1) - ml*X',
+//   X' = X * 2^(s-24), and y = acc * 2^(24-s) (+ bias).
+//
+// Two launches per call:
+// * gemv_mma_prep_kernel (grid: 2048-element slices x tokens) writes the planes in
+//   the lane order of the mma B fragment, the scaled sub-block sums X' and the
+//   exponents.  It triggers the main kernel's launch at once (programmatic
+//   dependent launch), so the main kernel's first weight loads overlap it.
+// * gemv_mma_kernel: a CTA owns a 16-row tile and a K range; its warps stride over
+//   the range's super-blocks with the next super-block's bytes in flight.  After
+//   griddepcontrol.wait the CTA copies its range of B fragments and X' into shared
+//   memory (cp.async), so a sub-block's B operand is one conflict-free 16-byte
+//   shared load.  When the fragments of the whole K would not fit, a cluster of S
+//   CTAs splits K and the partial sums meet over distributed shared memory.
+//   Every sum runs in a fixed order (deterministic results).
+//
+// Fragment layout of a sub-block (32 elements i = 8tq + 4st + r): lane tq of a quad
+// loads bytes 8tq..8tq+7 of the sub-block pair's 32-byte chunk; word st gives
+// a0 = bytes {0,2} (k slots 2tq, 2tq+1) and a2 = bytes {1,3} (k slots 2tq+8,
+// 2tq+9).  The B fragment uses the same slots, so the k order inside a sub-block
+// is permuted identically on both sides and the dot products are unchanged.
+// B fragments are stored compactly: sub-block sb, column col = 2*token + plane,
+// lane tq -> frag[sb * 8M + col * 4 + tq] (16 bytes: halves for k-step 0 then 1).
+#include "common.cuh"
+
+namespace {
+
+#ifndef FH3_GV_MIN_BLOCKS
+#define FH3_GV_MIN_BLOCKS 3  // resident CTAs per SM the register budget is sized for
+#endif
+#ifndef FH3_GV_SMEM_KB
+#define FH3_GV_SMEM_KB 64    // shared-memory bytes per CTA above which a cluster splits K
+#endif
+constexpr int kGvMaxWarps = 8;
+constexpr int kPrepSlice = 2048;  // elements of one token per prep CTA
+constexpr size_t kGvSmemTarget = FH3_GV_SMEM_KB * 1024;
+
+// half p (0..7) of a lane's 16-byte B fragment holds element 8tq + perm8(p) of the
+// sub-block (perm8 is its own inverse: it swaps 1<->2 and 5<->6)
+__host__ __device__ constexpr int perm8(int p) { return (p == 1 || p == 2 || p == 5 || p == 6) ? (p ^ 3) : p; }
+
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(fh3::smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
+    return static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// grid (ceil(K / 2048), M), 256 threads: thread -> 8 consecutive elements (one lane's
+// fragment of one sub-block); 4 consecutive threads cover a sub-block, a warp a
+// super-block.
+__global__ void __launch_bounds__(256) gemv_mma_prep_kernel(const float* __restrict__ x, int64_t K, int M,
+                                                            uint4* __restrict__ frag, uint32_t* __restrict__ mfrag,
+                                                            int* __restrict__ expo) {
+    pdl_launch_dependents();
+    __shared__ float red[8];
+    const int t = blockIdx.y;
+    const int lane = threadIdx.x & 31;
+    const float4* x4 = reinterpret_cast<const float4*>(x + static_cast<int64_t>(t) * K);
+    float amax = 0.0f;
+    {
+        const int64_t n4 = K / 4;
+        int64_t i = threadIdx.x;
+        for (; i + 3 * 256 < n4; i += 4 * 256) {  // four loads in flight per thread
+            const float4 a = __ldg(x4 + i), b = __ldg(x4 + i + 256), c = __ldg(x4 + i + 512), d = __ldg(x4 + i + 768);
+            amax = fmaxf(amax, fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
+                                     fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w)))));
+            amax = fmaxf(amax, fmaxf(fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(c.z), fabsf(c.w))),
+                                     fmaxf(fmaxf(fabsf(d.x), fabsf(d.y)), fmaxf(fabsf(d.z), fabsf(d.w)))));
+        }
+        for (; i < n4; i += 256) {
+            const float4 a = __ldg(x4 + i);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
+    int E = 0;
+    if (amax > 0.0f && amax <= 3.0e38f) frexpf(amax, &E);  // amax < 2^E
+    const int s = 14 - E;                                    // max|x| * 2^s < 2^14
+
+    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kPrepSlice + threadIdx.x * 8;
+    if (k0 < K) {  // K % 256 == 0: whole warps (super-blocks) are in or out
+        const float4 v0 = __ldg(x4 + k0 / 4), v1 = __ldg(x4 + k0 / 4 + 1);
+        const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t pl0[4], pl1[4];
+#pragma unroll
+        for (int p = 0; p < 8; p += 2) {
+            __half h0[2], h1[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const float v = ldexpf(e[perm8(p + u)], s);
+                h0[u] = __float2half_rn(v);
+                h1[u] = __float2half_rn(v - __half2float(h0[u]));
+            }
+            pl0[p / 2] = pack_half2(h0[0], h0[1]);
+            pl1[p / 2] = pack_half2(h1[0], h1[1]);
+        }
+        const int64_t sb = k0 >> 5;
+        const int tq = lane & 3;
+        const int64_t base = sb * 8 * M + 2 * t * 4 + tq;
+        frag[base] = make_uint4(pl0[0], pl0[1], pl0[2], pl0[3]);
+        frag[base + 4] = make_uint4(pl1[0], pl1[1], pl1[2], pl1[3]);
+        // sub-block sums X_j (lanes 4j..4j+3 hold sub-block j of this super-block)
+        float sum = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        // min-term B fragment: lane q (0..3) of a column holds (X_2q, X_2q+1) * 2^(s-5),
+        // split into two fp16 planes like x
+        const float xa = __shfl_sync(0xffffffffu, sum, 8 * (lane & 3));
+        const float xb = __shfl_sync(0xffffffffu, sum, 8 * (lane & 3) + 4);
+        if (lane < 4) {
+            const float va = ldexpf(xa, s - 5), vb = ldexpf(xb, s - 5);
+            const __half a0 = __float2half_rn(va), b0 = __float2half_rn(vb);
+            const __half a1 = __float2half_rn(va - __half2float(a0)), b1 = __float2half_rn(vb - __half2float(b0));
+            const int64_t mb = (k0 >> 8) * 8 * M + 2 * t * 4 + lane;
+            mfrag[mb] = pack_half2(a0, b0);
+            mfrag[mb + 4] = pack_half2(a1, b1);
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) expo[t] = 24 - s;
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// the same with a zero accumulator input
+__device__ __forceinline__ void mma_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+    const float z = 0.0f;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+// Raw bytes of one super-block for this lane: nibble words of rows g and g+8 for the
+// four chunks, and the 16-byte headers.
+struct SuperBlock {
+    uint2 q[2][4];
+    uint4 hd[2];
+};
+
+__device__ __forceinline__ void load_sb(SuperBlock& sbk, const uint8_t* row0, const uint8_t* row1, int b, int tq) {
+    const uint8_t* p0 = row0 + static_cast<size_t>(b) * fh3::kQ4KBytes;
+    const uint8_t* p1 = row1 + static_cast<size_t>(b) * fh3::kQ4KBytes;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        sbk.q[0][c] = __ldg(reinterpret_cast<const uint2*>(p0 + 16 + c * 32 + 8 * tq));
+        sbk.q[1][c] = __ldg(reinterpret_cast<const uint2*>(p1 + 16 + c * 32 + 8 * tq));
+    }
+    sbk.hd[0] = __ldg(reinterpret_cast<const uint4*>(p0));
+    sbk.hd[1] = __ldg(reinterpret_cast<const uint4*>(p1));
+}
+
+// Per-lane constants of the scale decode and the B-fragment slots.
+template <int NT>
+struct LaneCtx {
+    int slot[NT];      // B-fragment slot of this lane in tile nt (clamped into the live range)
+    uint32_t sel_sc0;  // byte_perm selectors: scale byte 2(tq&1) / 2(tq&1)+1 -> float 2^23 + byte
+    uint32_t sel_sc1;
+    uint32_t sel_m;    // min bytes 2(tq&1), 2(tq&1)+1 -> fp16 pair of integers (subnormals m * 2^-24)
+    bool lo;           // tq < 2: sub-blocks 0..3 (low scale words), else 4..7
+};
+
+template <int NT>
+__device__ __forceinline__ LaneCtx<NT> lane_ctx(int lane, int lanes) {
+    LaneCtx<NT> lc;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) lc.slot[nt] = min(nt * 32 + lane, lanes - 1);
+    const uint32_t k0 = 2u * (lane & 1 ? 1u : 0u);
+    lc.sel_sc0 = 0x5440u | k0;
+    lc.sel_sc1 = 0x5440u | (k0 + 1);
+    lc.sel_m = k0 | 0x40u | ((k0 + 1) << 8) | 0x4000u;
+    lc.lo = (lane & 3) < 2;
+    return lc;
+}
+
+// One super-block of rows g, g+8 against all tokens.  fsb: B fragments of the
+// super-block's 8 sub-blocks (stride `lanes` uint4), msb: its min-term B fragments.
+template <int NT, int LANES = 0>  // LANES: fragment slots per sub-block when known at compile time
+__device__ __forceinline__ void compute_sb(const SuperBlock& sbk, int lane, int lanes_rt, const LaneCtx<NT>& lc,
+                                           const uint4* __restrict__ fsb, const uint32_t* __restrict__ msb,
+                                           float (&acc)[2][NT]) {
+    const int lanes = LANES > 0 ? LANES : lanes_rt;
+    // lane tq decodes the scales of its sub-blocks 2tq, 2tq+1 (rows g, g+8) and the
+    // min-term A fragment; 6-bit fields as in get_scale_min_k4 (src/core/fh3_quant.c)
+    float dl[2][2];
+    uint32_t am[2];
+    float dm32[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint4 h = sbk.hd[i];
+        const float d = fh3::h2f_bits(h.x), dmin = fh3::h2f_bits(h.x >> 16);
+        const uint32_t scw = lc.lo ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
+        const uint32_t mw = lc.lo ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+        const float sc0 = __uint_as_float(__byte_perm(scw, 0x4B00u, lc.sel_sc0)) - 8388608.0f;  // exact
+        const float sc1 = __uint_as_float(__byte_perm(scw, 0x4B00u, lc.sel_sc1)) - 8388608.0f;
+        dl[i][0] = d * sc0;                // exact (17 significant bits), the fp32 value fh3 uses
+        dl[i][1] = (d * 0.0625f) * sc1;    // high nibbles enter the MMA as 16 q
+        am[i] = __byte_perm(mw, 0u, lc.sel_m);
+        dm32[i] = dmin * 32.0f;
+    }
+    // min term: one k16 MMA over the 8 sub-blocks (k slots 8..15 zero)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        float dm[4];
+        mma_16816_z(dm, am[0], am[1], 0u, 0u, msb[lc.slot[nt]], 0u);
+        acc[0][nt] = fmaf(-dm32[0], dm[0] + dm[1], acc[0][nt]);
+        acc[1][nt] = fmaf(-dm32[1], dm[2] + dm[3], acc[1][nt]);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        // scales of sub-blocks 2c, 2c+1 were decoded by lane tq == c of this row group
+        float dlc[2][2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) dlc[i][hh] = __shfl_sync(0xffffffffu, dl[i][hh], c, 4);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const uint4* fs = fsb + (2 * c + hh) * lanes;
+            const uint32_t mask = hh ? 0x00F000F0u : 0x000F000Fu;
+            const uint32_t a00 = sbk.q[0][c].x & mask, a01 = sbk.q[1][c].x & mask;
+            const uint32_t a02 = (sbk.q[0][c].x >> 8) & mask, a03 = (sbk.q[1][c].x >> 8) & mask;
+            const uint32_t a10 = sbk.q[0][c].y & mask, a11 = sbk.q[1][c].y & mask;
+            const uint32_t a12 = (sbk.q[0][c].y >> 8) & mask, a13 = (sbk.q[1][c].y >> 8) & mask;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const uint4 fb = fs[lc.slot[nt]];
+                float d4[4];
+                mma_16816_z(d4, a00, a01, a02, a03, fb.x, fb.y);
+                mma_16816(d4, a10, a11, a12, a13, fb.z, fb.w);
+                acc[0][nt] = fmaf(dlc[0][hh], d4[0] + d4[1], acc[0][nt]);
+                acc[1][nt] = fmaf(dlc[1][hh], d4[2] + d4[3], acc[1][nt]);
+            }
+        }
+    }
+}
+
+// Warp partials -> CTA partials (fixed order) -> cluster ranks (fixed order) -> y.
+// part: [nw][16][TT], cta_part: [16][TT] in shared memory.
+template <int NT>
+__device__ __forceinline__ void finish_tile(const float (&acc)[2][NT], float* part, float* cta_part, int warp, int nw,
+                                            int lane, int S, int rank, int M, int64_t N, const int* __restrict__ expo,
+                                            const float* __restrict__ bias, float* __restrict__ y, int64_t ldy) {
+    constexpr int TT = 4 * NT;
+    const int g = lane >> 2, tq = lane & 3;
+    // accumulator (row g or g+8, column 2tq / 2tq+1 of tile nt) -> token nt*4 + tq
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        part[(warp * 16 + g) * TT + nt * 4 + tq] = acc[0][nt];
+        part[(warp * 16 + g + 8) * TT + nt * 4 + tq] = acc[1][nt];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 16 * TT; i += blockDim.x) {
+        float v = part[i];
+        for (int w = 1; w < nw; ++w) v += part[w * 16 * TT + i];
+        cta_part[i] = v;
+    }
+    if (S > 1) fh3::cluster_sync_all();
+    else __syncthreads();
+    // rank r finishes rows r, r+S, ... of the tile, adding the ranks' partials in order
+    for (int i = threadIdx.x; i < 16 * TT; i += blockDim.x) {
+        const int r = i / TT, t = i - r * TT;
+        if (r % S != rank) continue;
+        const int64_t n = static_cast<int64_t>(blockIdx.x) * 16 + r;
+        if (t >= M || n >= N) continue;
+        float v;
+        if (S > 1) {
+            v = 0.0f;
+            const uint32_t la = fh3::smem_u32(cta_part + i);
+            for (int q = 0; q < S; ++q) {
+                float pv;
+                asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(fh3::mapa_shared(la, q)) : "memory");
+                v = q == 0 ? pv : v + pv;
+            }
+        } else {
+            v = cta_part[i];
+        }
+        v = ldexpf(v, expo[t]);
+        if (bias) v += bias[n];
+        y[t * ldy + n] = v;
+    }
+    if (S > 1) fh3::cluster_sync_all();  // peers' shared memory stays live until every rank has read it
+}
+
+// ---------------------------------------------------------------------------
+// 1..4 tokens: a CTA owns a 16-row tile; each warp takes every nw-th super-block and
+// stages that super-block's B fragments in its own shared-memory double buffer
+// (cp.async, one commit group per super-block), so no CTA-wide barrier precedes
+// the first MMA.  Weights of the next super-block load while this one computes.
+// Dynamic shared memory: per warp 2 stages x (8 * 8M uint4 + 8M u32); partials.
+// ---------------------------------------------------------------------------
+template <int LANES>
+__device__ __forceinline__ void stage_frag(uint4* st, const uint4* __restrict__ frag, const uint32_t* __restrict__ mfrag,
+                                           int b, int lane) {
+    const uint4* gf = frag + static_cast<int64_t>(b) * 8 * LANES;
+#pragma unroll
+    for (int i = 0; i < 8 * LANES / 32; ++i) cp_async16(st + i * 32 + lane, gf + i * 32 + lane);
+    const uint4* gm = reinterpret_cast<const uint4*>(mfrag + static_cast<int64_t>(b) * LANES);
+    if (lane < LANES / 4) cp_async16(st + 8 * LANES + lane, gm + lane);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int M>
+__global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_small_kernel(
+    const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, const uint4* __restrict__ frag,
+    const uint32_t* __restrict__ mfrag, const int* __restrict__ expo, const float* __restrict__ bias,
+    float* __restrict__ y, int64_t ldy) {
+    constexpr int LANES = 8 * M;                       // fragment slots per sub-block
+    constexpr int STAGE = 8 * LANES + LANES / 4;       // uint4 per stage
+    extern __shared__ __align__(16) uint8_t gv_smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nw = blockDim.x >> 5;
+    const int g = lane >> 2, tq = lane & 3;
+    uint4* st0 = reinterpret_cast<uint4*>(gv_smem) + static_cast<size_t>(warp) * 2 * STAGE;
+    uint4* st1 = st0 + STAGE;
+    float* part = reinterpret_cast<float*>(reinterpret_cast<uint4*>(gv_smem) + static_cast<size_t>(nw) * 2 * STAGE);
+    float* cta_part = part + nw * 16 * 4;
+
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 16 + g;
+    const int64_t r1 = r0 + 8;
+    const uint8_t* row0 = W + (r0 < N ? r0 : N - 1) * row_bytes;  // clamp loads; stores are masked
+    const uint8_t* row1 = W + (r1 < N ? r1 : N - 1) * row_bytes;
+    const LaneCtx<1> lc = lane_ctx<1>(lane, LANES);
+
+    float acc[2][1] = {{0.0f}, {0.0f}};
+    const int nbw = warp < nblk ? (nblk - warp + nw - 1) / nw : 0;  // super-blocks of this warp
+    if (nbw > 0) {
+        // prefetches past the warp's last super-block re-read its last one (cache hits)
+        const int blast = warp + (nbw - 1) * nw;
+        int b = warp;
+        SuperBlock sa, sbuf;
+        load_sb(sa, row0, row1, b, tq);  // weights do not depend on the prep kernel
+        load_sb(sbuf, row0, row1, min(b + nw, blast), tq);
+        pdl_wait();
+        stage_frag<LANES>(st0, frag, mfrag, b, lane);
+        stage_frag<LANES>(st1, frag, mfrag, min(b + nw, blast), lane);
+        for (int it = 0;; it += 2) {
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+            __syncwarp();
+            compute_sb<1, LANES>(sa, lane, LANES, lc, st0, reinterpret_cast<const uint32_t*>(st0 + 8 * LANES), acc);
+            if (it + 1 >= nbw) break;
+            __syncwarp();
+            const int b2 = min(b + 2 * nw, blast);
+            load_sb(sa, row0, row1, b2, tq);
+            stage_frag<LANES>(st0, frag, mfrag, b2, lane);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+            __syncwarp();
+            compute_sb<1, LANES>(sbuf, lane, LANES, lc, st1, reinterpret_cast<const uint32_t*>(st1 + 8 * LANES), acc);
+            if (it + 2 >= nbw) break;
+            __syncwarp();
+            const int b3 = min(b + 3 * nw, blast);
+            load_sb(sbuf, row0, row1, b3, tq);
+            stage_frag<LANES>(st1, frag, mfrag, b3, lane);
+            b += 2 * nw;
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");  // no copy outlives the CTA
+    }
+    finish_tile<1>(acc, part, cta_part, warp, nw, lane, 1, 0, M, N, expo, bias, y, ldy);
+}
+
+// ---------------------------------------------------------------------------
+// 5..16 tokens: a CTA owns a 16-row tile and a K range; the range's B fragments are
+// copied to shared memory once.  When the fragments of the whole K would not fit, a
+// cluster of S CTAs splits K and the partial sums meet over distributed shared memory.
+// grid (ceil(N / 16), S), cluster (1, S, 1) when S > 1.  Dynamic shared memory:
+// B fragments [nsb*8][8M] uint4, min-term B fragments [nsb][8M] u32, partials.
+// ---------------------------------------------------------------------------
+template <int NT>
+__global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_kernel(
+    const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, const uint4* __restrict__ frag,
+    const uint32_t* __restrict__ mfrag, const int* __restrict__ expo, int M, const float* __restrict__ bias,
+    float* __restrict__ y, int64_t ldy, int S, int nsb_max) {
+    extern __shared__ __align__(16) uint8_t gv_smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nw = blockDim.x >> 5;
+    const int g = lane >> 2, tq = lane & 3;
+    const int rank = S > 1 ? static_cast<int>(fh3::cluster_ctarank()) : 0;
+    const int b_lo = static_cast<int>(static_cast<int64_t>(nblk) * rank / S);
+    const int b_hi = static_cast<int>(static_cast<int64_t>(nblk) * (rank + 1) / S);
+    const int nsb = b_hi - b_lo;
+    const int lanes = 8 * M;  // fragment slots per sub-block
+
+    uint4* sfrag = reinterpret_cast<uint4*>(gv_smem);
+    uint32_t* smfrag = reinterpret_cast<uint32_t*>(gv_smem + static_cast<size_t>(nsb_max) * 8 * lanes * 16);
+    float* part = reinterpret_cast<float*>(smfrag + static_cast<size_t>(nsb_max) * lanes);  // [nw][16][4NT]
+    float* cta_part = part + kGvMaxWarps * 16 * 4 * NT;                                      // [16][4NT]
+
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 16 + g;
+    const int64_t r1 = r0 + 8;
+    const uint8_t* row0 = W + (r0 < N ? r0 : N - 1) * row_bytes;  // clamp loads; stores are masked
+    const uint8_t* row1 = W + (r1 < N ? r1 : N - 1) * row_bytes;
+
+    // weights do not depend on the prep kernel: start loading before waiting for it
+    SuperBlock sa, sbuf;
+    int b = b_lo + warp;
+    if (b < b_hi) load_sb(sa, row0, row1, b, tq);
+    const LaneCtx<NT> lc = lane_ctx<NT>(lane, lanes);
+
+    pdl_wait();
+    {
+        const uint4* gf = frag + static_cast<int64_t>(b_lo) * 8 * lanes;
+        const int nf = nsb * 8 * lanes;
+        for (int i = threadIdx.x; i < nf; i += blockDim.x) cp_async16(sfrag + i, gf + i);
+        const uint4* gm = reinterpret_cast<const uint4*>(mfrag + static_cast<int64_t>(b_lo) * lanes);
+        const int nm = nsb * lanes / 4;  // 8M words per super-block: whole 16-byte units
+        for (int i = threadIdx.x; i < nm; i += blockDim.x) cp_async16(reinterpret_cast<uint4*>(smfrag) + i, gm + i);
+        cp_async_wait_all();
+        __syncthreads();
+    }
+
+    float acc[2][NT];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[i][nt] = 0.0f;
+
+    // two super-blocks in flight: the next one's bytes load while this one computes
+    while (b < b_hi) {
+        const int b1 = b + nw;
+        if (b1 < b_hi) load_sb(sbuf, row0, row1, b1, tq);
+        compute_sb<NT>(sa, lane, lanes, lc, sfrag + (b - b_lo) * 8 * lanes, smfrag + (b - b_lo) * lanes, acc);
+        if (b1 >= b_hi) break;
+        const int b2 = b1 + nw;
+        if (b2 < b_hi) load_sb(sa, row0, row1, b2, tq);
+        compute_sb<NT>(sbuf, lane, lanes, lc, sfrag + (b1 - b_lo) * 8 * lanes, smfrag + (b1 - b_lo) * lanes, acc);
+        b = b2;
+    }
+    finish_tile<NT>(acc, part, cta_part, warp, nw, lane, S, rank, M, N, expo, bias, y, ldy);
+}
+
+size_t gv_smem_bytes(int M, int NT, int nsb_max) {
+    return static_cast<size_t>(nsb_max) * (8 * 8 * M * 16 + 8 * M * 4) + (kGvMaxWarps + 1) * 16 * 4 * NT * 4;
+}
+
+cudaLaunchAttribute pdl_attr() {
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+    return a;
+}
+
+int set_smem(const void* fn, size_t smem, int& cur, const char* what) {
+    if (static_cast<int>(smem) <= cur) return 0;
+    const int rc = fh3host::check_cuda(
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)), what);
+    if (rc == 0) cur = static_cast<int>(smem);
+    return rc;
+}
+
+template <int M>
+int launch_small(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, float* y,
+                 const float* bias, cudaStream_t s) {
+    const int64_t N = w->out, K = w->in;
+    const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
+    // balanced warps: the fewest that keep the per-warp count at ceil(nblk / 8)
+    const int per = (nblk + kGvMaxWarps - 1) / kGvMaxWarps;
+    const int warps = (nblk + per - 1) / per;
+    const int lanes = 8 * M;
+    const size_t smem = static_cast<size_t>(warps) * 2 * (8 * lanes + lanes / 4) * 16 + (warps + 1) * 16 * 4 * 4;
+    static int smem_set = 0;
+    int rc = set_smem(reinterpret_cast<const void*>(gemv_mma_small_kernel<M>), smem, smem_set,
+                      "gemv_mma_small_kernel smem attribute");
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((N + 15) / 16), 1, 1);
+    cfg.blockDim = dim3(warps * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return fh3host::check_cuda(cudaLaunchKernelEx(&cfg, gemv_mma_small_kernel<M>, w->data,
+                                                  fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, K), nblk, N, frag, mfrag, expo,
+                                                  bias, y, N),
+                               "gemv_mma_small_kernel launch");
+}
+
+template <int NT>
+int launch_mma(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, int M, float* y,
+               const float* bias, cudaStream_t s) {
+    const int64_t N = w->out, K = w->in;
+    const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
+    int S = 1;
+    while (S < 8 && S < nblk && gv_smem_bytes(M, NT, (nblk + S - 1) / S) > kGvSmemTarget) S *= 2;
+    const int nsb_max = (nblk + S - 1) / S;
+    const int per = (nsb_max + kGvMaxWarps - 1) / kGvMaxWarps;
+    const int warps = (nsb_max + per - 1) / per;
+    const size_t smem = gv_smem_bytes(M, NT, nsb_max);
+    static int smem_set[5] = {0, 0, 0, 0, 0};  // per instantiation, grows only
+    int rc = set_smem(reinterpret_cast<const void*>(gemv_mma_kernel<NT>), smem, smem_set[NT],
+                      "gemv_mma_kernel smem attribute");
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>(S), 1);
+    cfg.blockDim = dim3(warps * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na++] = pdl_attr();
+    if (S > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = S;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return fh3host::check_cuda(
+        cudaLaunchKernelEx(&cfg, gemv_mma_kernel<NT>, w->data, fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, K), nblk, N,
+                           frag, mfrag, expo, M, bias, y, N, S, nsb_max),
+        "gemv_mma_kernel launch");
+}
+
+}  // namespace
+
+namespace fh3host {
+
+// 1..16-token Q4_K GEMV on warp MMAs; scratch slot 5 holds the activation fragments.
+int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s) {
+    DevCtx* c = ctx();
+    if (!c) return set_error(FH3CUDA_E_NODEV, "gemv_mma: call fh3cuda_init first");
+    const int NT = (n_tok + 3) / 4;
+    const int64_t K = w->in;
+    const size_t fbytes = static_cast<size_t>(K) * n_tok * 4;  // (K/32) sub-blocks x 8M slots x 16 B
+    const size_t mbytes = static_cast<size_t>(K / 256) * 8 * n_tok * sizeof(uint32_t);
+    uint8_t* base = static_cast<uint8_t*>(scratch(c, 5, fbytes + mbytes + 256, s));
+    if (!base) return FH3_E_NOMEM;
+    auto* frag = reinterpret_cast<uint4*>(base);
+    auto* mfrag = reinterpret_cast<uint32_t*>(base + fbytes);
+    auto* expo = reinterpret_cast<int*>(base + fbytes + mbytes);
+    const dim3 pgrid(static_cast<unsigned>((K + kPrepSlice - 1) / kPrepSlice), static_cast<unsigned>(n_tok));
+    gemv_mma_prep_kernel<<<pgrid, 256, 0, s>>>(x, K, n_tok, frag, mfrag, expo);
+    const int rc = check_cuda(cudaGetLastError(), "gemv_mma_prep_kernel launch");
+    if (rc) return rc;
+    switch (n_tok) {
+        case 1: return launch_small<1>(w, frag, mfrag, expo, y, bias, s);
+        case 2: return launch_small<2>(w, frag, mfrag, expo, y, bias, s);
+        case 3: return launch_small<3>(w, frag, mfrag, expo, y, bias, s);
+        case 4: return launch_small<4>(w, frag, mfrag, expo, y, bias, s);
+        default: break;
+    }
+    switch (NT) {
+        case 2: return launch_mma<2>(w, frag, mfrag, expo, n_tok, y, bias, s);
+        case 3: return launch_mma<3>(w, frag, mfrag, expo, n_tok, y, bias, s);
+        default: return launch_mma<4>(w, frag, mfrag, expo, n_tok, y, bias, s);
+    }
+}
+
+}  // namespace fh3host

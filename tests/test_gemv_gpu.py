@@ -25,6 +25,14 @@ def gemv_path(request):
     return request.param
 
 
+@pytest.fixture(autouse=True, params=["mma", "fp32"])
+def gemv_kernel(request, monkeypatch):
+    """...and on both GEMV kernels: the tensor-core kernel (default) and the fp32
+    CUDA-core kernel (FH3CUDA_GEMV_KERNEL=fp32)."""
+    monkeypatch.setenv("FH3CUDA_GEMV_KERNEL", request.param)
+    return request.param
+
+
 def _run(fh3, w_raw, K, N, x, bias=None):
     import torch
     w = fh3.Q4KWeight.from_bytes(w_raw, K, N)
