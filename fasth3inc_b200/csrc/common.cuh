@@ -384,4 +384,8 @@ void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
 // 1..16-token Q4_K GEMV on warp-level tensor-core MMAs (gemv_mma.cu); arguments
 // already validated by the caller
 int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
+// the fp32 CUDA-core GEMV (gemv.cu): uses no memory beyond x, y, bias and the weights
+int gemv_fp32(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
+// argument checks shared by the GEMV entry points (FH3_OK or the error code, message set)
+int gemv_args_ok(const Fh3CudaW* w, const float* x, const float* y, int n_tok, const char* who);
 }  // namespace fh3host

@@ -164,22 +164,20 @@ int launch(const Fh3CudaW* w, const float* x, float* y, const float* bias, cudaS
 
 }  // namespace
 
-extern "C" int fh3cuda_gemv_q4k_dev(const Fh3CudaW* w, const float* x, float* y, int n_tok,
-                                    const float* bias, void* stream) {
-    using namespace fh3host;
-    DevCtx* c = ctx();
-    if (!c) return set_error(FH3CUDA_E_NODEV, "fh3cuda_gemv_q4k_dev: call fh3cuda_init first");
+namespace fh3host {
+
+int gemv_args_ok(const Fh3CudaW* w, const float* x, const float* y, int n_tok, const char* who) {
+    if (!ctx()) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);
     if (!w || !x || !y || !w->data || n_tok <= 0 || n_tok > 16 || w->in <= 0 || w->out <= 0)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemv_q4k_dev: bad arguments (n_tok must be 1..16)");
+        return set_error(FH3_E_INVALID, "%s: bad arguments (n_tok must be 1..16)", who);
     if (w->type != FH3CUDA_TYPE_Q4_K || (w->in % fh3::kQ4KBlock) != 0)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemv_q4k_dev: Q4_K weights with in %% 256 == 0 required");
+        return set_error(FH3_E_INVALID, "%s: Q4_K weights with in %% 256 == 0 required", who);
     if ((reinterpret_cast<uintptr_t>(w->data) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
-        return set_error(FH3_E_INVALID, "fh3cuda_gemv_q4k_dev: weights and x must be 16-byte aligned");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // FH3CUDA_GEMV_KERNEL=fp32 selects the CUDA-core kernel below; the default is the
-    // tensor-core kernel of gemv_mma.cu
-    const char* kernel = getenv("FH3CUDA_GEMV_KERNEL");
-    if (!(kernel && strcmp(kernel, "fp32") == 0)) return gemv_mma(w, x, y, n_tok, bias, s);
+        return set_error(FH3_E_INVALID, "%s: weights and x must be 16-byte aligned", who);
+    return FH3_OK;
+}
+
+int gemv_fp32(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s) {
     switch (n_tok) {
         case 1: return launch<1, 4>(w, x, y, bias, s);
         case 2: return launch<2, 4>(w, x, y, bias, s);
@@ -198,4 +196,19 @@ extern "C" int fh3cuda_gemv_q4k_dev(const Fh3CudaW* w, const float* x, float* y,
         case 15: return launch<15, 1>(w, x, y, bias, s);
         default: return launch<16, 1>(w, x, y, bias, s);
     }
+}
+
+}  // namespace fh3host
+
+extern "C" int fh3cuda_gemv_q4k_dev(const Fh3CudaW* w, const float* x, float* y, int n_tok,
+                                    const float* bias, void* stream) {
+    using namespace fh3host;
+    const int rc = gemv_args_ok(w, x, y, n_tok, "fh3cuda_gemv_q4k_dev");
+    if (rc != FH3_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // FH3CUDA_GEMV_KERNEL=fp32 selects the CUDA-core kernel; the default is the
+    // tensor-core kernel of gemv_mma.cu
+    const char* kernel = getenv("FH3CUDA_GEMV_KERNEL");
+    if (kernel && strcmp(kernel, "fp32") == 0) return gemv_fp32(w, x, y, n_tok, bias, s);
+    return gemv_mma(w, x, y, n_tok, bias, s);
 }

@@ -68,7 +68,13 @@ extern "C" int fh3cuda_matmul_noalloc_dev(const Fh3CudaW* w, const float* x, flo
         return set_error(FH3_E_INVALID, "fh3cuda_matmul_noalloc_dev: bad arguments");
     if (w->type != FH3CUDA_TYPE_Q4_K || (w->in % fh3::kQ4KBlock) != 0)
         return set_error(FH3_E_INVALID, "fh3cuda_matmul_noalloc_dev: Q4_K weights with in %% 256 == 0 required");
-    if (n_tok <= 16) return fh3cuda_gemv_q4k_dev(w, x, y, n_tok, bias, stream);  // needs no scratch
+    if (n_tok <= 16) {
+        // the CUDA-core GEMV reads x and the weights and writes y, nothing else (the
+        // default tensor-core GEMV stages activation fragments in allocated scratch)
+        const int rc = gemv_args_ok(w, x, y, n_tok, "fh3cuda_matmul_noalloc_dev");
+        if (rc != FH3_OK) return rc;
+        return gemv_fp32(w, x, y, n_tok, bias, static_cast<cudaStream_t>(stream));
+    }
     const int64_t elems = static_cast<int64_t>(n_tok) * w->in;
     if (elems > kNoAllocMaxElems)
         return set_error(FH3_E_INVALID,
