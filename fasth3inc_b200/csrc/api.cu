@@ -91,6 +91,17 @@ void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s) {
     return p;
 }
 
+void* scratch_zeroed(DevCtx* c, int slot, size_t bytes, cudaStream_t s) {
+    if (!c || slot < 0 || slot >= 8) return nullptr;
+    const void* before = c->scratch_ptr[slot];
+    const size_t size_before = c->scratch_size[slot];
+    void* p = scratch(c, slot, bytes, s);
+    if (p && (p != before || c->scratch_size[slot] != size_before)) {
+        if (check_cuda(cudaMemsetAsync(p, 0, c->scratch_size[slot], s), "scratch_zeroed: memset")) return nullptr;
+    }
+    return p;
+}
+
 }  // namespace fh3host
 
 using namespace fh3host;

@@ -381,6 +381,8 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
                       const cuuint32_t* estride, CUtensorMapSwizzle swz);
 // scratch of at least `bytes` for slot `slot` (cached, grows)
 void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
+// the same, zero-filled whenever it is (re)allocated; users keep it zero between calls
+void* scratch_zeroed(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
 // 1..16-token Q4_K GEMV on warp-level tensor-core MMAs (gemv_mma.cu); arguments
 // already validated by the caller
 int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);

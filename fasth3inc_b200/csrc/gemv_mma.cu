@@ -39,6 +39,10 @@
 // is permuted identically on both sides and the dot products are unchanged.
 // B fragments are stored compactly: sub-block sb, column col = 2*token + plane,
 // lane tq -> frag[sb * 8M + col * 4 + tq] (16 bytes: halves for k-step 0 then 1).
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 
 namespace {
@@ -236,13 +240,17 @@ __device__ __forceinline__ void compute_sb(const SuperBlock& sbk, int lane, int 
         am[i] = __byte_perm(mw, 0u, lc.sel_m);
         dm32[i] = dmin * 32.0f;
     }
+    // two partial sums per accumulator (low / high nibble sub-blocks) shorten the
+    // dependent FMA chains; the min term starts the low one
+    float ph[2][NT][2];
     // min term: one k16 MMA over the 8 sub-blocks (k slots 8..15 zero)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         float dm[4];
         mma_16816_z(dm, am[0], am[1], 0u, 0u, msb[lc.slot[nt]], 0u);
-        acc[0][nt] = fmaf(-dm32[0], dm[0] + dm[1], acc[0][nt]);
-        acc[1][nt] = fmaf(-dm32[1], dm[2] + dm[3], acc[1][nt]);
+        ph[0][nt][0] = -dm32[0] * (dm[0] + dm[1]);
+        ph[1][nt][0] = -dm32[1] * (dm[2] + dm[3]);
+        ph[0][nt][1] = ph[1][nt][1] = 0.0f;
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -266,11 +274,15 @@ __device__ __forceinline__ void compute_sb(const SuperBlock& sbk, int lane, int 
                 float d4[4];
                 mma_16816_z(d4, a00, a01, a02, a03, fb.x, fb.y);
                 mma_16816(d4, a10, a11, a12, a13, fb.z, fb.w);
-                acc[0][nt] = fmaf(dlc[0][hh], d4[0] + d4[1], acc[0][nt]);
-                acc[1][nt] = fmaf(dlc[1][hh], d4[2] + d4[3], acc[1][nt]);
+                ph[0][nt][hh] = fmaf(dlc[0][hh], d4[0] + d4[1], ph[0][nt][hh]);
+                ph[1][nt][hh] = fmaf(dlc[1][hh], d4[2] + d4[3], ph[1][nt][hh]);
             }
         }
     }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[i][nt] += ph[i][nt][0] + ph[i][nt][1];
 }
 
 // Warp partials -> CTA partials (fixed order) -> cluster ranks (fixed order) -> y.
@@ -398,6 +410,214 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_
 }
 
 // ---------------------------------------------------------------------------
+// 1..2 tokens, persistent stream-K, one launch: one CTA per SM.  The ntiles * nblk
+// units (16-row tile, super-block) are split into equal contiguous runs, one per
+// warp of the grid; a warp streams its run with two units in flight in registers
+// (coalesced 8-byte loads: a quad reads a chunk's 32 bytes of a row).  The first two
+// units load before griddepcontrol.wait (weights do not depend on the previous
+// kernel); then every CTA builds the B fragments of the whole K from x itself (the
+// work of gemv_mma_prep_kernel, done once per SM into shared memory), which saves
+// the prep launch.  When a run ends inside a tile, the warp stores its partial sums
+// and counts itself on the tile's counter; the last of the tile's segments adds the
+// partials in segment order (deterministic) and writes y, then zeroes the counter
+// for the next call.
+// Dynamic shared memory: fragments [nblk*8][8M] uint4 | min-term fragments
+// [nblk][8M] u32 | exponents, reduction slots.
+// ---------------------------------------------------------------------------
+#ifndef FH3_GV_STREAM_WARPS
+#define FH3_GV_STREAM_WARPS 16  // warps of the one CTA per SM
+#endif
+constexpr int kStreamWarps = FH3_GV_STREAM_WARPS;
+
+__device__ __forceinline__ int64_t stream_warp_of(int64_t u, int64_t GW, int64_t units) {
+    return ((u + 1) * GW - 1) / units;  // the warp whose run [w*U/GW, (w+1)*U/GW) holds unit u
+}
+
+// x (M x K fp32) -> this CTA's shared-memory B fragments, min-term fragments and
+// per-token exponents (the same values gemv_mma_prep_kernel writes to global memory).
+template <int M>
+__device__ __forceinline__ void build_fragments(const float* __restrict__ x, int64_t K, uint4* sfrag,
+                                                uint32_t* smfrag, int* sexp, float* sred) {
+    constexpr int LANES = 8 * M;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const int k4 = static_cast<int>(K / 4);
+    float am[M];
+#pragma unroll
+    for (int t = 0; t < M; ++t) am[t] = 0.0f;
+    for (int i = threadIdx.x; i < k4; i += blockDim.x) {
+#pragma unroll
+        for (int t = 0; t < M; ++t) {
+            const float4 v = __ldg(x4 + t * k4 + i);
+            am[t] = fmaxf(am[t], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < M; ++t) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) am[t] = fmaxf(am[t], __shfl_xor_sync(0xffffffffu, am[t], o));
+        if (lane == 0) sred[warp * M + t] = am[t];
+    }
+    __syncthreads();
+    if (threadIdx.x < M) {
+        float a = 0.0f;
+        for (int w = 0; w < nw; ++w) a = fmaxf(a, sred[w * M + threadIdx.x]);
+        int E = 0;
+        if (a > 0.0f && a <= 3.0e38f) frexpf(a, &E);  // a < 2^E
+        sexp[threadIdx.x] = 14 - E;                    // max|x| * 2^s < 2^14
+    }
+    __syncthreads();
+    // thread -> 8 consecutive elements (one lane's fragment of one sub-block); a warp
+    // covers one super-block of one token (K % 256 == 0)
+    const int per_tok = static_cast<int>(K / 8);
+    for (int idx = threadIdx.x; idx < M * per_tok; idx += blockDim.x) {
+        const int t = M == 1 ? 0 : idx / per_tok;
+        const int k0 = (idx - t * per_tok) * 8;
+        const int s = sexp[t];
+        const float4 v0 = __ldg(x4 + t * k4 + k0 / 4), v1 = __ldg(x4 + t * k4 + k0 / 4 + 1);
+        const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t pl0[4], pl1[4];
+#pragma unroll
+        for (int p = 0; p < 8; p += 2) {
+            __half h0[2], h1[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const float v = ldexpf(e[perm8(p + u)], s);
+                h0[u] = __float2half_rn(v);
+                h1[u] = __float2half_rn(v - __half2float(h0[u]));
+            }
+            pl0[p / 2] = pack_half2(h0[0], h0[1]);
+            pl1[p / 2] = pack_half2(h1[0], h1[1]);
+        }
+        const int sb = k0 >> 5;
+        const int tq = lane & 3;
+        uint4* f = sfrag + sb * LANES + 2 * t * 4 + tq;
+        f[0] = make_uint4(pl0[0], pl0[1], pl0[2], pl0[3]);
+        f[4] = make_uint4(pl1[0], pl1[1], pl1[2], pl1[3]);
+        float sum = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        const float xa = __shfl_sync(0xffffffffu, sum, 8 * (lane & 3));
+        const float xb = __shfl_sync(0xffffffffu, sum, 8 * (lane & 3) + 4);
+        if (lane < 4) {
+            const float va = ldexpf(xa, s - 5), vb = ldexpf(xb, s - 5);
+            const __half a0 = __float2half_rn(va), b0 = __float2half_rn(vb);
+            const __half a1 = __float2half_rn(va - __half2float(a0)), b1 = __float2half_rn(vb - __half2float(b0));
+            uint32_t* m = smfrag + (k0 >> 8) * LANES + 2 * t * 4 + lane;
+            m[0] = pack_half2(a0, b0);
+            m[4] = pack_half2(a1, b1);
+        }
+    }
+    __syncthreads();
+}
+
+template <int M>
+__global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
+    const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, int64_t units, int seg_max,
+    const float* __restrict__ x, const float* __restrict__ bias, float* __restrict__ y, int64_t ldy,
+    float* __restrict__ partials, int* __restrict__ counters, int* status) {
+    constexpr int LANES = 8 * M;
+    extern __shared__ __align__(128) uint8_t gv_smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nw = blockDim.x >> 5;
+    const int g = lane >> 2, tq = lane & 3;
+    const int64_t K = static_cast<int64_t>(nblk) * fh3::kQ4KBlock;
+
+    uint4* sfrag = reinterpret_cast<uint4*>(gv_smem);
+    uint32_t* smfrag = reinterpret_cast<uint32_t*>(sfrag + static_cast<size_t>(nblk) * 8 * LANES);
+    int* sexp = reinterpret_cast<int*>(smfrag + static_cast<size_t>(nblk) * LANES);  // [M]
+    float* sred = reinterpret_cast<float*>(sexp + 4);                                 // [nw][M]
+
+    // at most one warp per unit, so every run is non-empty and the runs meeting a
+    // tile are consecutive warps (segment index = warp - first warp of the tile)
+    const int64_t GW = min(static_cast<int64_t>(gridDim.x) * nw, units);
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * nw + warp;
+    const int64_t u0 = gw < GW ? gw * units / GW : units;
+    const int64_t u1 = gw < GW ? (gw + 1) * units / GW : units;
+    const int n = static_cast<int>(u1 - u0);
+
+    // next unit to load, as (tile, super-block); rows past N are clamped (stores are masked)
+    int lt = static_cast<int>(u0 / nblk), lb = static_cast<int>(u0 % nblk);
+    auto load_next = [&](SuperBlock& d) {
+        const int64_t r0 = static_cast<int64_t>(lt) * 16 + g, r1 = r0 + 8;
+        load_sb(d, W + (r0 < N ? r0 : N - 1) * row_bytes, W + (r1 < N ? r1 : N - 1) * row_bytes, lb, tq);
+        if (++lb == nblk) {
+            lb = 0;
+            ++lt;
+        }
+    };
+    SuperBlock sa, sbuf;
+    if (n > 0) load_next(sa);
+    if (n > 1) load_next(sbuf);
+    pdl_launch_dependents();  // the next kernel may start its own weight loads
+
+    pdl_wait();  // x, y and the scratch are ours from here on
+    build_fragments<M>(x, K, sfrag, smfrag, sexp, sred);
+
+    const LaneCtx<1> lc = lane_ctx<1>(lane, LANES);
+    float acc[2][1] = {{0.0f}, {0.0f}};
+    int t = static_cast<int>(u0 / nblk), b = static_cast<int>(u0 % nblk);  // unit being computed
+    // end of this warp's segment of tile t: direct store, or partials + last-arriver sum
+    auto finish_segment = [&]() {
+        const int64_t wf = stream_warp_of(static_cast<int64_t>(t) * nblk, GW, units);
+        const int64_t wl = stream_warp_of(static_cast<int64_t>(t + 1) * nblk - 1, GW, units);
+        const int nseg = static_cast<int>(wl - wf + 1);
+        const int64_t r0 = static_cast<int64_t>(t) * 16 + g, r1 = r0 + 8;
+        if (nseg == 1) {
+            if (tq < M) {
+                if (r0 < N) y[tq * ldy + r0] = ldexpf(acc[0][0], 24 - sexp[tq]) + (bias ? bias[r0] : 0.0f);
+                if (r1 < N) y[tq * ldy + r1] = ldexpf(acc[1][0], 24 - sexp[tq]) + (bias ? bias[r1] : 0.0f);
+            }
+        } else if (nseg > seg_max) {
+            if (lane == 0) fh3::record_status(status, FH3_ERR);  // never write past the slots
+        } else {
+            const int seg = static_cast<int>(gw - wf);
+            float* pp = partials + (static_cast<int64_t>(t) * seg_max + seg) * 16 * M;
+            if (tq < M) {
+                pp[g * M + tq] = acc[0][0];
+                pp[(g + 8) * M + tq] = acc[1][0];
+            }
+            __threadfence();
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) old = atomicAdd(&counters[t], 1);
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old == nseg - 1) {  // last segment: add all in segment order
+                __threadfence();
+                if (tq < M) {
+                    const float* pt = partials + static_cast<int64_t>(t) * seg_max * 16 * M;
+                    float v0 = 0.0f, v1 = 0.0f;
+                    for (int q = 0; q < nseg; ++q) {
+                        v0 += __ldcg(pt + (q * 16 + g) * M + tq);
+                        v1 += __ldcg(pt + (q * 16 + g + 8) * M + tq);
+                    }
+                    if (r0 < N) y[tq * ldy + r0] = ldexpf(v0, 24 - sexp[tq]) + (bias ? bias[r0] : 0.0f);
+                    if (r1 < N) y[tq * ldy + r1] = ldexpf(v1, 24 - sexp[tq]) + (bias ? bias[r1] : 0.0f);
+                }
+                if (lane == 0) counters[t] = 0;
+            }
+        }
+        acc[0][0] = acc[1][0] = 0.0f;
+    };
+    auto step = [&](const SuperBlock& cur, int i) {
+        compute_sb<1, LANES>(cur, lane, LANES, lc, sfrag + b * 8 * LANES, smfrag + b * LANES, acc);
+        if (b == nblk - 1 || i == n - 1) finish_segment();
+        if (++b == nblk) {
+            b = 0;
+            ++t;
+        }
+    };
+    for (int i = 0; i < n; i += 2) {
+        step(sa, i);
+        if (i + 2 < n) load_next(sa);
+        if (i + 1 >= n) break;
+        step(sbuf, i + 1);
+        if (i + 3 < n) load_next(sbuf);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // 5..16 tokens: a CTA owns a 16-row tile and a K range; the range's B fragments are
 // copied to shared memory once.  When the fragments of the whole K would not fit, a
 // cluster of S CTAs splits K and the partial sums meet over distributed shared memory.
@@ -515,6 +735,43 @@ int launch_small(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, co
                                "gemv_mma_small_kernel launch");
 }
 
+// Launch the stream-K kernel when its shared memory fits; returns 1 (not launched) otherwise.
+template <int M>
+int launch_stream(const Fh3CudaW* w, const float* x, float* y, const float* bias, cudaStream_t s) {
+    using namespace fh3host;
+    DevCtx* c = ctx();
+    const int64_t N = w->out, K = w->in;
+    const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
+    constexpr int LANES = 8 * M;
+    const size_t smem = static_cast<size_t>(nblk) * (8 * LANES * 16 + LANES * 4) + (kStreamWarps * M + 8) * 4;
+    if (smem > 227 * 1024) return 1;
+    const int sms = ctx_sms(c);
+    const int64_t ntiles = (N + 15) / 16;
+    const int64_t units = ntiles * nblk;
+    const int64_t GW = std::min<int64_t>(static_cast<int64_t>(sms) * kStreamWarps, units);
+    const int64_t per = units / GW;  // >= 1: each run spans at least `per` units
+    const int seg_max = static_cast<int>(std::min<int64_t>(nblk, (nblk + per - 1) / per + 1));
+    float* partials = static_cast<float*>(scratch(c, 6, static_cast<size_t>(ntiles) * seg_max * 16 * M * 4, s));
+    int* counters = static_cast<int*>(scratch_zeroed(c, 7, static_cast<size_t>(ntiles) * 4, s));
+    if (!partials || !counters) return FH3_E_NOMEM;
+
+    static int smem_set = 0;
+    int rc = set_smem(reinterpret_cast<const void*>(gemv_stream_kernel<M>), smem, smem_set,
+                      "gemv_stream_kernel smem attribute");
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms), 1, 1);
+    cfg.blockDim = dim3(kStreamWarps * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemv_stream_kernel<M>, w->data, fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, K),
+                                         nblk, N, units, seg_max, x, bias, y, N, partials, counters, ctx_status(c)),
+                      "gemv_stream_kernel launch");
+}
+
 template <int NT>
 int launch_mma(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, int M, float* y,
                const float* bias, cudaStream_t s) {
@@ -561,6 +818,14 @@ namespace fh3host {
 int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s) {
     DevCtx* c = ctx();
     if (!c) return set_error(FH3CUDA_E_NODEV, "gemv_mma: call fh3cuda_init first");
+    // 1..2 tokens: the single-launch stream-K kernel; FH3CUDA_GEMV_KERNEL=mma-cta
+    // selects the prep + CTA-per-tile kernels instead
+    const char* kname = getenv("FH3CUDA_GEMV_KERNEL");
+    const bool cta = kname && strcmp(kname, "mma-cta") == 0;
+    if (!cta && n_tok <= 2) {
+        const int r = n_tok == 1 ? launch_stream<1>(w, x, y, bias, s) : launch_stream<2>(w, x, y, bias, s);
+        if (r != 1) return r;
+    }
     const int NT = (n_tok + 3) / 4;
     const int64_t K = w->in;
     const size_t fbytes = static_cast<size_t>(K) * n_tok * 4;  // (K/32) sub-blocks x 8M slots x 16 B

@@ -25,10 +25,11 @@ def gemv_path(request):
     return request.param
 
 
-@pytest.fixture(autouse=True, params=["mma", "fp32"])
+@pytest.fixture(autouse=True, params=["mma", "mma-cta", "fp32"])
 def gemv_kernel(request, monkeypatch):
-    """...and on both GEMV kernels: the tensor-core kernel (default) and the fp32
-    CUDA-core kernel (FH3CUDA_GEMV_KERNEL=fp32)."""
+    """...and on every GEMV kernel: the tensor-core kernels (default: persistent
+    stream-K for 1..2 tokens, CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile)
+    and the fp32 CUDA-core kernel (FH3CUDA_GEMV_KERNEL=fp32)."""
     monkeypatch.setenv("FH3CUDA_GEMV_KERNEL", request.param)
     return request.param
 
