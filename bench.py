@@ -28,9 +28,10 @@ sys.path.insert(0, ROOT)
 METRIC = "Q4_K DiT step ms & dequant-GEMM TFLOP/s (GEMV GB/s) at 1/2/4/8 B200 vs host CPU"
 UNIT = "TFLOP/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram__bytes_read.sum + dram__bytes_write.sum of one gemm_q4k_tc_kernel launch (fc1 shape,
-# scaled to the bench's rows) from profiles/gemm_q4k_tc_fc1.md; None until captured.
-GEMM_TRAFFIC_BYTES_PER_FLOP = None
+# dram__bytes_read.sum + dram__bytes_write.sum per FLOP of one gemm_q4k_pair_kernel fc1 launch
+# (8192 rows: 531.7 MB for 2.319 TFLOP, profiles/gemm_q4k_pair_fc1_m8192.md), scaled to the
+# bench's fc1 launch at this rank's rows.
+GEMM_TRAFFIC_BYTES_PER_FLOP = 531.7e6 / 2.319e12
 
 
 def parse():
@@ -45,6 +46,13 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV (1..4 token) measurement")
+    ap.add_argument("--case", choices=["gemm", "gemv"], default=None,
+                    help="run one kernel's launches on a small case (for ncu) instead of the bench")
+    ap.add_argument("--case-rows", type=int, default=8192, help="--case gemm: activation rows")
+    ap.add_argument("--case-kn", type=int, nargs=2, default=(5120, 13824), help="--case gemv: in, out")
+    ap.add_argument("--case-m", type=int, default=1, help="--case gemv: tokens")
+    ap.add_argument("--case-reps", type=int, default=3)
     return ap.parse_args()
 
 
@@ -289,6 +297,9 @@ def run_ours(args):
                          f"{min(rows_s, T)} text rows = {f / 1e9:.1f} GFLOP in {dt:.2f} s; same weights as the GPU"}
 
     peaks, src = load_peaks()
+    gemv = None
+    if rank == 0 and not args.no_gemv:
+        gemv = measure_gemv(fh3, torch, float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])), src)
     peak = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
     roof = None
     if gemm_tflops:
@@ -297,6 +308,7 @@ def run_ours(args):
             traffic = int(GEMM_TRAFFIC_BYTES_PER_FLOP * 2 * m_loc * D_MODEL * 2 * FFN)
         roof = {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(gemm_tflops / peak, 4), "traffic": traffic,
+                "traffic_note": "bytes of one fc1 launch at this rank's rows, scaled from an 8192-row ncu capture",
                 "kernel": "gemm_q4k_pair_kernel", "peak_source": f"{src} bf16_tflops_sustained",
                 "gemm_share_of_step": round(float(mx[1]) / (ms * args.steps), 4)}
     if rank == 0:
@@ -316,11 +328,77 @@ def run_ours(args):
             "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(float(mx[3])), "clocks": clk, "device_status": status,
+            "gemv": gemv,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- GEMV and kernel cases
+GEMV_SHAPES = ((5120, 13824), (13824, 5120), (5120, 5120))   # (in, out): fc-up, fc-down, attention proj
+
+
+def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100) -> dict:
+    """Device time of back-to-back GEMV calls (1 and 4 tokens) on weights larger than L2.
+
+    A sleep kernel holds the stream while the host queues `reps` calls, so the CUDA events
+    bracket GPU time only (each call's launches, chained by programmatic dependent launch).
+    GB/s counts the algorithmic bytes of one call: Q4_K weights + x + y."""
+    import math
+    out = {"unit": "GB/s", "peak": hbm_gbs, "peak_source": f"{peak_src} hbm_gbs", "reps": reps,
+           "method": "sleep-held stream, CUDA events around back-to-back calls, weights rotated > L2",
+           "shapes": []}
+    for K, N in GEMV_SHAPES:
+        wbytes = N * K // 256 * 144
+        nw = max(4, math.ceil(300e6 / wbytes))
+        ws = [fh3.make_weights(N, K, seed=100 + i, stream_id=9) for i in range(nw)]
+        for M in (1, 4):
+            x = torch.randn((M, K), device="cuda")
+            y = torch.empty((M, N), device="cuda")
+            for i in range(2 * nw):
+                fh3.gemv(ws[i % nw], x, out=y)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(40_000_000)
+            e0.record()
+            for i in range(reps):
+                fh3.gemv(ws[i % nw], x, out=y)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1000.0 / reps
+            gbs = (wbytes + 4 * M * (K + N)) / us / 1e3
+            out["shapes"].append({"in": K, "out": N, "tokens": M, "us_per_call": round(us, 2),
+                                  "achieved": round(gbs, 1), "frac": round(gbs / hbm_gbs, 4)})
+        del ws
+        torch.cuda.synchronize()
+    return out
+
+
+def run_case(args):
+    """One kernel's launches on a small case, for ncu (prints a one-line JSON summary)."""
+    import torch
+    import fasth3inc_b200 as fh3
+    from fasth3inc_b200.trunk import D_MODEL, FFN
+    fh3.init(0)
+    if args.case == "gemm":
+        w = fh3.make_weights(2 * FFN, D_MODEL, seed=1, stream_id=1)     # fc1: [up; gate]
+        x = fh3.to_bf16(torch.randn((args.case_rows, D_MODEL), device="cuda"))
+        y = torch.empty((args.case_rows, FFN), dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.case_reps):
+            fh3.gemm(w, x, fh3.EPI_SWIGLU, out=y)
+        shape = {"rows": args.case_rows, "in": D_MODEL, "out": 2 * FFN, "epilogue": "swiglu"}
+    else:
+        K, N = args.case_kn
+        ws = [fh3.make_weights(N, K, seed=i, stream_id=3) for i in range(args.case_reps)]
+        x = torch.randn((args.case_m, K), device="cuda")
+        y = torch.empty((args.case_m, N), device="cuda")
+        for w in ws:
+            fh3.gemv(w, x, out=y)
+        shape = {"in": K, "out": N, "tokens": args.case_m}
+    torch.cuda.synchronize()
+    print(json.dumps({"case": args.case, **shape, "reps": args.case_reps, "status": fh3.device_status()}))
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -372,7 +450,9 @@ def run_reference(args):
 def main():
     args = parse()
     os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -115,7 +115,8 @@ def matmul(w: Q4KWeight, x, bias=None, out=None, stream=None):
 
 
 def gemv(w: Q4KWeight, x, bias=None, out=None, stream=None):
-    """The fp32 CUDA-core GEMV (1..16 tokens)."""
+    """Q4_K GEMV for 1..16 tokens (fh3cuda_gemv_q4k_dev): tensor-core kernels by default,
+    the fp32 CUDA-core kernel with FH3CUDA_GEMV_KERNEL=fp32."""
     torch = _torch()
     _ensure(x)
     n_tok = x.shape[0]
