@@ -222,6 +222,33 @@ void oracle_rmsnorm(float *x, const float *w, int n, int dim, float eps) {
     }
 }
 
+/* Restates fh3_rope3 (src/core/fh3_ops.c:458-505): for token i and head h the
+ * first rot_dim channels rotate in halves, v0 = x[j], v1 = x[rot/2 + j]:
+ * x[j] = v0*cos[j] - v1*sin[j], x[rot/2+j] = v1*cos[rot/2+j] + v0*sin[rot/2+j]
+ * (two products rounded, then one add/sub: -ffp-contract=off, as the
+ * reference's mul/sub intrinsics); cos/sin are [n][rot_dim]; channels
+ * rot_dim..head_dim-1 are untouched.  Invalid arguments leave x unchanged. */
+void oracle_rope3(float *x, const float *cos_t, const float *sin_t, int n, int heads, int head_dim, int rot_dim) {
+    if (!x || !cos_t || !sin_t || n <= 0 || heads <= 0 || head_dim <= 0 || rot_dim <= 0 || rot_dim > head_dim ||
+        (rot_dim % 2) != 0)
+        return;
+    const int half = rot_dim / 2;
+    for (int i = 0; i < n; i++) {
+        const float *c = cos_t + (size_t)i * rot_dim;
+        const float *s = sin_t + (size_t)i * rot_dim;
+        for (int h = 0; h < heads; h++) {
+            float *v = x + ((size_t)i * heads + h) * head_dim;
+            for (int j = 0; j < half; j++) {
+                const float v0 = v[j], v1 = v[half + j];
+                const float a = v0 * c[j], b = v1 * s[j];
+                const float e = v1 * c[half + j], f = v0 * s[half + j];
+                v[j] = a - b;
+                v[half + j] = e + f;
+            }
+        }
+    }
+}
+
 /* Restates fh3_modulate (src/core/fh3_ops.c:529-557): x = fma(x, 1+scale,
  * shift) on whole 8-wide vectors of each 1024-element chunk, and the unfused
  * x*(1+scale)+shift on a chunk's tail. shift/scale span the whole n*dim

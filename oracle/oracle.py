@@ -67,6 +67,8 @@ class Oracle:
         lib.oracle_swiglu.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.oracle_rmsnorm.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
         lib.oracle_modulate.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
+        lib.oracle_rope3.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int]
         lib.oracle_gate_residual.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.oracle_rng_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _c_f32p, ctypes.c_size_t]
         lib.oracle_quantize_q4k.restype = ctypes.c_int
@@ -116,6 +118,24 @@ class Oracle:
         w = np.ascontiguousarray(w, dtype=np.float32)
         self.lib.oracle_rmsnorm(_ptr(x, _c_f32p), _ptr(w, _c_f32p), x.shape[0], x.shape[1], eps)
         return x
+
+    def rope3(self, x: np.ndarray, cos: np.ndarray, sin: np.ndarray, heads: int, head_dim: int,
+              rot_dim: int) -> np.ndarray:
+        """x [n][heads*head_dim] rotated per head (a copy); cos/sin [n][rot_dim]."""
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        c = np.ascontiguousarray(cos, dtype=np.float32)
+        s = np.ascontiguousarray(sin, dtype=np.float32)
+        self.lib.oracle_rope3(_ptr(x, _c_f32p), _ptr(c, _c_f32p), _ptr(s, _c_f32p), x.shape[0], heads,
+                              head_dim, rot_dim)
+        return x
+
+    def qk_norm_rope(self, x: np.ndarray, w: np.ndarray, cos: np.ndarray, sin: np.ndarray, heads: int,
+                     head_dim: int, rot_dim: int, eps: float) -> np.ndarray:
+        """fh3_dit.c:397-401 for one of q / k: per-head rmsnorm, then rope3 (a copy)."""
+        n = x.shape[0]
+        y = self.rmsnorm(np.asarray(x, dtype=np.float32).reshape(n * heads, head_dim), w, eps)
+        y = y.reshape(n, heads * head_dim)
+        return self.rope3(y, cos, sin, heads, head_dim, rot_dim) if rot_dim > 0 else y
 
     def modulate(self, x: np.ndarray, shift: np.ndarray, scale: np.ndarray) -> np.ndarray:
         x = np.array(x, dtype=np.float32, copy=True, order="C")
@@ -179,6 +199,8 @@ class Reference:
         lib.fh3_swiglu.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.fh3_rmsnorm.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
         lib.fh3_modulate.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
+        lib.fh3_rope3.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int]
         lib.fh3_gate_residual.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.fh3_rng_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _c_f32p, ctypes.c_size_t]
         self.lib = lib
@@ -224,6 +246,14 @@ class Reference:
         x = np.array(x, dtype=np.float32, copy=True, order="C")
         w = np.ascontiguousarray(w, dtype=np.float32)
         self.lib.fh3_rmsnorm(_ptr(x, _c_f32p), _ptr(w, _c_f32p), x.shape[0], x.shape[1], eps)
+        return x
+
+    def rope3(self, x, cos, sin, heads: int, head_dim: int, rot_dim: int):
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        c = np.ascontiguousarray(cos, dtype=np.float32)
+        s = np.ascontiguousarray(sin, dtype=np.float32)
+        self.lib.fh3_rope3(_ptr(x, _c_f32p), _ptr(c, _c_f32p), _ptr(s, _c_f32p), x.shape[0], heads, head_dim,
+                           rot_dim)
         return x
 
     def modulate(self, x, shift, scale):

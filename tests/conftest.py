@@ -72,6 +72,39 @@ def read_matmul_golden():
     return t, K, N, M, w, x, bias, y
 
 
+def read_rmsnorm_golden():
+    """tests/fixtures/ops/rmsnorm.bin: <II f> n, dim, eps; x [n][dim]; w [dim]; ref [n][dim]."""
+    with open(os.path.join(GOLDEN, "rmsnorm.bin"), "rb") as f:
+        b = f.read()
+    n, dim = struct.unpack("<II", b[:8])
+    (eps,) = struct.unpack("<f", b[8:12])
+    a = np.frombuffer(b[12:], np.float32)
+    x = a[:n * dim].reshape(n, dim).copy()
+    w = a[n * dim:n * dim + dim].copy()
+    ref = a[n * dim + dim:n * dim + dim + n * dim].reshape(n, dim).copy()
+    return n, dim, eps, x, w, ref
+
+
+def read_rope3_golden():
+    """tests/fixtures/ops/rope3.bin: <IIII> n, heads, head_dim, rot_dim; x; cos [n][rot]; sin; ref."""
+    with open(os.path.join(GOLDEN, "rope3.bin"), "rb") as f:
+        b = f.read()
+    n, heads, hd, rot = struct.unpack("<IIII", b[:16])
+    a = np.frombuffer(b[16:], np.float32)
+    nx, nr = n * heads * hd, n * rot
+    x = a[:nx].reshape(n, heads * hd).copy()
+    c = a[nx:nx + nr].reshape(n, rot).copy()
+    s = a[nx + nr:nx + 2 * nr].reshape(n, rot).copy()
+    ref = a[nx + 2 * nr:nx + 2 * nr + nx].reshape(n, heads * hd).copy()
+    return n, heads, hd, rot, x, c, s, ref
+
+
+def close_like_reference(got, ref, tol=1e-5) -> bool:
+    """check_close of the reference's tests/unit/test_ops.c:41-56: |a-r| / max(|r|, 1) <= tol."""
+    got, ref = np.asarray(got, np.float32), np.asarray(ref, np.float32)
+    return bool(np.all(np.abs(got - ref) / np.maximum(np.abs(ref), 1.0) <= tol))
+
+
 @pytest.fixture(scope="session")
 def fh3():
     """The product package on cuda:0; the CUDA library must load (no fallback)."""

@@ -5,6 +5,9 @@
      tests/fixtures/quant/matmul_ref.bin  -> matmul_ref.bin  (fp64 numpy matmul output)
    Their layouts are documented in the reference's tools/emit_quant_fixtures.py:75-81,134-141
    and read by tests/unit/test_quant.c:54-81 and tests/unit/test_matmul.c:196-231.
+   Also the op fixtures tests/fixtures/ops/{rmsnorm,rope3}.bin -> {rmsnorm,rope3}.bin,
+   read by the reference's tests/unit/test_ops.c:58-96 (<u32 n, u32 dim, f32 eps>, x, w, ref)
+   and :98-140 (<u32 n, heads, head_dim, rot_dim>, x, cos, sin, ref).
 2. Writes ref_cases.npz: seeded inputs (this project's Q4_K quantiser + fh3_rng_normal)
    with outputs computed by the REFERENCE'S OWN fh3_matmul / fh3_dequant / fh3_swiglu,
    compiled from its sources into oracle/_ref/libfh3ref.so (oracle/Makefile).  These pin
@@ -47,6 +50,8 @@ def main() -> None:
     fx = os.path.join(args.ref, "tests", "fixtures", "quant")
     for name in ("Q4_K.bin", "matmul_ref.bin"):
         shutil.copyfile(os.path.join(fx, name), os.path.join(HERE, name))
+    for name in ("rmsnorm.bin", "rope3.bin"):
+        shutil.copyfile(os.path.join(args.ref, "tests", "fixtures", "ops", name), os.path.join(HERE, name))
     build()
     o = Oracle()
     r = Reference()
@@ -71,6 +76,15 @@ def main() -> None:
     h[0, 96:100] = [-100.0, -80.5, -79.5, 90.0]
     out["swiglu/h"] = h
     out["swiglu/y"] = r.swiglu(h)
+    # q/k normalisation + rope as fh3_dit.c:397-401 (40 heads x 128, rot 96), by the reference
+    n, H, D, R = 7, 40, 128, 96
+    x = (o.rng_normal(79, 1, n * H * D) * 3.0).reshape(n, H * D)
+    wq = 1.0 + 0.1 * o.rng_normal(79, 2, D)
+    ang = o.rng_normal(79, 3, n * R).reshape(n, R)
+    cs, sn = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    out["qkrope/x"], out["qkrope/w"], out["qkrope/cos"], out["qkrope/sin"] = x, wq, cs, sn
+    out["qkrope/dims"] = np.array([n, H, D, R], dtype=np.int64)
+    out["qkrope/y"] = r.rope3(r.rmsnorm(x.reshape(n * H, D), wq, 1e-6).reshape(n, H * D), cs, sn, H, D, R)
     # fh3_rng_normal itself
     out["rng/seed7_stream3"] = r.rng_normal(7, 3, 1001)
     np.savez_compressed(os.path.join(HERE, "ref_cases.npz"), **out)

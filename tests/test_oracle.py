@@ -10,7 +10,8 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import read_matmul_golden, read_q4k_golden, rel_fro
+from conftest import (close_like_reference, read_matmul_golden, read_q4k_golden, read_rmsnorm_golden,
+                      read_rope3_golden, rel_fro)
 
 Q4K = 12
 
@@ -124,3 +125,37 @@ def test_oracle_rejects_bad_arguments(oracle):
         oracle.matmul(99, np.zeros(144, np.uint8), 256, 1, np.zeros((1, 256), np.float32))
     with pytest.raises(ValueError):
         oracle.quantize_q4k(np.zeros((1, 100), np.float32))
+
+
+def test_rmsnorm_matches_reference_op_fixture(oracle):
+    """tests/fixtures/ops/rmsnorm.bin of the reference, with its own tolerance rule."""
+    n, dim, eps, x, w, ref = read_rmsnorm_golden()
+    assert close_like_reference(oracle.rmsnorm(x, w, eps), ref)
+
+
+def test_rope3_matches_reference_op_fixture(oracle):
+    """tests/fixtures/ops/rope3.bin (rot_dim 96 of head_dim 128), with the reference's tolerance."""
+    n, heads, hd, rot, x, c, s, ref = read_rope3_golden()
+    got = oracle.rope3(x, c, s, heads, hd, rot)
+    assert close_like_reference(got, ref)
+    # channels past rot_dim are untouched
+    xv, gv = x.reshape(n, heads, hd), got.reshape(n, heads, hd)
+    assert np.array_equal(xv[:, :, rot:], gv[:, :, rot:])
+
+
+def test_qk_norm_rope_bitwise_equals_reference_case(oracle, golden_cases):
+    """fh3_dit.c:397-401 (per-head rmsnorm, then rope3) computed by the reference itself."""
+    n, H, D, R = (int(v) for v in golden_cases["qkrope/dims"])
+    got = oracle.qk_norm_rope(golden_cases["qkrope/x"], golden_cases["qkrope/w"], golden_cases["qkrope/cos"],
+                              golden_cases["qkrope/sin"], H, D, R, 1e-6)
+    assert np.array_equal(got.view(np.uint32), golden_cases["qkrope/y"].view(np.uint32))
+
+
+def test_rope3_bitwise_equals_live_reference(oracle, reference):
+    rng = np.random.default_rng(3)
+    for n, H, D, R in ((3, 2, 128, 96), (2, 3, 64, 64), (1, 1, 16, 2)):
+        x = rng.standard_normal((n, H * D)).astype(np.float32)
+        c = rng.standard_normal((n, R)).astype(np.float32)
+        s = rng.standard_normal((n, R)).astype(np.float32)
+        a, b = oracle.rope3(x, c, s, H, D, R), reference.rope3(x, c, s, H, D, R)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (n, H, D, R)
