@@ -26,7 +26,7 @@ from ._lib import (EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, F32, Q4_K, Fh3CudaE
 __all__ = [
     "Q4_K", "F32", "EPI_F32", "EPI_BF16", "EPI_SWIGLU", "EPI_RESID", "Fh3CudaError", "Q4KWeight",
     "init", "row_bytes", "dequant", "matmul", "gemv", "gemm", "matmul_host", "rmsnorm_modulate",
-    "to_bf16", "swiglu", "make_weights", "device_status",
+    "to_bf16", "swiglu", "qk_norm_rope", "make_weights", "device_status",
 ]
 
 _inited: set[int] = set()
@@ -162,6 +162,24 @@ def rmsnorm_modulate(x, shift, scale, norm_w=None, eps: float = 1e-6, out=None, 
         out = torch.empty((n, dim), dtype=torch.bfloat16, device=x.device)
     check(load().fh3cuda_rmsnorm_modulate_dev(_ptr(x), _ptr(norm_w), _ptr(shift), _ptr(scale), _ptr(out),
                                               n, dim, eps, _stream(stream)))
+    return out
+
+
+def qk_norm_rope(src, norm_w, cos=None, sin=None, heads: int = 1, head_dim: int = 128, rot_dim: int = 0,
+                 eps: float = 1e-6, out=None, out_bf16: bool = False, stream=None):
+    """fh3_rmsnorm per head then fh3_rope3 (fh3_dit.c:397-401) on a [n][>= heads*head_dim]
+    fp32 or bf16 view (e.g. the q or k third of a QKV output); returns [n][heads*head_dim]."""
+    torch = _torch()
+    _ensure(src)
+    n = src.shape[0]
+    if src.stride(-1) != 1:
+        raise ValueError("src rows must be contiguous")
+    if out is None:
+        dt = torch.bfloat16 if out_bf16 else torch.float32
+        out = torch.empty((n, heads * head_dim), dtype=dt, device=src.device)
+    check(load().fh3cuda_qk_norm_rope_dev(
+        _ptr(src), int(src.dtype == torch.bfloat16), src.stride(0), _ptr(out), int(out.dtype == torch.bfloat16),
+        out.stride(0), _ptr(norm_w), _ptr(cos), _ptr(sin), n, heads, head_dim, rot_dim, eps, _stream(stream)))
     return out
 
 

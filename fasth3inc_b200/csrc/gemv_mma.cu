@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_
     float* __restrict__ y, int64_t ldy) {
     constexpr int LANES = 8 * M;                       // fragment slots per sub-block
     constexpr int STAGE = 8 * LANES + LANES / 4;       // uint4 per stage
-    extern __shared__ __align__(16) uint8_t gv_smem[];
+    extern __shared__ __align__(128) uint8_t gv_smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int nw = blockDim.x >> 5;
@@ -629,7 +629,7 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_
     const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, const uint4* __restrict__ frag,
     const uint32_t* __restrict__ mfrag, const int* __restrict__ expo, int M, const float* __restrict__ bias,
     float* __restrict__ y, int64_t ldy, int S, int nsb_max) {
-    extern __shared__ __align__(16) uint8_t gv_smem[];
+    extern __shared__ __align__(128) uint8_t gv_smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int nw = blockDim.x >> 5;

@@ -5,6 +5,8 @@
 //                                 then modulate (:529-557), written as bf16
 //   fh3cuda_swiglu_dev            fh3_swiglu (:507-527) on fp32 (the unfused form;
 //                                 the GEMM has it as an epilogue)
+//   fh3cuda_qk_norm_rope_dev      per-head rmsnorm (:410-456) then fh3_rope3 (:458-505)
+//                                 of q or k straight from the QKV output, bit-exact
 // All HBM-bound streaming kernels with 16-byte accesses.
 #include "common.cuh"
 
@@ -79,7 +81,123 @@ int grid_for(int64_t work, int threads) {
     return static_cast<int>(g);
 }
 
+// ---------------------------------------------------------------------------
+// q / k after the QKV projection (fh3_dit.c:397-401): for token i and head h the
+// head_dim-vector is rms-normalised with the shared weights w[head_dim], then its
+// first rot_dim channels are rotated by cos/sin row i.  An 8-lane group owns one
+// vector, staged in shared memory (16-byte global accesses).  Bit-exact with fh3:
+// lane j sums x[j + 8m]^2 with fmaf in increasing m (the reference's eight AVX2
+// lanes), the lanes meet in its fixed tree ((0+1)+(2+3))+((4+5)+(6+7)), then
+// var = sum / dim, inv = 1 / sqrt(var + eps) correctly rounded, y = (x*inv)*w and
+// the rotation with its products rounded before the add/sub.
+// ---------------------------------------------------------------------------
+constexpr int kQkThreads = 256;  // 32 vectors per CTA
+
+template <bool SRC_BF16, bool DST_BF16>
+__global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(
+    const void* __restrict__ src, int64_t ld_src, void* __restrict__ dst, int64_t ld_dst, const float* __restrict__ w,
+    const float* __restrict__ cs, const float* __restrict__ sn, int64_t nvec, int heads, int hd, int rot, float eps) {
+    extern __shared__ __align__(16) float qk_smem[];
+    const int l8 = threadIdx.x & 7;
+    const int grp = threadIdx.x >> 3;
+    const int64_t v = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 3) + grp;
+    if (v >= nvec) return;  // whole 8-lane groups leave together
+    const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+    const int64_t i = v / heads;
+    const int h = static_cast<int>(v - i * heads);
+    float* vec = qk_smem + grp * (hd + 8);  // padded: the four groups of a warp use different banks
+
+    // load: lane l8 takes elements 4*l8 .. 4*l8+3 of every 32
+    if (SRC_BF16) {
+        const __nv_bfloat16* s = static_cast<const __nv_bfloat16*>(src) + i * ld_src + static_cast<int64_t>(h) * hd;
+        for (int d = 4 * l8; d < hd; d += 32) {
+            const uint2 u = *reinterpret_cast<const uint2*>(s + d);
+            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+            *reinterpret_cast<float4*>(vec + d) = make_float4(a.x, a.y, b.x, b.y);
+        }
+    } else {
+        const float* s = static_cast<const float*>(src) + i * ld_src + static_cast<int64_t>(h) * hd;
+        for (int d = 4 * l8; d < hd; d += 32)
+            *reinterpret_cast<float4*>(vec + d) = *reinterpret_cast<const float4*>(s + d);
+    }
+    __syncwarp(gmask);
+    float ss = 0.0f;
+    for (int d = l8; d < hd; d += 8) ss = fmaf(vec[d], vec[d], ss);
+    ss = __fadd_rn(ss, __shfl_xor_sync(gmask, ss, 1, 8));
+    ss = __fadd_rn(ss, __shfl_xor_sync(gmask, ss, 2, 8));
+    ss = __fadd_rn(ss, __shfl_xor_sync(gmask, ss, 4, 8));
+    const float var = __fdiv_rn(ss, static_cast<float>(hd));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    for (int d = l8; d < hd; d += 8) vec[d] = __fmul_rn(__fmul_rn(vec[d], inv), w[d]);
+    __syncwarp(gmask);
+    if (rot > 0) {
+        const int half = rot / 2;
+        const float* c = cs + i * rot;
+        const float* sg = sn + i * rot;
+        for (int j = l8; j < half; j += 8) {
+            const float v0 = vec[j], v1 = vec[half + j];
+            vec[j] = __fsub_rn(__fmul_rn(v0, c[j]), __fmul_rn(v1, sg[j]));
+            vec[half + j] = __fadd_rn(__fmul_rn(v1, c[half + j]), __fmul_rn(v0, sg[half + j]));
+        }
+        __syncwarp(gmask);
+    }
+    if (DST_BF16) {
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(dst) + i * ld_dst + static_cast<int64_t>(h) * hd;
+        for (int d = 4 * l8; d < hd; d += 32) {
+            const float4 f = *reinterpret_cast<const float4*>(vec + d);
+            const __nv_bfloat162 a = __floats2bfloat162_rn(f.x, f.y), b = __floats2bfloat162_rn(f.z, f.w);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t*>(&a);
+            u.y = *reinterpret_cast<const uint32_t*>(&b);
+            *reinterpret_cast<uint2*>(o + d) = u;
+        }
+    } else {
+        float* o = static_cast<float*>(dst) + i * ld_dst + static_cast<int64_t>(h) * hd;
+        for (int d = 4 * l8; d < hd; d += 32)
+            *reinterpret_cast<float4*>(o + d) = *reinterpret_cast<const float4*>(vec + d);
+    }
+}
+
 }  // namespace
+
+extern "C" int fh3cuda_qk_norm_rope_dev(const void* src, int src_bf16, int64_t ld_src, void* dst, int dst_bf16,
+                                        int64_t ld_dst, const float* norm_w, const float* cos_t, const float* sin_t,
+                                        int n, int heads, int head_dim, int rot_dim, float eps, void* stream) {
+    using namespace fh3host;
+    const char* who = "fh3cuda_qk_norm_rope_dev";
+    if (!ctx()) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);
+    if (!src || !dst || !norm_w || n <= 0 || heads <= 0)
+        return set_error(FH3_E_INVALID, "%s: bad arguments", who);
+    if (head_dim < 32 || head_dim > 256 || (head_dim % 32) != 0)
+        return set_error(FH3_E_INVALID, "%s: head_dim must be a multiple of 32 in [32, 256] (got %d)", who, head_dim);
+    if (rot_dim < 0 || rot_dim > head_dim || (rot_dim % 2) != 0 || (rot_dim > 0 && (!cos_t || !sin_t)))
+        return set_error(FH3_E_INVALID, "%s: rot_dim must be even in [0, head_dim] with cos/sin given", who);
+    const int64_t row = static_cast<int64_t>(heads) * head_dim;
+    if (ld_src < row || ld_dst < row || (ld_src % 8) != 0 || (ld_dst % 8) != 0 ||
+        (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15))
+        return set_error(FH3_E_INVALID, "%s: rows must hold heads*head_dim elements, strides a multiple of 8, "
+                         "pointers 16-byte aligned", who);
+    if (src == dst && (src_bf16 != dst_bf16 || ld_src != ld_dst))
+        return set_error(FH3_E_INVALID, "%s: in place needs the same element type and stride", who);
+    const int64_t nvec = static_cast<int64_t>(n) * heads;
+    const int groups = kQkThreads / 8;
+    const unsigned grid = static_cast<unsigned>((nvec + groups - 1) / groups);
+    const size_t smem = static_cast<size_t>(groups) * (head_dim + 8) * sizeof(float);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define FH3_QK_LAUNCH(SB, DB)                                                                              \
+    qk_norm_rope_kernel<SB, DB><<<grid, kQkThreads, smem, s>>>(src, ld_src, dst, ld_dst, norm_w, cos_t, sin_t, \
+                                                               nvec, heads, head_dim, rot_dim, eps)
+    if (src_bf16) {
+        if (dst_bf16) FH3_QK_LAUNCH(true, true);
+        else FH3_QK_LAUNCH(true, false);
+    } else {
+        if (dst_bf16) FH3_QK_LAUNCH(false, true);
+        else FH3_QK_LAUNCH(false, false);
+    }
+#undef FH3_QK_LAUNCH
+    return check_cuda(cudaGetLastError(), "qk_norm_rope launch");
+}
 
 extern "C" int fh3cuda_f32_to_bf16_dev(const float* x, void* y, int64_t n, void* stream) {
     using namespace fh3host;

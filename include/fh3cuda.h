@@ -186,6 +186,21 @@ FH3CUDA_API int fh3cuda_rmsnorm_modulate_dev(const float *x, const float *norm_w
 /* fh3_swiglu (src/core/fh3_ops.c:507-527) on device fp32 buffers. */
 FH3CUDA_API int fh3cuda_swiglu_dev(const float *in, float *out, int n, int F, void *stream);
 
+/* q or k after the QKV projection, as fh3_dit.c:397-401: fh3_rmsnorm over each
+ * head (src/core/fh3_ops.c:410-456, rows = n*heads, dim = head_dim, weights
+ * norm_w[head_dim]) then fh3_rope3 (:458-505, cos/sin [n][rot_dim]), fused and
+ * bit-exact with the reference.  Row i of src / dst starts at i*ld_src / i*ld_dst
+ * elements and holds heads*head_dim elements (a strided view of the QKV output
+ * works); element types fp32 or bf16 (flags src_bf16 / dst_bf16; a bf16 output
+ * is the fp32 result rounded once).  head_dim a multiple of 32 up to 256;
+ * rot_dim even, 0 (normalisation only) .. head_dim; strides multiples of 8,
+ * pointers 16-byte aligned.  src == dst (in place) needs the same type and
+ * stride; other overlaps are not allowed. */
+FH3CUDA_API int fh3cuda_qk_norm_rope_dev(const void *src, int src_bf16, int64_t ld_src, void *dst, int dst_bf16,
+                                         int64_t ld_dst, const float *norm_w, const float *cos_t,
+                                         const float *sin_t, int n, int heads, int head_dim, int rot_dim,
+                                         float eps, void *stream);
+
 /* Seeded synthetic Q4_K weights on the device: rows x n weights drawn from
  * scale * N(0,1) (Philox4x32-10 + Box-Muller), quantised with the same
  * per-block rule as the project's CPU quantiser.  Benchmark input generator;
