@@ -46,10 +46,11 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV (1..4 token) measurement")
-    ap.add_argument("--case", choices=["gemm", "gemv"], default=None,
+    ap.add_argument("--no-gemv", action="store_true",
+                    help="skip the GEMV (1..4 token) and q/k norm+rope measurements")
+    ap.add_argument("--case", choices=["gemm", "gemv", "qk"], default=None,
                     help="run one kernel's launches on a small case (for ncu) instead of the bench")
-    ap.add_argument("--case-rows", type=int, default=8192, help="--case gemm: activation rows")
+    ap.add_argument("--case-rows", type=int, default=8192, help="--case gemm / qk: activation rows")
     ap.add_argument("--case-kn", type=int, nargs=2, default=(5120, 13824), help="--case gemv: in, out")
     ap.add_argument("--case-m", type=int, default=1, help="--case gemv: tokens")
     ap.add_argument("--case-reps", type=int, default=3)
@@ -297,9 +298,11 @@ def run_ours(args):
                          f"{min(rows_s, T)} text rows = {f / 1e9:.1f} GFLOP in {dt:.2f} s; same weights as the GPU"}
 
     peaks, src = load_peaks()
-    gemv = None
+    gemv = qk = None
     if rank == 0 and not args.no_gemv:
-        gemv = measure_gemv(fh3, torch, float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])), src)
+        hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        gemv = measure_gemv(fh3, torch, hbm, src)
+        qk = measure_qk_norm_rope(fh3, torch, m_loc, hbm, src)
     peak = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
     roof = None
     if gemm_tflops:
@@ -328,7 +331,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(float(mx[3])), "clocks": clk, "device_status": status,
-            "gemv": gemv,
+            "gemv": gemv, "qk_norm_rope": qk,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -376,6 +379,37 @@ def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100) -> 
     return out
 
 
+def measure_qk_norm_rope(fh3, torch, rows: int, hbm_gbs: float, peak_src: str, reps: int = 20) -> dict:
+    """Device time of the fused q/k rmsnorm + rope3 on the q third of a bf16 QKV output of
+    `rows` tokens (40 heads x 128, rot 96), bf16 out; algorithmic bytes = q read + q written
+    + the cos/sin rows + the norm weights.  The inputs exceed L2."""
+    H, D, R = 40, 128, 96
+    inner = H * D
+    qkv = torch.randn((rows, 3 * inner), device="cuda").to(torch.bfloat16)
+    out = torch.empty((rows, inner), dtype=torch.bfloat16, device="cuda")
+    w = torch.ones(D, device="cuda")
+    ang = torch.rand((rows, R), device="cuda")
+    cs, sn = torch.cos(ang), torch.sin(ang)
+    for _ in range(3):
+        fh3.qk_norm_rope(qkv[:, :inner], w, cs, sn, H, D, R, 1e-6, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for r in range(reps):
+        src = qkv[:, (r % 2) * inner:(r % 2 + 1) * inner]       # q and k alternate
+        fh3.qk_norm_rope(src, w, cs, sn, H, D, R, 1e-6, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    nbytes = rows * inner * 2 * 2 + rows * R * 4 * 2 + D * 4
+    gbs = nbytes / us / 1e3
+    del qkv, out
+    return {"kernel": "qk_norm_rope_kernel", "rows": rows, "heads": H, "head_dim": D, "rot_dim": R,
+            "dtype": "bf16 in, bf16 out", "us_per_launch": round(us, 2), "bound": "hbm", "achieved": round(gbs, 1),
+            "unit": "GB/s", "peak": hbm_gbs, "frac": round(gbs / hbm_gbs, 4), "peak_source": f"{peak_src} hbm_gbs",
+            "bytes_per_launch": nbytes}
+
+
 def run_case(args):
     """One kernel's launches on a small case, for ncu (prints a one-line JSON summary)."""
     import torch
@@ -389,6 +423,15 @@ def run_case(args):
         for _ in range(args.case_reps):
             fh3.gemm(w, x, fh3.EPI_SWIGLU, out=y)
         shape = {"rows": args.case_rows, "in": D_MODEL, "out": 2 * FFN, "epilogue": "swiglu"}
+    elif args.case == "qk":
+        H, Dh, R = 40, 128, 96
+        qkv = torch.randn((args.case_rows, 3 * H * Dh), device="cuda").to(torch.bfloat16)
+        out = torch.empty((args.case_rows, H * Dh), dtype=torch.bfloat16, device="cuda")
+        ang = torch.rand((args.case_rows, R), device="cuda")
+        for r in range(args.case_reps):
+            fh3.qk_norm_rope(qkv[:, (r % 2) * H * Dh:(r % 2 + 1) * H * Dh], torch.ones(Dh, device="cuda"),
+                             torch.cos(ang), torch.sin(ang), H, Dh, R, 1e-6, out=out)
+        shape = {"rows": args.case_rows, "heads": H, "head_dim": Dh, "rot_dim": R}
     else:
         K, N = args.case_kn
         ws = [fh3.make_weights(N, K, seed=i, stream_id=3) for i in range(args.case_reps)]

@@ -8,6 +8,8 @@
 //   fh3cuda_qk_norm_rope_dev      per-head rmsnorm (:410-456) then fh3_rope3 (:458-505)
 //                                 of q or k straight from the QKV output, bit-exact
 // All HBM-bound streaming kernels with 16-byte accesses.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace {
@@ -159,6 +161,130 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(
     }
 }
 
+// The same for a compile-time head_dim HD and half rotation HALF (a multiple of 8,
+// or 0).  An 8-lane group takes kQkHeadsPerGroup heads of one token: the norm
+// weights and the token's cos/sin live in registers for all of them, the next
+// head's row is loaded while the current one is computed, and each lane keeps its
+// HD/8 strided values in registers after one staging pass; both halves of every
+// rotation pair (channels j and j + HALF) are in the same lane.
+constexpr int kQkHeadsPerGroup = 8;
+
+template <bool SRC_BF16, int HD>
+struct QkRaw {
+    using T = typename std::conditional<SRC_BF16, uint2, float4>::type;  // 4 elements per lane and step
+    T r[HD / 32];
+};
+
+template <bool SRC_BF16, int HD>
+__device__ __forceinline__ void qk_load(QkRaw<SRC_BF16, HD>& raw, const void* src, int64_t off, int l8) {
+#pragma unroll
+    for (int k = 0; k < HD / 32; ++k) {
+        if (SRC_BF16)
+            raw.r[k] = *reinterpret_cast<const typename QkRaw<SRC_BF16, HD>::T*>(
+                static_cast<const __nv_bfloat16*>(src) + off + 4 * l8 + 32 * k);
+        else
+            raw.r[k] = *reinterpret_cast<const typename QkRaw<SRC_BF16, HD>::T*>(
+                static_cast<const float*>(src) + off + 4 * l8 + 32 * k);
+    }
+}
+
+template <bool SRC_BF16, bool DST_BF16, int HD, int HALF>
+__global__ void __launch_bounds__(kQkThreads) qk_norm_rope_reg_kernel(
+    const void* __restrict__ src, int64_t ld_src, void* __restrict__ dst, int64_t ld_dst, const float* __restrict__ w,
+    const float* __restrict__ cs, const float* __restrict__ sn, int64_t nunits, int heads, float eps) {
+    static_assert(HD % 32 == 0 && HALF % 8 == 0 && 2 * HALF <= HD, "register path shape");
+    constexpr int NV = HD / 8;
+    constexpr int NR = HALF / 8 > 0 ? HALF / 8 : 1;
+    constexpr int ROT = 2 * HALF;
+    __shared__ __align__(16) float qk_stage[kQkThreads / 8][HD + 8];
+    const int l8 = threadIdx.x & 7;
+    const int grp = threadIdx.x >> 3;
+    const int64_t u = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 3) + grp;
+    if (u >= nunits) return;  // whole 8-lane groups leave together
+    const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+    const int chunks = (heads + kQkHeadsPerGroup - 1) / kQkHeadsPerGroup;
+    const int64_t i = u / chunks;
+    const int h0 = static_cast<int>(u - i * chunks) * kQkHeadsPerGroup;
+    const int h1 = min(heads, h0 + kQkHeadsPerGroup);
+    float* vec = qk_stage[grp];
+
+    float wr[NV];
+#pragma unroll
+    for (int m = 0; m < NV; ++m) wr[m] = __ldg(w + l8 + 8 * m);
+    float c0[NR], s0[NR], c1[NR], s1[NR];
+    if (HALF > 0) {
+#pragma unroll
+        for (int m = 0; m < NR; ++m) {
+            const int j = l8 + 8 * m;
+            c0[m] = __ldg(cs + i * ROT + j);
+            s0[m] = __ldg(sn + i * ROT + j);
+            c1[m] = __ldg(cs + i * ROT + HALF + j);
+            s1[m] = __ldg(sn + i * ROT + HALF + j);
+        }
+    }
+    QkRaw<SRC_BF16, HD> cur, nxt;
+    qk_load<SRC_BF16, HD>(cur, src, i * ld_src + static_cast<int64_t>(h0) * HD, l8);
+    for (int h = h0; h < h1; ++h) {
+        if (h + 1 < h1) qk_load<SRC_BF16, HD>(nxt, src, i * ld_src + static_cast<int64_t>(h + 1) * HD, l8);
+#pragma unroll
+        for (int k = 0; k < HD / 32; ++k) {
+            float4 f;
+            if (SRC_BF16) {
+                const uint2 q = *reinterpret_cast<const uint2*>(&cur.r[k]);
+                const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+                const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+                f = make_float4(a.x, a.y, b.x, b.y);
+            } else {
+                f = *reinterpret_cast<const float4*>(&cur.r[k]);
+            }
+            *reinterpret_cast<float4*>(vec + 4 * l8 + 32 * k) = f;
+        }
+        __syncwarp(gmask);
+        float val[NV];
+        float ss = 0.0f;
+#pragma unroll
+        for (int m = 0; m < NV; ++m) {
+            val[m] = vec[l8 + 8 * m];
+            ss = fmaf(val[m], val[m], ss);
+        }
+        ss = __fadd_rn(ss, __shfl_xor_sync(gmask, ss, 1, 8));
+        ss = __fadd_rn(ss, __shfl_xor_sync(gmask, ss, 2, 8));
+        ss = __fadd_rn(ss, __shfl_xor_sync(gmask, ss, 4, 8));
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(HD)), eps)));
+#pragma unroll
+        for (int m = 0; m < NV; ++m) val[m] = __fmul_rn(__fmul_rn(val[m], inv), wr[m]);
+        if (HALF > 0) {
+#pragma unroll
+            for (int m = 0; m < HALF / 8; ++m) {
+                const float v0 = val[m], v1 = val[m + HALF / 8];
+                val[m] = __fsub_rn(__fmul_rn(v0, c0[m]), __fmul_rn(v1, s0[m]));
+                val[m + HALF / 8] = __fadd_rn(__fmul_rn(v1, c1[m]), __fmul_rn(v0, s1[m]));
+            }
+        }
+        __syncwarp(gmask);  // every lane has read the staged input
+#pragma unroll
+        for (int m = 0; m < NV; ++m) vec[l8 + 8 * m] = val[m];
+        __syncwarp(gmask);
+        const int64_t oo = i * ld_dst + static_cast<int64_t>(h) * HD;
+#pragma unroll
+        for (int k = 0; k < HD / 32; ++k) {
+            const int d = 4 * l8 + 32 * k;
+            const float4 f = *reinterpret_cast<const float4*>(vec + d);
+            if (DST_BF16) {
+                const __nv_bfloat162 a = __floats2bfloat162_rn(f.x, f.y), b = __floats2bfloat162_rn(f.z, f.w);
+                uint2 q;
+                q.x = *reinterpret_cast<const uint32_t*>(&a);
+                q.y = *reinterpret_cast<const uint32_t*>(&b);
+                *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(dst) + oo + d) = q;
+            } else {
+                *reinterpret_cast<float4*>(static_cast<float*>(dst) + oo + d) = f;
+            }
+        }
+        __syncwarp(gmask);  // the stage is rewritten by the next head
+        if (h + 1 < h1) cur = nxt;
+    }
+}
+
 }  // namespace
 
 extern "C" int fh3cuda_qk_norm_rope_dev(const void* src, int src_bf16, int64_t ld_src, void* dst, int dst_bf16,
@@ -185,6 +311,30 @@ extern "C" int fh3cuda_qk_norm_rope_dev(const void* src, int src_bf16, int64_t l
     const unsigned grid = static_cast<unsigned>((nvec + groups - 1) / groups);
     const size_t smem = static_cast<size_t>(groups) * (head_dim + 8) * sizeof(float);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // head_dim 128 with rot_dim 0 / 96 / 128 (the DiT's q and k): the register path
+    if (head_dim == 128 && (rot_dim == 0 || rot_dim == 96 || rot_dim == 128)) {
+        const int64_t nunits = static_cast<int64_t>(n) * ((heads + kQkHeadsPerGroup - 1) / kQkHeadsPerGroup);
+        const unsigned rgrid = static_cast<unsigned>((nunits + groups - 1) / groups);
+#define FH3_QK_REG(SB, DB, HALF)                                                                     \
+    qk_norm_rope_reg_kernel<SB, DB, 128, HALF><<<rgrid, kQkThreads, 0, s>>>(src, ld_src, dst, ld_dst, norm_w, \
+                                                                           cos_t, sin_t, nunits, heads, eps)
+#define FH3_QK_REG_ROT(SB, DB)                                  \
+    do {                                                         \
+        if (rot_dim == 0) FH3_QK_REG(SB, DB, 0);                 \
+        else if (rot_dim == 96) FH3_QK_REG(SB, DB, 48);          \
+        else FH3_QK_REG(SB, DB, 64);                             \
+    } while (0)
+        if (src_bf16) {
+            if (dst_bf16) FH3_QK_REG_ROT(true, true);
+            else FH3_QK_REG_ROT(true, false);
+        } else {
+            if (dst_bf16) FH3_QK_REG_ROT(false, true);
+            else FH3_QK_REG_ROT(false, false);
+        }
+#undef FH3_QK_REG_ROT
+#undef FH3_QK_REG
+        return check_cuda(cudaGetLastError(), "qk_norm_rope launch");
+    }
 #define FH3_QK_LAUNCH(SB, DB)                                                                              \
     qk_norm_rope_kernel<SB, DB><<<grid, kQkThreads, smem, s>>>(src, ld_src, dst, ld_dst, norm_w, cos_t, sin_t, \
                                                                nvec, heads, head_dim, rot_dim, eps)
