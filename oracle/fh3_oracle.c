@@ -249,6 +249,52 @@ void oracle_rope3(float *x, const float *cos_t, const float *sin_t, int n, int h
     }
 }
 
+/* Restates fh3_attention (src/core/fh3_ops.c:587-695): dense, non-causal
+ * softmax attention over q/k/v laid out [n][heads][hd]; scale = 1/sqrtf(hd);
+ * keys in tiles of 64 with the reference's online softmax: scores = dot*scale
+ * (8-lane dot order), m_new = max(m, tile max), alpha = expf(m - m_new),
+ * l *= alpha, acc *= alpha, then per key p = expf(s - m_new), l += p,
+ * acc = fmaf(p, v, acc); o = acc * (l > 0 ? 1/l : 0). */
+void oracle_attention(const float *q, const float *k, const float *v, float *o, int n, int heads, int hd) {
+    if (!q || !k || !v || !o || n <= 0 || heads <= 0 || hd <= 0) return;
+    const float scale = 1.0f / sqrtf((float)hd);
+    int hi;
+#pragma omp parallel for schedule(static)
+    for (hi = 0; hi < heads * n; hi++) {
+        const int h = hi / n, i = hi % n;
+        float *acc = (float *)calloc((size_t)hd, sizeof(float));
+        float scores[64];
+        if (!acc) continue;
+        const float *qi = q + ((size_t)i * heads + h) * hd;
+        float *oi = o + ((size_t)i * heads + h) * hd;
+        float m = -1e30f, l = 0.0f;
+        for (int j0 = 0; j0 < n; j0 += 64) {
+            const int B = (j0 + 64 <= n) ? 64 : (n - j0);
+            for (int t = 0; t < B; t++) {
+                const float *kj = k + ((size_t)(j0 + t) * heads + h) * hd;
+                scores[t] = dot_ref_order(qi, kj, hd) * scale;
+            }
+            float mt = scores[0];
+            for (int t = 1; t < B; t++)
+                if (scores[t] > mt) mt = scores[t];
+            const float mn = (m > mt) ? m : mt;
+            const float alpha = expf(m - mn);
+            l *= alpha;
+            for (int d = 0; d < hd; d++) acc[d] *= alpha;
+            for (int t = 0; t < B; t++) {
+                const float *vj = v + ((size_t)(j0 + t) * heads + h) * hd;
+                const float p = expf(scores[t] - mn);
+                l += p;
+                for (int d = 0; d < hd; d++) acc[d] = fmaf(p, vj[d], acc[d]);
+            }
+            m = mn;
+        }
+        const float inv = (l > 0.0f) ? (1.0f / l) : 0.0f;
+        for (int d = 0; d < hd; d++) oi[d] = acc[d] * inv;
+        free(acc);
+    }
+}
+
 /* Restates fh3_modulate (src/core/fh3_ops.c:529-557): x = fma(x, 1+scale,
  * shift) on whole 8-wide vectors of each 1024-element chunk, and the unfused
  * x*(1+scale)+shift on a chunk's tail. shift/scale span the whole n*dim

@@ -22,6 +22,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libfh3ref.so")
+# the reference source tree (only where it exists: the container that builds the checker)
+REF_TREE = os.environ.get("FH3_REF_TREE", "/root/reference")
 
 Q4K = 12
 F32 = 0
@@ -69,6 +71,8 @@ class Oracle:
         lib.oracle_modulate.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.oracle_rope3.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int]
+        lib.oracle_attention.argtypes = [_c_f32p, _c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_int]
         lib.oracle_gate_residual.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.oracle_rng_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _c_f32p, ctypes.c_size_t]
         lib.oracle_quantize_q4k.restype = ctypes.c_int
@@ -128,6 +132,14 @@ class Oracle:
         self.lib.oracle_rope3(_ptr(x, _c_f32p), _ptr(c, _c_f32p), _ptr(s, _c_f32p), x.shape[0], heads,
                               head_dim, rot_dim)
         return x
+
+    def attention(self, q: np.ndarray, k: np.ndarray, v: np.ndarray, heads: int, hd: int) -> np.ndarray:
+        """q/k/v [n][heads*hd] fp32 -> o [n][heads*hd] (fh3_attention semantics)."""
+        q, k, v = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v))
+        o = np.empty_like(q)
+        self.lib.oracle_attention(_ptr(q, _c_f32p), _ptr(k, _c_f32p), _ptr(v, _c_f32p), _ptr(o, _c_f32p),
+                                  q.shape[0], heads, hd)
+        return o
 
     def qk_norm_rope(self, x: np.ndarray, w: np.ndarray, cos: np.ndarray, sin: np.ndarray, heads: int,
                      head_dim: int, rot_dim: int, eps: float) -> np.ndarray:
@@ -201,6 +213,8 @@ class Reference:
         lib.fh3_modulate.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.fh3_rope3.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int]
+        lib.fh3_attention.argtypes = [_c_f32p, _c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int]
         lib.fh3_gate_residual.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.fh3_rng_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _c_f32p, ctypes.c_size_t]
         self.lib = lib
@@ -247,6 +261,13 @@ class Reference:
         w = np.ascontiguousarray(w, dtype=np.float32)
         self.lib.fh3_rmsnorm(_ptr(x, _c_f32p), _ptr(w, _c_f32p), x.shape[0], x.shape[1], eps)
         return x
+
+    def attention(self, q, k, v, heads: int, hd: int):
+        q, k, v = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v))
+        o = np.empty_like(q)
+        self.lib.fh3_attention(_ptr(q, _c_f32p), _ptr(k, _c_f32p), _ptr(v, _c_f32p), _ptr(o, _c_f32p),
+                               q.shape[0], heads, hd)
+        return o
 
     def rope3(self, x, cos, sin, heads: int, head_dim: int, rot_dim: int):
         x = np.array(x, dtype=np.float32, copy=True, order="C")

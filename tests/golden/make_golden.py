@@ -85,6 +85,12 @@ def main() -> None:
     out["qkrope/x"], out["qkrope/w"], out["qkrope/cos"], out["qkrope/sin"] = x, wq, cs, sn
     out["qkrope/dims"] = np.array([n, H, D, R], dtype=np.int64)
     out["qkrope/y"] = r.rope3(r.rmsnorm(x.reshape(n * H, D), wq, 1e-6).reshape(n, H * D), cs, sn, H, D, R)
+    # dense attention (fh3_attention), by the reference: n not a multiple of the 64-key tile
+    n, H, D = 200, 2, 128
+    for nm, st in (("q", 1), ("k", 2), ("v", 3)):
+        out[f"attn/{nm}"] = o.rng_normal(80, st, n * H * D).reshape(n, H * D)
+    out["attn/dims"] = np.array([n, H, D], dtype=np.int64)
+    out["attn/y"] = r.attention(out["attn/q"], out["attn/k"], out["attn/v"], H, D)
     # fh3_rng_normal itself
     out["rng/seed7_stream3"] = r.rng_normal(7, 3, 1001)
     np.savez_compressed(os.path.join(HERE, "ref_cases.npz"), **out)

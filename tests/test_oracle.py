@@ -159,3 +159,28 @@ def test_rope3_bitwise_equals_live_reference(oracle, reference):
         s = rng.standard_normal((n, R)).astype(np.float32)
         a, b = oracle.rope3(x, c, s, H, D, R), reference.rope3(x, c, s, H, D, R)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (n, H, D, R)
+
+
+def test_attention_bitwise_equals_reference_case(oracle, golden_cases):
+    """fh3_attention on n = 200 (a partial 64-key tile), 2 heads x 128, computed by the reference."""
+    n, H, D = (int(v) for v in golden_cases["attn/dims"])
+    got = oracle.attention(golden_cases["attn/q"], golden_cases["attn/k"], golden_cases["attn/v"], H, D)
+    assert np.array_equal(got.view(np.uint32), golden_cases["attn/y"].view(np.uint32))
+
+
+def test_attention_matches_reference_op_fixture(oracle):
+    """The reference's tests/fixtures/ops/attention.bin (n = 777, 4 heads x 128; 6.4 MB, read in
+    place where the reference tree exists, not copied), with its own tolerance rule."""
+    import os
+    import struct
+    from oracle.oracle import REF_TREE
+    path = os.path.join(REF_TREE, "tests", "fixtures", "ops", "attention.bin")
+    if not os.path.exists(path):
+        pytest.skip("reference tree not present")
+    with open(path, "rb") as f:
+        b = f.read()
+    n, heads, hd = struct.unpack("<III", b[:12])
+    a = np.frombuffer(b[12:], np.float32)
+    c = n * heads * hd
+    q, k, v, ref = (a[i * c:(i + 1) * c].reshape(n, heads * hd) for i in range(4))
+    assert close_like_reference(oracle.attention(q, k, v, heads, hd), ref)
