@@ -26,7 +26,7 @@ from ._lib import (EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, F32, Q4_K, Fh3CudaE
 __all__ = [
     "Q4_K", "F32", "EPI_F32", "EPI_BF16", "EPI_SWIGLU", "EPI_RESID", "Fh3CudaError", "Q4KWeight",
     "init", "row_bytes", "dequant", "matmul", "gemv", "gemm", "matmul_host", "rmsnorm_modulate",
-    "to_bf16", "swiglu", "qk_norm_rope", "make_weights", "device_status",
+    "to_bf16", "swiglu", "qk_norm_rope", "attention", "make_weights", "device_status",
 ]
 
 _inited: set[int] = set()
@@ -180,6 +180,24 @@ def qk_norm_rope(src, norm_w, cos=None, sin=None, heads: int = 1, head_dim: int 
     check(load().fh3cuda_qk_norm_rope_dev(
         _ptr(src), int(src.dtype == torch.bfloat16), src.stride(0), _ptr(out), int(out.dtype == torch.bfloat16),
         out.stride(0), _ptr(norm_w), _ptr(cos), _ptr(sin), n, heads, head_dim, rot_dim, eps, _stream(stream)))
+    return out
+
+
+def attention(q, k, v, heads: int, head_dim: int = 128, out=None, out_bf16: bool = False, stream=None):
+    """fh3_attention on bf16 [n][>= heads*head_dim] views (e.g. the thirds of a QKV output);
+    returns o [n][heads*head_dim] (fp32, or bf16 with out_bf16)."""
+    torch = _torch()
+    for t in (q, k, v):
+        _ensure(t)
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise ValueError("q, k, v must be bf16 with contiguous rows")
+    n = q.shape[0]
+    if out is None:
+        out = torch.empty((n, heads * head_dim), dtype=torch.bfloat16 if out_bf16 else torch.float32,
+                          device=q.device)
+    check(load().fh3cuda_attention_dev(_ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0), _ptr(out),
+                                       int(out.dtype == torch.bfloat16), out.stride(0), n, heads, head_dim,
+                                       _stream(stream)))
     return out
 
 

@@ -30,7 +30,7 @@ EXPORTED = [
     "fh3cuda_upload_weights", "fh3cuda_release_weights", "fh3cuda_gemv_q4k_dev",
     "fh3cuda_gemm_q4k_dev", "fh3cuda_f32_to_bf16_dev", "fh3cuda_rmsnorm_modulate_dev",
     "fh3cuda_swiglu_dev", "fh3cuda_make_q4k_weights_dev", "fh3cuda_matmul_noalloc_dev",
-    "fh3cuda_qk_norm_rope_dev",
+    "fh3cuda_qk_norm_rope_dev", "fh3cuda_attention_dev",
 ]
 
 
@@ -89,6 +89,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         "fh3cuda_swiglu_dev": (c_int, [vp, vp, c_int, c_int, vp]),
         "fh3cuda_qk_norm_rope_dev": (c_int, [vp, c_int, i64, vp, c_int, i64, vp, vp, vp, c_int, c_int, c_int,
                                               c_int, ctypes.c_float, vp]),
+        "fh3cuda_attention_dev": (c_int, [vp, i64, vp, i64, vp, i64, vp, c_int, i64, c_int, c_int, c_int, vp]),
         "fh3cuda_make_q4k_weights_dev": (c_int, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, i64, i64,
                                                  vp, vp]),
     }

@@ -12,7 +12,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libfh3cuda.so")
-SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemm.cu", "ops.cu", "gen.cu", "noalloc.cu"]
+SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemm.cu", "ops.cu", "attention.cu", "gen.cu",
+           "noalloc.cu"]
 HEADERS = ["common.cuh"]
 
 NVCC_FLAGS = [

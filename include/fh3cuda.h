@@ -201,6 +201,17 @@ FH3CUDA_API int fh3cuda_qk_norm_rope_dev(const void *src, int src_bf16, int64_t 
                                          const float *sin_t, int n, int heads, int head_dim, int rot_dim,
                                          float eps, void *stream);
 
+/* Dense, non-causal softmax attention, fh3_attention (include/fh3/fh3.h:117,
+ * src/core/fh3_ops.c:587-695): o = softmax(q k^T / sqrt(128)) v per head, on
+ * bf16 q/k/v with fp32 softmax and accumulation (rel. error of bf16 operands,
+ * not bit-exact).  head_dim 128.  Element (token i, head h, channel d) of q is
+ * q[i*ldq + h*128 + d] (likewise k, v; o with ldo), so the thirds of a bf16
+ * QKV output can be passed directly.  o is fp32 (o_bf16 = 0) or bf16.  Strides
+ * multiples of 8, pointers 16-byte aligned. */
+FH3CUDA_API int fh3cuda_attention_dev(const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v,
+                                      int64_t ldv, void *o, int o_bf16, int64_t ldo, int n, int heads,
+                                      int head_dim, void *stream);
+
 /* Seeded synthetic Q4_K weights on the device: rows x n weights drawn from
  * scale * N(0,1) (Philox4x32-10 + Box-Muller), quantised with the same
  * per-block rule as the project's CPU quantiser.  Benchmark input generator;
