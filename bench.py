@@ -47,8 +47,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true",
-                    help="skip the GEMV (1..4 token) and q/k norm+rope measurements")
-    ap.add_argument("--case", choices=["gemm", "gemv", "qk"], default=None,
+                    help="skip the GEMV (1..4 token), q/k norm+rope and attention measurements")
+    ap.add_argument("--case", choices=["gemm", "gemv", "qk", "attn"], default=None,
                     help="run one kernel's launches on a small case (for ncu) instead of the bench")
     ap.add_argument("--case-rows", type=int, default=8192, help="--case gemm / qk: activation rows")
     ap.add_argument("--case-kn", type=int, nargs=2, default=(5120, 13824), help="--case gemv: in, out")
@@ -298,11 +298,13 @@ def run_ours(args):
                          f"{min(rows_s, T)} text rows = {f / 1e9:.1f} GFLOP in {dt:.2f} s; same weights as the GPU"}
 
     peaks, src = load_peaks()
-    gemv = qk = None
+    gemv = qk = attn = None
     if rank == 0 and not args.no_gemv:
         hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
         gemv = measure_gemv(fh3, torch, hbm, src)
         qk = measure_qk_norm_rope(fh3, torch, m_loc, hbm, src)
+        attn = measure_attention(fh3, torch, m_loc, float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])),
+                                 src)
     peak = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
     roof = None
     if gemm_tflops:
@@ -331,7 +333,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(float(mx[3])), "clocks": clk, "device_status": status,
-            "gemv": gemv, "qk_norm_rope": qk,
+            "gemv": gemv, "qk_norm_rope": qk, "attention": attn,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -410,6 +412,32 @@ def measure_qk_norm_rope(fh3, torch, rows: int, hbm_gbs: float, peak_src: str, r
             "bytes_per_launch": nbytes}
 
 
+def measure_attention(fh3, torch, rows: int, peak: float, peak_src: str, reps: int = 3) -> dict:
+    """Device time of one dense attention over `rows` tokens (40 heads x 128, bf16 q/k/v as
+    the thirds of a QKV output, bf16 o); FLOPs = 4 * rows^2 * 40 * 128 (QK^T and PV)."""
+    H, D = 40, 128
+    inner = H * D
+    qkv = torch.randn((rows, 3 * inner), device="cuda").to(torch.bfloat16)
+    o = torch.empty((rows, inner), dtype=torch.bfloat16, device="cuda")
+    q, k, v = qkv[:, :inner], qkv[:, inner:2 * inner], qkv[:, 2 * inner:]
+    fh3.attention(q, k, v, H, out=o)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fh3.attention(q, k, v, H, out=o)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 4.0 * rows * rows * H * D
+    tf = flops / (ms * 1e-3) / 1e12
+    del qkv, o
+    return {"kernel": "attention_kernel", "rows": rows, "heads": H, "head_dim": D, "ms_per_launch": round(ms, 3),
+            "bound": "tensor", "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak, "frac": round(tf / peak, 4),
+            "peak_source": f"{peak_src} bf16_tflops", "flop_per_launch": flops,
+            "note": "mma.sync bf16 (legacy tensor path); not part of the GEMM-only step"}
+
+
 def run_case(args):
     """One kernel's launches on a small case, for ncu (prints a one-line JSON summary)."""
     import torch
@@ -423,6 +451,13 @@ def run_case(args):
         for _ in range(args.case_reps):
             fh3.gemm(w, x, fh3.EPI_SWIGLU, out=y)
         shape = {"rows": args.case_rows, "in": D_MODEL, "out": 2 * FFN, "epilogue": "swiglu"}
+    elif args.case == "attn":
+        H, Dh = 40, 128
+        qkv = torch.randn((args.case_rows, 3 * H * Dh), device="cuda").to(torch.bfloat16)
+        out = torch.empty((args.case_rows, H * Dh), dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.case_reps):
+            fh3.attention(qkv[:, :H * Dh], qkv[:, H * Dh:2 * H * Dh], qkv[:, 2 * H * Dh:], H, out=out)
+        shape = {"rows": args.case_rows, "heads": H, "head_dim": Dh}
     elif args.case == "qk":
         H, Dh, R = 40, 128, 96
         qkv = torch.randn((args.case_rows, 3 * H * Dh), device="cuda").to(torch.bfloat16)
