@@ -217,10 +217,13 @@ __device__ __forceinline__ LaneCtx<NT> lane_ctx(int lane, int lanes) {
 
 // One super-block of rows g, g+8 against all tokens.  fsb: B fragments of the
 // super-block's 8 sub-blocks (stride `lanes` uint4), msb: its min-term B fragments.
+// fscale multiplies this super-block's contribution (the stream kernel's
+// per-super-block activation exponent; 1 elsewhere, where a per-token exponent is
+// applied at the end).
 template <int NT, int LANES = 0>  // LANES: fragment slots per sub-block when known at compile time
 __device__ __forceinline__ void compute_sb(const SuperBlock& sbk, int lane, int lanes_rt, const LaneCtx<NT>& lc,
                                            const uint4* __restrict__ fsb, const uint32_t* __restrict__ msb,
-                                           float (&acc)[2][NT]) {
+                                           float (&acc)[2][NT], float fscale = 1.0f) {
     const int lanes = LANES > 0 ? LANES : lanes_rt;
     // lane tq decodes the scales of its sub-blocks 2tq, 2tq+1 (rows g, g+8) and the
     // min-term A fragment; 6-bit fields as in get_scale_min_k4 (src/core/fh3_quant.c)
@@ -282,7 +285,7 @@ __device__ __forceinline__ void compute_sb(const SuperBlock& sbk, int lane, int 
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[i][nt] += ph[i][nt][0] + ph[i][nt][1];
+        for (int nt = 0; nt < NT; ++nt) acc[i][nt] = fmaf(fscale, ph[i][nt][0] + ph[i][nt][1], acc[i][nt]);
 }
 
 // Warp partials -> CTA partials (fixed order) -> cluster ranks (fixed order) -> y.
@@ -433,65 +436,64 @@ __device__ __forceinline__ int64_t stream_warp_of(int64_t u, int64_t GW, int64_t
     return ((u + 1) * GW - 1) / units;  // the warp whose run [w*U/GW, (w+1)*U/GW) holds unit u
 }
 
-// x (M x K fp32) -> this CTA's shared-memory B fragments, min-term fragments and
-// per-token exponents (the same values gemv_mma_prep_kernel writes to global memory).
+// x (M x K fp32) -> this CTA's shared-memory B fragments and min-term fragments in
+// one pass over x: a warp takes one super-block (256 elements) of one token at a
+// time, its own power of two 2^s (max|x| of the super-block below 2^14) and stores
+// fs[t][b] = 2^(24 - s), the factor that brings the super-block's partial sums back
+// to x's units (exact; |x| below 2^117).
 template <int M>
-__device__ __forceinline__ void build_fragments(const float* __restrict__ x, int64_t K, uint4* sfrag,
-                                                uint32_t* smfrag, int* sexp, float* sred) {
+__device__ __forceinline__ void build_fragments(const float* __restrict__ x, int nblk, uint4* sfrag,
+                                                uint32_t* smfrag, float* sfs) {
     constexpr int LANES = 8 * M;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    const int k4 = static_cast<int>(K / 4);
-    float am[M];
+    const int k4 = nblk * 64;
+    const int items = M * nblk;
+    constexpr int kBatch = 4;  // items of a warp whose loads are in flight together
+    for (int it0 = warp; it0 < items; it0 += kBatch * nw) {
+    float4 xv[kBatch][2];
 #pragma unroll
-    for (int t = 0; t < M; ++t) am[t] = 0.0f;
-    for (int i = threadIdx.x; i < k4; i += blockDim.x) {
-#pragma unroll
-        for (int t = 0; t < M; ++t) {
-            const float4 v = __ldg(x4 + t * k4 + i);
-            am[t] = fmaxf(am[t], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    for (int u = 0; u < kBatch; ++u) {
+        const int it = it0 + u * nw;
+        if (it < items) {
+            const int t = M == 1 ? 0 : it / nblk;
+            const int k0 = (it - t * nblk) * 256 + lane * 8;
+            xv[u][0] = __ldg(x4 + t * k4 + k0 / 4);
+            xv[u][1] = __ldg(x4 + t * k4 + k0 / 4 + 1);
         }
     }
 #pragma unroll
-    for (int t = 0; t < M; ++t) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) am[t] = fmaxf(am[t], __shfl_xor_sync(0xffffffffu, am[t], o));
-        if (lane == 0) sred[warp * M + t] = am[t];
-    }
-    __syncthreads();
-    if (threadIdx.x < M) {
-        float a = 0.0f;
-        for (int w = 0; w < nw; ++w) a = fmaxf(a, sred[w * M + threadIdx.x]);
-        int E = 0;
-        if (a > 0.0f && a <= 3.0e38f) frexpf(a, &E);  // a < 2^E
-        sexp[threadIdx.x] = 14 - E;                    // max|x| * 2^s < 2^14
-    }
-    __syncthreads();
-    // thread -> 8 consecutive elements (one lane's fragment of one sub-block); a warp
-    // covers one super-block of one token (K % 256 == 0)
-    const int per_tok = static_cast<int>(K / 8);
-    for (int idx = threadIdx.x; idx < M * per_tok; idx += blockDim.x) {
-        const int t = M == 1 ? 0 : idx / per_tok;
-        const int k0 = (idx - t * per_tok) * 8;
-        const int s = sexp[t];
-        const float4 v0 = __ldg(x4 + t * k4 + k0 / 4), v1 = __ldg(x4 + t * k4 + k0 / 4 + 1);
+    for (int u = 0; u < kBatch; ++u) {
+        const int it = it0 + u * nw;
+        if (it >= items) break;  // warp-uniform
+        const int t = M == 1 ? 0 : it / nblk;
+        const int b = it - t * nblk;
+        const int k0 = b * 256 + lane * 8;  // this lane: elements k0 .. k0+7 = quad piece of sub-block
+        const float4 v0 = xv[u][0], v1 = xv[u][1];
         const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float am = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) am = fmaxf(am, fabsf(e[u]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        int E = 0;
+        if (am > 0.0f && am <= 3.0e38f) frexpf(am, &E);  // am < 2^E
+        const int sx = 14 - E;                            // max|x| * 2^sx < 2^14
         uint32_t pl0[4], pl1[4];
 #pragma unroll
         for (int p = 0; p < 8; p += 2) {
             __half h0[2], h1[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-                const float v = ldexpf(e[perm8(p + u)], s);
+                const float v = ldexpf(e[perm8(p + u)], sx);
                 h0[u] = __float2half_rn(v);
                 h1[u] = __float2half_rn(v - __half2float(h0[u]));
             }
             pl0[p / 2] = pack_half2(h0[0], h0[1]);
             pl1[p / 2] = pack_half2(h1[0], h1[1]);
         }
-        const int sb = k0 >> 5;
         const int tq = lane & 3;
-        uint4* f = sfrag + sb * LANES + 2 * t * 4 + tq;
+        uint4* f = sfrag + (k0 >> 5) * LANES + 2 * t * 4 + tq;
         f[0] = make_uint4(pl0[0], pl0[1], pl0[2], pl0[3]);
         f[4] = make_uint4(pl1[0], pl1[1], pl1[2], pl1[3]);
         float sum = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
@@ -500,13 +502,15 @@ __device__ __forceinline__ void build_fragments(const float* __restrict__ x, int
         const float xa = __shfl_sync(0xffffffffu, sum, 8 * (lane & 3));
         const float xb = __shfl_sync(0xffffffffu, sum, 8 * (lane & 3) + 4);
         if (lane < 4) {
-            const float va = ldexpf(xa, s - 5), vb = ldexpf(xb, s - 5);
+            const float va = ldexpf(xa, sx - 5), vb = ldexpf(xb, sx - 5);
             const __half a0 = __float2half_rn(va), b0 = __float2half_rn(vb);
             const __half a1 = __float2half_rn(va - __half2float(a0)), b1 = __float2half_rn(vb - __half2float(b0));
-            uint32_t* m = smfrag + (k0 >> 8) * LANES + 2 * t * 4 + lane;
+            uint32_t* m = smfrag + b * LANES + 2 * t * 4 + lane;
             m[0] = pack_half2(a0, b0);
             m[4] = pack_half2(a1, b1);
         }
+        if (lane == 0) sfs[t * nblk + b] = ldexpf(1.0f, 24 - sx);
+    }
     }
     __syncthreads();
 }
@@ -522,12 +526,10 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
     const int warp = threadIdx.x >> 5;
     const int nw = blockDim.x >> 5;
     const int g = lane >> 2, tq = lane & 3;
-    const int64_t K = static_cast<int64_t>(nblk) * fh3::kQ4KBlock;
 
     uint4* sfrag = reinterpret_cast<uint4*>(gv_smem);
     uint32_t* smfrag = reinterpret_cast<uint32_t*>(sfrag + static_cast<size_t>(nblk) * 8 * LANES);
-    int* sexp = reinterpret_cast<int*>(smfrag + static_cast<size_t>(nblk) * LANES);  // [M]
-    float* sred = reinterpret_cast<float*>(sexp + 4);                                 // [nw][M]
+    float* sfs = reinterpret_cast<float*>(smfrag + static_cast<size_t>(nblk) * LANES);  // [M][nblk]
 
     // at most one warp per unit, so every run is non-empty and the runs meeting a
     // tile are consecutive warps (segment index = warp - first warp of the tile)
@@ -553,7 +555,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
     pdl_launch_dependents();  // the next kernel may start its own weight loads
 
     pdl_wait();  // x, y and the scratch are ours from here on
-    build_fragments<M>(x, K, sfrag, smfrag, sexp, sred);
+    build_fragments<M>(x, nblk, sfrag, smfrag, sfs);
+    const float* my_fs = sfs + (tq < M ? tq : M - 1) * nblk;  // this lane's token
 
     const LaneCtx<1> lc = lane_ctx<1>(lane, LANES);
     float acc[2][1] = {{0.0f}, {0.0f}};
@@ -566,8 +569,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
         const int64_t r0 = static_cast<int64_t>(t) * 16 + g, r1 = r0 + 8;
         if (nseg == 1) {
             if (tq < M) {
-                if (r0 < N) y[tq * ldy + r0] = ldexpf(acc[0][0], 24 - sexp[tq]) + (bias ? bias[r0] : 0.0f);
-                if (r1 < N) y[tq * ldy + r1] = ldexpf(acc[1][0], 24 - sexp[tq]) + (bias ? bias[r1] : 0.0f);
+                if (r0 < N) y[tq * ldy + r0] = acc[0][0] + (bias ? bias[r0] : 0.0f);
+                if (r1 < N) y[tq * ldy + r1] = acc[1][0] + (bias ? bias[r1] : 0.0f);
             }
         } else if (nseg > seg_max) {
             if (lane == 0) fh3::record_status(status, FH3_ERR);  // never write past the slots
@@ -578,22 +581,36 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
                 pp[g * M + tq] = acc[0][0];
                 pp[(g + 8) * M + tq] = acc[1][0];
             }
-            __threadfence();
+            // the warp's stores, then lane 0's release/acquire count: it publishes them at
+            // GPU scope and, for the last segment, acquires the other segments' stores
             __syncwarp();
             int old = 0;
-            if (lane == 0) old = atomicAdd(&counters[t], 1);
+            if (lane == 0)
+                asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(counters + t) : "memory");
             old = __shfl_sync(0xffffffffu, old, 0);
             if (old == nseg - 1) {  // last segment: add all in segment order
-                __threadfence();
+                __syncwarp();
                 if (tq < M) {
                     const float* pt = partials + static_cast<int64_t>(t) * seg_max * 16 * M;
                     float v0 = 0.0f, v1 = 0.0f;
-                    for (int q = 0; q < nseg; ++q) {
-                        v0 += __ldcg(pt + (q * 16 + g) * M + tq);
-                        v1 += __ldcg(pt + (q * 16 + g + 8) * M + tq);
+                    for (int q0 = 0; q0 < nseg; q0 += 4) {  // four segments' loads in flight, added in order
+                        float a0[4], a1[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const bool ok = q0 + u < nseg;
+                            a0[u] = ok ? __ldcg(pt + ((q0 + u) * 16 + g) * M + tq) : 0.0f;
+                            a1[u] = ok ? __ldcg(pt + ((q0 + u) * 16 + g + 8) * M + tq) : 0.0f;
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (q0 + u < nseg) {
+                                v0 += a0[u];
+                                v1 += a1[u];
+                            }
+                        }
                     }
-                    if (r0 < N) y[tq * ldy + r0] = ldexpf(v0, 24 - sexp[tq]) + (bias ? bias[r0] : 0.0f);
-                    if (r1 < N) y[tq * ldy + r1] = ldexpf(v1, 24 - sexp[tq]) + (bias ? bias[r1] : 0.0f);
+                    if (r0 < N) y[tq * ldy + r0] = v0 + (bias ? bias[r0] : 0.0f);
+                    if (r1 < N) y[tq * ldy + r1] = v1 + (bias ? bias[r1] : 0.0f);
                 }
                 if (lane == 0) counters[t] = 0;
             }
@@ -601,7 +618,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
         acc[0][0] = acc[1][0] = 0.0f;
     };
     auto step = [&](const SuperBlock& cur, int i) {
-        compute_sb<1, LANES>(cur, lane, LANES, lc, sfrag + b * 8 * LANES, smfrag + b * LANES, acc);
+        compute_sb<1, LANES>(cur, lane, LANES, lc, sfrag + b * 8 * LANES, smfrag + b * LANES, acc, my_fs[b]);
         if (b == nblk - 1 || i == n - 1) finish_segment();
         if (++b == nblk) {
             b = 0;
@@ -743,7 +760,7 @@ int launch_stream(const Fh3CudaW* w, const float* x, float* y, const float* bias
     const int64_t N = w->out, K = w->in;
     const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
     constexpr int LANES = 8 * M;
-    const size_t smem = static_cast<size_t>(nblk) * (8 * LANES * 16 + LANES * 4) + (kStreamWarps * M + 8) * 4;
+    const size_t smem = static_cast<size_t>(nblk) * (8 * LANES * 16 + LANES * 4 + M * 4);
     if (smem > 227 * 1024) return 1;
     const int sms = ctx_sms(c);
     const int64_t ntiles = (N + 15) / 16;
