@@ -88,13 +88,21 @@ static uint16_t f2h(float f) {
     return (uint16_t)(sign | out);
 }
 
-/* Restates fh3_row_bytes (src/core/fh3_quant.c:14-34) for the two types this
- * path uses: F32 (:17) and Q4_K (:27). */
+/* Restates fh3_row_bytes (src/core/fh3_quant.c:14-34) for the types fh3_dequant
+ * can expand (:284-318): F32, F16, BF16, Q8_0 and the K-quants Q2_K..Q6_K. */
 size_t oracle_row_bytes(int type, int64_t n) {
     if (n <= 0) return 0;
-    if (type == 0) return (size_t)n * 4;
-    if (type == Q4K_TYPE) return (size_t)((n + 255) / 256) * Q4K_BYTES;
-    return 0;
+    switch (type) {
+        case 0: return (size_t)n * 4;                      /* F32  */
+        case 1: case 30: return (size_t)n * 2;             /* F16, BF16 */
+        case 8: return (size_t)((n + 31) / 32) * 34;       /* Q8_0 */
+        case 10: return (size_t)((n + 255) / 256) * 84;    /* Q2_K */
+        case 11: return (size_t)((n + 255) / 256) * 110;   /* Q3_K */
+        case Q4K_TYPE: return (size_t)((n + 255) / 256) * Q4K_BYTES;
+        case 13: return (size_t)((n + 255) / 256) * 176;   /* Q5_K */
+        case 14: return (size_t)((n + 255) / 256) * 210;   /* Q6_K */
+        default: return 0;
+    }
 }
 
 /* Unpack the 6-bit scale and min of sub-block j (0..7) from the 12 packed
@@ -139,6 +147,155 @@ void oracle_dequant_q4k(const uint8_t *src, float *dst, int64_t n) {
     }
 }
 
+/* Restates dequant_q8_0 (src/core/fh3_quant.c:58-71): blocks of 32 int8 with one
+ * fp16 scale, w = (float)q * d. */
+static void dq_q8_0(const uint8_t *src, float *dst, int64_t n) {
+    for (int64_t b = 0; b < n / 32; b++) {
+        const uint8_t *blk = src + b * 34;
+        uint16_t dh;
+        memcpy(&dh, blk, 2);
+        const float d = h2f(dh);
+        for (int i = 0; i < 32; i++) dst[b * 32 + i] = (float)(int8_t)blk[2 + i] * d;
+    }
+}
+
+/* Restates dequant_q2_k (src/core/fh3_quant.c:73-108): 84-byte blocks, 16 bytes of
+ * 4-bit scale|min pairs, 64 bytes of 2-bit quants, fp16 d and dmin at 80/82; for
+ * chunk c (2) and shift s (4) the two 16-weight groups g0 = 2(4c+s), g0+1 read
+ * bytes 0..15 / 16..31 of the chunk: w = (d*sc)*q - dmin*m. */
+static void dq_q2_k(const uint8_t *src, float *dst, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t *blk = src + b * 84;
+        uint16_t dh, mh;
+        memcpy(&dh, blk + 80, 2);
+        memcpy(&mh, blk + 82, 2);
+        const float d = h2f(dh), dmin = h2f(mh);
+        float *out = dst + b * 256;
+        for (int c = 0; c < 2; c++) {
+            for (int sh = 0; sh < 4; sh++) {
+                for (int half = 0; half < 2; half++) {
+                    const int grp = (c * 4 + sh) * 2 + half;
+                    const float dl = d * (float)(blk[grp] & 0x0F);
+                    const float ml = dmin * (float)(blk[grp] >> 4);
+                    for (int l = 0; l < 16; l++) {
+                        const int q = (blk[16 + c * 32 + half * 16 + l] >> (2 * sh)) & 3;
+                        const float prod = dl * (float)q;
+                        *out++ = prod - ml;
+                    }
+                }
+            }
+        }
+    }
+}
+
+/* Restates dequant_q3_k (src/core/fh3_quant.c:110-152): 110-byte blocks: hmask[32],
+ * qs[64], 12 scale bytes (8 low nibbles + 4 bytes of 2-bit highs), fp16 d at 108;
+ * 16 groups of 16: scale = (low | high<<4) - 32, q = low2 - (hbit ? 0 : 4),
+ * w = (d*scale) * q. */
+static void dq_q3_k(const uint8_t *src, float *dst, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t *blk = src + b * 110;
+        const uint8_t *hm = blk, *qs = blk + 32, *sr = blk + 96;
+        uint16_t dh;
+        memcpy(&dh, blk + 108, 2);
+        const float d = h2f(dh);
+        float *out = dst + b * 256;
+        for (int g = 0; g < 16; g++) {
+            const int lo = (g < 8) ? (sr[g] & 0x0F) : ((sr[g - 8] >> 4) & 0x0F);
+            const int hi = (sr[8 + (g % 4)] >> ((g / 4) * 2)) & 3;
+            const float dl = d * (float)((lo | (hi << 4)) - 32);
+            const int c = g / 8, rem = g % 8;
+            const int shl = (rem / 2) * 2, offl = c * 32 + (rem % 2) * 16;
+            const int shh = g / 2, offh = (g % 2) * 16;
+            for (int l = 0; l < 16; l++) {
+                const int q = ((qs[offl + l] >> shl) & 3) - ((((hm[offh + l] >> shh) & 1) ^ 1) << 2);
+                *out++ = dl * (float)q;
+            }
+        }
+    }
+}
+
+/* Restates dequant_q5_k (src/core/fh3_quant.c:198-240): Q4_K's layout plus 32 bytes
+ * of fifth bits (qh) before the nibbles: q = nibble | ((qh[l] >> g) & 1) << 4,
+ * w = (d*sc)*q - dmin*m. */
+static void dq_q5_k(const uint8_t *src, float *dst, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t *blk = src + b * 176;
+        uint16_t dh, mh;
+        memcpy(&dh, blk, 2);
+        memcpy(&mh, blk + 2, 2);
+        const float d = h2f(dh), dmin = h2f(mh);
+        const uint8_t *qh = blk + 16, *qs = blk + 48;
+        float *out = dst + b * 256;
+        for (int g = 0; g < 8; g++) {
+            int sc, m;
+            q4k_scale_min(blk + 4, g, &sc, &m);
+            const float dl = d * (float)sc, ml = dmin * (float)m;
+            for (int l = 0; l < 32; l++) {
+                const int q = ((qs[(g / 2) * 32 + l] >> ((g % 2) * 4)) & 0x0F) | (((qh[l] >> g) & 1) << 4);
+                const float prod = dl * (float)q;
+                out[g * 32 + l] = prod - ml;
+            }
+        }
+    }
+}
+
+/* Restates dequant_q6_k (src/core/fh3_quant.c:242-282): 210-byte blocks: ql[128]
+ * (4 low bits), qh[64] (2 high bits), 16 int8 scales, fp16 d at 208; 16 groups of
+ * 16: q = (low | high<<4) - 32, w = (d*scale) * q. */
+static void dq_q6_k(const uint8_t *src, float *dst, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t *blk = src + b * 210;
+        const uint8_t *ql = blk, *qh = blk + 128;
+        const int8_t *sc = (const int8_t *)(blk + 192);
+        uint16_t dh;
+        memcpy(&dh, blk + 208, 2);
+        const float d = h2f(dh);
+        float *out = dst + b * 256;
+        for (int g = 0; g < 16; g++) {
+            const float dl = d * (float)sc[g];
+            const int c = g / 8, rem = g % 8;
+            const int shl = (rem / 4) * 4, offl = c * 64 + (rem % 4) * 16;
+            const int shh = (rem / 2) * 2, offh = c * 32 + (rem % 2) * 16;
+            for (int l = 0; l < 16; l++) {
+                const int q = (((ql[offl + l] >> shl) & 0x0F) | (((qh[offh + l] >> shh) & 3) << 4)) - 32;
+                out[g * 16 + l] = dl * (float)q;
+            }
+        }
+    }
+}
+
+/* Restates fh3_dequant (src/core/fh3_quant.c:284-318): one row of n weights of any
+ * type above into fp32 (exact for F32/F16/BF16).  Returns -8 for other types. */
+int oracle_dequant(int type, const uint8_t *src, float *dst, int64_t n) {
+    if (!src || !dst || n <= 0) return -8;
+    switch (type) {
+        case 0: memcpy(dst, src, (size_t)n * 4); return 0;
+        case 1:
+            for (int64_t i = 0; i < n; i++) {
+                uint16_t h;
+                memcpy(&h, src + 2 * i, 2);
+                dst[i] = h2f(h);
+            }
+            return 0;
+        case 30:
+            for (int64_t i = 0; i < n; i++) {
+                uint16_t h;
+                memcpy(&h, src + 2 * i, 2);
+                const uint32_t u = (uint32_t)h << 16;
+                memcpy(dst + i, &u, 4);
+            }
+            return 0;
+        case 8: dq_q8_0(src, dst, n); return 0;
+        case 10: dq_q2_k(src, dst, n); return 0;
+        case 11: dq_q3_k(src, dst, n); return 0;
+        case Q4K_TYPE: oracle_dequant_q4k(src, dst, n); return 0;
+        case 13: dq_q5_k(src, dst, n); return 0;
+        case 14: dq_q6_k(src, dst, n); return 0;
+        default: return -8;
+    }
+}
+
 /* fixed 8-lane tree of src/core/fh3_ops.c:19-27 */
 static float tree8(const float a[8]) {
     float s01 = a[0] + a[1], s23 = a[2] + a[3];
@@ -173,12 +330,8 @@ int oracle_matmul(int type, const uint8_t *wdata, int64_t in, int64_t out,
     for (o = 0; o < out; o++) {
         float *wrow = (float *)malloc((size_t)in * sizeof(float));
         if (!wrow) continue;
-        if (type == Q4K_TYPE) {
-            memset(wrow, 0, (size_t)in * sizeof(float));
-            oracle_dequant_q4k(wdata + (size_t)o * rb, wrow, in);
-        } else {
-            memcpy(wrow, wdata + (size_t)o * rb, (size_t)in * 4);
-        }
+        memset(wrow, 0, (size_t)in * sizeof(float));
+        oracle_dequant(type, wdata + (size_t)o * rb, wrow, in);
         for (int t = 0; t < n_tok; t++) {
             float d = dot_ref_order(x + (size_t)t * in, wrow, in);
             if (bias) d += bias[o];

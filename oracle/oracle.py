@@ -63,6 +63,8 @@ class Oracle:
         lib.oracle_row_bytes.restype = ctypes.c_size_t
         lib.oracle_row_bytes.argtypes = [ctypes.c_int, ctypes.c_int64]
         lib.oracle_dequant_q4k.argtypes = [_c_u8p, _c_f32p, ctypes.c_int64]
+        lib.oracle_dequant.restype = ctypes.c_int
+        lib.oracle_dequant.argtypes = [ctypes.c_int, _c_u8p, _c_f32p, ctypes.c_int64]
         lib.oracle_matmul.restype = ctypes.c_int
         lib.oracle_matmul.argtypes = [ctypes.c_int, _c_u8p, ctypes.c_int64, ctypes.c_int64,
                                       _c_f32p, _c_f32p, ctypes.c_int, _c_f32p]
@@ -90,6 +92,18 @@ class Oracle:
         raw = np.ascontiguousarray(raw, dtype=np.uint8)
         out = np.zeros(n, dtype=np.float32)
         self.lib.oracle_dequant_q4k(_ptr(raw, _c_u8p), _ptr(out, _c_f32p), n)
+        return out
+
+    def dequant(self, type_: int, raw: np.ndarray, rows: int, n: int) -> np.ndarray:
+        """rows x n weights of any fh3_dequant type -> fp32 [rows][n]."""
+        raw = np.ascontiguousarray(raw, dtype=np.uint8)
+        rb = self.row_bytes(type_, n)
+        out = np.zeros((rows, n), dtype=np.float32)
+        for r in range(rows):
+            row = np.ascontiguousarray(raw[r * rb:(r + 1) * rb])
+            rc = self.lib.oracle_dequant(type_, _ptr(row, _c_u8p), _ptr(out[r], _c_f32p), n)
+            if rc != 0:
+                raise ValueError(f"oracle_dequant: type {type_} not supported")
         return out
 
     def dequant_rows(self, raw: np.ndarray, rows: int, n: int) -> np.ndarray:

@@ -5,6 +5,8 @@
      tests/fixtures/quant/matmul_ref.bin  -> matmul_ref.bin  (fp64 numpy matmul output)
    Their layouts are documented in the reference's tools/emit_quant_fixtures.py:75-81,134-141
    and read by tests/unit/test_quant.c:54-81 and tests/unit/test_matmul.c:196-231.
+   The other formats' fixtures tests/fixtures/quant/{F16,BF16,Q8_0,Q2_K,Q3_K,Q5_K,Q6_K}.bin (same
+   layout as Q4_K.bin: <u32 type, rows, cols, nbytes>, raw bytes, gguf-py's fp32 dequantisation).
    Also the op fixtures tests/fixtures/ops/{rmsnorm,rope3}.bin -> {rmsnorm,rope3}.bin,
    read by the reference's tests/unit/test_ops.c:58-96 (<u32 n, u32 dim, f32 eps>, x, w, ref)
    and :98-140 (<u32 n, heads, head_dim, rot_dim>, x, cos, sin, ref).
@@ -48,7 +50,8 @@ def main() -> None:
     ap.add_argument("--ref", default="/root/reference")
     args = ap.parse_args()
     fx = os.path.join(args.ref, "tests", "fixtures", "quant")
-    for name in ("Q4_K.bin", "matmul_ref.bin"):
+    for name in ("Q4_K.bin", "matmul_ref.bin", "F16.bin", "BF16.bin", "Q8_0.bin", "Q2_K.bin", "Q3_K.bin",
+                 "Q5_K.bin", "Q6_K.bin"):
         shutil.copyfile(os.path.join(fx, name), os.path.join(HERE, name))
     for name in ("rmsnorm.bin", "rope3.bin"):
         shutil.copyfile(os.path.join(args.ref, "tests", "fixtures", "ops", name), os.path.join(HERE, name))
@@ -91,6 +94,20 @@ def main() -> None:
         out[f"attn/{nm}"] = o.rng_normal(80, st, n * H * D).reshape(n, H * D)
     out["attn/dims"] = np.array([n, H, D], dtype=np.int64)
     out["attn/y"] = r.attention(out["attn/q"], out["attn/k"], out["attn/v"], H, D)
+    # fh3_matmul on the other formats' fixture weights (rows x 512), by the reference
+    import struct
+    for i, nm in enumerate(("F16", "BF16", "Q8_0", "Q2_K", "Q3_K", "Q5_K", "Q6_K")):
+        with open(os.path.join(HERE, f"{nm}.bin"), "rb") as f:
+            b = f.read()
+        t, rows, cols, nb = struct.unpack("<IIII", b[:16])
+        w = np.frombuffer(b[16:16 + nb], np.uint8).copy()
+        x = o.rng_normal(90 + i, 1, 5 * cols).reshape(5, cols)
+        bias = o.rng_normal(90 + i, 2, rows)
+        out[f"fmt_{nm}/w"] = w
+        out[f"fmt_{nm}/x"] = x
+        out[f"fmt_{nm}/bias"] = bias
+        out[f"fmt_{nm}/dims"] = np.array([t, cols, rows, 5], dtype=np.int64)
+        out[f"fmt_{nm}/y"] = r.matmul(t, w, cols, rows, x, bias)
     # fh3_rng_normal itself
     out["rng/seed7_stream3"] = r.rng_normal(7, 3, 1001)
     np.savez_compressed(os.path.join(HERE, "ref_cases.npz"), **out)

@@ -184,3 +184,47 @@ def test_attention_matches_reference_op_fixture(oracle):
     c = n * heads * hd
     q, k, v, ref = (a[i * c:(i + 1) * c].reshape(n, heads * hd) for i in range(4))
     assert close_like_reference(oracle.attention(q, k, v, heads, hd), ref)
+
+
+FORMATS = ("F16", "BF16", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K")
+
+
+def _read_format_golden(name):
+    import os
+    import struct
+    from conftest import GOLDEN
+    with open(os.path.join(GOLDEN, f"{name}.bin"), "rb") as f:
+        b = f.read()
+    t, rows, cols, nb = struct.unpack("<IIII", b[:16])
+    raw = np.frombuffer(b[16:16 + nb], np.uint8).copy()
+    ref = np.frombuffer(b[16 + nb:], np.float32).reshape(rows, cols).copy()
+    return t, rows, cols, raw, ref
+
+
+@pytest.mark.parametrize("name", FORMATS)
+def test_dequant_formats_match_reference_goldens(oracle, name):
+    """tests/fixtures/quant/<format>.bin of the reference (gguf-py 0.19.0 output): bit-exact."""
+    t, rows, cols, raw, ref = _read_format_golden(name)
+    got = oracle.dequant(t, raw, rows, cols)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", [f for f in FORMATS if f != "Q4_K"])
+def test_matmul_formats_bitwise_equal_reference_cases(oracle, golden_cases, name):
+    t, K, N, M = (int(v) for v in golden_cases[f"fmt_{name}/dims"])
+    got = oracle.matmul(t, golden_cases[f"fmt_{name}/w"], K, N, golden_cases[f"fmt_{name}/x"],
+                        golden_cases[f"fmt_{name}/bias"])
+    assert np.array_equal(got.view(np.uint32), golden_cases[f"fmt_{name}/y"].view(np.uint32))
+
+
+def test_dequant_formats_bitwise_equal_live_reference_on_random_blocks(oracle, reference):
+    rng = np.random.default_rng(11)
+    for t in (1, 30, 8, 10, 11, 12, 13, 14):
+        n = 768
+        rb = oracle.row_bytes(t, n)
+        raw = rng.integers(0, 256, size=rb * 2, dtype=np.uint8)
+        got = oracle.dequant(t, raw, 2, n)
+        live = np.stack([reference.dequant(t, raw[i * rb:(i + 1) * rb], n) for i in range(2)])
+        nan = np.isnan(got)
+        assert np.array_equal(nan, np.isnan(live)), t
+        assert np.array_equal(got[~nan].view(np.uint32), live[~nan].view(np.uint32)), t
