@@ -20,11 +20,12 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from ._lib import (EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, F32, Q4_K, Fh3CudaError, Fh3CudaW,
+from ._lib import (BF16, EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, F16, F32, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, Q8_0,
+                   Fh3CudaError, Fh3CudaW,
                    check, load)
 
 __all__ = [
-    "Q4_K", "F32", "EPI_F32", "EPI_BF16", "EPI_SWIGLU", "EPI_RESID", "Fh3CudaError", "Q4KWeight",
+    "Q4_K", "F32", "F16", "BF16", "Q8_0", "Q2_K", "Q3_K", "Q5_K", "Q6_K", "Weight", "EPI_F32", "EPI_BF16", "EPI_SWIGLU", "EPI_RESID", "Fh3CudaError", "Q4KWeight",
     "init", "row_bytes", "dequant", "matmul", "gemv", "gemm", "matmul_host", "rmsnorm_modulate",
     "to_bf16", "swiglu", "qk_norm_rope", "attention", "make_weights", "device_status",
 ]
@@ -69,26 +70,32 @@ def row_bytes(type_: int, n: int) -> int:
 
 @dataclass
 class Q4KWeight:
-    """A Q4_K weight matrix resident in HBM: `out` rows of `in_` weights (Fh3W)."""
-    data: object  # torch.uint8 tensor on the device, out * row_bytes(Q4_K, in_) bytes
+    """A weight matrix resident in HBM: `out` rows of `in_` weights of format `type`
+    (Fh3W; Q4_K unless given)."""
+    data: object  # torch.uint8 tensor on the device, out * row_bytes(type, in_) bytes
     in_: int
     out: int
+    type: int = Q4_K
 
     @property
     def desc(self) -> Fh3CudaW:
-        return Fh3CudaW(Q4_K, self.in_, self.out, self.data.data_ptr())
+        return Fh3CudaW(self.type, self.in_, self.out, self.data.data_ptr())
 
     @property
     def nbytes(self) -> int:
-        return self.out * row_bytes(Q4_K, self.in_)
+        return self.out * row_bytes(self.type, self.in_)
 
     @classmethod
-    def from_bytes(cls, raw: np.ndarray, in_: int, out: int, device: int | str = "cuda") -> "Q4KWeight":
+    def from_bytes(cls, raw: np.ndarray, in_: int, out: int, device: int | str = "cuda",
+                   type_: int = Q4_K) -> "Q4KWeight":
         torch = _torch()
         raw = np.ascontiguousarray(raw, dtype=np.uint8)
-        if raw.size != out * row_bytes(Q4_K, in_):
-            raise ValueError("byte count does not match out * row_bytes(Q4_K, in)")
-        return cls(torch.from_numpy(raw).to(device), in_, out)
+        if raw.size != out * row_bytes(type_, in_):
+            raise ValueError("byte count does not match out * row_bytes(type, in)")
+        return cls(torch.from_numpy(raw).to(device), in_, out, type_)
+
+
+Weight = Q4KWeight  # any format fh3_dequant expands
 
 
 def dequant(type_: int, src, n: int, rows: int = 1, out=None, stream=None):
@@ -228,7 +235,7 @@ def device_status(stream=None) -> int:
 
 
 def matmul_host(w_raw: np.ndarray, in_: int, out: int, x: np.ndarray, bias: np.ndarray | None = None,
-                y: np.ndarray | None = None) -> np.ndarray:
+                y: np.ndarray | None = None, type_: int = Q4_K) -> np.ndarray:
     """fh3_matmul on HOST buffers through the C drop-in (fh3cuda_matmul).
 
     Raises Fh3CudaError with the drop-in's recorded status on failure.
@@ -242,7 +249,7 @@ def matmul_host(w_raw: np.ndarray, in_: int, out: int, x: np.ndarray, bias: np.n
     if y is None:
         y = np.empty((n_tok, out), dtype=np.float32)
     b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
-    d = Fh3CudaW(Q4_K, in_, out, w_raw.ctypes.data)
+    d = Fh3CudaW(type_, in_, out, w_raw.ctypes.data)
     L.fh3cuda_matmul(ctypes.byref(d), x.ctypes.data, y.ctypes.data, n_tok,
                      None if b is None else b.ctypes.data)
     rc = L.fh3cuda_take_status()

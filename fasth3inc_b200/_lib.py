@@ -12,6 +12,8 @@ from . import build as _build
 
 Q4_K = 12
 F32 = 0
+# the other formats fh3_dequant expands (fh3's enum values, include/fh3/fh3.h:64-78)
+F16, BF16, Q8_0, Q2_K, Q3_K, Q5_K, Q6_K = 1, 30, 8, 10, 11, 13, 14
 
 FH3_OK = 0
 FH3_ERR = -1

@@ -47,7 +47,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         return LIB
     cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), "-I", os.path.join(ROOT, "include"), "-o", LIB + ".tmp"]
     cmd += [os.path.join(CSRC, f) for f in SOURCES]
-    cmd += ["-lcuda"] if False else []
+    cmd += ["-lcublas"]  # plain fp32 GEMMs of the non-Q4_K weight formats
     if verbose:
         print(" ".join(cmd))
     out = subprocess.run(cmd, capture_output=True, text=True)

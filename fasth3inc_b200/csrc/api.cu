@@ -7,17 +7,25 @@
 #include <mutex>
 #include <vector>
 
+#include <cublas_v2.h>
+
 #include "common.cuh"
 
 namespace fh3host {
+
+// scratch slots: 0 bf16 activations of the GEMM, 1 staged weights, 2-4 the host
+// drop-in's x / y / bias, 5 GEMV fragments, 6 split-tile partials, 7 tile counters,
+// 8 fp32 weight rows of the non-Q4_K formats
+constexpr int kScratchSlots = 9;
 
 struct DevCtx {
     int device = -1;
     int sms = 0;
     int* d_status = nullptr;      // written by bounded device-side waits
     cudaStream_t stream = nullptr; // the drop-in's stream
-    void* scratch_ptr[8] = {};
-    size_t scratch_size[8] = {};
+    void* scratch_ptr[kScratchSlots] = {};
+    size_t scratch_size[kScratchSlots] = {};
+    cublasHandle_t blas = nullptr; // fp32 GEMMs of the non-Q4_K formats (created on first use)
 };
 
 namespace {
@@ -71,7 +79,7 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
 }
 
 void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s) {
-    if (!c || slot < 0 || slot >= 8) return nullptr;
+    if (!c || slot < 0 || slot >= kScratchSlots) return nullptr;
     if (c->scratch_size[slot] >= bytes && c->scratch_ptr[slot]) return c->scratch_ptr[slot];
     // grow: earlier work on this stream may still read the old buffer
     if (c->scratch_ptr[slot]) {
@@ -92,7 +100,7 @@ void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s) {
 }
 
 void* scratch_zeroed(DevCtx* c, int slot, size_t bytes, cudaStream_t s) {
-    if (!c || slot < 0 || slot >= 8) return nullptr;
+    if (!c || slot < 0 || slot >= kScratchSlots) return nullptr;
     const void* before = c->scratch_ptr[slot];
     const size_t size_before = c->scratch_size[slot];
     void* p = scratch(c, slot, bytes, s);
@@ -170,12 +178,98 @@ extern "C" int fh3cuda_device_status(void* stream) {
 }
 
 extern "C" size_t fh3cuda_row_bytes(int type, int64_t n) {
-    // fh3_row_bytes (src/core/fh3_quant.c:14-34) for F32 (:17) and Q4_K (:27)
+    // fh3_row_bytes (src/core/fh3_quant.c:14-34) for the formats fh3_dequant expands
     if (n <= 0) return 0;
-    if (type == FH3CUDA_TYPE_F32) return static_cast<size_t>(n) * 4;
-    if (type == FH3CUDA_TYPE_Q4_K) return static_cast<size_t>((n + 255) / 256) * fh3::kQ4KBytes;
-    return 0;
+    switch (type) {
+        case FH3CUDA_TYPE_F32: return static_cast<size_t>(n) * 4;
+        case FH3CUDA_TYPE_F16:
+        case FH3CUDA_TYPE_BF16: return static_cast<size_t>(n) * 2;
+        case FH3CUDA_TYPE_Q8_0: return static_cast<size_t>((n + 31) / 32) * 34;
+        case FH3CUDA_TYPE_Q2_K: return static_cast<size_t>((n + 255) / 256) * 84;
+        case FH3CUDA_TYPE_Q3_K: return static_cast<size_t>((n + 255) / 256) * 110;
+        case FH3CUDA_TYPE_Q4_K: return static_cast<size_t>((n + 255) / 256) * fh3::kQ4KBytes;
+        case FH3CUDA_TYPE_Q5_K: return static_cast<size_t>((n + 255) / 256) * 176;
+        case FH3CUDA_TYPE_Q6_K: return static_cast<size_t>((n + 255) / 256) * 210;
+        default: return 0;
+    }
 }
+
+namespace fh3fmt {
+
+__global__ void add_bias_kernel(float* __restrict__ y, const float* __restrict__ bias, int64_t n_tok, int64_t out) {
+    const int64_t total = n_tok * out;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = __fadd_rn(y[i], bias[i % out]);
+}
+
+// fh3_matmul (src/core/fh3_ops.c:317-404) for the formats other than Q4_K (the text
+// encoder's Q5_K / Q6_K, the F16 globals, ...): rows of W are expanded bit-exactly to
+// fp32 (fh3cuda_dequant_dev) in chunks of at most 256 MB of scratch, and each chunk
+// is multiplied by a plain fp32 cuBLAS GEMM (no TF32) into its columns of y; the
+// bias is added afterwards, as the reference adds it to the finished dot product.
+int matmul_other(DevCtx* c, const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias,
+                 cudaStream_t s) {
+    const int64_t K = w->in, N = w->out;
+    int be = 1;
+    switch (w->type) {
+        case FH3CUDA_TYPE_F32: case FH3CUDA_TYPE_F16: case FH3CUDA_TYPE_BF16: be = 1; break;
+        case FH3CUDA_TYPE_Q8_0: be = 32; break;
+        case FH3CUDA_TYPE_Q2_K: case FH3CUDA_TYPE_Q3_K: case FH3CUDA_TYPE_Q5_K: case FH3CUDA_TYPE_Q6_K: be = 256; break;
+        default:
+            return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: weight type %d is not a format fh3_dequant expands",
+                             w->type);
+    }
+    if (K % be)
+        return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: in = %lld is not a multiple of the %d-weight block",
+                         static_cast<long long>(K), be);
+    if (!c->blas) {
+        if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) {
+            c->blas = nullptr;
+            return set_error(FH3CUDA_E_CUDA, "fh3cuda_matmul_dev: cublasCreate failed");
+        }
+        cublasSetMathMode(c->blas, CUBLAS_DEFAULT_MATH);
+    }
+    if (cublasSetStream(c->blas, s) != CUBLAS_STATUS_SUCCESS)
+        return set_error(FH3CUDA_E_CUDA, "fh3cuda_matmul_dev: cublasSetStream failed");
+    const size_t rb = fh3cuda_row_bytes(w->type, K);
+    int64_t chunk = N;
+    float* wf = nullptr;
+    if (w->type != FH3CUDA_TYPE_F32) {
+        const int64_t cap_rows = (int64_t(256) << 20) / (K * 4);
+        chunk = cap_rows < 1 ? 1 : (cap_rows < N ? cap_rows : N);
+        wf = static_cast<float*>(scratch(c, 8, static_cast<size_t>(chunk) * K * 4, s));
+        if (!wf) return FH3_E_NOMEM;
+    }
+    const float one = 1.0f, zero = 0.0f;
+    for (int64_t o0 = 0; o0 < N; o0 += chunk) {
+        const int64_t rows = (o0 + chunk <= N) ? chunk : N - o0;
+        const float* wrows;
+        if (w->type == FH3CUDA_TYPE_F32) {
+            wrows = reinterpret_cast<const float*>(w->data + o0 * rb);
+        } else {
+            const int rc = fh3cuda_dequant_dev(w->type, w->data + o0 * rb, wf, rows, K, s);
+            if (rc != FH3_OK) return rc;
+            wrows = wf;
+        }
+        // column-major view: y^T[N x M] (ld N) = W[rows x K]^T-view x^T[K x M]
+        const cublasStatus_t st = cublasSgemm(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(rows), n_tok,
+                                              static_cast<int>(K), &one, wrows, static_cast<int>(K), x,
+                                              static_cast<int>(K), &zero, y + o0, static_cast<int>(N));
+        if (st != CUBLAS_STATUS_SUCCESS)
+            return set_error(FH3CUDA_E_CUDA, "fh3cuda_matmul_dev: cublasSgemm failed (%d)", static_cast<int>(st));
+    }
+    if (bias) {
+        const int64_t total = static_cast<int64_t>(n_tok) * N;
+        int64_t grid = (total + 255) / 256;
+        if (grid > static_cast<int64_t>(c->sms) * 16) grid = static_cast<int64_t>(c->sms) * 16;
+        add_bias_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(y, bias, n_tok, N);
+        return check_cuda(cudaGetLastError(), "add_bias launch");
+    }
+    return FH3_OK;
+}
+
+}  // namespace fh3fmt
 
 extern "C" int fh3cuda_matmul_dev(const Fh3CudaW* w, const float* x, float* y, int n_tok,
                                   const float* bias, void* stream) {
@@ -183,9 +277,10 @@ extern "C" int fh3cuda_matmul_dev(const Fh3CudaW* w, const float* x, float* y, i
     if (!c) return set_error(FH3CUDA_E_NODEV, "fh3cuda_matmul_dev: call fh3cuda_init first");
     if (!w || !x || !y || !w->data || n_tok <= 0 || w->in <= 0 || w->out <= 0)
         return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: bad arguments");
-    if (w->type != FH3CUDA_TYPE_Q4_K || (w->in % fh3::kQ4KBlock) != 0)
-        return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: Q4_K weights with in %% 256 == 0 required (type %d)",
-                         w->type);
+    if (w->type != FH3CUDA_TYPE_Q4_K)
+        return fh3fmt::matmul_other(c, w, x, y, n_tok, bias, static_cast<cudaStream_t>(stream));
+    if ((w->in % fh3::kQ4KBlock) != 0)
+        return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: Q4_K weights need in %% 256 == 0");
     if (n_tok <= 16) return fh3cuda_gemv_q4k_dev(w, x, y, n_tok, bias, stream);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t abytes = static_cast<size_t>(n_tok) * static_cast<size_t>(w->in) * 2;
@@ -266,8 +361,8 @@ int matmul_host(const Fh3CudaW* w, const float* x, float* y, int n_tok, const fl
     // fh3_matmul returns silently on these (src/core/fh3_ops.c:318-321); report them instead
     if (!w || !x || !y || !w->data || n_tok <= 0 || w->in <= 0 || w->out <= 0)
         return set_error(FH3_E_INVALID, "fh3_matmul drop-in: bad arguments");
-    if (w->type != FH3CUDA_TYPE_Q4_K || (w->in % fh3::kQ4KBlock) != 0)
-        return set_error(FH3_E_INVALID, "fh3_matmul drop-in: only Q4_K weights with in %% 256 == 0 (type %d)",
+    if (fh3cuda_row_bytes(w->type, w->in) == 0)
+        return set_error(FH3_E_INVALID, "fh3_matmul drop-in: weight type %d is not a format fh3_dequant expands",
                          w->type);
     cudaStream_t s = c->stream;
     const size_t wbytes = static_cast<size_t>(w->out) * fh3cuda_row_bytes(w->type, w->in);

@@ -1,5 +1,6 @@
-// dequant.cu -- Q4_K -> fp32, bit-exact with fh3's dequant_q4_k
-// (src/core/fh3_quant.c:154-196).
+// dequant.cu -- fh3_dequant on the GPU: Q4_K (the trunk's format) and every other
+// format the reference expands, bit-exact with its fp32 arithmetic
+// (src/core/fh3_quant.c:36-318).
 //
 // One warp per 256-weight super-block: lane l writes weights 8l..8l+7 (sub-block
 // l/4), so a warp reads its 144-byte block once (8-byte nibble loads plus the
@@ -54,6 +55,141 @@ __global__ void __launch_bounds__(256) dequant_q4k_kernel(const uint8_t* __restr
     }
 }
 
+// ---------------------------------------------------------------------------
+// The other formats of fh3_dequant (src/core/fh3_quant.c:36-318), bit-exact with
+// its fp32 arithmetic (explicit roundings, no contraction).  A thread writes 16
+// consecutive outputs (a "group"): K-quant blocks hold 16 groups, Q8_0 blocks 2;
+// F16 / BF16 are converted 16 elements per thread.  Block sizes (34, 84, 110, 176,
+// 210 bytes) are not 16-byte multiples, so the bytes are read one by one (these
+// formats are the text encoder's and the globals', not the DiT trunk's).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float f16_at(const uint8_t* p) {
+    return fh3::h2f_bits(static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8));
+}
+
+// 16 outputs of group gi (0..15) of a Q2_K block (fh3_quant.c:73-108): group
+// (c*4 + shift)*2 + half reads bytes 16 + 32c + 16half .. +15 at bit 2*shift.
+__device__ __forceinline__ void grp_q2_k(const uint8_t* blk, int gi, float (&o)[16]) {
+    const float d = f16_at(blk + 80), dmin = f16_at(blk + 82);
+    const float dl = __fmul_rn(d, static_cast<float>(blk[gi] & 0x0F));
+    const float ml = __fmul_rn(dmin, static_cast<float>(blk[gi] >> 4));
+    const int c = gi >> 3, sh = (gi >> 1) & 3, half = gi & 1;
+    const uint8_t* q = blk + 16 + c * 32 + half * 16;
+#pragma unroll
+    for (int l = 0; l < 16; ++l) o[l] = __fsub_rn(__fmul_rn(dl, static_cast<float>((q[l] >> (2 * sh)) & 3)), ml);
+}
+
+// Q3_K (fh3_quant.c:110-152): scale (low nibble | 2 high bits << 4) - 32, quant
+// 2 low bits minus 4 when the hmask bit is clear.
+__device__ __forceinline__ void grp_q3_k(const uint8_t* blk, int g, float (&o)[16]) {
+    const uint8_t* hm = blk;
+    const uint8_t* qs = blk + 32;
+    const uint8_t* sr = blk + 96;
+    const float d = f16_at(blk + 108);
+    const int lo = g < 8 ? (sr[g] & 0x0F) : ((sr[g - 8] >> 4) & 0x0F);
+    const int hi = (sr[8 + (g & 3)] >> ((g >> 2) * 2)) & 3;
+    const float dl = __fmul_rn(d, static_cast<float>((lo | (hi << 4)) - 32));
+    const int c = g >> 3, rem = g & 7;
+    const int shl = (rem >> 1) * 2, offl = c * 32 + (rem & 1) * 16;
+    const int shh = g >> 1, offh = (g & 1) * 16;
+#pragma unroll
+    for (int l = 0; l < 16; ++l) {
+        const int q = ((qs[offl + l] >> shl) & 3) - ((((hm[offh + l] >> shh) & 1) ^ 1) << 2);
+        o[l] = __fmul_rn(dl, static_cast<float>(q));
+    }
+}
+
+// Q5_K (fh3_quant.c:198-240): Q4_K's scales, fifth bit of weight l of sub-block j
+// in bit j of qh[l]; group gi = half gi%2 of sub-block gi/2.
+__device__ __forceinline__ void grp_q5_k(const uint8_t* blk, int gi, float (&o)[16]) {
+    const float d = f16_at(blk), dmin = f16_at(blk + 2);
+    const int j = gi >> 1, l0 = (gi & 1) * 16;
+    const uint8_t* s = blk + 4;
+    int sc, m;
+    if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+    const float dl = __fmul_rn(d, static_cast<float>(sc)), ml = __fmul_rn(dmin, static_cast<float>(m));
+    const uint8_t* qh = blk + 16;
+    const uint8_t* qs = blk + 48 + (j >> 1) * 32;
+    const int shq = (j & 1) * 4;
+#pragma unroll
+    for (int l = 0; l < 16; ++l) {
+        const int q = ((qs[l0 + l] >> shq) & 0x0F) | (((qh[l0 + l] >> j) & 1) << 4);
+        o[l] = __fsub_rn(__fmul_rn(dl, static_cast<float>(q)), ml);
+    }
+}
+
+// Q6_K (fh3_quant.c:242-282): 4 low bits from ql, 2 high bits from qh, minus 32,
+// times d * int8 scale of the 16-weight group.
+__device__ __forceinline__ void grp_q6_k(const uint8_t* blk, int g, float (&o)[16]) {
+    const uint8_t* ql = blk;
+    const uint8_t* qh = blk + 128;
+    const float d = f16_at(blk + 208);
+    const float dl = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(blk[192 + g])));
+    const int c = g >> 3, rem = g & 7;
+    const int shl = (rem >> 2) * 4, offl = c * 64 + (rem & 3) * 16;
+    const int shh = (rem >> 1) * 2, offh = c * 32 + (rem & 1) * 16;
+#pragma unroll
+    for (int l = 0; l < 16; ++l) {
+        const int q = (((ql[offl + l] >> shl) & 0x0F) | (((qh[offh + l] >> shh) & 3) << 4)) - 32;
+        o[l] = __fmul_rn(dl, static_cast<float>(q));
+    }
+}
+
+// Q8_0 (fh3_quant.c:58-71): group gi (0, 1) of a 32-weight block, (float)q * d.
+__device__ __forceinline__ void grp_q8_0(const uint8_t* blk, int gi, float (&o)[16]) {
+    const float d = f16_at(blk);
+#pragma unroll
+    for (int l = 0; l < 16; ++l)
+        o[l] = __fmul_rn(static_cast<float>(static_cast<int8_t>(blk[2 + gi * 16 + l])), d);
+}
+
+// rows x (whole blocks of) n weights of format TYPE; thread per 16-output group
+template <int TYPE>
+__global__ void __launch_bounds__(256) dequant_blocks_kernel(const uint8_t* __restrict__ src, float* __restrict__ dst,
+                                                             int64_t rows, int64_t n, size_t row_bytes, int blk_elems,
+                                                             int blk_bytes) {
+    const int gpb = blk_elems / 16;                 // groups per block
+    const int64_t gpr = (n / blk_elems) * gpb;      // groups per row (whole blocks only)
+    const int64_t total = rows * gpr;
+    for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = g / gpr;
+        const int64_t gr = g - r * gpr;
+        const int64_t b = gr / gpb;
+        const int gi = static_cast<int>(gr - b * gpb);
+        const uint8_t* blk = src + r * row_bytes + b * blk_bytes;
+        float o[16];
+        if (TYPE == 8) grp_q8_0(blk, gi, o);
+        else if (TYPE == 10) grp_q2_k(blk, gi, o);
+        else if (TYPE == 11) grp_q3_k(blk, gi, o);
+        else if (TYPE == 13) grp_q5_k(blk, gi, o);
+        else grp_q6_k(blk, gi, o);
+        float* out = dst + r * n + b * blk_elems + gi * 16;
+#pragma unroll
+        for (int l = 0; l < 16; ++l) out[l] = o[l];
+    }
+}
+
+// F16 (exact) and BF16 (bits << 16) element-wise
+template <bool BF16>
+__global__ void __launch_bounds__(256) dequant_half_kernel(const uint8_t* __restrict__ src, float* __restrict__ dst,
+                                                           int64_t rows, int64_t n, size_t row_bytes) {
+    const int64_t total = rows * n;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / n, e = i - r * n;
+        const uint8_t* p = src + r * row_bytes + 2 * e;
+        const uint32_t h = static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8);
+        dst[i] = BF16 ? __uint_as_float(h << 16) : fh3::h2f_bits(h);
+    }
+}
+
 }  // namespace
 
 extern "C" int fh3cuda_dequant_dev(int type, const void* src, float* dst, int64_t rows, int64_t n,
@@ -61,10 +197,52 @@ extern "C" int fh3cuda_dequant_dev(int type, const void* src, float* dst, int64_
     using namespace fh3host;
     DevCtx* c = ctx();
     if (!c) return set_error(FH3CUDA_E_NODEV, "fh3cuda_dequant_dev: call fh3cuda_init first");
-    if (type != FH3CUDA_TYPE_Q4_K)
-        return set_error(FH3_E_INVALID, "fh3cuda_dequant_dev: unsupported type %d", type);
     if (!src || !dst || rows <= 0 || n <= 0)
         return set_error(FH3_E_INVALID, "fh3cuda_dequant_dev: bad arguments");
+    if (type != FH3CUDA_TYPE_Q4_K) {
+        const size_t rb = fh3cuda_row_bytes(type, n);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const auto* sp = static_cast<const uint8_t*>(src);
+        const int64_t cap = static_cast<int64_t>(ctx_sms(c)) * 16;
+        auto grid_for = [&](int64_t threads) {
+            const int64_t g = (threads + 255) / 256;
+            return static_cast<unsigned>(g < 1 ? 1 : (g > cap ? cap : g));
+        };
+        switch (type) {
+            case FH3CUDA_TYPE_F32:
+                return check_cuda(cudaMemcpy2DAsync(dst, static_cast<size_t>(n) * 4, src, rb, static_cast<size_t>(n) * 4,
+                                                    static_cast<size_t>(rows), cudaMemcpyDeviceToDevice, s),
+                                  "fh3cuda_dequant_dev: F32 copy");
+            case FH3CUDA_TYPE_F16:
+                dequant_half_kernel<false><<<grid_for(rows * n), 256, 0, s>>>(sp, dst, rows, n, rb);
+                return check_cuda(cudaGetLastError(), "dequant_half_kernel launch");
+            case FH3CUDA_TYPE_BF16:
+                dequant_half_kernel<true><<<grid_for(rows * n), 256, 0, s>>>(sp, dst, rows, n, rb);
+                return check_cuda(cudaGetLastError(), "dequant_half_kernel launch");
+            default: break;
+        }
+        int be = 256, bb = 0;
+        switch (type) {
+            case FH3CUDA_TYPE_Q8_0: be = 32; bb = 34; break;
+            case FH3CUDA_TYPE_Q2_K: bb = 84; break;
+            case FH3CUDA_TYPE_Q3_K: bb = 110; break;
+            case FH3CUDA_TYPE_Q5_K: bb = 176; break;
+            case FH3CUDA_TYPE_Q6_K: bb = 210; break;
+            default: return set_error(FH3_E_INVALID, "fh3cuda_dequant_dev: unsupported type %d", type);
+        }
+        if (n / be == 0) return FH3_OK;  // no whole block: nothing written, as in the reference
+        const unsigned grid = grid_for(rows * (n / be) * (be / 16));
+#define FH3_DQ(T) dequant_blocks_kernel<T><<<grid, 256, 0, s>>>(sp, dst, rows, n, rb, be, bb)
+        switch (type) {
+            case FH3CUDA_TYPE_Q8_0: FH3_DQ(8); break;
+            case FH3CUDA_TYPE_Q2_K: FH3_DQ(10); break;
+            case FH3CUDA_TYPE_Q3_K: FH3_DQ(11); break;
+            case FH3CUDA_TYPE_Q5_K: FH3_DQ(13); break;
+            default: FH3_DQ(14); break;
+        }
+#undef FH3_DQ
+        return check_cuda(cudaGetLastError(), "dequant_blocks_kernel launch");
+    }
     if ((reinterpret_cast<uintptr_t>(src) & 15) != 0)
         return set_error(FH3_E_INVALID, "fh3cuda_dequant_dev: src must be 16-byte aligned");
     const int64_t bpr = n / fh3::kQ4KBlock;

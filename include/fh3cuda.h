@@ -16,8 +16,9 @@
  *     (include/fh3/fh3.h:218-226) and add three of their own.
  *   - "_dev" entry points take device pointers and a cudaStream_t passed as
  *     void* (NULL = the legacy default stream); they are asynchronous.
- *   - Weights are fh3 rows: row o of a Q4_K matrix with `in` columns starts at
- *     data + o * fh3cuda_row_bytes(12, in); `in` must be a multiple of 256.
+ *   - Weights are fh3 rows: row o of a matrix of type t with `in` columns
+ *     starts at data + o * fh3cuda_row_bytes(t, in); for block formats `in`
+ *     must be a multiple of the block (256 for the K-quants, 32 for Q8_0).
  *   - Device-side waits inside the kernels are bounded; a wait that gives up
  *     records FH3CUDA_E_TIMEOUT in the device status word, read by
  *     fh3cuda_device_status().
@@ -48,8 +49,15 @@ extern "C" {
 #define FH3CUDA_E_NODEV   (-22)  /* no usable sm_100 device / not initialised */
 
 /* Weight types this path accepts (GGML ids, include/fh3/fh3.h:63-79). */
-#define FH3CUDA_TYPE_F32  0
+#define FH3CUDA_TYPE_F32  0   /* fh3's enum values, include/fh3/fh3.h:64-78 */
+#define FH3CUDA_TYPE_F16  1
+#define FH3CUDA_TYPE_Q8_0 8
+#define FH3CUDA_TYPE_Q2_K 10
+#define FH3CUDA_TYPE_Q3_K 11
 #define FH3CUDA_TYPE_Q4_K 12
+#define FH3CUDA_TYPE_Q5_K 13
+#define FH3CUDA_TYPE_Q6_K 14
+#define FH3CUDA_TYPE_BF16 30
 
 /* Same layout as the reference's weight descriptor Fh3W
  * (include/fh3/fh3.h:82-87), so a pointer to one may be passed as the other. */
@@ -87,13 +95,15 @@ FH3CUDA_API int fh3cuda_sm_count(void);
 /* ---- format ------------------------------------------------------------ */
 
 /* Bytes of one weight row: replaces fh3_row_bytes (include/fh3/fh3.h:103,
- * src/core/fh3_quant.c:14-34) for F32 and Q4_K; 0 for other types. */
+ * src/core/fh3_quant.c:14-34) for the formats fh3_dequant expands (F32, F16,
+ * BF16, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K); 0 for other types. */
 FH3CUDA_API size_t fh3cuda_row_bytes(int type, int64_t n);
 
-/* Dequantise `rows` Q4_K rows of `n` weights to fp32, bit-exact with
- * fh3_dequant (include/fh3/fh3.h:104, src/core/fh3_quant.c:154-196,284-318):
- * dst[r*n + k].  Like the reference, only whole 256-weight blocks are
- * written; a partial trailing block of a row is left untouched. */
+/* Dequantise `rows` rows of `n` weights of any format above to fp32,
+ * bit-exact with fh3_dequant (include/fh3/fh3.h:104, src/core/fh3_quant.c:36-318):
+ * dst[r*n + k].  Like the reference, only whole blocks are written; a partial
+ * trailing block of a row is left untouched.  Q4_K sources must be 16-byte
+ * aligned. */
 FH3CUDA_API int fh3cuda_dequant_dev(int type, const void *src, float *dst, int64_t rows, int64_t n,
                         void *stream);
 
@@ -101,10 +111,12 @@ FH3CUDA_API int fh3cuda_dequant_dev(int type, const void *src, float *dst, int64
 
 /* y[t][o] = sum_k x[t][k] * W[o][k] (+ bias[o]), all pointers on the device.
  * Replaces fh3_matmul (include/fh3/fh3.h:107, src/core/fh3_ops.c:317-404) on
- * device buffers.  n_tok <= 16 runs the fp32 CUDA-core GEMV (relative
+ * device buffers.  Q4_K (the DiT trunk): n_tok <= 16 runs the GEMV (relative
  * Frobenius error <= 1e-5 against fh3_matmul); larger n_tok runs the tcgen05
- * GEMM on bf16 operands with fp32 accumulation (<= 5e-3).  Internal scratch
- * (bf16 activations) is cached per device and grows on demand. */
+ * GEMM on bf16 operands with fp32 accumulation (<= 5e-3).  Every other format
+ * fh3_dequant expands (the text encoder's Q5_K / Q6_K, F16 / F32 globals, ...):
+ * rows expanded bit-exactly to fp32, then an fp32 cuBLAS GEMM (<= 1e-5).
+ * Internal scratch is cached per device and grows on demand. */
 FH3CUDA_API int fh3cuda_matmul_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
                        const float *bias_or_null, void *stream);
 
@@ -151,7 +163,8 @@ FH3CUDA_API int fh3cuda_release_weights(const void *host);
 
 /* ---- explicit kernels (tests, benchmarks, fused trunk) ----------------- */
 
-/* fp32 CUDA-core GEMV, 1 <= n_tok <= 16; same contract as fh3cuda_matmul_dev. */
+/* Q4_K GEMV, 1 <= n_tok <= 16; same contract as fh3cuda_matmul_dev (tensor-core
+ * kernels; the fp32 CUDA-core kernel with FH3CUDA_GEMV_KERNEL=fp32). */
 FH3CUDA_API int fh3cuda_gemv_q4k_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
                          const float *bias_or_null, void *stream);
 

@@ -48,7 +48,11 @@ def test_row_bytes_matches_reference_rule(lib, oracle):
         assert lib.fh3cuda_row_bytes(12, n) == oracle.row_bytes(12, n) == ((n + 255) // 256) * 144
         assert lib.fh3cuda_row_bytes(0, n) == 4 * n
     assert lib.fh3cuda_row_bytes(12, 0) == 0
-    assert lib.fh3cuda_row_bytes(13, 256) == 0  # Q5_K is not on this path
+    for t in (1, 30, 8, 10, 11, 13, 14):      # every other format fh3_dequant expands
+        for n in (32, 256, 1000, 5376):
+            assert lib.fh3cuda_row_bytes(t, n) == oracle.row_bytes(t, n) > 0
+    for t in (2, 3, 6, 7, 9, 15, 99):         # row sizes without an expander in fh3_dequant
+        assert lib.fh3cuda_row_bytes(t, 256) == 0
 
 
 def test_fh3w_layout_matches_reference_struct():

@@ -69,7 +69,7 @@ def test_rejects_bad_arguments(fh3):
     buf = torch.zeros(1024, dtype=torch.uint8, device="cuda")
     out = torch.zeros(256, dtype=torch.float32, device="cuda")
     with pytest.raises(fh3.Fh3CudaError) as e:
-        fh3.dequant(13, buf, 256, 1, out=out)   # Q5_K is not on this path
+        fh3.dequant(2, buf, 256, 1, out=out)    # Q4_0: fh3_dequant has no expander for it
     assert e.value.code == -8
     with pytest.raises(fh3.Fh3CudaError):
         fh3.dequant(Q4K, buf[1:], 256, 1, out=out)  # misaligned source

@@ -64,7 +64,7 @@ def test_bad_arguments_are_recorded_not_silent(fh3):
     d = _lib.Fh3CudaW(Q4K, 256, 4, w.ctypes.data)
     L.fh3cuda_matmul(ctypes.byref(d), x.ctypes.data, y.ctypes.data, 0, None)  # n_tok = 0
     assert L.fh3cuda_take_status() == -8
-    d2 = _lib.Fh3CudaW(14, 256, 4, w.ctypes.data)  # Q6_K: not on this path
+    d2 = _lib.Fh3CudaW(2, 256, 4, w.ctypes.data)   # Q4_0: fh3_dequant has no expander for it
     L.fh3cuda_matmul(ctypes.byref(d2), x.ctypes.data, y.ctypes.data, 1, None)
     assert L.fh3cuda_take_status() == -8
     assert np.all(y == 5.0)
