@@ -630,6 +630,242 @@ int oracle_make_q4k_weights(uint64_t seed, uint64_t stream, float scale,
     return 0;
 }
 
+/* ---- video sparse attention (fh3_vsa_attention, src/core/fh3_vsa.c:186-507) ----
+ *
+ * Tile geometry (build_vsa_geometry, src/core/fh3_vsa.c:32-161), restated in
+ * closed form: text tokens [0, T) and audio tokens [T, T+A) are cut into runs of
+ * `tile` tokens ("prefix" tiles); video tokens [T+A, N) on the grid (gt, gh, gw)
+ * are cut into 4x4x4 cells, visited t-major then h then w, the tokens of a cell in
+ * row-major (t, h, w) order.  A sequence whose modality counts do not add up to N
+ * is all video; a grid whose product is not V is (1, 1, V). */
+typedef struct {
+    int n, T, A, V, tile, nT, nA, npre, gt, gh, gw, ct, ch, cw, nvid, ntiles;
+} VsaGeo;
+
+static int vsa_geo(VsaGeo *g, int n, int T, int A, int V, int gt, int gh, int gw, int tile) {
+    memset(g, 0, sizeof(*g));
+    if (n <= 0) return -1;
+    if (tile <= 0) tile = 64;
+    if (T < 0) T = 0;
+    if (A < 0) A = 0;
+    if (V < 0) V = 0;
+    if (T + A + V != n) { T = 0; A = 0; V = n; }
+    if (gt <= 0 || gh <= 0 || gw <= 0 || (int64_t)gt * gh * gw != V) { gt = 1; gh = 1; gw = V; }
+    g->n = n; g->T = T; g->A = A; g->V = V; g->tile = tile;
+    g->nT = (T + tile - 1) / tile;
+    g->nA = (A + tile - 1) / tile;
+    g->npre = g->nT + g->nA;
+    g->gt = gt; g->gh = gh; g->gw = gw;
+    g->ct = (gt + 3) / 4; g->ch = (gh + 3) / 4; g->cw = (gw + 3) / 4;
+    g->nvid = V > 0 ? g->ct * g->ch * g->cw : 0;
+    g->ntiles = g->npre + g->nvid;
+    return g->ntiles > 0 ? 0 : -1;
+}
+
+/* tokens of tile i: count, offset in tile order, and token of its r-th member */
+static int vsa_tile_count(const VsaGeo *g, int i) {
+    if (i < g->nT) return (i + 1) * g->tile <= g->T ? g->tile : g->T - i * g->tile;
+    if (i < g->npre) { int a = i - g->nT; return (a + 1) * g->tile <= g->A ? g->tile : g->A - a * g->tile; }
+    int v = i - g->npre, tt = v / (g->ch * g->cw), hh = (v / g->cw) % g->ch, ww = v % g->cw;
+    int et = g->gt - 4 * tt < 4 ? g->gt - 4 * tt : 4;
+    int eh = g->gh - 4 * hh < 4 ? g->gh - 4 * hh : 4;
+    int ew = g->gw - 4 * ww < 4 ? g->gw - 4 * ww : 4;
+    return et * eh * ew;
+}
+
+static int vsa_tile_token(const VsaGeo *g, int i, int r) {
+    if (i < g->nT) return i * g->tile + r;
+    if (i < g->npre) return g->T + (i - g->nT) * g->tile + r;
+    int v = i - g->npre, tt = v / (g->ch * g->cw), hh = (v / g->cw) % g->ch, ww = v % g->cw;
+    int eh = g->gh - 4 * hh < 4 ? g->gh - 4 * hh : 4;
+    int ew = g->gw - 4 * ww < 4 ? g->gw - 4 * ww : 4;
+    int dt = r / (eh * ew), dh = (r / ew) % eh, dw = r % ew;
+    return g->T + g->A + ((4 * tt + dt) * g->gh + 4 * hh + dh) * g->gw + 4 * ww + dw;
+}
+
+/* number of tiles (and the prefix / video split) of a sequence */
+int oracle_vsa_tiles(int n, int T, int A, int V, int gt, int gh, int gw, int tile, int *out3) {
+    VsaGeo g;
+    if (vsa_geo(&g, n, T, A, V, gt, gh, gw, tile)) return -1;
+    out3[0] = g.ntiles;
+    out3[1] = g.npre;
+    out3[2] = g.nvid;
+    return 0;
+}
+
+/* compute_topk (src/core/fh3_vsa.c:163-169), float arithmetic as there */
+static int vsa_topk(float sparsity, int nblocks) {
+    if (nblocks <= 0) return 0;
+    int k = (int)ceilf((1.0f - sparsity) * (float)nblocks);
+    return k < 1 ? 1 : (k > nblocks ? nblocks : k);
+}
+
+/* Restates fh3_vsa_attention (src/core/fh3_vsa.c:186-507).  q/k/v/gate/o are
+ * [n][heads][hd] fp32; gate may be NULL (no coarse branch).  Operation order
+ * follows the reference where it fixes the rounding: tile means accumulate
+ * q * (1/count) over the tile's tokens in tile order (:230-256); a tile score is
+ * a sequential dot product times 1/sqrt(hd) (:268-281); a video query tile keeps
+ * the prefix key tiles and the top-k video key tiles by (score desc, index asc)
+ * (:295-356), all key tiles when sparsity <= 0 or k covers them all; prefix query
+ * tiles keep all key tiles.  Fine attention: max, expf, sequential sum, and
+ * o += (p * (1/sum)) * v over the kept keys in tile order (:372-432).  Coarse:
+ * the same softmax over every tile score of the row, against the tile means of v
+ * (:442-473); o = fine + coarse * gate (:476-487).
+ * Optional outputs: scores [heads][ntiles][ntiles] and mask (same shape, 0/1).
+ * Returns 0, or -8 where the reference returns silently. */
+int oracle_vsa(int tile, float sparsity, const float *q, const float *k, const float *v, const float *gate,
+               float *o, int n, int T, int A, int V, int gt, int gh, int gw, int heads, int hd,
+               float *scores_out, uint8_t *mask_out) {
+    if (!q || !k || !v || !o || n <= 0 || heads <= 0 || hd <= 0) return -8;
+    VsaGeo g;
+    if (vsa_geo(&g, n, T, A, V, gt, gh, gw, tile)) return -8;
+    const int nt = g.ntiles;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const size_t pool_sz = (size_t)heads * nt * hd;
+    float *qp = (float *)calloc(pool_sz, sizeof(float));
+    float *kp = (float *)calloc(pool_sz, sizeof(float));
+    float *vp = gate ? (float *)calloc(pool_sz, sizeof(float)) : NULL;
+    float *S = (float *)malloc((size_t)heads * nt * nt * sizeof(float));
+    uint8_t *M = (uint8_t *)calloc((size_t)heads * nt * nt, 1);
+    int *off = (int *)malloc((size_t)(nt + 1) * sizeof(int));
+    int *tok = (int *)malloc((size_t)n * sizeof(int));
+    float *fine = (float *)calloc((size_t)n * heads * hd, sizeof(float));
+    if (!qp || !kp || (gate && !vp) || !S || !M || !off || !tok || !fine) {
+        free(qp); free(kp); free(vp); free(S); free(M); free(off); free(tok); free(fine);
+        return -8;
+    }
+    off[0] = 0;
+    for (int i = 0; i < nt; i++) {
+        int c = vsa_tile_count(&g, i);
+        for (int r = 0; r < c; r++) tok[off[i] + r] = vsa_tile_token(&g, i, r);
+        off[i + 1] = off[i] + c;
+    }
+    /* tile means */
+    for (int i = 0; i < nt; i++) {
+        const int c = off[i + 1] - off[i];
+        const float inv = 1.0f / (float)c;
+        for (int r = 0; r < c; r++) {
+            const int t = tok[off[i] + r];
+            for (int h = 0; h < heads; h++) {
+                const size_t src = ((size_t)t * heads + h) * hd, dst = ((size_t)h * nt + i) * hd;
+                for (int d = 0; d < hd; d++) {
+                    qp[dst + d] += q[src + d] * inv;
+                    kp[dst + d] += k[src + d] * inv;
+                    if (vp) vp[dst + d] += v[src + d] * inv;
+                }
+            }
+        }
+    }
+    /* tile scores */
+    int hi;
+#pragma omp parallel for schedule(static)
+    for (hi = 0; hi < heads * nt; hi++) {
+        const int h = hi / nt, i = hi % nt;
+        const float *a = qp + ((size_t)h * nt + i) * hd;
+        for (int j = 0; j < nt; j++) {
+            const float *b = kp + ((size_t)h * nt + j) * hd;
+            float dot = 0.0f;
+            for (int d = 0; d < hd; d++) dot += a[d] * b[d];
+            S[((size_t)h * nt + i) * nt + j] = dot * scale;
+        }
+    }
+    /* tile mask: a video key tile j is kept for row (h, i) when fewer than k video
+     * key tiles precede it in (score desc, index asc) order */
+    const int kv = vsa_topk(sparsity, g.nvid);
+    const int dense = sparsity <= 0.0f || kv == g.nvid;
+#pragma omp parallel for schedule(static)
+    for (hi = 0; hi < heads * nt; hi++) {
+        const int i = hi % nt;
+        const float *s = S + (size_t)hi * nt;
+        uint8_t *m = M + (size_t)hi * nt;
+        if (i < g.npre || dense) {
+            memset(m, 1, (size_t)nt);
+            continue;
+        }
+        memset(m, 1, (size_t)g.npre);
+        for (int j = g.npre; j < nt; j++) {
+            int before = 0;
+            for (int j2 = g.npre; j2 < nt && before < kv; j2++)
+                if (s[j2] > s[j] || (s[j2] == s[j] && j2 < j)) before++;
+            m[j] = before < kv;
+        }
+    }
+    /* fine attention per (head, query tile) */
+#pragma omp parallel for schedule(dynamic)
+    for (hi = 0; hi < heads * nt; hi++) {
+        const int h = hi / nt, i = hi % nt;
+        const uint8_t *m = M + (size_t)hi * nt;
+        int nk = 0;
+        for (int j = 0; j < nt; j++)
+            if (m[j]) nk += off[j + 1] - off[j];
+        int *keys = (int *)malloc((size_t)nk * sizeof(int));
+        float *p = (float *)malloc((size_t)nk * sizeof(float));
+        if (!keys || !p) { free(keys); free(p); continue; }
+        nk = 0;
+        for (int j = 0; j < nt; j++)
+            if (m[j])
+                for (int r = off[j]; r < off[j + 1]; r++) keys[nk++] = tok[r];
+        for (int r = off[i]; r < off[i + 1]; r++) {
+            const float *qi = q + ((size_t)tok[r] * heads + h) * hd;
+            float mx = -1e30f;
+            for (int e = 0; e < nk; e++) {
+                const float *kj = k + ((size_t)keys[e] * heads + h) * hd;
+                float dot = 0.0f;
+                for (int d = 0; d < hd; d++) dot += qi[d] * kj[d];
+                p[e] = dot * scale;
+                if (p[e] > mx) mx = p[e];
+            }
+            float sum = 0.0f;
+            for (int e = 0; e < nk; e++) {
+                p[e] = expf(p[e] - mx);
+                sum += p[e];
+            }
+            const float inv = 1.0f / sum;
+            float *oi = fine + ((size_t)tok[r] * heads + h) * hd;
+            for (int e = 0; e < nk; e++) {
+                const float *vj = v + ((size_t)keys[e] * heads + h) * hd;
+                const float w = p[e] * inv;
+                for (int d = 0; d < hd; d++) oi[d] += w * vj[d];
+            }
+        }
+        free(keys);
+        free(p);
+    }
+    /* coarse branch and combination */
+    if (gate) {
+        float *w = (float *)malloc((size_t)nt * sizeof(float));
+        float *c = (float *)malloc((size_t)hd * sizeof(float));
+        for (int i = 0; i < nt && w && c; i++) {
+            for (int h = 0; h < heads; h++) {
+                const float *s = S + ((size_t)h * nt + i) * nt;
+                float mx = -1e30f, sum = 0.0f;
+                for (int j = 0; j < nt; j++) if (s[j] > mx) mx = s[j];
+                for (int j = 0; j < nt; j++) sum += expf(s[j] - mx);
+                const float inv = 1.0f / sum;
+                for (int d = 0; d < hd; d++) c[d] = 0.0f;
+                for (int j = 0; j < nt; j++) {
+                    const float wj = expf(s[j] - mx) * inv;
+                    const float *vj = vp + ((size_t)h * nt + j) * hd;
+                    for (int d = 0; d < hd; d++) c[d] += wj * vj[d];
+                }
+                for (int r = off[i]; r < off[i + 1]; r++) {
+                    const size_t e = ((size_t)tok[r] * heads + h) * hd;
+                    for (int d = 0; d < hd; d++) o[e + d] = fine[e + d] + c[d] * gate[e + d];
+                }
+            }
+        }
+        if (!w || !c) memcpy(o, fine, (size_t)n * heads * hd * sizeof(float));
+        free(w);
+        free(c);
+    } else {
+        memcpy(o, fine, (size_t)n * heads * hd * sizeof(float));
+    }
+    if (scores_out) memcpy(scores_out, S, (size_t)heads * nt * nt * sizeof(float));
+    if (mask_out) memcpy(mask_out, M, (size_t)heads * nt * nt);
+    free(qp); free(kp); free(vp); free(S); free(M); free(off); free(tok); free(fine);
+    return 0;
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

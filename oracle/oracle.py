@@ -8,7 +8,7 @@ Two libraries sit behind it:
   * ``liboracle.so``       -- this project's C restatement (oracle/fh3_oracle.c),
                               built by ``make -C oracle``; always available.
   * ``_ref/libfh3ref.so``  -- the reference's own fh3_quant.c / fh3_ops.c /
-                              fh3_sched.c compiled from its sources by the same
+                              fh3_vsa.c / fh3_sched.c compiled from its sources by the same
                               Makefile, where the reference tree exists.
 """
 from __future__ import annotations
@@ -53,6 +53,19 @@ class _Fh3W(ctypes.Structure):
                 ("out", ctypes.c_int64), ("data", _c_u8p)]
 
 
+class _Fh3Seq(ctypes.Structure):
+    """Mirror of the reference's struct Fh3Seq (src/model/fh3_seq.h:31-45)."""
+    _fields_ = [("seq_len", ctypes.c_int), ("num_text", ctypes.c_int), ("num_audio", ctypes.c_int),
+                ("num_video", ctypes.c_int), ("grid_t", ctypes.c_int), ("grid_h", ctypes.c_int),
+                ("grid_w", ctypes.c_int), ("tags", ctypes.c_void_p), ("pair_index", ctypes.c_void_p),
+                ("pos", ctypes.c_void_p), ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p)]
+
+
+class _Fh3VsaCfg(ctypes.Structure):
+    """Mirror of the reference's Fh3VsaCfg (include/fh3/fh3.h:41-44)."""
+    _fields_ = [("tile", ctypes.c_int), ("sparsity", ctypes.c_float)]
+
+
 class Oracle:
     """This project's C restatement of the reference path."""
 
@@ -83,6 +96,11 @@ class Oracle:
         lib.oracle_make_q4k_weights.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                                 ctypes.c_int64, ctypes.c_int64, _c_u8p]
         lib.oracle_num_threads.restype = ctypes.c_int
+        lib.oracle_vsa_tiles.restype = ctypes.c_int
+        lib.oracle_vsa_tiles.argtypes = [ctypes.c_int] * 8 + [ctypes.POINTER(ctypes.c_int)]
+        lib.oracle_vsa.restype = ctypes.c_int
+        lib.oracle_vsa.argtypes = ([ctypes.c_int, ctypes.c_float] + [_c_f32p] * 5 + [ctypes.c_int] * 9 +
+                                   [_c_f32p, _c_u8p])
         self.lib = lib
 
     def row_bytes(self, type_: int, n: int) -> int:
@@ -154,6 +172,30 @@ class Oracle:
         self.lib.oracle_attention(_ptr(q, _c_f32p), _ptr(k, _c_f32p), _ptr(v, _c_f32p), _ptr(o, _c_f32p),
                                   q.shape[0], heads, hd)
         return o
+
+    def vsa_tiles(self, seq: tuple, tile: int = 64) -> tuple[int, int, int]:
+        """(num_tiles, num_prefix_tiles, num_video_tiles) of seq = (n, T, A, V, gt, gh, gw)."""
+        out = (ctypes.c_int * 3)()
+        if self.lib.oracle_vsa_tiles(*seq, tile, out):
+            raise ValueError("empty sequence")
+        return out[0], out[1], out[2]
+
+    def vsa(self, q: np.ndarray, k: np.ndarray, v: np.ndarray, gate: np.ndarray | None, seq: tuple, heads: int,
+            hd: int, tile: int = 64, sparsity: float = 0.8, want_tiles: bool = False):
+        """fh3_vsa_attention semantics; q/k/v/gate [n][heads*hd] fp32, seq = (n, T, A, V, gt, gh, gw).
+        With want_tiles also returns the tile scores and the 0/1 tile mask, [heads][nt][nt]."""
+        q, k, v = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v))
+        g = None if gate is None else np.ascontiguousarray(gate, dtype=np.float32)
+        o = np.zeros_like(q)
+        nt = self.vsa_tiles(seq, tile)[0]
+        sc = np.zeros((heads, nt, nt), np.float32) if want_tiles else None
+        mk = np.zeros((heads, nt, nt), np.uint8) if want_tiles else None
+        rc = self.lib.oracle_vsa(tile, sparsity, _ptr(q, _c_f32p), _ptr(k, _c_f32p), _ptr(v, _c_f32p),
+                                 _ptr(g, _c_f32p), _ptr(o, _c_f32p), *seq, heads, hd, _ptr(sc, _c_f32p),
+                                 _ptr(mk, _c_u8p))
+        if rc:
+            raise ValueError(f"oracle_vsa failed ({rc})")
+        return (o, sc, mk) if want_tiles else o
 
     def qk_norm_rope(self, x: np.ndarray, w: np.ndarray, cos: np.ndarray, sin: np.ndarray, heads: int,
                      head_dim: int, rot_dim: int, eps: float) -> np.ndarray:
@@ -231,6 +273,8 @@ class Reference:
                                       ctypes.c_int]
         lib.fh3_gate_residual.argtypes = [_c_f32p, _c_f32p, _c_f32p, ctypes.c_int, ctypes.c_int]
         lib.fh3_rng_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _c_f32p, ctypes.c_size_t]
+        lib.fh3_vsa_attention.argtypes = [ctypes.POINTER(_Fh3VsaCfg)] + [_c_f32p] * 5 + [
+            ctypes.POINTER(_Fh3Seq), ctypes.c_int, ctypes.c_int]
         self.lib = lib
 
     @staticmethod
@@ -281,6 +325,17 @@ class Reference:
         o = np.empty_like(q)
         self.lib.fh3_attention(_ptr(q, _c_f32p), _ptr(k, _c_f32p), _ptr(v, _c_f32p), _ptr(o, _c_f32p),
                                q.shape[0], heads, hd)
+        return o
+
+    def vsa(self, q, k, v, gate, seq: tuple, heads: int, hd: int, tile: int = 64, sparsity: float = 0.8):
+        """fh3_vsa_attention itself; seq = (n, T, A, V, gt, gh, gw)."""
+        q, k, v = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v))
+        g = None if gate is None else np.ascontiguousarray(gate, dtype=np.float32)
+        o = np.zeros_like(q)
+        sq = _Fh3Seq(*seq)
+        cfg = _Fh3VsaCfg(tile, sparsity)
+        self.lib.fh3_vsa_attention(ctypes.byref(cfg), _ptr(q, _c_f32p), _ptr(k, _c_f32p), _ptr(v, _c_f32p),
+                                   _ptr(g, _c_f32p), _ptr(o, _c_f32p), ctypes.byref(sq), heads, hd)
         return o
 
     def rope3(self, x, cos, sin, heads: int, head_dim: int, rot_dim: int):

@@ -122,3 +122,51 @@ def rel_fro(a, b) -> float:
     b = np.asarray(b, dtype=np.float64)
     den = np.linalg.norm(b)
     return float(np.linalg.norm(a - b) / (den if den > 0 else 1.0))
+
+
+VSA_FIXTURES = ("vsa_n784", "vsa_padded", "vsa_sparsity0")
+
+
+def read_vsa_golden(name: str):
+    """tests/fixtures/vsa/<name>.bin of the reference (tests/unit/test_vsa.c:56-133):
+    <9I> n, T, A, V, grid_t, grid_h, grid_w, heads, head_dim; <f> sparsity; <I> has_gate;
+    then q, k, v, [gate], ref, each [n][heads*head_dim] fp32.
+    Returns (seq = (n, T, A, V, gt, gh, gw), heads, head_dim, sparsity, q, k, v, gate|None, ref)."""
+    with open(os.path.join(GOLDEN, "vsa", name + ".bin"), "rb") as f:
+        b = f.read()
+    hdr = struct.unpack("<9I", b[:36])
+    (sp,) = struct.unpack("<f", b[36:40])
+    (has_gate,) = struct.unpack("<I", b[40:44])
+    n, heads, hd = hdr[0], hdr[7], hdr[8]
+    e = n * heads * hd
+    arrs, off = [], 44
+    for _ in range(5 if has_gate else 4):
+        arrs.append(np.frombuffer(b, np.float32, e, off).reshape(n, heads * hd).copy())
+        off += 4 * e
+    assert off == len(b)
+    q, k, v = arrs[:3]
+    gate = arrs[3] if has_gate else None
+    return tuple(hdr[:7]), heads, hd, sp, q, k, v, gate, arrs[-1]
+
+
+def vsa_case(golden_cases, name: str):
+    """A reference-computed fh3_vsa_attention case from ref_cases.npz (tests/golden/make_golden.py)."""
+    p = f"vsa_{name}/"
+    seq = tuple(int(x) for x in golden_cases[p + "seq"])
+    heads, hd, tile = (int(x) for x in golden_cases[p + "cfg"])
+    sp = float(golden_cases[p + "sparsity"][0])
+    gate = golden_cases.get(p + "gate")
+    return (seq, heads, hd, tile, sp, golden_cases[p + "q"], golden_cases[p + "k"], golden_cases[p + "v"], gate,
+            golden_cases[p + "y"])
+
+
+VSA_CASES = ("hd128_tied", "nogate_tile32", "tile100", "mismatch_allvideo", "badgrid")
+
+
+def rel_l2(a, b) -> float:
+    """Relative L2 (Frobenius) error as tests/unit/test_vsa.c:43-53 computes it (fp64 sums)."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    den = np.sqrt(np.sum(b * b))
+    num = np.sqrt(np.sum((a - b) ** 2))
+    return float(num / den) if den > 0 else float(num)

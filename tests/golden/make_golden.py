@@ -10,6 +10,9 @@
    Also the op fixtures tests/fixtures/ops/{rmsnorm,rope3}.bin -> {rmsnorm,rope3}.bin,
    read by the reference's tests/unit/test_ops.c:58-96 (<u32 n, u32 dim, f32 eps>, x, w, ref)
    and :98-140 (<u32 n, heads, head_dim, rot_dim>, x, cos, sin, ref).
+   And the video-sparse-attention fixtures tests/fixtures/vsa/{vsa_n784,vsa_padded,vsa_sparsity0}.bin
+   -> vsa/*.bin (<u32 n, T, A, V, grid_t, grid_h, grid_w, heads, head_dim; f32 sparsity; u32 has_gate>,
+   then q, k, v, [gate], ref as [n][heads][head_dim] fp32), read by tests/unit/test_vsa.c:56-133.
 2. Writes ref_cases.npz: seeded inputs (this project's Q4_K quantiser + fh3_rng_normal)
    with outputs computed by the REFERENCE'S OWN fh3_matmul / fh3_dequant / fh3_swiglu,
    compiled from its sources into oracle/_ref/libfh3ref.so (oracle/Makefile).  These pin
@@ -55,6 +58,9 @@ def main() -> None:
         shutil.copyfile(os.path.join(fx, name), os.path.join(HERE, name))
     for name in ("rmsnorm.bin", "rope3.bin"):
         shutil.copyfile(os.path.join(args.ref, "tests", "fixtures", "ops", name), os.path.join(HERE, name))
+    os.makedirs(os.path.join(HERE, "vsa"), exist_ok=True)
+    for name in ("vsa_n784.bin", "vsa_padded.bin", "vsa_sparsity0.bin"):
+        shutil.copyfile(os.path.join(args.ref, "tests", "fixtures", "vsa", name), os.path.join(HERE, "vsa", name))
     build()
     o = Oracle()
     r = Reference()
@@ -108,6 +114,30 @@ def main() -> None:
         out[f"fmt_{nm}/bias"] = bias
         out[f"fmt_{nm}/dims"] = np.array([t, cols, rows, 5], dtype=np.int64)
         out[f"fmt_{nm}/y"] = r.matmul(t, w, cols, rows, x, bias)
+    # fh3_vsa_attention by the reference on cases its fixtures do not cover:
+    # (name, seq = (n, T, A, V, gt, gh, gw), heads, head_dim, tile, sparsity, gate?, tied video key tiles?)
+    vsa_cases = [
+        ("hd128_tied", (8 + 4 * 4 * 16, 8, 0, 256, 4, 4, 16), 1, 128, 64, 0.6, True, True),
+        ("nogate_tile32", (40 + 30 + 4 * 5 * 6, 40, 30, 120, 4, 5, 6), 2, 64, 32, 0.7, False, False),
+        ("tile100", (130 + 128, 130, 0, 128, 4, 4, 8), 1, 64, 100, 0.9, True, False),
+        ("mismatch_allvideo", (200, 50, 50, 50, 2, 5, 5), 1, 64, 64, 0.5, True, False),
+        ("badgrid", (20 + 150, 20, 0, 150, 3, 7, 7), 1, 64, 64, 0.6, True, False),
+    ]
+    for ci, (nm, seq, H, D, tile, sp, has_gate, tied) in enumerate(vsa_cases):
+        n = seq[0]
+        qv = o.rng_normal(120 + ci, 1, n * H * D).reshape(n, H * D)
+        kv = o.rng_normal(120 + ci, 2, n * H * D).reshape(n, H * D)
+        vv = o.rng_normal(120 + ci, 3, n * H * D).reshape(n, H * D)
+        gv = o.rng_normal(120 + ci, 4, n * H * D).reshape(n, H * D) if has_gate else None
+        if tied:  # every video token's k equal to the first video token's: all video tile scores tie
+            kv[seq[1] + seq[2]:] = kv[seq[1] + seq[2]]
+        out[f"vsa_{nm}/q"], out[f"vsa_{nm}/k"], out[f"vsa_{nm}/v"] = qv, kv, vv
+        if gv is not None:
+            out[f"vsa_{nm}/gate"] = gv
+        out[f"vsa_{nm}/seq"] = np.array(seq, dtype=np.int64)
+        out[f"vsa_{nm}/cfg"] = np.array([H, D, tile], dtype=np.int64)
+        out[f"vsa_{nm}/sparsity"] = np.array([sp], dtype=np.float32)
+        out[f"vsa_{nm}/y"] = r.vsa(qv, kv, vv, gv, seq, H, D, tile, sp)
     # fh3_rng_normal itself
     out["rng/seed7_stream3"] = r.rng_normal(7, 3, 1001)
     np.savez_compressed(os.path.join(HERE, "ref_cases.npz"), **out)
