@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true",
                     help="skip the GEMV (1..4 token), q/k norm+rope and attention measurements")
-    ap.add_argument("--case", choices=["gemm", "gemv", "qk", "attn"], default=None,
+    ap.add_argument("--case", choices=["gemm", "gemv", "qk", "attn", "vsa"], default=None,
                     help="run one kernel's launches on a small case (for ncu) instead of the bench")
     ap.add_argument("--case-rows", type=int, default=8192, help="--case gemm / qk: activation rows")
     ap.add_argument("--case-kn", type=int, nargs=2, default=(5120, 13824), help="--case gemv: in, out")
@@ -298,13 +298,14 @@ def run_ours(args):
                          f"{min(rows_s, T)} text rows = {f / 1e9:.1f} GFLOP in {dt:.2f} s; same weights as the GPU"}
 
     peaks, src = load_peaks()
-    gemv = qk = attn = None
+    gemv = qk = attn = vsa = None
     if rank == 0 and not args.no_gemv:
         hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
         gemv = measure_gemv(fh3, torch, hbm, src)
         qk = measure_qk_norm_rope(fh3, torch, m_loc, hbm, src)
         attn = measure_attention(fh3, torch, m_loc, float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])),
                                  src)
+        vsa = measure_vsa(fh3, torch, m_loc, float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])), src)
     peak = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
     roof = None
     if gemm_tflops:
@@ -333,7 +334,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(float(mx[3])), "clocks": clk, "device_status": status,
-            "gemv": gemv, "qk_norm_rope": qk, "attention": attn,
+            "gemv": gemv, "qk_norm_rope": qk, "attention": attn, "vsa_attention": vsa,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -438,6 +439,60 @@ def measure_attention(fh3, torch, rows: int, peak: float, peak_src: str, reps: i
             "note": "mma.sync bf16 (legacy tensor path); not part of the GEMM-only step"}
 
 
+def vsa_seq(rows: int):
+    """A DiT sequence of `rows` tokens for video sparse attention: 1024 audio tokens then a
+    video grid of 30 x 52 latent patches per frame (21 frames, 33,784 rows)."""
+    audio = 1024
+    frames = max(1, (rows - audio) // (30 * 52))
+    v = frames * 30 * 52
+    return (audio + v, 0, audio, v, frames, 30, 52)
+
+
+def measure_vsa(fh3, torch, rows: int, peak: float, peak_src: str, reps: int = 3) -> dict:
+    """Device time of one video sparse attention call (fh3_vsa_attention, tile 64, sparsity 0.8,
+    with the coarse gate) over a `rows`-token sequence, 40 heads x 128, bf16 q/k/v/gate/o.
+    FLOPs = 4 * 128 * sum over heads and query tiles of (query rows x kept keys): the fine
+    pass's QK^T and PV over the keys the tile mask keeps (the tile stage is a few GFLOP)."""
+    H, D = 40, 128
+    inner = H * D
+    seq = vsa_seq(rows)
+    n = seq[0]
+    qkv = torch.randn((n, 3 * inner), device="cuda").to(torch.bfloat16)
+    gate = torch.randn((n, inner), device="cuda").to(torch.bfloat16)
+    o = torch.empty((n, inner), dtype=torch.bfloat16, device="cuda")
+    q, k, v = qkv[:, :inner], qkv[:, inner:2 * inner], qkv[:, 2 * inner:]
+    _, mask = fh3.vsa_tiles(q, k, seq, H, D, 64, 0.8)
+    nt, npre, nvid = fh3.vsa_num_tiles(seq)
+    # tokens per tile from the geometry (prefix runs of 64, then 4x4x4 cells of the grid)
+    cnt = [min(64, seq[2] - 64 * a) for a in range(npre)]
+    ct, ch, cw = (seq[4] + 3) // 4, (seq[5] + 3) // 4, (seq[6] + 3) // 4
+    for c in range(nvid):
+        tt, hh, ww = c // (ch * cw), (c // cw) % ch, c % cw
+        cnt.append(min(4, seq[4] - 4 * tt) * min(4, seq[5] - 4 * hh) * min(4, seq[6] - 4 * ww))
+    cnt_t = torch.tensor(cnt, dtype=torch.float64, device="cuda")
+    keys = (mask.double() * cnt_t).sum(dim=2)                 # [H][nt] kept keys per query tile
+    flops = float(4.0 * D * (keys * cnt_t).sum().item())
+    del mask
+    fh3.vsa_attention(q, k, v, gate, seq, H, D, out=o)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fh3.vsa_attention(q, k, v, gate, seq, H, D, out=o)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    tf = flops / (ms * 1e-3) / 1e12
+    del qkv, gate, o
+    return {"kernel": "vsa_fine_kernel (+ tile stage and coarse pass in the timed call)", "rows": n,
+            "seq": {"audio": seq[2], "video": seq[3], "grid": list(seq[4:])}, "tiles": nt, "heads": H,
+            "head_dim": D, "sparsity": 0.8, "ms_per_call": round(ms, 3), "bound": "tensor",
+            "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak, "frac": round(tf / peak, 4),
+            "peak_source": f"{peak_src} bf16_tflops", "flop_per_call": flops,
+            "dense_equivalent_ms": round(4.0 * n * n * H * D / (tf * 1e12) * 1e3, 3),
+            "note": "mma.sync bf16 fine pass; not part of the GEMM-only step"}
+
+
 def run_case(args):
     """One kernel's launches on a small case, for ncu (prints a one-line JSON summary)."""
     import torch
@@ -458,6 +513,17 @@ def run_case(args):
         for _ in range(args.case_reps):
             fh3.attention(qkv[:, :H * Dh], qkv[:, H * Dh:2 * H * Dh], qkv[:, 2 * H * Dh:], H, out=out)
         shape = {"rows": args.case_rows, "heads": H, "head_dim": Dh}
+    elif args.case == "vsa":
+        H, Dh = 40, 128
+        seq = vsa_seq(args.case_rows)
+        n = seq[0]
+        qkv = torch.randn((n, 3 * H * Dh), device="cuda").to(torch.bfloat16)
+        gate = torch.randn((n, H * Dh), device="cuda").to(torch.bfloat16)
+        out = torch.empty((n, H * Dh), dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.case_reps):
+            fh3.vsa_attention(qkv[:, :H * Dh], qkv[:, H * Dh:2 * H * Dh], qkv[:, 2 * H * Dh:], gate, seq, H, Dh,
+                              out=out)
+        shape = {"rows": n, "heads": H, "head_dim": Dh, "grid": list(seq[4:])}
     elif args.case == "qk":
         H, Dh, R = 40, 128, 96
         qkv = torch.randn((args.case_rows, 3 * H * Dh), device="cuda").to(torch.bfloat16)

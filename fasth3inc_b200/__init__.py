@@ -27,7 +27,8 @@ from ._lib import (BF16, EPI_BF16, EPI_F32, EPI_RESID, EPI_SWIGLU, F16, F32, Q2_
 __all__ = [
     "Q4_K", "F32", "F16", "BF16", "Q8_0", "Q2_K", "Q3_K", "Q5_K", "Q6_K", "Weight", "EPI_F32", "EPI_BF16", "EPI_SWIGLU", "EPI_RESID", "Fh3CudaError", "Q4KWeight",
     "init", "row_bytes", "dequant", "matmul", "gemv", "gemm", "matmul_host", "rmsnorm_modulate",
-    "to_bf16", "swiglu", "qk_norm_rope", "attention", "make_weights", "device_status",
+    "to_bf16", "swiglu", "qk_norm_rope", "attention", "vsa_attention", "vsa_tiles", "vsa_num_tiles",
+    "make_weights", "device_status",
 ]
 
 _inited: set[int] = set()
@@ -206,6 +207,55 @@ def attention(q, k, v, heads: int, head_dim: int = 128, out=None, out_bf16: bool
                                        int(out.dtype == torch.bfloat16), out.stride(0), n, heads, head_dim,
                                        _stream(stream)))
     return out
+
+
+def vsa_num_tiles(seq, tile: int = 64) -> tuple[int, int, int]:
+    """(num_tiles, num_prefix_tiles, num_video_tiles) of seq = (n, T, A, V, grid_t, grid_h, grid_w)."""
+    from ._lib import Fh3CudaSeq
+    a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    check(load().fh3cuda_vsa_num_tiles(ctypes.byref(Fh3CudaSeq(*seq)), tile, ctypes.byref(a), ctypes.byref(b),
+                                       ctypes.byref(c)))
+    return a.value, b.value, c.value
+
+
+def vsa_attention(q, k, v, gate, seq, heads: int, head_dim: int, tile: int = 64, sparsity: float = 0.8, out=None,
+                  out_bf16: bool = False, stream=None):
+    """fh3_vsa_attention (src/core/fh3_vsa.c:186-507) on [n][>= heads*head_dim] device views.
+
+    q, k, v (and gate, or None) all fp32 or all bf16; seq = (n, T, A, V, grid_t, grid_h, grid_w)
+    as fh3's Fh3Seq; returns o [n][heads*head_dim] (fp32, or bf16 with out_bf16)."""
+    from ._lib import Fh3CudaSeq
+    torch = _torch()
+    dt = q.dtype
+    for t in (q, k, v) + ((gate,) if gate is not None else ()):
+        _ensure(t)
+        if t.dtype != dt or dt not in (torch.float32, torch.bfloat16) or t.stride(-1) != 1:
+            raise ValueError("q, k, v, gate must share one dtype (fp32 or bf16) with contiguous rows")
+    n = q.shape[0]
+    if out is None:
+        out = torch.empty((n, heads * head_dim), dtype=torch.bfloat16 if out_bf16 else torch.float32,
+                          device=q.device)
+    check(load().fh3cuda_vsa_attention_dev(
+        tile, sparsity, ctypes.byref(Fh3CudaSeq(*seq)), _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v),
+        v.stride(0), int(dt == torch.bfloat16), _ptr(gate) if gate is not None else None,
+        gate.stride(0) if gate is not None else 0, _ptr(out), int(out.dtype == torch.bfloat16), out.stride(0),
+        heads, head_dim, _stream(stream)))
+    return out
+
+
+def vsa_tiles(q, k, seq, heads: int, head_dim: int, tile: int = 64, sparsity: float = 0.8, stream=None):
+    """The tile stage of vsa_attention: (scores [heads][T][T] fp32, mask [heads][T][T] uint8) on the device."""
+    from ._lib import Fh3CudaSeq
+    torch = _torch()
+    for t in (q, k):
+        _ensure(t)
+    nt = vsa_num_tiles(seq, tile)[0]
+    scores = torch.empty((heads, nt, nt), dtype=torch.float32, device=q.device)
+    mask = torch.empty((heads, nt, nt), dtype=torch.uint8, device=q.device)
+    check(load().fh3cuda_vsa_tiles_dev(tile, sparsity, ctypes.byref(Fh3CudaSeq(*seq)), _ptr(q), q.stride(0), _ptr(k),
+                                       k.stride(0), int(q.dtype == torch.bfloat16), heads, head_dim, _ptr(scores),
+                                       _ptr(mask), _stream(stream)))
+    return scores, mask
 
 
 def swiglu(h, out=None, stream=None):

@@ -32,7 +32,8 @@ EXPORTED = [
     "fh3cuda_upload_weights", "fh3cuda_release_weights", "fh3cuda_gemv_q4k_dev",
     "fh3cuda_gemm_q4k_dev", "fh3cuda_f32_to_bf16_dev", "fh3cuda_rmsnorm_modulate_dev",
     "fh3cuda_swiglu_dev", "fh3cuda_make_q4k_weights_dev", "fh3cuda_matmul_noalloc_dev",
-    "fh3cuda_qk_norm_rope_dev", "fh3cuda_attention_dev",
+    "fh3cuda_qk_norm_rope_dev", "fh3cuda_attention_dev", "fh3cuda_vsa_num_tiles", "fh3cuda_vsa_attention_dev",
+    "fh3cuda_vsa_tiles_dev",
 ]
 
 
@@ -40,6 +41,13 @@ class Fh3CudaW(ctypes.Structure):
     """Same layout as fh3's Fh3W (include/fh3/fh3.h:82-87)."""
     _fields_ = [("type", ctypes.c_int), ("in_", ctypes.c_int64), ("out", ctypes.c_int64),
                 ("data", ctypes.c_void_p)]
+
+
+class Fh3CudaSeq(ctypes.Structure):
+    """The fields of fh3's struct Fh3Seq (src/model/fh3_seq.h:31-38) that video sparse attention reads."""
+    _fields_ = [("seq_len", ctypes.c_int32), ("num_text", ctypes.c_int32), ("num_audio", ctypes.c_int32),
+                ("num_video", ctypes.c_int32), ("grid_t", ctypes.c_int32), ("grid_h", ctypes.c_int32),
+                ("grid_w", ctypes.c_int32)]
 
 
 class Fh3CudaError(RuntimeError):
@@ -94,6 +102,12 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         "fh3cuda_attention_dev": (c_int, [vp, i64, vp, i64, vp, i64, vp, c_int, i64, c_int, c_int, c_int, vp]),
         "fh3cuda_make_q4k_weights_dev": (c_int, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, i64, i64,
                                                  vp, vp]),
+        "fh3cuda_vsa_num_tiles": (c_int, [ctypes.POINTER(Fh3CudaSeq), c_int, ctypes.POINTER(c_int),
+                                          ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+        "fh3cuda_vsa_attention_dev": (c_int, [c_int, ctypes.c_float, ctypes.POINTER(Fh3CudaSeq), vp, i64, vp, i64,
+                                              vp, i64, c_int, vp, i64, vp, c_int, i64, c_int, c_int, vp]),
+        "fh3cuda_vsa_tiles_dev": (c_int, [c_int, ctypes.c_float, ctypes.POINTER(Fh3CudaSeq), vp, i64, vp, i64,
+                                          c_int, c_int, c_int, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

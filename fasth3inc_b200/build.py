@@ -12,9 +12,9 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libfh3cuda.so")
-SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemm.cu", "ops.cu", "attention.cu", "gen.cu",
-           "noalloc.cu"]
-HEADERS = ["common.cuh"]
+SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemm.cu", "ops.cu", "attention.cu", "vsa.cu",
+           "gen.cu", "noalloc.cu"]
+HEADERS = ["common.cuh", "flash.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -15,8 +15,8 @@ namespace fh3host {
 
 // scratch slots: 0 bf16 activations of the GEMM, 1 staged weights, 2-4 the host
 // drop-in's x / y / bias, 5 GEMV fragments, 6 split-tile partials, 7 tile counters,
-// 8 fp32 weight rows of the non-Q4_K formats
-constexpr int kScratchSlots = 9;
+// 8 fp32 weight rows of the non-Q4_K formats, 9 video sparse attention's tile data
+constexpr int kScratchSlots = 10;
 
 struct DevCtx {
     int device = -1;

@@ -225,6 +225,51 @@ FH3CUDA_API int fh3cuda_attention_dev(const void *q, int64_t ldq, const void *k,
                                       int64_t ldv, void *o, int o_bf16, int64_t ldo, int n, int heads,
                                       int head_dim, void *stream);
 
+/* The fields of the reference's struct Fh3Seq (src/model/fh3_seq.h:31-38) that
+ * video sparse attention reads: N = text + audio + video tokens in that order,
+ * and the video grid (t, h, w) in tokens.  Counts that do not add up to seq_len
+ * make the whole sequence video; a grid whose product is not num_video is taken
+ * as (1, 1, num_video) (src/core/fh3_vsa.c:42-64). */
+typedef struct Fh3CudaSeq {
+    int32_t seq_len;
+    int32_t num_text;
+    int32_t num_audio;
+    int32_t num_video;
+    int32_t grid_t;
+    int32_t grid_h;
+    int32_t grid_w;
+} Fh3CudaSeq;
+
+/* Tile counts of a sequence for video sparse attention (build_vsa_geometry,
+ * src/core/fh3_vsa.c:32-161): text and audio runs of `tile` tokens (tile <= 0:
+ * 64) and 4x4x4 cells of the video grid.  Any output pointer may be NULL. */
+FH3CUDA_API int fh3cuda_vsa_num_tiles(const Fh3CudaSeq *seq, int tile, int *num_tiles, int *num_prefix,
+                                      int *num_video);
+
+/* Video sparse attention, fh3_vsa_attention (include/fh3/fh3.h:118,
+ * src/core/fh3_vsa.c:186-507), with Fh3VsaCfg's fields (tile, sparsity) passed
+ * directly.  Element (token t, head h, channel d) of q is q[t*ldq + h*head_dim
+ * + d]; likewise k, v, gate and o.  q, k, v and gate are fp32 (in_bf16 = 0) or
+ * bf16; o is fp32 (o_bf16 = 0) or bf16.  gate may be NULL (no coarse branch, as
+ * in the reference).  The tile means, tile scores and the kept key tiles are
+ * computed in fp32 in the reference's order, so the tile mask is the
+ * reference's bit for bit; the fine attention runs on bf16 operands with fp32
+ * softmax and accumulation (bf16 operand error, not bit-exact).  head_dim 64
+ * or 128.  Strides of o and gate (and of q, k, v when bf16) multiples of 8,
+ * those pointers 16-byte aligned. */
+FH3CUDA_API int fh3cuda_vsa_attention_dev(int tile, float sparsity, const Fh3CudaSeq *seq, const void *q,
+                                          int64_t ldq, const void *k, int64_t ldk, const void *v, int64_t ldv,
+                                          int in_bf16, const void *gate, int64_t ldg, void *o, int o_bf16,
+                                          int64_t ldo, int heads, int head_dim, void *stream);
+
+/* The tile stage of fh3cuda_vsa_attention_dev alone: tile scores [heads][T][T]
+ * fp32 (src/core/fh3_vsa.c:268-281) into `scores` and the 0/1 tile mask
+ * [heads][T][T] (:283-356) into `mask` (device buffers; either may be NULL),
+ * T = num_tiles.  Synchronises the stream when the mask is asked for. */
+FH3CUDA_API int fh3cuda_vsa_tiles_dev(int tile, float sparsity, const Fh3CudaSeq *seq, const void *q, int64_t ldq,
+                                      const void *k, int64_t ldk, int in_bf16, int heads, int head_dim,
+                                      float *scores, uint8_t *mask, void *stream);
+
 /* Seeded synthetic Q4_K weights on the device: rows x n weights drawn from
  * scale * N(0,1) (Philox4x32-10 + Box-Muller), quantised with the same
  * per-block rule as the project's CPU quantiser.  Benchmark input generator;

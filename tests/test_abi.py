@@ -7,6 +7,7 @@ import ctypes
 import os
 import re
 
+import numpy as np
 import pytest
 
 from conftest import HAS_GPU, ROOT
@@ -91,3 +92,28 @@ def test_package_api_raises_without_gpu():
     import fasth3inc_b200 as f
     with pytest.raises(Exception):
         f.init(0)
+
+
+def test_vsa_num_tiles_matches_oracle_geometry(oracle):
+    """The host-side tile geometry of fh3cuda_vsa_num_tiles against the oracle's restatement of
+    build_vsa_geometry (src/core/fh3_vsa.c:32-161), fallbacks included (no GPU needed)."""
+    import fasth3inc_b200 as fh3
+    rng = np.random.default_rng(3)
+    for _ in range(300):
+        T, A = (int(x) for x in rng.integers(0, 200, 2))
+        gt, gh, gw = (int(x) for x in rng.integers(1, 13, 3))
+        V = gt * gh * gw
+        n = T + A + V + (int(rng.integers(0, 3)) if rng.random() < 0.1 else 0)   # sometimes a count mismatch
+        if rng.random() < 0.1:
+            gw += 1                                                               # sometimes a grid mismatch
+        tile = int(rng.choice([16, 32, 64, 100]))
+        seq = (n, T, A, V, gt, gh, gw)
+        assert fh3.vsa_num_tiles(seq, tile) == oracle.vsa_tiles(seq, tile), (seq, tile)
+
+
+def test_fh3cudaseq_matches_reference_fh3seq_prefix():
+    from fasth3inc_b200._lib import Fh3CudaSeq
+    # src/model/fh3_seq.h:31-38: seven leading ints of struct Fh3Seq
+    assert ctypes.sizeof(Fh3CudaSeq) == 28
+    assert [getattr(Fh3CudaSeq, f).offset for f in ("seq_len", "num_text", "num_audio", "num_video", "grid_t",
+                                                     "grid_h", "grid_w")] == [0, 4, 8, 12, 16, 20, 24]
