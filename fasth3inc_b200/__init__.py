@@ -192,20 +192,27 @@ def qk_norm_rope(src, norm_w, cos=None, sin=None, heads: int = 1, head_dim: int 
 
 
 def attention(q, k, v, heads: int, head_dim: int = 128, out=None, out_bf16: bool = False, stream=None):
-    """fh3_attention on bf16 [n][>= heads*head_dim] views (e.g. the thirds of a QKV output);
-    returns o [n][heads*head_dim] (fp32, or bf16 with out_bf16)."""
+    """fh3_attention on [n][>= heads*head_dim] views (e.g. the thirds of a QKV output); returns
+    o [n][heads*head_dim].  bf16 q/k/v run on tensor cores (head_dim 128; o fp32, or bf16 with
+    out_bf16); fp32 q/k/v run in fp32 (head_dim a multiple of 32 up to 256; o fp32)."""
     torch = _torch()
+    dt = q.dtype
     for t in (q, k, v):
         _ensure(t)
-        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
-            raise ValueError("q, k, v must be bf16 with contiguous rows")
+        if t.dtype != dt or dt not in (torch.bfloat16, torch.float32) or t.stride(-1) != 1:
+            raise ValueError("q, k, v must share one dtype (bf16 or fp32) with contiguous rows")
     n = q.shape[0]
+    f32 = dt == torch.float32
     if out is None:
-        out = torch.empty((n, heads * head_dim), dtype=torch.bfloat16 if out_bf16 else torch.float32,
+        out = torch.empty((n, heads * head_dim), dtype=torch.bfloat16 if (out_bf16 and not f32) else torch.float32,
                           device=q.device)
-    check(load().fh3cuda_attention_dev(_ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0), _ptr(out),
-                                       int(out.dtype == torch.bfloat16), out.stride(0), n, heads, head_dim,
-                                       _stream(stream)))
+    if f32:
+        check(load().fh3cuda_attention_f32_dev(_ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0),
+                                               _ptr(out), out.stride(0), n, heads, head_dim, _stream(stream)))
+    else:
+        check(load().fh3cuda_attention_dev(_ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0),
+                                           _ptr(out), int(out.dtype == torch.bfloat16), out.stride(0), n, heads,
+                                           head_dim, _stream(stream)))
     return out
 
 
@@ -223,7 +230,9 @@ def vsa_attention(q, k, v, gate, seq, heads: int, head_dim: int, tile: int = 64,
     """fh3_vsa_attention (src/core/fh3_vsa.c:186-507) on [n][>= heads*head_dim] device views.
 
     q, k, v (and gate, or None) all fp32 or all bf16; seq = (n, T, A, V, grid_t, grid_h, grid_w)
-    as fh3's Fh3Seq; returns o [n][heads*head_dim] (fp32, or bf16 with out_bf16)."""
+    as fh3's Fh3Seq; returns o [n][heads*head_dim] (fp32, or bf16 with out_bf16 for bf16 operands).
+    The tile mask is the reference's exactly; bf16 operands run the fine pass on tensor cores,
+    fp32 operands in fp32."""
     from ._lib import Fh3CudaSeq
     torch = _torch()
     dt = q.dtype
@@ -233,7 +242,8 @@ def vsa_attention(q, k, v, gate, seq, heads: int, head_dim: int, tile: int = 64,
             raise ValueError("q, k, v, gate must share one dtype (fp32 or bf16) with contiguous rows")
     n = q.shape[0]
     if out is None:
-        out = torch.empty((n, heads * head_dim), dtype=torch.bfloat16 if out_bf16 else torch.float32,
+        out = torch.empty((n, heads * head_dim),
+                          dtype=torch.bfloat16 if (out_bf16 and dt == torch.bfloat16) else torch.float32,
                           device=q.device)
     check(load().fh3cuda_vsa_attention_dev(
         tile, sparsity, ctypes.byref(Fh3CudaSeq(*seq)), _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v),

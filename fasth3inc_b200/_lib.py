@@ -33,7 +33,10 @@ EXPORTED = [
     "fh3cuda_gemm_q4k_dev", "fh3cuda_f32_to_bf16_dev", "fh3cuda_rmsnorm_modulate_dev",
     "fh3cuda_swiglu_dev", "fh3cuda_make_q4k_weights_dev", "fh3cuda_matmul_noalloc_dev",
     "fh3cuda_qk_norm_rope_dev", "fh3cuda_attention_dev", "fh3cuda_vsa_num_tiles", "fh3cuda_vsa_attention_dev",
-    "fh3cuda_vsa_tiles_dev",
+    "fh3cuda_vsa_tiles_dev", "fh3cuda_attention_f32_dev", "fh3cuda_pack_open", "fh3cuda_pack_num_layers",
+    "fh3cuda_pack_device_bytes", "fh3cuda_pack_layer", "fh3cuda_pack_close", "fh3cuda_adaln_open",
+    "fh3cuda_adaln_dims", "fh3cuda_adaln_row", "fh3cuda_adaln_close", "fh3cuda_dit_prepare_text_dev",
+    "fh3cuda_dit_forward_dev",
 ]
 
 
@@ -48,6 +51,38 @@ class Fh3CudaSeq(ctypes.Structure):
     _fields_ = [("seq_len", ctypes.c_int32), ("num_text", ctypes.c_int32), ("num_audio", ctypes.c_int32),
                 ("num_video", ctypes.c_int32), ("grid_t", ctypes.c_int32), ("grid_h", ctypes.c_int32),
                 ("grid_w", ctypes.c_int32)]
+
+
+class Fh3CudaLayerView(ctypes.Structure):
+    """fh3's Fh3LayerView (include/fh3/fh3.h:90-100) with device pointers."""
+    _fields_ = [(n, Fh3CudaW) for n in ("qkv", "gate_compress", "out", "fc1", "fc2", "norm1", "norm2", "q_norm",
+                                        "k_norm")]
+
+
+class Fh3CudaDitCfg(ctypes.Structure):
+    """The fields of fh3's Fh3DitCfg (src/model/fh3_dit.h:19-39) the device forward uses (+ attn_bf16)."""
+    _fields_ = [("attn", ctypes.c_int32), ("vsa_tile", ctypes.c_int32), ("vsa_sparsity", ctypes.c_float),
+                ("hidden_size", ctypes.c_int32), ("num_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("num_layers", ctypes.c_int32), ("num_refiner_layers", ctypes.c_int32), ("ffn_dim", ctypes.c_int32),
+                ("norm_eps", ctypes.c_float), ("qk_norm_eps", ctypes.c_float), ("final_norm_eps", ctypes.c_float),
+                ("attn_bf16", ctypes.c_int32)]
+
+
+class Fh3CudaRefinerBlock(ctypes.Structure):
+    """fh3's Fh3RefinerBlock (src/model/fh3_dit.h:41-50) with device pointers."""
+    _fields_ = [("norm1", ctypes.c_void_p), ("qkv", Fh3CudaW), ("q_norm", ctypes.c_void_p),
+                ("k_norm", ctypes.c_void_p), ("out", Fh3CudaW), ("norm2", ctypes.c_void_p), ("fc1", Fh3CudaW),
+                ("fc2", Fh3CudaW)]
+
+
+class Fh3CudaDitGlobals(ctypes.Structure):
+    """The global weights of fh3's Fh3Dit (src/model/fh3_dit.h:52-86) as device data."""
+    _fields_ = [("video_patch_proj", Fh3CudaW), ("video_patch_proj_bias", ctypes.c_void_p),
+                ("audio_patch_proj", Fh3CudaW), ("audio_patch_proj_bias", ctypes.c_void_p),
+                ("condition_proj", Fh3CudaW), ("condition_proj_bias", ctypes.c_void_p),
+                ("refiner", Fh3CudaRefinerBlock * 4), ("refiner_final_norm", ctypes.c_void_p),
+                ("final_norm", ctypes.c_void_p), ("video_out", Fh3CudaW), ("video_out_bias", ctypes.c_void_p),
+                ("audio_out", Fh3CudaW), ("audio_out_bias", ctypes.c_void_p)]
 
 
 class Fh3CudaError(RuntimeError):
@@ -102,6 +137,20 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         "fh3cuda_attention_dev": (c_int, [vp, i64, vp, i64, vp, i64, vp, c_int, i64, c_int, c_int, c_int, vp]),
         "fh3cuda_make_q4k_weights_dev": (c_int, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, i64, i64,
                                                  vp, vp]),
+        "fh3cuda_pack_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(vp)]),
+        "fh3cuda_pack_num_layers": (c_int, [vp]),
+        "fh3cuda_pack_device_bytes": (ctypes.c_uint64, [vp]),
+        "fh3cuda_pack_layer": (c_int, [vp, c_int, ctypes.POINTER(Fh3CudaLayerView)]),
+        "fh3cuda_pack_close": (None, [vp]),
+        "fh3cuda_adaln_open": (c_int, [ctypes.c_char_p, ctypes.c_uint64, ctypes.POINTER(vp)]),
+        "fh3cuda_adaln_dims": (c_int, [vp] + [ctypes.POINTER(c_int)] * 4),
+        "fh3cuda_adaln_row": (vp, [vp, c_int, c_int, c_int, c_int]),
+        "fh3cuda_adaln_close": (None, [vp]),
+        "fh3cuda_dit_prepare_text_dev": (c_int, [ctypes.POINTER(Fh3CudaDitCfg), ctypes.POINTER(Fh3CudaDitGlobals),
+                                                 vp, c_int, vp, vp]),
+        "fh3cuda_dit_forward_dev": (c_int, [ctypes.POINTER(Fh3CudaDitCfg), ctypes.POINTER(Fh3CudaDitGlobals), vp, vp,
+                                            ctypes.POINTER(Fh3CudaSeq), vp, vp, c_int, vp, vp, vp, vp, vp, vp]),
+        "fh3cuda_attention_f32_dev": (c_int, [vp, i64, vp, i64, vp, i64, vp, i64, c_int, c_int, c_int, vp]),
         "fh3cuda_vsa_num_tiles": (c_int, [ctypes.POINTER(Fh3CudaSeq), c_int, ctypes.POINTER(c_int),
                                           ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
         "fh3cuda_vsa_attention_dev": (c_int, [c_int, ctypes.c_float, ctypes.POINTER(Fh3CudaSeq), vp, i64, vp, i64,

@@ -15,8 +15,9 @@ namespace fh3host {
 
 // scratch slots: 0 bf16 activations of the GEMM, 1 staged weights, 2-4 the host
 // drop-in's x / y / bias, 5 GEMV fragments, 6 split-tile partials, 7 tile counters,
-// 8 fp32 weight rows of the non-Q4_K formats, 9 video sparse attention's tile data
-constexpr int kScratchSlots = 10;
+// 8 fp32 weight rows of the non-Q4_K formats, 9 video sparse attention's tile data,
+// 10 the DiT forward's activations
+constexpr int kScratchSlots = 11;
 
 struct DevCtx {
     int device = -1;
@@ -56,6 +57,7 @@ DevCtx* ctx() {
 }
 int* ctx_status(DevCtx* c) { return c ? c->d_status : nullptr; }
 int ctx_sms(DevCtx* c) { return c ? c->sms : 0; }
+int ctx_device(DevCtx* c) { return c ? c->device : -1; }
 
 int set_error(int code, const char* fmt, ...) {
     va_list ap;

@@ -378,6 +378,7 @@ struct DevCtx;
 DevCtx* ctx();                       // context of the current device (nullptr if not initialised)
 int* ctx_status(DevCtx* c);          // device status word
 int ctx_sms(DevCtx* c);
+int ctx_device(DevCtx* c);               // CUDA ordinal of the context (-1 if none)
 int set_error(int code, const char* fmt, ...);
 int check_cuda(cudaError_t e, const char* what);
 // cuTensorMapEncodeTiled through the runtime's driver entry point
@@ -393,6 +394,12 @@ void* scratch_zeroed(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
 int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
 // the fp32 CUDA-core GEMV (gemv.cu): uses no memory beyond x, y, bias and the weights
 int gemv_fp32(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
+// fp32 softmax attention (attention_f32.cu): dense over n keys when sel is null, else
+// the fine pass of video sparse attention over the kept key tiles (+ outc * gate)
+int attention_f32_launch(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                         float* o, int64_t ldo, int n, int heads, int head_dim, const int* perm, const int* toff,
+                         const int* sel, const int* selcnt, int nt, const float* gate, int64_t ldg,
+                         const float* outc, cudaStream_t s);
 // argument checks shared by the GEMV entry points (FH3_OK or the error code, message set)
 int gemv_args_ok(const Fh3CudaW* w, const float* x, const float* y, int n_tok, const char* who);
 }  // namespace fh3host

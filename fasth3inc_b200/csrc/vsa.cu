@@ -17,8 +17,9 @@
 //   vsa_fine_kernel    flash attention of 64 query rows over the kept key tiles,
 //                      gathered by token index (cp.async, zero-filled past a tile's
 //                      end); the coarse term times the gate is added in the epilogue.
-// The tile mask is therefore exactly the reference's; the fine pass runs on bf16
-// operands (fh3flash::WarpFlash, flash.cuh) with fp32 softmax and accumulation.
+// The tile mask is therefore exactly the reference's; with bf16 operands the fine pass
+// runs on tensor cores (fh3flash::WarpFlash, flash.cuh) with fp32 softmax and
+// accumulation, with fp32 operands in fp32 (attention_f32.cu).
 //
 // Operands: element (token t, head h, channel d) of q at q[t*ldq + h*head_dim + d]
 // (likewise k, v, gate, o), fp32 or bf16.
@@ -340,16 +341,6 @@ __global__ void __launch_bounds__(128) vsa_coarse_kernel(const float* __restrict
     }
 }
 
-__global__ void vsa_to_bf16_kernel(const float* __restrict__ x, int64_t ld, __nv_bfloat16* __restrict__ y, int n,
-                                   int width) {
-    const int64_t total = static_cast<int64_t>(n) * width;
-    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
-         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t t = e / width, c = e - t * width;
-        y[e] = __float2bfloat16_rn(x[t * ld + c]);
-    }
-}
-
 // rows of a gathered tile: row r < rows is token toks[r] (head h), later rows are zero
 template <int HD>
 __device__ __forceinline__ void load_rows(uint32_t tile, const __nv_bfloat16* __restrict__ base, int64_t ld, int h,
@@ -492,12 +483,10 @@ struct VsaBufs {
     int* sel;
     int* selcnt;
     float* outc;
-    __nv_bfloat16 *qb, *kb, *vb;  // bf16 copies of fp32 q / k / v (fine pass)
 };
 
-size_t vsa_layout(const VsaGeo& g, int heads, int hd, bool gate, bool convert, uint8_t* base, VsaBufs* b) {
+size_t vsa_layout(const VsaGeo& g, int heads, int hd, bool gate, uint8_t* base, VsaBufs* b) {
     const size_t nt = g.ntiles, pool = static_cast<size_t>(heads) * nt * hd * 4;
-    const size_t act = static_cast<size_t>(g.n) * heads * hd * 2;
     size_t off = 0;
     auto take = [&](size_t bytes) {
         uint8_t* p = base ? base + off : nullptr;
@@ -514,11 +503,6 @@ size_t vsa_layout(const VsaGeo& g, int heads, int hd, bool gate, bool convert, u
     x.sel = reinterpret_cast<int*>(take(static_cast<size_t>(heads) * nt * nt * 4));
     x.selcnt = reinterpret_cast<int*>(take(static_cast<size_t>(heads) * nt * 4));
     x.outc = gate ? reinterpret_cast<float*>(take(nt * heads * hd * 4)) : nullptr;
-    if (convert) {
-        x.qb = reinterpret_cast<__nv_bfloat16*>(take(act));
-        x.kb = reinterpret_cast<__nv_bfloat16*>(take(act));
-        x.vb = reinterpret_cast<__nv_bfloat16*>(take(act));
-    }
     if (b) *b = x;
     return off;
 }
@@ -527,8 +511,8 @@ constexpr int kVsaSlot = 9;
 
 // geometry, tile means, scores and kept lists; returns FH3_OK or an error code
 int vsa_prepare(const char* who, int tile, float sparsity, const Fh3CudaSeq* seq, const void* q, int64_t ldq,
-                const void* k, int64_t ldk, const void* v, int64_t ldv, int in_bf16, bool with_gate, bool convert,
-                int heads, int head_dim, cudaStream_t s, VsaGeo& g, VsaBufs& b) {
+                const void* k, int64_t ldk, const void* v, int64_t ldv, int in_bf16, bool with_gate, int heads,
+                int head_dim, cudaStream_t s, VsaGeo& g, VsaBufs& b) {
     using namespace fh3host;
     if (!ctx()) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);
     if (!seq || !q || !k || (with_gate && !v) || heads <= 0 || heads > 65535)
@@ -540,10 +524,10 @@ int vsa_prepare(const char* who, int tile, float sparsity, const Fh3CudaSeq* seq
     if (ldq < row || ldk < row || (v && ldv < row))
         return set_error(FH3_E_INVALID, "%s: rows must hold heads*head_dim elements", who);
     if (g.nvid > 48 * 1024) return set_error(FH3_E_INVALID, "%s: more than 49152 video tiles", who);
-    const size_t bytes = vsa_layout(g, heads, head_dim, with_gate, convert, nullptr, nullptr);
+    const size_t bytes = vsa_layout(g, heads, head_dim, with_gate, nullptr, nullptr);
     uint8_t* base = static_cast<uint8_t*>(scratch(ctx(), kVsaSlot, bytes, s));
     if (!base) return FH3_E_NOMEM;
-    vsa_layout(g, heads, head_dim, with_gate, convert, base, &b);
+    vsa_layout(g, heads, head_dim, with_gate, base, &b);
     const int nt = g.ntiles;
 
     vsa_perm_kernel<<<nt, 64, 0, s>>>(g, b.perm, b.toff);
@@ -596,8 +580,8 @@ extern "C" int fh3cuda_vsa_tiles_dev(int tile, float sparsity, const Fh3CudaSeq*
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     VsaGeo g;
     VsaBufs b;
-    int rc = vsa_prepare(who, tile, sparsity, seq, q, ldq, k, ldk, nullptr, 0, in_bf16, false, false, heads,
-                         head_dim, s, g, b);
+    int rc = vsa_prepare(who, tile, sparsity, seq, q, ldq, k, ldk, nullptr, 0, in_bf16, false, heads, head_dim, s,
+                         g, b);
     if (rc) return rc;
     const size_t nn = static_cast<size_t>(heads) * g.ntiles * g.ntiles;
     if (scores) {
@@ -630,46 +614,42 @@ extern "C" int fh3cuda_vsa_attention_dev(int tile, float sparsity, const Fh3Cuda
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (!q || !k || !v || !o) return set_error(FH3_E_INVALID, "%s: bad arguments", who);
     const int64_t rowe = static_cast<int64_t>(heads) * head_dim;
-    if (ldo < rowe || (ldo % 8) || !aligned16(o) || (gate && (ldg < rowe || (ldg % 8) || !aligned16(gate))) ||
-        (in_bf16 && ((ldq % 8) || (ldk % 8) || (ldv % 8) || !aligned16(q) || !aligned16(k) || !aligned16(v))))
-        return set_error(FH3_E_INVALID, "%s: strides must be multiples of 8 elements and pointers 16-byte aligned "
-                         "(o, gate; q/k/v when bf16)", who);
+    if (in_bf16) {
+        if (ldo < rowe || (ldo % 8) || !aligned16(o) || (gate && (ldg < rowe || (ldg % 8) || !aligned16(gate))) ||
+            (ldq % 8) || (ldk % 8) || (ldv % 8) || !aligned16(q) || !aligned16(k) || !aligned16(v))
+            return set_error(FH3_E_INVALID, "%s: bf16 operands need strides that are multiples of 8 elements and "
+                             "16-byte aligned pointers (q, k, v, gate, o)", who);
+    } else if (o_bf16 || ldo < rowe || (gate && ldg < rowe)) {
+        return set_error(FH3_E_INVALID, "%s: fp32 operands give an fp32 output (o_bf16 = 0); rows must hold "
+                         "heads*head_dim elements", who);
+    }
     VsaGeo g;
     VsaBufs b;
-    int rc = vsa_prepare(who, tile, sparsity, seq, q, ldq, k, ldk, v, ldv, in_bf16, gate != nullptr, !in_bf16,
-                         heads, head_dim, s, g, b);
+    int rc = vsa_prepare(who, tile, sparsity, seq, q, ldq, k, ldk, v, ldv, in_bf16, gate != nullptr, heads,
+                         head_dim, s, g, b);
     if (rc) return rc;
     const int nt = g.ntiles;
     if (gate) {
         const int R = static_cast<int>(std::min<int64_t>(kCoarseRows, std::max<int64_t>(1, (200 * 1024) / (4 * nt))));
         const size_t csm = static_cast<size_t>(R) * nt * 4;
+        if (csm > 227 * 1024) return set_error(FH3_E_INVALID, "%s: too many tiles for the coarse pass", who);
         if (csm > 48 * 1024) {
             rc = check_cuda(cudaFuncSetAttribute(vsa_coarse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(csm)), "vsa coarse smem attribute");
             if (rc) return rc;
         }
-        if (csm > 227 * 1024) return set_error(FH3_E_INVALID, "%s: too many tiles for the coarse pass", who);
         vsa_coarse_kernel<<<dim3(static_cast<unsigned>((nt + R - 1) / R), static_cast<unsigned>(heads)), 128, csm,
                             s>>>(b.S, b.vp, b.outc, nt, heads, head_dim, R);
     }
-    const __nv_bfloat16 *qb, *kb, *vb;
-    int64_t lq = ldq, lk = ldk, lv = ldv;
-    if (in_bf16) {
-        qb = static_cast<const __nv_bfloat16*>(q);
-        kb = static_cast<const __nv_bfloat16*>(k);
-        vb = static_cast<const __nv_bfloat16*>(v);
-    } else {
-        const int w = static_cast<int>(rowe);
-        const int blocks = std::max(1, std::min(ctx_sms(ctx()) * 8,
-                                                static_cast<int>((static_cast<int64_t>(g.n) * w + 255) / 256)));
-        vsa_to_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(q), ldq, b.qb, g.n, w);
-        vsa_to_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(k), ldk, b.kb, g.n, w);
-        vsa_to_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(v), ldv, b.vb, g.n, w);
-        qb = b.qb;
-        kb = b.kb;
-        vb = b.vb;
-        lq = lk = lv = rowe;
-    }
+    if (!in_bf16)  // fp32 operands: the fine pass in fp32 (attention_f32.cu)
+        return attention_f32_launch(static_cast<const float*>(q), ldq, static_cast<const float*>(k), ldk,
+                                    static_cast<const float*>(v), ldv, static_cast<float*>(o), ldo, g.n, heads,
+                                    head_dim, b.perm, b.toff, b.sel, b.selcnt, nt, static_cast<const float*>(gate),
+                                    ldg, b.outc, s);
+    const auto* qb = static_cast<const __nv_bfloat16*>(q);
+    const auto* kb = static_cast<const __nv_bfloat16*>(k);
+    const auto* vb = static_cast<const __nv_bfloat16*>(v);
+    const int64_t lq = ldq, lk = ldk, lv = ldv;
     const int max_rows = std::max(64, g.npre > 0 ? std::min(g.tile, std::max(g.T, g.A)) : 64);
     const int qsplit = (max_rows + kKeys - 1) / kKeys;
     const float scale_log2 = (1.0f / sqrtf(static_cast<float>(head_dim))) * 1.4426950408889634f;

@@ -42,6 +42,10 @@ extern "C" {
 /* Status codes (values of include/fh3/fh3.h:218-226, plus three). */
 #define FH3_OK              0
 #define FH3_ERR           (-1)
+#define FH3_E_IO          (-2)
+#define FH3_E_TRUNCATED   (-3)
+#define FH3_E_BAD_MAGIC   (-4)
+#define FH3_E_BAD_VERSION (-5)
 #define FH3_E_NOMEM       (-7)
 #define FH3_E_INVALID     (-8)
 #define FH3CUDA_E_CUDA    (-20)  /* a CUDA runtime/driver call failed        */
@@ -253,14 +257,23 @@ FH3CUDA_API int fh3cuda_vsa_num_tiles(const Fh3CudaSeq *seq, int tile, int *num_
  * bf16; o is fp32 (o_bf16 = 0) or bf16.  gate may be NULL (no coarse branch, as
  * in the reference).  The tile means, tile scores and the kept key tiles are
  * computed in fp32 in the reference's order, so the tile mask is the
- * reference's bit for bit; the fine attention runs on bf16 operands with fp32
- * softmax and accumulation (bf16 operand error, not bit-exact).  head_dim 64
- * or 128.  Strides of o and gate (and of q, k, v when bf16) multiples of 8,
- * those pointers 16-byte aligned. */
+ * reference's bit for bit.  With bf16 operands the fine attention runs on
+ * tensor cores with fp32 softmax and accumulation (bf16 operand error, not
+ * bit-exact); their strides must be multiples of 8 and the pointers (q, k, v,
+ * gate, o) 16-byte aligned.  With fp32 operands it runs in fp32 (the CPU
+ * path's accuracy) and o must be fp32.  head_dim 64 or 128. */
 FH3CUDA_API int fh3cuda_vsa_attention_dev(int tile, float sparsity, const Fh3CudaSeq *seq, const void *q,
                                           int64_t ldq, const void *k, int64_t ldk, const void *v, int64_t ldv,
                                           int in_bf16, const void *gate, int64_t ldg, void *o, int o_bf16,
                                           int64_t ldo, int heads, int head_dim, void *stream);
+
+/* fh3_attention on fp32 operands in fp32 arithmetic (the CPU path's accuracy,
+ * for parity work and small shapes; the bf16 tensor-core kernel above carries
+ * the production shapes).  Layout as fh3cuda_attention_dev; head_dim a
+ * multiple of 32 up to 256. */
+FH3CUDA_API int fh3cuda_attention_f32_dev(const float *q, int64_t ldq, const float *k, int64_t ldk, const float *v,
+                                          int64_t ldv, float *o, int64_t ldo, int n, int heads, int head_dim,
+                                          void *stream);
 
 /* The tile stage of fh3cuda_vsa_attention_dev alone: tile scores [heads][T][T]
  * fp32 (src/core/fh3_vsa.c:268-281) into `scores` and the 0/1 tile mask
@@ -269,6 +282,115 @@ FH3CUDA_API int fh3cuda_vsa_attention_dev(int tile, float sparsity, const Fh3Cud
 FH3CUDA_API int fh3cuda_vsa_tiles_dev(int tile, float sparsity, const Fh3CudaSeq *seq, const void *q, int64_t ldq,
                                       const void *k, int64_t ldk, int in_bf16, int heads, int head_dim,
                                       float *scores, uint8_t *mask, void *stream);
+
+/* ---- packed trunk and AdaLN table, resident in HBM ------------------------ */
+
+/* A packed DiT trunk (FH3P, src/io/fh3_pack.h:29-88) read once into device
+ * memory: replaces fh3_pack_open + the NVMe ring of fh3_trunk_open /
+ * fh3_trunk_acquire (src/io/fh3_pack.c:23-106, src/io/fh3_trunk.c:135-501).
+ * Errors as fh3_pack_open: FH3_E_IO, FH3_E_TRUNCATED, FH3_E_BAD_MAGIC,
+ * FH3_E_BAD_VERSION, FH3_E_INVALID, plus FH3_E_NOMEM. */
+typedef struct Fh3CudaPack Fh3CudaPack;
+
+/* fh3's Fh3LayerView (include/fh3/fh3.h:90-100) with device data pointers */
+typedef struct Fh3CudaLayerView {
+    Fh3CudaW qkv;
+    Fh3CudaW gate_compress;
+    Fh3CudaW out;
+    Fh3CudaW fc1;
+    Fh3CudaW fc2;
+    Fh3CudaW norm1;
+    Fh3CudaW norm2;
+    Fh3CudaW q_norm;
+    Fh3CudaW k_norm;
+} Fh3CudaLayerView;
+
+FH3CUDA_API int fh3cuda_pack_open(const char *path, Fh3CudaPack **out);
+FH3CUDA_API int fh3cuda_pack_num_layers(const Fh3CudaPack *p);
+FH3CUDA_API uint64_t fh3cuda_pack_device_bytes(const Fh3CudaPack *p);
+/* fh3_pack_layer / fh3_trunk_layer (src/io/fh3_pack.c:140-205) */
+FH3CUDA_API int fh3cuda_pack_layer(const Fh3CudaPack *p, int L, Fh3CudaLayerView *out);
+FH3CUDA_API void fh3cuda_pack_close(Fh3CudaPack *p);
+
+/* The folded AdaLN table (FH3A) in device memory: fh3_adaln_open (expect_hash
+ * 0 skips the schedule check) and fh3_adaln_row (src/io/fh3_pack.c:188-355);
+ * a row is a device pointer to hidden_size floats, NULL outside the table. */
+typedef struct Fh3CudaAdaln Fh3CudaAdaln;
+FH3CUDA_API int fh3cuda_adaln_open(const char *path, uint64_t expect_hash, Fh3CudaAdaln **out);
+FH3CUDA_API int fh3cuda_adaln_dims(const Fh3CudaAdaln *a, int *n_steps, int *n_blocks, int *pairs_per_step,
+                                   int *hidden_size);
+FH3CUDA_API const float *fh3cuda_adaln_row(const Fh3CudaAdaln *a, int step, int block, int pair, int chunk);
+FH3CUDA_API void fh3cuda_adaln_close(Fh3CudaAdaln *a);
+
+/* ---- the DiT forward on the device ----------------------------------------- */
+
+/* The fields of fh3's Fh3DitCfg (src/model/fh3_dit.h:19-39) the forward uses, and
+ * one of this library's: attn_bf16 = 0 runs attention in fp32 (the CPU path's
+ * accuracy), 1 on bf16 tensor cores (dense attention then needs head_dim 128). */
+typedef struct Fh3CudaDitCfg {
+    int32_t attn;          /* 0 dense (FH3_ATTN_DENSE), 1 video sparse (FH3_ATTN_VSA) */
+    int32_t vsa_tile;      /* Fh3VsaCfg.tile (<= 0: 64) */
+    float vsa_sparsity;    /* Fh3VsaCfg.sparsity */
+    int32_t hidden_size;
+    int32_t num_heads;
+    int32_t head_dim;
+    int32_t num_layers;
+    int32_t num_refiner_layers;  /* 0..4 */
+    int32_t ffn_dim;
+    float norm_eps;
+    float qk_norm_eps;
+    float final_norm_eps;
+    int32_t attn_bf16;
+} Fh3CudaDitCfg;
+
+/* Fh3RefinerBlock (src/model/fh3_dit.h:41-50) with device pointers */
+typedef struct Fh3CudaRefinerBlock {
+    const float *norm1;
+    Fh3CudaW qkv;
+    const float *q_norm;
+    const float *k_norm;
+    Fh3CudaW out;
+    const float *norm2;
+    Fh3CudaW fc1;
+    Fh3CudaW fc2;
+} Fh3CudaRefinerBlock;
+
+/* The global weights of fh3's Fh3Dit (src/model/fh3_dit.h:52-86: patch and
+ * condition projections, text refiner, final layer) as device data; a host loads
+ * them from dit_globals (fh3_dit_open, src/model/fh3_dit.c:55-180) and uploads
+ * them once.  Biases may be NULL. */
+typedef struct Fh3CudaDitGlobals {
+    Fh3CudaW video_patch_proj;
+    const float *video_patch_proj_bias;
+    Fh3CudaW audio_patch_proj;
+    const float *audio_patch_proj_bias;
+    Fh3CudaW condition_proj;
+    const float *condition_proj_bias;
+    Fh3CudaRefinerBlock refiner[4];
+    const float *refiner_final_norm;
+    const float *final_norm;
+    Fh3CudaW video_out;
+    const float *video_out_bias;
+    Fh3CudaW audio_out;
+    const float *audio_out_bias;
+} Fh3CudaDitGlobals;
+
+/* fh3_dit_prepare_text (src/model/fh3_dit.c:221-281): text_emb [T][text_dim] ->
+ * text_rows [T][hidden_size], device fp32. */
+FH3CUDA_API int fh3cuda_dit_prepare_text_dev(const Fh3CudaDitCfg *cfg, const Fh3CudaDitGlobals *g,
+                                             const float *text_emb, int T, float *text_rows, void *stream);
+
+/* fh3_dit_forward (src/model/fh3_dit.c:283-467) for denoising step `step`: trunk
+ * layers from a resident pack, modulation from a resident AdaLN table, rows text
+ * | audio | video as seq counts them, cos_t / sin_t the [seq_len][96] rope tables
+ * of fh3_seq_build (src/model/fh3_seq.c:147-168); x_video [V][video patch dim],
+ * x_audio [A][audio patch dim], text_rows [T][hidden] -> v_video, v_audio.  All
+ * device fp32.  FH3_E_INVALID for a step outside the table (as the reference). */
+FH3CUDA_API int fh3cuda_dit_forward_dev(const Fh3CudaDitCfg *cfg, const Fh3CudaDitGlobals *g,
+                                        const Fh3CudaPack *trunk, const Fh3CudaAdaln *adaln,
+                                        const Fh3CudaSeq *seq, const float *cos_t, const float *sin_t, int step,
+                                        const float *x_video, const float *x_audio, const float *text_rows,
+                                        float *v_video, float *v_audio, void *stream);
 
 /* Seeded synthetic Q4_K weights on the device: rows x n weights drawn from
  * scale * N(0,1) (Philox4x32-10 + Box-Muller), quantised with the same

@@ -61,6 +61,14 @@ class _Fh3Seq(ctypes.Structure):
                 ("pos", ctypes.c_void_p), ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p)]
 
 
+class _Fh3SeqSpec(ctypes.Structure):
+    """Mirror of the reference's Fh3SeqSpec (src/model/fh3_seq.h:13-29)."""
+    _fields_ = [(n, ctypes.c_int) for n in ("num_text", "num_audio", "num_video", "latent_frames", "latent_height",
+                                            "latent_width", "patch_t", "patch_h", "patch_w", "audio_latents",
+                                            "audio_channels")] + [
+        ("custom_pos", ctypes.c_void_p), ("grid_t", ctypes.c_int), ("grid_h", ctypes.c_int), ("grid_w", ctypes.c_int)]
+
+
 class _Fh3VsaCfg(ctypes.Structure):
     """Mirror of the reference's Fh3VsaCfg (include/fh3/fh3.h:41-44)."""
     _fields_ = [("tile", ctypes.c_int), ("sparsity", ctypes.c_float)]
@@ -275,6 +283,9 @@ class Reference:
         lib.fh3_rng_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _c_f32p, ctypes.c_size_t]
         lib.fh3_vsa_attention.argtypes = [ctypes.POINTER(_Fh3VsaCfg)] + [_c_f32p] * 5 + [
             ctypes.POINTER(_Fh3Seq), ctypes.c_int, ctypes.c_int]
+        lib.fh3_seq_build.restype = ctypes.c_int
+        lib.fh3_seq_build.argtypes = [ctypes.POINTER(_Fh3SeqSpec), ctypes.POINTER(_Fh3Seq)]
+        lib.fh3_seq_free.argtypes = [ctypes.POINTER(_Fh3Seq)]
         self.lib = lib
 
     @staticmethod
@@ -326,6 +337,21 @@ class Reference:
         self.lib.fh3_attention(_ptr(q, _c_f32p), _ptr(k, _c_f32p), _ptr(v, _c_f32p), _ptr(o, _c_f32p),
                                q.shape[0], heads, hd)
         return o
+
+    def seq_build(self, num_text: int, num_audio: int, num_video: int, pos: np.ndarray | None = None, **spec):
+        """fh3_seq_build itself: (pair_index [N], cos [N][96], sin [N][96]) of a sequence."""
+        p = None if pos is None else np.ascontiguousarray(pos, dtype=np.float64)
+        sp = _Fh3SeqSpec(num_text=num_text, num_audio=num_audio, num_video=num_video,
+                         custom_pos=None if p is None else p.ctypes.data, **spec)
+        sq = _Fh3Seq()
+        if self.lib.fh3_seq_build(ctypes.byref(sp), ctypes.byref(sq)):
+            raise ValueError("fh3_seq_build failed")
+        n = sq.seq_len
+        pair = np.ctypeslib.as_array(ctypes.cast(sq.pair_index, ctypes.POINTER(ctypes.c_int)), (n,)).copy()
+        cos = np.ctypeslib.as_array(ctypes.cast(sq.cos, _c_f32p), (n, 96)).copy()
+        sin = np.ctypeslib.as_array(ctypes.cast(sq.sin, _c_f32p), (n, 96)).copy()
+        self.lib.fh3_seq_free(ctypes.byref(sq))
+        return pair, cos, sin
 
     def vsa(self, q, k, v, gate, seq: tuple, heads: int, hd: int, tile: int = 64, sparsity: float = 0.8):
         """fh3_vsa_attention itself; seq = (n, T, A, V, gt, gh, gw)."""

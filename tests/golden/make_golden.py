@@ -13,6 +13,9 @@
    And the video-sparse-attention fixtures tests/fixtures/vsa/{vsa_n784,vsa_padded,vsa_sparsity0}.bin
    -> vsa/*.bin (<u32 n, T, A, V, grid_t, grid_h, grid_w, heads, head_dim; f32 sparsity; u32 has_gate>,
    then q, k, v, [gate], ref as [n][heads][head_dim] fp32), read by tests/unit/test_vsa.c:56-133.
+   And the tiny end-to-end model tests/fixtures/tiny_h3/ -> tiny_h3/ (tools/make_tiny_h3.py: a
+   3-layer F32 DiT packed as FH3P + FH3A + GGUF globals, inputs, and torch's outputs at steps 0 and 7,
+   dense and VSA), read by tests/unit/test_dit_tiny.c.
 2. Writes ref_cases.npz: seeded inputs (this project's Q4_K quantiser + fh3_rng_normal)
    with outputs computed by the REFERENCE'S OWN fh3_matmul / fh3_dequant / fh3_swiglu,
    compiled from its sources into oracle/_ref/libfh3ref.so (oracle/Makefile).  These pin
@@ -48,6 +51,12 @@ CASES = [
 ]
 
 
+TINY_H3 = ("meta.json", "dit_trunk.bin", "dit_globals.bin", "adaln_table.bin", "pos.bin", "x_video.bin",
+           "x_audio.bin", "text_emb.bin", "text_rows.bin", "video_v_step0.bin", "video_v_step7.bin",
+           "audio_v_step0.bin", "audio_v_step7.bin", "video_v_vsa_step0.bin", "video_v_vsa_step7.bin",
+           "audio_v_vsa_step0.bin", "audio_v_vsa_step7.bin")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -61,6 +70,9 @@ def main() -> None:
     os.makedirs(os.path.join(HERE, "vsa"), exist_ok=True)
     for name in ("vsa_n784.bin", "vsa_padded.bin", "vsa_sparsity0.bin"):
         shutil.copyfile(os.path.join(args.ref, "tests", "fixtures", "vsa", name), os.path.join(HERE, "vsa", name))
+    os.makedirs(os.path.join(HERE, "tiny_h3"), exist_ok=True)
+    for name in TINY_H3:
+        shutil.copyfile(os.path.join(args.ref, "tests", "fixtures", "tiny_h3", name), os.path.join(HERE, "tiny_h3", name))
     build()
     o = Oracle()
     r = Reference()

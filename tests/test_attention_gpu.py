@@ -101,3 +101,24 @@ def test_rejects_bad_arguments(fh3):
         fh3.attention(x, x, x, 4, head_dim=64)        # only head_dim 128
     with pytest.raises(fh3.Fh3CudaError):
         fh3.attention(x[:, 1:], x, x, 1)              # misaligned view
+
+
+# ---- fp32 operands (fh3cuda_attention_f32_dev): the CPU path's accuracy ----
+TOL_F32 = 1e-5
+
+
+def test_f32_reference_case(fh3, golden_cases):
+    n, H, D = (int(v) for v in golden_cases["attn/dims"])
+    q, k, v = (golden_cases[f"attn/{x}"] for x in "qkv")
+    dev = lambda a: __import__("torch").from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+    got = fh3.attention(dev(q), dev(k), dev(v), H, D).cpu().numpy()
+    assert rel_fro(got, golden_cases["attn/y"]) <= TOL_F32
+
+
+@pytest.mark.parametrize("n,H,D", [(1, 1, 128), (18, 2, 128), (65, 3, 64), (130, 2, 256), (40, 1, 32)])
+def test_f32_vs_oracle(fh3, oracle, n, H, D):
+    import torch
+    rng = np.random.default_rng(n * 7 + D)
+    q, k, v = (rng.standard_normal((n, H * D)).astype(np.float32) for _ in range(3))
+    got = fh3.attention(*(torch.from_numpy(a).cuda() for a in (q, k, v)), H, D).cpu().numpy()
+    assert rel_fro(got, oracle.attention(q, k, v, H, D)) <= TOL_F32

@@ -1,13 +1,13 @@
 """Video sparse attention (fh3_vsa_attention, src/core/fh3_vsa.c:186-507) on the GPU.
 
-Two bars:
+Three bars:
 * the tile stage (tile means, tile scores, kept key tiles) is computed in fp32 in the
   reference's order, so the scores and the 0/1 tile mask equal the oracle's BIT FOR BIT
   (the oracle equals the reference's compiled function, tests/test_vsa_oracle.py);
-* the fine pass runs on bf16 operands with fp32 softmax and accumulation, so the output
-  is compared with fp32 computations at relative L2 (Frobenius) error <= 1e-2 on the
-  same bf16-rounded inputs, and <= 2e-2 against the reference's fp32-input fixtures
-  (the reference's own test asks 1e-5 of an fp32 CPU path, tests/unit/test_vsa.c:175).
+* fp32 operands run the fine pass in fp32: the output meets the reference's own bar,
+  relative L2 error <= 1e-5 against its fixtures (tests/unit/test_vsa.c:175);
+* bf16 operands run it on tensor cores with fp32 softmax and accumulation: relative L2
+  (Frobenius) error <= 1e-2 against fp32 attention on the same bf16-rounded inputs.
 """
 from __future__ import annotations
 
@@ -17,7 +17,8 @@ import pytest
 from conftest import VSA_CASES, VSA_FIXTURES, read_vsa_golden, rel_l2, vsa_case
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-2
+TOL = 1e-2      # bf16 operands
+TOL_F32 = 1e-5  # fp32 operands, the reference's bar
 
 
 def _dev(a, bf16=False):
@@ -40,14 +41,24 @@ def test_tile_mask_bitwise_equals_oracle_on_fixture(fh3, oracle, name):
 
 
 @pytest.mark.parametrize("name", VSA_FIXTURES)
-def test_output_vs_reference_fixture(fh3, oracle, name):
+def test_fp32_output_matches_reference_fixture(fh3, name):
     seq, heads, hd, sp, q, k, v, gate, ref = read_vsa_golden(name)
     got = _np(fh3.vsa_attention(_dev(q), _dev(k), _dev(v), None if gate is None else _dev(gate), seq, heads, hd,
                                 64, sp))
-    assert rel_l2(got, ref) <= 2 * TOL
-    # against fp32 attention on the bf16-rounded q/k/v the fine pass used (gate kept fp32)
-    r = lambda a: _np(_dev(a, True))
-    same = oracle.vsa(r(q), r(k), r(v), gate, seq, heads, hd, 64, sp)
+    assert rel_l2(got, ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("name", VSA_FIXTURES)
+def test_bf16_output_vs_oracle_on_fixture(fh3, oracle, name):
+    """The fixture's q/k/v/gate rounded to bf16: tensor-core fine pass against fp32 VSA on the
+    same rounded values; the mask must still be the oracle's."""
+    seq, heads, hd, sp, q, k, v, gate, _ = read_vsa_golden(name)
+    qb, kb, vb, gb = (_dev(a, True) for a in (q, k, v, gate))
+    got = _np(fh3.vsa_attention(qb, kb, vb, gb, seq, heads, hd, 64, sp))
+    same, sc_ref, mk_ref = oracle.vsa(_np(qb), _np(kb), _np(vb), _np(gb), seq, heads, hd, 64, sp, want_tiles=True)
+    sc, mk = fh3.vsa_tiles(qb, kb, seq, heads, hd, 64, sp)
+    np.testing.assert_array_equal(sc.cpu().numpy(), sc_ref)
+    np.testing.assert_array_equal(mk.cpu().numpy(), mk_ref)
     assert rel_l2(got, same) <= TOL
 
 
@@ -62,7 +73,7 @@ def test_reference_cases(fh3, oracle, golden_cases, name):
     np.testing.assert_array_equal(mk.cpu().numpy(), mk_ref)
     got = _np(fh3.vsa_attention(_dev(q), _dev(k), _dev(v), None if gate is None else _dev(gate), seq, heads, hd,
                                 tile, sp))
-    assert rel_l2(got, y) <= 2 * TOL
+    assert rel_l2(got, y) <= TOL_F32
 
 
 @pytest.mark.parametrize("hd,out_bf16", [(128, False), (128, True), (64, True)])
@@ -133,6 +144,10 @@ def test_rejects_bad_arguments(fh3):
         fh3.vsa_attention(x, x, x, None, seq, 1, 96)           # head_dim 96
     with pytest.raises(Fh3CudaError):
         fh3.vsa_attention(x, x, x, None, (0, 0, 0, 0, 1, 1, 1), 1, 64)   # empty sequence
-    y = torch.zeros((64, 130), device="cuda")
+    xb = torch.zeros((64, 64), device="cuda", dtype=torch.bfloat16)
+    y = torch.zeros((64, 130), device="cuda", dtype=torch.bfloat16)
     with pytest.raises(Fh3CudaError):
-        fh3.vsa_attention(x, x, x, None, seq, 1, 64, out=y[:, 1:65])   # o not 16-byte aligned
+        fh3.vsa_attention(xb, xb, xb, None, seq, 1, 64, out=y[:, 1:65])   # bf16: o not 16-byte aligned
+    x64 = torch.zeros((64, 64), device="cuda")
+    with pytest.raises(Fh3CudaError):
+        fh3.vsa_attention(x64, x64, x64, None, seq, 1, 64, out=y[:, :64])  # fp32 operands need an fp32 o
