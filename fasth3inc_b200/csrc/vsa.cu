@@ -355,12 +355,27 @@ __device__ __forceinline__ void load_rows(uint32_t tile, const __nv_bfloat16* __
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// the same with the tokens listed in shared memory
+template <int HD>
+__device__ __forceinline__ void load_rows_smem(uint32_t tile, const __nv_bfloat16* __restrict__ base, int64_t ld,
+                                               int h, const int* toks, int rows) {
+    constexpr int CH = HD / 8;
+    for (int idx = threadIdx.x; idx < kKeys * CH; idx += blockDim.x) {
+        const int r = idx / CH, c = idx % CH;
+        const bool ok = r < rows;
+        const int64_t t = ok ? toks[r] : 0;
+        cp_async16_zfill(tile + swz<HD>(r, c), base + t * ld + h * HD + c * 8, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 constexpr int kFineWarps = 4;  // 64 query rows a CTA
 
 // Fine pass (src/core/fh3_vsa.c:372-432) and the combination with the coarse term
 // (:476-487).  grid (tiles * qsplit, heads): CTA (i, sub) owns rows 64*sub.. of query
-// tile i and walks the key tiles kept for (h, i) in 64-key chunks, the next chunk's
-// K and V in flight while this one is used.  Dynamic shared memory: Q + 2 x (K, V).
+// tile i and walks the keys of the tiles kept for (h, i), packed into 64-key chunks
+// across tile boundaries, the next chunk's K and V in flight while this one is used.
+// Dynamic shared memory: Q + 2 x (K, V).
 template <int HD, bool OUT_BF16>
 __global__ void __launch_bounds__(kFineWarps * 32, 2) vsa_fine_kernel(
     const int* __restrict__ perm, const int* __restrict__ toff, const int* __restrict__ sel,
@@ -384,52 +399,91 @@ __global__ void __launch_bounds__(kFineWarps * 32, 2) vsa_fine_kernel(
     const int* lst = sel + row * nt;
     const int L = selcnt[row];  // >= 1
 
-    // key chunks: (position l in the kept list, chunk c of that tile)
-    auto chunk_rows = [&](int l, int c, const int*& toks) {
-        const int j = lst[l], o0 = toff[j];
-        toks = perm + o0 + c * kKeys;
-        return min(kKeys, toff[j + 1] - o0 - c * kKeys);
-    };
-    auto advance = [&](int& l, int& c) {
-        const int j = lst[l];
-        if (++c * kKeys >= toff[j + 1] - toff[j]) {
-            ++l;
-            c = 0;
+    // The kept key tiles' tokens, concatenated, are cut into chunks of 64 keys (only the
+    // last one partial).  Warp 0 lists chunk t's tokens in s_tok[t % 3] two chunks ahead;
+    // s_cnt holds how many of the 64 slots are filled (0: no chunk).
+    __shared__ int s_tok[3][kKeys];
+    __shared__ int s_cnt[3];
+    int cl = 0, cr = 0;  // warp 0: next key = token cr of kept tile cl
+    auto fill = [&](int buf) {  // warp 0 only
+        int filled = 0;
+        while (filled < kKeys && cl < L) {  // warp-uniform; one pass unless tiles are tiny
+            const int e = cl + lane;
+            int cnt = 0, off = 0;
+            if (e < L) {
+                const int j = lst[e];
+                off = toff[j];
+                cnt = toff[j + 1] - off;
+            }
+            if (lane == 0) {
+                off += cr;
+                cnt -= cr;
+            }
+            int incl = cnt;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, d);
+                if (lane >= d) incl += y;
+            }
+            const int take = min(kKeys - filled, __shfl_sync(0xffffffffu, incl, 31));
+            const int excl = incl - cnt;
+            for (int kk = 0; kk < 32; ++kk) {  // the entries this chunk reaches, in order
+                const int ek = __shfl_sync(0xffffffffu, excl, kk);
+                if (ek >= take) break;
+                const int ck = __shfl_sync(0xffffffffu, cnt, kk), ok = __shfl_sync(0xffffffffu, off, kk);
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int pslot = lane + 32 * half;
+                    if (pslot >= ek && pslot < ek + ck && pslot < take) s_tok[buf][filled + pslot] = perm[ok + pslot - ek];
+                }
+            }
+            // entries used up (the scan is monotone), and where the next chunk starts
+            const int used = __popc(__ballot_sync(0xffffffffu, incl <= take));
+            if (used == 32) {
+                cl = min(cl + 32, L);
+                cr = 0;
+            } else {
+                const int ex = __shfl_sync(0xffffffffu, excl, used);
+                cr = (used == 0 ? cr : 0) + take - ex;
+                cl = min(cl + used, L);
+            }
+            filled += take;
         }
+        if (lane == 0) s_cnt[buf] = filled;
     };
 
+    if (warp == 0) {
+        fill(0);
+        fill(1);
+    }
     load_rows<HD>(sQ, q, ldq, h, perm + qoff, qrows);
-    int l = 0, c = 0;
-    const int* toks;
-    int rows = chunk_rows(0, 0, toks);
-    load_rows<HD>(sK[0], k, ldk, h, toks, rows);
-    load_rows<HD>(sV[0], v, ldv, h, toks, rows);
+    __syncthreads();
+    load_rows_smem<HD>(sK[0], k, ldk, h, s_tok[0], s_cnt[0]);
+    load_rows_smem<HD>(sV[0], v, ldv, h, s_tok[0], s_cnt[0]);
 
+    // warps whose 16 query rows all lie past the tile's end skip the arithmetic
+    const bool busy = warp * 16 < qrows;
     WarpFlash<HD> wf;
     wf.init();
     for (int t = 0;; ++t) {
-        const int st = t & 1;
-        int ln = l, cn = c;
-        advance(ln, cn);
-        const bool more = ln < L;
-        int nrows = 0;
+        const int st = t & 1, nb = (t + 1) % 3;
+        const int rows = s_cnt[t % 3], nrows = s_cnt[nb];
+        const bool more = nrows > 0;
         if (more) {
-            const int* ntoks;
-            nrows = chunk_rows(ln, cn, ntoks);
-            load_rows<HD>(sK[st ^ 1], k, ldk, h, ntoks, nrows);
-            load_rows<HD>(sV[st ^ 1], v, ldv, h, ntoks, nrows);
+            load_rows_smem<HD>(sK[st ^ 1], k, ldk, h, s_tok[nb], nrows);
+            load_rows_smem<HD>(sV[st ^ 1], v, ldv, h, s_tok[nb], nrows);
             asm volatile("cp.async.wait_group 2;" ::: "memory");  // all but the two newest groups
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        if (t == 0) wf.load_q(sQ, warp * 16, lane);
-        wf.step(sK[st], sV[st], rows, scale_log2, lane);
+        if (busy) {
+            if (t == 0) wf.load_q(sQ, warp * 16, lane);
+            wf.step(sK[st], sV[st], rows, scale_log2, lane);
+        }
+        if (warp == 0 && more) fill((t + 2) % 3);  // chunk t+2
         __syncthreads();  // the next iteration's prefetch overwrites this stage
         if (!more) break;
-        l = ln;
-        c = cn;
-        rows = nrows;
     }
 
     float i0, i1;
