@@ -125,12 +125,20 @@ __device__ __forceinline__ void dequant_row_stage(const uint8_t* raw, const uint
         const uint32_t wa = qw[2 * (j & 3)], wb = qw[2 * (j & 3) + 1];
         const uint32_t va = ((hh ? (wa >> 4) : wa) & 0x0F0F0F0Fu) | 0x80808080u;
         const uint32_t vb = ((hh ? (wb >> 4) : wb) & 0x0F0F0F0Fu) | 0x80808080u;
-        const float sj = s[hh], nj = nm[hh];
+        // two weights per packed fp32x2 subtract and FMA: (1 + q/128) - 1 = q/128 exact, then
+        // one rounding of s * q/128 + nm, the same fp32 weight as the scalar form
+        const uint64_t s2 = fh3::f2_pack(s[hh], s[hh]), n2 = fh3::f2_pack(nm[hh], nm[hh]);
+        const uint64_t one2 = fh3::f2_pack(-1.0f, -1.0f);
+        auto w2 = [&](uint32_t v, uint32_t sel_a, uint32_t sel_b) {
+            const uint64_t nb = fh3::f2_pack(fh3::nib_f(v, sel_a), fh3::nib_f(v, sel_b));
+            const float2 w = fh3::f2_unpack(fh3::f2_fma(s2, fh3::f2_add(nb, one2), n2));
+            return pack_bf16(w.x, w.y);
+        };
         uint4 pk;
-        pk.x = pack_bf16(fmaf(sj, fh3::nib_f(va, fh3::kSel0) - 1.0f, nj), fmaf(sj, fh3::nib_f(va, fh3::kSel1) - 1.0f, nj));
-        pk.y = pack_bf16(fmaf(sj, fh3::nib_f(va, fh3::kSel2) - 1.0f, nj), fmaf(sj, fh3::nib_f(va, fh3::kSel3) - 1.0f, nj));
-        pk.z = pack_bf16(fmaf(sj, fh3::nib_f(vb, fh3::kSel0) - 1.0f, nj), fmaf(sj, fh3::nib_f(vb, fh3::kSel1) - 1.0f, nj));
-        pk.w = pack_bf16(fmaf(sj, fh3::nib_f(vb, fh3::kSel2) - 1.0f, nj), fmaf(sj, fh3::nib_f(vb, fh3::kSel3) - 1.0f, nj));
+        pk.x = w2(va, fh3::kSel0, fh3::kSel1);
+        pk.y = w2(va, fh3::kSel2, fh3::kSel3);
+        pk.z = w2(vb, fh3::kSel0, fh3::kSel1);
+        pk.w = w2(vb, fh3::kSel2, fh3::kSel3);
         // 16-byte chunk j of this 128-byte row, XOR-swizzled by row % 8
         *reinterpret_cast<uint4*>(brow + ((static_cast<uint32_t>(j) ^ swz) << 4)) = pk;
     }
