@@ -28,10 +28,10 @@ sys.path.insert(0, ROOT)
 METRIC = "Q4_K DiT step ms & dequant-GEMM TFLOP/s (GEMV GB/s) at 1/2/4/8 B200 vs host CPU"
 UNIT = "TFLOP/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram__bytes_read.sum + dram__bytes_write.sum per FLOP of one gemm_q4k_pair_kernel fc1 launch
-# (8192 rows: 531.7 MB for 2.319 TFLOP, profiles/gemm_q4k_pair_fc1_m8192.md), scaled to the
-# bench's fc1 launch at this rank's rows.
-GEMM_TRAFFIC_BYTES_PER_FLOP = 531.7e6 / 2.319e12
+# dram__bytes_read.sum + dram__bytes_write.sum per FLOP of one gemm_bf16_pair_kernel fc1 launch
+# (8192 rows: 1324.5 + 219.5 MB for 2.319 TFLOP, profiles/gemm_bf16_pair_fc1_m8192.md), scaled to
+# the bench's fc1 launch at this rank's rows.
+GEMM_TRAFFIC_BYTES_PER_FLOP = (1324.5e6 + 219.5e6) / 2.319e12
 
 
 def parse():
@@ -314,8 +314,10 @@ def run_ours(args):
             traffic = int(GEMM_TRAFFIC_BYTES_PER_FLOP * 2 * m_loc * D_MODEL * 2 * FFN)
         roof = {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(gemm_tflops / peak, 4), "traffic": traffic,
-                "traffic_note": "bytes of one fc1 launch at this rank's rows, scaled from an 8192-row ncu capture",
-                "kernel": "gemm_q4k_pair_kernel", "peak_source": f"{src} bf16_tflops_sustained",
+                "traffic_note": "DRAM bytes of one fc1 gemm_bf16_pair_kernel launch at this rank's rows, scaled "
+                                "from an 8192-row ncu capture; the GEMM time includes each call's Q4_K -> bf16 "
+                                "pass (dequant_q4k_bf16_kernel)",
+                "kernel": "gemm_bf16_pair_kernel", "peak_source": f"{src} bf16_tflops_sustained",
                 "gemm_share_of_step": round(float(mx[1]) / (ms * args.steps), 4)}
     if rank == 0:
         line = {

@@ -36,7 +36,7 @@ EXPORTED = [
     "fh3cuda_vsa_tiles_dev", "fh3cuda_attention_f32_dev", "fh3cuda_pack_open", "fh3cuda_pack_num_layers",
     "fh3cuda_pack_device_bytes", "fh3cuda_pack_layer", "fh3cuda_pack_close", "fh3cuda_adaln_open",
     "fh3cuda_adaln_dims", "fh3cuda_adaln_row", "fh3cuda_adaln_close", "fh3cuda_dit_prepare_text_dev",
-    "fh3cuda_dit_forward_dev",
+    "fh3cuda_dit_forward_dev", "fh3cuda_gemm_launches",
 ]
 
 
@@ -150,6 +150,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
                                                  vp, c_int, vp, vp]),
         "fh3cuda_dit_forward_dev": (c_int, [ctypes.POINTER(Fh3CudaDitCfg), ctypes.POINTER(Fh3CudaDitGlobals), vp, vp,
                                             ctypes.POINTER(Fh3CudaSeq), vp, vp, c_int, vp, vp, vp, vp, vp, vp]),
+        "fh3cuda_gemm_launches": (c_int, [i64]),
         "fh3cuda_attention_f32_dev": (c_int, [vp, i64, vp, i64, vp, i64, vp, i64, c_int, c_int, c_int, vp]),
         "fh3cuda_vsa_num_tiles": (c_int, [ctypes.POINTER(Fh3CudaSeq), c_int, ctypes.POINTER(c_int),
                                           ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),

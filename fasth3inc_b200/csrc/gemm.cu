@@ -34,6 +34,7 @@
 // No TMA multicast anywhere.  Every mbarrier wait is bounded (common.cuh); on a
 // timeout the kernel flags FH3CUDA_E_TIMEOUT, drains its own copies/MMAs, frees
 // TMEM and returns.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -701,18 +702,218 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
     }
 }
 
+// =============================================================================
+// Two-pass large-M path.  Above kTwoPassRows token rows each weight tile would be
+// dequantised once per 256-row M tile by the fused kernels (132 times a call at the
+// DiT's 33,784 rows); instead dequant_q4k_bf16_kernel expands the call's weights once
+// into a bf16 [N][K] matrix (the same bf16 values the fused dequantisers produce:
+// fh3's fp32 weight rounded once), and gemm_bf16_pair_kernel runs the pair tile walk
+// with both operands loaded by TMA (128-byte swizzle) -- no dequantiser warps, the
+// tensor pipe fed at TMA rate.  MMA shapes and k order equal the fused kernel's, so
+// the two paths give the same results.
+// =============================================================================
+constexpr int64_t kTwoPassRows = 4096;
+
+// one thread per (weight row, K-64 stage): 64 weights into 128 contiguous bytes
+__global__ void dequant_q4k_bf16_kernel(const uint8_t* __restrict__ w, size_t rb, int64_t N, int K,
+                                        __nv_bfloat16* __restrict__ out) {
+    const int stages = K / BK;
+    const int64_t total = N * stages;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t n = idx / stages;
+        const int st = static_cast<int>(idx - n * stages);
+        const uint8_t* raw = w + n * rb + static_cast<size_t>(st >> 2) * fh3::kQ4KBytes;
+        const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
+        dequant_row_stage<0, 8>(raw, hdr, st & 3, reinterpret_cast<uint8_t*>(out + n * K + st * BK), 0u);
+    }
+}
+
+namespace bfp {
+constexpr int BN = 256;
+constexpr int S = 6;                     // stages of (A, B) halves
+constexpr int B_BYTES = 128 * BK * 2;    // this CTA's 128 weight rows
+constexpr int STAGE = A_BYTES + B_BYTES; // 32 KB
+constexpr int OFF_BAR = S * STAGE;
+constexpr int kNumBars = 2 * S + 4 + 1;
+constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+constexpr int kThreads = 32 * (kEpiWarp0 + kNumEpiWarps);  // producer, MMA, 4 epilogue warps
+static_assert(STAGE % 1024 == 0 && SMEM_BYTES <= 232448, "shared memory layout");
+}  // namespace bfp
+
+__global__ void __launch_bounds__(bfp::kThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const Params p) {
+    using namespace bfp;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* full = bars;               // leader: 1 arrival + both CTAs' A and B bytes
+    uint64_t* empty = full + S;          // both: 1 (leader's commit)
+    uint64_t* acc_full = empty + S;      // both: 1 (leader's commit)
+    uint64_t* acc_empty = acc_full + 2;  // leader: 2 x kNumEpiWarps
+    uint64_t* drain = acc_empty + 2;     // both: 1 (leader's commit)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t cr = fh3::cluster_ctarank();
+    const bool leader = cr == 0;
+    const bool swiglu = p.epi == FH3CUDA_EPI_SWIGLU;
+    const int64_t num_m = (p.M + 255) / 256;
+    const int64_t num_n = swiglu ? (p.n_out + 127) / 128 : (p.N + BN - 1) / BN;
+    const int64_t num_tiles = num_m * num_n;
+    const int ksteps = static_cast<int>(p.K / BK);
+    const int64_t pair = blockIdx.x >> 1;
+    const int64_t npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            fh3::mbar_init(&full[i], 1);
+            fh3::mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            fh3::mbar_init(&acc_full[i], 1);
+            fh3::mbar_init(&acc_empty[i], 2 * kNumEpiWarps);
+        }
+        fh3::mbar_init(drain, 1);
+        *abort_flag = 0;
+        fh3::fence_mbar_init();
+    }
+    if (warp == 1) {
+        fh3::tmem_alloc_pair(tmem_slot, kTmemCols);
+        fh3::tmem_relinquish_pair();
+    }
+    if (warp == 0 && lane == 0) {
+        fh3::tma_prefetch_desc(&tmA);
+        fh3::tma_prefetch_desc(&tmB);
+    }
+    fh3::tc_fence_before();
+    fh3::cluster_sync_all();
+    fh3::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ A and B producer (both CTAs)
+        if (lane == 0) {
+            Ring r;
+            uint32_t filled = 0, par = 0;
+            bool ok = true;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                int64_t mb, nb;
+                tile_coords(tile, num_m, num_n, mb, nb);
+                const int m0 = static_cast<int>(mb * 256 + cr * 128);
+                const int wrow = swiglu ? static_cast<int>(cr ? p.n_out + nb * 128 : nb * 128)
+                                        : static_cast<int>(nb * BN + cr * 128);
+                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                    if (!(ok = fh3::mbar_wait(&empty[r.idx], r.phase ^ 1u, abort_flag, p.status))) break;
+                    // both CTAs' A and B bytes are counted on the leader's full barrier
+                    if (leader) fh3::mbar_arrive_expect_tx(&full[r.idx], 2 * STAGE);
+                    const uint32_t bar = fh3::mapa_shared(fh3::smem_u32(&full[r.idx]), 0);
+                    uint8_t* st = smem + r.idx * STAGE;
+                    fh3::tma_load_2d_pair(st, &tmA, bar, ks * BK, m0);
+                    fh3::tma_load_2d_pair(st + A_BYTES, &tmB, bar, ks * BK, wrow);
+                    filled |= 1u << r.idx;
+                    par = (par & ~(1u << r.idx)) | (r.phase << r.idx);
+                    r.next<S>();
+                }
+            }
+            if (!ok) {
+                volatile int no_abort = 0;
+                if (leader)
+                    for (int i = 0; i < S; ++i)
+                        if (filled & (1u << i)) fh3::mbar_wait_cluster(&full[i], (par >> i) & 1u, &no_abort, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (leader)
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = fh3::idesc_bf16_f32(256, BN);
+            Ring r, racc;
+            bool ok = true;
+            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+                if (!(ok = fh3::mbar_wait(&acc_empty[racc.idx], racc.phase ^ 1u, abort_flag, p.status))) break;
+                fh3::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(racc.idx * BN);
+                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                    if (!(ok = fh3::mbar_wait(&full[r.idx], r.phase, abort_flag, p.status))) break;
+                    fh3::tc_fence_after();
+                    const uint64_t ad = fh3::sdesc_sw128(fh3::smem_u32(smem + r.idx * STAGE));
+                    const uint64_t bd = fh3::sdesc_sw128(fh3::smem_u32(smem + r.idx * STAGE + A_BYTES));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        fh3::umma_f16_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0 ? 1u : 0u);
+                    fh3::umma_commit_pair(&empty[r.idx], 0x3);
+                    r.next<S>();
+                }
+                if (ok) fh3::umma_commit_pair(&acc_full[racc.idx], 0x3);
+                racc.next<2>();
+            }
+            fh3::umma_commit_pair(drain, 0x3);
+        }
+        if (lane == 0) {
+            volatile int no_abort = 0;
+            fh3::mbar_wait_cluster(drain, 0, &no_abort, nullptr);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int q = warp & 3;
+        const uint32_t acc_empty_leader = fh3::mapa_shared(fh3::smem_u32(acc_empty), 0);
+        Ring racc;
+        for (int64_t tile = pair; tile < num_tiles; tile += npairs) {
+            int64_t mb, nb;
+            tile_coords(tile, num_m, num_n, mb, nb);
+            int ok = 1;
+            if (lane == 0) ok = fh3::mbar_wait(&acc_full[racc.idx], racc.phase, abort_flag, p.status);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            fh3::tc_fence_after();
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(racc.idx * BN);
+            epilogue_tile(p, tbase, mb * 256 + cr * 128 + q * 32 + lane, nb);
+            fh3::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (leader) fh3::mbar_arrive(&acc_empty[racc.idx]);
+                else fh3::mbar_arrive_remote(acc_empty_leader + 8u * racc.idx);
+            }
+            racc.next<2>();
+        }
+    }
+
+    fh3::tc_fence_before();
+    __syncthreads();
+    fh3::cluster_sync_all();  // the peer is done with our barriers and the pair's MMAs have retired
+    if (warp == 1) {
+        fh3::tc_fence_after();
+        fh3::tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+}
+
 std::once_flag g_attr_once;
 cudaError_t g_attr_err = cudaSuccess;
 int g_pair_clusters = 0;  // co-resident CTA pairs on device 0's layout (queried once)
+int g_bf_clusters = 0;    // the same for gemm_bf16_pair_kernel
 
 bool use_pair_kernel(int64_t n_tok) {
     const char* e = getenv("FH3CUDA_GEMM_KERNEL");
     if (e && strcmp(e, "1sm") == 0) return false;
-    if (e && strcmp(e, "2sm") == 0) return true;
+    if (e && (strcmp(e, "2sm") == 0 || strcmp(e, "two-pass") == 0)) return true;
     return n_tok > 128;
 }
 
 }  // namespace
+
+// kernel launches one fh3cuda_gemm_q4k_dev call of n_tok rows makes (the two-pass path
+// adds the dequantisation pass); the same rule as the dispatch below
+extern "C" int fh3cuda_gemm_launches(int64_t n_tok) {
+    const char* gk = getenv("FH3CUDA_GEMM_KERNEL");
+    const bool force_fused = gk && (strcmp(gk, "2sm") == 0 || strcmp(gk, "1sm") == 0);
+    const bool force_two = gk && strcmp(gk, "two-pass") == 0;
+    const bool two = use_pair_kernel(n_tok) && !force_fused && (force_two || n_tok >= kTwoPassRows);
+    return two ? 2 : 1;
+}
 
 extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y,
                                     int64_t ldy, int64_t n_tok, const float* bias, const float* gate,
@@ -758,6 +959,14 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
             cfg.attrs = at;
             cfg.numAttrs = 1;
             g_attr_err = cudaOccupancyMaxActiveClusters(&g_pair_clusters, gemm_q4k_pair_kernel, &cfg);
+            if (g_attr_err == cudaSuccess)
+                g_attr_err = cudaFuncSetAttribute(gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  bfp::SMEM_BYTES);
+            if (g_attr_err == cudaSuccess) {
+                cfg.blockDim = dim3(bfp::kThreads, 1, 1);
+                cfg.dynamicSmemBytes = bfp::SMEM_BYTES;
+                g_attr_err = cudaOccupancyMaxActiveClusters(&g_bf_clusters, gemm_bf16_pair_kernel, &cfg);
+            }
         }
     });
     if (g_attr_err != cudaSuccess) return check_cuda(g_attr_err, "gemm kernel attributes");
@@ -783,6 +992,32 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
                                   gstr, box, es, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(W) failed: %d", (int)r);
     }
+    // large M: dequantise the weights once to bf16, then the TMA-fed bf16 pair kernel;
+    // FH3CUDA_GEMM_KERNEL=2sm / 1sm force the fused kernels, =two-pass this path
+    const char* gk = getenv("FH3CUDA_GEMM_KERNEL");
+    const bool force_fused = gk && (strcmp(gk, "2sm") == 0 || strcmp(gk, "1sm") == 0);
+    const bool force_two = gk && strcmp(gk, "two-pass") == 0;
+    const bool two_pass = pair && g_bf_clusters > 0 && !force_fused && (force_two || n_tok >= kTwoPassRows);
+    __nv_bfloat16* wb = nullptr;
+    CUtensorMap tmB;
+    if (two_pass) {
+        const int64_t N = w->out, K = w->in;
+        wb = static_cast<__nv_bfloat16*>(scratch(c, 11, static_cast<size_t>(N) * K * 2, static_cast<cudaStream_t>(stream)));
+        if (!wb) return FH3_E_NOMEM;
+        const int64_t work = N * (K / BK);
+        const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 16));
+        dequant_q4k_bf16_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(w->data, rb, N,
+                                                                                          static_cast<int>(K), wb);
+        int rc = check_cuda(cudaGetLastError(), "dequant_q4k_bf16_kernel launch");
+        if (rc) return rc;
+        const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+        const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(K) * 2};
+        const cuuint32_t box[2] = {BK, 128};
+        const cuuint32_t es[2] = {1, 1};
+        CUresult r = encode_tiled(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wb, gdim, gstr, box, es,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+        if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(B) failed: %d", (int)r);
+    }
     Params p;
     p.M = n_tok;
     p.N = w->out;
@@ -798,7 +1033,8 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
     const int64_t num_n = epi == FH3CUDA_EPI_SWIGLU ? (n_out + 127) / 128 : (w->out + 255) / 256;
     if (pair) {
         const int64_t tiles = ((n_tok + 255) / 256) * num_n;
-        const int64_t pairs = tiles < g_pair_clusters ? tiles : g_pair_clusters;
+        const int64_t avail = two_pass ? g_bf_clusters : g_pair_clusters;
+        const int64_t pairs = tiles < avail ? tiles : avail;
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute at[1];
         at[0].id = cudaLaunchAttributeClusterDimension;
@@ -806,11 +1042,13 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
         at[0].val.clusterDim.y = 1;
         at[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-        cfg.blockDim = dim3(kThreadsPair, 1, 1);
-        cfg.dynamicSmemBytes = two::SMEM_BYTES;
+        cfg.blockDim = dim3(two_pass ? bfp::kThreads : kThreadsPair, 1, 1);
+        cfg.dynamicSmemBytes = two_pass ? bfp::SMEM_BYTES : two::SMEM_BYTES;
         cfg.stream = s;
         cfg.attrs = at;
         cfg.numAttrs = 1;
+        if (two_pass)
+            return check_cuda(cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel, tmA, tmB, p), "gemm_bf16_pair_kernel launch");
         return check_cuda(cudaLaunchKernelEx(&cfg, gemm_q4k_pair_kernel, tmA, tmW, p), "gemm_q4k_pair_kernel launch");
     }
     const int64_t tiles = ((n_tok + 127) / 128) * num_n;

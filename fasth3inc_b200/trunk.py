@@ -152,7 +152,7 @@ class Runner:
         if rec:
             e1.record(self.stream)
             self.gemm_events.append((e0, e1, 2 * rows * w.in_ * w.out))
-        self.launches += 1
+        self.launches += self.L.fh3cuda_gemm_launches(rows)
 
     def _norm(self, h, shift, scale, out):
         check(self.L.fh3cuda_rmsnorm_modulate_dev(h.data_ptr(), None, shift.data_ptr(), scale.data_ptr(),

@@ -17,10 +17,11 @@ Q4K = 12
 TOL = 5e-3
 
 
-@pytest.fixture(autouse=True, params=["2sm", "1sm"])
+@pytest.fixture(autouse=True, params=["2sm", "1sm", "two-pass"])
 def gemm_kernel(request, monkeypatch):
-    """Run every test on both GEMM kernels: the CTA-pair (cta_group::2) kernel that serves
-    M > 128 by default, and the one-SM kernel that serves M <= 128."""
+    """Run every test on every GEMM path: the fused CTA-pair (cta_group::2) kernel that serves
+    128 < M < 4096 by default, the fused one-SM kernel (M <= 128), and the two-pass path of
+    M >= 4096 (weights dequantised to bf16 once per call, then the TMA-fed bf16 pair kernel)."""
     monkeypatch.setenv("FH3CUDA_GEMM_KERNEL", request.param)
     return request.param
 
@@ -148,3 +149,25 @@ def test_rejects_bad_arguments(fh3):
     bad = fh3.Q4KWeight(w.data, 320, 64)
     with pytest.raises(fh3.Fh3CudaError):
         fh3.gemm(bad, torch.zeros((32, 320), dtype=torch.bfloat16, device="cuda"))
+
+
+def test_two_pass_equals_fused_bitwise(fh3, monkeypatch):
+    """Both paths feed the tensor cores the same bf16 weights (fh3's fp32 weight rounded once) in
+    the same shared-memory layout, MMA shape and k order, so their outputs are identical."""
+    import torch
+    N, K, M = 1000, 1280, 4200
+    w = fh3.make_weights(N, K, seed=5, stream_id=2)
+    x = fh3.to_bf16(torch.randn((M, K), device="cuda"))
+    g = torch.randn(N, device="cuda")
+    outs = {}
+    for kern in ("2sm", "two-pass"):
+        monkeypatch.setenv("FH3CUDA_GEMM_KERNEL", kern)
+        y = fh3.gemm(w, x, fh3.EPI_F32)
+        yb = fh3.gemm(w, x, fh3.EPI_BF16)
+        h = torch.ones((M, N), device="cuda")
+        fh3.gemm(w, x, fh3.EPI_RESID, gate=g, out=h)
+        w2 = fh3.make_weights(2 * 512, K, seed=6, stream_id=2)
+        ys = fh3.gemm(w2, x, fh3.EPI_SWIGLU)
+        outs[kern] = (y, yb, h, ys)
+    for a, b in zip(outs["2sm"], outs["two-pass"]):
+        assert torch.equal(a, b)
