@@ -105,8 +105,21 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 // chunks 0-3 come from the low nibbles (sub-block 2*sub), 4-7 from the high nibbles
 // (sub-block 2*sub+1).
 template <int J0, int NJ>
+__device__ __forceinline__ void dequant_row_stage_q(const uint4& hdr, const uint4& q0, const uint4& q1, int sub,
+                                                    uint8_t* brow, uint32_t swz);
+
+template <int J0, int NJ>
 __device__ __forceinline__ void dequant_row_stage(const uint8_t* raw, const uint4& hdr, int sub, uint8_t* brow,
                                                   uint32_t swz) {
+    const uint4 q0 = *reinterpret_cast<const uint4*>(raw + 16 + sub * 32);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(raw + 32 + sub * 32);
+    dequant_row_stage_q<J0, NJ>(hdr, q0, q1, sub, brow, swz);
+}
+
+// the same on the stage's 32 nibble bytes already loaded (q0, q1)
+template <int J0, int NJ>
+__device__ __forceinline__ void dequant_row_stage_q(const uint4& hdr, const uint4& q0, const uint4& q1, int sub,
+                                                    uint8_t* brow, uint32_t swz) {
     const float d = fh3::h2f_bits(hdr.x), dmin = fh3::h2f_bits(hdr.x >> 16);
     float s[2], nm[2];
 #pragma unroll
@@ -117,8 +130,6 @@ __device__ __forceinline__ void dequant_row_stage(const uint8_t* raw, const uint
         s[hh] = __fmul_rn(d, static_cast<float>(sc)) * 128.0f;
         nm[hh] = -__fmul_rn(dmin, static_cast<float>(m));
     }
-    const uint4 q0 = *reinterpret_cast<const uint4*>(raw + 16 + sub * 32);
-    const uint4 q1 = *reinterpret_cast<const uint4*>(raw + 32 + sub * 32);
     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
     for (int j = J0; j < J0 + NJ; ++j) {
@@ -712,20 +723,26 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
 // tensor pipe fed at TMA rate.  MMA shapes and k order equal the fused kernel's, so
 // the two paths give the same results.
 // =============================================================================
-constexpr int64_t kTwoPassRows = 4096;
+constexpr int64_t kTwoPassRows = 2048;
 
-// one thread per (weight row, K-64 stage): 64 weights into 128 contiguous bytes
+// one thread per (weight row, super-block): its 144 bytes in nine 16-byte loads issued
+// together, then 256 weights into 512 contiguous bytes
 __global__ void dequant_q4k_bf16_kernel(const uint8_t* __restrict__ w, size_t rb, int64_t N, int K,
                                         __nv_bfloat16* __restrict__ out) {
-    const int stages = K / BK;
-    const int64_t total = N * stages;
+    const int nblk = K / fh3::kQ4KBlock;
+    const int64_t total = N * nblk;
     for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
          idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t n = idx / stages;
-        const int st = static_cast<int>(idx - n * stages);
-        const uint8_t* raw = w + n * rb + static_cast<size_t>(st >> 2) * fh3::kQ4KBytes;
-        const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
-        dequant_row_stage<0, 8>(raw, hdr, st & 3, reinterpret_cast<uint8_t*>(out + n * K + st * BK), 0u);
+        const int64_t n = idx / nblk;
+        const int b = static_cast<int>(idx - n * nblk);
+        const uint4* raw = reinterpret_cast<const uint4*>(w + n * rb + static_cast<size_t>(b) * fh3::kQ4KBytes);
+        uint4 v[9];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) v[i] = __ldcs(raw + i);  // read once: keep L2 for the GEMM's tiles
+        uint8_t* dst = reinterpret_cast<uint8_t*>(out + n * K + static_cast<int64_t>(b) * fh3::kQ4KBlock);
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub)
+            dequant_row_stage_q<0, 8>(v[0], v[1 + 2 * sub], v[2 + 2 * sub], sub, dst + sub * 128, 0u);
     }
 }
 
@@ -1004,7 +1021,7 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
         const int64_t N = w->out, K = w->in;
         wb = static_cast<__nv_bfloat16*>(scratch(c, 11, static_cast<size_t>(N) * K * 2, static_cast<cudaStream_t>(stream)));
         if (!wb) return FH3_E_NOMEM;
-        const int64_t work = N * (K / BK);
+        const int64_t work = N * (K / fh3::kQ4KBlock);
         const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 16));
         dequant_q4k_bf16_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(w->data, rb, N,
                                                                                           static_cast<int>(K), wb);

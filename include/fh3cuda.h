@@ -183,7 +183,7 @@ FH3CUDA_API int fh3cuda_gemv_q4k_dev(const Fh3CudaW *w, const float *x, float *y
 /* tcgen05 GEMM on bf16 activations: y = epi(x_bf16 . W^T), x_bf16 holding
  * n_tok rows of K = w->in values with row stride ldx elements (ldx >= K, a
  * multiple of 8).  W is Q4_K, dequantised to bf16 in shared memory by the GEMM
- * (fewer than 4096 rows), or from 4096 rows on expanded once per call to a bf16
+ * (fewer than 2048 rows), or from 2048 rows on expanded once per call to a bf16
  * copy in device scratch that a TMA-fed kernel reads (each weight is then
  * dequantised once per call instead of once per 256-row tile; same bf16 values,
  * same results).  ldy is the row stride of y in elements.  gate is used by FH3CUDA_EPI_RESID only.
@@ -193,7 +193,7 @@ FH3CUDA_API int fh3cuda_gemm_q4k_dev(const Fh3CudaW *w, const void *x_bf16, int6
                                      const float *gate, int epilogue, void *stream);
 
 /* Kernel launches one fh3cuda_gemm_q4k_dev call of n_tok rows makes: 1 for the
- * fused kernels, 2 from 4096 rows on, where the weights are first expanded to a
+ * fused kernels, 2 from 2048 rows on, where the weights are first expanded to a
  * bf16 copy (the same bf16 values the fused dequantisers produce) and a TMA-fed
  * bf16 pair kernel runs the tiles.  FH3CUDA_GEMM_KERNEL=2sm / 1sm / two-pass in the
  * environment forces a path. */

@@ -20,8 +20,8 @@ TOL = 5e-3
 @pytest.fixture(autouse=True, params=["2sm", "1sm", "two-pass"])
 def gemm_kernel(request, monkeypatch):
     """Run every test on every GEMM path: the fused CTA-pair (cta_group::2) kernel that serves
-    128 < M < 4096 by default, the fused one-SM kernel (M <= 128), and the two-pass path of
-    M >= 4096 (weights dequantised to bf16 once per call, then the TMA-fed bf16 pair kernel)."""
+    128 < M < 2048 by default, the fused one-SM kernel (M <= 128), and the two-pass path of
+    M >= 2048 (weights dequantised to bf16 once per call, then the TMA-fed bf16 pair kernel)."""
     monkeypatch.setenv("FH3CUDA_GEMM_KERNEL", request.param)
     return request.param
 
