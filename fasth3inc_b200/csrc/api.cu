@@ -16,8 +16,9 @@ namespace fh3host {
 // scratch slots: 0 bf16 activations of the GEMM, 1 staged weights, 2-4 the host
 // drop-in's x / y / bias, 5 GEMV fragments, 6 split-tile partials, 7 tile counters,
 // 8 fp32 weight rows of the non-Q4_K formats, 9 video sparse attention's tile data,
-// 10 the DiT forward's activations, 11 bf16 weights of the two-pass large-M GEMM
-constexpr int kScratchSlots = 12;
+// 10 the DiT forward's activations, 11 bf16 weights of the two-pass large-M GEMM,
+// 12 the transposed V of the tensor-core attention
+constexpr int kScratchSlots = 13;
 
 struct DevCtx {
     int device = -1;

@@ -15,6 +15,9 @@
 //
 // Operands: element (token i, head h, channel d) of q / k / v at
 // base + i*ld + h*128 + d (bf16), o at o + i*ldo + h*128 + d (fp32 or bf16).
+#include <cstdlib>
+#include <cstring>
+
 #include "flash.cuh"
 
 namespace {
@@ -134,6 +137,9 @@ extern "C" int fh3cuda_attention_dev(const void* q, int64_t ldq, const void* k, 
     const auto* qb = static_cast<const __nv_bfloat16*>(q);
     const auto* kb = static_cast<const __nv_bfloat16*>(k);
     const auto* vb = static_cast<const __nv_bfloat16*>(v);
+    // tcgen05 kernel (attention_tc.cu) by default; FH3CUDA_ATTN_KERNEL=mma selects the mma.sync one
+    const char* ak = getenv("FH3CUDA_ATTN_KERNEL");
+    if (!(ak && strcmp(ak, "mma") == 0)) return attention_tc(qb, ldq, kb, ldk, vb, ldv, o, o_bf16 != 0, ldo, n, heads, s);
     if (o_bf16)
         attention_kernel<true><<<grid, kAttnWarps * 32, kAttnSmem, s>>>(qb, ldq, kb, ldk, vb, ldv, o, ldo, n,
                                                                          scale_log2);

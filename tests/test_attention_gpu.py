@@ -1,11 +1,12 @@
 """Dense attention (fh3_attention, src/core/fh3_ops.c:587-695) on the GPU.
 
-The kernel takes bf16 q/k/v (fp32 softmax and accumulation, P rounded to bf16 for the
-second product), so it is compared with fp32 computations on the SAME bf16-rounded inputs:
+The kernels take bf16 q/k/v (fp32 softmax and accumulation, P rounded to bf16 for the
+second product), so they are compared with fp32 computations on the SAME bf16-rounded inputs:
 the oracle (bitwise equal to the reference, tests/test_oracle.py) and torch's fp32
-attention.  Tolerance: relative Frobenius error <= 1e-2 (the bf16 operand bar of the
-chained block test); against the reference's own fp32-input case the input rounding is
-included, tolerance 2e-2."""
+attention.  Two kernels serve bf16 operands: tcgen05 (score and output tiles in tensor
+memory, the default) and mma.sync.  Tolerance: relative Frobenius error <= 1e-2 (the bf16
+operand bar of the chained block test); against the reference's own fp32-input case the
+input rounding is included, tolerance 2e-2.  fp32 operands run in fp32 at 1e-5."""
 from __future__ import annotations
 
 import numpy as np
@@ -15,6 +16,17 @@ from conftest import rel_fro
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
+
+
+@pytest.fixture(autouse=True, params=["tc", "mma"])
+def attn_kernel(request, monkeypatch):
+    """Every bf16 test on both kernels: tcgen05 with TMEM accumulators (the default) and the
+    mma.sync flash kernel (FH3CUDA_ATTN_KERNEL=mma)."""
+    if request.param == "mma":
+        monkeypatch.setenv("FH3CUDA_ATTN_KERNEL", "mma")
+    else:
+        monkeypatch.delenv("FH3CUDA_ATTN_KERNEL", raising=False)
+    return request.param
 
 
 def _bf16(a):
