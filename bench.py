@@ -435,10 +435,11 @@ def measure_attention(fh3, torch, rows: int, peak: float, peak_src: str, reps: i
     flops = 4.0 * rows * rows * H * D
     tf = flops / (ms * 1e-3) / 1e12
     del qkv, o
-    return {"kernel": "attention_kernel", "rows": rows, "heads": H, "head_dim": D, "ms_per_launch": round(ms, 3),
+    return {"kernel": "attention_tc_kernel (+ vt_transpose_kernel)", "rows": rows, "heads": H, "head_dim": D,
+            "ms_per_launch": round(ms, 3),
             "bound": "tensor", "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak, "frac": round(tf / peak, 4),
             "peak_source": f"{peak_src} bf16_tflops", "flop_per_launch": flops,
-            "note": "mma.sync bf16 (legacy tensor path); not part of the GEMM-only step"}
+            "note": "tcgen05, score and output tiles in TMEM; not part of the GEMM-only step"}
 
 
 def vsa_seq(rows: int):

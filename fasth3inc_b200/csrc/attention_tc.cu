@@ -229,15 +229,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
 #pragma unroll
             for (int c = 0; c < 4; ++c) fh3::tmem_ld32(trow + b * 128 + c * 32, v[c]);
             fh3::tmem_ld_wait();
-            float mx = -INFINITY;
+            // row max of the raw scores (the scale is positive); keys past n only in the last tile
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            if (kb + kTcKeys <= n) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 4; ++c)
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const float sv = kb + c * 32 + e < n ? __uint_as_float(v[c][e]) * scale_log2 : -INFINITY;
-                    v[c][e] = __float_as_uint(sv);
-                    mx = fmaxf(mx, sv);
-                }
+                    for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        if (kb + c * 32 + e >= n) v[c][e] = __float_as_uint(-INFINITY);
+                        mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                    }
+            }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
             const bool raise = mx > m_ref + 8.0f;  // always true on the first tile
             if (j > 0 && __any_sync(0xffffffffu, raise)) {
                 // rescale this warp's rows of O once PV_{j-1} has landed (PV_j waits for our P_j)
@@ -259,7 +267,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
             if (raise) m_ref = mx;
             if (!(ok = wait_warp(&B.p_empty[b], ((j >> 1) & 1) ^ 1u))) break;  // P_{j-2} consumed
             uint8_t* pb = smem + OFF_P + b * kTile;
-            float rs = 0.0f;
+            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const float nm = -m_ref;
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -268,9 +277,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int e = 8 * t + 2 * u;
-                        const float p0 = exp2f(__uint_as_float(v[c][e]) - m_ref);
-                        const float p1 = exp2f(__uint_as_float(v[c][e + 1]) - m_ref);
-                        rs += p0 + p1;
+                        const float p0 = exp2f(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
+                        const float p1 = exp2f(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
+                        rs4[u] += p0 + p1;
                         const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                         pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
                     }
@@ -283,7 +292,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
                 fh3::mbar_arrive(&B.s_empty[b]);
                 fh3::mbar_arrive(&B.p_full[b]);
             }
-            l += rs;
+            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
         }
         if (ok) ok = wait_warp(B.o_full, (T - 1) & 1);  // the last PV has landed
         const int row = q0 + r;
