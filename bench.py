@@ -487,13 +487,13 @@ def measure_vsa(fh3, torch, rows: int, peak: float, peak_src: str, reps: int = 3
     ms = e0.elapsed_time(e1) / reps
     tf = flops / (ms * 1e-3) / 1e12
     del qkv, gate, o
-    return {"kernel": "vsa_fine_kernel (+ tile stage and coarse pass in the timed call)", "rows": n,
+    return {"kernel": "vsa_tc_kernel (+ tile stage, tile-order copies and coarse pass in the timed call)", "rows": n,
             "seq": {"audio": seq[2], "video": seq[3], "grid": list(seq[4:])}, "tiles": nt, "heads": H,
             "head_dim": D, "sparsity": 0.8, "ms_per_call": round(ms, 3), "bound": "tensor",
             "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak, "frac": round(tf / peak, 4),
             "peak_source": f"{peak_src} bf16_tflops", "flop_per_call": flops,
             "dense_equivalent_ms": round(4.0 * n * n * H * D / (tf * 1e12) * 1e3, 3),
-            "note": "mma.sync bf16 fine pass; not part of the GEMM-only step"}
+            "note": "tcgen05 fine pass, TMEM score and output tiles; not part of the GEMM-only step"}
 
 
 def run_case(args):

@@ -13,7 +13,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libfh3cuda.so")
 SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemm.cu", "ops.cu", "attention.cu", "attention_tc.cu", "attention_f32.cu",
-           "vsa.cu", "trunk_io.cu", "dit.cu", "gen.cu", "noalloc.cu"]
+           "vsa.cu", "vsa_tc.cu", "trunk_io.cu", "dit.cu", "gen.cu", "noalloc.cu"]
 HEADERS = ["common.cuh", "flash.cuh"]
 
 NVCC_FLAGS = [

@@ -17,8 +17,9 @@ namespace fh3host {
 // drop-in's x / y / bias, 5 GEMV fragments, 6 split-tile partials, 7 tile counters,
 // 8 fp32 weight rows of the non-Q4_K formats, 9 video sparse attention's tile data,
 // 10 the DiT forward's activations, 11 bf16 weights of the two-pass large-M GEMM,
-// 12 the transposed V of the tensor-core attention
-constexpr int kScratchSlots = 13;
+// 12 the transposed V of the tensor-core attention, 13 video sparse attention's tile-order
+// copies of q, k and v
+constexpr int kScratchSlots = 14;
 
 struct DevCtx {
     int device = -1;

@@ -412,6 +412,12 @@ int gemv_fp32(const Fh3CudaW* w, const float* x, float* y, int n_tok, const floa
 // dense attention on tcgen05, head_dim 128 (attention_tc.cu); arguments already validated
 int attention_tc(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, int64_t ldk, const __nv_bfloat16* v,
                  int64_t ldv, void* o, bool o_bf16, int64_t ldo, int n, int heads, cudaStream_t s);
+// video sparse attention's fine pass + coarse * gate on tcgen05 (vsa_tc.cu): tiles of at most
+// 64 tokens, head_dim 128, bf16 operands; the tile-stage arrays come from vsa.cu
+int vsa_fine_tc(const int* perm, const int* toff, const int* sel, const int* selcnt, int nt, int n,
+                const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, int64_t ldk, const __nv_bfloat16* v,
+                int64_t ldv, const __nv_bfloat16* gate, int64_t ldg, const float* outc, int heads, void* o, bool o_bf16,
+                int64_t ldo, cudaStream_t s);
 // fp32 softmax attention (attention_f32.cu): dense over n keys when sel is null, else
 // the fine pass of video sparse attention over the kept key tiles (+ outc * gate)
 int attention_f32_launch(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,

@@ -24,6 +24,8 @@
 // Operands: element (token t, head h, channel d) of q at q[t*ldq + h*head_dim + d]
 // (likewise k, v, gate, o), fp32 or bf16.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <vector>
 
 #include "flash.cuh"
@@ -706,6 +708,12 @@ extern "C" int fh3cuda_vsa_attention_dev(int tile, float sparsity, const Fh3Cuda
     const int64_t lq = ldq, lk = ldk, lv = ldv;
     const int max_rows = std::max(64, g.npre > 0 ? std::min(g.tile, std::max(g.T, g.A)) : 64);
     const int qsplit = (max_rows + kKeys - 1) / kKeys;
+    // tcgen05 fine pass (vsa_tc.cu) for tiles of at most 64 tokens and head_dim 128;
+    // FH3CUDA_VSA_KERNEL=mma selects the mma.sync kernel below
+    const char* vk = getenv("FH3CUDA_VSA_KERNEL");
+    if (head_dim == 128 && qsplit == 1 && !(vk && strcmp(vk, "mma") == 0))
+        return vsa_fine_tc(b.perm, b.toff, b.sel, b.selcnt, nt, g.n, qb, lq, kb, lk, vb, lv,
+                           static_cast<const __nv_bfloat16*>(gate), ldg, b.outc, heads, o, o_bf16 != 0, ldo, s);
     const float scale_log2 = (1.0f / sqrtf(static_cast<float>(head_dim))) * 1.4426950408889634f;
     const dim3 grid(static_cast<unsigned>(nt * qsplit), static_cast<unsigned>(heads));
     const int smem = 5 * kKeys * head_dim * 2;

@@ -1,0 +1,479 @@
+// vsa_tc.cu -- the fine pass of video sparse attention (src/core/fh3_vsa.c:372-432) on
+// the 5th-generation tensor cores, for bf16 operands with head_dim 128 and tiles of at
+// most 64 tokens (the DiT's configuration).
+//
+// Kept key tiles are arbitrary token sets, so each call first lays q, k and v out in
+// tile order: every tile's tokens become one contiguous run, padded to a multiple of 8
+// rows (vsa_padoff_kernel, vsa_pidx_kernel), q and k rows are gathered into Qp / Kp
+// (vsa_rows_kernel) and v transposed into VpT[h*128 + d][position] (vsa_vt_kernel).
+// Then a kept tile is one TMA box of K rows and one of V^T columns.
+//
+// vsa_tc_kernel: a CTA owns one query tile (<= 64 rows) of one head.  The tile's queries
+// fill both halves of an M = 128 MMA and its kept key tiles are walked two at a time: in
+// chunk c, rows 0..63 take the keys of lst[2c] and rows 64..127 those of lst[2c+1]:
+//   S_c = Q K_c^T     (M 128, N 128, K 128) into one of two TMEM score tiles
+//   P_c               four softmax warps, one (query, half) row per thread, against a
+//                     reference max raised only when a chunk's max exceeds it by more
+//                     than 2^8 (that row of O in TMEM and its sum are then rescaled once)
+//   O += P_c V_c      (M 128, N 128, K 128) accumulating in TMEM; the P quadrants that
+//                     pair a row with the other half's keys are zero
+// then the two halves of each query (rows r and r + 64) are merged, coarse * gate is
+// added and rows are scattered back to token order.  The same roles, barrier protocol
+// and bounded waits as attention_tc.cu.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace {
+
+// poff[i] = sum over tiles before i of count rounded up to 8; poff[nt] = the total.
+// One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) vsa_padoff_kernel(const int* __restrict__ toff, int nt,
+                                                          int* __restrict__ poff) {
+    __shared__ int part[1024];
+    const int t = threadIdx.x;
+    const int per = (nt + 1023) / 1024;
+    const int i0 = min(nt, t * per), i1 = min(nt, i0 + per);
+    int sum = 0;
+    for (int i = i0; i < i1; ++i) sum += (toff[i + 1] - toff[i] + 7) & ~7;
+    part[t] = sum;
+    __syncthreads();
+    if (t == 0) {
+        int run = 0;
+        for (int u = 0; u < 1024; ++u) {
+            const int x = part[u];
+            part[u] = run;
+            run += x;
+        }
+        poff[nt] = run;
+    }
+    __syncthreads();
+    int run = part[t];
+    for (int i = i0; i < i1; ++i) {
+        poff[i] = run;
+        run += (toff[i + 1] - toff[i] + 7) & ~7;
+    }
+}
+
+// pidx[padded position] = token, or -1 in a tile's padding.  grid (tiles), 64 threads.
+__global__ void vsa_pidx_kernel(const int* __restrict__ perm, const int* __restrict__ toff,
+                                const int* __restrict__ poff, int* __restrict__ pidx) {
+    const int i = blockIdx.x;
+    const int cnt = toff[i + 1] - toff[i], pcnt = poff[i + 1] - poff[i];
+    for (int r = threadIdx.x; r < pcnt; r += blockDim.x) pidx[poff[i] + r] = r < cnt ? perm[toff[i] + r] : -1;
+}
+
+// Qp[p] = q[pidx[p]] and Kp[p] = k[pidx[p]] (whole rows of heads*128 bf16), zero in padding
+__global__ void vsa_rows_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq, const __nv_bfloat16* __restrict__ k,
+                                int64_t ldk, const int* __restrict__ pidx, int P, int width,
+                                __nv_bfloat16* __restrict__ qp, __nv_bfloat16* __restrict__ kp) {
+    const int cw = width / 8;  // 16-byte chunks a row
+    const int64_t total = static_cast<int64_t>(P) * cw;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t p = e / cw;
+        const int c = static_cast<int>(e - p * cw);
+        const int t = pidx[p];
+        uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
+        if (t >= 0) {
+            a = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(t) * ldq + c * 8);
+            b = *reinterpret_cast<const uint4*>(k + static_cast<int64_t>(t) * ldk + c * 8);
+        }
+        *reinterpret_cast<uint4*>(qp + p * width + c * 8) = a;
+        *reinterpret_cast<uint4*>(kp + p * width + c * 8) = b;
+    }
+}
+
+// VpT[c][p] = v[pidx[p]][c] (c = h*128 + d), zero in padding; 32 x 32 tiles through
+// shared memory.  grid (ceil(P/32), width/32).
+__global__ void __launch_bounds__(256) vsa_vt_kernel(const __nv_bfloat16* __restrict__ v, int64_t ldv,
+                                                     const int* __restrict__ pidx, int P,
+                                                     __nv_bfloat16* __restrict__ vpt) {
+    __shared__ __nv_bfloat16 t[32][34];
+    const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (int r = ty; r < 32; r += 8) {
+        const int p = p0 + r;
+        const int tok = p < P ? pidx[p] : -1;
+        t[r][tx] = tok >= 0 ? v[static_cast<int64_t>(tok) * ldv + c0 + tx] : __float2bfloat16(0.0f);
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+        const int p = p0 + tx;
+        if (p < P) vpt[static_cast<int64_t>(c0 + r) * P + p] = t[tx][r];
+    }
+}
+
+}  // namespace
+
+namespace {
+
+constexpr int kVB = 128 * 64 * 2;            // [128][64] bf16 128-byte-swizzle block: 16 KB
+constexpr int kVH = 64 * 64 * 2;             // a 64-row box inside such a block: 8 KB
+constexpr int kVT = 2 * kVB;                 // [128][128] operand: 32 KB
+constexpr int V_OFF_Q = 0;                   // Q: the query tile in rows 0..63 and again in 64..127
+constexpr int V_OFF_KV = V_OFF_Q + kVT;      // 2 stages: K [128 keys][128] + V^T [128][128 keys]
+constexpr int V_OFF_P = V_OFF_KV + 2 * 2 * kVT;
+constexpr int V_OFF_BAR = V_OFF_P + 2 * kVT;
+// q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full, drain
+constexpr int kVBars = 1 + 2 * 6 + 1 + 1;
+constexpr int V_OFF_MISC = V_OFF_BAR + kVBars * 8;
+constexpr int kVSmem = V_OFF_MISC + 64 + 1024;
+constexpr int kVThreads = 6 * 32;
+constexpr uint32_t kVTmemCols = 512;  // S0 at 0, S1 at 128, O at 256
+constexpr uint32_t kVTmemO = 256;
+static_assert(kVSmem <= 232448, "shared memory budget");
+
+// Chunk c pairs kept tiles lst[2c] (keys 0..63 of the chunk, used by query rows 0..63) and
+// lst[2c+1] (keys 64..127, used by the same queries repeated in rows 64..127); the P
+// quadrants that pair rows with the other tile's keys stay zero, so the output rows
+// 0..63 and 64..127 accumulate the two halves of the key walk, merged at the end.
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
+    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    const __grid_constant__ CUtensorMap tmVt, const int* __restrict__ perm, const int* __restrict__ toff,
+    const int* __restrict__ poff, const int* __restrict__ sel, const int* __restrict__ selcnt, int nt,
+    const __nv_bfloat16* __restrict__ gate, int64_t ldg, const float* __restrict__ outc, int heads,
+    void* __restrict__ o, int64_t ldo, float scale_log2, int* status) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + V_OFF_BAR);
+    uint64_t* q_full = bar;
+    uint64_t* kv_full = bar + 1;
+    uint64_t* kv_empty = bar + 3;
+    uint64_t* s_full = bar + 5;
+    uint64_t* s_empty = bar + 7;
+    uint64_t* p_full = bar + 9;
+    uint64_t* p_empty = bar + 11;
+    uint64_t* o_full = bar + 13;
+    uint64_t* drain = bar + 14;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + V_OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + V_OFF_MISC + 8);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.x, h = blockIdx.y;
+    const size_t rowi = static_cast<size_t>(h) * nt + i;
+    const int* lst = sel + rowi * nt;
+    const int L = selcnt[rowi];            // >= 1
+    const int C = (L + 1) / 2;             // chunks
+    const int qrows = toff[i + 1] - toff[i];  // <= 64
+
+    // the P quadrants (rows 0..63, keys 64..127) and (rows 64..127, keys 0..63) of both buffers
+    // stay zero: block 1 rows 0..63 and block 0 rows 64..127
+    for (int e = threadIdx.x; e < 2 * 2 * 512; e += blockDim.x) {
+        const int buf = e >> 10, q = (e >> 9) & 1, off = (e & 511) * 16;
+        *reinterpret_cast<uint4*>(smem + V_OFF_P + buf * kVT + (q ? 0 : kVB) + (q ? 64 * 128 : 0) + off) =
+            make_uint4(0u, 0u, 0u, 0u);
+    }
+    fh3::fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        fh3::mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            fh3::mbar_init(&kv_full[s], 1);
+            fh3::mbar_init(&kv_empty[s], 1);
+            fh3::mbar_init(&s_full[s], 1);
+            fh3::mbar_init(&s_empty[s], 4);
+            fh3::mbar_init(&p_full[s], 4);
+            fh3::mbar_init(&p_empty[s], 1);
+        }
+        fh3::mbar_init(o_full, 1);
+        fh3::mbar_init(drain, 1);
+        *abort_flag = 0;
+        fh3::fence_mbar_init();
+    }
+    if (warp == 1) {
+        fh3::tmem_alloc(tmem_slot, kVTmemCols);
+        fh3::tmem_relinquish();
+    }
+    fh3::tc_fence_before();
+    __syncthreads();
+    fh3::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t filled = 0, par = 0;
+            fh3::mbar_arrive_expect_tx(q_full, 4 * kVH);
+            for (int c = 0; c < 2; ++c)
+                for (int half = 0; half < 2; ++half)
+                    fh3::tma_load_2d(smem + V_OFF_Q + c * kVB + half * kVH, &tmQ, q_full, h * 128 + c * 64, poff[i]);
+            bool ok = true;
+            for (int cc = 0; cc < C && ok; ++cc) {
+                const int st = cc & 1;
+                const uint32_t ph = static_cast<uint32_t>((cc >> 1) & 1);
+                if (!(ok = fh3::mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, status))) break;
+                // a chunk with one tile loads it twice; the second half is masked out
+                const int ya = poff[lst[2 * cc]], yb = poff[lst[min(2 * cc + 1, L - 1)]];
+                uint8_t* sb = smem + V_OFF_KV + st * 2 * kVT;
+                fh3::mbar_arrive_expect_tx(&kv_full[st], 2 * kVT);
+                for (int c = 0; c < 2; ++c) {
+                    fh3::tma_load_2d(sb + c * kVB, &tmK, &kv_full[st], h * 128 + c * 64, ya);
+                    fh3::tma_load_2d(sb + c * kVB + kVH, &tmK, &kv_full[st], h * 128 + c * 64, yb);
+                }
+                fh3::tma_load_2d(sb + kVT, &tmVt, &kv_full[st], ya, h * 128);
+                fh3::tma_load_2d(sb + kVT + kVB, &tmVt, &kv_full[st], yb, h * 128);
+                filled |= 1u << st;
+                par = (par & ~(1u << st)) | (ph << st);
+            }
+            volatile int no_abort = 0;
+            fh3::mbar_wait(q_full, 0, &no_abort, nullptr);
+            if (!ok)
+                for (int s = 0; s < 2; ++s)
+                    if (filled & (1u << s)) fh3::mbar_wait(&kv_full[s], (par >> s) & 1u, &no_abort, nullptr);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = fh3::idesc_bf16_f32(128, 128);
+            const uint32_t qa = fh3::smem_u32(smem + V_OFF_Q);
+            bool ok = fh3::mbar_wait(q_full, 0, abort_flag, status);
+            auto pv = [&](int cc) {
+                const int bi = cc & 1;
+                if (!(ok = fh3::mbar_wait(&p_full[bi], (cc >> 1) & 1, abort_flag, status))) return;
+                fh3::tc_fence_after();
+                const uint32_t pa = fh3::smem_u32(smem + V_OFF_P + bi * kVT);
+                const uint32_t va = fh3::smem_u32(smem + V_OFF_KV + bi * 2 * kVT + kVT);
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        fh3::umma_f16(tmem + kVTmemO, fh3::sdesc_sw128(pa + c * kVB) + 2 * kk,
+                                      fh3::sdesc_sw128(va + c * kVB) + 2 * kk, idesc, (cc | c | kk) != 0 ? 1u : 0u);
+                fh3::umma_commit(o_full);
+                fh3::umma_commit(&p_empty[bi]);
+                fh3::umma_commit(&kv_empty[bi]);
+            };
+            for (int cc = 0; cc < C && ok; ++cc) {
+                const int b = cc & 1;
+                if (!(ok = fh3::mbar_wait(&kv_full[b], (cc >> 1) & 1, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait(&s_empty[b], ((cc >> 1) & 1) ^ 1u, abort_flag, status))) break;
+                fh3::tc_fence_after();
+                const uint32_t ka = fh3::smem_u32(smem + V_OFF_KV + b * 2 * kVT);
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        fh3::umma_f16(tmem + b * 128, fh3::sdesc_sw128(qa + c * kVB) + 2 * kk,
+                                      fh3::sdesc_sw128(ka + c * kVB) + 2 * kk, idesc, (c | kk) != 0 ? 1u : 0u);
+                fh3::umma_commit(&s_full[b]);
+                if (cc >= 1) pv(cc - 1);
+            }
+            if (ok) pv(C - 1);
+            fh3::umma_commit(drain);
+            volatile int no_abort = 0;
+            fh3::mbar_wait(drain, 0, &no_abort, nullptr);
+        }
+    } else {
+        // ------------------------------------------------------------ softmax, merge and epilogue (warps 2-5)
+        const int qw = warp & 3;          // TMEM lanes 32*qw .. 32*qw+31
+        const int half = qw >> 1;         // rows 0..63: the chunk's first tile; rows 64..127: its second
+        const int r = qw * 32 + lane;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(qw * 32) << 16);
+        float m_ref = -INFINITY, lsum = 0.0f;
+        bool ok = true;
+        auto wait_warp = [&](uint64_t* bw, uint32_t parity) {
+            int w = 1;
+            if (lane == 0) w = fh3::mbar_wait(bw, parity, abort_flag, status);
+            return __shfl_sync(0xffffffffu, w, 0) != 0;
+        };
+        for (int cc = 0; cc < C && ok; ++cc) {
+            const int b = cc & 1;
+            const int li = 2 * cc + half;
+            const int cnt = li < L ? toff[lst[li] + 1] - toff[lst[li]] : 0;  // valid keys of this half
+            if (!(ok = wait_warp(&s_full[b], (cc >> 1) & 1))) break;
+            fh3::tc_fence_after();
+            uint32_t v[2][32];
+            fh3::tmem_ld32(trow + b * 128 + half * 64, v[0]);
+            fh3::tmem_ld32(trow + b * 128 + half * 64 + 32, v[1]);
+            fh3::tmem_ld_wait();
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    if (c * 32 + e >= cnt) v[c][e] = __float_as_uint(-INFINITY);  // other tiles' keys, padding
+                    mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
+            const bool raise = mx > m_ref + 8.0f;  // false while a half-row has seen no key
+            if (cc > 0 && __any_sync(0xffffffffu, raise)) {
+                if (!(ok = wait_warp(o_full, (cc - 1) & 1))) break;  // the previous P V has landed
+                fh3::tc_fence_after();
+                const float a = raise ? exp2f(m_ref - mx) : 1.0f;  // 0 while this row's O is still empty
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t ov[32];
+                    fh3::tmem_ld32(trow + kVTmemO + c * 32, ov);
+                    fh3::tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
+                    fh3::tmem_st32(trow + kVTmemO + c * 32, ov);
+                }
+                fh3::tmem_st_wait();
+                lsum *= a;
+            }
+            if (raise) m_ref = mx;
+            if (!(ok = wait_warp(&p_empty[b], ((cc >> 1) & 1) ^ 1u))) break;  // P_{cc-2} consumed
+            uint8_t* pb = smem + V_OFF_P + b * kVT + half * kVB;
+            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;  // no key seen yet: every p is 0
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e = 8 * t + 2 * u;
+                        const float p0 = exp2f(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
+                        const float p1 = exp2f(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
+                        rs4[u] += p0 + p1;
+                        const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                        pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                    }
+                    const int ch = c * 4 + t;
+                    *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+            lsum += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+            fh3::tc_fence_before();
+            fh3::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                fh3::mbar_arrive(&s_empty[b]);
+                fh3::mbar_arrive(&p_full[b]);
+            }
+        }
+        if (ok) ok = wait_warp(o_full, (C - 1) & 1);  // the last P V has landed (P buffers free)
+        uint32_t ov[4][32];
+        if (ok) {
+            fh3::tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) fh3::tmem_ld32(trow + kVTmemO + c * 32, ov[c]);
+            fh3::tmem_ld_wait();
+        }
+        // merge the halves: rows 64..127 hand (m, l, O) to rows 0..63 through the P buffers
+        float* xch = reinterpret_cast<float*>(smem + V_OFF_P);  // [64][130]
+        if (half == 1 && ok) {
+            float* d = xch + (r - 64) * 130;
+            d[0] = m_ref;
+            d[1] = lsum;
+#pragma unroll
+            for (int e = 0; e < 128; ++e) d[2 + e] = __uint_as_float(ov[e >> 5][e & 31]);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps, on every path
+        if (half == 0 && ok && r < qrows) {
+            const float* x = xch + r * 130;
+            const float mb = x[0], lb = x[1];
+            const float m = fmaxf(m_ref, mb);  // finite: the query's tiles hold keys
+            const float wa = m_ref == -INFINITY ? 0.0f : exp2f(m_ref - m);
+            const float wb = mb == -INFINITY ? 0.0f : exp2f(mb - m);
+            const float inv = 1.0f / (lsum * wa + lb * wb);
+            const int64_t t = perm[toff[i] + r];
+            const float* cb = gate ? outc + (static_cast<size_t>(i) * heads + h) * 128 : nullptr;
+            const int64_t col = static_cast<int64_t>(h) * 128;
+#pragma unroll
+            for (int d = 0; d < 128; d += 8) {
+                float w8[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    w8[u] = (__uint_as_float(ov[(d + u) >> 5][(d + u) & 31]) * wa + x[2 + d + u] * wb) * inv;
+                if (cb) {
+                    const uint4 g4 = *reinterpret_cast<const uint4*>(gate + t * ldg + col + d);
+                    const __nv_bfloat16* g8 = reinterpret_cast<const __nv_bfloat16*>(&g4);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) w8[u] += cb[d + u] * __bfloat162float(g8[u]);
+                }
+                if (OUT_BF16) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const __nv_bfloat162 pp = __floats2bfloat162_rn(w8[2 * u], w8[2 * u + 1]);
+                        w[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                    }
+                    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o) + t * ldo + col + d) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+                } else {
+                    float* of = static_cast<float*>(o) + t * ldo + col + d;
+                    *reinterpret_cast<float4*>(of) = make_float4(w8[0], w8[1], w8[2], w8[3]);
+                    *reinterpret_cast<float4*>(of + 4) = make_float4(w8[4], w8[5], w8[6], w8[7]);
+                }
+            }
+        }
+    }
+
+    fh3::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fh3::tc_fence_after();
+        fh3::tmem_dealloc(tmem, kVTmemCols);
+    }
+}
+
+}  // namespace
+
+namespace fh3host {
+
+// The fine pass + coarse * gate on tcgen05; tiles of at most 64 tokens, head_dim 128,
+// bf16 q / k / v / gate.  The tile-stage arrays come from vsa.cu.
+int vsa_fine_tc(const int* perm, const int* toff, const int* sel, const int* selcnt, int nt, int n,
+                const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, int64_t ldk, const __nv_bfloat16* v,
+                int64_t ldv, const __nv_bfloat16* gate, int64_t ldg, const float* outc, int heads, void* o, bool o_bf16,
+                int64_t ldo, cudaStream_t s) {
+    DevCtx* c = ctx();
+    const int width = heads * 128;
+    const int64_t pmax = ((static_cast<int64_t>(n) + 7 * static_cast<int64_t>(nt)) + 31) & ~static_cast<int64_t>(31);
+    auto al = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+    const size_t b_poff = al(static_cast<size_t>(nt + 1) * 4), b_pidx = al(static_cast<size_t>(pmax) * 4);
+    const size_t b_act = al(static_cast<size_t>(pmax) * width * 2);
+    uint8_t* base = static_cast<uint8_t*>(scratch(c, 13, b_poff + b_pidx + 3 * b_act, s));
+    if (!base) return FH3_E_NOMEM;
+    int* poff = reinterpret_cast<int*>(base);
+    int* pidx = reinterpret_cast<int*>(base + b_poff);
+    auto* qp = reinterpret_cast<__nv_bfloat16*>(base + b_poff + b_pidx);
+    auto* kp = reinterpret_cast<__nv_bfloat16*>(base + b_poff + b_pidx + b_act);
+    auto* vpt = reinterpret_cast<__nv_bfloat16*>(base + b_poff + b_pidx + 2 * b_act);
+    int rc = check_cuda(cudaMemsetAsync(pidx, 0xFF, static_cast<size_t>(pmax) * 4, s), "vsa pidx memset");
+    if (rc) return rc;
+    vsa_padoff_kernel<<<1, 1024, 0, s>>>(toff, nt, poff);
+    vsa_pidx_kernel<<<nt, 64, 0, s>>>(perm, toff, poff, pidx);
+    const int64_t work = pmax * (width / 8);
+    const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 16));
+    vsa_rows_kernel<<<blocks, 256, 0, s>>>(q, ldq, k, ldk, pidx, static_cast<int>(pmax), width, qp, kp);
+    vsa_vt_kernel<<<dim3(static_cast<unsigned>(pmax / 32), static_cast<unsigned>(width / 32)), 256, 0, s>>>(
+        v, ldv, pidx, static_cast<int>(pmax), vpt);
+    rc = check_cuda(cudaGetLastError(), "vsa tile-order launches");
+    if (rc) return rc;
+    CUtensorMap tq, tk, tvt;
+    const cuuint32_t es[2] = {1, 1};
+    auto enc = [&](CUtensorMap* m, void* ptr, cuuint64_t w, cuuint64_t hgt, int64_t ld, cuuint32_t bw, cuuint32_t bh) {
+        const cuuint64_t gdim[2] = {w, hgt};
+        const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(ld) * 2};
+        const cuuint32_t box[2] = {bw, bh};
+        return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, gdim, gstr, box, es,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+    };
+    if (enc(&tq, qp, width, static_cast<cuuint64_t>(pmax), width, 64, 64) != CUDA_SUCCESS ||
+        enc(&tk, kp, width, static_cast<cuuint64_t>(pmax), width, 64, 64) != CUDA_SUCCESS ||
+        enc(&tvt, vpt, static_cast<cuuint64_t>(pmax), width, pmax, 64, 128) != CUDA_SUCCESS)
+        return set_error(FH3CUDA_E_CUDA, "vsa: cuTensorMapEncodeTiled failed");
+    static bool attr = false;
+    if (!attr) {
+        rc = check_cuda(cudaFuncSetAttribute(vsa_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kVSmem),
+                        "vsa_tc smem attribute");
+        if (!rc) rc = check_cuda(cudaFuncSetAttribute(vsa_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      kVSmem), "vsa_tc smem attribute");
+        if (rc) return rc;
+        attr = true;
+    }
+    const float scale_log2 = (1.0f / sqrtf(128.0f)) * 1.4426950408889634f;
+    const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(heads));
+    if (o_bf16)
+        vsa_tc_kernel<true><<<grid, kVThreads, kVSmem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate, ldg,
+                                                            outc, heads, o, ldo, scale_log2, ctx_status(c));
+    else
+        vsa_tc_kernel<false><<<grid, kVThreads, kVSmem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate, ldg,
+                                                             outc, heads, o, ldo, scale_log2, ctx_status(c));
+    return check_cuda(cudaGetLastError(), "vsa_tc_kernel launch");
+}
+
+}  // namespace fh3host

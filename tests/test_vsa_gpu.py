@@ -21,6 +21,17 @@ TOL = 1e-2      # bf16 operands
 TOL_F32 = 1e-5  # fp32 operands, the reference's bar
 
 
+@pytest.fixture(autouse=True, params=["tc", "mma"])
+def vsa_kernel(request, monkeypatch):
+    """bf16 head_dim-128 cases on both fine passes: tcgen05 (tile-order operands, TMEM tiles;
+    the default for tiles of at most 64 tokens) and mma.sync (FH3CUDA_VSA_KERNEL=mma)."""
+    if request.param == "mma":
+        monkeypatch.setenv("FH3CUDA_VSA_KERNEL", "mma")
+    else:
+        monkeypatch.delenv("FH3CUDA_VSA_KERNEL", raising=False)
+    return request.param
+
+
 def _dev(a, bf16=False):
     import torch
     t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
@@ -151,3 +162,18 @@ def test_rejects_bad_arguments(fh3):
     x64 = torch.zeros((64, 64), device="cuda")
     with pytest.raises(Fh3CudaError):
         fh3.vsa_attention(x64, x64, x64, None, seq, 1, 64, out=y[:, :64])  # fp32 operands need an fp32 o
+
+
+@pytest.mark.parametrize("seq", [(64 * 3 + 7 * 9 * 10, 64 * 3, 0, 630, 7, 9, 10),      # ragged cells of 1..4 per axis
+                                 (30 + 20 + 6 * 6 * 6, 30, 20, 216, 6, 6, 6)])
+def test_bf16_hd128_ragged_tiles_vs_oracle(fh3, oracle, seq):
+    """Ragged video cells (counts 1..64), partial prefix tiles, gate and bf16 output on head_dim 128:
+    the tcgen05 pass pads every tile's run to 8 rows and masks the rest."""
+    import torch
+    n, heads, hd = seq[0], 2, 128
+    g = torch.Generator(device="cuda").manual_seed(n)
+    q, k, v, gate = (torch.randn((n, heads * hd), device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
+    got = _np(fh3.vsa_attention(q, k, v, gate, seq, heads, hd, 64, 0.7, out_bf16=True))
+    f = lambda t: np.ascontiguousarray(_np(t))
+    ref = oracle.vsa(f(q), f(k), f(v), f(gate), seq, heads, hd, 64, 0.7)
+    assert rel_l2(got, ref) <= TOL
