@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
             bool ok = true;
             for (int j = 0; j < T && ok; ++j) {
                 const int st = j & 1;
-                if (!(ok = fh3::mbar_wait(&B.kv_empty[st], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(&B.kv_empty[st], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
                 uint8_t* kvb = smem + OFF_KV + st * 2 * kTile;
                 fh3::mbar_arrive_expect_tx(&B.kv_full[st], 2 * kTile);
                 for (int c = 0; c < 2; ++c) {
@@ -156,21 +156,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
                 par = (par & ~(1u << st)) | (static_cast<uint32_t>((j >> 1) & 1) << st);
             }
             volatile int no_abort = 0;
-            fh3::mbar_wait(B.q_full, 0, &no_abort, nullptr);  // Q lands before the CTA can leave
+            fh3::mbar_wait<true>(B.q_full, 0, &no_abort, nullptr);  // Q lands before the CTA can leave
             if (!ok)
                 for (int i = 0; i < 2; ++i)
-                    if (filled & (1u << i)) fh3::mbar_wait(&B.kv_full[i], (par >> i) & 1u, &no_abort, nullptr);
+                    if (filled & (1u << i)) fh3::mbar_wait<true>(&B.kv_full[i], (par >> i) & 1u, &no_abort, nullptr);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = fh3::idesc_bf16_f32(128, 128);
             const uint32_t qa = fh3::smem_u32(smem + OFF_Q);
-            bool ok = fh3::mbar_wait(B.q_full, 0, abort_flag, status);
+            bool ok = fh3::mbar_wait<true>(B.q_full, 0, abort_flag, status);
             // O += P_i V_i (the output tile accumulates across key tiles)
             auto pv = [&](int i) {
                 const int bi = i & 1;
-                if (!(ok = fh3::mbar_wait(&B.p_full[bi], (i >> 1) & 1, abort_flag, status))) return;
+                if (!(ok = fh3::mbar_wait<true>(&B.p_full[bi], (i >> 1) & 1, abort_flag, status))) return;
                 fh3::tc_fence_after();
                 const uint32_t pa = fh3::smem_u32(smem + OFF_P + bi * kTile);
                 const uint32_t va = fh3::smem_u32(smem + OFF_KV + bi * 2 * kTile + kTile);
@@ -186,8 +186,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
             };
             for (int j = 0; j < T && ok; ++j) {
                 const int b = j & 1;
-                if (!(ok = fh3::mbar_wait(&B.kv_full[b], (j >> 1) & 1, abort_flag, status))) break;
-                if (!(ok = fh3::mbar_wait(&B.s_empty[b], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(&B.kv_full[b], (j >> 1) & 1, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(&B.s_empty[b], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
                 fh3::tc_fence_after();
                 const uint32_t ka = fh3::smem_u32(smem + OFF_KV + b * 2 * kTile);
                 const uint32_t d = tmem + b * 128;
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
             if (ok) pv(T - 1);
             fh3::umma_commit(B.drain);  // every MMA issued retires before TMEM is freed
             volatile int no_abort = 0;
-            fh3::mbar_wait(B.drain, 0, &no_abort, nullptr);
+            fh3::mbar_wait<true>(B.drain, 0, &no_abort, nullptr);
         }
     } else {
         // ------------------------------------------------------------ softmax and epilogue (warps 2-5)
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
         bool ok = true;
         auto wait_warp = [&](uint64_t* bar, uint32_t parity) {
             int w = 1;
-            if (lane == 0) w = fh3::mbar_wait(bar, parity, abort_flag, status);
+            if (lane == 0) w = fh3::mbar_wait<true>(bar, parity, abort_flag, status);
             return __shfl_sync(0xffffffffu, w, 0) != 0;
         };
         for (int j = 0; j < T && ok; ++j) {

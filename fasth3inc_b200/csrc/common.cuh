@@ -145,15 +145,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait without the suspend-time hint: for waits on the critical path (the softmax
+// and MMA roles of the attention kernels), where a suspended thread's wake-up delay costs
+__device__ __forceinline__ bool mbar_try_wait_spin(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete.  Gives up when `abort` (a
 // shared flag other roles raise on their own timeout) is set, or after
 // kWaitLimitNs; then records FH3CUDA_E_TIMEOUT and returns false.
+template <bool SPIN = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           int* status) {
-    if (mbar_try_wait(bar, parity)) return true;
+    auto probe = [&]() { return SPIN ? mbar_try_wait_spin(bar, parity) : mbar_try_wait(bar, parity); };
+    if (probe()) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (probe()) return true;
         if ((it & 63) == 0) {
             if (*abort) return false;
             if (globaltimer() - t0 > kWaitLimitNs) {

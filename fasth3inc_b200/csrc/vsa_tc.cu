@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
             for (int cc = 0; cc < C && ok; ++cc) {
                 const int st = cc & 1;
                 const uint32_t ph = static_cast<uint32_t>((cc >> 1) & 1);
-                if (!(ok = fh3::mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(&kv_empty[st], ph ^ 1u, abort_flag, status))) break;
                 // a chunk with one tile loads it twice; the second half is masked out
                 const int ya = poff[lst[2 * cc]], yb = poff[lst[min(2 * cc + 1, L - 1)]];
                 uint8_t* sb = smem + V_OFF_KV + st * 2 * kVT;
@@ -216,20 +216,20 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
                 par = (par & ~(1u << st)) | (ph << st);
             }
             volatile int no_abort = 0;
-            fh3::mbar_wait(q_full, 0, &no_abort, nullptr);
+            fh3::mbar_wait<true>(q_full, 0, &no_abort, nullptr);
             if (!ok)
                 for (int s = 0; s < 2; ++s)
-                    if (filled & (1u << s)) fh3::mbar_wait(&kv_full[s], (par >> s) & 1u, &no_abort, nullptr);
+                    if (filled & (1u << s)) fh3::mbar_wait<true>(&kv_full[s], (par >> s) & 1u, &no_abort, nullptr);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = fh3::idesc_bf16_f32(128, 128);
             const uint32_t qa = fh3::smem_u32(smem + V_OFF_Q);
-            bool ok = fh3::mbar_wait(q_full, 0, abort_flag, status);
+            bool ok = fh3::mbar_wait<true>(q_full, 0, abort_flag, status);
             auto pv = [&](int cc) {
                 const int bi = cc & 1;
-                if (!(ok = fh3::mbar_wait(&p_full[bi], (cc >> 1) & 1, abort_flag, status))) return;
+                if (!(ok = fh3::mbar_wait<true>(&p_full[bi], (cc >> 1) & 1, abort_flag, status))) return;
                 fh3::tc_fence_after();
                 const uint32_t pa = fh3::smem_u32(smem + V_OFF_P + bi * kVT);
                 const uint32_t va = fh3::smem_u32(smem + V_OFF_KV + bi * 2 * kVT + kVT);
@@ -245,8 +245,8 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
             };
             for (int cc = 0; cc < C && ok; ++cc) {
                 const int b = cc & 1;
-                if (!(ok = fh3::mbar_wait(&kv_full[b], (cc >> 1) & 1, abort_flag, status))) break;
-                if (!(ok = fh3::mbar_wait(&s_empty[b], ((cc >> 1) & 1) ^ 1u, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(&kv_full[b], (cc >> 1) & 1, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(&s_empty[b], ((cc >> 1) & 1) ^ 1u, abort_flag, status))) break;
                 fh3::tc_fence_after();
                 const uint32_t ka = fh3::smem_u32(smem + V_OFF_KV + b * 2 * kVT);
 #pragma unroll
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
             if (ok) pv(C - 1);
             fh3::umma_commit(drain);
             volatile int no_abort = 0;
-            fh3::mbar_wait(drain, 0, &no_abort, nullptr);
+            fh3::mbar_wait<true>(drain, 0, &no_abort, nullptr);
         }
     } else {
         // ------------------------------------------------------------ softmax, merge and epilogue (warps 2-5)
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
         bool ok = true;
         auto wait_warp = [&](uint64_t* bw, uint32_t parity) {
             int w = 1;
-            if (lane == 0) w = fh3::mbar_wait(bw, parity, abort_flag, status);
+            if (lane == 0) w = fh3::mbar_wait<true>(bw, parity, abort_flag, status);
             return __shfl_sync(0xffffffffu, w, 0) != 0;
         };
         for (int cc = 0; cc < C && ok; ++cc) {
