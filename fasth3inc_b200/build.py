@@ -12,7 +12,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libfh3cuda.so")
-SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemm.cu", "ops.cu", "attention.cu", "attention_tc.cu", "attention_f32.cu",
+SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemv_tc.cu", "gemm.cu", "ops.cu", "attention.cu", "attention_tc.cu", "attention_f32.cu",
            "vsa.cu", "vsa_tc.cu", "trunk_io.cu", "dit.cu", "gen.cu", "noalloc.cu"]
 HEADERS = ["common.cuh", "flash.cuh"]
 

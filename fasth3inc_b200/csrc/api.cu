@@ -18,8 +18,8 @@ namespace fh3host {
 // 8 fp32 weight rows of the non-Q4_K formats, 9 video sparse attention's tile data,
 // 10 the DiT forward's activations, 11 bf16 weights of the two-pass large-M GEMM,
 // 12 the transposed V of the tensor-core attention, 13 video sparse attention's tile-order
-// copies of q, k and v
-constexpr int kScratchSlots = 14;
+// copies of q, k and v, 14 / 15 the tcgen05 GEMV's split-tile partials and counters
+constexpr int kScratchSlots = 16;
 
 struct DevCtx {
     int device = -1;

@@ -229,6 +229,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
 #pragma unroll
             for (int c = 0; c < 4; ++c) fh3::tmem_ld32(trow + b * 128 + c * 32, v[c]);
             fh3::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) fh3::tmem_regs_ready(v[c]);
             // row max of the raw scores (the scale is positive); keys past n only in the last tile
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             if (kb + kTcKeys <= n) {
@@ -257,6 +259,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
                     uint32_t ov[32];
                     fh3::tmem_ld32(trow + kTmemO + c * 32, ov);
                     fh3::tmem_ld_wait();
+                    fh3::tmem_regs_ready(ov);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
                     fh3::tmem_st32(trow + kTmemO + c * 32, ov);
@@ -302,6 +305,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
 #pragma unroll
             for (int c = 0; c < 4; ++c) fh3::tmem_ld32(trow + kTmemO + c * 32, ov[c]);
             fh3::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) fh3::tmem_regs_ready(ov[c]);
             if (row < n) {
                 const float inv = 1.0f / l;
                 const int64_t base = static_cast<int64_t>(row) * ldo + static_cast<int64_t>(h) * kTcHD;

@@ -360,6 +360,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// tcgen05.ld fills its destination registers asynchronously: they hold the data only
+// after tcgen05.wait::ld, but the compiler sees them as written by the ld itself and may
+// schedule arithmetic on them ahead of the wait.  Passing them through an empty asm
+// after the wait makes every use depend on a definition that follows it.
+template <int W>
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[W]) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) asm volatile("" : "+r"(r[i]));
+}
 // 32 lanes x 32 consecutive fp32 columns written back (one row per thread).
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
@@ -422,6 +431,9 @@ void* scratch_zeroed(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
 // 1..16-token Q4_K GEMV on warp-level tensor-core MMAs (gemv_mma.cu); arguments
 // already validated by the caller
 int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
+// 1..5-token Q4_K GEMV on tcgen05 integer MMAs (gemv_tc.cu); returns 1 without launching
+// when the shape or pointers do not suit it
+int gemv_tc(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
 // the fp32 CUDA-core GEMV (gemv.cu): uses no memory beyond x, y, bias and the weights
 int gemv_fp32(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
 // dense attention on tcgen05, head_dim 128 (attention_tc.cu); arguments already validated

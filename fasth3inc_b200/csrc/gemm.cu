@@ -178,6 +178,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tbase, i
             fh3::tmem_ld32(tbase + cc * 32, v);
             fh3::tmem_ld32(tbase + 128 + cc * 32, g);
             fh3::tmem_ld_wait();
+            fh3::tmem_regs_ready(v);
+            fh3::tmem_regs_ready(g);
             const int64_t f0 = nb * 128 + cc * 32;
             if (!row_ok || f0 >= p.n_out) continue;
             __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy;
@@ -205,6 +207,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tbase, i
         uint32_t v[32];
         fh3::tmem_ld32(tbase + cc * 32, v);
         fh3::tmem_ld_wait();
+        fh3::tmem_regs_ready(v);
         const int64_t n0 = nb * 256 + cc * 32;
         if (!row_ok || n0 >= p.N) continue;
         float o[32];

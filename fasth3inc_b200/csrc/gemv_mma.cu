@@ -837,8 +837,18 @@ int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float
     if (!c) return set_error(FH3CUDA_E_NODEV, "gemv_mma: call fh3cuda_init first");
     // 1..2 tokens: the single-launch stream-K kernel; FH3CUDA_GEMV_KERNEL=mma-cta
     // selects the prep + CTA-per-tile kernels instead
+    // 1..5 tokens: the tcgen05 kernel (gemv_tc.cu) when out <= in or at 5 tokens (measured
+    // faster there: 5120->5120 and 13824->5120 at 1..5 tokens, 5120->13824 at 5 tokens; the
+    // warp-MMA kernels stay ahead for 5120->13824 at 1..4 tokens).  FH3CUDA_GEMV_KERNEL=tc
+    // forces it for every shape; mma-stream / mma-cta force the warp-MMA kernels.
     const char* kname = getenv("FH3CUDA_GEMV_KERNEL");
     const bool cta = kname && strcmp(kname, "mma-cta") == 0;
+    const bool warp_mma = kname && (cta || strcmp(kname, "mma-stream") == 0);
+    const bool tc_forced = kname && strcmp(kname, "tc") == 0;
+    if (!warp_mma && n_tok <= 5 && (tc_forced || w->out <= w->in || n_tok == 5)) {
+        const int r = gemv_tc(w, x, y, n_tok, bias, s);
+        if (r != 1) return r;
+    }
     if (!cta && n_tok <= 2) {
         const int r = n_tok == 1 ? launch_stream<1>(w, x, y, bias, s) : launch_stream<2>(w, x, y, bias, s);
         if (r != 1) return r;

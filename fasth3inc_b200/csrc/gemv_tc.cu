@@ -1,0 +1,691 @@
+// gemv_tc.cu -- Q4_K GEMV for 1..5 tokens on tcgen05 integer MMAs.
+//
+// The small-M regime of fh3_matmul (src/core/fh3_ops.c:317-404):
+//   y[t][n] = sum_j ( (d*sc_j) * P_tnj - (dmin*m_j) * X_tj ),  P = sum_{k in j} q_nk x_tk,
+//   X_tj = sum_{k in j} x_tk over the 32-weight sub-blocks j of each super-block
+//   (w = (d*sc)*q - dmin*m as dequant_q4_k, src/core/fh3_quant.c:154-196).
+//
+// Work unit: a tile of 128 weight rows x one super-block (256 k).  One persistent CTA
+// per SM walks a contiguous run of units (stream-K over (tile, super-block), the
+// super-block fastest); a tile split between CTAs is finished by the last CTA to
+// arrive on the tile's counter, adding the runs' partial sums in run order.
+//
+// * Weights: one TMA box per unit, 144 bytes x 128 rows (the super-block column of the
+//   tile), into a 5-stage ring.  The first stages load before griddepcontrol.wait.
+// * A operand: warps 0-3 (one weight row per thread, the row's TMEM lane) expand the
+//   row's 128 nibble bytes into 256 u8 values q in k order (low nibbles of chunk c are
+//   k = 64c + i, high nibbles k = 64c + 32 + i) and write them to tensor memory.
+// * B operand: x of token t and super-block b, rounded to a 23-bit integer under a
+//   power of two 2^s (max|x| * 2^s < 2^22), in three balanced signed base-256 digits;
+//   row 3t + p of the B matrix holds digit p.  Built once per CTA for the super-blocks
+//   its run touches, K-major in the 128-byte swizzle layout.
+// * One kind::i8 MMA per sub-block (M 128, N 16, K 32) into its own 16 TMEM columns:
+//   int32 plane sums, exact.  P = P0 + 256 P1 + 65536 P2 (one fp32 rounding), then the
+//   scales in fp32 as the reference forms them (d*sc and dmin*m are exact products).
+// Roles (576 threads): warps 0-7 expand (two warps per TMEM lane quarter, each half of
+// the row's nibbles), warps 8-15 read the accumulators (two per lane quarter, each four
+// sub-blocks; the pair's sums meet in shared memory at the end of a tile segment),
+// warp 16 issues the TMA loads, warp 17 allocates TMEM and issues the MMAs.  Four A
+// buffers and two accumulator buffers let expansion run ahead of the MMAs and the
+// accumulator reads trail them.
+// Every wait is bounded; on a timeout the kernel records FH3CUDA_E_TIMEOUT, lets its
+// copies and MMAs finish and frees tensor memory.
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kGtThreads = 576;
+constexpr int kGtRows = 128;                     // rows of a tile = TMEM lanes
+constexpr int kGtStages = 6;
+constexpr int kGtStageBytes = kGtRows * fh3::kQ4KBytes;  // 18432
+constexpr int kGtSlotsMax = 20;                  // super-block columns of B a CTA can hold
+constexpr int kGtSlotBytes = 4096;               // 2 halves x 16 rows x 128 B
+constexpr int kGtMaxTok = 5;
+constexpr int kGtABufs = 4;
+constexpr int kGtHdrs = 8;                       // ring of the units' 16-byte row headers
+constexpr int kGtPreSegs = 2;                    // other segments of the last tile read ahead
+constexpr uint32_t kGtTmemCols = 512;
+constexpr uint32_t kTmD = 0;                     // accumulators: 2 buffers x 8 sub-blocks x 16 columns
+constexpr uint32_t kTmA = 256;                   // A operand: 4 buffers x 64 columns
+constexpr int kWarpTma = 16, kWarpMma = 17;
+#ifndef FH3_GT_SPIN
+#define FH3_GT_SPIN 0
+#endif
+constexpr bool kGtSpin = FH3_GT_SPIN != 0;  // spin (no suspend-time hint) in the role warps' waits
+
+constexpr int OFF_STAGE = 0;
+constexpr int OFF_B = OFF_STAGE + kGtStages * kGtStageBytes;           // 1024-aligned
+constexpr int OFF_X = OFF_B + kGtSlotsMax * kGtSlotBytes;              // sub-block sums [slot][t][8]
+constexpr int OFF_FS = OFF_X + kGtSlotsMax * kGtMaxTok * 8 * 4;        // 2^-s [slot][t]
+constexpr int OFF_RED = OFF_FS + kGtSlotsMax * kGtMaxTok * 4;          // pair exchange [quarter][lane][t]
+constexpr int OFF_HDR = OFF_RED + 4 * 32 * kGtMaxTok * 4;               // [kGtHdrs][128] x 16 B
+constexpr int OFF_BAR = OFF_HDR + kGtHdrs * kGtRows * 16;
+constexpr int kNumBars = 2 * kGtStages + 2 * kGtABufs + 4 + 2 * kGtHdrs + 8 + 2;
+constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
+constexpr int kGtSmem = OFF_MISC + 16 + 1024;                          // + alignment slack
+static_assert(OFF_B % 1024 == 0, "B slots must be 1024-byte aligned");
+static_assert(OFF_BAR % 8 == 0, "mbarriers must be 8-byte aligned");
+static_assert(kGtSmem <= 227 * 1024, "shared memory");
+
+struct GtBars {
+    uint64_t* full;    // [kGtStages] TMA -> expanders
+    uint64_t* empty;   // [kGtStages] expanders (8 warps) -> TMA
+    uint64_t* afull;   // [kGtABufs] A written (8 warps) -> MMA
+    uint64_t* aempty;  // [kGtABufs] MMA done -> expanders
+    uint64_t* dfull;   // [2] MMA done -> accumulator readers
+    uint64_t* dempty;  // [2] accumulators read (8 warps) -> MMA
+    uint64_t* xfull;   // [4] part-1 warp's sums in shared memory -> part-0 warp
+    uint64_t* xempty;  // [4] part-0 warp has read them -> part-1 warp
+    uint64_t* hfull;   // [kGtHdrs] headers copied (4 warps) -> accumulator readers
+    uint64_t* hempty;  // [kGtHdrs] headers read (8 warps) -> expanders
+    uint64_t* bfull;   // B operand built (8 warps) -> MMA and accumulator readers
+    uint64_t* drain;
+};
+__device__ __forceinline__ GtBars gt_bars(uint8_t* smem) {
+    uint64_t* b = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    GtBars r;
+    r.full = b;
+    r.empty = r.full + kGtStages;
+    r.afull = r.empty + kGtStages;
+    r.aempty = r.afull + kGtABufs;
+    r.dfull = r.aempty + kGtABufs;
+    r.dempty = r.dfull + 2;
+    r.xfull = r.dempty + 2;
+    r.xempty = r.xfull + 4;
+    r.hfull = r.xempty + 4;
+    r.hempty = r.hfull + kGtHdrs;
+    r.bfull = r.hempty + kGtHdrs;
+    r.drain = r.bfull + 1;
+    return r;
+}
+
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// D[tmem] = A[tmem] * B[smem desc]^T, kind::i8 (A u8, B s8, D s32), one thread.
+__device__ __forceinline__ void umma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// kind::i8 instruction descriptor: A u8, B s8, D s32, both K-major
+__host__ __device__ constexpr uint32_t idesc_u8s8_s32(int m, int n) {
+    return (2u << 4)                                  // D format: s32
+           | (0u << 7)                                // A format: unsigned 8-bit
+           | (1u << 10)                               // B format: signed 8-bit
+           | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+           | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+// 32 lanes x W consecutive 32-bit columns (one row per thread)
+template <int W>
+__device__ __forceinline__ void tmem_ld_w(uint32_t taddr, uint32_t (&r)[W]) {
+    static_assert(W == 4 || W == 8 || W == 16, "width");
+    if constexpr (W == 4) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                     : "r"(taddr));
+    } else if constexpr (W == 8) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                       "=r"(r[7])
+                     : "r"(taddr));
+    } else {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+            "%14, %15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+    }
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(fh3::smem_u32(p)));
+    return v;
+}
+
+__device__ __forceinline__ int64_t gt_cta_of(int64_t u, int64_t G, int64_t units) {
+    return ((u + 1) * G - 1) / units;  // the CTA whose run [c*U/G, (c+1)*U/G) holds unit u
+}
+
+// 2^e exactly for -149 <= e <= 127 (subnormal below -126)
+__device__ __forceinline__ float pow2_exact(int e) {
+    return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23) : __uint_as_float(1u << (e + 149));
+}
+
+// B operand and sub-block sums of one super-block (slot `slot`) for token t from the
+// warp's x values (lane l holds elements 8l .. 8l+7, sub-block l/4).
+template <int M>
+__device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int t, int slot, uint8_t* smem,
+                                        int lane) {
+    const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float am = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(e[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    // E with am < 2^E from the exponent field (subnormal am scaled up by 2^64 first)
+    int E = 0;
+    if (am > 0.0f && am <= 3.0e38f)
+        E = am >= 1.17549435e-38f ? static_cast<int>(__float_as_uint(am) >> 23) - 126
+                                  : static_cast<int>(__float_as_uint(am * 18446744073709551616.0f) >> 23) - 190;
+    const int s = min(22 - E, 149);                  // max|x| * 2^s < 2^22
+    const int s1 = min(s, 127);
+    const float m1 = pow2_exact(s1), m2 = pow2_exact(s - s1);  // x * 2^s exactly, in two steps
+    uint32_t pw[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        // round to the nearest integer (ties to even) through the bits of 1.5 * 2^23 + v, |v| < 2^22
+        const int xi = __float_as_int((e[i] * m1) * m2 + 12582912.0f) - 0x4B400000;
+        const int d0 = ((xi + 128) & 255) - 128;
+        const int x1 = (xi - d0) >> 8;                   // exact: xi - d0 is a multiple of 256
+        const int d1 = ((x1 + 128) & 255) - 128;
+        const int d2 = (x1 - d1) >> 8;                   // |d2| <= 64
+        const int sh = 8 * (i & 3);
+        pw[0][i >> 2] |= static_cast<uint32_t>(d0 & 255) << sh;
+        pw[1][i >> 2] |= static_cast<uint32_t>(d1 & 255) << sh;
+        pw[2][i >> 2] |= static_cast<uint32_t>(d2 & 255) << sh;
+    }
+    // element kk = 8l + i: half kk >> 7, 16-byte chunk (kk & 127) >> 4, byte 8(l & 1) + i
+    const int h = lane >> 4, c = (lane & 15) >> 1;
+    uint8_t* bs = smem + OFF_B + slot * kGtSlotBytes + h * 2048;
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        const int n = 3 * t + p;
+        uint8_t* dst = bs + (n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4) + 8 * (lane & 1);
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pw[p][0], pw[p][1]);
+    }
+    float sum = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    float* sx = reinterpret_cast<float*>(smem + OFF_X) + (slot * M + t) * 8;
+    if ((lane & 3) == 0) sx[lane >> 2] = sum;
+    if (lane == 0) reinterpret_cast<float*>(smem + OFF_FS)[slot * M + t] = pow2_exact(-s);
+}
+
+// exact int -> float for |v| < 2^22 on the FMA pipe: the bits of 1.5 * 2^23 + v
+__device__ __forceinline__ float small_i2f(uint32_t v) {
+    return __uint_as_float(v + 0x4B400000u) - 12582912.0f;
+}
+
+template <int M>
+__global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
+    const __grid_constant__ CUtensorMap tmW, int nblk, int64_t N, int64_t units, int seg_max,
+    const float* __restrict__ x, const float* __restrict__ bias, float* __restrict__ y, int64_t ldy,
+    float* __restrict__ partials, int* __restrict__ counters, int* status) {
+    static_assert(M >= 1 && M <= kGtMaxTok, "1..5 tokens");
+    constexpr int W = M == 1 ? 4 : (M == 2 ? 8 : 16);  // accumulator columns read per sub-block
+    constexpr int JB = M <= 2 ? 4 : 2;                  // sub-blocks read per batch
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const GtBars B = gt_bars(smem);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int64_t G = gridDim.x;  // <= units: every run is non-empty
+    const int64_t u0 = static_cast<int64_t>(blockIdx.x) * units / G;
+    const int n = static_cast<int>((static_cast<int64_t>(blockIdx.x) + 1) * units / G - u0);
+    const int b_first = static_cast<int>(u0 % nblk);
+    const int nslots = min(nblk, n);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kGtStages; ++i) {
+            fh3::mbar_init(&B.full[i], 1);
+            fh3::mbar_init(&B.empty[i], 8);
+        }
+        for (int i = 0; i < kGtABufs; ++i) {
+            fh3::mbar_init(&B.afull[i], 8);
+            fh3::mbar_init(&B.aempty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            fh3::mbar_init(&B.dfull[i], 1);
+            fh3::mbar_init(&B.dempty[i], 8);
+        }
+        for (int i = 0; i < 4; ++i) {
+            fh3::mbar_init(&B.xfull[i], 1);
+            fh3::mbar_init(&B.xempty[i], 1);
+        }
+        for (int i = 0; i < kGtHdrs; ++i) {
+            fh3::mbar_init(&B.hfull[i], 4);
+            fh3::mbar_init(&B.hempty[i], 8);
+        }
+        fh3::mbar_init(B.bfull, 8);
+        fh3::mbar_init(B.drain, 1);
+        *abort_flag = 0;
+        fh3::fence_mbar_init();
+    }
+    if (warp == kWarpMma) {
+        fh3::tmem_alloc(tmem_slot, kGtTmemCols);
+        fh3::tmem_relinquish();
+    }
+    fh3::tc_fence_before();
+    __syncthreads();
+    fh3::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // unit i of this run -> stage i % kGtStages; weights do not depend on earlier kernels.
+    // (lt, lb): tile and super-block of the next unit to load
+    int issued = 0;
+    int lt = static_cast<int>(u0 / nblk), lb = b_first;
+    auto issue = [&](int i) {
+        const int st = i % kGtStages;
+        fh3::mbar_arrive_expect_tx(&B.full[st], kGtStageBytes);
+        fh3::tma_load_2d(smem + OFF_STAGE + st * kGtStageBytes, &tmW, &B.full[st], lb * fh3::kQ4KBytes,
+                         lt * kGtRows);
+        if (++lb == nblk) {
+            lb = 0;
+            ++lt;
+        }
+    };
+    if (warp == kWarpTma && lane == 0) {
+        fh3::tma_prefetch_desc(&tmW);
+        for (; issued < min(n, kGtStages); ++issued) issue(issued);
+    }
+    pdl_launch_dependents();
+    // Only the accumulator readers touch x, y and the scratch (after griddepcontrol.wait);
+    // the weight pipeline starts at once.
+
+    // every lane waits (the TMA bytes, shared-memory handoffs and TMEM results become
+    // visible to each of them)
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+        const bool w = fh3::mbar_wait<kGtSpin>(bar, parity, abort_flag, status);
+        return __all_sync(0xffffffffu, w);
+    };
+
+    if (warp == kWarpTma) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            for (; issued < n; ++issued) {
+                const int st = issued % kGtStages;
+                if (!fh3::mbar_wait<kGtSpin>(&B.empty[st], ((issued / kGtStages) - 1) & 1, abort_flag, status))
+                    break;
+                issue(issued);
+            }
+            // every copy issued lands before the CTA can leave
+            volatile int no_abort = 0;
+            for (int i = max(0, issued - kGtStages); i < issued; ++i)
+                fh3::mbar_wait<true>(&B.full[i % kGtStages], (i / kGtStages) & 1, &no_abort, nullptr);
+        }
+    } else if (warp == kWarpMma) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_u8s8_s32(128, 16);
+            const uint32_t bbase = fh3::smem_u32(smem + OFF_B);
+            const bool bok = fh3::mbar_wait<true>(B.bfull, 0, abort_flag, status);
+            int slot = 0;  // (b - b_first) mod nblk of unit i
+            for (int i = 0; i < n && bok; ++i, slot = slot + 1 == nblk ? 0 : slot + 1) {
+                const int ab = i % kGtABufs, d = i & 1;
+                if (!fh3::mbar_wait<true>(&B.afull[ab], (i / kGtABufs) & 1, abort_flag, status)) break;
+                if (i >= 2 && !fh3::mbar_wait<true>(&B.dempty[d], ((i >> 1) - 1) & 1, abort_flag, status)) break;
+                fh3::tc_fence_after();
+                const uint32_t bs = bbase + slot * kGtSlotBytes;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    umma_i8_ts(tmem + kTmD + 128 * d + 16 * j, tmem + kTmA + 64 * ab + 8 * j,
+                               fh3::sdesc_sw128(bs + (j >> 2) * 2048) + 2 * (j & 3), idesc, 0u);
+                fh3::umma_commit(&B.dfull[d]);
+                fh3::umma_commit(&B.aempty[ab]);
+            }
+            fh3::umma_commit(B.drain);  // every MMA issued retires before TMEM is freed
+            volatile int no_abort = 0;
+            fh3::mbar_wait<true>(B.drain, 0, &no_abort, nullptr);
+        }
+    } else if (warp < 8) {
+        // ------------------------------------------------------------ expanders
+        // part p of the row: nibble bytes 64p .. 64p+63 (chunks 2p, 2p+1) -> A columns 32p ..
+        const int q = warp & 3, part = warp >> 2;
+        const int r = q * 32 + lane;
+        const uint32_t ta0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + kTmA + 32 * part;
+        for (int i = 0; i < n; ++i) {
+            const int st = i % kGtStages, ab = i % kGtABufs;
+            if (!wait_all(&B.full[st], (i / kGtStages) & 1)) break;
+            const uint8_t* rp = smem + OFF_STAGE + st * kGtStageBytes + r * fh3::kQ4KBytes + 16 + 64 * part;
+            uint4 qv[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) qv[c] = lds128(rp + 16 * c);
+            uint4 hd = make_uint4(0u, 0u, 0u, 0u);
+            if (part == 0) hd = lds128(rp - 16);  // the row's header: d, dmin, scales, mins
+            // these generic-proxy reads must be performed before the TMA (async proxy)
+            // refills the stage: a cross-proxy fence, then the release
+            fh3::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) fh3::mbar_arrive(&B.empty[st]);
+            if (part == 0) {  // header -> ring slot i % kGtHdrs for the accumulator readers
+                const int hs = i % kGtHdrs;
+                if (i >= kGtHdrs && !wait_all(&B.hempty[hs], ((i / kGtHdrs) - 1) & 1)) break;
+                *reinterpret_cast<uint4*>(smem + OFF_HDR + (hs * kGtRows + r) * 16) = hd;
+                __syncwarp();
+                if (lane == 0) fh3::mbar_arrive(&B.hfull[hs]);
+            }
+            if (i >= kGtABufs && !wait_all(&B.aempty[ab], ((i / kGtABufs) - 1) & 1)) break;
+            fh3::tc_fence_after();
+            uint32_t o[32];
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                const uint32_t w[8] = {qv[2 * cc].x,     qv[2 * cc].y,     qv[2 * cc].z,     qv[2 * cc].w,
+                                       qv[2 * cc + 1].x, qv[2 * cc + 1].y, qv[2 * cc + 1].z, qv[2 * cc + 1].w};
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    o[16 * cc + k] = w[k] & 0x0F0F0F0Fu;             // k = 64c + 4k .. +3
+                    o[16 * cc + 8 + k] = (w[k] >> 4) & 0x0F0F0F0Fu;  // k = 64c + 32 + 4k .. +3
+                }
+            }
+            fh3::tmem_st32(ta0 + 64 * ab, o);
+            fh3::tmem_st_wait();
+            fh3::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) fh3::mbar_arrive(&B.afull[ab]);
+        }
+    } else {
+        // ------------------------------------------------------------ accumulator readers
+        // part p: sub-blocks 4p .. 4p+3 of each unit; the part-1 warp hands its sums to the
+        // part-0 warp of its lane quarter at the end of every tile segment
+        const int q = warp & 3, part = (warp - 8) >> 2;
+        const int r = q * 32 + lane;
+        const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + kTmD;
+        const float* sx = reinterpret_cast<const float*>(smem + OFF_X);
+        const float* sfs = reinterpret_cast<const float*>(smem + OFF_FS);
+        float* red = reinterpret_cast<float*>(smem + OFF_RED) + (q * 32 + lane) * M;
+        float acc[M];
+#pragma unroll
+        for (int t = 0; t < M; ++t) acc[t] = 0.0f;
+        int fc = 0;  // tile segments finished
+        // The run's last tile: when it is split and, two units before the run ends, every
+        // other segment has already counted itself, this segment is the last one; the others'
+        // partials are read then, off the critical path (no CTA ever waits for another).
+        const int64_t t_last = (u0 + n - 1) / nblk;
+        const int64_t cf_last = gt_cta_of(t_last * nblk, G, units);
+        const int nseg_last = static_cast<int>(gt_cta_of((t_last + 1) * nblk - 1, G, units) - cf_last + 1);
+        const int seg_last = static_cast<int>(blockIdx.x - cf_last);
+        bool pre = false;
+        float pv[kGtPreSegs][M];
+        auto try_prefetch = [&]() {
+            if (part != 0 || nseg_last < 2 || nseg_last > kGtPreSegs + 1 || nseg_last > seg_max) return;
+            int cnt = 0;
+            if (lane == 0)
+                asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(cnt) : "l"(counters + t_last * 4 + q) : "memory");
+            cnt = __shfl_sync(0xffffffffu, cnt, 0);
+            if (cnt != nseg_last - 1) return;
+            const float* pt = partials + (t_last * seg_max * kGtRows + r) * M;
+#pragma unroll
+            for (int k = 0; k < kGtPreSegs; ++k) {
+                const int sg = k < seg_last ? k : k + 1;
+#pragma unroll
+                for (int t = 0; t < M; ++t)
+                    pv[k][t] = sg < nseg_last ? __ldcg(pt + static_cast<int64_t>(sg) * kGtRows * M + t) : 0.0f;
+            }
+            pre = true;
+        };
+        {
+            // B operand of the super-blocks this run touches: (token, slot) items over the
+            // eight warps, four items' x loads in flight at a time
+            pdl_wait();  // x, y and the scratch are ours from here on
+            const int w8 = warp - 8, items = M * nslots;
+            for (int it0 = w8; it0 < items; it0 += 4 * 8) {
+                float4 xv[4][2];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int it = it0 + 8 * k;
+                    if (it < items) {
+                        const int t = it / nslots, slot = it - t * nslots;
+                        const float4* xr = reinterpret_cast<const float4*>(
+                                               x + (static_cast<int64_t>(t) * nblk + (b_first + slot) % nblk) * 256) +
+                                           2 * lane;
+                        xv[k][0] = __ldg(xr);
+                        xv[k][1] = __ldg(xr + 1);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int it = it0 + 8 * k;
+                    if (it < items) {
+                        const int t = it / nslots;
+                        build_b<M>(xv[k][0], xv[k][1], t, it - t * nslots, smem, lane);
+                    }
+                }
+            }
+            fh3::fence_proxy_async_smem();  // B is read by the tensor cores
+            __syncwarp();
+            if (lane == 0) fh3::mbar_arrive(B.bfull);
+        }
+        bool ok = wait_all(B.bfull, 0);  // every warp's sub-block sums and scales
+        // end of this run's segment of `tile`: the pair's sums, then y or partials + count
+        auto finish_segment = [&](int64_t tile) -> bool {
+            if (part == 1) {
+                if (fc >= 1 && !wait_all(&B.xempty[q], (fc - 1) & 1)) return false;
+#pragma unroll
+                for (int t = 0; t < M; ++t) red[t] = acc[t];
+                __syncwarp();
+                if (lane == 0) fh3::mbar_arrive(&B.xfull[q]);
+            } else {
+                if (!wait_all(&B.xfull[q], fc & 1)) return false;
+#pragma unroll
+                for (int t = 0; t < M; ++t) acc[t] += red[t];
+                __syncwarp();
+                if (lane == 0) fh3::mbar_arrive(&B.xempty[q]);
+                const int64_t cf = gt_cta_of(tile * nblk, G, units);
+                const int64_t cl = gt_cta_of((tile + 1) * nblk - 1, G, units);
+                const int nseg = static_cast<int>(cl - cf + 1);
+                const int64_t row = tile * kGtRows + r;
+                if (nseg == 1) {
+                    if (row < N) {
+                        const float bv = bias ? bias[row] : 0.0f;
+#pragma unroll
+                        for (int t = 0; t < M; ++t) y[t * ldy + row] = acc[t] + bv;
+                    }
+                } else if (nseg > seg_max) {
+                    if (lane == 0) fh3::record_status(status, FH3_ERR);  // never write past the slots
+                } else if (pre && tile == t_last) {
+                    // every other segment had arrived when checked: this one is the last, and
+                    // their partials are already in registers
+                    const int seg = static_cast<int>(blockIdx.x - cf);
+                    float v[M];
+#pragma unroll
+                    for (int t = 0; t < M; ++t) v[t] = 0.0f;
+#pragma unroll
+                    for (int sg = 0; sg < kGtPreSegs + 1; ++sg) {
+                        if (sg >= nseg) break;
+#pragma unroll
+                        for (int t = 0; t < M; ++t) {
+                            const float lo = pv[sg < kGtPreSegs ? sg : kGtPreSegs - 1][t];  // segment sg < seg
+                            const float hi = pv[sg > 0 ? sg - 1 : 0][t];                     // segment sg > seg
+                            v[t] += sg == seg ? acc[t] : (sg < seg ? lo : hi);
+                        }
+                    }
+                    if (row < N) {
+                        const float bv = bias ? bias[row] : 0.0f;
+#pragma unroll
+                        for (int t = 0; t < M; ++t) y[t * ldy + row] = v[t] + bv;
+                    }
+                    __syncwarp();
+                    if (lane == 0) counters[tile * 4 + q] = 0;
+                } else {
+                    const int seg = static_cast<int>(blockIdx.x - cf);
+                    float* pp = partials + ((tile * seg_max + seg) * kGtRows + r) * M;
+#pragma unroll
+                    for (int t = 0; t < M; ++t) pp[t] = acc[t];
+                    // the warp's stores, then lane 0's release/acquire count on the counter of
+                    // (tile, quarter): it publishes them at GPU scope and, for the last segment,
+                    // acquires the other segments' stores of these 32 rows
+                    __syncwarp();
+                    int old = 0;
+                    int* ctr = counters + tile * 4 + q;
+                    if (lane == 0)
+                        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
+                    old = __shfl_sync(0xffffffffu, old, 0);
+                    if (old == nseg - 1) {  // last segment: add all in run order
+                        __syncwarp();
+                        const float* pt = partials + (tile * seg_max * kGtRows + r) * M;
+                        float v[M];
+#pragma unroll
+                        for (int t = 0; t < M; ++t) v[t] = 0.0f;
+                        for (int sg = 0; sg < nseg; ++sg)
+#pragma unroll
+                            for (int t = 0; t < M; ++t) v[t] += __ldcg(pt + static_cast<int64_t>(sg) * kGtRows * M + t);
+                        if (row < N) {
+                            const float bv = bias ? bias[row] : 0.0f;
+#pragma unroll
+                            for (int t = 0; t < M; ++t) y[t * ldy + row] = v[t] + bv;
+                        }
+                        if (lane == 0) *ctr = 0;
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < M; ++t) acc[t] = 0.0f;
+            ++fc;
+            return true;
+        };
+        int64_t tile = u0 / nblk;
+        int b = b_first, slot = 0;  // super-block and B slot of unit i
+        for (int i = 0; i < n && ok; ++i) {
+            const int hs = i % kGtHdrs, d = i & 1;
+            if (i == max(0, n - 2)) try_prefetch();
+            // the row's header: d, dmin, the 6-bit scales and mins
+            if (!wait_all(&B.hfull[hs], (i / kGtHdrs) & 1)) break;
+            const uint4 hd = lds128(smem + OFF_HDR + (hs * kGtRows + r) * 16);
+            __syncwarp();
+            if (lane == 0) fh3::mbar_arrive(&B.hempty[hs]);
+            if (!wait_all(&B.dfull[d], (i >> 1) & 1)) break;
+            fh3::tc_fence_after();
+            const float dd = fh3::h2f_bits(hd.x), dmin = fh3::h2f_bits(hd.x >> 16);
+            float sum[M], msum[M];
+#pragma unroll
+            for (int t = 0; t < M; ++t) sum[t] = msum[t] = 0.0f;
+#pragma unroll
+            for (int j0 = 0; j0 < 4; j0 += JB) {  // JB sub-blocks' accumulators in registers at a time
+                uint32_t v[JB][W];
+#pragma unroll
+                for (int jj = 0; jj < JB; ++jj) tmem_ld_w<W>(tl + 128 * d + 16 * (4 * part + j0 + jj), v[jj]);
+                fh3::tmem_ld_wait();
+#pragma unroll
+                for (int jj = 0; jj < JB; ++jj) fh3::tmem_regs_ready(v[jj]);
+                if (j0 + JB == 4) {  // every column of this buffer is read
+                    fh3::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) fh3::mbar_arrive(&B.dempty[d]);
+                }
+#pragma unroll
+                for (int jj = 0; jj < JB; ++jj) {
+                    const int j = 4 * part + j0 + jj;
+                    int sc, m;
+                    fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, j, sc, m);
+                    const float dsc = dd * small_i2f(static_cast<uint32_t>(sc));
+                    const float dm = dmin * small_i2f(static_cast<uint32_t>(m));
+#pragma unroll
+                    for (int t = 0; t < M; ++t) {
+                        const float p = fmaf(65536.0f, small_i2f(v[jj][3 * t + 2]),
+                                             fmaf(256.0f, small_i2f(v[jj][3 * t + 1]), small_i2f(v[jj][3 * t])));
+                        sum[t] = fmaf(dsc, p, sum[t]);
+                        msum[t] = fmaf(dm, sx[(slot * M + t) * 8 + j], msum[t]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < M; ++t) acc[t] = fmaf(sfs[slot * M + t], sum[t], acc[t]) - msum[t];
+            if (b == nblk - 1 || i == n - 1)
+                if (!finish_segment(tile)) break;
+            if (++b == nblk) {
+                b = 0;
+                ++tile;
+            }
+            slot = slot + 1 == nblk ? 0 : slot + 1;
+        }
+    }
+
+    fh3::tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        fh3::tc_fence_after();
+        fh3::tmem_dealloc(tmem, kGtTmemCols);
+    }
+}
+
+cudaLaunchAttribute pdl_attr() {
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+    return a;
+}
+
+template <int M>
+int launch_tc(const CUtensorMap& tm, int nblk, int64_t N, int64_t units, int seg_max, int grid, const float* x,
+              const float* bias, float* y, float* partials, int* counters, int* status, cudaStream_t s) {
+    static bool attr = false;
+    if (!attr) {
+        const int rc = fh3host::check_cuda(
+            cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGtSmem),
+            "gemv_tc_kernel smem attribute");
+        if (rc) return rc;
+        attr = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(kGtThreads, 1, 1);
+    cfg.dynamicSmemBytes = kGtSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1] = {pdl_attr()};
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return fh3host::check_cuda(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M>, tm, nblk, N, units, seg_max, x, bias, y,
+                                                  N, partials, counters, status),
+                               "gemv_tc_kernel launch");
+}
+
+}  // namespace
+
+namespace fh3host {
+
+// 1..5-token Q4_K GEMV on tcgen05 integer MMAs; returns 1 (nothing launched) when the
+// shape or the pointers do not suit it, so the caller takes the warp-MMA kernels.
+int gemv_tc(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s) {
+    DevCtx* c = ctx();
+    if (!c) return set_error(FH3CUDA_E_NODEV, "gemv_tc: call fh3cuda_init first");
+    if (n_tok < 1 || n_tok > kGtMaxTok) return 1;
+    if ((reinterpret_cast<uintptr_t>(w->data) & 15) || (reinterpret_cast<uintptr_t>(x) & 15)) return 1;
+    const int64_t N = w->out, K = w->in;
+    const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
+    const int64_t ntiles = (N + kGtRows - 1) / kGtRows;
+    const int64_t units = ntiles * nblk;
+    const int grid = static_cast<int>(std::min<int64_t>(ctx_sms(c), units));
+    const int64_t per = units / grid;  // >= 1
+    const int64_t run_max = (units + grid - 1) / grid;
+    if (std::min<int64_t>(nblk, run_max) > kGtSlotsMax) return 1;
+    const int seg_max = static_cast<int>(std::min<int64_t>(nblk, (nblk + per - 1) / per + 1));
+    float* partials =
+        static_cast<float*>(scratch(c, 14, static_cast<size_t>(ntiles) * seg_max * kGtRows * n_tok * 4, s));
+    int* counters = static_cast<int*>(scratch_zeroed(c, 15, static_cast<size_t>(ntiles) * 4 * 4, s));  // (tile, warp)
+    if (!partials || !counters) return FH3_E_NOMEM;
+
+    CUtensorMap tm;
+    const size_t row_bytes = static_cast<size_t>(nblk) * fh3::kQ4KBytes;
+    const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(N)};
+    const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(row_bytes)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(fh3::kQ4KBytes), static_cast<cuuint32_t>(kGtRows)};
+    const cuuint32_t es[2] = {1, 1};
+    if (encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w->data), gdim, gstr, box, es,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
+        return 1;
+    int* st = ctx_status(c);
+    switch (n_tok) {
+        case 1: return launch_tc<1>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
+        case 2: return launch_tc<2>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
+        case 3: return launch_tc<3>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
+        case 4: return launch_tc<4>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
+        default: return launch_tc<5>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
+    }
+}
+
+}  // namespace fh3host

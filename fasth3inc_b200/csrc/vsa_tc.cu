@@ -286,6 +286,8 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
             fh3::tmem_ld32(trow + b * 128 + half * 64, v[0]);
             fh3::tmem_ld32(trow + b * 128 + half * 64 + 32, v[1]);
             fh3::tmem_ld_wait();
+            fh3::tmem_regs_ready(v[0]);
+            fh3::tmem_regs_ready(v[1]);
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int c = 0; c < 2; ++c)
@@ -305,6 +307,7 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
                     uint32_t ov[32];
                     fh3::tmem_ld32(trow + kVTmemO + c * 32, ov);
                     fh3::tmem_ld_wait();
+                    fh3::tmem_regs_ready(ov);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
                     fh3::tmem_st32(trow + kVTmemO + c * 32, ov);
@@ -350,6 +353,8 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
 #pragma unroll
             for (int c = 0; c < 4; ++c) fh3::tmem_ld32(trow + kVTmemO + c * 32, ov[c]);
             fh3::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) fh3::tmem_regs_ready(ov[c]);
         }
         // merge the halves: rows 64..127 hand (m, l, O) to rows 0..63 through the P buffers
         float* xch = reinterpret_cast<float*>(smem + V_OFF_P);  // [64][130]

@@ -1,4 +1,4 @@
-"""The fp32 CUDA-core GEMV (1..16 tokens) against fh3_matmul.
+"""The small-M GEMV kernels (1..16 tokens) against fh3_matmul.
 
 Tolerance: relative Frobenius error <= 1e-5 for the fp32
 GEMV path, checked against the reference's own outputs (tests/golden) and the
@@ -25,12 +25,17 @@ def gemv_path(request):
     return request.param
 
 
-@pytest.fixture(autouse=True, params=["mma", "mma-cta", "fp32"])
+@pytest.fixture(autouse=True, params=["default", "tc", "mma-stream", "mma-cta", "fp32"])
 def gemv_kernel(request, monkeypatch):
-    """...and on every GEMV kernel: the tensor-core kernels (default: persistent
-    stream-K for 1..2 tokens, CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile)
-    and the fp32 CUDA-core kernel (FH3CUDA_GEMV_KERNEL=fp32)."""
-    monkeypatch.setenv("FH3CUDA_GEMV_KERNEL", request.param)
+    """...and on every GEMV kernel: the default choice (tcgen05 integer MMAs for 1..5
+    tokens when out <= in or at 5 tokens, warp-level MMAs otherwise), the tcgen05 kernel forced for every
+    shape ("tc"), the warp-MMA kernels ("mma-stream": persistent stream-K for 1..2 tokens,
+    CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile) and the fp32 CUDA-core kernel
+    (FH3CUDA_GEMV_KERNEL=fp32)."""
+    if request.param == "default":
+        monkeypatch.delenv("FH3CUDA_GEMV_KERNEL", raising=False)
+    else:
+        monkeypatch.setenv("FH3CUDA_GEMV_KERNEL", request.param)
     return request.param
 
 
@@ -115,3 +120,39 @@ def test_activation_ranges_and_zero_groups(fh3, oracle):
     got = _run(fh3, w, K, N, x)
     for t in range(M):
         assert rel_fro(got[t], ref[t]) <= TOL, t
+
+
+def test_split_tiles_repeat_bitwise(fh3, oracle):
+    """Tiles split between CTAs (stream-K) are summed in a fixed order: repeated calls
+    give identical bits, and consecutive calls on other weights leave no state behind."""
+    import torch
+    K, N = 13824, 1000
+    ws = [fh3.Q4KWeight.from_bytes(oracle.make_weights(seed=20 + i, stream=1, rows=N, n=K), K, N) for i in range(2)]
+    for M in (1, 3, 5):
+        x = torch.from_numpy(oracle.rng_normal(21, M, M * K).reshape(M, K).astype(np.float32)).cuda()
+        runs = []
+        for r in range(3):
+            runs.append([fh3.gemv(w, x).cpu().numpy() for w in ws])
+        for r in range(1, 3):
+            for a, b in zip(runs[0], runs[r]):
+                assert np.array_equal(a, b), (M, r)
+        ref = oracle.matmul(Q4K, oracle.make_weights(seed=20, stream=1, rows=N, n=K), K, N, x.cpu().numpy())
+        assert rel_fro(runs[0][0], ref) <= TOL, M
+
+
+def test_fresh_weight_buffers_first_call(fh3, oracle):
+    """The first call on a freshly uploaded weight buffer (its pages cold, its TMA loads
+    unevenly timed) gives the same result as later calls: guards the stage hand-off of
+    the tcgen05 kernel, whose generic-proxy reads of a stage precede its TMA refill."""
+    import torch
+    K, N = 13824, 5120
+    w = oracle.make_weights(seed=K + N, stream=1, rows=N, n=K)
+    for M in (3, 5):
+        x = oracle.rng_normal(M + 7, 2, M * K).reshape(M, K).astype(np.float32)
+        ref = oracle.matmul(Q4K, w, K, N, x)
+        keep = []
+        for trial in range(4):
+            W = fh3.Q4KWeight.from_bytes(w, K, N)
+            keep.append(W)
+            got = fh3.gemv(W, torch.from_numpy(x).cuda()).cpu().numpy()
+            assert rel_fro(got, ref) <= TOL, (M, trial)
