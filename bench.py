@@ -348,8 +348,18 @@ def run_ours(args):
 GEMV_SHAPES = ((5120, 13824), (13824, 5120), (5120, 5120))   # (in, out): fc-up, fc-down, attention proj
 
 
+def gemv_kernel_name(K: int, N: int, M: int) -> str:
+    """The kernel the default GEMV dispatch (csrc/gemv_mma.cu, gemv_mma) picks."""
+    if M <= 5 and (N <= K or M == 5):
+        return "gemv_tc_kernel"
+    if M <= 2:
+        return "gemv_stream_kernel"
+    return "gemv_mma_small_kernel" if M <= 4 else "gemv_mma_kernel"
+
+
 def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100) -> dict:
-    """Device time of back-to-back GEMV calls (1 and 4 tokens) on weights larger than L2.
+    """Device time of back-to-back GEMV calls (1, 4 and 16 tokens) on
+    weights larger than L2.
 
     A sleep kernel holds the stream while the host queues `reps` calls, so the CUDA events
     bracket GPU time only (each call's launches, chained by programmatic dependent launch).
@@ -362,7 +372,7 @@ def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100) -> 
         wbytes = N * K // 256 * 144
         nw = max(4, math.ceil(300e6 / wbytes))
         ws = [fh3.make_weights(N, K, seed=100 + i, stream_id=9) for i in range(nw)]
-        for M in (1, 4):
+        for M in (1, 4, 16):
             x = torch.randn((M, K), device="cuda")
             y = torch.empty((M, N), device="cuda")
             for i in range(2 * nw):
@@ -377,7 +387,8 @@ def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100) -> 
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1000.0 / reps
             gbs = (wbytes + 4 * M * (K + N)) / us / 1e3
-            out["shapes"].append({"in": K, "out": N, "tokens": M, "us_per_call": round(us, 2),
+            out["shapes"].append({"in": K, "out": N, "tokens": M, "kernel": gemv_kernel_name(K, N, M),
+                                  "us_per_call": round(us, 2),
                                   "achieved": round(gbs, 1), "frac": round(gbs / hbm_gbs, 4)})
         del ws
         torch.cuda.synchronize()
