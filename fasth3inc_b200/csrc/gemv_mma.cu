@@ -641,8 +641,12 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
 // grid (ceil(N / 16), S), cluster (1, S, 1) when S > 1.  Dynamic shared memory:
 // B fragments [nsb*8][8M] uint4, min-term B fragments [nsb][8M] u32, partials.
 // ---------------------------------------------------------------------------
+#ifndef FH3_GV_WIDE_MIN_BLOCKS
+#define FH3_GV_WIDE_MIN_BLOCKS 2  // 8..16 tokens: a looser register budget (no spills)
+#endif
 template <int NT>
-__global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_kernel(
+__global__ void __launch_bounds__(kGvMaxWarps * 32, NT == 1 ? FH3_GV_MIN_BLOCKS : FH3_GV_WIDE_MIN_BLOCKS)
+    gemv_mma_kernel(
     const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, const uint4* __restrict__ frag,
     const uint32_t* __restrict__ mfrag, const int* __restrict__ expo, int M, const float* __restrict__ bias,
     float* __restrict__ y, int64_t ldy, int S, int nsb_max) {
@@ -837,15 +841,15 @@ int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float
     if (!c) return set_error(FH3CUDA_E_NODEV, "gemv_mma: call fh3cuda_init first");
     // 1..2 tokens: the single-launch stream-K kernel; FH3CUDA_GEMV_KERNEL=mma-cta
     // selects the prep + CTA-per-tile kernels instead
-    // 1..5 tokens: the tcgen05 kernel (gemv_tc.cu) when out <= in or at 5 tokens (measured
-    // faster there: 5120->5120 and 13824->5120 at 1..5 tokens, 5120->13824 at 5 tokens; the
+    // The tcgen05 kernel (gemv_tc.cu) when out <= in or from 5 tokens on (measured faster
+    // there: 5120->5120 and 13824->5120 at every token count, 5120->13824 from 5 tokens; the
     // warp-MMA kernels stay ahead for 5120->13824 at 1..4 tokens).  FH3CUDA_GEMV_KERNEL=tc
     // forces it for every shape; mma-stream / mma-cta force the warp-MMA kernels.
     const char* kname = getenv("FH3CUDA_GEMV_KERNEL");
     const bool cta = kname && strcmp(kname, "mma-cta") == 0;
     const bool warp_mma = kname && (cta || strcmp(kname, "mma-stream") == 0);
     const bool tc_forced = kname && strcmp(kname, "tc") == 0;
-    if (!warp_mma && n_tok <= 5 && (tc_forced || w->out <= w->in || n_tok == 5)) {
+    if (!warp_mma && (tc_forced || w->out <= w->in || n_tok >= 5)) {
         const int r = gemv_tc(w, x, y, n_tok, bias, s);
         if (r != 1) return r;
     }

@@ -1,4 +1,4 @@
-// gemv_tc.cu -- Q4_K GEMV for 1..5 tokens on tcgen05 integer MMAs.
+// gemv_tc.cu -- Q4_K GEMV for 1..16 tokens on tcgen05 integer MMAs.
 //
 // The small-M regime of fh3_matmul (src/core/fh3_ops.c:317-404):
 //   y[t][n] = sum_j ( (d*sc_j) * P_tnj - (dmin*m_j) * X_tj ),  P = sum_{k in j} q_nk x_tk,
@@ -6,27 +6,32 @@
 //   (w = (d*sc)*q - dmin*m as dequant_q4_k, src/core/fh3_quant.c:154-196).
 //
 // Work unit: a tile of 128 weight rows x one super-block (256 k).  One persistent CTA
-// per SM walks a contiguous run of units (stream-K over (tile, super-block), the
-// super-block fastest); a tile split between CTAs is finished by the last CTA to
-// arrive on the tile's counter, adding the runs' partial sums in run order.
+// per SM walks a contiguous run of units (stream-K); a tile split between CTAs is
+// finished by the last CTA to arrive on the tile's counter, adding the pieces' partial
+// sums in a fixed order.  Unit order: the super-blocks are cut into chunks of `cw`
+// (for 1..5 tokens one chunk, the whole K); within a chunk the units go tile by tile,
+// the super-block fastest.  Chunks bound the super-blocks one run touches, so the B
+// operand of 6..16 tokens (up to 12 KB a super-block) fits in shared memory.
 //
 // * Weights: one TMA box per unit, 144 bytes x 128 rows (the super-block column of the
-//   tile), into a 5-stage ring.  The first stages load before griddepcontrol.wait.
-// * A operand: warps 0-3 (one weight row per thread, the row's TMEM lane) expand the
+//   tile), into a 6-stage ring.  The first stages load before griddepcontrol.wait.
+// * A operand: warps 0-7 (two per TMEM lane quarter, one weight row per lane) expand the
 //   row's 128 nibble bytes into 256 u8 values q in k order (low nibbles of chunk c are
 //   k = 64c + i, high nibbles k = 64c + 32 + i) and write them to tensor memory.
 // * B operand: x of token t and super-block b, rounded to a 23-bit integer under a
 //   power of two 2^s (max|x| * 2^s < 2^22), in three balanced signed base-256 digits;
 //   row 3t + p of the B matrix holds digit p.  Built once per CTA for the super-blocks
 //   its run touches, K-major in the 128-byte swizzle layout.
-// * One kind::i8 MMA per sub-block (M 128, N 16, K 32) into its own 16 TMEM columns:
-//   int32 plane sums, exact.  P = P0 + 256 P1 + 65536 P2 (one fp32 rounding), then the
-//   scales in fp32 as the reference forms them (d*sc and dmin*m are exact products).
+// * One kind::i8 MMA per sub-block (M 128, N = 3 * tokens rounded up to 16, K 32) into
+//   its own TMEM columns: int32 plane sums, exact.  P = P0 + 256 P1 + 65536 P2 (one fp32
+//   rounding), then the scales in fp32 as the reference forms them (d*sc and dmin*m are
+//   exact products).
 // Roles (576 threads): warps 0-7 expand (two warps per TMEM lane quarter, each half of
 // the row's nibbles), warps 8-15 read the accumulators (two per lane quarter, each four
-// sub-blocks; the pair's sums meet in shared memory at the end of a tile segment),
-// warp 16 issues the TMA loads, warp 17 allocates TMEM and issues the MMAs.  Four A
-// buffers and two accumulator buffers let expansion run ahead of the MMAs and the
+// sub-blocks; the pair's sums meet in shared memory at the end of a tile piece),
+// warp 16 issues the TMA loads, warp 17 allocates TMEM and issues the MMAs.  A and
+// accumulator buffers (4 and 2 for 1..5 tokens; fewer above, where one unit's
+// accumulators take 256 or 384 columns) let expansion run ahead of the MMAs and the
 // accumulator reads trail them.
 // Every wait is bounded; on a timeout the kernel records FH3CUDA_E_TIMEOUT, lets its
 // copies and MMAs finish and frees tensor memory.
@@ -38,63 +43,81 @@
 
 namespace {
 
-constexpr int kGtThreads = 576;
-constexpr int kGtRows = 128;                     // rows of a tile = TMEM lanes
+constexpr int kGtRows = 128;                               // rows of a tile = TMEM lanes
 constexpr int kGtStages = 6;
-constexpr int kGtStageBytes = kGtRows * fh3::kQ4KBytes;  // 18432
-constexpr int kGtSlotsMax = 20;                  // super-block columns of B a CTA can hold
-constexpr int kGtSlotBytes = 4096;               // 2 halves x 16 rows x 128 B
-constexpr int kGtMaxTok = 5;
-constexpr int kGtABufs = 4;
-constexpr int kGtHdrs = 8;                       // ring of the units' 16-byte row headers
-constexpr int kGtPreSegs = 2;                    // other segments of the last tile read ahead
+constexpr int kGtStageBytes = kGtRows * fh3::kQ4KBytes;    // 18432
+constexpr int kGtMaxTok = 16;
+constexpr int kGtHdrs = 8;                                 // ring of the units' 16-byte row headers
+constexpr int kGtPreSegs = 2;                              // other segments of the last tile read ahead
 constexpr uint32_t kGtTmemCols = 512;
-constexpr uint32_t kTmD = 0;                     // accumulators: 2 buffers x 8 sub-blocks x 16 columns
-constexpr uint32_t kTmA = 256;                   // A operand: 4 buffers x 64 columns
-constexpr int kWarpTma = 16, kWarpMma = 17;
 #ifndef FH3_GT_SPIN
 #define FH3_GT_SPIN 0
 #endif
 constexpr bool kGtSpin = FH3_GT_SPIN != 0;  // spin (no suspend-time hint) in the role warps' waits
 
-constexpr int OFF_STAGE = 0;
-constexpr int OFF_B = OFF_STAGE + kGtStages * kGtStageBytes;           // 1024-aligned
-constexpr int OFF_X = OFF_B + kGtSlotsMax * kGtSlotBytes;              // sub-block sums [slot][t][8]
-constexpr int OFF_FS = OFF_X + kGtSlotsMax * kGtMaxTok * 8 * 4;        // 2^-s [slot][t]
-constexpr int OFF_RED = OFF_FS + kGtSlotsMax * kGtMaxTok * 4;          // pair exchange [quarter][lane][t]
-constexpr int OFF_HDR = OFF_RED + 4 * 32 * kGtMaxTok * 4;               // [kGtHdrs][128] x 16 B
-constexpr int OFF_BAR = OFF_HDR + kGtHdrs * kGtRows * 16;
-constexpr int kNumBars = 2 * kGtStages + 2 * kGtABufs + 4 + 2 * kGtHdrs + 8 + 2;
-constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
-constexpr int kGtSmem = OFF_MISC + 16 + 1024;                          // + alignment slack
-static_assert(OFF_B % 1024 == 0, "B slots must be 1024-byte aligned");
-static_assert(OFF_BAR % 8 == 0, "mbarriers must be 8-byte aligned");
-static_assert(kGtSmem <= 227 * 1024, "shared memory");
+constexpr int align16(int v) { return (v + 15) & ~15; }
+
+// Per-token-count configuration: accumulator columns per sub-block, buffer counts,
+// B slots and the shared-memory layout.
+template <int M>
+struct GtCfg {
+    static constexpr int NC = M <= 5 ? 16 : (M <= 10 ? 32 : 48);  // B rows = accumulator columns per sub-block
+    static constexpr int DB = NC == 16 ? 2 : 1;                    // accumulator buffers
+    static constexpr int AB = NC == 48 ? 2 : 4;                    // A buffers (64 columns each)
+    static constexpr int DCOLS = 8 * NC;                           // accumulator columns of one unit
+    static constexpr uint32_t TM_A = DB * DCOLS;                   // first A column
+    static constexpr int SLOT_BYTES = 256 * NC;                    // B of one super-block: 2 halves x NC rows x 128 B
+    static constexpr int HALF_BYTES = 128 * NC;
+    static constexpr int SLOTS = NC == 16 ? 20 : (NC == 32 ? 10 : 6);
+    static constexpr int CHUNK = M <= 5 ? 0 : SLOTS / 2;          // super-blocks a chunk (0: the whole K)
+    // expander warps: two per TMEM lane quarter (half a row each) for 1..5 tokens; one
+    // (a whole row) above, so that 14 warps leave 128 registers a thread to the readers
+    static constexpr int EXP = M <= 5 ? 8 : 4;
+    static constexpr int WARP_RD = EXP;                            // first of the 8 accumulator readers
+    static constexpr int WARP_TMA = EXP + 8, WARP_MMA = EXP + 9;
+    static constexpr int THREADS = (EXP + 10) * 32;
+    static constexpr int OFF_STAGE = 0;
+    static constexpr int OFF_B = OFF_STAGE + kGtStages * kGtStageBytes;
+    static constexpr int OFF_X = OFF_B + SLOTS * SLOT_BYTES;       // sub-block sums [slot][t][8]
+    static constexpr int OFF_FS = OFF_X + SLOTS * M * 8 * 4;       // 2^-s [slot][t]
+    static constexpr int OFF_RED = OFF_FS + SLOTS * M * 4;         // pair exchange [quarter][lane][t]
+    static constexpr int OFF_HDR = align16(OFF_RED + 4 * 32 * M * 4);  // [kGtHdrs][128] x 16 B
+    static constexpr int OFF_BAR = OFF_HDR + kGtHdrs * kGtRows * 16;
+    static constexpr int NBARS = 2 * kGtStages + 2 * AB + 2 * DB + 8 + 2 * kGtHdrs + 2;
+    static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
+    static constexpr int SMEM = OFF_MISC + 16 + 1024;              // + alignment slack
+    static_assert(TM_A + 64 * AB <= kGtTmemCols, "tensor memory");
+    static_assert(OFF_B % 1024 == 0 && SLOT_BYTES % 1024 == 0 && HALF_BYTES % 1024 == 0, "B alignment");
+    static_assert(3 * M <= NC, "B rows");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+};
 
 struct GtBars {
     uint64_t* full;    // [kGtStages] TMA -> expanders
-    uint64_t* empty;   // [kGtStages] expanders (8 warps) -> TMA
-    uint64_t* afull;   // [kGtABufs] A written (8 warps) -> MMA
-    uint64_t* aempty;  // [kGtABufs] MMA done -> expanders
-    uint64_t* dfull;   // [2] MMA done -> accumulator readers
-    uint64_t* dempty;  // [2] accumulators read (8 warps) -> MMA
+    uint64_t* empty;   // [kGtStages] expanders (EXP warps) -> TMA
+    uint64_t* afull;   // [AB] A written (EXP warps) -> MMA
+    uint64_t* aempty;  // [AB] MMA done -> expanders
+    uint64_t* dfull;   // [DB] MMA done -> accumulator readers
+    uint64_t* dempty;  // [DB] accumulators read (8 warps) -> MMA
     uint64_t* xfull;   // [4] part-1 warp's sums in shared memory -> part-0 warp
     uint64_t* xempty;  // [4] part-0 warp has read them -> part-1 warp
-    uint64_t* hfull;   // [kGtHdrs] headers copied (4 warps) -> accumulator readers
+    uint64_t* hfull;   // [kGtHdrs] headers copied (one warp per lane quarter) -> accumulator readers
     uint64_t* hempty;  // [kGtHdrs] headers read (8 warps) -> expanders
     uint64_t* bfull;   // B operand built (8 warps) -> MMA and accumulator readers
     uint64_t* drain;
 };
+template <int M>
 __device__ __forceinline__ GtBars gt_bars(uint8_t* smem) {
-    uint64_t* b = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    using C = GtCfg<M>;
+    uint64_t* b = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     GtBars r;
     r.full = b;
     r.empty = r.full + kGtStages;
     r.afull = r.empty + kGtStages;
-    r.aempty = r.afull + kGtABufs;
-    r.dfull = r.aempty + kGtABufs;
-    r.dempty = r.dfull + 2;
-    r.xfull = r.dempty + 2;
+    r.aempty = r.afull + C::AB;
+    r.dfull = r.aempty + C::AB;
+    r.dempty = r.dfull + C::DB;
+    r.xfull = r.dempty + C::DB;
     r.xempty = r.xfull + 4;
     r.hfull = r.xempty + 4;
     r.hempty = r.hfull + kGtHdrs;
@@ -124,10 +147,10 @@ __host__ __device__ constexpr uint32_t idesc_u8s8_s32(int m, int n) {
            | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
 
-// 32 lanes x W consecutive 32-bit columns (one row per thread)
+// 32 lanes x W consecutive 32-bit columns (one row per thread); W > 16 in loads of 16
 template <int W>
-__device__ __forceinline__ void tmem_ld_w(uint32_t taddr, uint32_t (&r)[W]) {
-    static_assert(W == 4 || W == 8 || W == 16, "width");
+__device__ __forceinline__ void tmem_ld_w(uint32_t taddr, uint32_t* r) {
+    static_assert(W == 4 || W == 8 || W % 16 == 0, "width");
     if constexpr (W == 4) {
         asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
                      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -138,12 +161,17 @@ __device__ __forceinline__ void tmem_ld_w(uint32_t taddr, uint32_t (&r)[W]) {
                        "=r"(r[7])
                      : "r"(taddr));
     } else {
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-            "%14, %15}, [%16];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-            : "r"(taddr));
+#pragma unroll
+        for (int c = 0; c < W / 16; ++c) {
+            uint32_t* q = r + 16 * c;
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                "%13, %14, %15}, [%16];"
+                : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7]),
+                  "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]), "=r"(q[14]),
+                  "=r"(q[15])
+                : "r"(taddr + 16 * c));
+        }
     }
 }
 
@@ -155,8 +183,36 @@ __device__ __forceinline__ uint4 lds128(const uint8_t* p) {
     return v;
 }
 
-__device__ __forceinline__ int64_t gt_cta_of(int64_t u, int64_t G, int64_t units) {
-    return ((u + 1) * G - 1) / units;  // the CTA whose run [c*U/G, (c+1)*U/G) holds unit u
+// the CTA whose run [c*U/G, (c+1)*U/G) holds unit u (U * G < 2^32, checked by the host)
+__device__ __forceinline__ int gt_cta_of(uint32_t u, uint32_t G, uint32_t units) {
+    return static_cast<int>(((u + 1) * G - 1) / units);
+}
+
+// Position of a unit in the chunked order: chunk k (super-blocks k*cw .. k*cw + w - 1),
+// tile, super-block b.
+struct UnitPos {
+    int k, tile, b, w;
+};
+__device__ __forceinline__ UnitPos unit_pos(int64_t u, int ntiles, int nblk, int cw) {
+    const int64_t cu = static_cast<int64_t>(ntiles) * cw;  // units of a full chunk
+    UnitPos p;
+    p.k = static_cast<int>(u / cu);
+    const int64_t l = u - p.k * cu;
+    p.w = min(cw, nblk - p.k * cw);
+    p.tile = static_cast<int>(l / p.w);
+    p.b = p.k * cw + static_cast<int>(l - static_cast<int64_t>(p.tile) * p.w);
+    return p;
+}
+__device__ __forceinline__ void unit_next(UnitPos& p, int ntiles, int nblk, int cw) {
+    if (++p.b == p.k * cw + p.w) {
+        p.b = p.k * cw;
+        if (++p.tile == ntiles) {
+            p.tile = 0;
+            ++p.k;
+            p.b = p.k * cw;
+            p.w = min(cw, nblk - p.b);
+        }
+    }
 }
 
 // 2^e exactly for -149 <= e <= 127 (subnormal below -126)
@@ -169,6 +225,7 @@ __device__ __forceinline__ float pow2_exact(int e) {
 template <int M>
 __device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int t, int slot, uint8_t* smem,
                                         int lane) {
+    using C = GtCfg<M>;
     const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     float am = 0.0f;
 #pragma unroll
@@ -199,7 +256,7 @@ __device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int 
     }
     // element kk = 8l + i: half kk >> 7, 16-byte chunk (kk & 127) >> 4, byte 8(l & 1) + i
     const int h = lane >> 4, c = (lane & 15) >> 1;
-    uint8_t* bs = smem + OFF_B + slot * kGtSlotBytes + h * 2048;
+    uint8_t* bs = smem + C::OFF_B + slot * C::SLOT_BYTES + h * C::HALF_BYTES;
 #pragma unroll
     for (int p = 0; p < 3; ++p) {
         const int n = 3 * t + p;
@@ -209,9 +266,9 @@ __device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int 
     float sum = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    float* sx = reinterpret_cast<float*>(smem + OFF_X) + (slot * M + t) * 8;
+    float* sx = reinterpret_cast<float*>(smem + C::OFF_X) + (slot * M + t) * 8;
     if ((lane & 3) == 0) sx[lane >> 2] = sum;
-    if (lane == 0) reinterpret_cast<float*>(smem + OFF_FS)[slot * M + t] = pow2_exact(-s);
+    if (lane == 0) reinterpret_cast<float*>(smem + C::OFF_FS)[slot * M + t] = pow2_exact(-s);
 }
 
 // exact int -> float for |v| < 2^22 on the FMA pipe: the bits of 1.5 * 2^23 + v
@@ -220,36 +277,47 @@ __device__ __forceinline__ float small_i2f(uint32_t v) {
 }
 
 template <int M>
-__global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
-    const __grid_constant__ CUtensorMap tmW, int nblk, int64_t N, int64_t units, int seg_max,
-    const float* __restrict__ x, const float* __restrict__ bias, float* __restrict__ y, int64_t ldy,
+__global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
+    const __grid_constant__ CUtensorMap tmW, int nblk, int ntiles, int64_t N, int64_t units, int cw, int split,
+    int seg_max, const float* __restrict__ x, const float* __restrict__ bias, float* __restrict__ y, int64_t ldy,
     float* __restrict__ partials, int* __restrict__ counters, int* status) {
-    static_assert(M >= 1 && M <= kGtMaxTok, "1..5 tokens");
-    constexpr int W = M == 1 ? 4 : (M == 2 ? 8 : 16);  // accumulator columns read per sub-block
-    constexpr int JB = M <= 2 ? 4 : 2;                  // sub-blocks read per batch
+    using C = GtCfg<M>;
+    static_assert(M >= 1 && M <= kGtMaxTok, "1..16 tokens");
+    constexpr int W = M == 1 ? 4 : (M == 2 ? 8 : 16 * ((3 * M + 15) / 16));  // accumulator columns read per sub-block
+    constexpr int JB = M <= 2 ? 4 : (M <= 5 ? 2 : 1);                         // sub-blocks read per batch
+    constexpr bool kOneChunk = C::CHUNK == 0;                                 // cw == nblk
+    constexpr uint32_t idesc = idesc_u8s8_s32(128, C::NC);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const GtBars B = gt_bars(smem);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+    const GtBars B = gt_bars<M>(smem);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const int64_t G = gridDim.x;  // <= units: every run is non-empty
     const int64_t u0 = static_cast<int64_t>(blockIdx.x) * units / G;
     const int n = static_cast<int>((static_cast<int64_t>(blockIdx.x) + 1) * units / G - u0);
-    const int b_first = static_cast<int>(u0 % nblk);
-    const int nslots = min(nblk, n);
+    const UnitPos p_first = unit_pos(u0, ntiles, nblk, cw);
+    const UnitPos p_last = unit_pos(u0 + n - 1, ntiles, nblk, cw);
+    // B slots: with one chunk, the run's super-blocks cyclically from its first; with
+    // chunks, the super-blocks of the (at most two) chunks the run touches
+    const int sbase = kOneChunk ? p_first.b : p_first.k * cw;
+    const int nslots = kOneChunk ? min(nblk, n) : min(nblk, (p_last.k + 1) * cw) - sbase;
+    auto slot_of = [&](int b) {
+        const int d = b - sbase;
+        return d < 0 ? d + nblk : d;
+    };
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kGtStages; ++i) {
             fh3::mbar_init(&B.full[i], 1);
-            fh3::mbar_init(&B.empty[i], 8);
+            fh3::mbar_init(&B.empty[i], C::EXP);
         }
-        for (int i = 0; i < kGtABufs; ++i) {
-            fh3::mbar_init(&B.afull[i], 8);
+        for (int i = 0; i < C::AB; ++i) {
+            fh3::mbar_init(&B.afull[i], C::EXP);
             fh3::mbar_init(&B.aempty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < C::DB; ++i) {
             fh3::mbar_init(&B.dfull[i], 1);
             fh3::mbar_init(&B.dempty[i], 8);
         }
@@ -266,7 +334,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
         *abort_flag = 0;
         fh3::fence_mbar_init();
     }
-    if (warp == kWarpMma) {
+    if (warp == C::WARP_MMA) {
         fh3::tmem_alloc(tmem_slot, kGtTmemCols);
         fh3::tmem_relinquish();
     }
@@ -275,21 +343,17 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
     fh3::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // unit i of this run -> stage i % kGtStages; weights do not depend on earlier kernels.
-    // (lt, lb): tile and super-block of the next unit to load
+    // unit i of this run -> stage i % kGtStages; weights do not depend on earlier kernels
     int issued = 0;
-    int lt = static_cast<int>(u0 / nblk), lb = b_first;
+    UnitPos lp = p_first;  // the next unit to load
     auto issue = [&](int i) {
         const int st = i % kGtStages;
         fh3::mbar_arrive_expect_tx(&B.full[st], kGtStageBytes);
-        fh3::tma_load_2d(smem + OFF_STAGE + st * kGtStageBytes, &tmW, &B.full[st], lb * fh3::kQ4KBytes,
-                         lt * kGtRows);
-        if (++lb == nblk) {
-            lb = 0;
-            ++lt;
-        }
+        fh3::tma_load_2d(smem + C::OFF_STAGE + st * kGtStageBytes, &tmW, &B.full[st], lp.b * fh3::kQ4KBytes,
+                         lp.tile * kGtRows);
+        unit_next(lp, ntiles, nblk, cw);
     };
-    if (warp == kWarpTma && lane == 0) {
+    if (warp == C::WARP_TMA && lane == 0) {
         fh3::tma_prefetch_desc(&tmW);
         for (; issued < min(n, kGtStages); ++issued) issue(issued);
     }
@@ -304,7 +368,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
         return __all_sync(0xffffffffu, w);
     };
 
-    if (warp == kWarpTma) {
+    if (warp == C::WARP_TMA) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             for (; issued < n; ++issued) {
@@ -318,71 +382,77 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
             for (int i = max(0, issued - kGtStages); i < issued; ++i)
                 fh3::mbar_wait<true>(&B.full[i % kGtStages], (i / kGtStages) & 1, &no_abort, nullptr);
         }
-    } else if (warp == kWarpMma) {
+    } else if (warp == C::WARP_MMA) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_u8s8_s32(128, 16);
-            const uint32_t bbase = fh3::smem_u32(smem + OFF_B);
+            const uint32_t bbase = fh3::smem_u32(smem + C::OFF_B);
             const bool bok = fh3::mbar_wait<true>(B.bfull, 0, abort_flag, status);
-            int slot = 0;  // (b - b_first) mod nblk of unit i
-            for (int i = 0; i < n && bok; ++i, slot = slot + 1 == nblk ? 0 : slot + 1) {
-                const int ab = i % kGtABufs, d = i & 1;
-                if (!fh3::mbar_wait<true>(&B.afull[ab], (i / kGtABufs) & 1, abort_flag, status)) break;
-                if (i >= 2 && !fh3::mbar_wait<true>(&B.dempty[d], ((i >> 1) - 1) & 1, abort_flag, status)) break;
+            UnitPos mp = p_first;
+            for (int i = 0; i < n && bok; ++i) {
+                const int ab = i % C::AB, d = i % C::DB;
+                if (!fh3::mbar_wait<true>(&B.afull[ab], (i / C::AB) & 1, abort_flag, status)) break;
+                if (i >= C::DB && !fh3::mbar_wait<true>(&B.dempty[d], ((i / C::DB) - 1) & 1, abort_flag, status))
+                    break;
                 fh3::tc_fence_after();
-                const uint32_t bs = bbase + slot * kGtSlotBytes;
+                const uint32_t bs = bbase + slot_of(mp.b) * C::SLOT_BYTES;
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    umma_i8_ts(tmem + kTmD + 128 * d + 16 * j, tmem + kTmA + 64 * ab + 8 * j,
-                               fh3::sdesc_sw128(bs + (j >> 2) * 2048) + 2 * (j & 3), idesc, 0u);
+                    umma_i8_ts(tmem + C::DCOLS * d + C::NC * j, tmem + C::TM_A + 64 * ab + 8 * j,
+                               fh3::sdesc_sw128(bs + (j >> 2) * C::HALF_BYTES) + 2 * (j & 3), idesc, 0u);
                 fh3::umma_commit(&B.dfull[d]);
                 fh3::umma_commit(&B.aempty[ab]);
+                unit_next(mp, ntiles, nblk, cw);
             }
             fh3::umma_commit(B.drain);  // every MMA issued retires before TMEM is freed
             volatile int no_abort = 0;
             fh3::mbar_wait<true>(B.drain, 0, &no_abort, nullptr);
         }
-    } else if (warp < 8) {
+    } else if (warp < C::EXP) {
         // ------------------------------------------------------------ expanders
-        // part p of the row: nibble bytes 64p .. 64p+63 (chunks 2p, 2p+1) -> A columns 32p ..
-        const int q = warp & 3, part = warp >> 2;
+        // part p of a row: nibble bytes 64p .. 64p+63 (chunks 2p, 2p+1) -> A columns 32p ..;
+        // a warp takes PARTS consecutive parts of the rows of its lane quarter
+        constexpr int PARTS = 8 / C::EXP;
+        const int q = warp & 3, part0 = (warp >> 2) * PARTS;
         const int r = q * 32 + lane;
-        const uint32_t ta0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + kTmA + 32 * part;
+        const uint32_t ta0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::TM_A + 32 * part0;
         for (int i = 0; i < n; ++i) {
-            const int st = i % kGtStages, ab = i % kGtABufs;
+            const int st = i % kGtStages, ab = i % C::AB;
             if (!wait_all(&B.full[st], (i / kGtStages) & 1)) break;
-            const uint8_t* rp = smem + OFF_STAGE + st * kGtStageBytes + r * fh3::kQ4KBytes + 16 + 64 * part;
-            uint4 qv[4];
+            const uint8_t* rp = smem + C::OFF_STAGE + st * kGtStageBytes + r * fh3::kQ4KBytes + 16 + 64 * part0;
+            uint4 qv[4 * PARTS];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) qv[c] = lds128(rp + 16 * c);
+            for (int c = 0; c < 4 * PARTS; ++c) qv[c] = lds128(rp + 16 * c);
             uint4 hd = make_uint4(0u, 0u, 0u, 0u);
-            if (part == 0) hd = lds128(rp - 16);  // the row's header: d, dmin, scales, mins
+            if (part0 == 0) hd = lds128(rp - 16);  // the row's header: d, dmin, scales, mins
             // these generic-proxy reads must be performed before the TMA (async proxy)
             // refills the stage: a cross-proxy fence, then the release
             fh3::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) fh3::mbar_arrive(&B.empty[st]);
-            if (part == 0) {  // header -> ring slot i % kGtHdrs for the accumulator readers
+            if (part0 == 0) {  // header -> ring slot i % kGtHdrs for the accumulator readers
                 const int hs = i % kGtHdrs;
                 if (i >= kGtHdrs && !wait_all(&B.hempty[hs], ((i / kGtHdrs) - 1) & 1)) break;
-                *reinterpret_cast<uint4*>(smem + OFF_HDR + (hs * kGtRows + r) * 16) = hd;
+                *reinterpret_cast<uint4*>(smem + C::OFF_HDR + (hs * kGtRows + r) * 16) = hd;
                 __syncwarp();
                 if (lane == 0) fh3::mbar_arrive(&B.hfull[hs]);
             }
-            if (i >= kGtABufs && !wait_all(&B.aempty[ab], ((i / kGtABufs) - 1) & 1)) break;
+            if (i >= C::AB && !wait_all(&B.aempty[ab], ((i / C::AB) - 1) & 1)) break;
             fh3::tc_fence_after();
-            uint32_t o[32];
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const uint32_t w[8] = {qv[2 * cc].x,     qv[2 * cc].y,     qv[2 * cc].z,     qv[2 * cc].w,
-                                       qv[2 * cc + 1].x, qv[2 * cc + 1].y, qv[2 * cc + 1].z, qv[2 * cc + 1].w};
+            for (int pp = 0; pp < PARTS; ++pp) {
+                uint32_t o[32];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    o[16 * cc + k] = w[k] & 0x0F0F0F0Fu;             // k = 64c + 4k .. +3
-                    o[16 * cc + 8 + k] = (w[k] >> 4) & 0x0F0F0F0Fu;  // k = 64c + 32 + 4k .. +3
+                for (int cc = 0; cc < 2; ++cc) {
+                    const uint4 a = qv[4 * pp + 2 * cc], b2 = qv[4 * pp + 2 * cc + 1];
+                    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b2.x, b2.y, b2.z, b2.w};
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        o[16 * cc + k] = w[k] & 0x0F0F0F0Fu;             // k = 64c + 4k .. +3
+                        o[16 * cc + 8 + k] = (w[k] >> 4) & 0x0F0F0F0Fu;  // k = 64c + 32 + 4k .. +3
+                    }
                 }
+                fh3::tmem_st32(ta0 + 64 * ab + 32 * pp, o);
             }
-            fh3::tmem_st32(ta0 + 64 * ab, o);
             fh3::tmem_st_wait();
             fh3::tc_fence_before();
             __syncwarp();
@@ -391,48 +461,31 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
     } else {
         // ------------------------------------------------------------ accumulator readers
         // part p: sub-blocks 4p .. 4p+3 of each unit; the part-1 warp hands its sums to the
-        // part-0 warp of its lane quarter at the end of every tile segment
-        const int q = warp & 3, part = (warp - 8) >> 2;
+        // part-0 warp of its lane quarter at the end of every tile piece
+        const int q = warp & 3, part = (warp - C::WARP_RD) >> 2;
         const int r = q * 32 + lane;
-        const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + kTmD;
-        const float* sx = reinterpret_cast<const float*>(smem + OFF_X);
-        const float* sfs = reinterpret_cast<const float*>(smem + OFF_FS);
-        float* red = reinterpret_cast<float*>(smem + OFF_RED) + (q * 32 + lane) * M;
+        const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        const float* sx = reinterpret_cast<const float*>(smem + C::OFF_X);
+        const float* sfs = reinterpret_cast<const float*>(smem + C::OFF_FS);
+        float* red = reinterpret_cast<float*>(smem + C::OFF_RED) + (q * 32 + lane) * M;
+        const uint32_t uG = static_cast<uint32_t>(G), uU = static_cast<uint32_t>(units);
+        const int nch = kOneChunk ? 1 : (nblk + cw - 1) / cw;
+        // CTAs of tile `tile`'s piece in chunk kk: the first in cf, the count returned
+        auto piece_ctas = [&](int kk, int64_t tile, int& cf) {
+            const int w = min(cw, nblk - kk * cw);
+            const uint32_t s = static_cast<uint32_t>(static_cast<int64_t>(kk) * ntiles * cw + tile * w);
+            cf = gt_cta_of(s, uG, uU);
+            return gt_cta_of(s + w - 1, uG, uU) - cf + 1;
+        };
         float acc[M];
 #pragma unroll
         for (int t = 0; t < M; ++t) acc[t] = 0.0f;
-        int fc = 0;  // tile segments finished
-        // The run's last tile: when it is split and, two units before the run ends, every
-        // other segment has already counted itself, this segment is the last one; the others'
-        // partials are read then, off the critical path (no CTA ever waits for another).
-        const int64_t t_last = (u0 + n - 1) / nblk;
-        const int64_t cf_last = gt_cta_of(t_last * nblk, G, units);
-        const int nseg_last = static_cast<int>(gt_cta_of((t_last + 1) * nblk - 1, G, units) - cf_last + 1);
-        const int seg_last = static_cast<int>(blockIdx.x - cf_last);
-        bool pre = false;
-        float pv[kGtPreSegs][M];
-        auto try_prefetch = [&]() {
-            if (part != 0 || nseg_last < 2 || nseg_last > kGtPreSegs + 1 || nseg_last > seg_max) return;
-            int cnt = 0;
-            if (lane == 0)
-                asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(cnt) : "l"(counters + t_last * 4 + q) : "memory");
-            cnt = __shfl_sync(0xffffffffu, cnt, 0);
-            if (cnt != nseg_last - 1) return;
-            const float* pt = partials + (t_last * seg_max * kGtRows + r) * M;
-#pragma unroll
-            for (int k = 0; k < kGtPreSegs; ++k) {
-                const int sg = k < seg_last ? k : k + 1;
-#pragma unroll
-                for (int t = 0; t < M; ++t)
-                    pv[k][t] = sg < nseg_last ? __ldcg(pt + static_cast<int64_t>(sg) * kGtRows * M + t) : 0.0f;
-            }
-            pre = true;
-        };
+        int fc = 0;  // tile pieces finished
         {
             // B operand of the super-blocks this run touches: (token, slot) items over the
             // eight warps, four items' x loads in flight at a time
             pdl_wait();  // x, y and the scratch are ours from here on
-            const int w8 = warp - 8, items = M * nslots;
+            const int w8 = warp - C::WARP_RD, items = M * nslots;
             for (int it0 = w8; it0 < items; it0 += 4 * 8) {
                 float4 xv[4][2];
 #pragma unroll
@@ -441,7 +494,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
                     if (it < items) {
                         const int t = it / nslots, slot = it - t * nslots;
                         const float4* xr = reinterpret_cast<const float4*>(
-                                               x + (static_cast<int64_t>(t) * nblk + (b_first + slot) % nblk) * 256) +
+                                               x + (static_cast<int64_t>(t) * nblk + (sbase + slot) % nblk) * 256) +
                                            2 * lane;
                         xv[k][0] = __ldg(xr);
                         xv[k][1] = __ldg(xr + 1);
@@ -461,8 +514,36 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
             if (lane == 0) fh3::mbar_arrive(B.bfull);
         }
         bool ok = wait_all(B.bfull, 0);  // every warp's sub-block sums and scales
-        // end of this run's segment of `tile`: the pair's sums, then y or partials + count
-        auto finish_segment = [&](int64_t tile) -> bool {
+        // One chunk only: the run's last tile, when split.  If, two units before the run
+        // ends, every other segment has already counted itself, this segment is the last
+        // one; the others' partials are read then, off the critical path (no CTA ever waits
+        // for another).
+        constexpr int kPre = kOneChunk ? kGtPreSegs : 1;
+        const int64_t t_last = p_last.tile;
+        int cf_last = 0;
+        const int nseg_last = kOneChunk ? piece_ctas(0, t_last, cf_last) : 0;
+        const int seg_last = static_cast<int>(blockIdx.x) - cf_last;
+        bool pre = false;
+        float pv[kPre][M];
+        auto try_prefetch = [&]() {
+            if (part != 0 || nseg_last < 2 || nseg_last > kGtPreSegs + 1 || nseg_last > seg_max) return;
+            int cnt = 0;
+            if (lane == 0)
+                asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(cnt) : "l"(counters + t_last * 4 + q) : "memory");
+            cnt = __shfl_sync(0xffffffffu, cnt, 0);
+            if (cnt != nseg_last - 1) return;
+            const float* pt = partials + (t_last * seg_max * kGtRows + r) * M;
+#pragma unroll
+            for (int k = 0; k < kPre; ++k) {
+                const int sg = k < seg_last ? k : k + 1;
+#pragma unroll
+                for (int t = 0; t < M; ++t)
+                    pv[k][t] = sg < nseg_last ? __ldcg(pt + static_cast<int64_t>(sg) * kGtRows * M + t) : 0.0f;
+            }
+            pre = true;
+        };
+        // end of this run's piece of `tile` in chunk k: the pair's sums, then y or partials + count
+        auto finish_piece = [&](int64_t tile, int k) -> bool {
             if (part == 1) {
                 if (fc >= 1 && !wait_all(&B.xempty[q], (fc - 1) & 1)) return false;
 #pragma unroll
@@ -475,33 +556,39 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
                 for (int t = 0; t < M; ++t) acc[t] += red[t];
                 __syncwarp();
                 if (lane == 0) fh3::mbar_arrive(&B.xempty[q]);
-                const int64_t cf = gt_cta_of(tile * nblk, G, units);
-                const int64_t cl = gt_cta_of((tile + 1) * nblk - 1, G, units);
-                const int nseg = static_cast<int>(cl - cf + 1);
+                // the tile's contributions: one piece per chunk, each split between the CTAs
+                // its units fall in; contribution (kk, j) has partial slot kk * split + j
+                int total = 0;
+                for (int kk = 0; kk < nch; ++kk) {
+                    int cfk;
+                    total += piece_ctas(kk, tile, cfk);
+                }
+                int cf;
+                piece_ctas(k, tile, cf);
+                const int idx = k * split + (static_cast<int>(blockIdx.x) - cf);
                 const int64_t row = tile * kGtRows + r;
-                if (nseg == 1) {
+                if (total == 1) {
                     if (row < N) {
                         const float bv = bias ? bias[row] : 0.0f;
 #pragma unroll
                         for (int t = 0; t < M; ++t) y[t * ldy + row] = acc[t] + bv;
                     }
-                } else if (nseg > seg_max) {
+                } else if (idx >= seg_max || (kOneChunk && total > seg_max)) {
                     if (lane == 0) fh3::record_status(status, FH3_ERR);  // never write past the slots
-                } else if (pre && tile == t_last) {
+                } else if (kOneChunk && pre && tile == t_last) {
                     // every other segment had arrived when checked: this one is the last, and
                     // their partials are already in registers
-                    const int seg = static_cast<int>(blockIdx.x - cf);
                     float v[M];
 #pragma unroll
                     for (int t = 0; t < M; ++t) v[t] = 0.0f;
 #pragma unroll
-                    for (int sg = 0; sg < kGtPreSegs + 1; ++sg) {
-                        if (sg >= nseg) break;
+                    for (int sg = 0; sg < kPre + 1; ++sg) {
+                        if (sg >= total) break;
 #pragma unroll
                         for (int t = 0; t < M; ++t) {
-                            const float lo = pv[sg < kGtPreSegs ? sg : kGtPreSegs - 1][t];  // segment sg < seg
-                            const float hi = pv[sg > 0 ? sg - 1 : 0][t];                     // segment sg > seg
-                            v[t] += sg == seg ? acc[t] : (sg < seg ? lo : hi);
+                            const float lo = pv[sg < kPre ? sg : kPre - 1][t];  // segment sg < idx
+                            const float hi = pv[sg > 0 ? sg - 1 : 0][t];        // segment sg > idx
+                            v[t] += sg == idx ? acc[t] : (sg < idx ? lo : hi);
                         }
                     }
                     if (row < N) {
@@ -512,28 +599,33 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
                     __syncwarp();
                     if (lane == 0) counters[tile * 4 + q] = 0;
                 } else {
-                    const int seg = static_cast<int>(blockIdx.x - cf);
-                    float* pp = partials + ((tile * seg_max + seg) * kGtRows + r) * M;
+                    float* pp = partials + ((tile * seg_max + idx) * kGtRows + r) * M;
 #pragma unroll
                     for (int t = 0; t < M; ++t) pp[t] = acc[t];
                     // the warp's stores, then lane 0's release/acquire count on the counter of
-                    // (tile, quarter): it publishes them at GPU scope and, for the last segment,
-                    // acquires the other segments' stores of these 32 rows
+                    // (tile, quarter): it publishes them at GPU scope and, for the last piece,
+                    // acquires the other pieces' stores of these 32 rows
                     __syncwarp();
                     int old = 0;
                     int* ctr = counters + tile * 4 + q;
                     if (lane == 0)
                         asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
                     old = __shfl_sync(0xffffffffu, old, 0);
-                    if (old == nseg - 1) {  // last segment: add all in run order
+                    if (old == total - 1) {  // last piece: add all in (chunk, CTA) order
                         __syncwarp();
                         const float* pt = partials + (tile * seg_max * kGtRows + r) * M;
                         float v[M];
 #pragma unroll
                         for (int t = 0; t < M; ++t) v[t] = 0.0f;
-                        for (int sg = 0; sg < nseg; ++sg)
+                        for (int kk = 0; kk < nch; ++kk) {
+                            int cfk;
+                            const int nk = piece_ctas(kk, tile, cfk);
+                            for (int j = 0; j < nk; ++j) {
+                                const float* ps = pt + static_cast<int64_t>(kk * split + j) * kGtRows * M;
 #pragma unroll
-                            for (int t = 0; t < M; ++t) v[t] += __ldcg(pt + static_cast<int64_t>(sg) * kGtRows * M + t);
+                                for (int t = 0; t < M; ++t) v[t] += __ldcg(ps + t);
+                            }
+                        }
                         if (row < N) {
                             const float bv = bias ? bias[row] : 0.0f;
 #pragma unroll
@@ -548,18 +640,20 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
             ++fc;
             return true;
         };
-        int64_t tile = u0 / nblk;
-        int b = b_first, slot = 0;  // super-block and B slot of unit i
+        UnitPos ep = p_first;  // unit i
         for (int i = 0; i < n && ok; ++i) {
-            const int hs = i % kGtHdrs, d = i & 1;
-            if (i == max(0, n - 2)) try_prefetch();
+            const int hs = i % kGtHdrs, d = i % C::DB;
+            if constexpr (kOneChunk) {
+                if (i == max(0, n - 2)) try_prefetch();
+            }
             // the row's header: d, dmin, the 6-bit scales and mins
             if (!wait_all(&B.hfull[hs], (i / kGtHdrs) & 1)) break;
-            const uint4 hd = lds128(smem + OFF_HDR + (hs * kGtRows + r) * 16);
+            const uint4 hd = lds128(smem + C::OFF_HDR + (hs * kGtRows + r) * 16);
             __syncwarp();
             if (lane == 0) fh3::mbar_arrive(&B.hempty[hs]);
-            if (!wait_all(&B.dfull[d], (i >> 1) & 1)) break;
+            if (!wait_all(&B.dfull[d], (i / C::DB) & 1)) break;
             fh3::tc_fence_after();
+            const int slot = slot_of(ep.b);
             const float dd = fh3::h2f_bits(hd.x), dmin = fh3::h2f_bits(hd.x >> 16);
             float sum[M], msum[M];
 #pragma unroll
@@ -568,7 +662,8 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
             for (int j0 = 0; j0 < 4; j0 += JB) {  // JB sub-blocks' accumulators in registers at a time
                 uint32_t v[JB][W];
 #pragma unroll
-                for (int jj = 0; jj < JB; ++jj) tmem_ld_w<W>(tl + 128 * d + 16 * (4 * part + j0 + jj), v[jj]);
+                for (int jj = 0; jj < JB; ++jj)
+                    tmem_ld_w<W>(tl + C::DCOLS * d + C::NC * (4 * part + j0 + jj), v[jj]);
                 fh3::tmem_ld_wait();
 #pragma unroll
                 for (int jj = 0; jj < JB; ++jj) fh3::tmem_regs_ready(v[jj]);
@@ -595,19 +690,15 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(
             }
 #pragma unroll
             for (int t = 0; t < M; ++t) acc[t] = fmaf(sfs[slot * M + t], sum[t], acc[t]) - msum[t];
-            if (b == nblk - 1 || i == n - 1)
-                if (!finish_segment(tile)) break;
-            if (++b == nblk) {
-                b = 0;
-                ++tile;
-            }
-            slot = slot + 1 == nblk ? 0 : slot + 1;
+            if (ep.b == ep.k * cw + ep.w - 1 || i == n - 1)
+                if (!finish_piece(ep.tile, ep.k)) break;
+            unit_next(ep, ntiles, nblk, cw);
         }
     }
 
     fh3::tc_fence_before();
     __syncthreads();
-    if (warp == kWarpMma) {
+    if (warp == C::WARP_MMA) {
         fh3::tc_fence_after();
         fh3::tmem_dealloc(tmem, kGtTmemCols);
     }
@@ -620,72 +711,110 @@ cudaLaunchAttribute pdl_attr() {
     return a;
 }
 
+struct GtLaunch {
+    int nblk, ntiles, cw, split, seg_max, grid;
+    int64_t N, units;
+};
+
 template <int M>
-int launch_tc(const CUtensorMap& tm, int nblk, int64_t N, int64_t units, int seg_max, int grid, const float* x,
-              const float* bias, float* y, float* partials, int* counters, int* status, cudaStream_t s) {
+int launch_tc(const CUtensorMap& tm, const GtLaunch& L, const float* x, const float* bias, float* y,
+              float* partials, int* counters, int* status, cudaStream_t s) {
+    constexpr int smem = GtCfg<M>::SMEM;
     static bool attr = false;
     if (!attr) {
         const int rc = fh3host::check_cuda(
-            cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGtSmem),
+            cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
             "gemv_tc_kernel smem attribute");
         if (rc) return rc;
         attr = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-    cfg.blockDim = dim3(kGtThreads, 1, 1);
-    cfg.dynamicSmemBytes = kGtSmem;
+    cfg.gridDim = dim3(static_cast<unsigned>(L.grid), 1, 1);
+    cfg.blockDim = dim3(GtCfg<M>::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute at[1] = {pdl_attr()};
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return fh3host::check_cuda(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M>, tm, nblk, N, units, seg_max, x, bias, y,
-                                                  N, partials, counters, status),
+    return fh3host::check_cuda(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M>, tm, L.nblk, L.ntiles, L.N, L.units, L.cw,
+                                                  L.split, L.seg_max, x, bias, y, L.N, partials, counters, status),
                                "gemv_tc_kernel launch");
+}
+
+template <int M>
+int dispatch_tc(int n_tok, const CUtensorMap& tm, const GtLaunch& L, const float* x, const float* bias, float* y,
+                float* partials, int* counters, int* status, cudaStream_t s) {
+    if constexpr (M > kGtMaxTok) {
+        return 1;
+    } else {
+        if (n_tok == M) return launch_tc<M>(tm, L, x, bias, y, partials, counters, status, s);
+        return dispatch_tc<M + 1>(n_tok, tm, L, x, bias, y, partials, counters, status, s);
+    }
+}
+
+// super-blocks of a chunk for n_tok tokens (0: one chunk over the whole K), and the B slots
+int gt_chunk(int n_tok) {
+    switch (n_tok <= 5 ? 5 : (n_tok <= 10 ? 10 : 16)) {
+        case 5: return 0;
+        case 10: return GtCfg<10>::CHUNK;
+        default: return GtCfg<16>::CHUNK;
+    }
+}
+int gt_slots(int n_tok) {
+    return n_tok <= 5 ? GtCfg<5>::SLOTS : (n_tok <= 10 ? GtCfg<10>::SLOTS : GtCfg<16>::SLOTS);
 }
 
 }  // namespace
 
 namespace fh3host {
 
-// 1..5-token Q4_K GEMV on tcgen05 integer MMAs; returns 1 (nothing launched) when the
+// 1..16-token Q4_K GEMV on tcgen05 integer MMAs; returns 1 (nothing launched) when the
 // shape or the pointers do not suit it, so the caller takes the warp-MMA kernels.
 int gemv_tc(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s) {
     DevCtx* c = ctx();
     if (!c) return set_error(FH3CUDA_E_NODEV, "gemv_tc: call fh3cuda_init first");
     if (n_tok < 1 || n_tok > kGtMaxTok) return 1;
     if ((reinterpret_cast<uintptr_t>(w->data) & 15) || (reinterpret_cast<uintptr_t>(x) & 15)) return 1;
-    const int64_t N = w->out, K = w->in;
-    const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
-    const int64_t ntiles = (N + kGtRows - 1) / kGtRows;
-    const int64_t units = ntiles * nblk;
-    const int grid = static_cast<int>(std::min<int64_t>(ctx_sms(c), units));
-    const int64_t per = units / grid;  // >= 1
-    const int64_t run_max = (units + grid - 1) / grid;
-    if (std::min<int64_t>(nblk, run_max) > kGtSlotsMax) return 1;
-    const int seg_max = static_cast<int>(std::min<int64_t>(nblk, (nblk + per - 1) / per + 1));
-    float* partials =
-        static_cast<float*>(scratch(c, 14, static_cast<size_t>(ntiles) * seg_max * kGtRows * n_tok * 4, s));
-    int* counters = static_cast<int*>(scratch_zeroed(c, 15, static_cast<size_t>(ntiles) * 4 * 4, s));  // (tile, warp)
+    GtLaunch L;
+    L.N = w->out;
+    const int64_t K = w->in;
+    L.nblk = static_cast<int>(K / fh3::kQ4KBlock);
+    const int64_t ntiles = (L.N + kGtRows - 1) / kGtRows;
+    L.ntiles = static_cast<int>(ntiles);
+    L.units = ntiles * L.nblk;
+    L.grid = static_cast<int>(std::min<int64_t>(ctx_sms(c), L.units));
+    if (L.units * L.grid >= (int64_t(1) << 32)) return 1;  // unit -> CTA arithmetic is 32-bit
+    const int64_t per = L.units / L.grid;  // >= 1
+    const int64_t run_max = (L.units + L.grid - 1) / L.grid;
+    const int chunk = gt_chunk(n_tok);
+    if (chunk == 0) {
+        // one chunk: a run's super-blocks, cyclically, must fit the B slots
+        if (std::min<int64_t>(L.nblk, run_max) > gt_slots(n_tok)) return 1;
+        L.cw = L.nblk;
+        L.split = static_cast<int>(std::min<int64_t>(L.nblk, (L.nblk + per - 1) / per + 1));
+        L.seg_max = L.split;
+    } else {
+        // chunks: a run must touch at most two of them (2 * chunk <= slots)
+        L.cw = std::min(L.nblk, chunk);
+        if (ntiles * L.cw < run_max) return 1;
+        L.split = static_cast<int>(std::min<int64_t>(L.grid, (L.cw + per - 1) / per + 1));
+        L.seg_max = (L.nblk + L.cw - 1) / L.cw * L.split;
+    }
+    float* partials = static_cast<float*>(
+        scratch(c, 14, static_cast<size_t>(ntiles) * L.seg_max * kGtRows * n_tok * 4, s));
+    int* counters = static_cast<int*>(scratch_zeroed(c, 15, static_cast<size_t>(ntiles) * 4 * 4, s));  // (tile, quarter)
     if (!partials || !counters) return FH3_E_NOMEM;
 
     CUtensorMap tm;
-    const size_t row_bytes = static_cast<size_t>(nblk) * fh3::kQ4KBytes;
-    const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(N)};
+    const size_t row_bytes = static_cast<size_t>(L.nblk) * fh3::kQ4KBytes;
+    const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(L.N)};
     const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(row_bytes)};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(fh3::kQ4KBytes), static_cast<cuuint32_t>(kGtRows)};
     const cuuint32_t es[2] = {1, 1};
     if (encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w->data), gdim, gstr, box, es,
                      CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
         return 1;
-    int* st = ctx_status(c);
-    switch (n_tok) {
-        case 1: return launch_tc<1>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
-        case 2: return launch_tc<2>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
-        case 3: return launch_tc<3>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
-        case 4: return launch_tc<4>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
-        default: return launch_tc<5>(tm, nblk, N, units, seg_max, grid, x, bias, y, partials, counters, st, s);
-    }
+    return dispatch_tc<1>(n_tok, tm, L, x, bias, y, partials, counters, ctx_status(c), s);
 }
 
 }  // namespace fh3host

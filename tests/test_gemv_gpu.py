@@ -27,8 +27,8 @@ def gemv_path(request):
 
 @pytest.fixture(autouse=True, params=["default", "tc", "mma-stream", "mma-cta", "fp32"])
 def gemv_kernel(request, monkeypatch):
-    """...and on every GEMV kernel: the default choice (tcgen05 integer MMAs for 1..5
-    tokens when out <= in or at 5 tokens, warp-level MMAs otherwise), the tcgen05 kernel forced for every
+    """...and on every GEMV kernel: the default choice (tcgen05 integer MMAs when out <= in
+    or from 5 tokens on, warp-level MMAs otherwise), the tcgen05 kernel forced for every
     shape ("tc"), the warp-MMA kernels ("mma-stream": persistent stream-K for 1..2 tokens,
     CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile) and the fp32 CUDA-core kernel
     (FH3CUDA_GEMV_KERNEL=fp32)."""
@@ -128,7 +128,7 @@ def test_split_tiles_repeat_bitwise(fh3, oracle):
     import torch
     K, N = 13824, 1000
     ws = [fh3.Q4KWeight.from_bytes(oracle.make_weights(seed=20 + i, stream=1, rows=N, n=K), K, N) for i in range(2)]
-    for M in (1, 3, 5):
+    for M in (1, 3, 5, 8, 16):
         x = torch.from_numpy(oracle.rng_normal(21, M, M * K).reshape(M, K).astype(np.float32)).cuda()
         runs = []
         for r in range(3):
@@ -147,7 +147,7 @@ def test_fresh_weight_buffers_first_call(fh3, oracle):
     import torch
     K, N = 13824, 5120
     w = oracle.make_weights(seed=K + N, stream=1, rows=N, n=K)
-    for M in (3, 5):
+    for M in (3, 5, 9, 16):
         x = oracle.rng_normal(M + 7, 2, M * K).reshape(M, K).astype(np.float32)
         ref = oracle.matmul(Q4K, w, K, N, x)
         keep = []
