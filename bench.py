@@ -350,7 +350,7 @@ GEMV_SHAPES = ((5120, 13824), (13824, 5120), (5120, 5120))   # (in, out): fc-up,
 
 def gemv_kernel_name(K: int, N: int, M: int) -> str:
     """The kernel the default GEMV dispatch (csrc/gemv_mma.cu, gemv_mma) picks."""
-    if M <= 5 and (N <= K or M == 5):
+    if N <= K or M >= 5:
         return "gemv_tc_kernel"
     if M <= 2:
         return "gemv_stream_kernel"
