@@ -123,8 +123,9 @@ def matmul(w: Q4KWeight, x, bias=None, out=None, stream=None):
 
 
 def gemv(w: Q4KWeight, x, bias=None, out=None, stream=None):
-    """Q4_K GEMV for 1..16 tokens (fh3cuda_gemv_q4k_dev): tensor-core kernels by default,
-    the fp32 CUDA-core kernel with FH3CUDA_GEMV_KERNEL=fp32."""
+    """Q4_K GEMV for 1..16 tokens (fh3cuda_gemv_q4k_dev): tensor-core kernels by default
+    (tcgen05 integer MMAs when out <= in or from 5 tokens, warp-level MMAs otherwise);
+    FH3CUDA_GEMV_KERNEL=tc | mma-stream | mma-cta | fp32 selects one."""
     torch = _torch()
     _ensure(x)
     n_tok = x.shape[0]
