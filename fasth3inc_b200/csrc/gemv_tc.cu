@@ -655,41 +655,79 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
             fh3::tc_fence_after();
             const int slot = slot_of(ep.b);
             const float dd = fh3::h2f_bits(hd.x), dmin = fh3::h2f_bits(hd.x >> 16);
-            float sum[M], msum[M];
+            if constexpr (M <= 5) {
+                float sum[M], msum[M];
 #pragma unroll
-            for (int t = 0; t < M; ++t) sum[t] = msum[t] = 0.0f;
+                for (int t = 0; t < M; ++t) sum[t] = msum[t] = 0.0f;
 #pragma unroll
-            for (int j0 = 0; j0 < 4; j0 += JB) {  // JB sub-blocks' accumulators in registers at a time
-                uint32_t v[JB][W];
+                for (int j0 = 0; j0 < 4; j0 += JB) {  // JB sub-blocks' accumulators in registers at a time
+                    uint32_t v[JB][W];
 #pragma unroll
-                for (int jj = 0; jj < JB; ++jj)
-                    tmem_ld_w<W>(tl + C::DCOLS * d + C::NC * (4 * part + j0 + jj), v[jj]);
-                fh3::tmem_ld_wait();
+                    for (int jj = 0; jj < JB; ++jj)
+                        tmem_ld_w<W>(tl + C::DCOLS * d + C::NC * (4 * part + j0 + jj), v[jj]);
+                    fh3::tmem_ld_wait();
 #pragma unroll
-                for (int jj = 0; jj < JB; ++jj) fh3::tmem_regs_ready(v[jj]);
-                if (j0 + JB == 4) {  // every column of this buffer is read
-                    fh3::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) fh3::mbar_arrive(&B.dempty[d]);
-                }
+                    for (int jj = 0; jj < JB; ++jj) fh3::tmem_regs_ready(v[jj]);
+                    if (j0 + JB == 4) {  // every column of this buffer is read
+                        fh3::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) fh3::mbar_arrive(&B.dempty[d]);
+                    }
 #pragma unroll
-                for (int jj = 0; jj < JB; ++jj) {
-                    const int j = 4 * part + j0 + jj;
-                    int sc, m;
-                    fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, j, sc, m);
-                    const float dsc = dd * small_i2f(static_cast<uint32_t>(sc));
-                    const float dm = dmin * small_i2f(static_cast<uint32_t>(m));
+                    for (int jj = 0; jj < JB; ++jj) {
+                        const int j = 4 * part + j0 + jj;
+                        int sc, m;
+                        fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, j, sc, m);
+                        const float dsc = dd * small_i2f(static_cast<uint32_t>(sc));
+                        const float dm = dmin * small_i2f(static_cast<uint32_t>(m));
 #pragma unroll
-                    for (int t = 0; t < M; ++t) {
-                        const float p = fmaf(65536.0f, small_i2f(v[jj][3 * t + 2]),
-                                             fmaf(256.0f, small_i2f(v[jj][3 * t + 1]), small_i2f(v[jj][3 * t])));
-                        sum[t] = fmaf(dsc, p, sum[t]);
-                        msum[t] = fmaf(dm, sx[(slot * M + t) * 8 + j], msum[t]);
+                        for (int t = 0; t < M; ++t) {
+                            const float p = fmaf(65536.0f, small_i2f(v[jj][3 * t + 2]),
+                                                 fmaf(256.0f, small_i2f(v[jj][3 * t + 1]), small_i2f(v[jj][3 * t])));
+                            sum[t] = fmaf(dsc, p, sum[t]);
+                            msum[t] = fmaf(dm, sx[(slot * M + t) * 8 + j], msum[t]);
+                        }
                     }
                 }
-            }
 #pragma unroll
-            for (int t = 0; t < M; ++t) acc[t] = fmaf(sfs[slot * M + t], sum[t], acc[t]) - msum[t];
+                for (int t = 0; t < M; ++t) acc[t] = fmaf(sfs[slot * M + t], sum[t], acc[t]) - msum[t];
+            } else {
+                // 6..16 tokens: the 6-bit scales applied in integers, S_tp = sum over this part's
+                // four sub-blocks of sc_j * P_tjp (|S| <= 4 * 63 * 61440 < 2^24: exact, and exactly
+                // convertible), so each token costs three conversions a unit instead of twelve;
+                // the min term is subtracted from the accumulator directly
+                int S[M][3];
+#pragma unroll
+                for (int t = 0; t < M; ++t) S[t][0] = S[t][1] = S[t][2] = 0;
+#pragma unroll
+                for (int j0 = 0; j0 < 4; ++j0) {
+                    uint32_t v[W];
+                    tmem_ld_w<W>(tl + C::DCOLS * d + C::NC * (4 * part + j0), v);
+                    fh3::tmem_ld_wait();
+                    fh3::tmem_regs_ready(v);
+                    if (j0 == 3) {  // every column of this buffer is read
+                        fh3::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) fh3::mbar_arrive(&B.dempty[d]);
+                    }
+                    const int j = 4 * part + j0;
+                    int sc, m;
+                    fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, j, sc, m);
+                    const float ndm = -(dmin * small_i2f(static_cast<uint32_t>(m)));
+#pragma unroll
+                    for (int t = 0; t < M; ++t) {
+#pragma unroll
+                        for (int p = 0; p < 3; ++p) S[t][p] += sc * static_cast<int>(v[3 * t + p]);
+                        acc[t] = fmaf(ndm, sx[(slot * M + t) * 8 + j], acc[t]);
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < M; ++t) {
+                    const float p = fmaf(65536.0f, __int2float_rn(S[t][2]),
+                                         fmaf(256.0f, __int2float_rn(S[t][1]), __int2float_rn(S[t][0])));
+                    acc[t] = fmaf(dd * sfs[slot * M + t], p, acc[t]);  // 2^-s is a power of two: exact
+                }
+            }
             if (ep.b == ep.k * cw + ep.w - 1 || i == n - 1)
                 if (!finish_piece(ep.tile, ep.k)) break;
             unit_next(ep, ntiles, nblk, cw);
