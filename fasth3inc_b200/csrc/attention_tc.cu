@@ -20,6 +20,8 @@
 // timeout the roles stop, the MMAs issued so far retire before TMEM is freed, and the
 // producer lets its copies in flight land.  No TMA multicast.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -346,6 +348,318 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
 
 }  // namespace
 
+namespace {
+
+// ---------------------------------------------------------------------------
+// Two query tiles a CTA (ping-pong).  A CTA owns 256 query rows of one head: tiles A and
+// B of 128 rows, each with its own softmax warpgroup, TMEM score tile and TMEM output
+// tile (S_A 0, S_B 128, O_A 256, O_B 384).  A group writes P_j as bf16 pairs into the
+// first 64 columns of its score tile, and O += P_j V_j takes P from tensor memory.  MMA
+// issue order per key tile: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): the tensor cores run
+// one group's products while the other group's softmax runs, and every S commit also
+// covers the PV that read the same columns before.
+// Warps: 0 TMA producer, 1 TMEM owner and MMA issuer, 2-5 group A, 6-9 group B.
+// ---------------------------------------------------------------------------
+constexpr int kPpRows = 256;
+constexpr int PP_OFF_QA = 0;
+constexpr int PP_OFF_QB = PP_OFF_QA + kTile;
+constexpr int PP_OFF_KV = PP_OFF_QB + kTile;           // 2 stages x (K tile, V^T tile)
+constexpr int PP_OFF_BAR = PP_OFF_KV + 2 * 2 * kTile;
+// q_full, kv_full[2], kv_empty[2], s_full[2 groups], p_full[2 groups], o_full[2 groups], drain
+constexpr int kPpBars = 1 + 2 + 2 + 2 + 2 + 2 + 1;
+constexpr int PP_OFF_MISC = PP_OFF_BAR + kPpBars * 8;
+constexpr int kPpSmem = PP_OFF_MISC + 64 + 1024;
+constexpr int kPpThreads = 10 * 32;
+static_assert(kPpSmem <= 232448, "shared memory budget");
+
+struct PpBars {
+    uint64_t *q_full, *kv_full, *kv_empty, *s_full, *p_full, *o_full, *drain;
+};
+__device__ __forceinline__ PpBars pp_bars(uint8_t* smem) {
+    uint64_t* b = reinterpret_cast<uint64_t*>(smem + PP_OFF_BAR);
+    PpBars x;
+    x.q_full = b;
+    x.kv_full = b + 1;
+    x.kv_empty = b + 3;
+    x.s_full = b + 5;  // [group]
+    x.p_full = b + 7;  // [group]
+    x.o_full = b + 9;  // [group]
+    x.drain = b + 11;
+    return x;
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16 with A in tensor memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(kPpThreads, 1) attention_pp_kernel(
+    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    const __grid_constant__ CUtensorMap tmVt, void* __restrict__ o, int64_t ldo, int n, float scale_log2,
+    int* status) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const PpBars B = pp_bars(smem);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PP_OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + PP_OFF_MISC + 8);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.y;
+    const int q0 = blockIdx.x * kPpRows;
+    const int T = (n + kTcKeys - 1) / kTcKeys;
+
+    if (threadIdx.x == 0) {
+        fh3::mbar_init(B.q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            fh3::mbar_init(&B.kv_full[i], 1);
+            fh3::mbar_init(&B.kv_empty[i], 1);
+            fh3::mbar_init(&B.s_full[i], 1);
+            fh3::mbar_init(&B.p_full[i], 4);
+            fh3::mbar_init(&B.o_full[i], 1);
+        }
+        fh3::mbar_init(B.drain, 1);
+        *abort_flag = 0;
+        fh3::fence_mbar_init();
+    }
+    if (warp == 1) {
+        fh3::tmem_alloc(tmem_slot, kTmemCols);
+        fh3::tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        fh3::tma_prefetch_desc(&tmQ);
+        fh3::tma_prefetch_desc(&tmK);
+        fh3::tma_prefetch_desc(&tmVt);
+    }
+    fh3::tc_fence_before();
+    __syncthreads();
+    fh3::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t filled = 0, par = 0;
+            fh3::mbar_arrive_expect_tx(B.q_full, 2 * kTile);
+            for (int c = 0; c < 2; ++c) {
+                fh3::tma_load_2d(smem + PP_OFF_QA + c * kBlk, &tmQ, B.q_full, h * kTcHD + c * 64, q0);
+                fh3::tma_load_2d(smem + PP_OFF_QB + c * kBlk, &tmQ, B.q_full, h * kTcHD + c * 64, q0 + kTcRows);
+            }
+            bool ok = true;
+            for (int j = 0; j < T && ok; ++j) {
+                const int st = j & 1;
+                if (!(ok = fh3::mbar_wait<true>(&B.kv_empty[st], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
+                uint8_t* kvb = smem + PP_OFF_KV + st * 2 * kTile;
+                fh3::mbar_arrive_expect_tx(&B.kv_full[st], 2 * kTile);
+                for (int c = 0; c < 2; ++c) {
+                    fh3::tma_load_2d(kvb + c * kBlk, &tmK, &B.kv_full[st], h * kTcHD + c * 64, j * kTcKeys);
+                    fh3::tma_load_2d(kvb + kTile + c * kBlk, &tmVt, &B.kv_full[st], j * kTcKeys + c * 64, h * kTcHD);
+                }
+                filled |= 1u << st;
+                par = (par & ~(1u << st)) | (static_cast<uint32_t>((j >> 1) & 1) << st);
+            }
+            volatile int no_abort = 0;
+            fh3::mbar_wait<true>(B.q_full, 0, &no_abort, nullptr);  // Q lands before the CTA can leave
+            if (!ok)
+                for (int i = 0; i < 2; ++i)
+                    if (filled & (1u << i)) fh3::mbar_wait<true>(&B.kv_full[i], (par >> i) & 1u, &no_abort, nullptr);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = fh3::idesc_bf16_f32(128, 128);
+            bool ok = fh3::mbar_wait<true>(B.q_full, 0, abort_flag, status);
+            // S_g(j) = Q_g K_j^T into the group's score tile
+            auto qk = [&](int g, int j) {
+                const uint32_t qa = fh3::smem_u32(smem + (g ? PP_OFF_QB : PP_OFF_QA));
+                const uint32_t ka = fh3::smem_u32(smem + PP_OFF_KV + (j & 1) * 2 * kTile);
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        fh3::umma_f16(tmem + 128 * g, fh3::sdesc_sw128(qa + c * kBlk) + 2 * kk,
+                                      fh3::sdesc_sw128(ka + c * kBlk) + 2 * kk, idesc, (c | kk) != 0 ? 1u : 0u);
+                fh3::umma_commit(&B.s_full[g]);
+            };
+            // O_g += P_g(j) V_j, P_g in the first 64 columns of the score tile (bf16 pairs)
+            auto pv = [&](int g, int j) {
+                const uint32_t va = fh3::smem_u32(smem + PP_OFF_KV + (j & 1) * 2 * kTile + kTile);
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_f16_ts(tmem + 256 + 128 * g, tmem + 128 * g + 32 * c + 8 * kk,
+                                    fh3::sdesc_sw128(va + c * kBlk) + 2 * kk, idesc, (j | c | kk) != 0 ? 1u : 0u);
+            };
+            if (ok && (ok = fh3::mbar_wait<true>(&B.kv_full[0], 0, abort_flag, status))) {
+                fh3::tc_fence_after();
+                qk(0, 0);
+                qk(1, 0);
+            }
+            for (int j = 0; j < T && ok; ++j) {
+                const bool more = j + 1 < T;
+                if (more && !(ok = fh3::mbar_wait<true>(&B.kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag,
+                                                        status)))
+                    break;
+                for (int g = 0; g < 2 && ok; ++g) {
+                    if (!(ok = fh3::mbar_wait<true>(&B.p_full[g], j & 1, abort_flag, status))) break;
+                    fh3::tc_fence_after();
+                    pv(g, j);
+                    if (g == 1) fh3::umma_commit(&B.kv_empty[j & 1]);  // K_j and V_j are both consumed
+                    if (more) qk(g, j + 1);
+                    else fh3::umma_commit(&B.o_full[g]);
+                }
+            }
+            fh3::umma_commit(B.drain);  // every MMA issued retires before TMEM is freed
+            volatile int no_abort = 0;
+            fh3::mbar_wait<true>(B.drain, 0, &no_abort, nullptr);
+        }
+    } else {
+        // ------------------------------------------------------------ softmax and epilogue
+        // group g = (warp - 2) / 4 owns tile g; P_j = 2^(s - m_ref) against a reference max
+        // raised only when a tile's max exceeds it by more than 2^8 (then the row of O in
+        // TMEM and the row sum are rescaled once).  S_g(j) is committed after PV_g(j-1), so
+        // when it is visible the previous P has been consumed and O_g is up to date.
+        const int g = (warp - 2) >> 2;
+        const int qw = warp & 3;  // TMEM lanes 32*qw .. 32*qw+31 belong to this warp
+        const int r = qw * 32 + lane;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(qw * 32) << 16);
+        const uint32_t ts = trow + 128 * g, to = trow + 256 + 128 * g;
+        float m_ref = -INFINITY, l = 0.0f;
+        bool ok = true;
+        auto wait_warp = [&](uint64_t* bar, uint32_t parity) {
+            int w = 1;
+            if (lane == 0) w = fh3::mbar_wait<true>(bar, parity, abort_flag, status);
+            return __shfl_sync(0xffffffffu, w, 0) != 0;
+        };
+        for (int j = 0; j < T && ok; ++j) {
+            if (!(ok = wait_warp(&B.s_full[g], j & 1))) break;
+            fh3::tc_fence_after();
+            const int kb = j * kTcKeys;
+            const bool tail = kb + kTcKeys > n;  // keys past n only in the last tile
+            // pass 1: row max of the raw scores (the scale is positive), 64 columns at a time
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t v[2][32];
+#pragma unroll
+                for (int c = 0; c < 2; ++c) fh3::tmem_ld32(ts + 64 * hf + c * 32, v[c]);
+                fh3::tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < 2; ++c) fh3::tmem_regs_ready(v[c]);
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const float x = (tail && kb + 64 * hf + c * 32 + e >= n) ? -INFINITY : __uint_as_float(v[c][e]);
+                        mx4[e & 3] = fmaxf(mx4[e & 3], x);
+                    }
+            }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
+            const bool raise = mx > m_ref + 8.0f;  // always true on the first tile
+            if (j > 0 && __any_sync(0xffffffffu, raise)) {
+                // PV_g(j-1) has landed (S_g(j) was committed after it)
+                const float a = raise ? exp2f(m_ref - mx) : 1.0f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t ov[32];
+                    fh3::tmem_ld32(to + c * 32, ov);
+                    fh3::tmem_ld_wait();
+                    fh3::tmem_regs_ready(ov);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
+                    fh3::tmem_st32(to + c * 32, ov);
+                }
+                l *= a;
+            }
+            if (raise) m_ref = mx;
+            // pass 2: P as bf16 pairs over the consumed columns (keys 64hf.. -> columns 32hf..)
+            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const float nm = -m_ref;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t v[2][32];
+#pragma unroll
+                for (int c = 0; c < 2; ++c) fh3::tmem_ld32(ts + 64 * hf + c * 32, v[c]);
+                fh3::tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < 2; ++c) fh3::tmem_regs_ready(v[c]);
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t pk[16];  // keys 64hf + 32c .. +31 -> columns 32hf + 16c ..
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) {
+                        const int k0 = kb + 64 * hf + 32 * c + 2 * u;
+                        const float s0 = (tail && k0 >= n) ? -INFINITY : __uint_as_float(v[c][2 * u]);
+                        const float s1 = (tail && k0 + 1 >= n) ? -INFINITY : __uint_as_float(v[c][2 * u + 1]);
+                        const float p0 = exp2f(fmaf(s0, scale_log2, nm));
+                        const float p1 = exp2f(fmaf(s1, scale_log2, nm));
+                        rs4[u & 3] += p0 + p1;
+                        const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                        pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                    }
+                    fh3::tmem_st16(ts + 32 * hf + 16 * c, pk);
+                }
+            }
+            fh3::tmem_st_wait();
+            fh3::tc_fence_before();  // this warp's TMEM reads and writes are complete
+            __syncwarp();
+            if (lane == 0) fh3::mbar_arrive(&B.p_full[g]);
+            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+        }
+        if (ok) ok = wait_warp(&B.o_full[g], 0);  // the last PV has landed
+        if (ok) {
+            fh3::tc_fence_after();
+            const int row = q0 + kTcRows * g + r;
+            uint32_t ov[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) fh3::tmem_ld32(to + c * 32, ov[c]);
+            fh3::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) fh3::tmem_regs_ready(ov[c]);
+            if (row < n) {
+                const float inv = 1.0f / l;
+                const int64_t base = static_cast<int64_t>(row) * ldo + static_cast<int64_t>(h) * kTcHD;
+                if (OUT_BF16) {
+                    __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(o) + base;
+#pragma unroll
+                    for (int d = 0; d < kTcHD; d += 8) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int e = d + 2 * u;
+                            const __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(ov[e >> 5][e & 31]) * inv,
+                                                                            __uint_as_float(ov[(e + 1) >> 5][(e + 1) & 31]) * inv);
+                            w[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                        }
+                        *reinterpret_cast<uint4*>(ob + d) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+                    float* of = static_cast<float*>(o) + base;
+#pragma unroll
+                    for (int d = 0; d < kTcHD; d += 4)
+                        *reinterpret_cast<float4*>(of + d) = make_float4(
+                            __uint_as_float(ov[d >> 5][d & 31]) * inv, __uint_as_float(ov[d >> 5][(d & 31) + 1]) * inv,
+                            __uint_as_float(ov[d >> 5][(d & 31) + 2]) * inv, __uint_as_float(ov[d >> 5][(d & 31) + 3]) * inv);
+                }
+            }
+        }
+    }
+
+    fh3::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fh3::tc_fence_after();
+        fh3::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
 namespace fh3host {
 
 // Dense attention on tcgen05 (head_dim 128); arguments validated by fh3cuda_attention_dev.
@@ -373,6 +687,30 @@ int attention_tc(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, in
         enc(&tk, k, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(n), ldk) != CUDA_SUCCESS ||
         enc(&tvt, vt, static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(rows), npad) != CUDA_SUCCESS)
         return set_error(FH3CUDA_E_CUDA, "attention: cuTensorMapEncodeTiled failed");
+    const float scale_log2 = (1.0f / sqrtf(static_cast<float>(kTcHD))) * 1.4426950408889634f;
+    const char* kname = getenv("FH3CUDA_ATTN_KERNEL");
+    if (!(kname && strcmp(kname, "tc1") == 0)) {
+        // two query tiles a CTA (ping-pong); FH3CUDA_ATTN_KERNEL=tc1 keeps one tile a CTA
+        static bool attr_pp = false;
+        if (!attr_pp) {
+            rc = check_cuda(cudaFuncSetAttribute(attention_pp_kernel<false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem),
+                            "attention_pp smem attribute");
+            if (!rc) rc = check_cuda(cudaFuncSetAttribute(attention_pp_kernel<true>,
+                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem),
+                                     "attention_pp smem attribute");
+            if (rc) return rc;
+            attr_pp = true;
+        }
+        const dim3 grid(static_cast<unsigned>((n + kPpRows - 1) / kPpRows), static_cast<unsigned>(heads));
+        if (o_bf16)
+            attention_pp_kernel<true><<<grid, kPpThreads, kPpSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2,
+                                                                       ctx_status(c));
+        else
+            attention_pp_kernel<false><<<grid, kPpThreads, kPpSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2,
+                                                                        ctx_status(c));
+        return check_cuda(cudaGetLastError(), "attention_pp_kernel launch");
+    }
     static bool attr = false;
     if (!attr) {
         rc = check_cuda(cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -383,7 +721,6 @@ int attention_tc(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, in
         if (rc) return rc;
         attr = true;
     }
-    const float scale_log2 = (1.0f / sqrtf(static_cast<float>(kTcHD))) * 1.4426950408889634f;
     const dim3 grid(static_cast<unsigned>((n + kTcRows - 1) / kTcRows), static_cast<unsigned>(heads));
     if (o_bf16)
         attention_tc_kernel<true><<<grid, kTcThreads, kTcSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2, ctx_status(c));

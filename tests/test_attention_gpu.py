@@ -18,14 +18,15 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-2
 
 
-@pytest.fixture(autouse=True, params=["tc", "mma"])
+@pytest.fixture(autouse=True, params=["tc", "tc1", "mma"])
 def attn_kernel(request, monkeypatch):
-    """Every bf16 test on both kernels: tcgen05 with TMEM accumulators (the default) and the
-    mma.sync flash kernel (FH3CUDA_ATTN_KERNEL=mma)."""
-    if request.param == "mma":
-        monkeypatch.setenv("FH3CUDA_ATTN_KERNEL", "mma")
-    else:
+    """Every bf16 test on every kernel: tcgen05 with two query tiles a CTA (the default),
+    tcgen05 with one query tile a CTA (FH3CUDA_ATTN_KERNEL=tc1) and the mma.sync flash
+    kernel (FH3CUDA_ATTN_KERNEL=mma)."""
+    if request.param == "tc":
         monkeypatch.delenv("FH3CUDA_ATTN_KERNEL", raising=False)
+    else:
+        monkeypatch.setenv("FH3CUDA_ATTN_KERNEL", request.param)
     return request.param
 
 
