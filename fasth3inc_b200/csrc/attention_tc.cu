@@ -388,6 +388,14 @@ __device__ __forceinline__ PpBars pp_bars(uint8_t* smem) {
     return x;
 }
 
+// 2^x by the hardware approximation (MUFU; flushes subnormal results to zero, which a
+// softmax weight below 2^-126 may be)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16 with A in tensor memory.
 __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
@@ -551,13 +559,18 @@ __global__ void __launch_bounds__(kPpThreads, 1) attention_pp_kernel(
                 fh3::tmem_ld_wait();
 #pragma unroll
                 for (int c = 0; c < 2; ++c) fh3::tmem_regs_ready(v[c]);
+                if (!tail) {
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
+                    for (int c = 0; c < 2; ++c)
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const float x = (tail && kb + 64 * hf + c * 32 + e >= n) ? -INFINITY : __uint_as_float(v[c][e]);
-                        mx4[e & 3] = fmaxf(mx4[e & 3], x);
-                    }
+                        for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 2; ++c)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (kb + 64 * hf + c * 32 + e < n) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                }
             }
             const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
             const bool raise = mx > m_ref + 8.0f;  // always true on the first tile
@@ -588,16 +601,20 @@ __global__ void __launch_bounds__(kPpThreads, 1) attention_pp_kernel(
                 fh3::tmem_ld_wait();
 #pragma unroll
                 for (int c = 0; c < 2; ++c) fh3::tmem_regs_ready(v[c]);
+                if (tail) {  // keys past n weigh zero
+#pragma unroll
+                    for (int c = 0; c < 2; ++c)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (kb + 64 * hf + 32 * c + e >= n) v[c][e] = __float_as_uint(-INFINITY);
+                }
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
                     uint32_t pk[16];  // keys 64hf + 32c .. +31 -> columns 32hf + 16c ..
 #pragma unroll
                     for (int u = 0; u < 16; ++u) {
-                        const int k0 = kb + 64 * hf + 32 * c + 2 * u;
-                        const float s0 = (tail && k0 >= n) ? -INFINITY : __uint_as_float(v[c][2 * u]);
-                        const float s1 = (tail && k0 + 1 >= n) ? -INFINITY : __uint_as_float(v[c][2 * u + 1]);
-                        const float p0 = exp2f(fmaf(s0, scale_log2, nm));
-                        const float p1 = exp2f(fmaf(s1, scale_log2, nm));
+                        const float p0 = ex2_approx(fmaf(__uint_as_float(v[c][2 * u]), scale_log2, nm));
+                        const float p1 = ex2_approx(fmaf(__uint_as_float(v[c][2 * u + 1]), scale_log2, nm));
                         rs4[u & 3] += p0 + p1;
                         const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                         pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
