@@ -388,14 +388,6 @@ __device__ __forceinline__ PpBars pp_bars(uint8_t* smem) {
     return x;
 }
 
-// 2^x by the hardware approximation (MUFU; flushes subnormal results to zero, which a
-// softmax weight below 2^-126 may be)
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16 with A in tensor memory.
 __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
@@ -613,8 +605,8 @@ __global__ void __launch_bounds__(kPpThreads, 1) attention_pp_kernel(
                     uint32_t pk[16];  // keys 64hf + 32c .. +31 -> columns 32hf + 16c ..
 #pragma unroll
                     for (int u = 0; u < 16; ++u) {
-                        const float p0 = ex2_approx(fmaf(__uint_as_float(v[c][2 * u]), scale_log2, nm));
-                        const float p1 = ex2_approx(fmaf(__uint_as_float(v[c][2 * u + 1]), scale_log2, nm));
+                        const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][2 * u]), scale_log2, nm));
+                        const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][2 * u + 1]), scale_log2, nm));
                         rs4[u & 3] += p0 + p1;
                         const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                         pk[u] = *reinterpret_cast<const uint32_t*>(&pp);

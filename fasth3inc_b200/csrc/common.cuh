@@ -344,6 +344,14 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mas
         : "memory");
 }
 
+// 2^x by the hardware approximation (the MUFU instruction; a result below 2^-126 is
+// flushed to zero, which a softmax weight may be)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // 32 lanes x 32 consecutive fp32 columns (one row per thread).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(

@@ -289,13 +289,20 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
             fh3::tmem_regs_ready(v[0]);
             fh3::tmem_regs_ready(v[1]);
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            if (cnt == 64) {  // a full tile: no masking
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+                for (int c = 0; c < 2; ++c)
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    if (c * 32 + e >= cnt) v[c][e] = __float_as_uint(-INFINITY);  // other tiles' keys, padding
-                    mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
-                }
+                    for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+            } else {
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        if (c * 32 + e >= cnt) v[c][e] = __float_as_uint(-INFINITY);  // other tiles' keys, padding
+                        mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                    }
+            }
             const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
             const bool raise = mx > m_ref + 8.0f;  // false while a half-row has seen no key
             if (cc > 0 && __any_sync(0xffffffffu, raise)) {
@@ -328,8 +335,8 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int e = 8 * t + 2 * u;
-                        const float p0 = exp2f(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
-                        const float p1 = exp2f(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
+                        const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
+                        const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
                         rs4[u] += p0 + p1;
                         const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                         pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
