@@ -21,6 +21,8 @@
 // added and rows are scattered back to token order.  The same roles, barrier protocol
 // and bounded waits as attention_tc.cu.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -421,6 +423,301 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
     }
 }
 
+
+// M = 64 variant (the default): the query tile fills an M = 64 MMA once, so no tensor or
+// softmax work goes to duplicated rows, and one kept tile a step keeps a CTA small (two
+// 32 KB K / V^T stages, 256 TMEM columns) so that two CTAs share an SM and each one's
+// softmax runs while the other waits on its MMAs and loads:
+//   S_j = Q K_j^T     (M 64, N 64, K 128) into one of two TMEM score tiles (columns 0, 64)
+//   P_j               four softmax warps; query row m of an M = 64 MMA sits in TMEM lane
+//                     (m % 16) + 32 (m / 16), so lanes 0..15 of each warp hold a row each
+//   O += P_j V_j      (M 64, N 128, K 64) accumulating in TMEM columns 128..255
+// with the lazy 2^8 reference max of the other kernels and no merge at the end.
+constexpr int kV6Q = 64 * 64 * 2;            // [64][64] bf16 128-byte-swizzle block: 8 KB
+constexpr int kV6S = 2;                      // K / V^T stages
+constexpr int kV6Stage = 2 * kV6Q + kVB;     // K [64 keys][128] + V^T [128][64 keys]: 32 KB
+constexpr int V6_OFF_Q = 0;
+constexpr int V6_OFF_KV = V6_OFF_Q + 2 * kV6Q;
+constexpr int V6_OFF_P = V6_OFF_KV + kV6S * kV6Stage;
+constexpr int V6_OFF_BAR = V6_OFF_P + 2 * kV6Q;
+// q_full, kv_full[kV6S], kv_empty[kV6S], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full, drain
+constexpr int kV6Bars = 1 + 2 * kV6S + 8 + 2;
+constexpr int V6_OFF_MISC = V6_OFF_BAR + kV6Bars * 8;
+constexpr int kV6Smem = V6_OFF_MISC + 64 + 1024;
+constexpr uint32_t kV6TmemCols = 256;  // S0 at 0, S1 at 64, O at 128
+constexpr uint32_t kV6TmemO = 128;
+static_assert(kV6Smem <= 232448, "shared memory budget");
+static_assert(V6_OFF_KV % 1024 == 0 && kV6Stage % 1024 == 0 && V6_OFF_P % 1024 == 0, "swizzle alignment");
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
+    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    const __grid_constant__ CUtensorMap tmVt, const int* __restrict__ perm, const int* __restrict__ toff,
+    const int* __restrict__ poff, const int* __restrict__ sel, const int* __restrict__ selcnt, int nt,
+    const __nv_bfloat16* __restrict__ gate, int64_t ldg, const float* __restrict__ outc, int heads,
+    void* __restrict__ o, int64_t ldo, float scale_log2, int* status) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + V6_OFF_BAR);
+    uint64_t* q_full = bar;
+    uint64_t* kv_full = bar + 1;
+    uint64_t* kv_empty = kv_full + kV6S;
+    uint64_t* s_full = kv_empty + kV6S;
+    uint64_t* s_empty = s_full + 2;
+    uint64_t* p_full = s_empty + 2;
+    uint64_t* p_empty = p_full + 2;
+    uint64_t* o_full = p_empty + 2;
+    uint64_t* drain = o_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + V6_OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + V6_OFF_MISC + 8);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.x, h = blockIdx.y;
+    const size_t rowi = static_cast<size_t>(h) * nt + i;
+    const int* lst = sel + rowi * nt;
+    const int L = selcnt[rowi];               // >= 1
+    const int qrows = toff[i + 1] - toff[i];  // <= 64
+
+    if (threadIdx.x == 0) {
+        fh3::mbar_init(q_full, 1);
+        for (int s = 0; s < kV6S; ++s) {
+            fh3::mbar_init(&kv_full[s], 1);
+            fh3::mbar_init(&kv_empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            fh3::mbar_init(&s_full[s], 1);
+            fh3::mbar_init(&s_empty[s], 4);
+            fh3::mbar_init(&p_full[s], 4);
+            fh3::mbar_init(&p_empty[s], 1);
+        }
+        fh3::mbar_init(o_full, 1);
+        fh3::mbar_init(drain, 1);
+        *abort_flag = 0;
+        fh3::fence_mbar_init();
+    }
+    if (warp == 1) {
+        fh3::tmem_alloc(tmem_slot, kV6TmemCols);
+        fh3::tmem_relinquish();
+    }
+    fh3::tc_fence_before();
+    __syncthreads();
+    fh3::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t filled = 0, par = 0;
+            fh3::mbar_arrive_expect_tx(q_full, 2 * kV6Q);
+            for (int c = 0; c < 2; ++c)
+                fh3::tma_load_2d(smem + V6_OFF_Q + c * kV6Q, &tmQ, q_full, h * 128 + c * 64, poff[i]);
+            bool ok = true;
+            for (int j = 0, st = 0, ph = 0; j < L && ok; ++j) {
+                if (!(ok = fh3::mbar_wait<true>(&kv_empty[st], static_cast<uint32_t>(ph) ^ 1u, abort_flag, status))) break;
+                const int y = poff[lst[j]];
+                uint8_t* sb = smem + V6_OFF_KV + st * kV6Stage;
+                fh3::mbar_arrive_expect_tx(&kv_full[st], kV6Stage);
+                for (int c = 0; c < 2; ++c) fh3::tma_load_2d(sb + c * kV6Q, &tmK, &kv_full[st], h * 128 + c * 64, y);
+                fh3::tma_load_2d(sb + 2 * kV6Q, &tmVt, &kv_full[st], y, h * 128);
+                filled |= 1u << st;
+                par = (par & ~(1u << st)) | (static_cast<uint32_t>(ph) << st);
+                if (++st == kV6S) {
+                    st = 0;
+                    ph ^= 1;
+                }
+            }
+            volatile int no_abort = 0;
+            fh3::mbar_wait<true>(q_full, 0, &no_abort, nullptr);
+            if (!ok)
+                for (int s = 0; s < kV6S; ++s)
+                    if (filled & (1u << s)) fh3::mbar_wait<true>(&kv_full[s], (par >> s) & 1u, &no_abort, nullptr);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = fh3::idesc_bf16_f32(64, 64);
+            constexpr uint32_t idesc_o = fh3::idesc_bf16_f32(64, 128);
+            const uint32_t qa = fh3::smem_u32(smem + V6_OFF_Q);
+            bool ok = fh3::mbar_wait<true>(q_full, 0, abort_flag, status);
+            auto pv = [&](int j) {
+                const int bi = j & 1, st = j % kV6S;
+                if (!(ok = fh3::mbar_wait<true>(&p_full[bi], (j >> 1) & 1, abort_flag, status))) return;
+                fh3::tc_fence_after();
+                const uint32_t pa = fh3::smem_u32(smem + V6_OFF_P + bi * kV6Q);
+                const uint32_t va = fh3::smem_u32(smem + V6_OFF_KV + st * kV6Stage + 2 * kV6Q);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    fh3::umma_f16(tmem + kV6TmemO, fh3::sdesc_sw128(pa) + 2 * kk, fh3::sdesc_sw128(va) + 2 * kk, idesc_o,
+                                  (j | kk) != 0 ? 1u : 0u);
+                fh3::umma_commit(o_full);
+                fh3::umma_commit(&p_empty[bi]);
+                fh3::umma_commit(&kv_empty[st]);
+            };
+            for (int j = 0; j < L && ok; ++j) {
+                const int b = j & 1, st = j % kV6S;
+                if (!(ok = fh3::mbar_wait<true>(&kv_full[st], (j / kV6S) & 1, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(&s_empty[b], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
+                fh3::tc_fence_after();
+                const uint32_t ka = fh3::smem_u32(smem + V6_OFF_KV + st * kV6Stage);
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        fh3::umma_f16(tmem + b * 64, fh3::sdesc_sw128(qa + c * kV6Q) + 2 * kk,
+                                      fh3::sdesc_sw128(ka + c * kV6Q) + 2 * kk, idesc_s, (c | kk) != 0 ? 1u : 0u);
+                fh3::umma_commit(&s_full[b]);
+                if (j >= 1) pv(j - 1);
+            }
+            if (ok) pv(L - 1);
+            fh3::umma_commit(drain);
+            volatile int no_abort = 0;
+            fh3::mbar_wait<true>(drain, 0, &no_abort, nullptr);
+        }
+    } else {
+        // ------------------------------------------------------------ softmax and epilogue (warps 2-5)
+        const int qw = warp & 3;           // TMEM lanes 32*qw .. 32*qw+31; rows 16*qw .. 16*qw+15
+        const bool act = lane < 16;        // lanes 16..31 of the quarter hold no row of an M = 64 MMA
+        const int r = qw * 16 + lane;      // the query row of an active lane
+        const uint32_t trow = tmem + (static_cast<uint32_t>(qw * 32) << 16);
+        float m_ref = -INFINITY, lsum = 0.0f;
+        bool ok = true;
+        auto wait_warp = [&](uint64_t* bw, uint32_t parity) {
+            int w = 1;
+            if (lane == 0) w = fh3::mbar_wait<true>(bw, parity, abort_flag, status);
+            return __shfl_sync(0xffffffffu, w, 0) != 0;
+        };
+        for (int j = 0; j < L && ok; ++j) {
+            const int b = j & 1;
+            const int cnt = toff[lst[j] + 1] - toff[lst[j]];  // valid keys of the tile
+            if (!(ok = wait_warp(&s_full[b], (j >> 1) & 1))) break;
+            fh3::tc_fence_after();
+            uint32_t v[2][32];
+            fh3::tmem_ld32(trow + b * 64, v[0]);
+            fh3::tmem_ld32(trow + b * 64 + 32, v[1]);
+            fh3::tmem_ld_wait();
+            fh3::tmem_regs_ready(v[0]);
+            fh3::tmem_regs_ready(v[1]);
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            if (cnt == 64) {  // a full tile: no masking
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+            } else {
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        if (c * 32 + e >= cnt) v[c][e] = __float_as_uint(-INFINITY);  // the next tile's keys, padding
+                        mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                    }
+            }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
+            const bool raise = act && mx > m_ref + 8.0f;
+            if (j > 0 && __any_sync(0xffffffffu, raise)) {
+                if (!(ok = wait_warp(o_full, (j - 1) & 1))) break;  // the previous P V has landed
+                fh3::tc_fence_after();
+                const float a = raise ? exp2f(m_ref - mx) : 1.0f;  // 0 while this row's O is still empty
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t ov[32];
+                    fh3::tmem_ld32(trow + kV6TmemO + c * 32, ov);
+                    fh3::tmem_ld_wait();
+                    fh3::tmem_regs_ready(ov);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
+                    fh3::tmem_st32(trow + kV6TmemO + c * 32, ov);
+                }
+                fh3::tmem_st_wait();
+                lsum *= a;
+            }
+            if (raise) m_ref = mx;
+            if (!(ok = wait_warp(&p_empty[b], ((j >> 1) & 1) ^ 1u))) break;  // P_{j-2} consumed
+            if (act) {
+                uint8_t* pb = smem + V6_OFF_P + b * kV6Q;
+                float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;  // no key seen yet: every p is 0
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        uint32_t pk[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int e = 8 * t + 2 * u;
+                            const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
+                            const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
+                            rs4[u] += p0 + p1;
+                            const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                            pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                        }
+                        const int ch = c * 4 + t;
+                        *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    }
+                lsum += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+            }
+            fh3::tc_fence_before();
+            fh3::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                fh3::mbar_arrive(&s_empty[b]);
+                fh3::mbar_arrive(&p_full[b]);
+            }
+        }
+        if (ok) ok = wait_warp(o_full, (L - 1) & 1);  // the last P V has landed
+        if (ok) {
+            fh3::tc_fence_after();
+            const bool store = act && r < qrows;
+            const float inv = 1.0f / lsum;
+            const int64_t t = store ? perm[toff[i] + r] : 0;
+            const float* cb = gate ? outc + (static_cast<size_t>(i) * heads + h) * 128 : nullptr;
+            const int64_t col = static_cast<int64_t>(h) * 128;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t ov[32];
+                fh3::tmem_ld32(trow + kV6TmemO + c * 32, ov);
+                fh3::tmem_ld_wait();
+                fh3::tmem_regs_ready(ov);
+                if (!store) continue;
+#pragma unroll
+                for (int d8 = 0; d8 < 32; d8 += 8) {
+                    const int d = c * 32 + d8;
+                    float w8[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) w8[u] = __uint_as_float(ov[d8 + u]) * inv;
+                    if (cb) {
+                        const uint4 g4 = *reinterpret_cast<const uint4*>(gate + t * ldg + col + d);
+                        const __nv_bfloat16* g8 = reinterpret_cast<const __nv_bfloat16*>(&g4);
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) w8[u] += cb[d + u] * __bfloat162float(g8[u]);
+                    }
+                    if (OUT_BF16) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const __nv_bfloat162 pp = __floats2bfloat162_rn(w8[2 * u], w8[2 * u + 1]);
+                            w[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                        }
+                        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o) + t * ldo + col + d) =
+                            make_uint4(w[0], w[1], w[2], w[3]);
+                    } else {
+                        float* of = static_cast<float*>(o) + t * ldo + col + d;
+                        *reinterpret_cast<float4*>(of) = make_float4(w8[0], w8[1], w8[2], w8[3]);
+                        *reinterpret_cast<float4*>(of + 4) = make_float4(w8[4], w8[5], w8[6], w8[7]);
+                    }
+                }
+            }
+        }
+    }
+
+    fh3::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fh3::tc_fence_after();
+        fh3::tmem_dealloc(tmem, kV6TmemCols);
+    }
+}
+
 }  // namespace
 
 namespace fh3host {
@@ -474,11 +771,29 @@ int vsa_fine_tc(const int* perm, const int* toff, const int* sel, const int* sel
                         "vsa_tc smem attribute");
         if (!rc) rc = check_cuda(cudaFuncSetAttribute(vsa_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                       kVSmem), "vsa_tc smem attribute");
+        if (!rc) rc = check_cuda(cudaFuncSetAttribute(vsa_tc64_kernel<false>,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kV6Smem),
+                                 "vsa_tc64 smem attribute");
+        if (!rc) rc = check_cuda(cudaFuncSetAttribute(vsa_tc64_kernel<true>,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kV6Smem),
+                                 "vsa_tc64 smem attribute");
         if (rc) return rc;
         attr = true;
     }
     const float scale_log2 = (1.0f / sqrtf(128.0f)) * 1.4426950408889634f;
     const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(heads));
+    // FH3CUDA_VSA_KERNEL=tc128 selects the M = 128 kernel with duplicated query rows
+    const char* vk = getenv("FH3CUDA_VSA_KERNEL");
+    if (!(vk && strcmp(vk, "tc128") == 0)) {
+        if (o_bf16)
+            vsa_tc64_kernel<true><<<grid, kVThreads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate,
+                                                                   ldg, outc, heads, o, ldo, scale_log2, ctx_status(c));
+        else
+            vsa_tc64_kernel<false><<<grid, kVThreads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt,
+                                                                    gate, ldg, outc, heads, o, ldo, scale_log2,
+                                                                    ctx_status(c));
+        return check_cuda(cudaGetLastError(), "vsa_tc64_kernel launch");
+    }
     if (o_bf16)
         vsa_tc_kernel<true><<<grid, kVThreads, kVSmem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate, ldg,
                                                             outc, heads, o, ldo, scale_log2, ctx_status(c));
