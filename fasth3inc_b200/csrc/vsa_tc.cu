@@ -449,6 +449,25 @@ constexpr uint32_t kV6TmemO = 128;
 static_assert(kV6Smem <= 232448, "shared memory budget");
 static_assert(V6_OFF_KV % 1024 == 0 && kV6Stage % 1024 == 0 && V6_OFF_P % 1024 == 0, "swizzle alignment");
 
+// tcgen05.ld / st of shape 16x32bx2, 32 columns: threads 0..15 access lanes 0..15 of the
+// warp's lane quarter at columns [c, c + 32), threads 16..31 the same lanes at columns
+// [c + OFF, c + OFF + 32) (c = the column of taddr).  With the M = 64 layout (row m in lane
+// (m % 16) + 32 (m / 16)) a warp's 32 threads then hold 16 rows, two threads a row.
+template <int OFF>
+__device__ __forceinline__ void tmem_ld16x2_32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32], %33;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr), "n"(OFF));
+}
+template <int OFF>
+__device__ __forceinline__ void tmem_st16x2_32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x32bx2.x32.b32 [%0], %1, {%2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33};"
+        :: "r"(taddr), "n"(OFF), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
 template <bool OUT_BF16>
 __global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -574,11 +593,13 @@ __global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
         }
     } else {
         // ------------------------------------------------------------ softmax and epilogue (warps 2-5)
-        const int qw = warp & 3;           // TMEM lanes 32*qw .. 32*qw+31; rows 16*qw .. 16*qw+15
-        const bool act = lane < 16;        // lanes 16..31 of the quarter hold no row of an M = 64 MMA
-        const int r = qw * 16 + lane;      // the query row of an active lane
+        // thread lane holds row r = 16 qw + (lane & 15), keys 32 hf .. 32 hf + 31 of a score
+        // tile and O columns 64 hf .. 64 hf + 63; the row's two threads are lanes l and l ^ 16
+        const int qw = warp & 3;
+        const int hf = lane >> 4;
+        const int r = qw * 16 + (lane & 15);
         const uint32_t trow = tmem + (static_cast<uint32_t>(qw * 32) << 16);
-        float m_ref = -INFINITY, lsum = 0.0f;
+        float m_ref = -INFINITY, lsum = 0.0f;  // lsum: this thread's half of the row sum
         bool ok = true;
         auto wait_warp = [&](uint64_t* bw, uint32_t parity) {
             int w = 1;
@@ -587,75 +608,65 @@ __global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
         };
         for (int j = 0; j < L && ok; ++j) {
             const int b = j & 1;
-            const int cnt = toff[lst[j] + 1] - toff[lst[j]];  // valid keys of the tile
+            const int cnt = toff[lst[j] + 1] - toff[lst[j]] - 32 * hf;  // valid keys of this thread's half
             if (!(ok = wait_warp(&s_full[b], (j >> 1) & 1))) break;
             fh3::tc_fence_after();
-            uint32_t v[2][32];
-            fh3::tmem_ld32(trow + b * 64, v[0]);
-            fh3::tmem_ld32(trow + b * 64 + 32, v[1]);
+            uint32_t v[32];
+            tmem_ld16x2_32<32>(trow + b * 64, v);
             fh3::tmem_ld_wait();
-            fh3::tmem_regs_ready(v[0]);
-            fh3::tmem_regs_ready(v[1]);
+            fh3::tmem_regs_ready(v);
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (cnt == 64) {  // a full tile: no masking
+            if (cnt >= 32) {  // a full half: no masking
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
             } else {
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        if (c * 32 + e >= cnt) v[c][e] = __float_as_uint(-INFINITY);  // the next tile's keys, padding
-                        mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
-                    }
+                for (int e = 0; e < 32; ++e) {
+                    if (e >= cnt) v[e] = __float_as_uint(-INFINITY);  // the next tile's keys, padding
+                    mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
+                }
             }
-            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
-            const bool raise = act && mx > m_ref + 8.0f;
+            float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16)) * scale_log2;  // the row's max
+            const bool raise = mx > m_ref + 8.0f;  // the same in both threads of a row
             if (j > 0 && __any_sync(0xffffffffu, raise)) {
                 if (!(ok = wait_warp(o_full, (j - 1) & 1))) break;  // the previous P V has landed
                 fh3::tc_fence_after();
                 const float a = raise ? exp2f(m_ref - mx) : 1.0f;  // 0 while this row's O is still empty
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     uint32_t ov[32];
-                    fh3::tmem_ld32(trow + kV6TmemO + c * 32, ov);
+                    tmem_ld16x2_32<64>(trow + kV6TmemO + c * 32, ov);
                     fh3::tmem_ld_wait();
                     fh3::tmem_regs_ready(ov);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
-                    fh3::tmem_st32(trow + kV6TmemO + c * 32, ov);
+                    tmem_st16x2_32<64>(trow + kV6TmemO + c * 32, ov);
                 }
                 fh3::tmem_st_wait();
                 lsum *= a;
             }
             if (raise) m_ref = mx;
             if (!(ok = wait_warp(&p_empty[b], ((j >> 1) & 1) ^ 1u))) break;  // P_{j-2} consumed
-            if (act) {
-                uint8_t* pb = smem + V6_OFF_P + b * kV6Q;
-                float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;  // no key seen yet: every p is 0
+            uint8_t* pb = smem + V6_OFF_P + b * kV6Q;
+            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;  // no key seen yet: every p is 0
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
+            for (int t = 0; t < 4; ++t) {
+                uint32_t pk[4];
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int e = 8 * t + 2 * u;
-                            const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
-                            const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
-                            rs4[u] += p0 + p1;
-                            const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                            pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
-                        }
-                        const int ch = c * 4 + t;
-                        *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) =
-                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    }
-                lsum += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+                for (int u = 0; u < 4; ++u) {
+                    const int e = 8 * t + 2 * u;
+                    const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[e]), scale_log2, nm));
+                    const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[e + 1]), scale_log2, nm));
+                    rs4[u] += p0 + p1;
+                    const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                    pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                }
+                const int ch = hf * 4 + t;
+                *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
+            lsum += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
             fh3::tc_fence_before();
             fh3::fence_proxy_async_smem();
             __syncwarp();
@@ -667,21 +678,21 @@ __global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
         if (ok) ok = wait_warp(o_full, (L - 1) & 1);  // the last P V has landed
         if (ok) {
             fh3::tc_fence_after();
-            const bool store = act && r < qrows;
-            const float inv = 1.0f / lsum;
+            const float inv = 1.0f / (lsum + __shfl_xor_sync(0xffffffffu, lsum, 16));
+            const bool store = r < qrows;
             const int64_t t = store ? perm[toff[i] + r] : 0;
             const float* cb = gate ? outc + (static_cast<size_t>(i) * heads + h) * 128 : nullptr;
             const int64_t col = static_cast<int64_t>(h) * 128;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t ov[32];
-                fh3::tmem_ld32(trow + kV6TmemO + c * 32, ov);
+                tmem_ld16x2_32<64>(trow + kV6TmemO + c * 32, ov);  // O columns 64 hf + 32 c + e
                 fh3::tmem_ld_wait();
                 fh3::tmem_regs_ready(ov);
                 if (!store) continue;
 #pragma unroll
                 for (int d8 = 0; d8 < 32; d8 += 8) {
-                    const int d = c * 32 + d8;
+                    const int d = 64 * hf + 32 * c + d8;
                     float w8[8];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) w8[u] = __uint_as_float(ov[d8 + u]) * inv;
