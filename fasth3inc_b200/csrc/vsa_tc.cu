@@ -425,29 +425,38 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
 
 
 // M = 64 variant (the default): the query tile fills an M = 64 MMA once, so no tensor or
-// softmax work goes to duplicated rows, and one kept tile a step keeps a CTA small (two
-// 32 KB K / V^T stages, 256 TMEM columns) so that two CTAs share an SM and each one's
-// softmax runs while the other waits on its MMAs and loads:
-//   S_j = Q K_j^T     (M 64, N 64, K 128) into one of two TMEM score tiles (columns 0, 64)
-//   P_j               four softmax warps; query row m of an M = 64 MMA sits in TMEM lane
-//                     (m % 16) + 32 (m / 16), so lanes 0..15 of each warp hold a row each
-//   O += P_j V_j      (M 64, N 128, K 64) accumulating in TMEM columns 128..255
-// with the lazy 2^8 reference max of the other kernels and no merge at the end.
+// softmax work goes to duplicated rows.  Kept tiles go two a step (chunk c pairs lst[2c]
+// and lst[2c+1]; an odd last chunk repeats its tile with every key masked):
+//   S_c = Q [K_a; K_b]^T   (M 64, N 128, K 128) into one of two TMEM score tiles
+//   P_c                    four softmax warps; query row m of an M = 64 MMA sits in TMEM
+//                          lane (m % 16) + 32 (m / 16), and the 16x32bx2 load shape gives
+//                          lanes l and l + 16 of a warp the same row, one tile's keys each
+//   O += P_c [V_a; V_b]    (M 64, N 128, K 128) accumulating in TMEM
+// with the lazy 2^8 reference max of the other kernels and no merge at the end.  K and
+// V^T have rings of their own (three 32 KB stages each): a K stage is released as soon as
+// its S MMAs complete and a V^T stage when its P V MMAs do, and the S and P V MMAs are
+// issued by two threads, so a step's scores never wait behind the previous step's P.
+// A step does twice the keys of a one-tile step for the same number of barrier round
+// trips, which bound that kernel.
 constexpr int kV6Q = 64 * 64 * 2;            // [64][64] bf16 128-byte-swizzle block: 8 KB
-constexpr int kV6S = 2;                      // K / V^T stages
-constexpr int kV6Stage = 2 * kV6Q + kVB;     // K [64 keys][128] + V^T [128][64 keys]: 32 KB
+constexpr int kV6S = 3;                      // K stages and V^T stages
+constexpr int kV6K = 4 * kV6Q;               // K: 2 d-blocks x [tile a rows; tile b rows]: 32 KB
+constexpr int kV6V = 2 * kVB;                // V^T: [128][64 keys of tile a] + [128][64 of tile b]: 32 KB
 constexpr int V6_OFF_Q = 0;
-constexpr int V6_OFF_KV = V6_OFF_Q + 2 * kV6Q;
-constexpr int V6_OFF_P = V6_OFF_KV + kV6S * kV6Stage;
+constexpr int V6_OFF_K = V6_OFF_Q + 2 * kV6Q;
+constexpr int V6_OFF_V = V6_OFF_K + kV6S * kV6K;
+constexpr int V6_OFF_P = V6_OFF_V + kV6S * kV6V;  // [64][128 keys]: two 64-key blocks
 constexpr int V6_OFF_BAR = V6_OFF_P + 2 * kV6Q;
-// q_full, kv_full[kV6S], kv_empty[kV6S], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full, drain
-constexpr int kV6Bars = 1 + 2 * kV6S + 8 + 2;
+// q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_empty[2], p_full,
+// pv_done, drain_s, drain_o
+constexpr int kV6Bars = 1 + 4 * kV6S + 4 + 4;
 constexpr int V6_OFF_MISC = V6_OFF_BAR + kV6Bars * 8;
 constexpr int kV6Smem = V6_OFF_MISC + 64 + 1024;
-constexpr uint32_t kV6TmemCols = 256;  // S0 at 0, S1 at 64, O at 128
-constexpr uint32_t kV6TmemO = 128;
+constexpr int kV6Threads = 7 * 32;     // TMA, S MMAs, softmax x 4, P V MMAs
+constexpr uint32_t kV6TmemCols = 512;  // S0 at 0, S1 at 128, O at 256
+constexpr uint32_t kV6TmemO = 256;
 static_assert(kV6Smem <= 232448, "shared memory budget");
-static_assert(V6_OFF_KV % 1024 == 0 && kV6Stage % 1024 == 0 && V6_OFF_P % 1024 == 0, "swizzle alignment");
+static_assert(V6_OFF_K % 1024 == 0 && V6_OFF_V % 1024 == 0 && V6_OFF_P % 1024 == 0, "swizzle alignment");
 
 // tcgen05.ld / st of shape 16x32bx2, 32 columns: threads 0..15 access lanes 0..15 of the
 // warp's lane quarter at columns [c, c + 32), threads 16..31 the same lanes at columns
@@ -469,7 +478,7 @@ __device__ __forceinline__ void tmem_st16x2_32(uint32_t taddr, const uint32_t (&
 }
 
 template <bool OUT_BF16>
-__global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
+__global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmVt, const int* __restrict__ perm, const int* __restrict__ toff,
     const int* __restrict__ poff, const int* __restrict__ sel, const int* __restrict__ selcnt, int nt,
@@ -479,14 +488,16 @@ __global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + V6_OFF_BAR);
     uint64_t* q_full = bar;
-    uint64_t* kv_full = bar + 1;
-    uint64_t* kv_empty = kv_full + kV6S;
-    uint64_t* s_full = kv_empty + kV6S;
+    uint64_t* k_full = bar + 1;
+    uint64_t* k_empty = k_full + kV6S;
+    uint64_t* v_full = k_empty + kV6S;
+    uint64_t* v_empty = v_full + kV6S;
+    uint64_t* s_full = v_empty + kV6S;
     uint64_t* s_empty = s_full + 2;
     uint64_t* p_full = s_empty + 2;
-    uint64_t* p_empty = p_full + 2;
-    uint64_t* o_full = p_empty + 2;
-    uint64_t* drain = o_full + 1;
+    uint64_t* pv_done = p_full + 1;
+    uint64_t* drain_s = pv_done + 1;
+    uint64_t* drain_o = drain_s + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + V6_OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + V6_OFF_MISC + 8);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -494,22 +505,25 @@ __global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
     const size_t rowi = static_cast<size_t>(h) * nt + i;
     const int* lst = sel + rowi * nt;
     const int L = selcnt[rowi];               // >= 1
+    const int C = (L + 1) / 2;                // chunks
     const int qrows = toff[i + 1] - toff[i];  // <= 64
 
     if (threadIdx.x == 0) {
         fh3::mbar_init(q_full, 1);
         for (int s = 0; s < kV6S; ++s) {
-            fh3::mbar_init(&kv_full[s], 1);
-            fh3::mbar_init(&kv_empty[s], 1);
+            fh3::mbar_init(&k_full[s], 1);
+            fh3::mbar_init(&k_empty[s], 1);
+            fh3::mbar_init(&v_full[s], 1);
+            fh3::mbar_init(&v_empty[s], 1);
         }
         for (int s = 0; s < 2; ++s) {
             fh3::mbar_init(&s_full[s], 1);
             fh3::mbar_init(&s_empty[s], 4);
-            fh3::mbar_init(&p_full[s], 4);
-            fh3::mbar_init(&p_empty[s], 1);
         }
-        fh3::mbar_init(o_full, 1);
-        fh3::mbar_init(drain, 1);
+        fh3::mbar_init(p_full, 4);
+        fh3::mbar_init(pv_done, 1);
+        fh3::mbar_init(drain_s, 1);
+        fh3::mbar_init(drain_o, 1);
         *abort_flag = 0;
         fh3::fence_mbar_init();
     }
@@ -524,113 +538,156 @@ __global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
+        // K of chunk c goes out before V^T of chunk c - 1: a K stage frees up (S MMAs done)
+        // before a V^T stage does (P V MMAs done)
         if (lane == 0) {
-            uint32_t filled = 0, par = 0;
+            uint32_t kfill = 0, kpar = 0, vfill = 0, vpar = 0;
             fh3::mbar_arrive_expect_tx(q_full, 2 * kV6Q);
             for (int c = 0; c < 2; ++c)
                 fh3::tma_load_2d(smem + V6_OFF_Q + c * kV6Q, &tmQ, q_full, h * 128 + c * 64, poff[i]);
             bool ok = true;
-            for (int j = 0, st = 0, ph = 0; j < L && ok; ++j) {
-                if (!(ok = fh3::mbar_wait<true>(&kv_empty[st], static_cast<uint32_t>(ph) ^ 1u, abort_flag, status))) break;
-                const int y = poff[lst[j]];
-                uint8_t* sb = smem + V6_OFF_KV + st * kV6Stage;
-                fh3::mbar_arrive_expect_tx(&kv_full[st], kV6Stage);
-                for (int c = 0; c < 2; ++c) fh3::tma_load_2d(sb + c * kV6Q, &tmK, &kv_full[st], h * 128 + c * 64, y);
-                fh3::tma_load_2d(sb + 2 * kV6Q, &tmVt, &kv_full[st], y, h * 128);
-                filled |= 1u << st;
-                par = (par & ~(1u << st)) | (static_cast<uint32_t>(ph) << st);
-                if (++st == kV6S) {
-                    st = 0;
-                    ph ^= 1;
+            auto load_k = [&](int cc) {
+                const int st = cc % kV6S;
+                const uint32_t ph = static_cast<uint32_t>((cc / kV6S) & 1);
+                if (!(ok = fh3::mbar_wait<true>(&k_empty[st], ph ^ 1u, abort_flag, status))) return;
+                const int ya = poff[lst[2 * cc]], yb = poff[lst[min(2 * cc + 1, L - 1)]];
+                uint8_t* sb = smem + V6_OFF_K + st * kV6K;
+                fh3::mbar_arrive_expect_tx(&k_full[st], kV6K);
+                for (int c = 0; c < 2; ++c) {
+                    fh3::tma_load_2d(sb + c * 2 * kV6Q, &tmK, &k_full[st], h * 128 + c * 64, ya);
+                    fh3::tma_load_2d(sb + c * 2 * kV6Q + kV6Q, &tmK, &k_full[st], h * 128 + c * 64, yb);
                 }
+                kfill |= 1u << st;
+                kpar = (kpar & ~(1u << st)) | (ph << st);
+            };
+            auto load_v = [&](int cc) {
+                const int st = cc % kV6S;
+                const uint32_t ph = static_cast<uint32_t>((cc / kV6S) & 1);
+                if (!(ok = fh3::mbar_wait<true>(&v_empty[st], ph ^ 1u, abort_flag, status))) return;
+                const int ya = poff[lst[2 * cc]], yb = poff[lst[min(2 * cc + 1, L - 1)]];
+                uint8_t* sb = smem + V6_OFF_V + st * kV6V;
+                fh3::mbar_arrive_expect_tx(&v_full[st], kV6V);
+                fh3::tma_load_2d(sb, &tmVt, &v_full[st], ya, h * 128);
+                fh3::tma_load_2d(sb + kVB, &tmVt, &v_full[st], yb, h * 128);
+                vfill |= 1u << st;
+                vpar = (vpar & ~(1u << st)) | (ph << st);
+            };
+            for (int cc = 0; cc < C && ok; ++cc) {
+                load_k(cc);
+                if (ok && cc >= 1) load_v(cc - 1);
             }
+            if (ok) load_v(C - 1);
             volatile int no_abort = 0;
             fh3::mbar_wait<true>(q_full, 0, &no_abort, nullptr);
             if (!ok)
-                for (int s = 0; s < kV6S; ++s)
-                    if (filled & (1u << s)) fh3::mbar_wait<true>(&kv_full[s], (par >> s) & 1u, &no_abort, nullptr);
+                for (int s = 0; s < kV6S; ++s) {
+                    if (kfill & (1u << s)) fh3::mbar_wait<true>(&k_full[s], (kpar >> s) & 1u, &no_abort, nullptr);
+                    if (vfill & (1u << s)) fh3::mbar_wait<true>(&v_full[s], (vpar >> s) & 1u, &no_abort, nullptr);
+                }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+        // ------------------------------------------------------------ S MMAs
         if (lane == 0) {
-            constexpr uint32_t idesc_s = fh3::idesc_bf16_f32(64, 64);
-            constexpr uint32_t idesc_o = fh3::idesc_bf16_f32(64, 128);
+            constexpr uint32_t idesc = fh3::idesc_bf16_f32(64, 128);
             const uint32_t qa = fh3::smem_u32(smem + V6_OFF_Q);
             bool ok = fh3::mbar_wait<true>(q_full, 0, abort_flag, status);
-            auto pv = [&](int j) {
-                const int bi = j & 1, st = j % kV6S;
-                if (!(ok = fh3::mbar_wait<true>(&p_full[bi], (j >> 1) & 1, abort_flag, status))) return;
+            for (int cc = 0; cc < C && ok; ++cc) {
+                const int b = cc & 1, st = cc % kV6S;
+                if (!(ok = fh3::mbar_wait<true>(&k_full[st], (cc / kV6S) & 1, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(&s_empty[b], ((cc >> 1) & 1) ^ 1u, abort_flag, status))) break;
                 fh3::tc_fence_after();
-                const uint32_t pa = fh3::smem_u32(smem + V6_OFF_P + bi * kV6Q);
-                const uint32_t va = fh3::smem_u32(smem + V6_OFF_KV + st * kV6Stage + 2 * kV6Q);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    fh3::umma_f16(tmem + kV6TmemO, fh3::sdesc_sw128(pa) + 2 * kk, fh3::sdesc_sw128(va) + 2 * kk, idesc_o,
-                                  (j | kk) != 0 ? 1u : 0u);
-                fh3::umma_commit(o_full);
-                fh3::umma_commit(&p_empty[bi]);
-                fh3::umma_commit(&kv_empty[st]);
-            };
-            for (int j = 0; j < L && ok; ++j) {
-                const int b = j & 1, st = j % kV6S;
-                if (!(ok = fh3::mbar_wait<true>(&kv_full[st], (j / kV6S) & 1, abort_flag, status))) break;
-                if (!(ok = fh3::mbar_wait<true>(&s_empty[b], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
-                fh3::tc_fence_after();
-                const uint32_t ka = fh3::smem_u32(smem + V6_OFF_KV + st * kV6Stage);
+                const uint32_t ka = fh3::smem_u32(smem + V6_OFF_K + st * kV6K);
 #pragma unroll
                 for (int c = 0; c < 2; ++c)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        fh3::umma_f16(tmem + b * 64, fh3::sdesc_sw128(qa + c * kV6Q) + 2 * kk,
-                                      fh3::sdesc_sw128(ka + c * kV6Q) + 2 * kk, idesc_s, (c | kk) != 0 ? 1u : 0u);
+                        fh3::umma_f16(tmem + b * 128, fh3::sdesc_sw128(qa + c * kV6Q) + 2 * kk,
+                                      fh3::sdesc_sw128(ka + c * 2 * kV6Q) + 2 * kk, idesc, (c | kk) != 0 ? 1u : 0u);
                 fh3::umma_commit(&s_full[b]);
-                if (j >= 1) pv(j - 1);
+                fh3::umma_commit(&k_empty[st]);
             }
-            if (ok) pv(L - 1);
-            fh3::umma_commit(drain);
+            fh3::umma_commit(drain_s);
             volatile int no_abort = 0;
-            fh3::mbar_wait<true>(drain, 0, &no_abort, nullptr);
+            fh3::mbar_wait<true>(drain_s, 0, &no_abort, nullptr);
+        }
+    } else if (warp == 6) {
+        // ------------------------------------------------------------ P V MMAs
+        if (lane == 0) {
+            constexpr uint32_t idesc = fh3::idesc_bf16_f32(64, 128);
+            const uint32_t pa = fh3::smem_u32(smem + V6_OFF_P);
+            bool ok = true;
+            for (int cc = 0; cc < C && ok; ++cc) {
+                const int st = cc % kV6S;
+                if (!(ok = fh3::mbar_wait<true>(&v_full[st], (cc / kV6S) & 1, abort_flag, status))) break;
+                if (!(ok = fh3::mbar_wait<true>(p_full, cc & 1, abort_flag, status))) break;
+                fh3::tc_fence_after();
+                const uint32_t va = fh3::smem_u32(smem + V6_OFF_V + st * kV6V);
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        fh3::umma_f16(tmem + kV6TmemO, fh3::sdesc_sw128(pa + c * kV6Q) + 2 * kk,
+                                      fh3::sdesc_sw128(va + c * kVB) + 2 * kk, idesc, (cc | c | kk) != 0 ? 1u : 0u);
+                fh3::umma_commit(pv_done);
+                fh3::umma_commit(&v_empty[st]);
+            }
+            fh3::umma_commit(drain_o);
+            volatile int no_abort = 0;
+            fh3::mbar_wait<true>(drain_o, 0, &no_abort, nullptr);
         }
     } else {
         // ------------------------------------------------------------ softmax and epilogue (warps 2-5)
-        // thread lane holds row r = 16 qw + (lane & 15), keys 32 hf .. 32 hf + 31 of a score
-        // tile and O columns 64 hf .. 64 hf + 63; the row's two threads are lanes l and l ^ 16
+        // thread lane holds row r = 16 qw + (lane & 15) and the keys of one tile of a chunk
+        // (hf = 0: the first, columns 0..63; hf = 1: the second, columns 64..127), and O
+        // columns 64 hf .. 64 hf + 63; the row's two threads are lanes l and l ^ 16
         const int qw = warp & 3;
         const int hf = lane >> 4;
         const int r = qw * 16 + (lane & 15);
         const uint32_t trow = tmem + (static_cast<uint32_t>(qw * 32) << 16);
-        float m_ref = -INFINITY, lsum = 0.0f;  // lsum: this thread's half of the row sum
+        float m_ref = -INFINITY, lsum = 0.0f;  // lsum: this thread's part of the row sum
         bool ok = true;
         auto wait_warp = [&](uint64_t* bw, uint32_t parity) {
             int w = 1;
             if (lane == 0) w = fh3::mbar_wait<true>(bw, parity, abort_flag, status);
             return __shfl_sync(0xffffffffu, w, 0) != 0;
         };
-        for (int j = 0; j < L && ok; ++j) {
-            const int b = j & 1;
-            const int cnt = toff[lst[j] + 1] - toff[lst[j]] - 32 * hf;  // valid keys of this thread's half
-            if (!(ok = wait_warp(&s_full[b], (j >> 1) & 1))) break;
+        for (int cc = 0; cc < C && ok; ++cc) {
+            const int b = cc & 1;
+            const int li = 2 * cc + hf;
+            const int cnt = li < L ? toff[lst[li] + 1] - toff[lst[li]] : 0;  // valid keys of this thread's tile
+            if (!(ok = wait_warp(&s_full[b], (cc >> 1) & 1))) break;
             fh3::tc_fence_after();
-            uint32_t v[32];
-            tmem_ld16x2_32<32>(trow + b * 64, v);
+            uint32_t v[2][32];
+            tmem_ld16x2_32<64>(trow + b * 128, v[0]);       // keys 0..31 of the thread's tile
+            tmem_ld16x2_32<64>(trow + b * 128 + 32, v[1]);  // keys 32..63
             fh3::tmem_ld_wait();
-            fh3::tmem_regs_ready(v);
+            fh3::tmem_regs_ready(v[0]);
+            fh3::tmem_regs_ready(v[1]);
+            // the scores are in registers: the score tile may take chunk cc + 2
+            fh3::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) fh3::mbar_arrive(&s_empty[b]);
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (cnt >= 32) {  // a full half: no masking
+            if (cnt == 64) {  // a full tile: no masking
 #pragma unroll
-                for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
             } else {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    if (e >= cnt) v[e] = __float_as_uint(-INFINITY);  // the next tile's keys, padding
-                    mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
-                }
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        if (c * 32 + e >= cnt) v[c][e] = __float_as_uint(-INFINITY);  // the next tile's keys, padding
+                        mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                    }
             }
             float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16)) * scale_log2;  // the row's max
             const bool raise = mx > m_ref + 8.0f;  // the same in both threads of a row
-            if (j > 0 && __any_sync(0xffffffffu, raise)) {
-                if (!(ok = wait_warp(o_full, (j - 1) & 1))) break;  // the previous P V has landed
+            // P and O are free once the previous chunk's P V has completed
+            if (cc > 0 && !(ok = wait_warp(pv_done, (cc - 1) & 1))) break;
+            if (cc > 0 && __any_sync(0xffffffffu, raise)) {
                 fh3::tc_fence_after();
                 const float a = raise ? exp2f(m_ref - mx) : 1.0f;  // 0 while this row's O is still empty
 #pragma unroll
@@ -647,35 +704,34 @@ __global__ void __launch_bounds__(kVThreads, 2) vsa_tc64_kernel(
                 lsum *= a;
             }
             if (raise) m_ref = mx;
-            if (!(ok = wait_warp(&p_empty[b], ((j >> 1) & 1) ^ 1u))) break;  // P_{j-2} consumed
-            uint8_t* pb = smem + V6_OFF_P + b * kV6Q;
+            uint8_t* pb = smem + V6_OFF_P + hf * kV6Q;  // the key block of this thread's tile
             float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;  // no key seen yet: every p is 0
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                uint32_t pk[4];
+            for (int c = 0; c < 2; ++c)
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int e = 8 * t + 2 * u;
-                    const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[e]), scale_log2, nm));
-                    const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[e + 1]), scale_log2, nm));
-                    rs4[u] += p0 + p1;
-                    const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                    pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                for (int t = 0; t < 4; ++t) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e = 8 * t + 2 * u;
+                        const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
+                        const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
+                        rs4[u] += p0 + p1;
+                        const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                        pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
+                    }
+                    const int ch = c * 4 + t;
+                    *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
-                const int ch = hf * 4 + t;
-                *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            }
             lsum += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
             fh3::tc_fence_before();
             fh3::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
-                fh3::mbar_arrive(&s_empty[b]);
-                fh3::mbar_arrive(&p_full[b]);
-            }
+            if (lane == 0) fh3::mbar_arrive(p_full);
         }
-        if (ok) ok = wait_warp(o_full, (L - 1) & 1);  // the last P V has landed
+        if (ok) ok = wait_warp(pv_done, (C - 1) & 1);  // the last P V has landed
         if (ok) {
             fh3::tc_fence_after();
             const float inv = 1.0f / (lsum + __shfl_xor_sync(0xffffffffu, lsum, 16));
@@ -797,10 +853,10 @@ int vsa_fine_tc(const int* perm, const int* toff, const int* sel, const int* sel
     const char* vk = getenv("FH3CUDA_VSA_KERNEL");
     if (!(vk && strcmp(vk, "tc128") == 0)) {
         if (o_bf16)
-            vsa_tc64_kernel<true><<<grid, kVThreads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate,
+            vsa_tc64_kernel<true><<<grid, kV6Threads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate,
                                                                    ldg, outc, heads, o, ldo, scale_log2, ctx_status(c));
         else
-            vsa_tc64_kernel<false><<<grid, kVThreads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt,
+            vsa_tc64_kernel<false><<<grid, kV6Threads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt,
                                                                     gate, ldg, outc, heads, o, ldo, scale_log2,
                                                                     ctx_status(c));
         return check_cuda(cudaGetLastError(), "vsa_tc64_kernel launch");
