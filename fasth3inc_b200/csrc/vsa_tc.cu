@@ -425,19 +425,21 @@ __global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
 
 
 // M = 64 variant (the default): the query tile fills an M = 64 MMA once, so no tensor or
-// softmax work goes to duplicated rows.  Kept tiles go two a step (chunk c pairs lst[2c]
-// and lst[2c+1]; an odd last chunk repeats its tile with every key masked):
+// softmax work goes to duplicated rows.  Kept tiles go two a step (chunk c pairs tile
+// a = lst[2c] and tile b = lst[2c+1]; an odd last chunk repeats tile a with every key of
+// the copy masked):
 //   S_c = Q [K_a; K_b]^T   (M 64, N 128, K 128) into one of two TMEM score tiles
-//   P_c                    four softmax warps; query row m of an M = 64 MMA sits in TMEM
-//                          lane (m % 16) + 32 (m / 16), and the 16x32bx2 load shape gives
-//                          lanes l and l + 16 of a warp the same row, one tile's keys each
-//   O += P_c [V_a; V_b]    (M 64, N 128, K 128) accumulating in TMEM
-// with the lazy 2^8 reference max of the other kernels and no merge at the end.  K and
-// V^T have rings of their own (three 32 KB stages each): a K stage is released as soon as
-// its S MMAs complete and a V^T stage when its P V MMAs do, and the S and P V MMAs are
-// issued by two threads, so a step's scores never wait behind the previous step's P.
-// A step does twice the keys of a one-tile step for the same number of barrier round
-// trips, which bound that kernel.
+//   P_a, P_b               two softmax warpgroups, A on the keys of tile a, B on those of
+//                          tile b, each with its own running max, sum and output
+//   O_A += P_a V_a, O_B += P_b V_b   (M 64, N 128, K 64 each) accumulating in TMEM
+// and at the end the two partial outputs of each query are merged (shared memory), with
+// the lazy 2^8 reference max of the other kernels.  Query row m of an M = 64 MMA sits in
+// TMEM lane (m % 16) + 32 (m / 16); the 16x32bx2 load shape gives lanes l and l + 16 of a
+// warp the same row, 32 keys each.  K and V^T have rings of their own (three 32 KB stages
+// each): a K stage is released as soon as its S MMAs complete and a V^T stage when its
+// P V MMAs do, and the S and P V MMAs are issued by two threads, so a step's scores never
+// wait behind the previous step's P.  Two tiles a step halve the barrier round trips of a
+// one-tile step, and two warpgroups give each SM sub-partition two softmax warps.
 constexpr int kV6Q = 64 * 64 * 2;            // [64][64] bf16 128-byte-swizzle block: 8 KB
 constexpr int kV6S = 3;                      // K stages and V^T stages
 constexpr int kV6K = 4 * kV6Q;               // K: 2 d-blocks x [tile a rows; tile b rows]: 32 KB
@@ -445,18 +447,20 @@ constexpr int kV6V = 2 * kVB;                // V^T: [128][64 keys of tile a] + 
 constexpr int V6_OFF_Q = 0;
 constexpr int V6_OFF_K = V6_OFF_Q + 2 * kV6Q;
 constexpr int V6_OFF_V = V6_OFF_K + kV6S * kV6K;
-constexpr int V6_OFF_P = V6_OFF_V + kV6S * kV6V;  // [64][128 keys]: two 64-key blocks
+constexpr int V6_OFF_P = V6_OFF_V + kV6S * kV6V;  // P_a, P_b: [64][64 keys] each
 constexpr int V6_OFF_BAR = V6_OFF_P + 2 * kV6Q;
-// q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_empty[2], p_full,
-// pv_done, drain_s, drain_o
-constexpr int kV6Bars = 1 + 4 * kV6S + 4 + 4;
+// q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_empty[2], p_full[2],
+// pv_done[2], drain_s, drain_o
+constexpr int kV6Bars = 1 + 4 * kV6S + 8 + 2;
 constexpr int V6_OFF_MISC = V6_OFF_BAR + kV6Bars * 8;
 constexpr int kV6Smem = V6_OFF_MISC + 64 + 1024;
-constexpr int kV6Threads = 7 * 32;     // TMA, S MMAs, softmax x 4, P V MMAs
-constexpr uint32_t kV6TmemCols = 512;  // S0 at 0, S1 at 128, O at 256
+constexpr int kV6Threads = 11 * 32;    // TMA, S MMAs, softmax A x 4, softmax B x 4, P V MMAs
+constexpr int kV6WarpPV = 10;
+constexpr uint32_t kV6TmemCols = 512;  // S0 at 0, S1 at 128, O_A at 256, O_B at 384
 constexpr uint32_t kV6TmemO = 256;
 static_assert(kV6Smem <= 232448, "shared memory budget");
 static_assert(V6_OFF_K % 1024 == 0 && V6_OFF_V % 1024 == 0 && V6_OFF_P % 1024 == 0, "swizzle alignment");
+static_assert(64 * 130 * 4 <= kV6S * kV6K, "merge exchange fits the K ring");
 
 // tcgen05.ld / st of shape 16x32bx2, 32 columns: threads 0..15 access lanes 0..15 of the
 // warp's lane quarter at columns [c, c + 32), threads 16..31 the same lanes at columns
@@ -494,9 +498,9 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
     uint64_t* v_empty = v_full + kV6S;
     uint64_t* s_full = v_empty + kV6S;
     uint64_t* s_empty = s_full + 2;
-    uint64_t* p_full = s_empty + 2;
-    uint64_t* pv_done = p_full + 1;
-    uint64_t* drain_s = pv_done + 1;
+    uint64_t* p_full = s_empty + 2;   // [group]
+    uint64_t* pv_done = p_full + 2;   // [group]
+    uint64_t* drain_s = pv_done + 2;
     uint64_t* drain_o = drain_s + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + V6_OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + V6_OFF_MISC + 8);
@@ -518,10 +522,10 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
         }
         for (int s = 0; s < 2; ++s) {
             fh3::mbar_init(&s_full[s], 1);
-            fh3::mbar_init(&s_empty[s], 4);
+            fh3::mbar_init(&s_empty[s], 8);
+            fh3::mbar_init(&p_full[s], 4);
+            fh3::mbar_init(&pv_done[s], 1);
         }
-        fh3::mbar_init(p_full, 4);
-        fh3::mbar_init(pv_done, 1);
         fh3::mbar_init(drain_s, 1);
         fh3::mbar_init(drain_o, 1);
         *abort_flag = 0;
@@ -610,7 +614,7 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
             volatile int no_abort = 0;
             fh3::mbar_wait<true>(drain_s, 0, &no_abort, nullptr);
         }
-    } else if (warp == 6) {
+    } else if (warp == kV6WarpPV) {
         // ------------------------------------------------------------ P V MMAs
         if (lane == 0) {
             constexpr uint32_t idesc = fh3::idesc_bf16_f32(64, 128);
@@ -619,31 +623,33 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
             for (int cc = 0; cc < C && ok; ++cc) {
                 const int st = cc % kV6S;
                 if (!(ok = fh3::mbar_wait<true>(&v_full[st], (cc / kV6S) & 1, abort_flag, status))) break;
-                if (!(ok = fh3::mbar_wait<true>(p_full, cc & 1, abort_flag, status))) break;
-                fh3::tc_fence_after();
                 const uint32_t va = fh3::smem_u32(smem + V6_OFF_V + st * kV6V);
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
+                for (int g = 0; g < 2 && ok; ++g) {
+                    if (!(ok = fh3::mbar_wait<true>(&p_full[g], cc & 1, abort_flag, status))) break;
+                    fh3::tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        fh3::umma_f16(tmem + kV6TmemO, fh3::sdesc_sw128(pa + c * kV6Q) + 2 * kk,
-                                      fh3::sdesc_sw128(va + c * kVB) + 2 * kk, idesc, (cc | c | kk) != 0 ? 1u : 0u);
-                fh3::umma_commit(pv_done);
-                fh3::umma_commit(&v_empty[st]);
+                        fh3::umma_f16(tmem + kV6TmemO + g * 128, fh3::sdesc_sw128(pa + g * kV6Q) + 2 * kk,
+                                      fh3::sdesc_sw128(va + g * kVB) + 2 * kk, idesc, (cc | kk) != 0 ? 1u : 0u);
+                    fh3::umma_commit(&pv_done[g]);
+                }
+                if (ok) fh3::umma_commit(&v_empty[st]);
             }
             fh3::umma_commit(drain_o);
             volatile int no_abort = 0;
             fh3::mbar_wait<true>(drain_o, 0, &no_abort, nullptr);
         }
     } else {
-        // ------------------------------------------------------------ softmax and epilogue (warps 2-5)
-        // thread lane holds row r = 16 qw + (lane & 15) and the keys of one tile of a chunk
-        // (hf = 0: the first, columns 0..63; hf = 1: the second, columns 64..127), and O
-        // columns 64 hf .. 64 hf + 63; the row's two threads are lanes l and l ^ 16
+        // ------------------------------------------------------------ softmax, merge and epilogue (warps 2-9)
+        // group g (warps 2-5: A, 6-9: B) takes tile g of every chunk; thread lane holds row
+        // r = 16 qw + (lane & 15), keys 32 hf .. 32 hf + 31 of the tile and O_g columns
+        // 64 hf .. 64 hf + 63; the row's two threads are lanes l and l ^ 16
+        const int g = (warp - 2) >> 2;
         const int qw = warp & 3;
         const int hf = lane >> 4;
         const int r = qw * 16 + (lane & 15);
         const uint32_t trow = tmem + (static_cast<uint32_t>(qw * 32) << 16);
+        const uint32_t tO = trow + kV6TmemO + g * 128;
         float m_ref = -INFINITY, lsum = 0.0f;  // lsum: this thread's part of the row sum
         bool ok = true;
         auto wait_warp = [&](uint64_t* bw, uint32_t parity) {
@@ -653,88 +659,106 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
         };
         for (int cc = 0; cc < C && ok; ++cc) {
             const int b = cc & 1;
-            const int li = 2 * cc + hf;
-            const int cnt = li < L ? toff[lst[li] + 1] - toff[lst[li]] : 0;  // valid keys of this thread's tile
+            const int li = 2 * cc + g;
+            const int cnt = (li < L ? toff[lst[li] + 1] - toff[lst[li]] : 0) - 32 * hf;  // valid keys of this half
             if (!(ok = wait_warp(&s_full[b], (cc >> 1) & 1))) break;
             fh3::tc_fence_after();
-            uint32_t v[2][32];
-            tmem_ld16x2_32<64>(trow + b * 128, v[0]);       // keys 0..31 of the thread's tile
-            tmem_ld16x2_32<64>(trow + b * 128 + 32, v[1]);  // keys 32..63
+            uint32_t v[32];
+            tmem_ld16x2_32<32>(trow + b * 128 + g * 64, v);
             fh3::tmem_ld_wait();
-            fh3::tmem_regs_ready(v[0]);
-            fh3::tmem_regs_ready(v[1]);
+            fh3::tmem_regs_ready(v);
             // the scores are in registers: the score tile may take chunk cc + 2
             fh3::tc_fence_before();
             __syncwarp();
             if (lane == 0) fh3::mbar_arrive(&s_empty[b]);
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (cnt == 64) {  // a full tile: no masking
+            if (cnt >= 32) {  // a full half: no masking
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
             } else {
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        if (c * 32 + e >= cnt) v[c][e] = __float_as_uint(-INFINITY);  // the next tile's keys, padding
-                        mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
-                    }
+                for (int e = 0; e < 32; ++e) {
+                    if (e >= cnt) v[e] = __float_as_uint(-INFINITY);  // the next tile's keys, padding
+                    mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
+                }
             }
             float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16)) * scale_log2;  // the row's max
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16)) * scale_log2;  // the row's max over the tile
             const bool raise = mx > m_ref + 8.0f;  // the same in both threads of a row
-            // P and O are free once the previous chunk's P V has completed
-            if (cc > 0 && !(ok = wait_warp(pv_done, (cc - 1) & 1))) break;
+            // P_g and O_g are free once the previous chunk's P_g V has completed
+            if (cc > 0 && !(ok = wait_warp(&pv_done[g], (cc - 1) & 1))) break;
             if (cc > 0 && __any_sync(0xffffffffu, raise)) {
                 fh3::tc_fence_after();
                 const float a = raise ? exp2f(m_ref - mx) : 1.0f;  // 0 while this row's O is still empty
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
                     uint32_t ov[32];
-                    tmem_ld16x2_32<64>(trow + kV6TmemO + c * 32, ov);
+                    tmem_ld16x2_32<64>(tO + c * 32, ov);
                     fh3::tmem_ld_wait();
                     fh3::tmem_regs_ready(ov);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
-                    tmem_st16x2_32<64>(trow + kV6TmemO + c * 32, ov);
+                    tmem_st16x2_32<64>(tO + c * 32, ov);
                 }
                 fh3::tmem_st_wait();
                 lsum *= a;
             }
             if (raise) m_ref = mx;
-            uint8_t* pb = smem + V6_OFF_P + hf * kV6Q;  // the key block of this thread's tile
+            uint8_t* pb = smem + V6_OFF_P + g * kV6Q;
             float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;  // no key seen yet: every p is 0
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+            for (int t = 0; t < 4; ++t) {
+                uint32_t pk[4];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int e = 8 * t + 2 * u;
-                        const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
-                        const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
-                        rs4[u] += p0 + p1;
-                        const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                        pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
-                    }
-                    const int ch = c * 4 + t;
-                    *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) =
-                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                for (int u = 0; u < 4; ++u) {
+                    const int e = 8 * t + 2 * u;
+                    const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[e]), scale_log2, nm));
+                    const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[e + 1]), scale_log2, nm));
+                    rs4[u] += p0 + p1;
+                    const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                    pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
                 }
+                const int ch = hf * 4 + t;
+                *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
             lsum += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
             fh3::tc_fence_before();
             fh3::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) fh3::mbar_arrive(p_full);
+            if (lane == 0) fh3::mbar_arrive(&p_full[g]);
         }
-        if (ok) ok = wait_warp(pv_done, (C - 1) & 1);  // the last P V has landed
-        if (ok) {
+        if (ok) ok = wait_warp(&pv_done[g], (C - 1) & 1);  // the last P_g V has landed
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 16);      // the row's sum over group g's keys
+        // merge: group B hands (m, l, O_B) to group A through the K ring, free once every
+        // S MMA has completed (the last one before the last scores were read)
+        float* xch = reinterpret_cast<float*>(smem + V6_OFF_K);  // [64][130]
+        if (g == 1 && ok) {
             fh3::tc_fence_after();
-            const float inv = 1.0f / (lsum + __shfl_xor_sync(0xffffffffu, lsum, 16));
+            float* d = xch + r * 130;
+            if (hf == 0) {
+                d[0] = m_ref;
+                d[1] = lsum;
+            }
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+                uint32_t ov[32];
+                tmem_ld16x2_32<64>(tO + c * 32, ov);  // O columns 64 hf + 32 c + e
+                fh3::tmem_ld_wait();
+                fh3::tmem_regs_ready(ov);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) d[2 + 64 * hf + 32 * c + e] = __uint_as_float(ov[e]);
+            }
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps, on every path
+        if (g == 0 && ok) {
+            fh3::tc_fence_after();
+            const float* x = xch + r * 130;
+            const float mb = x[0], lb = x[1];
+            const float m = fmaxf(m_ref, mb);  // finite: every chunk's first tile holds keys
+            const float wa = exp2f(m_ref - m);
+            const float wb = mb == -INFINITY ? 0.0f : exp2f(mb - m);
+            const float inv = 1.0f / (lsum * wa + lb * wb);
             const bool store = r < qrows;
             const int64_t t = store ? perm[toff[i] + r] : 0;
             const float* cb = gate ? outc + (static_cast<size_t>(i) * heads + h) * 128 : nullptr;
@@ -742,7 +766,7 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
 #pragma unroll 1
             for (int c = 0; c < 2; ++c) {
                 uint32_t ov[32];
-                tmem_ld16x2_32<64>(trow + kV6TmemO + c * 32, ov);  // O columns 64 hf + 32 c + e
+                tmem_ld16x2_32<64>(tO + c * 32, ov);  // O columns 64 hf + 32 c + e
                 fh3::tmem_ld_wait();
                 fh3::tmem_regs_ready(ov);
                 if (!store) continue;
@@ -751,7 +775,7 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
                     const int d = 64 * hf + 32 * c + d8;
                     float w8[8];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) w8[u] = __uint_as_float(ov[d8 + u]) * inv;
+                    for (int u = 0; u < 8; ++u) w8[u] = (__uint_as_float(ov[d8 + u]) * wa + x[2 + d + u] * wb) * inv;
                     if (cb) {
                         const uint4 g4 = *reinterpret_cast<const uint4*>(gate + t * ldg + col + d);
                         const __nv_bfloat16* g8 = reinterpret_cast<const __nv_bfloat16*>(&g4);
