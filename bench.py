@@ -498,7 +498,7 @@ def measure_vsa(fh3, torch, rows: int, peak: float, peak_src: str, reps: int = 3
     ms = e0.elapsed_time(e1) / reps
     tf = flops / (ms * 1e-3) / 1e12
     del qkv, gate, o
-    return {"kernel": "vsa_tc_kernel (+ tile stage, tile-order copies and coarse pass in the timed call)", "rows": n,
+    return {"kernel": "vsa_tc64_kernel (+ tile stage, tile-order copies and coarse pass in the timed call)", "rows": n,
             "seq": {"audio": seq[2], "video": seq[3], "grid": list(seq[4:])}, "tiles": nt, "heads": H,
             "head_dim": D, "sparsity": 0.8, "ms_per_call": round(ms, 3), "bound": "tensor",
             "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak, "frac": round(tf / peak, 4),
