@@ -8,9 +8,14 @@
 // (vsa_rows_kernel) and v transposed into VpT[h*128 + d][position] (vsa_vt_kernel).
 // Then a kept tile is one TMA box of K rows and one of V^T columns.
 //
-// vsa_tc_kernel: a CTA owns one query tile (<= 64 rows) of one head.  The tile's queries
-// fill both halves of an M = 128 MMA and its kept key tiles are walked two at a time: in
-// chunk c, rows 0..63 take the keys of lst[2c] and rows 64..127 those of lst[2c+1]:
+// vsa_tc64_kernel (the default, below): a CTA owns one query tile of one head in an
+// M = 64 MMA and walks its kept tiles two a step, one softmax warpgroup per tile of the
+// step, each with its own running max, sum and TMEM output, merged at the end.
+//
+// vsa_tc_kernel (FH3CUDA_VSA_KERNEL=tc128): a CTA owns one query tile (<= 64 rows) of one
+// head.  The tile's queries fill both halves of an M = 128 MMA and its kept key tiles are
+// walked two at a time: in chunk c, rows 0..63 take the keys of lst[2c] and rows 64..127
+// those of lst[2c+1]:
 //   S_c = Q K_c^T     (M 128, N 128, K 128) into one of two TMEM score tiles
 //   P_c               four softmax warps, one (query, half) row per thread, against a
 //                     reference max raised only when a chunk's max exceeds it by more
