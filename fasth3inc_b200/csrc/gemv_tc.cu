@@ -44,7 +44,7 @@
 namespace {
 
 constexpr int kGtRows = 128;                               // rows of a tile = TMEM lanes
-constexpr int kGtStages = 6;
+constexpr int kGtStages = 6;                               // weight stages (fewer for 9..16 tokens)
 constexpr int kGtStageBytes = kGtRows * fh3::kQ4KBytes;    // 18432
 constexpr int kGtMaxTok = 16;
 constexpr int kGtHdrs = 8;                                 // ring of the units' 16-byte row headers
@@ -61,40 +61,52 @@ constexpr int align16(int v) { return (v + 15) & ~15; }
 // B slots and the shared-memory layout.
 template <int M>
 struct GtCfg {
-    static constexpr int NC = M <= 5 ? 16 : (M <= 10 ? 32 : 48);  // B rows = accumulator columns per sub-block
-    static constexpr int DB = NC == 16 ? 2 : 1;                    // accumulator buffers
-    static constexpr int AB = NC == 48 ? 2 : 4;                    // A buffers (64 columns each)
-    static constexpr int DCOLS = 8 * NC;                           // accumulator columns of one unit
+    // 1..5 tokens: kind::i8 MMAs of the nibbles, one accumulator per sub-block (eight a
+    // unit), the B operand of the run's super-blocks resident in shared memory.
+    // 6..16 tokens: kind::f16 MMAs of sc * q (the 6-bit scale folded into the A operand,
+    // exact in fp16) into one accumulator a unit, and of the mins against the sub-block
+    // sums into a second; the B blocks are built once per call by gemv_xprep_kernel and
+    // streamed from L2 beside the weights, so the units run tile by tile over the whole K.
+    static constexpr bool F16 = M > 5;
+    static constexpr int NC = F16 ? (M <= 8 ? 16 : 32) : 16;       // B rows = accumulator columns (a sub-block's / a unit's)
+    static constexpr int DB = 2;                                   // accumulator buffers
+    static constexpr int ACOLS = F16 ? 144 : 64;                   // TMEM columns of one A buffer (f16: 128 of sc*q, 16 of mins)
+    static constexpr int AB = F16 ? 2 : 4;                         // A buffers
+    static constexpr int DCOLS = F16 ? 2 * NC : 8 * NC;            // accumulator columns of one unit
     static constexpr uint32_t TM_A = DB * DCOLS;                   // first A column
-    static constexpr int SLOT_BYTES = 256 * NC;                    // B of one super-block: 2 halves x NC rows x 128 B
-    static constexpr int HALF_BYTES = 128 * NC;
-    static constexpr int SLOTS = NC == 16 ? 20 : (NC == 32 ? 10 : 6);
-    static constexpr int CHUNK = M <= 5 ? 0 : SLOTS / 2;          // super-blocks a chunk (0: the whole K)
+    static constexpr int STAGES = F16 ? 5 : kGtStages;
+    // B of one super-block: K blocks of 128 bytes x NC rows (i8: 2 blocks of 128 k;
+    // f16: 4 blocks of 64 k and one holding the 8 sub-block sums)
+    static constexpr int SLOT_BYTES = (F16 ? 640 : 256) * NC;
+    static constexpr int HALF_BYTES = 128 * NC;                    // one K block
+    static constexpr int SLOTS = F16 ? 4 : 20;                     // i8: resident B slots; f16: the B ring's stages
+    static constexpr int CHUNK = 0;                                // super-blocks a chunk (0: the whole K)
     // expander warps: two per TMEM lane quarter (half a row each) for 1..5 tokens; one
-    // (a whole row) above, so that 14 warps leave 128 registers a thread to the readers
-    static constexpr int EXP = M <= 5 ? 8 : 4;
+    // (a whole row) above
+    static constexpr int EXP = F16 ? 4 : 8;
     static constexpr int WARP_RD = EXP;                            // first of the 8 accumulator readers
     static constexpr int WARP_TMA = EXP + 8, WARP_MMA = EXP + 9;
     static constexpr int THREADS = (EXP + 10) * 32;
     static constexpr int OFF_STAGE = 0;
-    static constexpr int OFF_B = OFF_STAGE + kGtStages * kGtStageBytes;
-    static constexpr int OFF_X = OFF_B + SLOTS * SLOT_BYTES;       // sub-block sums [slot][t][8]
-    static constexpr int OFF_FS = OFF_X + SLOTS * M * 8 * 4;       // 2^-s [slot][t]
-    static constexpr int OFF_RED = OFF_FS + SLOTS * M * 4;         // pair exchange [quarter][lane][t]
+    static constexpr int OFF_B = OFF_STAGE + STAGES * kGtStageBytes;
+    static constexpr int OFF_X = OFF_B + SLOTS * SLOT_BYTES;       // i8: sub-block sums [slot][t][8]
+    static constexpr int OFF_FS = OFF_X + (F16 ? 0 : SLOTS * M * 8 * 4);  // i8: 2^-s [slot][t]
+    static constexpr int OFF_RED = OFF_FS + (F16 ? 0 : SLOTS * M * 4);    // pair exchange [quarter][lane][t]
     static constexpr int OFF_HDR = align16(OFF_RED + 4 * 32 * M * 4);  // [kGtHdrs][128] x 16 B
     static constexpr int OFF_BAR = OFF_HDR + kGtHdrs * kGtRows * 16;
-    static constexpr int NBARS = 2 * kGtStages + 2 * AB + 2 * DB + 8 + 2 * kGtHdrs + 2;
+    static constexpr int NBARS = 2 * STAGES + 2 * AB + 2 * DB + 8 + 2 * kGtHdrs + 2 + (F16 ? 2 * SLOTS : 0);
     static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
     static constexpr int SMEM = OFF_MISC + 16 + 1024;              // + alignment slack
-    static_assert(TM_A + 64 * AB <= kGtTmemCols, "tensor memory");
+    static_assert(TM_A + ACOLS * AB <= kGtTmemCols, "tensor memory");
     static_assert(OFF_B % 1024 == 0 && SLOT_BYTES % 1024 == 0 && HALF_BYTES % 1024 == 0, "B alignment");
-    static_assert(3 * M <= NC, "B rows");
+    static_assert((F16 ? 2 : 3) * M <= NC, "B rows");
+    static_assert(SLOT_BYTES % 1024 == 0 && OFF_B % 1024 == 0, "B blocks are 1024-byte aligned");
     static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct GtBars {
-    uint64_t* full;    // [kGtStages] TMA -> expanders
-    uint64_t* empty;   // [kGtStages] expanders (EXP warps) -> TMA
+    uint64_t* full;    // [STAGES] TMA -> expanders
+    uint64_t* empty;   // [STAGES] expanders (EXP warps) -> TMA
     uint64_t* afull;   // [AB] A written (EXP warps) -> MMA
     uint64_t* aempty;  // [AB] MMA done -> expanders
     uint64_t* dfull;   // [DB] MMA done -> accumulator readers
@@ -105,6 +117,8 @@ struct GtBars {
     uint64_t* hempty;  // [kGtHdrs] headers read (8 warps) -> expanders
     uint64_t* bfull;   // B operand built (8 warps) -> MMA and accumulator readers
     uint64_t* drain;
+    uint64_t* bring;   // f16: [SLOTS] B block landed (TMA) -> MMA
+    uint64_t* bfree;   // f16: [SLOTS] MMA done -> TMA
 };
 template <int M>
 __device__ __forceinline__ GtBars gt_bars(uint8_t* smem) {
@@ -112,8 +126,8 @@ __device__ __forceinline__ GtBars gt_bars(uint8_t* smem) {
     uint64_t* b = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     GtBars r;
     r.full = b;
-    r.empty = r.full + kGtStages;
-    r.afull = r.empty + kGtStages;
+    r.empty = r.full + C::STAGES;
+    r.afull = r.empty + C::STAGES;
     r.aempty = r.afull + C::AB;
     r.dfull = r.aempty + C::AB;
     r.dempty = r.dfull + C::DB;
@@ -123,6 +137,8 @@ __device__ __forceinline__ GtBars gt_bars(uint8_t* smem) {
     r.hempty = r.hfull + kGtHdrs;
     r.bfull = r.hempty + kGtHdrs;
     r.drain = r.bfull + 1;
+    r.bring = r.drain + 1;
+    r.bfree = r.bring + (C::F16 ? C::SLOTS : 0);
     return r;
 }
 
@@ -145,6 +161,32 @@ __host__ __device__ constexpr uint32_t idesc_u8s8_s32(int m, int n) {
            | (1u << 10)                               // B format: signed 8-bit
            | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
            | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+// D[tmem] = A[tmem] * B[smem desc]^T, kind::f16 (A and B f16, D f32), one thread.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// kind::f16 instruction descriptor: A and B f16, D f32, both K-major
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
+    return (1u << 4)                                  // D format: f32
+           | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+           | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+// a * b + c on f16 pairs, one rounding
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// f16 bits of a small integer |v| <= 2048 * 64 with at most 11 significant bits (exact)
+__device__ __forceinline__ uint32_t half_bits_int(int v) {
+    return static_cast<uint32_t>(__half_as_ushort(__int2half_rn(v)));
 }
 
 // 32 lanes x W consecutive 32-bit columns (one row per thread); W > 16 in loads of 16
@@ -271,6 +313,103 @@ __device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int 
     if (lane == 0) reinterpret_cast<float*>(smem + C::OFF_FS)[slot * M + t] = pow2_exact(-s);
 }
 
+// B blocks of 6..16 tokens, once per call: block b (GtCfg<M>::SLOT_BYTES bytes) holds, for
+// token t, rows 2t and 2t + 1 (f16, K-major, 128-byte swizzle):
+//  * K blocks 0..3: x * 2^s as hi + lo, hi = f16(x 2^s), lo = f16(x 2^s - hi), with one
+//    power of two a token (max|x| * 2^s < 2^15; the residual is below 2^-22 of max|x|), in
+//    the A operand's k order: k = 64c + 32hb + 4u + r sits at e = 64c + 8u + 4hb + 2(r & 1)
+//    + (r >> 1), so that one 32-bit word of nibbles gives the f16 pairs (k, k + 2) of A with
+//    a mask (see the expanders);
+//  * K block 4, elements 0..7: the sub-block sums X_j = sum of x over sub-block j (in fp32)
+//    times 2^(s-5), as hi + lo; elements 8..15 zero.
+// fs[t] = 2^-s.  Grid (tokens, groups of 4 super-blocks), 256 threads: thread k of a
+// super-block; every CTA first finds its token's max|x| over the whole row.
+template <int M>
+__global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict__ x, int nblk,
+                                                         uint8_t* __restrict__ bglob, float* __restrict__ fs) {
+    using C = GtCfg<M>;
+    pdl_launch_dependents();  // the GEMV's weight stream may start now; its B loads wait for this grid
+    __shared__ float red[8];
+    const int t = blockIdx.x, k = threadIdx.x, lane = k & 31, wid = k >> 5;
+    const int64_t K = static_cast<int64_t>(nblk) * 256;
+    const float* xr = x + t * K;
+    float am = 0.0f;
+    {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        int64_t i = k;
+        for (; i + 3 * 256 < K / 4; i += 4 * 256) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float4 v = __ldg(x4 + i + u * 256);
+                a4[u] = fmaxf(a4[u], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            }
+        }
+        for (; i < K / 4; i += 256) {
+            const float4 v = __ldg(x4 + i);
+            a4[0] = fmaxf(a4[0], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+        am = fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if (lane == 0) red[wid] = am;
+    __syncthreads();
+    am = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) am = fmaxf(am, red[w]);
+    int E = 0;  // am < 2^E
+    if (am > 0.0f && am <= 3.0e38f)
+        E = am >= 1.17549435e-38f ? static_cast<int>(__float_as_uint(am) >> 23) - 126
+                                  : static_cast<int>(__float_as_uint(am * 18446744073709551616.0f) >> 23) - 190;
+    const int s = min(15 - E, 149);
+    const int s1 = min(s, 127), sx = s - 5, sx1 = max(min(sx, 127), -126);
+    const float m1 = pow2_exact(s1), m2 = pow2_exact(s - s1);     // x * 2^s exactly, in two steps
+    const float n1 = pow2_exact(sx1), n2 = pow2_exact(sx - sx1);   // X * 2^(s-5)
+    if (blockIdx.y == 0 && k == 0) fs[t] = pow2_exact(-s);
+    // this thread's element of a super-block and its position in the A operand's k order
+    const int c = k >> 6, hb = (k >> 5) & 1, u = (k >> 2) & 7, r = k & 3;
+    const int ee = 8 * u + 4 * hb + 2 * (r & 1) + (r >> 1);  // within K block c
+    const int b0 = blockIdx.y * 4, b1 = min(nblk, b0 + 4);
+    float v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = b0 + q < b1 ? __ldg(xr + static_cast<int64_t>(b0 + q) * 256 + k) : 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (b0 + q >= b1) break;
+        uint8_t* blk = bglob + static_cast<size_t>(b0 + q) * C::SLOT_BYTES;
+        const float xs = (v[q] * m1) * m2;
+        const __half hi = __float2half_rn(xs);
+        const __half lo = __float2half_rn(xs - __half2float(hi));  // the difference is exact in fp32
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            const int n = 2 * t + p;
+            *reinterpret_cast<__half*>(blk + c * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 +
+                                       (((ee >> 3) ^ (n & 7)) << 4) + (ee & 7) * 2) = p ? lo : hi;
+        }
+        // sub-block wid = elements 32 wid .. 32 wid + 31 of this super-block
+        float X = v[q];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) X += __shfl_xor_sync(0xffffffffu, X, o);
+        if (lane == 0) {
+            const float xs2 = (X * n1) * n2;
+            const __half xh = __float2half_rn(xs2);
+            const __half xl = __float2half_rn(xs2 - __half2float(xh));
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int n = 2 * t + p;
+                *reinterpret_cast<__half*>(blk + 4 * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 +
+                                           ((n & 7) << 4) + wid * 2) = p ? xl : xh;
+            }
+        }
+        if (k < 2) {  // elements 8..15 of K block 4 meet the zero columns of A: keep them finite
+            const int n = 2 * t + k;
+            *reinterpret_cast<uint4*>(blk + 4 * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 +
+                                      ((1 ^ (n & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+}
+
 // exact int -> float for |v| < 2^22 on the FMA pipe: the bits of 1.5 * 2^23 + v
 __device__ __forceinline__ float small_i2f(uint32_t v) {
     return __uint_as_float(v + 0x4B400000u) - 12582912.0f;
@@ -280,13 +419,15 @@ template <int M>
 __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
     const __grid_constant__ CUtensorMap tmW, int nblk, int ntiles, int64_t N, int64_t units, int cw, int split,
     int seg_max, const float* __restrict__ x, const float* __restrict__ bias, float* __restrict__ y, int64_t ldy,
-    float* __restrict__ partials, int* __restrict__ counters, int* status) {
+    float* __restrict__ partials, int* __restrict__ counters, const uint8_t* __restrict__ bglob,
+    const float* __restrict__ fsg, int* status) {
     using C = GtCfg<M>;
     static_assert(M >= 1 && M <= kGtMaxTok, "1..16 tokens");
     constexpr int W = M == 1 ? 4 : (M == 2 ? 8 : 16 * ((3 * M + 15) / 16));  // accumulator columns read per sub-block
     constexpr int JB = M <= 2 ? 4 : (M <= 5 ? 2 : 1);                         // sub-blocks read per batch
     constexpr bool kOneChunk = C::CHUNK == 0;                                 // cw == nblk
     constexpr uint32_t idesc = idesc_u8s8_s32(128, C::NC);
+    constexpr uint32_t idesc16 = idesc_f16_f32(128, C::NC);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const GtBars B = gt_bars<M>(smem);
@@ -309,7 +450,7 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
     };
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kGtStages; ++i) {
+        for (int i = 0; i < C::STAGES; ++i) {
             fh3::mbar_init(&B.full[i], 1);
             fh3::mbar_init(&B.empty[i], C::EXP);
         }
@@ -319,7 +460,7 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
         }
         for (int i = 0; i < C::DB; ++i) {
             fh3::mbar_init(&B.dfull[i], 1);
-            fh3::mbar_init(&B.dempty[i], 8);
+            fh3::mbar_init(&B.dempty[i], C::F16 ? 4 : 8);  // f16: the part-0 readers alone read them
         }
         for (int i = 0; i < 4; ++i) {
             fh3::mbar_init(&B.xfull[i], 1);
@@ -331,6 +472,11 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
         }
         fh3::mbar_init(B.bfull, 8);
         fh3::mbar_init(B.drain, 1);
+        if constexpr (C::F16)
+            for (int i = 0; i < C::SLOTS; ++i) {
+                fh3::mbar_init(&B.bring[i], 1);
+                fh3::mbar_init(&B.bfree[i], 1);
+            }
         *abort_flag = 0;
         fh3::fence_mbar_init();
     }
@@ -343,11 +489,11 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
     fh3::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // unit i of this run -> stage i % kGtStages; weights do not depend on earlier kernels
+    // unit i of this run -> stage i % STAGES; weights do not depend on earlier kernels
     int issued = 0;
     UnitPos lp = p_first;  // the next unit to load
     auto issue = [&](int i) {
-        const int st = i % kGtStages;
+        const int st = i % C::STAGES;
         fh3::mbar_arrive_expect_tx(&B.full[st], kGtStageBytes);
         fh3::tma_load_2d(smem + C::OFF_STAGE + st * kGtStageBytes, &tmW, &B.full[st], lp.b * fh3::kQ4KBytes,
                          lp.tile * kGtRows);
@@ -355,7 +501,7 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
     };
     if (warp == C::WARP_TMA && lane == 0) {
         fh3::tma_prefetch_desc(&tmW);
-        for (; issued < min(n, kGtStages); ++issued) issue(issued);
+        for (; issued < min(n, C::STAGES); ++issued) issue(issued);
     }
     pdl_launch_dependents();
     // Only the accumulator readers touch x, y and the scratch (after griddepcontrol.wait);
@@ -370,17 +516,48 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
 
     if (warp == C::WARP_TMA) {
         // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
+        if (C::F16 && lane == 0) {
+            // weights of unit i, then its B block (super-block b of the pre-pass's output;
+            // after griddepcontrol.wait), each into its own ring
+            pdl_wait();
+            UnitPos bp = p_first;
+            int bissued = 0;
+            bool ok = true;
+            for (int i = 0; i < n && ok; ++i) {
+                if (i >= issued) {
+                    const int st = i % C::STAGES;
+                    if (!(ok = fh3::mbar_wait<kGtSpin>(&B.empty[st], ((i / C::STAGES) - 1) & 1, abort_flag, status)))
+                        break;
+                    issue(i);
+                    issued = i + 1;
+                }
+                const int bs = i % C::SLOTS;
+                if (i >= C::SLOTS &&
+                    !(ok = fh3::mbar_wait<kGtSpin>(&B.bfree[bs], ((i / C::SLOTS) - 1) & 1, abort_flag, status)))
+                    break;
+                fh3::mbar_arrive_expect_tx(&B.bring[bs], C::SLOT_BYTES);
+                fh3::bulk_load(smem + C::OFF_B + bs * C::SLOT_BYTES, bglob + static_cast<size_t>(bp.b) * C::SLOT_BYTES,
+                               C::SLOT_BYTES, &B.bring[bs]);
+                bissued = i + 1;
+                unit_next(bp, ntiles, nblk, cw);
+            }
+            // every copy issued lands before the CTA can leave
+            volatile int no_abort = 0;
+            for (int i = max(0, issued - C::STAGES); i < issued; ++i)
+                fh3::mbar_wait<true>(&B.full[i % C::STAGES], (i / C::STAGES) & 1, &no_abort, nullptr);
+            for (int i = max(0, bissued - C::SLOTS); i < bissued; ++i)
+                fh3::mbar_wait<true>(&B.bring[i % C::SLOTS], (i / C::SLOTS) & 1, &no_abort, nullptr);
+        } else if (lane == 0) {
             for (; issued < n; ++issued) {
-                const int st = issued % kGtStages;
-                if (!fh3::mbar_wait<kGtSpin>(&B.empty[st], ((issued / kGtStages) - 1) & 1, abort_flag, status))
+                const int st = issued % C::STAGES;
+                if (!fh3::mbar_wait<kGtSpin>(&B.empty[st], ((issued / C::STAGES) - 1) & 1, abort_flag, status))
                     break;
                 issue(issued);
             }
             // every copy issued lands before the CTA can leave
             volatile int no_abort = 0;
-            for (int i = max(0, issued - kGtStages); i < issued; ++i)
-                fh3::mbar_wait<true>(&B.full[i % kGtStages], (i / kGtStages) & 1, &no_abort, nullptr);
+            for (int i = max(0, issued - C::STAGES); i < issued; ++i)
+                fh3::mbar_wait<true>(&B.full[i % C::STAGES], (i / C::STAGES) & 1, &no_abort, nullptr);
         }
     } else if (warp == C::WARP_MMA) {
         // ------------------------------------------------------------ MMA issuer
@@ -395,10 +572,28 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
                     break;
                 fh3::tc_fence_after();
                 const uint32_t bs = bbase + slot_of(mp.b) * C::SLOT_BYTES;
+                if constexpr (C::F16) {
+                    // the unit's B block from the ring; 16 steps of K = 16 of sc * q into the
+                    // unit's first accumulator, one of the mins against the sub-block sums into
+                    // its second
+                    const int bsl = i % C::SLOTS;
+                    if (!fh3::mbar_wait<true>(&B.bring[bsl], (i / C::SLOTS) & 1, abort_flag, status)) break;
+                    fh3::tc_fence_after();
+                    const uint32_t bb = bbase + bsl * C::SLOT_BYTES;
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    umma_i8_ts(tmem + C::DCOLS * d + C::NC * j, tmem + C::TM_A + 64 * ab + 8 * j,
-                               fh3::sdesc_sw128(bs + (j >> 2) * C::HALF_BYTES) + 2 * (j & 3), idesc, 0u);
+                    for (int k = 0; k < 16; ++k)
+                        umma_f16_ts(tmem + C::DCOLS * d, tmem + C::TM_A + C::ACOLS * ab + 8 * k,
+                                    fh3::sdesc_sw128(bb + (k >> 2) * C::HALF_BYTES) + 2 * (k & 3), idesc16,
+                                    k != 0 ? 1u : 0u);
+                    umma_f16_ts(tmem + C::DCOLS * d + C::NC, tmem + C::TM_A + C::ACOLS * ab + 128,
+                                fh3::sdesc_sw128(bb + 4 * C::HALF_BYTES), idesc16, 0u);
+                    fh3::umma_commit(&B.bfree[bsl]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        umma_i8_ts(tmem + C::DCOLS * d + C::NC * j, tmem + C::TM_A + C::ACOLS * ab + 8 * j,
+                                   fh3::sdesc_sw128(bs + (j >> 2) * C::HALF_BYTES) + 2 * (j & 3), idesc, 0u);
+                }
                 fh3::umma_commit(&B.dfull[d]);
                 fh3::umma_commit(&B.aempty[ab]);
                 unit_next(mp, ntiles, nblk, cw);
@@ -416,8 +611,8 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
         const int r = q * 32 + lane;
         const uint32_t ta0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::TM_A + 32 * part0;
         for (int i = 0; i < n; ++i) {
-            const int st = i % kGtStages, ab = i % C::AB;
-            if (!wait_all(&B.full[st], (i / kGtStages) & 1)) break;
+            const int st = i % C::STAGES, ab = i % C::AB;
+            if (!wait_all(&B.full[st], (i / C::STAGES) & 1)) break;
             const uint8_t* rp = smem + C::OFF_STAGE + st * kGtStageBytes + r * fh3::kQ4KBytes + 16 + 64 * part0;
             uint4 qv[4 * PARTS];
 #pragma unroll
@@ -438,20 +633,59 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
             }
             if (i >= C::AB && !wait_all(&B.aempty[ab], ((i / C::AB) - 1) & 1)) break;
             fh3::tc_fence_after();
+            if constexpr (C::F16) {
+                // column 32c + 4u + {0, 1, 2, 3} of chunk c, word u (bytes b0..b3) holds the f16
+                // pairs sc * (lo b0, lo b2), (lo b1, lo b3), (hi b0, hi b2), (hi b1, hi b3):
+                // 0x6400 | q is the f16 1024 + q, and (1024 + q) * sc - 1024 sc = sc * q exactly
+                uint32_t s2[8], n2[8], mo[16];
 #pragma unroll
-            for (int pp = 0; pp < PARTS; ++pp) {
-                uint32_t o[32];
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const uint4 a = qv[4 * pp + 2 * cc], b2 = qv[4 * pp + 2 * cc + 1];
-                    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b2.x, b2.y, b2.z, b2.w};
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        o[16 * cc + k] = w[k] & 0x0F0F0F0Fu;             // k = 64c + 4k .. +3
-                        o[16 * cc + 8 + k] = (w[k] >> 4) & 0x0F0F0F0Fu;  // k = 64c + 32 + 4k .. +3
-                    }
+                for (int j = 0; j < 8; ++j) {
+                    int sc, m;
+                    fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, j, sc, m);
+                    const uint32_t hs = half_bits_int(sc), hn = half_bits_int(-1024 * sc);
+                    s2[j] = hs | (hs << 16);
+                    n2[j] = hn | (hn << 16);
+                    if (j & 1)
+                        mo[j >> 1] |= half_bits_int(m) << 16;
+                    else
+                        mo[j >> 1] = half_bits_int(m);
                 }
-                fh3::tmem_st32(ta0 + 64 * ab + 32 * pp, o);
+#pragma unroll
+                for (int j = 4; j < 16; ++j) mo[j] = 0u;
+                // columns 128 .. 143: the mins m_0 .. m_7 as elements 0..7 of one K = 16 step
+                fh3::tmem_st16(ta0 + C::ACOLS * ab + 128, mo);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 a = qv[2 * c], b2 = qv[2 * c + 1];
+                    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b2.x, b2.y, b2.z, b2.w};
+                    uint32_t o[32];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        o[4 * u + 0] = hfma2_bits((w[u] & 0x000F000Fu) | 0x64006400u, s2[2 * c], n2[2 * c]);
+                        o[4 * u + 1] = hfma2_bits(((w[u] >> 8) & 0x000F000Fu) | 0x64006400u, s2[2 * c], n2[2 * c]);
+                        o[4 * u + 2] =
+                            hfma2_bits(((w[u] >> 4) & 0x000F000Fu) | 0x64006400u, s2[2 * c + 1], n2[2 * c + 1]);
+                        o[4 * u + 3] =
+                            hfma2_bits(((w[u] >> 12) & 0x000F000Fu) | 0x64006400u, s2[2 * c + 1], n2[2 * c + 1]);
+                    }
+                    fh3::tmem_st32(ta0 + C::ACOLS * ab + 32 * c, o);
+                }
+            } else {
+#pragma unroll
+                for (int pp = 0; pp < PARTS; ++pp) {
+                    uint32_t o[32];
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc) {
+                        const uint4 a = qv[4 * pp + 2 * cc], b2 = qv[4 * pp + 2 * cc + 1];
+                        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b2.x, b2.y, b2.z, b2.w};
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            o[16 * cc + k] = w[k] & 0x0F0F0F0Fu;             // k = 64c + 4k .. +3
+                            o[16 * cc + 8 + k] = (w[k] >> 4) & 0x0F0F0F0Fu;  // k = 64c + 32 + 4k .. +3
+                        }
+                    }
+                    fh3::tmem_st32(ta0 + C::ACOLS * ab + 32 * pp, o);
+                }
             }
             fh3::tmem_st_wait();
             fh3::tc_fence_before();
@@ -485,7 +719,7 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
             // B operand of the super-blocks this run touches: (token, slot) items over the
             // eight warps, four items' x loads in flight at a time
             pdl_wait();  // x, y and the scratch are ours from here on
-            const int w8 = warp - C::WARP_RD, items = M * nslots;
+            const int w8 = warp - C::WARP_RD, items = C::F16 ? 0 : M * nslots;  // f16: B comes from the pre-pass
             for (int it0 = w8; it0 < items; it0 += 4 * 8) {
                 float4 xv[4][2];
 #pragma unroll
@@ -505,7 +739,7 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
                     const int it = it0 + 8 * k;
                     if (it < items) {
                         const int t = it / nslots;
-                        build_b<M>(xv[k][0], xv[k][1], t, it - t * nslots, smem, lane);
+                        if constexpr (!C::F16) build_b<M>(xv[k][0], xv[k][1], t, it - t * nslots, smem, lane);
                     }
                 }
             }
@@ -514,6 +748,9 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
             if (lane == 0) fh3::mbar_arrive(B.bfull);
         }
         bool ok = wait_all(B.bfull, 0);  // every warp's sub-block sums and scales
+        float fsr[C::F16 ? M : 1];       // f16: 2^-s of each token, from the pre-pass
+#pragma unroll
+        for (int t = 0; t < (C::F16 ? M : 1); ++t) fsr[t] = C::F16 ? __ldg(fsg + t) : 0.0f;
         // One chunk only: the run's last tile, when split.  If, two units before the run
         // ends, every other segment has already counted itself, this segment is the last
         // one; the others' partials are read then, off the critical path (no CTA ever waits
@@ -651,8 +888,12 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
             const uint4 hd = lds128(smem + C::OFF_HDR + (hs * kGtRows + r) * 16);
             __syncwarp();
             if (lane == 0) fh3::mbar_arrive(&B.hempty[hs]);
-            if (!wait_all(&B.dfull[d], (i / C::DB) & 1)) break;
-            fh3::tc_fence_after();
+            // 6..16 tokens: the part-1 warps read no accumulator (and release none), so they do
+            // not wait for the MMA either
+            if (!C::F16 || part == 0) {
+                if (!wait_all(&B.dfull[d], (i / C::DB) & 1)) break;
+                fh3::tc_fence_after();
+            }
             const int slot = slot_of(ep.b);
             const float dd = fh3::h2f_bits(hd.x), dmin = fh3::h2f_bits(hd.x >> 16);
             if constexpr (M <= 5) {
@@ -692,40 +933,24 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
 #pragma unroll
                 for (int t = 0; t < M; ++t) acc[t] = fmaf(sfs[slot * M + t], sum[t], acc[t]) - msum[t];
             } else {
-                // 6..16 tokens: the 6-bit scales applied in integers, S_tp = sum over this part's
-                // four sub-blocks of sc_j * P_tjp (|S| <= 4 * 63 * 61440 < 2^24: exact, and exactly
-                // convertible), so each token costs three conversions a unit instead of twelve;
-                // the min term is subtracted from the accumulator directly
-                int S[M][3];
-#pragma unroll
-                for (int t = 0; t < M; ++t) S[t][0] = S[t][1] = S[t][2] = 0;
-#pragma unroll
-                for (int j0 = 0; j0 < 4; ++j0) {
-                    uint32_t v[W];
-                    tmem_ld_w<W>(tl + C::DCOLS * d + C::NC * (4 * part + j0), v);
+                // 6..16 tokens: accumulator 1 holds sum_j sc_j P_tj and accumulator 2 sum_j m_j X_tj
+                // (x and X scaled by 2^s and 2^(s-5)), each as hi and lo columns 2t, 2t + 1; the
+                // part-0 warp reads both, the part-1 warp has nothing to add
+                if (part == 0) {
+                    uint32_t v[2 * C::NC];
+                    tmem_ld_w<2 * C::NC>(tl + C::DCOLS * d, v);
                     fh3::tmem_ld_wait();
                     fh3::tmem_regs_ready(v);
-                    if (j0 == 3) {  // every column of this buffer is read
-                        fh3::tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) fh3::mbar_arrive(&B.dempty[d]);
-                    }
-                    const int j = 4 * part + j0;
-                    int sc, m;
-                    fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, j, sc, m);
-                    const float ndm = -(dmin * small_i2f(static_cast<uint32_t>(m)));
+                    fh3::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) fh3::mbar_arrive(&B.dempty[d]);
+                    const float dm32 = 32.0f * dmin;
 #pragma unroll
                     for (int t = 0; t < M; ++t) {
-#pragma unroll
-                        for (int p = 0; p < 3; ++p) S[t][p] += sc * static_cast<int>(v[3 * t + p]);
-                        acc[t] = fmaf(ndm, sx[(slot * M + t) * 8 + j], acc[t]);
+                        const float p = __uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1]);
+                        const float q = __uint_as_float(v[C::NC + 2 * t]) + __uint_as_float(v[C::NC + 2 * t + 1]);
+                        acc[t] = fmaf(fsr[t], fmaf(dd, p, -dm32 * q), acc[t]);
                     }
-                }
-#pragma unroll
-                for (int t = 0; t < M; ++t) {
-                    const float p = fmaf(65536.0f, __int2float_rn(S[t][2]),
-                                         fmaf(256.0f, __int2float_rn(S[t][1]), __int2float_rn(S[t][0])));
-                    acc[t] = fmaf(dd * sfs[slot * M + t], p, acc[t]);  // 2^-s is a power of two: exact
                 }
             }
             if (ep.b == ep.k * cw + ep.w - 1 || i == n - 1)
@@ -756,8 +981,14 @@ struct GtLaunch {
 
 template <int M>
 int launch_tc(const CUtensorMap& tm, const GtLaunch& L, const float* x, const float* bias, float* y,
-              float* partials, int* counters, int* status, cudaStream_t s) {
+              float* partials, int* counters, uint8_t* bglob, float* fsg, int* status, cudaStream_t s) {
     constexpr int smem = GtCfg<M>::SMEM;
+    if constexpr (GtCfg<M>::F16) {
+        // the B blocks first (an ordinary launch: it reads x, written by earlier work)
+        gemv_xprep_kernel<M><<<dim3(M, static_cast<unsigned>((L.nblk + 3) / 4)), 256, 0, s>>>(x, L.nblk, bglob, fsg);
+        const int rc = fh3host::check_cuda(cudaGetLastError(), "gemv_xprep_kernel launch");
+        if (rc) return rc;
+    }
     static bool attr = false;
     if (!attr) {
         const int rc = fh3host::check_cuda(
@@ -775,32 +1006,32 @@ int launch_tc(const CUtensorMap& tm, const GtLaunch& L, const float* x, const fl
     cfg.attrs = at;
     cfg.numAttrs = 1;
     return fh3host::check_cuda(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M>, tm, L.nblk, L.ntiles, L.N, L.units, L.cw,
-                                                  L.split, L.seg_max, x, bias, y, L.N, partials, counters, status),
+                                                  L.split, L.seg_max, x, bias, y, L.N, partials, counters,
+                                                  static_cast<const uint8_t*>(bglob), static_cast<const float*>(fsg),
+                                                  status),
                                "gemv_tc_kernel launch");
 }
 
 template <int M>
 int dispatch_tc(int n_tok, const CUtensorMap& tm, const GtLaunch& L, const float* x, const float* bias, float* y,
-                float* partials, int* counters, int* status, cudaStream_t s) {
+                float* partials, int* counters, uint8_t* bglob, float* fsg, int* status, cudaStream_t s) {
     if constexpr (M > kGtMaxTok) {
         return 1;
     } else {
-        if (n_tok == M) return launch_tc<M>(tm, L, x, bias, y, partials, counters, status, s);
-        return dispatch_tc<M + 1>(n_tok, tm, L, x, bias, y, partials, counters, status, s);
+        if (n_tok == M) return launch_tc<M>(tm, L, x, bias, y, partials, counters, bglob, fsg, status, s);
+        return dispatch_tc<M + 1>(n_tok, tm, L, x, bias, y, partials, counters, bglob, fsg, status, s);
     }
 }
 
 // super-blocks of a chunk for n_tok tokens (0: one chunk over the whole K), and the B slots
 int gt_chunk(int n_tok) {
-    switch (n_tok <= 5 ? 5 : (n_tok <= 10 ? 10 : 16)) {
-        case 5: return 0;
-        case 10: return GtCfg<10>::CHUNK;
-        default: return GtCfg<16>::CHUNK;
-    }
+    return n_tok <= 5 ? GtCfg<5>::CHUNK : (n_tok <= 8 ? GtCfg<8>::CHUNK : GtCfg<16>::CHUNK);
 }
-int gt_slots(int n_tok) {
-    return n_tok <= 5 ? GtCfg<5>::SLOTS : (n_tok <= 10 ? GtCfg<10>::SLOTS : GtCfg<16>::SLOTS);
+int gt_slots(int n_tok) {  // 6..16 tokens stream B: no limit
+    return n_tok <= 5 ? GtCfg<5>::SLOTS : (1 << 30);
 }
+// bytes of one B block of 6..16 tokens
+int gt_bblock(int n_tok) { return n_tok <= 8 ? GtCfg<8>::SLOT_BYTES : GtCfg<16>::SLOT_BYTES; }
 
 }  // namespace
 
@@ -842,6 +1073,14 @@ int gemv_tc(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float*
         scratch(c, 14, static_cast<size_t>(ntiles) * L.seg_max * kGtRows * n_tok * 4, s));
     int* counters = static_cast<int*>(scratch_zeroed(c, 15, static_cast<size_t>(ntiles) * 4 * 4, s));  // (tile, quarter)
     if (!partials || !counters) return FH3_E_NOMEM;
+    uint8_t* bglob = nullptr;  // 6..16 tokens: the pre-pass's B blocks, then 2^-s of each token
+    float* fsg = nullptr;
+    if (n_tok > 5) {
+        const size_t bb = static_cast<size_t>(L.nblk) * gt_bblock(n_tok);
+        bglob = static_cast<uint8_t*>(scratch(c, 9, bb + 256, s));
+        if (!bglob) return FH3_E_NOMEM;
+        fsg = reinterpret_cast<float*>(bglob + bb);
+    }
 
     CUtensorMap tm;
     const size_t row_bytes = static_cast<size_t>(L.nblk) * fh3::kQ4KBytes;
@@ -852,7 +1091,7 @@ int gemv_tc(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float*
     if (encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w->data), gdim, gstr, box, es,
                      CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
         return 1;
-    return dispatch_tc<1>(n_tok, tm, L, x, bias, y, partials, counters, ctx_status(c), s);
+    return dispatch_tc<1>(n_tok, tm, L, x, bias, y, partials, counters, bglob, fsg, ctx_status(c), s);
 }
 
 }  // namespace fh3host
