@@ -351,7 +351,7 @@ GEMV_SHAPES = ((5120, 13824), (13824, 5120), (5120, 5120))   # (in, out): fc-up,
 def gemv_kernel_name(K: int, N: int, M: int) -> str:
     """The kernel the default GEMV dispatch (csrc/gemv_mma.cu, gemv_mma) picks."""
     if N <= K or M >= 5:
-        return "gemv_tc_kernel"
+        return "gemv_tc_kernel (i8 A)" if M <= 5 else "gemv_tc_kernel (f16 A = sc*q) + gemv_xprep_kernel"
     if M <= 2:
         return "gemv_stream_kernel"
     return "gemv_mma_small_kernel" if M <= 4 else "gemv_mma_kernel"
@@ -446,7 +446,7 @@ def measure_attention(fh3, torch, rows: int, peak: float, peak_src: str, reps: i
     flops = 4.0 * rows * rows * H * D
     tf = flops / (ms * 1e-3) / 1e12
     del qkv, o
-    return {"kernel": "attention_tc_kernel (+ vt_transpose_kernel)", "rows": rows, "heads": H, "head_dim": D,
+    return {"kernel": "attention_pp_kernel (+ vt_transpose_kernel)", "rows": rows, "heads": H, "head_dim": D,
             "ms_per_launch": round(ms, 3),
             "bound": "tensor", "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak, "frac": round(tf / peak, 4),
             "peak_source": f"{peak_src} bf16_tflops", "flop_per_launch": flops,

@@ -322,42 +322,47 @@ __device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int 
 //    a mask (see the expanders);
 //  * K block 4, elements 0..7: the sub-block sums X_j = sum of x over sub-block j (in fp32)
 //    times 2^(s-5), as hi + lo; elements 8..15 zero.
-// fs[t] = 2^-s.  Grid (tokens, groups of 4 super-blocks), 256 threads: thread k of a
-// super-block; every CTA first finds its token's max|x| over the whole row.
+// fs[t] = 2^-s.  Grid (tokens, groups of 4 super-blocks), 1024 threads: thread k of
+// super-block q of the group (one element each); every CTA first finds its token's max|x|
+// over the whole row (up to four 16-byte loads a thread in flight at once).
 template <int M>
-__global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict__ x, int nblk,
-                                                         uint8_t* __restrict__ bglob, float* __restrict__ fs) {
+__global__ void __launch_bounds__(1024) gemv_xprep_kernel(const float* __restrict__ x, int nblk,
+                                                          uint8_t* __restrict__ bglob, float* __restrict__ fs) {
     using C = GtCfg<M>;
     pdl_launch_dependents();  // the GEMV's weight stream may start now; its B loads wait for this grid
-    __shared__ float red[8];
-    const int t = blockIdx.x, k = threadIdx.x, lane = k & 31, wid = k >> 5;
+    __shared__ float red[32];
+    const int t = blockIdx.x, tid = threadIdx.x, k = tid & 255, q = tid >> 8, lane = tid & 31, wid = (tid >> 5) & 7;
     const int64_t K = static_cast<int64_t>(nblk) * 256;
     const float* xr = x + t * K;
+    const int b = blockIdx.y * 4 + q;
+    const float v = b < nblk ? __ldg(xr + static_cast<int64_t>(b) * 256 + k) : 0.0f;
     float am = 0.0f;
     {
         const float4* x4 = reinterpret_cast<const float4*>(xr);
         float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        int64_t i = k;
-        for (; i + 3 * 256 < K / 4; i += 4 * 256) {
+        int64_t i = tid;
+        for (; i + 3 * 1024 < K / 4; i += 4 * 1024) {
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const float4 v = __ldg(x4 + i + u * 256);
-                a4[u] = fmaxf(a4[u], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                const float4 w = __ldg(x4 + i + u * 1024);
+                a4[u] = fmaxf(a4[u], fmaxf(fmaxf(fabsf(w.x), fabsf(w.y)), fmaxf(fabsf(w.z), fabsf(w.w))));
             }
         }
-        for (; i < K / 4; i += 256) {
-            const float4 v = __ldg(x4 + i);
-            a4[0] = fmaxf(a4[0], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-        }
+#pragma unroll
+        for (int u = 0; u < 3; ++u, i += 1024)
+            if (i < K / 4) {
+                const float4 w = __ldg(x4 + i);
+                a4[u] = fmaxf(a4[u], fmaxf(fmaxf(fabsf(w.x), fabsf(w.y)), fmaxf(fabsf(w.z), fabsf(w.w))));
+            }
         am = fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3]));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    if (lane == 0) red[wid] = am;
+    if (lane == 0) red[tid >> 5] = am;
     __syncthreads();
     am = red[0];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) am = fmaxf(am, red[w]);
+    for (int w = 1; w < 32; ++w) am = fmaxf(am, red[w]);
     int E = 0;  // am < 2^E
     if (am > 0.0f && am <= 3.0e38f)
         E = am >= 1.17549435e-38f ? static_cast<int>(__float_as_uint(am) >> 23) - 126
@@ -366,19 +371,13 @@ __global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict
     const int s1 = min(s, 127), sx = s - 5, sx1 = max(min(sx, 127), -126);
     const float m1 = pow2_exact(s1), m2 = pow2_exact(s - s1);     // x * 2^s exactly, in two steps
     const float n1 = pow2_exact(sx1), n2 = pow2_exact(sx - sx1);   // X * 2^(s-5)
-    if (blockIdx.y == 0 && k == 0) fs[t] = pow2_exact(-s);
+    if (blockIdx.y == 0 && tid == 0) fs[t] = pow2_exact(-s);
     // this thread's element of a super-block and its position in the A operand's k order
     const int c = k >> 6, hb = (k >> 5) & 1, u = (k >> 2) & 7, r = k & 3;
     const int ee = 8 * u + 4 * hb + 2 * (r & 1) + (r >> 1);  // within K block c
-    const int b0 = blockIdx.y * 4, b1 = min(nblk, b0 + 4);
-    float v[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = b0 + q < b1 ? __ldg(xr + static_cast<int64_t>(b0 + q) * 256 + k) : 0.0f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        if (b0 + q >= b1) break;
-        uint8_t* blk = bglob + static_cast<size_t>(b0 + q) * C::SLOT_BYTES;
-        const float xs = (v[q] * m1) * m2;
+    if (b < nblk) {  // uniform over each warp
+        uint8_t* blk = bglob + static_cast<size_t>(b) * C::SLOT_BYTES;
+        const float xs = (v * m1) * m2;
         const __half hi = __float2half_rn(xs);
         const __half lo = __float2half_rn(xs - __half2float(hi));  // the difference is exact in fp32
 #pragma unroll
@@ -388,7 +387,7 @@ __global__ void __launch_bounds__(256) gemv_xprep_kernel(const float* __restrict
                                        (((ee >> 3) ^ (n & 7)) << 4) + (ee & 7) * 2) = p ? lo : hi;
         }
         // sub-block wid = elements 32 wid .. 32 wid + 31 of this super-block
-        float X = v[q];
+        float X = v;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) X += __shfl_xor_sync(0xffffffffu, X, o);
         if (lane == 0) {
@@ -937,8 +936,18 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
                 // (x and X scaled by 2^s and 2^(s-5)), each as hi and lo columns 2t, 2t + 1; the
                 // part-0 warp reads both, the part-1 warp has nothing to add
                 if (part == 0) {
-                    uint32_t v[2 * C::NC];
-                    tmem_ld_w<2 * C::NC>(tl + C::DCOLS * d, v);
+                    // the two accumulators one after the other (fewer live registers)
+                    float dp[M];
+                    {
+                        uint32_t v[C::NC];
+                        tmem_ld_w<C::NC>(tl + C::DCOLS * d, v);
+                        fh3::tmem_ld_wait();
+                        fh3::tmem_regs_ready(v);
+#pragma unroll
+                        for (int t = 0; t < M; ++t) dp[t] = dd * (__uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1]));
+                    }
+                    uint32_t v[C::NC];
+                    tmem_ld_w<C::NC>(tl + C::DCOLS * d + C::NC, v);
                     fh3::tmem_ld_wait();
                     fh3::tmem_regs_ready(v);
                     fh3::tc_fence_before();
@@ -947,9 +956,8 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
                     const float dm32 = 32.0f * dmin;
 #pragma unroll
                     for (int t = 0; t < M; ++t) {
-                        const float p = __uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1]);
-                        const float q = __uint_as_float(v[C::NC + 2 * t]) + __uint_as_float(v[C::NC + 2 * t + 1]);
-                        acc[t] = fmaf(fsr[t], fmaf(dd, p, -dm32 * q), acc[t]);
+                        const float q = __uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1]);
+                        acc[t] = fmaf(fsr[t], fmaf(-dm32, q, dp[t]), acc[t]);
                     }
                 }
             }
@@ -985,7 +993,7 @@ int launch_tc(const CUtensorMap& tm, const GtLaunch& L, const float* x, const fl
     constexpr int smem = GtCfg<M>::SMEM;
     if constexpr (GtCfg<M>::F16) {
         // the B blocks first (an ordinary launch: it reads x, written by earlier work)
-        gemv_xprep_kernel<M><<<dim3(M, static_cast<unsigned>((L.nblk + 3) / 4)), 256, 0, s>>>(x, L.nblk, bglob, fsg);
+        gemv_xprep_kernel<M><<<dim3(M, static_cast<unsigned>((L.nblk + 3) / 4)), 1024, 0, s>>>(x, L.nblk, bglob, fsg);
         const int rc = fh3host::check_cuda(cudaGetLastError(), "gemv_xprep_kernel launch");
         if (rc) return rc;
     }
