@@ -448,7 +448,7 @@ void* scratch_zeroed(DevCtx* c, int slot, size_t bytes, cudaStream_t s);
 // 1..16-token Q4_K GEMV on warp-level tensor-core MMAs (gemv_mma.cu); arguments
 // already validated by the caller
 int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
-// 1..16-token Q4_K GEMV on tcgen05 integer MMAs (gemv_tc.cu); returns 1 without launching
+// 1..16-token Q4_K GEMV on tcgen05 MMAs (gemv_tc.cu); returns 1 without launching
 // when the shape or pointers do not suit it
 int gemv_tc(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s);
 // the fp32 CUDA-core GEMV (gemv.cu): uses no memory beyond x, y, bias and the weights

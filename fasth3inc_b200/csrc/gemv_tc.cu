@@ -6,33 +6,31 @@
 //   (w = (d*sc)*q - dmin*m as dequant_q4_k, src/core/fh3_quant.c:154-196).
 //
 // Work unit: a tile of 128 weight rows x one super-block (256 k).  One persistent CTA
-// per SM walks a contiguous run of units (stream-K); a tile split between CTAs is
-// finished by the last CTA to arrive on the tile's counter, adding the pieces' partial
-// sums in a fixed order.  Unit order: the super-blocks are cut into chunks of `cw`
-// (for 1..5 tokens one chunk, the whole K); within a chunk the units go tile by tile,
-// the super-block fastest.  Chunks bound the super-blocks one run touches, so the B
-// operand of 6..16 tokens (up to 12 KB a super-block) fits in shared memory.
+// per SM walks a contiguous run of units (stream-K, tile by tile, the super-block
+// fastest); a tile split between CTAs is finished by the last CTA to arrive on the tile's
+// counter, adding the pieces' partial sums in a fixed order.
 //
 // * Weights: one TMA box per unit, 144 bytes x 128 rows (the super-block column of the
-//   tile), into a 6-stage ring.  The first stages load before griddepcontrol.wait.
-// * A operand: warps 0-7 (two per TMEM lane quarter, one weight row per lane) expand the
-//   row's 128 nibble bytes into 256 u8 values q in k order (low nibbles of chunk c are
-//   k = 64c + i, high nibbles k = 64c + 32 + i) and write them to tensor memory.
-// * B operand: x of token t and super-block b, rounded to a 23-bit integer under a
-//   power of two 2^s (max|x| * 2^s < 2^22), in three balanced signed base-256 digits;
-//   row 3t + p of the B matrix holds digit p.  Built once per CTA for the super-blocks
-//   its run touches, K-major in the 128-byte swizzle layout.
-// * One kind::i8 MMA per sub-block (M 128, N = 3 * tokens rounded up to 16, K 32) into
-//   its own TMEM columns: int32 plane sums, exact.  P = P0 + 256 P1 + 65536 P2 (one fp32
-//   rounding), then the scales in fp32 as the reference forms them (d*sc and dmin*m are
-//   exact products).
-// Roles (576 threads): warps 0-7 expand (two warps per TMEM lane quarter, each half of
-// the row's nibbles), warps 8-15 read the accumulators (two per lane quarter, each four
-// sub-blocks; the pair's sums meet in shared memory at the end of a tile piece),
-// warp 16 issues the TMA loads, warp 17 allocates TMEM and issues the MMAs.  A and
-// accumulator buffers (4 and 2 for 1..5 tokens; fewer above, where one unit's
-// accumulators take 256 or 384 columns) let expansion run ahead of the MMAs and the
-// accumulator reads trail them.
+//   tile), into a ring of stages.  The first stages load before griddepcontrol.wait.
+// * 1..5 tokens (kind::i8): warps 0-7 (two per TMEM lane quarter, one weight row per
+//   lane) expand the row's 128 nibble bytes into 256 u8 values q in k order (low nibbles
+//   of chunk c are k = 64c + i, high nibbles k = 64c + 32 + i) in tensor memory.  B = x of
+//   token t and super-block b, rounded to a 23-bit integer under a power of two 2^s
+//   (max|x| * 2^s < 2^22), in three balanced signed base-256 digits (row 3t + p holds digit
+//   p), built once per CTA for the super-blocks its run touches, K-major in the 128-byte
+//   swizzle layout.  One MMA per sub-block (M 128, N 16, K 32) into its own TMEM columns:
+//   int32 plane sums, exact; P = P0 + 256 P1 + 65536 P2 (one fp32 rounding), then the
+//   scales in fp32 as the reference forms them (d*sc and dmin*m are exact products).
+// * 6..16 tokens (kind::f16): warps 0-3 (one row per lane) write A = sc * q as f16 (exact)
+//   and the eight mins; gemv_xprep_kernel writes B once per call (x as f16 hi + lo pieces
+//   and the sub-block sums, in the A operand's k order) and each unit bulk-copies its B
+//   block from L2 into a ring; 16 MMAs (K 16) give sum_j sc_j P_tj and one more the min
+//   term, each in one accumulator of 2 x tokens columns.
+// Roles: the expanders, eight accumulator readers (two per lane quarter; for 6..16 tokens
+// the part-0 warp of a quarter reads both accumulators and the part-1 warp has nothing to
+// add), one TMA warp and one warp that
+// allocates TMEM and issues the MMAs.  A and accumulator buffers let expansion run ahead
+// of the MMAs and the accumulator reads trail them.
 // Every wait is bounded; on a timeout the kernel records FH3CUDA_E_TIMEOUT, lets its
 // copies and MMAs finish and frees tensor memory.
 #include <algorithm>
@@ -44,7 +42,7 @@
 namespace {
 
 constexpr int kGtRows = 128;                               // rows of a tile = TMEM lanes
-constexpr int kGtStages = 6;                               // weight stages (fewer for 9..16 tokens)
+constexpr int kGtStages = 6;                               // weight stages of 1..5 tokens (6..16: 5)
 constexpr int kGtStageBytes = kGtRows * fh3::kQ4KBytes;    // 18432
 constexpr int kGtMaxTok = 16;
 constexpr int kGtHdrs = 8;                                 // ring of the units' 16-byte row headers
@@ -1045,7 +1043,7 @@ int gt_bblock(int n_tok) { return n_tok <= 8 ? GtCfg<8>::SLOT_BYTES : GtCfg<16>:
 
 namespace fh3host {
 
-// 1..16-token Q4_K GEMV on tcgen05 integer MMAs; returns 1 (nothing launched) when the
+// 1..16-token Q4_K GEMV on tcgen05 MMAs; returns 1 (nothing launched) when the
 // shape or the pointers do not suit it, so the caller takes the warp-MMA kernels.
 int gemv_tc(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s) {
     DevCtx* c = ctx();
