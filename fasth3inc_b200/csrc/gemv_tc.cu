@@ -79,9 +79,8 @@ struct GtCfg {
     static constexpr int HALF_BYTES = 128 * NC;                    // one K block
     static constexpr int SLOTS = F16 ? 4 : 20;                     // i8: resident B slots; f16: the B ring's stages
     static constexpr int CHUNK = 0;                                // super-blocks a chunk (0: the whole K)
-    // expander warps: two per TMEM lane quarter (half a row each) for 1..5 tokens; one
-    // (a whole row) above
-    static constexpr int EXP = F16 ? 4 : 8;
+    // expander warps: two per TMEM lane quarter, half a row each
+    static constexpr int EXP = 8;
     static constexpr int WARP_RD = EXP;                            // first of the 8 accumulator readers
     static constexpr int WARP_TMA = EXP + 8, WARP_MMA = EXP + 9;
     static constexpr int THREADS = (EXP + 10) * 32;
@@ -328,6 +327,7 @@ __global__ void __launch_bounds__(1024) gemv_xprep_kernel(const float* __restric
                                                           uint8_t* __restrict__ bglob, float* __restrict__ fs) {
     using C = GtCfg<M>;
     pdl_launch_dependents();  // the GEMV's weight stream may start now; its B loads wait for this grid
+    pdl_wait();               // x, and the B buffer the previous call may still be reading
     __shared__ float red[32];
     const int t = blockIdx.x, tid = threadIdx.x, k = tid & 255, q = tid >> 8, lane = tid & 31, wid = (tid >> 5) & 7;
     const int64_t K = static_cast<int64_t>(nblk) * 256;
@@ -615,7 +615,8 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
 #pragma unroll
             for (int c = 0; c < 4 * PARTS; ++c) qv[c] = lds128(rp + 16 * c);
             uint4 hd = make_uint4(0u, 0u, 0u, 0u);
-            if (part0 == 0) hd = lds128(rp - 16);  // the row's header: d, dmin, scales, mins
+            if (part0 == 0 || C::F16)  // the row's header: d, dmin, scales, mins
+                hd = lds128(smem + C::OFF_STAGE + st * kGtStageBytes + r * fh3::kQ4KBytes);
             // these generic-proxy reads must be performed before the TMA (async proxy)
             // refills the stage: a cross-proxy fence, then the release
             fh3::fence_proxy_async_smem();
@@ -633,39 +634,48 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
             if constexpr (C::F16) {
                 // column 32c + 4u + {0, 1, 2, 3} of chunk c, word u (bytes b0..b3) holds the f16
                 // pairs sc * (lo b0, lo b2), (lo b1, lo b3), (hi b0, hi b2), (hi b1, hi b3):
-                // 0x6400 | q is the f16 1024 + q, and (1024 + q) * sc - 1024 sc = sc * q exactly
-                uint32_t s2[8], n2[8], mo[16];
+                // 0x6400 | q is the f16 1024 + q, and (1024 + q) * sc - 1024 sc = sc * q exactly.
+                // This warp's half of the row: chunks 2 part0 and 2 part0 + 1.
+                const uint32_t taf = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::TM_A + C::ACOLS * ab;
+                if (part0 == 0) {
+                    // columns 128 .. 143: the mins m_0 .. m_7 as elements 0..7 of one K = 16 step
+                    uint32_t mo[16];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    int sc, m;
-                    fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, j, sc, m);
-                    const uint32_t hs = half_bits_int(sc), hn = half_bits_int(-1024 * sc);
-                    s2[j] = hs | (hs << 16);
-                    n2[j] = hn | (hn << 16);
-                    if (j & 1)
-                        mo[j >> 1] |= half_bits_int(m) << 16;
-                    else
-                        mo[j >> 1] = half_bits_int(m);
+                    for (int j = 0; j < 8; ++j) {
+                        int sc, m;
+                        fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, j, sc, m);
+                        if (j & 1)
+                            mo[j >> 1] |= half_bits_int(m) << 16;
+                        else
+                            mo[j >> 1] = half_bits_int(m);
+                    }
+#pragma unroll
+                    for (int j = 4; j < 16; ++j) mo[j] = 0u;
+                    fh3::tmem_st16(taf + 128, mo);
                 }
 #pragma unroll
-                for (int j = 4; j < 16; ++j) mo[j] = 0u;
-                // columns 128 .. 143: the mins m_0 .. m_7 as elements 0..7 of one K = 16 step
-                fh3::tmem_st16(ta0 + C::ACOLS * ab + 128, mo);
+                for (int cl = 0; cl < 2; ++cl) {
+                    const int c = 2 * part0 + cl;
+                    uint32_t s2[2], n2[2];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint4 a = qv[2 * c], b2 = qv[2 * c + 1];
+                    for (int h = 0; h < 2; ++h) {
+                        int sc, m;
+                        fh3::q4k_scale_min_words(hd.y, hd.z, hd.w, 2 * c + h, sc, m);
+                        const uint32_t hs = half_bits_int(sc), hn = half_bits_int(-1024 * sc);
+                        s2[h] = hs | (hs << 16);
+                        n2[h] = hn | (hn << 16);
+                    }
+                    const uint4 a = qv[2 * cl], b2 = qv[2 * cl + 1];
                     const uint32_t w[8] = {a.x, a.y, a.z, a.w, b2.x, b2.y, b2.z, b2.w};
                     uint32_t o[32];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
-                        o[4 * u + 0] = hfma2_bits((w[u] & 0x000F000Fu) | 0x64006400u, s2[2 * c], n2[2 * c]);
-                        o[4 * u + 1] = hfma2_bits(((w[u] >> 8) & 0x000F000Fu) | 0x64006400u, s2[2 * c], n2[2 * c]);
-                        o[4 * u + 2] =
-                            hfma2_bits(((w[u] >> 4) & 0x000F000Fu) | 0x64006400u, s2[2 * c + 1], n2[2 * c + 1]);
-                        o[4 * u + 3] =
-                            hfma2_bits(((w[u] >> 12) & 0x000F000Fu) | 0x64006400u, s2[2 * c + 1], n2[2 * c + 1]);
+                        o[4 * u + 0] = hfma2_bits((w[u] & 0x000F000Fu) | 0x64006400u, s2[0], n2[0]);
+                        o[4 * u + 1] = hfma2_bits(((w[u] >> 8) & 0x000F000Fu) | 0x64006400u, s2[0], n2[0]);
+                        o[4 * u + 2] = hfma2_bits(((w[u] >> 4) & 0x000F000Fu) | 0x64006400u, s2[1], n2[1]);
+                        o[4 * u + 3] = hfma2_bits(((w[u] >> 12) & 0x000F000Fu) | 0x64006400u, s2[1], n2[1]);
                     }
-                    fh3::tmem_st32(ta0 + C::ACOLS * ab + 32 * c, o);
+                    fh3::tmem_st32(taf + 32 * c, o);
                 }
             } else {
 #pragma unroll
@@ -752,7 +762,7 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
         // ends, every other segment has already counted itself, this segment is the last
         // one; the others' partials are read then, off the critical path (no CTA ever waits
         // for another).
-        constexpr int kPre = kOneChunk ? kGtPreSegs : 1;
+        constexpr int kPre = kOneChunk && !C::F16 ? kGtPreSegs : 1;
         const int64_t t_last = p_last.tile;
         int cf_last = 0;
         const int nseg_last = kOneChunk ? piece_ctas(0, t_last, cf_last) : 0;
@@ -760,7 +770,7 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
         bool pre = false;
         float pv[kPre][M];
         auto try_prefetch = [&]() {
-            if (part != 0 || nseg_last < 2 || nseg_last > kGtPreSegs + 1 || nseg_last > seg_max) return;
+            if (C::F16 || part != 0 || nseg_last < 2 || nseg_last > kGtPreSegs + 1 || nseg_last > seg_max) return;
             int cnt = 0;
             if (lane == 0)
                 asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(cnt) : "l"(counters + t_last * 4 + q) : "memory");
@@ -990,9 +1000,17 @@ int launch_tc(const CUtensorMap& tm, const GtLaunch& L, const float* x, const fl
               float* partials, int* counters, uint8_t* bglob, float* fsg, int* status, cudaStream_t s) {
     constexpr int smem = GtCfg<M>::SMEM;
     if constexpr (GtCfg<M>::F16) {
-        // the B blocks first (an ordinary launch: it reads x, written by earlier work)
-        gemv_xprep_kernel<M><<<dim3(M, static_cast<unsigned>((L.nblk + 3) / 4)), 1024, 0, s>>>(x, L.nblk, bglob, fsg);
-        const int rc = fh3host::check_cuda(cudaGetLastError(), "gemv_xprep_kernel launch");
+        // the B blocks first; a programmatic dependent launch too, so its CTAs are placed
+        // as the previous kernel's leave (it waits for that kernel before touching memory)
+        cudaLaunchConfig_t pc = {};
+        pc.gridDim = dim3(M, static_cast<unsigned>((L.nblk + 3) / 4), 1);
+        pc.blockDim = dim3(1024, 1, 1);
+        pc.stream = s;
+        cudaLaunchAttribute pa[1] = {pdl_attr()};
+        pc.attrs = pa;
+        pc.numAttrs = 1;
+        const int rc = fh3host::check_cuda(cudaLaunchKernelEx(&pc, gemv_xprep_kernel<M>, x, L.nblk, bglob, fsg),
+                                           "gemv_xprep_kernel launch");
         if (rc) return rc;
     }
     static bool attr = false;
