@@ -21,8 +21,8 @@
 //   swizzle layout.  One MMA per sub-block (M 128, N 16, K 32) into its own TMEM columns:
 //   int32 plane sums, exact; P = P0 + 256 P1 + 65536 P2 (one fp32 rounding), then the
 //   scales in fp32 as the reference forms them (d*sc and dmin*m are exact products).
-// * 6..16 tokens (kind::f16): warps 0-3 (one row per lane) write A = sc * q as f16 (exact)
-//   and the eight mins; gemv_xprep_kernel writes B once per call (x as f16 hi + lo pieces
+// * 6..16 tokens (kind::f16): warps 0-7 (two per TMEM lane quarter, half a row each)
+//   write A = sc * q as f16 (exact) and the eight mins; gemv_xprep_kernel writes B once per call (x as f16 hi + lo pieces
 //   and the sub-block sums, in the A operand's k order) and each unit bulk-copies its B
 //   block from L2 into a ring; 16 MMAs (K 16) give sum_j sc_j P_tj and one more the min
 //   term, each in one accumulator of 2 x tokens columns.
