@@ -13,11 +13,12 @@
 //   subnormals q * 2^-24, exact; high nibbles (word & 0x00F000F0) are 16 q * 2^-24.
 //   Eight weights cost one shift and four ANDs.
 // * B operand = x split into two fp16 planes x*2^s = h0 + h1 (22 significant bits)
-//   under a per-token power of two 2^s that puts max|x| just below 2^14.
+//   under a power of two 2^s per token and super-block that puts the super-block's
+//   max|x| just below 2^14.
 // * mma.sync.m16n8k16 (fp16 x fp16 -> fp32): a product of a 4-bit integer and an
 //   11-bit significand is exact; per sub-block two MMAs (k = 32) into a zeroed
 //   accumulator give the plane sums of P in fp32.  acc += dl*(P0 + P1) - ml*X',
-//   X' = X * 2^(s-24), and y = acc * 2^(24-s) (+ bias).
+//   X' = X * 2^(s-24), each super-block's contribution times 2^(24-s) (+ bias).
 //
 // Two launches per call:
 // * gemv_mma_prep_kernel (grid: 2048-element slices x tokens) writes the planes in
@@ -79,43 +80,27 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // super-block.
 __global__ void __launch_bounds__(256) gemv_mma_prep_kernel(const float* __restrict__ x, int64_t K, int M,
                                                             uint4* __restrict__ frag, uint32_t* __restrict__ mfrag,
-                                                            int* __restrict__ expo) {
+                                                            int* __restrict__ expo, float* __restrict__ fsb) {
     pdl_launch_dependents();
-    __shared__ float red[8];
     const int t = blockIdx.y;
     const int lane = threadIdx.x & 31;
     const float4* x4 = reinterpret_cast<const float4*>(x + static_cast<int64_t>(t) * K);
-    float amax = 0.0f;
-    {
-        const int64_t n4 = K / 4;
-        int64_t i = threadIdx.x;
-        for (; i + 3 * 256 < n4; i += 4 * 256) {  // four loads in flight per thread
-            const float4 a = __ldg(x4 + i), b = __ldg(x4 + i + 256), c = __ldg(x4 + i + 512), d = __ldg(x4 + i + 768);
-            amax = fmaxf(amax, fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
-                                     fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w)))));
-            amax = fmaxf(amax, fmaxf(fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(c.z), fabsf(c.w))),
-                                     fmaxf(fmaxf(fabsf(d.x), fabsf(d.y)), fmaxf(fabsf(d.z), fabsf(d.w)))));
-        }
-        for (; i < n4; i += 256) {
-            const float4 a = __ldg(x4 + i);
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) red[threadIdx.x >> 5] = amax;
-    __syncthreads();
-    amax = red[0];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
-    int E = 0;
-    if (amax > 0.0f && amax <= 3.0e38f) frexpf(amax, &E);  // amax < 2^E
-    const int s = 14 - E;                                    // max|x| * 2^s < 2^14
+    if (blockIdx.x == 0 && threadIdx.x == 0) expo[t] = 0;  // the scales are applied per super-block
 
     const int64_t k0 = static_cast<int64_t>(blockIdx.x) * kPrepSlice + threadIdx.x * 8;
     if (k0 < K) {  // K % 256 == 0: whole warps (super-blocks) are in or out
         const float4 v0 = __ldg(x4 + k0 / 4), v1 = __ldg(x4 + k0 / 4 + 1);
         const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        // this warp's super-block: its own power of two, max|x| * 2^s < 2^14
+        float amax = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) amax = fmaxf(amax, fabsf(e[u]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        int E = 0;
+        if (amax > 0.0f && amax <= 3.0e38f) frexpf(amax, &E);  // amax < 2^E
+        const int s = 14 - E;
+        if (lane == 0) fsb[(k0 >> 8) * M + t] = ldexpf(1.0f, 24 - s);
         uint32_t pl0[4], pl1[4];
 #pragma unroll
         for (int p = 0; p < 8; p += 2) {
@@ -151,7 +136,6 @@ __global__ void __launch_bounds__(256) gemv_mma_prep_kernel(const float* __restr
             mfrag[mb + 4] = pack_half2(a1, b1);
         }
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) expo[t] = 24 - s;
 }
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -217,13 +201,12 @@ __device__ __forceinline__ LaneCtx<NT> lane_ctx(int lane, int lanes) {
 
 // One super-block of rows g, g+8 against all tokens.  fsb: B fragments of the
 // super-block's 8 sub-blocks (stride `lanes` uint4), msb: its min-term B fragments.
-// fscale multiplies this super-block's contribution (the stream kernel's
-// per-super-block activation exponent; 1 elsewhere, where a per-token exponent is
-// applied at the end).
+// fsc[nt] multiplies this super-block's contribution to token tile nt of this lane
+// (2^(24-s), s the super-block's activation exponent of that token).
 template <int NT, int LANES = 0>  // LANES: fragment slots per sub-block when known at compile time
 __device__ __forceinline__ void compute_sb(const SuperBlock& sbk, int lane, int lanes_rt, const LaneCtx<NT>& lc,
                                            const uint4* __restrict__ fsb, const uint32_t* __restrict__ msb,
-                                           float (&acc)[2][NT], float fscale = 1.0f) {
+                                           float (&acc)[2][NT], const float (&fsc)[NT]) {
     const int lanes = LANES > 0 ? LANES : lanes_rt;
     // lane tq decodes the scales of its sub-blocks 2tq, 2tq+1 (rows g, g+8) and the
     // min-term A fragment; 6-bit fields as in get_scale_min_k4 (src/core/fh3_quant.c)
@@ -285,7 +268,7 @@ __device__ __forceinline__ void compute_sb(const SuperBlock& sbk, int lane, int 
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[i][nt] = fmaf(fscale, ph[i][nt][0] + ph[i][nt][1], acc[i][nt]);
+        for (int nt = 0; nt < NT; ++nt) acc[i][nt] = fmaf(fsc[nt], ph[i][nt][0] + ph[i][nt][1], acc[i][nt]);
 }
 
 // Warp partials -> CTA partials (fixed order) -> cluster ranks (fixed order) -> y.
@@ -356,8 +339,8 @@ __device__ __forceinline__ void stage_frag(uint4* st, const uint4* __restrict__ 
 template <int M>
 __global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_small_kernel(
     const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, const uint4* __restrict__ frag,
-    const uint32_t* __restrict__ mfrag, const int* __restrict__ expo, const float* __restrict__ bias,
-    float* __restrict__ y, int64_t ldy) {
+    const uint32_t* __restrict__ mfrag, const int* __restrict__ expo, const float* __restrict__ fsb,
+    const float* __restrict__ bias, float* __restrict__ y, int64_t ldy) {
     constexpr int LANES = 8 * M;                       // fragment slots per sub-block
     constexpr int STAGE = 8 * LANES + LANES / 4;       // uint4 per stage
     extern __shared__ __align__(128) uint8_t gv_smem[];
@@ -386,25 +369,34 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_
         load_sb(sa, row0, row1, b, tq);  // weights do not depend on the prep kernel
         load_sb(sbuf, row0, row1, min(b + nw, blast), tq);
         pdl_wait();
+        // this lane's token (tq; lanes past the last token reuse its factors, their sums
+        // are never stored) and the staged super-blocks' factors
+        const int tf = min(tq, M - 1);
         stage_frag<LANES>(st0, frag, mfrag, b, lane);
+        float f0[1] = {__ldg(fsb + static_cast<int64_t>(b) * M + tf)};
         stage_frag<LANES>(st1, frag, mfrag, min(b + nw, blast), lane);
+        float f1[1] = {__ldg(fsb + static_cast<int64_t>(min(b + nw, blast)) * M + tf)};
         for (int it = 0;; it += 2) {
             asm volatile("cp.async.wait_group 1;" ::: "memory");
             __syncwarp();
-            compute_sb<1, LANES>(sa, lane, LANES, lc, st0, reinterpret_cast<const uint32_t*>(st0 + 8 * LANES), acc);
+            compute_sb<1, LANES>(sa, lane, LANES, lc, st0, reinterpret_cast<const uint32_t*>(st0 + 8 * LANES), acc,
+                                 f0);
             if (it + 1 >= nbw) break;
             __syncwarp();
             const int b2 = min(b + 2 * nw, blast);
             load_sb(sa, row0, row1, b2, tq);
             stage_frag<LANES>(st0, frag, mfrag, b2, lane);
+            f0[0] = __ldg(fsb + static_cast<int64_t>(b2) * M + tf);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
             __syncwarp();
-            compute_sb<1, LANES>(sbuf, lane, LANES, lc, st1, reinterpret_cast<const uint32_t*>(st1 + 8 * LANES), acc);
+            compute_sb<1, LANES>(sbuf, lane, LANES, lc, st1, reinterpret_cast<const uint32_t*>(st1 + 8 * LANES), acc,
+                                 f1);
             if (it + 2 >= nbw) break;
             __syncwarp();
             const int b3 = min(b + 3 * nw, blast);
             load_sb(sbuf, row0, row1, b3, tq);
             stage_frag<LANES>(st1, frag, mfrag, b3, lane);
+            f1[0] = __ldg(fsb + static_cast<int64_t>(b3) * M + tf);
             b += 2 * nw;
         }
         asm volatile("cp.async.wait_group 0;" ::: "memory");  // no copy outlives the CTA
@@ -618,7 +610,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
         acc[0][0] = acc[1][0] = 0.0f;
     };
     auto step = [&](const SuperBlock& cur, int i) {
-        compute_sb<1, LANES>(cur, lane, LANES, lc, sfrag + b * 8 * LANES, smfrag + b * LANES, acc, my_fs[b]);
+        const float f1[1] = {my_fs[b]};
+        compute_sb<1, LANES>(cur, lane, LANES, lc, sfrag + b * 8 * LANES, smfrag + b * LANES, acc, f1);
         if (b == nblk - 1 || i == n - 1) finish_segment();
         if (++b == nblk) {
             b = 0;
@@ -648,8 +641,8 @@ template <int NT>
 __global__ void __launch_bounds__(kGvMaxWarps * 32, NT == 1 ? FH3_GV_MIN_BLOCKS : FH3_GV_WIDE_MIN_BLOCKS)
     gemv_mma_kernel(
     const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, const uint4* __restrict__ frag,
-    const uint32_t* __restrict__ mfrag, const int* __restrict__ expo, int M, const float* __restrict__ bias,
-    float* __restrict__ y, int64_t ldy, int S, int nsb_max) {
+    const uint32_t* __restrict__ mfrag, const int* __restrict__ expo, const float* __restrict__ fsb, int M,
+    const float* __restrict__ bias, float* __restrict__ y, int64_t ldy, int S, int nsb_max) {
     extern __shared__ __align__(128) uint8_t gv_smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -695,15 +688,29 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, NT == 1 ? FH3_GV_MIN_BLOCKS 
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) acc[i][nt] = 0.0f;
 
+    // the super-block's factor for token nt * 4 + tq of this lane (lanes past the last
+    // token reuse its factors; their sums are never stored)
+    auto factors = [&](int bb, float (&f)[NT]) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) f[nt] = __ldg(fsb + static_cast<int64_t>(bb) * M + min(nt * 4 + tq, M - 1));
+    };
     // two super-blocks in flight: the next one's bytes load while this one computes
+    float fa[NT], fb[NT];
+    if (b < b_hi) factors(b, fa);
     while (b < b_hi) {
         const int b1 = b + nw;
-        if (b1 < b_hi) load_sb(sbuf, row0, row1, b1, tq);
-        compute_sb<NT>(sa, lane, lanes, lc, sfrag + (b - b_lo) * 8 * lanes, smfrag + (b - b_lo) * lanes, acc);
+        if (b1 < b_hi) {
+            load_sb(sbuf, row0, row1, b1, tq);
+            factors(b1, fb);
+        }
+        compute_sb<NT>(sa, lane, lanes, lc, sfrag + (b - b_lo) * 8 * lanes, smfrag + (b - b_lo) * lanes, acc, fa);
         if (b1 >= b_hi) break;
         const int b2 = b1 + nw;
-        if (b2 < b_hi) load_sb(sa, row0, row1, b2, tq);
-        compute_sb<NT>(sbuf, lane, lanes, lc, sfrag + (b1 - b_lo) * 8 * lanes, smfrag + (b1 - b_lo) * lanes, acc);
+        if (b2 < b_hi) {
+            load_sb(sa, row0, row1, b2, tq);
+            factors(b2, fa);
+        }
+        compute_sb<NT>(sbuf, lane, lanes, lc, sfrag + (b1 - b_lo) * 8 * lanes, smfrag + (b1 - b_lo) * lanes, acc, fb);
         b = b2;
     }
     finish_tile<NT>(acc, part, cta_part, warp, nw, lane, S, rank, M, N, expo, bias, y, ldy);
@@ -729,8 +736,8 @@ int set_smem(const void* fn, size_t smem, int& cur, const char* what) {
 }
 
 template <int M>
-int launch_small(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, float* y,
-                 const float* bias, cudaStream_t s) {
+int launch_small(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, const float* fsb,
+                 float* y, const float* bias, cudaStream_t s) {
     const int64_t N = w->out, K = w->in;
     const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
     // balanced warps: the fewest that keep the per-warp count at ceil(nblk / 8)
@@ -752,7 +759,7 @@ int launch_small(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, co
     cfg.numAttrs = 1;
     return fh3host::check_cuda(cudaLaunchKernelEx(&cfg, gemv_mma_small_kernel<M>, w->data,
                                                   fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, K), nblk, N, frag, mfrag, expo,
-                                                  bias, y, N),
+                                                  fsb, bias, y, N),
                                "gemv_mma_small_kernel launch");
 }
 
@@ -794,8 +801,8 @@ int launch_stream(const Fh3CudaW* w, const float* x, float* y, const float* bias
 }
 
 template <int NT>
-int launch_mma(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, int M, float* y,
-               const float* bias, cudaStream_t s) {
+int launch_mma(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, const float* fsb, int M,
+               float* y, const float* bias, cudaStream_t s) {
     const int64_t N = w->out, K = w->in;
     const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
     int S = 1;
@@ -827,7 +834,7 @@ int launch_mma(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, cons
     cfg.numAttrs = na;
     return fh3host::check_cuda(
         cudaLaunchKernelEx(&cfg, gemv_mma_kernel<NT>, w->data, fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, K), nblk, N,
-                           frag, mfrag, expo, M, bias, y, N, S, nsb_max),
+                           frag, mfrag, expo, fsb, M, bias, y, N, S, nsb_max),
         "gemv_mma_kernel launch");
 }
 
@@ -861,26 +868,28 @@ int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float
     const int64_t K = w->in;
     const size_t fbytes = static_cast<size_t>(K) * n_tok * 4;  // (K/32) sub-blocks x 8M slots x 16 B
     const size_t mbytes = static_cast<size_t>(K / 256) * 8 * n_tok * sizeof(uint32_t);
-    uint8_t* base = static_cast<uint8_t*>(scratch(c, 5, fbytes + mbytes + 256, s));
+    const size_t sbytes = static_cast<size_t>(K / 256) * n_tok * 4;  // per-super-block factors
+    uint8_t* base = static_cast<uint8_t*>(scratch(c, 5, fbytes + mbytes + 256 + sbytes, s));
     if (!base) return FH3_E_NOMEM;
     auto* frag = reinterpret_cast<uint4*>(base);
     auto* mfrag = reinterpret_cast<uint32_t*>(base + fbytes);
     auto* expo = reinterpret_cast<int*>(base + fbytes + mbytes);
+    auto* fsb = reinterpret_cast<float*>(base + fbytes + mbytes + 256);
     const dim3 pgrid(static_cast<unsigned>((K + kPrepSlice - 1) / kPrepSlice), static_cast<unsigned>(n_tok));
-    gemv_mma_prep_kernel<<<pgrid, 256, 0, s>>>(x, K, n_tok, frag, mfrag, expo);
+    gemv_mma_prep_kernel<<<pgrid, 256, 0, s>>>(x, K, n_tok, frag, mfrag, expo, fsb);
     const int rc = check_cuda(cudaGetLastError(), "gemv_mma_prep_kernel launch");
     if (rc) return rc;
     switch (n_tok) {
-        case 1: return launch_small<1>(w, frag, mfrag, expo, y, bias, s);
-        case 2: return launch_small<2>(w, frag, mfrag, expo, y, bias, s);
-        case 3: return launch_small<3>(w, frag, mfrag, expo, y, bias, s);
-        case 4: return launch_small<4>(w, frag, mfrag, expo, y, bias, s);
+        case 1: return launch_small<1>(w, frag, mfrag, expo, fsb, y, bias, s);
+        case 2: return launch_small<2>(w, frag, mfrag, expo, fsb, y, bias, s);
+        case 3: return launch_small<3>(w, frag, mfrag, expo, fsb, y, bias, s);
+        case 4: return launch_small<4>(w, frag, mfrag, expo, fsb, y, bias, s);
         default: break;
     }
     switch (NT) {
-        case 2: return launch_mma<2>(w, frag, mfrag, expo, n_tok, y, bias, s);
-        case 3: return launch_mma<3>(w, frag, mfrag, expo, n_tok, y, bias, s);
-        default: return launch_mma<4>(w, frag, mfrag, expo, n_tok, y, bias, s);
+        case 2: return launch_mma<2>(w, frag, mfrag, expo, fsb, n_tok, y, bias, s);
+        case 3: return launch_mma<3>(w, frag, mfrag, expo, fsb, n_tok, y, bias, s);
+        default: return launch_mma<4>(w, frag, mfrag, expo, fsb, n_tok, y, bias, s);
     }
 }
 

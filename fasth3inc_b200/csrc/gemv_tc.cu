@@ -313,15 +313,15 @@ __device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int 
 // B blocks of 6..16 tokens, once per call: block b (GtCfg<M>::SLOT_BYTES bytes) holds, for
 // token t, rows 2t and 2t + 1 (f16, K-major, 128-byte swizzle):
 //  * K blocks 0..3: x * 2^s as hi + lo, hi = f16(x 2^s), lo = f16(x 2^s - hi), with one
-//    power of two a token (max|x| * 2^s < 2^15; the residual is below 2^-22 of max|x|), in
-//    the A operand's k order: k = 64c + 32hb + 4u + r sits at e = 64c + 8u + 4hb + 2(r & 1)
-//    + (r >> 1), so that one 32-bit word of nibbles gives the f16 pairs (k, k + 2) of A with
-//    a mask (see the expanders);
+//    power of two per token and super-block (max|x| * 2^s < 2^15 over the super-block, as
+//    the 1..5-token operands; the residual is below 2^-22 of that max), in the A operand's
+//    k order: k = 64c + 32hb + 4u + r sits at e = 64c + 8u + 4hb + 2(r & 1) + (r >> 1), so
+//    that one 32-bit word of nibbles gives the f16 pairs (k, k + 2) of A with a mask (see
+//    the expanders);
 //  * K block 4, elements 0..7: the sub-block sums X_j = sum of x over sub-block j (in fp32)
 //    times 2^(s-5), as hi + lo; elements 8..15 zero.
-// fs[t] = 2^-s.  Grid (tokens, groups of 4 super-blocks), 1024 threads: thread k of
-// super-block q of the group (one element each); every CTA first finds its token's max|x|
-// over the whole row (up to four 16-byte loads a thread in flight at once).
+// fs[b * M + t] = 2^-s.  Grid (tokens, groups of 4 super-blocks), 1024 threads: thread k of
+// super-block q of the group (one element each).
 template <int M>
 __global__ void __launch_bounds__(1024) gemv_xprep_kernel(const float* __restrict__ x, int nblk,
                                                           uint8_t* __restrict__ bglob, float* __restrict__ fs) {
@@ -331,36 +331,17 @@ __global__ void __launch_bounds__(1024) gemv_xprep_kernel(const float* __restric
     __shared__ float red[32];
     const int t = blockIdx.x, tid = threadIdx.x, k = tid & 255, q = tid >> 8, lane = tid & 31, wid = (tid >> 5) & 7;
     const int64_t K = static_cast<int64_t>(nblk) * 256;
-    const float* xr = x + t * K;
     const int b = blockIdx.y * 4 + q;
-    const float v = b < nblk ? __ldg(xr + static_cast<int64_t>(b) * 256 + k) : 0.0f;
-    float am = 0.0f;
-    {
-        const float4* x4 = reinterpret_cast<const float4*>(xr);
-        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        int64_t i = tid;
-        for (; i + 3 * 1024 < K / 4; i += 4 * 1024) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float4 w = __ldg(x4 + i + u * 1024);
-                a4[u] = fmaxf(a4[u], fmaxf(fmaxf(fabsf(w.x), fabsf(w.y)), fmaxf(fabsf(w.z), fabsf(w.w))));
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 3; ++u, i += 1024)
-            if (i < K / 4) {
-                const float4 w = __ldg(x4 + i);
-                a4[u] = fmaxf(a4[u], fmaxf(fmaxf(fabsf(w.x), fabsf(w.y)), fmaxf(fabsf(w.z), fabsf(w.w))));
-            }
-        am = fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3]));
-    }
+    const float v = b < nblk ? __ldg(x + t * K + static_cast<int64_t>(b) * 256 + k) : 0.0f;
+    float am = fabsf(v);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
     if (lane == 0) red[tid >> 5] = am;
     __syncthreads();
-    am = red[0];
+    am = red[8 * q];
 #pragma unroll
-    for (int w = 1; w < 32; ++w) am = fmaxf(am, red[w]);
+    for (int w = 1; w < 8; ++w) am = fmaxf(am, red[8 * q + w]);  // over super-block b
+    if (b >= nblk) return;  // uniform over each warp, after the CTA barrier
     int E = 0;  // am < 2^E
     if (am > 0.0f && am <= 3.0e38f)
         E = am >= 1.17549435e-38f ? static_cast<int>(__float_as_uint(am) >> 23) - 126
@@ -369,41 +350,39 @@ __global__ void __launch_bounds__(1024) gemv_xprep_kernel(const float* __restric
     const int s1 = min(s, 127), sx = s - 5, sx1 = max(min(sx, 127), -126);
     const float m1 = pow2_exact(s1), m2 = pow2_exact(s - s1);     // x * 2^s exactly, in two steps
     const float n1 = pow2_exact(sx1), n2 = pow2_exact(sx - sx1);   // X * 2^(s-5)
-    if (blockIdx.y == 0 && tid == 0) fs[t] = pow2_exact(-s);
-    // this thread's element of a super-block and its position in the A operand's k order
+    if (k == 0) fs[static_cast<size_t>(b) * M + t] = pow2_exact(-s);
+    // this thread's element and its position in the A operand's k order
     const int c = k >> 6, hb = (k >> 5) & 1, u = (k >> 2) & 7, r = k & 3;
     const int ee = 8 * u + 4 * hb + 2 * (r & 1) + (r >> 1);  // within K block c
-    if (b < nblk) {  // uniform over each warp
-        uint8_t* blk = bglob + static_cast<size_t>(b) * C::SLOT_BYTES;
-        const float xs = (v * m1) * m2;
-        const __half hi = __float2half_rn(xs);
-        const __half lo = __float2half_rn(xs - __half2float(hi));  // the difference is exact in fp32
+    uint8_t* blk = bglob + static_cast<size_t>(b) * C::SLOT_BYTES;
+    const float xs = (v * m1) * m2;
+    const __half hi = __float2half_rn(xs);
+    const __half lo = __float2half_rn(xs - __half2float(hi));  // the difference is exact in fp32
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        const int n = 2 * t + p;
+        *reinterpret_cast<__half*>(blk + c * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 +
+                                   (((ee >> 3) ^ (n & 7)) << 4) + (ee & 7) * 2) = p ? lo : hi;
+    }
+    // sub-block wid = elements 32 wid .. 32 wid + 31 of this super-block
+    float X = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) X += __shfl_xor_sync(0xffffffffu, X, o);
+    if (lane == 0) {
+        const float xs2 = (X * n1) * n2;
+        const __half xh = __float2half_rn(xs2);
+        const __half xl = __float2half_rn(xs2 - __half2float(xh));
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
             const int n = 2 * t + p;
-            *reinterpret_cast<__half*>(blk + c * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 +
-                                       (((ee >> 3) ^ (n & 7)) << 4) + (ee & 7) * 2) = p ? lo : hi;
+            *reinterpret_cast<__half*>(blk + 4 * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 + ((n & 7) << 4) +
+                                       wid * 2) = p ? xl : xh;
         }
-        // sub-block wid = elements 32 wid .. 32 wid + 31 of this super-block
-        float X = v;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) X += __shfl_xor_sync(0xffffffffu, X, o);
-        if (lane == 0) {
-            const float xs2 = (X * n1) * n2;
-            const __half xh = __float2half_rn(xs2);
-            const __half xl = __float2half_rn(xs2 - __half2float(xh));
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-                const int n = 2 * t + p;
-                *reinterpret_cast<__half*>(blk + 4 * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 +
-                                           ((n & 7) << 4) + wid * 2) = p ? xl : xh;
-            }
-        }
-        if (k < 2) {  // elements 8..15 of K block 4 meet the zero columns of A: keep them finite
-            const int n = 2 * t + k;
-            *reinterpret_cast<uint4*>(blk + 4 * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 +
-                                      ((1 ^ (n & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
-        }
+    }
+    if (k < 2) {  // elements 8..15 of K block 4 meet the zero columns of A: keep them finite
+        const int n = 2 * t + k;
+        *reinterpret_cast<uint4*>(blk + 4 * C::HALF_BYTES + (n >> 3) * 1024 + (n & 7) * 128 + ((1 ^ (n & 7)) << 4)) =
+            make_uint4(0u, 0u, 0u, 0u);
     }
 }
 
@@ -755,9 +734,7 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
             if (lane == 0) fh3::mbar_arrive(B.bfull);
         }
         bool ok = wait_all(B.bfull, 0);  // every warp's sub-block sums and scales
-        float fsr[C::F16 ? M : 1];       // f16: 2^-s of each token, from the pre-pass
-#pragma unroll
-        for (int t = 0; t < (C::F16 ? M : 1); ++t) fsr[t] = C::F16 ? __ldg(fsg + t) : 0.0f;
+
         // One chunk only: the run's last tile, when split.  If, two units before the run
         // ends, every other segment has already counted itself, this segment is the last
         // one; the others' partials are read then, off the critical path (no CTA ever waits
@@ -895,8 +872,16 @@ __global__ void __launch_bounds__(GtCfg<M>::THREADS, 1) gemv_tc_kernel(
             const uint4 hd = lds128(smem + C::OFF_HDR + (hs * kGtRows + r) * 16);
             __syncwarp();
             if (lane == 0) fh3::mbar_arrive(&B.hempty[hs]);
-            // 6..16 tokens: the part-1 warps read no accumulator (and release none), so they do
-            // not wait for the MMA either
+            // 6..16 tokens: 2^-s of the unit's super-block for each token (the pre-pass's), loaded
+            // before the accumulator wait; the part-1 warps read no accumulator (and release
+            // none), so they do not wait for the MMA either
+            float fsr[C::F16 ? M : 1];
+            if constexpr (C::F16) {
+                if (part == 0) {
+#pragma unroll
+                    for (int t = 0; t < M; ++t) fsr[t] = __ldg(fsg + static_cast<size_t>(ep.b) * M + t);
+                }
+            }
             if (!C::F16 || part == 0) {
                 if (!wait_all(&B.dfull[d], (i / C::DB) & 1)) break;
                 fh3::tc_fence_after();
@@ -1101,7 +1086,7 @@ int gemv_tc(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float*
     float* fsg = nullptr;
     if (n_tok > 5) {
         const size_t bb = static_cast<size_t>(L.nblk) * gt_bblock(n_tok);
-        bglob = static_cast<uint8_t*>(scratch(c, 9, bb + 256, s));
+        bglob = static_cast<uint8_t*>(scratch(c, 9, bb + static_cast<size_t>(L.nblk) * n_tok * 4 + 256, s));
         if (!bglob) return FH3_E_NOMEM;
         fsg = reinterpret_cast<float*>(bglob + bb);
     }

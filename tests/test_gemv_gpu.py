@@ -78,6 +78,24 @@ def test_baseline_shapes_vs_oracle(fh3, oracle, K, N, M):
     assert rel_fro(got, ref) <= TOL
 
 
+@pytest.mark.parametrize("M", [3, 6, 16])
+def test_large_super_block_against_zero_weights(fh3, oracle, M):
+    """x of one super-block near 1e8 meets all-zero weights (d = dmin = 0 in every row's
+    header), so y comes from the other super-blocks alone: their x must keep their own
+    precision, i.e. x is scaled per super-block, not per token (integer planes up to 5
+    tokens, f16 pieces from 6)."""
+    K, N, b0 = 1280, 64, 2
+    w = oracle.make_weights(seed=11, stream=1, rows=N, n=K).copy()
+    nblk = K // 256
+    rows = w.reshape(N, nblk, 144)
+    rows[:, b0, 0:4] = 0  # fp16 d and dmin of super-block b0
+    x = oracle.rng_normal(M, 12, M * K).reshape(M, K).astype(np.float32)
+    x[:, b0 * 256:(b0 + 1) * 256] *= np.float32(1e8)
+    ref = oracle.matmul(Q4K, w, K, N, x)
+    got = _run(fh3, w, K, N, x)
+    assert rel_fro(got, ref) <= TOL
+
+
 def test_every_token_count_and_row_tail(fh3, oracle):
     K, N = 1280, 37  # N not a multiple of the rows-per-warp
     w = oracle.make_weights(seed=5, stream=1, rows=N, n=K)
