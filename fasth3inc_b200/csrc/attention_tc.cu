@@ -63,6 +63,13 @@ __global__ void __launch_bounds__(256) vt_transpose_kernel(const __nv_bfloat16* 
     }
 }
 
+// vt[c][tok] = v[tok][c] in 64 x 64 tiles of 16-byte accesses (v 16-byte aligned, ldv % 8 == 0).
+// grid (ceil(n/64), heads*128/64), 256 threads.
+__global__ void __launch_bounds__(256) vt_transpose64_kernel(const __nv_bfloat16* __restrict__ v, int64_t ldv,
+                                                             __nv_bfloat16* __restrict__ vt, int64_t ldt, int n) {
+    fh3::transpose64_bf16(v, ldv, [](int p) { return p; }, blockIdx.y * 64, blockIdx.x * 64, n, vt, ldt);
+}
+
 struct Bars {
     uint64_t *q_full, *kv_full, *kv_empty, *s_full, *s_empty, *p_full, *p_empty, *o_full, *o_empty, *drain;
 };
@@ -679,8 +686,12 @@ int attention_tc(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, in
     const int64_t rows = static_cast<int64_t>(heads) * kTcHD;
     auto* vt = static_cast<__nv_bfloat16*>(scratch(c, 12, static_cast<size_t>(rows) * npad * 2, s));
     if (!vt) return FH3_E_NOMEM;
-    vt_transpose_kernel<<<dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>(heads * 4)), 256, 0, s>>>(
-        v, ldv, vt, npad, n);
+    if ((reinterpret_cast<uintptr_t>(v) & 15) == 0 && ldv % 8 == 0)
+        vt_transpose64_kernel<<<dim3(static_cast<unsigned>((n + 63) / 64), static_cast<unsigned>(heads * 2)), 256, 0,
+                                s>>>(v, ldv, vt, npad, n);
+    else
+        vt_transpose_kernel<<<dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>(heads * 4)), 256, 0,
+                              s>>>(v, ldv, vt, npad, n);
     int rc = check_cuda(cudaGetLastError(), "vt_transpose_kernel launch");
     if (rc) return rc;
     CUtensorMap tq, tk, tvt;

@@ -402,6 +402,51 @@ __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// out[c][p] = in[row_of(p)][c] over one 64-column x 64-position tile (columns c0.., positions
+// p0..): 16-byte loads of 8 columns and 16-byte stores of 8 positions (eight lanes write one
+// 128-byte run of an output row) through a shared tile of 33-word rows, so the transposed
+// reads meet at most two-way bank conflicts.  row_of(p) < 0 reads zeros; nothing is stored at
+// positions >= np.  256 threads.  Every in + row * ldi + c0 and out + c * ldo + p (p a
+// multiple of 8) must be 16-byte aligned.
+template <typename RowOf>
+__device__ __forceinline__ void transpose64_bf16(const __nv_bfloat16* __restrict__ in, int64_t ldi, RowOf row_of,
+                                                 int c0, int p0, int np, __nv_bfloat16* __restrict__ out,
+                                                 int64_t ldo) {
+    __shared__ uint32_t tile[64][33];  // [position][column pair]
+    const int tid = threadIdx.x;
+    for (int e = tid; e < 512; e += 256) {
+        const int r = e >> 3, ch = e & 7;
+        const int p = p0 + r;
+        const int64_t row = p < np ? static_cast<int64_t>(row_of(p)) : -1;
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (row >= 0) val = __ldg(reinterpret_cast<const uint4*>(in + row * ldi + c0 + 8 * ch));
+        tile[r][4 * ch + 0] = val.x;
+        tile[r][4 * ch + 1] = val.y;
+        tile[r][4 * ch + 2] = val.z;
+        tile[r][4 * ch + 3] = val.w;
+    }
+    __syncthreads();
+    for (int e = tid; e < 512; e += 256) {
+        const int c = e >> 3, ch = e & 7;  // column c0 + c, positions p0 + 8ch .. +7
+        const int p = p0 + 8 * ch;
+        if (p >= np) continue;
+        uint32_t h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t w = tile[8 * ch + j][c >> 1];
+            h[j] = (c & 1) ? (w >> 16) : (w & 0xFFFFu);
+        }
+        __nv_bfloat16* dst = out + static_cast<int64_t>(c0 + c) * ldo + p;
+        if (p + 8 <= np) {
+            *reinterpret_cast<uint4*>(dst) =
+                make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+        } else {
+            for (int j = 0; j < 8 && p + j < np; ++j)
+                reinterpret_cast<unsigned short*>(dst)[j] = static_cast<unsigned short>(h[j]);
+        }
+    }
+}
+
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
 // layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 B (64 bf16),
 // 8-row atoms of 1024 B (stride-byte-offset), version 1, layout 2 (SW128).

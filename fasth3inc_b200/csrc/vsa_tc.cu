@@ -111,6 +111,14 @@ __global__ void __launch_bounds__(256) vsa_vt_kernel(const __nv_bfloat16* __rest
     }
 }
 
+// The same in 64 x 64 tiles of 16-byte accesses (v 16-byte aligned, ldv % 8 == 0).
+// grid (ceil(P/64), width/64), 256 threads.
+__global__ void __launch_bounds__(256) vsa_vt64_kernel(const __nv_bfloat16* __restrict__ v, int64_t ldv,
+                                                       const int* __restrict__ pidx, int P,
+                                                       __nv_bfloat16* __restrict__ vpt) {
+    fh3::transpose64_bf16(v, ldv, [pidx](int p) { return pidx[p]; }, blockIdx.y * 64, blockIdx.x * 64, P, vpt, P);
+}
+
 }  // namespace
 
 namespace {
@@ -844,8 +852,12 @@ int vsa_fine_tc(const int* perm, const int* toff, const int* sel, const int* sel
     const int64_t work = pmax * (width / 8);
     const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 16));
     vsa_rows_kernel<<<blocks, 256, 0, s>>>(q, ldq, k, ldk, pidx, static_cast<int>(pmax), width, qp, kp);
-    vsa_vt_kernel<<<dim3(static_cast<unsigned>(pmax / 32), static_cast<unsigned>(width / 32)), 256, 0, s>>>(
-        v, ldv, pidx, static_cast<int>(pmax), vpt);
+    if ((reinterpret_cast<uintptr_t>(v) & 15) == 0 && ldv % 8 == 0)
+        vsa_vt64_kernel<<<dim3(static_cast<unsigned>((pmax + 63) / 64), static_cast<unsigned>(width / 64)), 256, 0, s>>>(
+            v, ldv, pidx, static_cast<int>(pmax), vpt);
+    else
+        vsa_vt_kernel<<<dim3(static_cast<unsigned>(pmax / 32), static_cast<unsigned>(width / 32)), 256, 0, s>>>(
+            v, ldv, pidx, static_cast<int>(pmax), vpt);
     rc = check_cuda(cudaGetLastError(), "vsa tile-order launches");
     if (rc) return rc;
     CUtensorMap tq, tk, tvt;
