@@ -45,27 +45,10 @@ constexpr uint32_t kTmemCols = 512;    // S0 S1 at 0 and 128, O at 256 (power-of
 constexpr uint32_t kTmemO = 256;
 static_assert(kTcSmem <= 232448, "shared memory budget");
 
-// v [n][ldv] (head h at columns h*128..) -> vt [heads*128][ldt]: vt[h*128 + d][t] = v[t][h*128 + d].
-// 32 x 32 tiles through shared memory, both sides coalesced.  grid (ceil(n/32), heads*4).
+// vt[c][tok] = v[tok][c] (c = h*128 + d) in 64 x 64 tiles of 16-byte accesses (the entry
+// point checks that v is 16-byte aligned and ldv a multiple of 8).  grid (ceil(n/64),
+// heads*128/64), 256 threads.
 __global__ void __launch_bounds__(256) vt_transpose_kernel(const __nv_bfloat16* __restrict__ v, int64_t ldv,
-                                                           __nv_bfloat16* __restrict__ vt, int64_t ldt, int n) {
-    __shared__ __nv_bfloat16 t[32][34];
-    const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;  // c: column h*128 + d
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-    for (int r = ty; r < 32; r += 8) {
-        const int tok = t0 + r;
-        t[r][tx] = tok < n ? v[static_cast<int64_t>(tok) * ldv + c0 + tx] : __float2bfloat16(0.0f);
-    }
-    __syncthreads();
-    for (int r = ty; r < 32; r += 8) {
-        const int tok = t0 + tx;
-        if (tok < n) vt[static_cast<int64_t>(c0 + r) * ldt + tok] = t[tx][r];
-    }
-}
-
-// vt[c][tok] = v[tok][c] in 64 x 64 tiles of 16-byte accesses (v 16-byte aligned, ldv % 8 == 0).
-// grid (ceil(n/64), heads*128/64), 256 threads.
-__global__ void __launch_bounds__(256) vt_transpose64_kernel(const __nv_bfloat16* __restrict__ v, int64_t ldv,
                                                              __nv_bfloat16* __restrict__ vt, int64_t ldt, int n) {
     fh3::transpose64_bf16(v, ldv, [](int p) { return p; }, blockIdx.y * 64, blockIdx.x * 64, n, vt, ldt);
 }
@@ -686,12 +669,8 @@ int attention_tc(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, in
     const int64_t rows = static_cast<int64_t>(heads) * kTcHD;
     auto* vt = static_cast<__nv_bfloat16*>(scratch(c, 12, static_cast<size_t>(rows) * npad * 2, s));
     if (!vt) return FH3_E_NOMEM;
-    if ((reinterpret_cast<uintptr_t>(v) & 15) == 0 && ldv % 8 == 0)
-        vt_transpose64_kernel<<<dim3(static_cast<unsigned>((n + 63) / 64), static_cast<unsigned>(heads * 2)), 256, 0,
-                                s>>>(v, ldv, vt, npad, n);
-    else
-        vt_transpose_kernel<<<dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>(heads * 4)), 256, 0,
-                              s>>>(v, ldv, vt, npad, n);
+    vt_transpose_kernel<<<dim3(static_cast<unsigned>((n + 63) / 64), static_cast<unsigned>(heads * 2)), 256, 0, s>>>(
+        v, ldv, vt, npad, n);
     int rc = check_cuda(cudaGetLastError(), "vt_transpose_kernel launch");
     if (rc) return rc;
     CUtensorMap tq, tk, tvt;

@@ -91,29 +91,10 @@ __global__ void vsa_rows_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq
     }
 }
 
-// VpT[c][p] = v[pidx[p]][c] (c = h*128 + d), zero in padding; 32 x 32 tiles through
-// shared memory.  grid (ceil(P/32), width/32).
-__global__ void __launch_bounds__(256) vsa_vt_kernel(const __nv_bfloat16* __restrict__ v, int64_t ldv,
-                                                     const int* __restrict__ pidx, int P,
-                                                     __nv_bfloat16* __restrict__ vpt) {
-    __shared__ __nv_bfloat16 t[32][34];
-    const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    for (int r = ty; r < 32; r += 8) {
-        const int p = p0 + r;
-        const int tok = p < P ? pidx[p] : -1;
-        t[r][tx] = tok >= 0 ? v[static_cast<int64_t>(tok) * ldv + c0 + tx] : __float2bfloat16(0.0f);
-    }
-    __syncthreads();
-    for (int r = ty; r < 32; r += 8) {
-        const int p = p0 + tx;
-        if (p < P) vpt[static_cast<int64_t>(c0 + r) * P + p] = t[tx][r];
-    }
-}
-
-// The same in 64 x 64 tiles of 16-byte accesses (v 16-byte aligned, ldv % 8 == 0).
+// VpT[c][p] = v[pidx[p]][c] (c = h*128 + d), zero in padding, in 64 x 64 tiles of 16-byte
+// accesses (the entry point checks that v is 16-byte aligned and ldv a multiple of 8).
 // grid (ceil(P/64), width/64), 256 threads.
-__global__ void __launch_bounds__(256) vsa_vt64_kernel(const __nv_bfloat16* __restrict__ v, int64_t ldv,
+__global__ void __launch_bounds__(256) vsa_vt_kernel(const __nv_bfloat16* __restrict__ v, int64_t ldv,
                                                        const int* __restrict__ pidx, int P,
                                                        __nv_bfloat16* __restrict__ vpt) {
     fh3::transpose64_bf16(v, ldv, [pidx](int p) { return pidx[p]; }, blockIdx.y * 64, blockIdx.x * 64, P, vpt, P);
@@ -852,12 +833,8 @@ int vsa_fine_tc(const int* perm, const int* toff, const int* sel, const int* sel
     const int64_t work = pmax * (width / 8);
     const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 16));
     vsa_rows_kernel<<<blocks, 256, 0, s>>>(q, ldq, k, ldk, pidx, static_cast<int>(pmax), width, qp, kp);
-    if ((reinterpret_cast<uintptr_t>(v) & 15) == 0 && ldv % 8 == 0)
-        vsa_vt64_kernel<<<dim3(static_cast<unsigned>((pmax + 63) / 64), static_cast<unsigned>(width / 64)), 256, 0, s>>>(
-            v, ldv, pidx, static_cast<int>(pmax), vpt);
-    else
-        vsa_vt_kernel<<<dim3(static_cast<unsigned>(pmax / 32), static_cast<unsigned>(width / 32)), 256, 0, s>>>(
-            v, ldv, pidx, static_cast<int>(pmax), vpt);
+    vsa_vt_kernel<<<dim3(static_cast<unsigned>((pmax + 63) / 64), static_cast<unsigned>(width / 64)), 256, 0, s>>>(
+        v, ldv, pidx, static_cast<int>(pmax), vpt);
     rc = check_cuda(cudaGetLastError(), "vsa tile-order launches");
     if (rc) return rc;
     CUtensorMap tq, tk, tvt;
