@@ -46,6 +46,12 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the output check (N = 1: sampled rows against the CPU oracle through all "
+                         "blocks; N > 1: rank 0 recomputes every other rank's shard and compares bitwise)")
+    ap.add_argument("--parity-rows", type=int, default=4)
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="run each projection as one fh3cuda_gemm_q4k_dev call (no second stream)")
     ap.add_argument("--no-gemv", action="store_true",
                     help="skip the GEMV (1..4 token), q/k norm+rope and attention measurements")
     ap.add_argument("--case", choices=["gemm", "gemv", "qk", "attn", "vsa"], default=None,
@@ -112,6 +118,52 @@ class Clocks:
 
 
 # ----------------------------------------------------------------------------- CPU legs
+def host_cpu() -> dict:
+    """CPU model, logical CPUs this process may run on, and the physical cores among them."""
+    avail = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else list(range(os.cpu_count() or 1))
+    cores = set()
+    for c in avail:
+        base = f"/sys/devices/system/cpu/cpu{c}/topology/"
+        try:
+            with open(base + "physical_package_id") as f:
+                pkg = f.read().strip()
+            with open(base + "core_id") as f:
+                core = f.read().strip()
+        except OSError:
+            pkg, core = "0", str(c)
+        cores.add((pkg, core))
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"model": model, "logical_cpus": len(avail), "physical_cores": len(cores)}
+
+
+def pin_cpu_threads(n: int) -> int:
+    """Give the OpenMP runtime of the CPU legs n threads, whatever the launcher set.
+
+    torch.distributed.run exports OMP_NUM_THREADS=1 to every rank; the reference's fh3_matmul
+    (and the oracle) run on the system libgomp, whose thread count is set here both through the
+    environment (read when libgomp initialises) and through omp_set_num_threads (which overrides
+    it afterwards).  Returns the thread count the oracle library then reports."""
+    import ctypes
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    from oracle import oracle as orc
+    o = orc.Oracle()
+    if orc.Reference.available():
+        orc.Reference()
+    try:
+        ctypes.CDLL("libgomp.so.1").omp_set_num_threads(n)
+    except OSError:
+        pass
+    return o.num_threads()
+
+
 def cpu_sample(trunk_block_raw, rows_s: int, text_s: int, threads: int, use_ref: bool, reps: int = 1):
     """Time the reference's fh3_matmul (or the oracle port) on one block's projections.
 
@@ -189,18 +241,26 @@ def run_ours(args):
     h0 = h_full[r0:r1].clone()
     h = h0.clone()
     stream = torch.cuda.current_stream(local)
-    runner = Runner(trunk, ws, stream)
+    runner = Runner(trunk, ws, stream, overlap=not args.no_overlap)
     # gather target: padded equal shards for all_gather_into_tensor
     shard = (M + world - 1) // world
     gather_out = torch.empty((shard * world, D_MODEL), device=dev) if world > 1 else None
     send = torch.empty((shard, D_MODEL), device=dev) if world > 1 else None
+
+    ag_events = None   # (start, end) of each all-gather when recording
 
     def step():
         h.copy_(h0)  # every step starts from the same latents
         runner.step(h, text_bf)
         if world > 1:
             send[:m_loc].copy_(h)
+            if ag_events is not None:
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
             dist.all_gather_into_tensor(gather_out, send)
+            if ag_events is not None:
+                a1.record(stream)
+                ag_events.append((a0, a1))
 
     for _ in range(args.warmup):
         step()
@@ -215,7 +275,8 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
-    runner.gemm_events = []
+    runner.gemm_events, runner.expand_events, runner.norm_events = [], [], []
+    ag_events = []
     runner.launches = 0
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -228,11 +289,19 @@ def run_ours(args):
         dist.barrier()
     clk = clocks.stop()
     ms_local = e0.elapsed_time(e1) / args.steps
-    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in runner.gemm_events)
-    gemm_flops = sum(f for _, _, f in runner.gemm_events)
+    def total_ms(evs, tag_prefix=None):
+        return sum(a.elapsed_time(b) for a, b, _, t in evs if tag_prefix is None or t.startswith(tag_prefix))
+    gemm_ms = total_ms(runner.gemm_events)
+    gemm_flops = sum(f for _, _, f, _ in runner.gemm_events)
+    ckv_ms = sum(a.elapsed_time(b) for a, b, _, t in runner.gemm_events if t == f"fused:{T}")
+    expand_ms = total_ms(runner.expand_events)
+    norm_ms = total_ms(runner.norm_events)
+    ag_ms = sum(a.elapsed_time(b) for a, b in ag_events)
     launches = runner.launches
-    runner.gemm_events = None
-    stat = torch.tensor([ms_local, gemm_ms, float(gemm_flops), float(launches)], device=dev, dtype=torch.float64)
+    runner.gemm_events = runner.expand_events = runner.norm_events = None
+    ag_events = None
+    stat = torch.tensor([ms_local, gemm_ms, float(gemm_flops), float(launches), ckv_ms, expand_ms, norm_ms, ag_ms],
+                        device=dev, dtype=torch.float64)
     if world > 1:
         mx = stat.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
@@ -286,22 +355,47 @@ def run_ours(args):
     e2e_val = total_flops / (float(e2e_ms[0]) * 1e-3) / 1e12
     status = fh3.device_status()
 
+    # ---- output check (outside every timed region)
+    parity = None
+    if not args.no_parity:
+        if world > 1:
+            parity = {"method": "rank 0 recomputed every other rank's row shard on its own GPU (same launches) and "
+                                "compared the all-gathered rows bit for bit", "shards_checked": 0,
+                      "bitwise_equal": None}
+            if rank == 0:
+                ok = True
+                for r in range(1, world):
+                    a, b = rows_for_rank(M, r, world)
+                    hr = h_full[a:b].clone()
+                    runner.step(hr, text_bf)
+                    ok = ok and bool(torch.equal(hr, gather_out[r * shard:r * shard + (b - a)]))
+                    parity["shards_checked"] += 1
+                ok = ok and bool(torch.equal(h, gather_out[:m_loc]))
+                parity["bitwise_equal"] = ok
+                parity["ok"] = ok
+        elif rank == 0:
+            parity = parity_vs_oracle(fh3, torch, trunk, h0, h, text_bf, args.parity_rows)
+
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
+    hc = host_cpu()
+    cpu_threads = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
+        cpu_threads = pin_cpu_threads(hc["physical_cores"])
         raw = host_block_weights(trunk, 0)
-        rows_s = size_cpu_sample(raw, threads, True, args.cpu_seconds)
-        f, dt, kind = cpu_sample(raw, rows_s, min(rows_s, T), threads, True, reps=1)
-        cpu = {"value": round(f / dt / 1e12, 5), "unit": UNIT, "cores": threads, "kind": kind,
-               "sample": f"block 0's 7 Q4_K projections (fh3_matmul, OpenMP) on {rows_s} latent rows and "
-                         f"{min(rows_s, T)} text rows = {f / 1e9:.1f} GFLOP in {dt:.2f} s; same weights as the GPU"}
+        rows_s = size_cpu_sample(raw, cpu_threads, True, args.cpu_seconds)
+        f, dt, kind = cpu_sample(raw, rows_s, min(rows_s, T), cpu_threads, True, reps=1)
+        cpu = {"value": round(f / dt / 1e12, 5), "unit": UNIT, "cores": cpu_threads, "kind": kind,
+               "cpu": hc,
+               "sample": f"block 0's 7 Q4_K projections (fh3_matmul, OpenMP, {cpu_threads} threads) on {rows_s} "
+                         f"latent rows and {min(rows_s, T)} text rows = {f / 1e9:.1f} GFLOP in {dt:.2f} s; same "
+                         f"weights as the GPU"}
 
     peaks, src = load_peaks()
     gemv = qk = attn = vsa = None
     if rank == 0 and not args.no_gemv:
         hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-        gemv = measure_gemv(fh3, torch, hbm, src)
+        gemv = measure_gemv(fh3, torch, hbm, src, cpu_threads=cpu_threads)
         qk = measure_qk_norm_rope(fh3, torch, m_loc, hbm, src)
         attn = measure_attention(fh3, torch, m_loc, float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])),
                                  src)
@@ -315,10 +409,23 @@ def run_ours(args):
         roof = {"bound": "tensor", "achieved": round(gemm_tflops, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(gemm_tflops / peak, 4), "traffic": traffic,
                 "traffic_note": "DRAM bytes of one fc1 gemm_bf16_pair_kernel launch at this rank's rows, scaled "
-                                "from an 8192-row ncu capture; the GEMM time includes each call's Q4_K -> bf16 "
-                                "pass (dequant_q4k_bf16_kernel)",
+                                "from an 8192-row ncu capture",
+                "achieved_note": "GEMM FLOPs / the GEMM launches' CUDA-event time on the main stream (the "
+                                 "Q4_K -> bf16 expansions run beside them on a second stream; their time is "
+                                 "in breakdown.expand_ms)",
                 "kernel": "gemm_bf16_pair_kernel", "peak_source": f"{src} bf16_tflops_sustained",
                 "gemm_share_of_step": round(float(mx[1]) / (ms * args.steps), 4)}
+    breakdown = {"unit": "ms per step, max over ranks of each rank's CUDA-event sums",
+                 "gemm_ms": round(float(mx[1]) / args.steps, 3),
+                 "ckv_gemm_ms": round(float(mx[4]) / args.steps, 3),
+                 "expand_ms_side_stream": round(float(mx[5]) / args.steps, 3),
+                 "norm_ms": round(float(mx[6]) / args.steps, 3),
+                 "allgather_ms": round(float(mx[7]) / args.steps, 3),
+                 "rows_per_rank": m_loc,
+                 "ms_per_step_x_sm_ghz": round(ms * clk["sm_mhz"] / 1000.0, 2) if clk.get("sm_mhz") else None,
+                 "note": "the expansions overlap the GEMMs (second stream); ckv is the 512-text-row K/V "
+                         "projection every rank computes; ms_per_step_x_sm_ghz normalises the step by the median "
+                         "SM clock seen in the timed region"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -332,16 +439,59 @@ def run_ours(args):
                        "step_gflop": round(total_flops / 1e9, 1), "parallelism": f"rows{world}",
                        "l2": "inputs larger than L2 (11.87 GB of Q4_K weights streamed every step)",
                        "trunk_build_s": round(t_build, 1)},
-            "roofline": roof, "cpu_baseline": cpu,
+            "roofline": roof, "breakdown": breakdown, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": int(float(mx[3])), "clocks": clk, "device_status": status,
+            "gpu_launches": int(float(mx[3])), "clocks": clk, "device_status": status, "parity": parity,
             "gemv": gemv, "qk_norm_rope": qk, "attention": attn, "vsa_attention": vsa,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def parity_vs_oracle(fh3, torch, trunk, h0, h, text_bf, n_rows: int) -> dict:
+    """Sampled output rows of the bench's own step against the CPU oracle composed in fp32
+    through every block (fh3_rmsnorm, fh3_modulate, fh3_matmul, fh3_swiglu, fh3_gate_residual
+    restated: src/core/fh3_ops.c:317-585).  Rows are independent in every projection."""
+    import numpy as np
+
+    from oracle.oracle import Oracle, rel_fro
+    o = Oracle()
+    t0 = time.time()
+    M, d = h0.shape
+    F = trunk.F
+    rows = np.unique(np.concatenate([[0, M - 1], np.random.default_rng(7).choice(M, max(0, n_rows - 2),
+                                                                              replace=False)]))
+    n = len(rows)
+    ri = torch.from_numpy(rows).to(h0.device)
+    hs = h0.index_select(0, ri).cpu().numpy()
+    start = hs.copy()
+    ones = np.ones(d, np.float32)
+
+    def norm_mod(x, shift, scale):
+        return o.modulate(o.rmsnorm(x, ones, 1e-6), np.tile(shift, (n, 1)), np.tile(scale, (n, 1)))
+
+    for blk in trunk.blocks:
+        raw = {k: w.data.cpu().numpy() for k, w in blk.w.items()}
+        v = [t.cpu().numpy() for t in (blk.shift1, blk.scale1, blk.gate1, blk.shift_c, blk.scale_c, blk.gate_c,
+                                       blk.shift2, blk.scale2, blk.gate2)]
+
+        def mm(name, x, out, inn):
+            return o.matmul(12, raw[name], inn, out, x)
+        qkv = mm("qkv", norm_mod(hs, v[0], v[1]), 3 * d, d)
+        hs = o.gate_residual(hs, np.tile(v[2], (n, 1)), mm("o", qkv[:, 2 * d:], d, d))
+        cq = mm("cq", norm_mod(hs, v[3], v[4]), d, d)
+        hs = o.gate_residual(hs, np.tile(v[5], (n, 1)), mm("co", cq, d, d))
+        g = o.swiglu(mm("fc1", norm_mod(hs, v[6], v[7]), 2 * F, d))
+        hs = o.gate_residual(hs, np.tile(v[8], (n, 1)), mm("fc2", g, d, F))
+    got = h.index_select(0, ri).cpu().numpy()
+    err = rel_fro(got - start, hs - start)
+    return {"method": f"{n} sampled rows of the step's output against the CPU oracle composed in fp32 through "
+                      f"all {len(trunk.blocks)} blocks (relative Frobenius error of the residual increment)",
+            "rows": [int(r) for r in rows], "rel_err": float(f"{err:.3e}"), "tol": 1e-2, "ok": bool(err <= 1e-2),
+            "seconds": round(time.time() - t0, 1)}
 
 
 # ----------------------------------------------------------------------------- GEMV and kernel cases
@@ -357,9 +507,30 @@ def gemv_kernel_name(K: int, N: int, M: int) -> str:
     return "gemv_mma_small_kernel" if M <= 4 else "gemv_mma_kernel"
 
 
-def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100) -> dict:
+def cpu_gemv_us(K: int, N: int, M: int, reps: int = 5) -> tuple[float, str]:
+    """Best-of-reps time of the reference's fh3_matmul (oracle/_ref; the oracle port if it is
+    absent) on one M-token GEMV, as benchmarks/bench_matmul.c:76-94 times it."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    o = orc.Oracle()
+    impl, kind = (orc.Reference(), "reference") if orc.Reference.available() else (o, "port")
+    raw = o.make_weights(seed=100, stream=9, rows=N, n=K)
+    x = np.random.default_rng(M).standard_normal((M, K), dtype=np.float32)
+    best = None
+    for i in range(reps + 1):
+        t0 = time.perf_counter()
+        impl.matmul(12, raw, K, N, x)
+        dt = time.perf_counter() - t0
+        if i > 0:
+            best = dt if best is None else min(best, dt)
+    return best * 1e6, kind
+
+
+def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100, cpu_threads=None) -> dict:
     """Device time of back-to-back GEMV calls (1, 4 and 16 tokens) on
-    weights larger than L2.
+    weights larger than L2, with the reference's CPU fh3_matmul timed beside each shape when
+    cpu_threads is given (rank 0 at N = 1).
 
     A sleep kernel holds the stream while the host queues `reps` calls, so the CUDA events
     bracket GPU time only (each call's launches, chained by programmatic dependent launch).
@@ -367,6 +538,8 @@ def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100) -> 
     import math
     out = {"unit": "GB/s", "peak": hbm_gbs, "peak_source": f"{peak_src} hbm_gbs", "reps": reps,
            "method": "sleep-held stream, CUDA events around back-to-back calls, weights rotated > L2",
+           "cpu_threads": cpu_threads,
+           "cpu_method": "fh3_matmul on the host, best of 5 calls after one warm-up (bench_matmul.c:76-94)",
            "shapes": []}
     for K, N in GEMV_SHAPES:
         wbytes = N * K // 256 * 144
@@ -387,9 +560,12 @@ def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100) -> 
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1000.0 / reps
             gbs = (wbytes + 4 * M * (K + N)) / us / 1e3
-            out["shapes"].append({"in": K, "out": N, "tokens": M, "kernel": gemv_kernel_name(K, N, M),
-                                  "us_per_call": round(us, 2),
-                                  "achieved": round(gbs, 1), "frac": round(gbs / hbm_gbs, 4)})
+            entry = {"in": K, "out": N, "tokens": M, "kernel": gemv_kernel_name(K, N, M),
+                     "us_per_call": round(us, 2), "achieved": round(gbs, 1), "frac": round(gbs / hbm_gbs, 4)}
+            if cpu_threads:
+                cus, kind = cpu_gemv_us(K, N, M)
+                entry.update({"cpu_us": round(cus, 1), "cpu_kind": kind})
+            out["shapes"].append(entry)
         del ws
         torch.cuda.synchronize()
     return out
@@ -570,7 +746,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    hc = host_cpu()
+    threads = pin_cpu_threads(hc["physical_cores"])
     o = orc.Oracle()
     raw = {}
     for i, (name, out, inn) in enumerate(block_shapes()):
@@ -597,7 +774,7 @@ def run_reference(args):
                                "7 projections)", "blocks": args.blocks, "rows": args.rows,
                    "text_rows": args.text_rows, "sample_rows": rows_s, "sample_text_rows": T,
                    "full_step_gflop": round(args.blocks * block_flops(args.rows, args.text_rows) / 1e9, 1)},
-        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": kind,
+        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": kind, "cpu": hc,
                          "sample": f"fh3_matmul (OpenMP, {threads} threads) over block 0's 7 Q4_K projections on "
                                    f"{rows_s} latent + {T} text rows, {f / 1e9:.1f} GFLOP per step"},
         "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -607,7 +784,6 @@ def run_reference(args):
 
 def main():
     args = parse()
-    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
     if args.case:
         run_case(args)
     elif args.impl == "reference":

@@ -154,6 +154,36 @@ def gemm(w: Q4KWeight, x_bf16, epi: int = EPI_F32, bias=None, gate=None, out=Non
     return out
 
 
+def q4k_to_bf16(w: Q4KWeight, out=None, stream=None):
+    """W's Q4_K rows as bf16 [out][in] (fh3's fp32 weight rounded once): the first half of
+    the two-pass GEMM."""
+    torch = _torch()
+    _ensure(w.data)
+    if out is None:
+        out = torch.empty((w.out, w.in_), dtype=torch.bfloat16, device=w.data.device)
+    d = w.desc
+    check(load().fh3cuda_q4k_to_bf16_dev(ctypes.byref(d), _ptr(out), _stream(stream)))
+    return out
+
+
+def gemm_bf16w(w_bf16, x_bf16, epi: int = EPI_F32, bias=None, gate=None, out=None, stream=None):
+    """The tcgen05 GEMM on a bf16 [out][in] weight matrix (fh3cuda_gemm_bf16w_dev): the
+    second half of the two-pass GEMM, same epilogues as gemm()."""
+    torch = _torch()
+    _ensure(x_bf16)
+    n_tok = x_bf16.shape[0]
+    N, K = w_bf16.shape
+    n_out = N // 2 if epi == EPI_SWIGLU else N
+    if out is None:
+        dt = torch.bfloat16 if epi in (EPI_BF16, EPI_SWIGLU) else torch.float32
+        out = torch.empty((n_tok, n_out), dtype=dt, device=x_bf16.device)
+    if x_bf16.stride(-1) != 1 or not w_bf16.is_contiguous():
+        raise ValueError("x_bf16 rows and the weight matrix must be contiguous")
+    check(load().fh3cuda_gemm_bf16w_dev(_ptr(w_bf16), N, K, _ptr(x_bf16), x_bf16.stride(0), _ptr(out),
+                                        out.stride(0), n_tok, _ptr(bias), _ptr(gate), epi, _stream(stream)))
+    return out
+
+
 def to_bf16(x, out=None, stream=None):
     torch = _torch()
     _ensure(x)

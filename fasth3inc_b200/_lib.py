@@ -36,7 +36,8 @@ EXPORTED = [
     "fh3cuda_vsa_tiles_dev", "fh3cuda_attention_f32_dev", "fh3cuda_pack_open", "fh3cuda_pack_num_layers",
     "fh3cuda_pack_device_bytes", "fh3cuda_pack_layer", "fh3cuda_pack_close", "fh3cuda_adaln_open",
     "fh3cuda_adaln_dims", "fh3cuda_adaln_row", "fh3cuda_adaln_close", "fh3cuda_dit_prepare_text_dev",
-    "fh3cuda_dit_forward_dev", "fh3cuda_gemm_launches",
+    "fh3cuda_dit_forward_dev", "fh3cuda_gemm_launches", "fh3cuda_set_scratch_limit", "fh3cuda_alloc_stats",
+    "fh3cuda_wait_selftest_dev", "fh3cuda_q4k_to_bf16_dev", "fh3cuda_gemm_bf16w_dev",
 ]
 
 
@@ -151,6 +152,11 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         "fh3cuda_dit_forward_dev": (c_int, [ctypes.POINTER(Fh3CudaDitCfg), ctypes.POINTER(Fh3CudaDitGlobals), vp, vp,
                                             ctypes.POINTER(Fh3CudaSeq), vp, vp, c_int, vp, vp, vp, vp, vp, vp]),
         "fh3cuda_gemm_launches": (c_int, [i64]),
+        "fh3cuda_set_scratch_limit": (None, [ctypes.c_uint64]),
+        "fh3cuda_wait_selftest_dev": (c_int, [ctypes.c_uint64, vp]),
+        "fh3cuda_q4k_to_bf16_dev": (c_int, [Wp, vp, vp]),
+        "fh3cuda_gemm_bf16w_dev": (c_int, [vp, i64, i64, vp, i64, vp, i64, i64, vp, vp, c_int, vp]),
+        "fh3cuda_alloc_stats": (None, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
         "fh3cuda_attention_f32_dev": (c_int, [vp, i64, vp, i64, vp, i64, vp, i64, c_int, c_int, c_int, vp]),
         "fh3cuda_vsa_num_tiles": (c_int, [ctypes.POINTER(Fh3CudaSeq), c_int, ctypes.POINTER(c_int),
                                           ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
@@ -174,3 +180,15 @@ def last_error() -> str:
 def check(rc: int) -> None:
     if rc != FH3_OK:
         raise Fh3CudaError(rc, last_error())
+
+
+def alloc_stats() -> tuple[int, int]:
+    """(cudaMalloc calls the library has made, scratch bytes it holds now)."""
+    a, b = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    load().fh3cuda_alloc_stats(ctypes.byref(a), ctypes.byref(b))
+    return int(a.value), int(b.value)
+
+
+def set_scratch_limit(nbytes: int) -> None:
+    """Budget for the library's scratch over all devices (0 = unlimited)."""
+    load().fh3cuda_set_scratch_limit(int(nbytes))

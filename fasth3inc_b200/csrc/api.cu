@@ -1,6 +1,7 @@
 // api.cu -- libfh3cuda's host side: per-device contexts, error reporting,
 // the weight registry, the device-pointer dispatcher and the host-pointer
 // drop-in for fh3_matmul (include/fh3/fh3.h:107, src/core/fh3_ops.c:317-404).
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -82,22 +83,50 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+namespace {
+std::atomic<uint64_t> g_alloc_calls{0};      // cudaMalloc calls made by the library
+std::atomic<uint64_t> g_scratch_held{0};     // bytes of scratch held, all devices
+std::atomic<uint64_t> g_scratch_limit{0};    // 0 = unlimited
+}  // namespace
+
+int dev_alloc(void** p, size_t bytes, bool limited, const char* who) {
+    *p = nullptr;
+    if (limited) {
+        const uint64_t lim = g_scratch_limit.load();
+        const uint64_t held = g_scratch_held.load();
+        if (lim != 0 && held + bytes > lim)
+            return set_error(FH3_E_NOMEM, "%s: %zu bytes of scratch would exceed the limit of %llu (%llu held)", who,
+                             bytes, static_cast<unsigned long long>(lim), static_cast<unsigned long long>(held));
+    }
+    g_alloc_calls.fetch_add(1);
+    if (cudaMalloc(p, bytes) != cudaSuccess) {
+        cudaGetLastError();  // a failed cudaMalloc leaves no sticky error; clear the last-error slot
+        *p = nullptr;
+        return set_error(FH3_E_NOMEM, "%s: cudaMalloc(%zu) failed", who, bytes);
+    }
+    if (limited) g_scratch_held.fetch_add(bytes);
+    return FH3_OK;
+}
+
+void dev_free(void* p, size_t bytes, bool limited) {
+    if (!p) return;
+    cudaFree(p);
+    if (limited) g_scratch_held.fetch_sub(bytes);
+}
+
 void* scratch(DevCtx* c, int slot, size_t bytes, cudaStream_t s) {
     if (!c || slot < 0 || slot >= kScratchSlots) return nullptr;
     if (c->scratch_size[slot] >= bytes && c->scratch_ptr[slot]) return c->scratch_ptr[slot];
     // grow: earlier work on this stream may still read the old buffer
     if (c->scratch_ptr[slot]) {
         cudaStreamSynchronize(s);
-        cudaFree(c->scratch_ptr[slot]);
+        dev_free(c->scratch_ptr[slot], c->scratch_size[slot], true);
         c->scratch_ptr[slot] = nullptr;
         c->scratch_size[slot] = 0;
     }
     size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
     void* p = nullptr;
-    if (cudaMalloc(&p, want) != cudaSuccess) {
-        set_error(FH3_E_NOMEM, "scratch: cudaMalloc(%zu) failed", want);
-        return nullptr;
-    }
+    if (dev_alloc(&p, want, true, "scratch") != FH3_OK) return nullptr;
     c->scratch_ptr[slot] = p;
     c->scratch_size[slot] = want;
     return p;
@@ -145,8 +174,13 @@ extern "C" int fh3cuda_init(int device) {
     DevCtx* c = new DevCtx();
     c->device = device;
     c->sms = prop.multiProcessorCount;
-    e = cudaMalloc(&c->d_status, sizeof(int) * 4);
-    if (e == cudaSuccess) e = cudaMemset(c->d_status, 0, sizeof(int) * 4);
+    void* st = nullptr;
+    if (dev_alloc(&st, sizeof(int) * 4, false, "fh3cuda_init") != FH3_OK) {
+        delete c;
+        return FH3_E_NOMEM;
+    }
+    c->d_status = static_cast<int*>(st);
+    e = cudaMemset(c->d_status, 0, sizeof(int) * 4);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         delete c;
@@ -165,6 +199,39 @@ extern "C" int fh3cuda_take_status(void) {
 }
 
 extern "C" int fh3cuda_sm_count(void) { return ctx_sms(ctx()); }
+
+extern "C" void fh3cuda_set_scratch_limit(uint64_t bytes) { g_scratch_limit.store(bytes); }
+
+namespace fh3selftest {
+// One CTA of one thread: an mbarrier that expects one arrival nobody makes, waited on
+// with the library's bounded wait (the routine every kernel's waits use) under
+// `limit_ns`.  Nothing else is in flight, so the kernel simply returns when the wait
+// gives up; the status word then holds FH3CUDA_E_TIMEOUT.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, int* status, int* gave_up) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    fh3::mbar_init(&bar, 1);
+    abort_flag = 0;
+    fh3::fence_mbar_init();
+    const bool ok = fh3::mbar_wait_for(&bar, 0u, &abort_flag, status, limit_ns);
+    *gave_up = ok ? 0 : 1;
+}
+}  // namespace fh3selftest
+
+extern "C" int fh3cuda_wait_selftest_dev(uint64_t limit_ns, void* stream) {
+    DevCtx* c = ctx();
+    if (!c) return set_error(FH3CUDA_E_NODEV, "fh3cuda_wait_selftest_dev: call fh3cuda_init first");
+    if (limit_ns == 0 || limit_ns > 2000000000ull)
+        return set_error(FH3_E_INVALID, "fh3cuda_wait_selftest_dev: limit must be in (0, 2 s]");
+    // the flag lives in the status block's second word (allocated at set-up)
+    fh3selftest::wait_selftest_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, c->d_status, c->d_status + 1);
+    return check_cuda(cudaGetLastError(), "wait_selftest_kernel launch");
+}
+
+extern "C" void fh3cuda_alloc_stats(uint64_t* alloc_calls, uint64_t* scratch_bytes) {
+    if (alloc_calls) *alloc_calls = g_alloc_calls.load();
+    if (scratch_bytes) *scratch_bytes = g_scratch_held.load();
+}
 
 extern "C" int fh3cuda_device_status(void* stream) {
     DevCtx* c = ctx();
@@ -320,7 +387,7 @@ extern "C" int fh3cuda_upload_weights(const void* host, size_t bytes, void** dev
     if (!host || bytes == 0 || !dev_out) return set_error(FH3_E_INVALID, "fh3cuda_upload_weights: bad arguments");
     if (!ctx()) return set_error(FH3CUDA_E_NODEV, "fh3cuda_upload_weights: call fh3cuda_init first");
     void* d = nullptr;
-    if (cudaMalloc(&d, bytes) != cudaSuccess) return set_error(FH3_E_NOMEM, "fh3cuda_upload_weights: cudaMalloc(%zu)", bytes);
+    if (dev_alloc(&d, bytes, false, "fh3cuda_upload_weights") != FH3_OK) return FH3_E_NOMEM;
     cudaError_t e = cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         cudaFree(d);
@@ -361,7 +428,16 @@ const uint8_t* lookup_weights(const uint8_t* host, size_t bytes) {
 
 int matmul_host(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias) {
     DevCtx* c = ctx();
-    if (!c) return set_error(FH3CUDA_E_NODEV, "fh3_matmul drop-in: call fh3cuda_init first");
+    if (!c) {
+        // an unmodified fh3 caller relinked onto the drop-in never calls fh3cuda_init: set up
+        // the calling thread's current device (device 0 unless the caller chose another)
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+        const int rc = fh3cuda_init(dev);
+        if (rc != FH3_OK) return rc;
+        c = ctx();
+        if (!c) return set_error(FH3CUDA_E_NODEV, "fh3_matmul drop-in: no device context");
+    }
     // fh3_matmul returns silently on these (src/core/fh3_ops.c:318-321); report them instead
     if (!w || !x || !y || !w->data || n_tok <= 0 || w->in <= 0 || w->out <= 0)
         return set_error(FH3_E_INVALID, "fh3_matmul drop-in: bad arguments");

@@ -161,9 +161,11 @@ __device__ __forceinline__ bool mbar_try_wait_spin(uint64_t* bar, uint32_t parit
 // Wait for phase `parity` of `bar` to complete.  Gives up when `abort` (a
 // shared flag other roles raise on their own timeout) is set, or after
 // kWaitLimitNs; then records FH3CUDA_E_TIMEOUT and returns false.
+// mbar_wait_for takes the limit as an argument (the self-test of the wait, which has
+// to run out in milliseconds, is its other caller).
 template <bool SPIN = false>
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* status) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                              uint64_t limit_ns) {
     auto probe = [&]() { return SPIN ? mbar_try_wait_spin(bar, parity) : mbar_try_wait(bar, parity); };
     if (probe()) return true;
     const uint64_t t0 = globaltimer();
@@ -171,13 +173,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         if (probe()) return true;
         if ((it & 63) == 0) {
             if (*abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > limit_ns) {
                 *abort = 1;
                 record_status(status, FH3CUDA_E_TIMEOUT);
                 return false;
             }
         }
     }
+}
+template <bool SPIN = false>
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          int* status) {
+    return mbar_wait_for<SPIN>(bar, parity, abort, status, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------
@@ -515,4 +522,12 @@ int attention_f32_launch(const float* q, int64_t ldq, const float* k, int64_t ld
                          const float* outc, cudaStream_t s);
 // argument checks shared by the GEMV entry points (FH3_OK or the error code, message set)
 int gemv_args_ok(const Fh3CudaW* w, const float* x, const float* y, int n_tok, const char* who);
+// fh3cuda_gemm_q4k_dev's body (gemm.cu); fused_only never takes the two-pass path,
+// which is the one GEMM path that needs scratch (its bf16 weight copy)
+int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_t ldy, int64_t n_tok,
+             const float* bias, const float* gate, int epi, void* stream, bool fused_only);
+// cudaMalloc that the library counts (fh3cuda_alloc_stats) and that honours the scratch
+// limit when `limited` (FH3_E_NOMEM with the message set on failure or refusal)
+int dev_alloc(void** p, size_t bytes, bool limited, const char* who);
+void dev_free(void* p, size_t bytes, bool limited);
 }  // namespace fh3host

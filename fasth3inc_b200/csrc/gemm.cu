@@ -116,41 +116,54 @@ __device__ __forceinline__ void dequant_row_stage(const uint8_t* raw, const uint
     dequant_row_stage_q<J0, NJ>(hdr, q0, q1, sub, brow, swz);
 }
 
+// The scale pair of sub-block `sb` of a super-block header: s = 128*(d*sc) (exact scaling
+// of fh3's rounded d*sc) and nm = -(dmin*m).
+__device__ __forceinline__ void q4k_sub_scales(const uint4& hdr, int sb, float& s, float& nm) {
+    const float d = fh3::h2f_bits(hdr.x), dmin = fh3::h2f_bits(hdr.x >> 16);
+    int sc, m;
+    fh3::q4k_scale_min_words(hdr.y, hdr.z, hdr.w, sb, sc, m);
+    s = __fmul_rn(d, static_cast<float>(sc)) * 128.0f;
+    nm = -__fmul_rn(dmin, static_cast<float>(m));
+}
+
+// Eight consecutive weights of one sub-block as bf16: the low (hh = 0) or high (hh = 1)
+// nibbles of the nibble bytes in wa (first four) and wb (next four).  Two weights per
+// packed fp32x2 subtract and FMA: (1 + q/128) - 1 = q/128 exact, then one rounding of
+// s * q/128 + nm, the same fp32 weight as fh3's (d*sc)*q - dmin*m, then one rounding
+// to bf16.  Every Q4_K -> bf16 path of this file goes through here.
+__device__ __forceinline__ uint4 q4k_chunk8_bf16(float s, float nm, uint32_t wa, uint32_t wb, int hh) {
+    const uint32_t va = ((hh ? (wa >> 4) : wa) & 0x0F0F0F0Fu) | 0x80808080u;
+    const uint32_t vb = ((hh ? (wb >> 4) : wb) & 0x0F0F0F0Fu) | 0x80808080u;
+    const uint64_t s2 = fh3::f2_pack(s, s), n2 = fh3::f2_pack(nm, nm);
+    const uint64_t one2 = fh3::f2_pack(-1.0f, -1.0f);
+    auto w2 = [&](uint32_t v, uint32_t sel_a, uint32_t sel_b) {
+        const uint64_t nb = fh3::f2_pack(fh3::nib_f(v, sel_a), fh3::nib_f(v, sel_b));
+        const float2 w = fh3::f2_unpack(fh3::f2_fma(s2, fh3::f2_add(nb, one2), n2));
+        return pack_bf16(w.x, w.y);
+    };
+    uint4 pk;
+    pk.x = w2(va, fh3::kSel0, fh3::kSel1);
+    pk.y = w2(va, fh3::kSel2, fh3::kSel3);
+    pk.z = w2(vb, fh3::kSel0, fh3::kSel1);
+    pk.w = w2(vb, fh3::kSel2, fh3::kSel3);
+    return pk;
+}
+
 // the same on the stage's 32 nibble bytes already loaded (q0, q1)
 template <int J0, int NJ>
 __device__ __forceinline__ void dequant_row_stage_q(const uint4& hdr, const uint4& q0, const uint4& q1, int sub,
                                                     uint8_t* brow, uint32_t swz) {
-    const float d = fh3::h2f_bits(hdr.x), dmin = fh3::h2f_bits(hdr.x >> 16);
     float s[2], nm[2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         if ((hh == 0 && J0 >= 4) || (hh == 1 && J0 + NJ <= 4)) continue;
-        int sc, m;
-        fh3::q4k_scale_min_words(hdr.y, hdr.z, hdr.w, 2 * sub + hh, sc, m);
-        s[hh] = __fmul_rn(d, static_cast<float>(sc)) * 128.0f;
-        nm[hh] = -__fmul_rn(dmin, static_cast<float>(m));
+        q4k_sub_scales(hdr, 2 * sub + hh, s[hh], nm[hh]);
     }
     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
     for (int j = J0; j < J0 + NJ; ++j) {
         const int hh = j >> 2;
-        const uint32_t wa = qw[2 * (j & 3)], wb = qw[2 * (j & 3) + 1];
-        const uint32_t va = ((hh ? (wa >> 4) : wa) & 0x0F0F0F0Fu) | 0x80808080u;
-        const uint32_t vb = ((hh ? (wb >> 4) : wb) & 0x0F0F0F0Fu) | 0x80808080u;
-        // two weights per packed fp32x2 subtract and FMA: (1 + q/128) - 1 = q/128 exact, then
-        // one rounding of s * q/128 + nm, the same fp32 weight as the scalar form
-        const uint64_t s2 = fh3::f2_pack(s[hh], s[hh]), n2 = fh3::f2_pack(nm[hh], nm[hh]);
-        const uint64_t one2 = fh3::f2_pack(-1.0f, -1.0f);
-        auto w2 = [&](uint32_t v, uint32_t sel_a, uint32_t sel_b) {
-            const uint64_t nb = fh3::f2_pack(fh3::nib_f(v, sel_a), fh3::nib_f(v, sel_b));
-            const float2 w = fh3::f2_unpack(fh3::f2_fma(s2, fh3::f2_add(nb, one2), n2));
-            return pack_bf16(w.x, w.y);
-        };
-        uint4 pk;
-        pk.x = w2(va, fh3::kSel0, fh3::kSel1);
-        pk.y = w2(va, fh3::kSel2, fh3::kSel3);
-        pk.z = w2(vb, fh3::kSel0, fh3::kSel1);
-        pk.w = w2(vb, fh3::kSel2, fh3::kSel3);
+        const uint4 pk = q4k_chunk8_bf16(s[hh], nm[hh], qw[2 * (j & 3)], qw[2 * (j & 3) + 1], hh);
         // 16-byte chunk j of this 128-byte row, XOR-swizzled by row % 8
         *reinterpret_cast<uint4*>(brow + ((static_cast<uint32_t>(j) ^ swz) << 4)) = pk;
     }
@@ -728,24 +741,50 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
 // =============================================================================
 constexpr int64_t kTwoPassRows = 2048;
 
-// one thread per (weight row, super-block): its 144 bytes in nine 16-byte loads issued
-// together, then 256 weights into 512 contiguous bytes
-__global__ void dequant_q4k_bf16_kernel(const uint8_t* __restrict__ w, size_t rb, int64_t N, int K,
-                                        __nv_bfloat16* __restrict__ out) {
+// Q4_K -> bf16 [N][K], one warp per super-block step: lane l writes output chunk l of
+// the super-block (weights 8l..8l+7, 16 bytes), so a warp's store is 512 contiguous
+// bytes; every lane reads the 16-byte header (one broadcast request) and the 8 nibble
+// bytes its chunk needs (the 32 lanes' reads cover the 128 nibble bytes).  kUnroll
+// super-blocks a warp are loaded before any is converted, to keep enough reads in
+// flight.  Loads are streaming (evict-first): the weights are read once, and L2 is kept
+// for the GEMM's tiles.
+constexpr int kExpandUnroll = 8;
+constexpr int kExpandThreads = 256;
+
+__global__ void __launch_bounds__(kExpandThreads)
+    dequant_q4k_bf16_kernel(const uint8_t* __restrict__ w, size_t rb, int64_t N, int K,
+                            __nv_bfloat16* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
     const int nblk = K / fh3::kQ4KBlock;
     const int64_t total = N * nblk;
-    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t n = idx / nblk;
-        const int b = static_cast<int>(idx - n * nblk);
-        const uint4* raw = reinterpret_cast<const uint4*>(w + n * rb + static_cast<size_t>(b) * fh3::kQ4KBytes);
-        uint4 v[9];
+    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int sub = lane >> 3, j = lane & 7, hh = j >> 2;
+    const int qoff = 16 + 32 * sub + 8 * (j & 3);  // this lane's 8 nibble bytes
+    for (int64_t base = warp0 * kExpandUnroll; base < total; base += nwarps * kExpandUnroll) {
+        uint4 hdr[kExpandUnroll];
+        uint2 q[kExpandUnroll];
 #pragma unroll
-        for (int i = 0; i < 9; ++i) v[i] = __ldcs(raw + i);  // read once: keep L2 for the GEMM's tiles
-        uint8_t* dst = reinterpret_cast<uint8_t*>(out + n * K + static_cast<int64_t>(b) * fh3::kQ4KBlock);
+        for (int u = 0; u < kExpandUnroll; ++u) {
+            const int64_t idx = base + u;
+            if (idx < total) {
+                const int64_t n = idx / nblk;
+                const uint8_t* blk = w + n * rb + static_cast<size_t>(idx - n * nblk) * fh3::kQ4KBytes;
+                hdr[u] = __ldcs(reinterpret_cast<const uint4*>(blk));
+                q[u] = __ldcs(reinterpret_cast<const uint2*>(blk + qoff));
+            }
+        }
 #pragma unroll
-        for (int sub = 0; sub < 4; ++sub)
-            dequant_row_stage_q<0, 8>(v[0], v[1 + 2 * sub], v[2 + 2 * sub], sub, dst + sub * 128, 0u);
+        for (int u = 0; u < kExpandUnroll; ++u) {
+            const int64_t idx = base + u;
+            if (idx < total) {
+                const int64_t n = idx / nblk;
+                float sc, nm;
+                q4k_sub_scales(hdr[u], 2 * sub + hh, sc, nm);
+                const uint4 pk = q4k_chunk8_bf16(sc, nm, q[u].x, q[u].y, hh);
+                *reinterpret_cast<uint4*>(out + n * K + (idx - n * nblk) * fh3::kQ4KBlock + lane * 8) = pk;
+            }
+        }
     }
 }
 
@@ -923,43 +962,9 @@ bool use_pair_kernel(int64_t n_tok) {
     return n_tok > 128;
 }
 
-}  // namespace
-
-// kernel launches one fh3cuda_gemm_q4k_dev call of n_tok rows makes (the two-pass path
-// adds the dequantisation pass); the same rule as the dispatch below
-extern "C" int fh3cuda_gemm_launches(int64_t n_tok) {
-    const char* gk = getenv("FH3CUDA_GEMM_KERNEL");
-    const bool force_fused = gk && (strcmp(gk, "2sm") == 0 || strcmp(gk, "1sm") == 0);
-    const bool force_two = gk && strcmp(gk, "two-pass") == 0;
-    const bool two = use_pair_kernel(n_tok) && !force_fused && (force_two || n_tok >= kTwoPassRows);
-    return two ? 2 : 1;
-}
-
-extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y,
-                                    int64_t ldy, int64_t n_tok, const float* bias, const float* gate,
-                                    int epi, void* stream) {
+// kernel attributes and the co-resident cluster counts, once per process
+int gemm_setup() {
     using namespace fh3host;
-    DevCtx* c = ctx();
-    if (!c) return set_error(FH3CUDA_E_NODEV, "fh3cuda_gemm_q4k_dev: call fh3cuda_init first");
-    if (!w || !w->data || !x_bf16 || !y || n_tok <= 0 || w->in <= 0 || w->out <= 0)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: bad arguments");
-    if (w->type != FH3CUDA_TYPE_Q4_K || (w->in % fh3::kQ4KBlock) != 0)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: Q4_K weights with in %% 256 == 0 required");
-    if (epi < FH3CUDA_EPI_F32 || epi > FH3CUDA_EPI_RESID)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: unknown epilogue %d", epi);
-    if (epi == FH3CUDA_EPI_RESID && !gate)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: the residual epilogue needs a gate");
-    if (epi == FH3CUDA_EPI_SWIGLU && (w->out % 2) != 0)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: SwiGLU needs an even number of rows");
-    if ((reinterpret_cast<uintptr_t>(w->data) & 15) || (reinterpret_cast<uintptr_t>(x_bf16) & 15))
-        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: weights and x must be 16-byte aligned");
-    if (n_tok > 0x7FFFFFFF || w->out > 0x7FFFFFFF)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: dimensions exceed the TMA coordinate range");
-    const int64_t n_out = epi == FH3CUDA_EPI_SWIGLU ? w->out / 2 : w->out;
-    if (ldy < n_out) return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: ldy < output columns");
-    if (ldx < w->in || (ldx % 8) != 0)
-        return set_error(FH3_E_INVALID, "fh3cuda_gemm_q4k_dev: ldx must be >= K and a multiple of 8");
-
     std::call_once(g_attr_once, [] {
         g_attr_err = cudaFuncSetAttribute(gemm_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           one::SMEM_BYTES);
@@ -989,20 +994,140 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
             }
         }
     });
-    if (g_attr_err != cudaSuccess) return check_cuda(g_attr_err, "gemm kernel attributes");
+    return g_attr_err == cudaSuccess ? FH3_OK : check_cuda(g_attr_err, "gemm kernel attributes");
+}
+
+// checks shared by both GEMM entry points on the activations, output and epilogue
+int check_gemm_args(const char* who, const void* x_bf16, int64_t ldx, const void* y, int64_t ldy, int64_t n_tok,
+                    int64_t N, int64_t K, const float* gate, int epi) {
+    using namespace fh3host;
+    if (!x_bf16 || !y || n_tok <= 0 || K <= 0 || N <= 0) return set_error(FH3_E_INVALID, "%s: bad arguments", who);
+    if (epi < FH3CUDA_EPI_F32 || epi > FH3CUDA_EPI_RESID)
+        return set_error(FH3_E_INVALID, "%s: unknown epilogue %d", who, epi);
+    if (epi == FH3CUDA_EPI_RESID && !gate) return set_error(FH3_E_INVALID, "%s: the residual epilogue needs a gate", who);
+    if (epi == FH3CUDA_EPI_SWIGLU && (N % 2) != 0)
+        return set_error(FH3_E_INVALID, "%s: SwiGLU needs an even number of rows", who);
+    if (reinterpret_cast<uintptr_t>(x_bf16) & 15) return set_error(FH3_E_INVALID, "%s: x must be 16-byte aligned", who);
+    if (n_tok > 0x7FFFFFFF || N > 0x7FFFFFFF)
+        return set_error(FH3_E_INVALID, "%s: dimensions exceed the TMA coordinate range", who);
+    const int64_t n_out = epi == FH3CUDA_EPI_SWIGLU ? N / 2 : N;
+    if (ldy < n_out) return set_error(FH3_E_INVALID, "%s: ldy < output columns", who);
+    if (ldx < K || (ldx % 8) != 0) return set_error(FH3_E_INVALID, "%s: ldx must be >= K and a multiple of 8", who);
+    return FH3_OK;
+}
+
+// tensor map of the bf16 activations: n_tok rows of K, row stride ldx, 128 x 64 boxes
+int map_activations(CUtensorMap* tmA, const void* x_bf16, int64_t ldx, int64_t n_tok, int64_t K) {
+    using namespace fh3host;
+    const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(n_tok)};
+    const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(ldx) * 2};
+    const cuuint32_t box[2] = {BK, 128};
+    const cuuint32_t es[2] = {1, 1};
+    CUresult r = encode_tiled(tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x_bf16), gdim, gstr, box,
+                              es, CU_TENSOR_MAP_SWIZZLE_128B);
+    return r == CUDA_SUCCESS ? FH3_OK : set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(A) failed: %d", (int)r);
+}
+
+Params make_params(int64_t n_tok, int64_t N, int64_t K, int64_t ldy, const float* bias, const float* gate, void* y,
+                   int epi, int* status) {
+    Params p;
+    p.M = n_tok;
+    p.N = N;
+    p.K = K;
+    p.n_out = epi == FH3CUDA_EPI_SWIGLU ? N / 2 : N;
+    p.ldy = ldy;
+    p.bias = bias;
+    p.gate = gate;
+    p.y = y;
+    p.epi = epi;
+    p.status = status;
+    return p;
+}
+
+cudaLaunchConfig_t pair_config(cudaLaunchAttribute* at, int64_t pairs, int threads, int smem, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+int64_t gemm_tiles(const Params& p, int64_t rows_per_tile) {
+    const int64_t num_n = p.epi == FH3CUDA_EPI_SWIGLU ? (p.n_out + 127) / 128 : (p.N + 255) / 256;
+    return ((p.M + rows_per_tile - 1) / rows_per_tile) * num_n;
+}
+
+// gemm_bf16_pair_kernel on a bf16 [N][K] weight matrix (K a multiple of 64, 16-byte aligned)
+int launch_bf16_pair(const CUtensorMap& tmA, const __nv_bfloat16* wb, const Params& p, cudaStream_t s) {
+    using namespace fh3host;
+    CUtensorMap tmB;
+    const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.K), static_cast<cuuint64_t>(p.N)};
+    const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(p.K) * 2};
+    const cuuint32_t box[2] = {BK, 128};
+    const cuuint32_t es[2] = {1, 1};
+    CUresult r = encode_tiled(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(wb), gdim, gstr,
+                              box, es, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(B) failed: %d", (int)r);
+    const int64_t tiles = gemm_tiles(p, 256);
+    const int64_t pairs = tiles < g_bf_clusters ? tiles : g_bf_clusters;
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = pair_config(at, pairs, bfp::kThreads, bfp::SMEM_BYTES, s);
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel, tmA, tmB, p), "gemm_bf16_pair_kernel launch");
+}
+
+// dequant_q4k_bf16_kernel over the whole weight matrix
+int launch_expand(fh3host::DevCtx* c, const Fh3CudaW* w, __nv_bfloat16* wb, cudaStream_t s) {
+    using namespace fh3host;
+    const int64_t work = w->out * (w->in / fh3::kQ4KBlock);
+    const int64_t per_block = (kExpandThreads / 32) * kExpandUnroll;
+    const int64_t cap = static_cast<int64_t>(ctx_sms(c)) * (2048 / kExpandThreads);
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + per_block - 1) / per_block, cap)));
+    dequant_q4k_bf16_kernel<<<blocks, kExpandThreads, 0, s>>>(w->data, fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, w->in),
+                                                              w->out, static_cast<int>(w->in), wb);
+    return check_cuda(cudaGetLastError(), "dequant_q4k_bf16_kernel launch");
+}
+
+}  // namespace
+
+// kernel launches one fh3cuda_gemm_q4k_dev call of n_tok rows makes (the two-pass path
+// adds the dequantisation pass); the same rule as the dispatch below
+extern "C" int fh3cuda_gemm_launches(int64_t n_tok) {
+    const char* gk = getenv("FH3CUDA_GEMM_KERNEL");
+    const bool force_fused = gk && (strcmp(gk, "2sm") == 0 || strcmp(gk, "1sm") == 0);
+    const bool force_two = gk && strcmp(gk, "two-pass") == 0;
+    const bool two = use_pair_kernel(n_tok) && !force_fused && (force_two || n_tok >= kTwoPassRows);
+    return two ? 2 : 1;
+}
+
+namespace fh3host {
+
+// The body of fh3cuda_gemm_q4k_dev.  fused_only keeps every row count on the fused
+// kernels (no bf16 weight copy, so no scratch) whatever FH3CUDA_GEMM_KERNEL says.
+int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_t ldy, int64_t n_tok,
+             const float* bias, const float* gate, int epi, void* stream, bool fused_only) {
+    const char* who = "fh3cuda_gemm_q4k_dev";
+    DevCtx* c = ctx();
+    if (!c) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);
+    if (!w || !w->data) return set_error(FH3_E_INVALID, "%s: bad arguments", who);
+    int rc = check_gemm_args(who, x_bf16, ldx, y, ldy, n_tok, w->out, w->in, gate, epi);
+    if (rc) return rc;
+    if (w->type != FH3CUDA_TYPE_Q4_K || (w->in % fh3::kQ4KBlock) != 0)
+        return set_error(FH3_E_INVALID, "%s: Q4_K weights with in %% 256 == 0 required", who);
+    if (reinterpret_cast<uintptr_t>(w->data) & 15)
+        return set_error(FH3_E_INVALID, "%s: weights and x must be 16-byte aligned", who);
+    if ((rc = gemm_setup())) return rc;
 
     const bool pair = use_pair_kernel(n_tok) && g_pair_clusters > 0;
     const size_t rb = fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, w->in);
     CUtensorMap tmA, tmW;
-    {
-        const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(w->in), static_cast<cuuint64_t>(n_tok)};
-        const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(ldx) * 2};
-        const cuuint32_t box[2] = {BK, 128};
-        const cuuint32_t es[2] = {1, 1};
-        CUresult r = encode_tiled(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x_bf16), gdim,
-                                  gstr, box, es, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(A) failed: %d", (int)r);
-    }
+    if ((rc = map_activations(&tmA, x_bf16, ldx, n_tok, w->in))) return rc;
     {
         const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(rb), static_cast<cuuint64_t>(w->out)};
         const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(rb)};
@@ -1012,67 +1137,72 @@ extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64
                                   gstr, box, es, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(W) failed: %d", (int)r);
     }
+    const Params p = make_params(n_tok, w->out, w->in, ldy, bias, gate, y, epi, ctx_status(c));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
     // large M: dequantise the weights once to bf16, then the TMA-fed bf16 pair kernel;
     // FH3CUDA_GEMM_KERNEL=2sm / 1sm force the fused kernels, =two-pass this path
     const char* gk = getenv("FH3CUDA_GEMM_KERNEL");
     const bool force_fused = gk && (strcmp(gk, "2sm") == 0 || strcmp(gk, "1sm") == 0);
     const bool force_two = gk && strcmp(gk, "two-pass") == 0;
-    const bool two_pass = pair && g_bf_clusters > 0 && !force_fused && (force_two || n_tok >= kTwoPassRows);
-    __nv_bfloat16* wb = nullptr;
-    CUtensorMap tmB;
+    const bool two_pass = !fused_only && pair && g_bf_clusters > 0 && !force_fused &&
+                          (force_two || n_tok >= kTwoPassRows);
     if (two_pass) {
-        const int64_t N = w->out, K = w->in;
-        wb = static_cast<__nv_bfloat16*>(scratch(c, 11, static_cast<size_t>(N) * K * 2, static_cast<cudaStream_t>(stream)));
+        auto* wb = static_cast<__nv_bfloat16*>(scratch(c, 11, static_cast<size_t>(w->out) * w->in * 2, s));
         if (!wb) return FH3_E_NOMEM;
-        const int64_t work = N * (K / fh3::kQ4KBlock);
-        const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 16));
-        dequant_q4k_bf16_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(w->data, rb, N,
-                                                                                          static_cast<int>(K), wb);
-        int rc = check_cuda(cudaGetLastError(), "dequant_q4k_bf16_kernel launch");
-        if (rc) return rc;
-        const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-        const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(K) * 2};
-        const cuuint32_t box[2] = {BK, 128};
-        const cuuint32_t es[2] = {1, 1};
-        CUresult r = encode_tiled(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wb, gdim, gstr, box, es,
-                                  CU_TENSOR_MAP_SWIZZLE_128B);
-        if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(B) failed: %d", (int)r);
+        if ((rc = launch_expand(c, w, wb, s))) return rc;
+        return launch_bf16_pair(tmA, wb, p, s);
     }
-    Params p;
-    p.M = n_tok;
-    p.N = w->out;
-    p.K = w->in;
-    p.n_out = n_out;
-    p.ldy = ldy;
-    p.bias = bias;
-    p.gate = gate;
-    p.y = y;
-    p.epi = epi;
-    p.status = ctx_status(c);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int64_t num_n = epi == FH3CUDA_EPI_SWIGLU ? (n_out + 127) / 128 : (w->out + 255) / 256;
     if (pair) {
-        const int64_t tiles = ((n_tok + 255) / 256) * num_n;
-        const int64_t avail = two_pass ? g_bf_clusters : g_pair_clusters;
-        const int64_t pairs = tiles < avail ? tiles : avail;
-        cudaLaunchConfig_t cfg = {};
+        const int64_t tiles = gemm_tiles(p, 256);
+        const int64_t pairs = tiles < g_pair_clusters ? tiles : g_pair_clusters;
         cudaLaunchAttribute at[1];
-        at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = 2;
-        at[0].val.clusterDim.y = 1;
-        at[0].val.clusterDim.z = 1;
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-        cfg.blockDim = dim3(two_pass ? bfp::kThreads : kThreadsPair, 1, 1);
-        cfg.dynamicSmemBytes = two_pass ? bfp::SMEM_BYTES : two::SMEM_BYTES;
-        cfg.stream = s;
-        cfg.attrs = at;
-        cfg.numAttrs = 1;
-        if (two_pass)
-            return check_cuda(cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel, tmA, tmB, p), "gemm_bf16_pair_kernel launch");
+        cudaLaunchConfig_t cfg = pair_config(at, pairs, kThreadsPair, two::SMEM_BYTES, s);
         return check_cuda(cudaLaunchKernelEx(&cfg, gemm_q4k_pair_kernel, tmA, tmW, p), "gemm_q4k_pair_kernel launch");
     }
-    const int64_t tiles = ((n_tok + 127) / 128) * num_n;
+    const int64_t tiles = gemm_tiles(p, 128);
     const int grid = static_cast<int>(tiles < ctx_sms(c) ? tiles : ctx_sms(c));
     gemm_q4k_tc_kernel<<<grid, kThreads, one::SMEM_BYTES, s>>>(tmA, tmW, p);
     return check_cuda(cudaGetLastError(), "gemm_q4k_tc_kernel launch");
+}
+
+}  // namespace fh3host
+
+extern "C" int fh3cuda_gemm_q4k_dev(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y,
+                                    int64_t ldy, int64_t n_tok, const float* bias, const float* gate,
+                                    int epi, void* stream) {
+    return fh3host::gemm_q4k(w, x_bf16, ldx, y, ldy, n_tok, bias, gate, epi, stream, false);
+}
+
+extern "C" int fh3cuda_q4k_to_bf16_dev(const Fh3CudaW* w, void* w_bf16, void* stream) {
+    using namespace fh3host;
+    const char* who = "fh3cuda_q4k_to_bf16_dev";
+    DevCtx* c = ctx();
+    if (!c) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);
+    if (!w || !w->data || !w_bf16 || w->in <= 0 || w->out <= 0)
+        return set_error(FH3_E_INVALID, "%s: bad arguments", who);
+    if (w->type != FH3CUDA_TYPE_Q4_K || (w->in % fh3::kQ4KBlock) != 0)
+        return set_error(FH3_E_INVALID, "%s: Q4_K weights with in %% 256 == 0 required", who);
+    if ((reinterpret_cast<uintptr_t>(w->data) & 15) || (reinterpret_cast<uintptr_t>(w_bf16) & 15))
+        return set_error(FH3_E_INVALID, "%s: weights and output must be 16-byte aligned", who);
+    return launch_expand(c, w, static_cast<__nv_bfloat16*>(w_bf16), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fh3cuda_gemm_bf16w_dev(const void* w_bf16, int64_t out, int64_t in, const void* x_bf16, int64_t ldx,
+                                      void* y, int64_t ldy, int64_t n_tok, const float* bias, const float* gate,
+                                      int epi, void* stream) {
+    using namespace fh3host;
+    const char* who = "fh3cuda_gemm_bf16w_dev";
+    DevCtx* c = ctx();
+    if (!c) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);
+    if (!w_bf16) return set_error(FH3_E_INVALID, "%s: bad arguments", who);
+    int rc = check_gemm_args(who, x_bf16, ldx, y, ldy, n_tok, out, in, gate, epi);
+    if (rc) return rc;
+    if ((in % BK) != 0 || (reinterpret_cast<uintptr_t>(w_bf16) & 15))
+        return set_error(FH3_E_INVALID, "%s: in must be a multiple of 64 and the weights 16-byte aligned", who);
+    if ((rc = gemm_setup())) return rc;
+    if (g_bf_clusters <= 0) return set_error(FH3CUDA_E_CUDA, "%s: the pair kernel cannot be resident", who);
+    CUtensorMap tmA;
+    if ((rc = map_activations(&tmA, x_bf16, ldx, n_tok, in))) return rc;
+    const Params p = make_params(n_tok, out, in, ldy, bias, gate, y, epi, ctx_status(c));
+    return launch_bf16_pair(tmA, static_cast<const __nv_bfloat16*>(w_bf16), p, static_cast<cudaStream_t>(stream));
 }

@@ -25,6 +25,14 @@
 // GEMM's TMA never reads beyond n_tok rows (rows past the end are zero-filled by TMA, not
 // read from the array).  Calls that overlap on the GPU (two streams, or two host threads
 // on one device) race on the array: serialise them.
+//
+// The GEMM runs on the fused kernels at every row count (dequantisation in shared
+// memory), never on the two-pass path that the allocating entry point takes from 2048
+// rows: that path expands the weights into a bf16 copy in allocated scratch.  So
+// FH3CUDA_GEMM_KERNEL=two-pass has no effect here, and large row counts trade the
+// two-pass path's speed for the absence of scratch.  The cached symbol address is only
+// valid for the CUDA context it was taken in; like the rest of the library's per-device
+// state it does not survive cudaDeviceReset.
 #include <mutex>
 
 #include "common.cuh"
@@ -86,5 +94,5 @@ extern "C" int fh3cuda_matmul_noalloc_dev(const Fh3CudaW* w, const float* x, flo
     if (rc != FH3_OK) return rc;
     rc = fh3cuda_f32_to_bf16_dev(x, act, elems, stream);
     if (rc != FH3_OK) return rc;
-    return fh3cuda_gemm_q4k_dev(w, act, w->in, y, w->out, n_tok, bias, nullptr, FH3CUDA_EPI_F32, stream);
+    return gemm_q4k(w, act, w->in, y, w->out, n_tok, bias, nullptr, FH3CUDA_EPI_F32, stream, /*fused_only=*/true);
 }

@@ -204,10 +204,10 @@ extern "C" int fh3cuda_pack_open(const char* path, Fh3CudaPack** out) {
     p->bytes = dev_off;
     if (!ctx()) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);  // the file checks out
     p->device = ctx_device(ctx());
-    if (cudaMalloc(&p->dev, p->bytes) != cudaSuccess) {
-        p->dev = nullptr;
-        return set_error(FH3_E_NOMEM, "%s: cudaMalloc(%llu) for the trunk failed", who,
-                         static_cast<unsigned long long>(p->bytes));
+    {
+        void* d = nullptr;
+        if (dev_alloc(&d, p->bytes, false, who) != FH3_OK) return FH3_E_NOMEM;
+        p->dev = static_cast<uint8_t*>(d);
     }
     Bounce bb;
     int rc = bb.init();
@@ -291,9 +291,10 @@ extern "C" int fh3cuda_adaln_open(const char* path, uint64_t expect_hash, Fh3Cud
     if (!ctx()) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);  // the file checks out
     a->device = ctx_device(ctx());
     const uint64_t trunk_alloc = (trunk_bytes + 255) & ~static_cast<uint64_t>(255);
-    if (cudaMalloc(&a->dev, trunk_alloc + final_bytes + 4) != cudaSuccess) {
-        a->dev = nullptr;
-        return set_error(FH3_E_NOMEM, "%s: cudaMalloc for the table failed", who);
+    {
+        void* d = nullptr;
+        if (dev_alloc(&d, trunk_alloc + final_bytes + 4, false, who) != FH3_OK) return FH3_E_NOMEM;
+        a->dev = static_cast<float*>(d);
     }
     Bounce bb;
     int rc = bb.init();

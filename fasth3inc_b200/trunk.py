@@ -127,55 +127,150 @@ class Workspace:
 
 
 class Runner:
-    """Launches one block / one step through the C ABI, optionally timing GEMMs with events."""
+    """Launches one block / one step through the C ABI, optionally timing launches with events.
 
-    def __init__(self, trunk: Trunk, ws: Workspace, stream=None):
+    With `overlap` (the default), every projection of 2048 rows or more runs as its two
+    halves: the Q4_K -> bf16 expansion of its weights (fh3cuda_q4k_to_bf16_dev) on a side
+    stream into one of two bf16 buffers, and the GEMM on that buffer
+    (fh3cuda_gemm_bf16w_dev) on the main stream.  The expansion of the next such
+    projection is issued before the current GEMM, waiting only for the GEMM that last
+    read its buffer, so it runs while the current GEMM runs: the expansion (HBM-bound)
+    leaves the critical path, which the GEMM (tensor-bound) holds.  The launches, the
+    bf16 weights and the results are the same as fh3cuda_gemm_q4k_dev's two-pass path.
+    Without `overlap` every projection is one fh3cuda_gemm_q4k_dev call."""
+
+    def __init__(self, trunk: Trunk, ws: Workspace, stream=None, overlap: bool = True):
         import torch
         self.t = trunk
         self.ws = ws
         self.L = _lib.load()
         self.stream = stream if stream is not None else torch.cuda.current_stream(trunk.device)
         self.s = self.stream.cuda_stream
-        self.gemm_events: list | None = None  # list of (start, end, flops) when recording
+        self.overlap = overlap
+        self.side = torch.cuda.Stream(device=trunk.device) if overlap else None
+        self.wbuf = None                        # two bf16 weight buffers (allocated on first use)
+        self.ev_exp = [torch.cuda.Event(), torch.cuda.Event()]
+        self.ev_use = [torch.cuda.Event(), torch.cuda.Event()]
+        # timing records when not None: lists of (start, end, flops or bytes)
+        self.gemm_events: list | None = None
+        self.expand_events: list | None = None
+        self.norm_events: list | None = None
         self.launches = 0
 
-    def _gemm(self, w: Q4KWeight, x, ldx: int, rows: int, y, ldy: int, epi: int, gate=None):
+    # -- one launch each --------------------------------------------------------------
+    def _timed(self, kind: str, stream, amount: int, tag: str = ""):
         import torch
+        rec = getattr(self, kind)
+        if rec is None:
+            return None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        rec.append((e0, e1, amount, tag))
+        return e1
+
+    def _gemm_fused(self, op):
+        w, x, ldx, rows, y, ldy, epi, gate = op[1:9]
         d = w.desc
-        rec = self.gemm_events is not None
-        if rec:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(self.stream)
+        e1 = self._timed("gemm_events", self.stream, 2 * rows * w.in_ * w.out, f"fused:{rows}")
         check(self.L.fh3cuda_gemm_q4k_dev(ctypes.byref(d), x, ldx, y, ldy, rows, None,
                                           None if gate is None else gate.data_ptr(), epi, self.s))
-        if rec:
+        if e1 is not None:
             e1.record(self.stream)
-            self.gemm_events.append((e0, e1, 2 * rows * w.in_ * w.out))
         self.launches += self.L.fh3cuda_gemm_launches(rows)
 
-    def _norm(self, h, shift, scale, out):
-        check(self.L.fh3cuda_rmsnorm_modulate_dev(h.data_ptr(), None, shift.data_ptr(), scale.data_ptr(),
-                                                  out.data_ptr(), h.shape[0], h.shape[1], 1e-6, self.s))
+    def _expand(self, w: Q4KWeight, slot: int):
+        """Issue w's expansion into buffer `slot` on the side stream."""
+        import torch
+        if self.wbuf is None:
+            big = max(out * inn for _, out, inn in block_shapes(self.t.d, self.t.F))
+            self.wbuf = [torch.empty(big, dtype=torch.bfloat16, device=self.stream.device) for _ in range(2)]
+        self.side.wait_event(self.ev_use[slot])          # the GEMM that last read this buffer
+        e1 = self._timed("expand_events", self.side, w.out * (row_bytes(Q4_K, w.in_) + 2 * w.in_))
+        d = w.desc
+        check(self.L.fh3cuda_q4k_to_bf16_dev(ctypes.byref(d), self.wbuf[slot].data_ptr(), self.side.cuda_stream))
+        if e1 is not None:
+            e1.record(self.side)
+        self.ev_exp[slot].record(self.side)
         self.launches += 1
 
-    def block(self, blk: Block, h, text_bf16) -> None:
-        ws, d = self.ws, self.t.d
+    def _gemm_expanded(self, op, slot: int):
+        w, x, ldx, rows, y, ldy, epi, gate = op[1:9]
+        self.stream.wait_event(self.ev_exp[slot])
+        e1 = self._timed("gemm_events", self.stream, 2 * rows * w.in_ * w.out, f"bf16w:{rows}")
+        check(self.L.fh3cuda_gemm_bf16w_dev(self.wbuf[slot].data_ptr(), w.out, w.in_, x, ldx, y, ldy, rows, None,
+                                            None if gate is None else gate.data_ptr(), epi, self.s))
+        if e1 is not None:
+            e1.record(self.stream)
+        self.ev_use[slot].record(self.stream)
+        self.launches += 1
+
+    def _norm(self, op):
+        h, shift, scale, out = op[1:5]
+        e1 = self._timed("norm_events", self.stream, h.numel() * 4 + out.numel() * 2)
+        check(self.L.fh3cuda_rmsnorm_modulate_dev(h.data_ptr(), None, shift.data_ptr(), scale.data_ptr(),
+                                                  out.data_ptr(), h.shape[0], h.shape[1], 1e-6, self.s))
+        if e1 is not None:
+            e1.record(self.stream)
+        self.launches += 1
+
+    # -- a block as a list of launches --------------------------------------------------
+    def _block_ops(self, blk: Block, h, text_bf16) -> list:
+        """One block's launches: ("norm", h, shift, scale, out, tap) and
+        ("gemm", w, x, ldx, rows, y, ldy, epi, gate, tap), tap = (stage name, tensor)."""
+        ws, d, F = self.ws, self.t.d, self.t.F
         M, T = h.shape[0], text_bf16.shape[0]
         W = blk.w
-        self._norm(h, blk.shift1, blk.scale1, ws.a)
-        self._gemm(W["qkv"], ws.a.data_ptr(), d, M, ws.qkv.data_ptr(), 3 * d, EPI_BF16)
         v = ws.qkv.data_ptr() + 2 * d * 2  # V third of each row (bf16)
-        self._gemm(W["o"], v, 3 * d, M, h.data_ptr(), d, EPI_RESID, blk.gate1)
-        self._norm(h, blk.shift_c, blk.scale_c, ws.a)
-        self._gemm(W["cq"], ws.a.data_ptr(), d, M, ws.cq.data_ptr(), d, EPI_BF16)
-        self._gemm(W["ckv"], text_bf16.data_ptr(), d, T, ws.ckv.data_ptr(), 2 * d, EPI_BF16)
-        self._gemm(W["co"], ws.cq.data_ptr(), d, M, h.data_ptr(), d, EPI_RESID, blk.gate_c)
-        self._norm(h, blk.shift2, blk.scale2, ws.a)
-        self._gemm(W["fc1"], ws.a.data_ptr(), d, M, ws.g.data_ptr(), self.t.F, EPI_SWIGLU)
-        self._gemm(W["fc2"], ws.g.data_ptr(), self.t.F, M, h.data_ptr(), d, EPI_RESID, blk.gate2)
+        return [
+            ("norm", h, blk.shift1, blk.scale1, ws.a, ("a1", ws.a)),
+            ("gemm", W["qkv"], ws.a.data_ptr(), d, M, ws.qkv.data_ptr(), 3 * d, EPI_BF16, None, ("qkv", ws.qkv)),
+            ("gemm", W["o"], v, 3 * d, M, h.data_ptr(), d, EPI_RESID, blk.gate1, ("h_o", h)),
+            ("norm", h, blk.shift_c, blk.scale_c, ws.a, ("c", ws.a)),
+            ("gemm", W["cq"], ws.a.data_ptr(), d, M, ws.cq.data_ptr(), d, EPI_BF16, None, ("cq", ws.cq)),
+            ("gemm", W["ckv"], text_bf16.data_ptr(), d, T, ws.ckv.data_ptr(), 2 * d, EPI_BF16, None,
+             ("ckv", ws.ckv)),
+            ("gemm", W["co"], ws.cq.data_ptr(), d, M, h.data_ptr(), d, EPI_RESID, blk.gate_c, ("h_co", h)),
+            ("norm", h, blk.shift2, blk.scale2, ws.a, ("a2", ws.a)),
+            ("gemm", W["fc1"], ws.a.data_ptr(), d, M, ws.g.data_ptr(), F, EPI_SWIGLU, None, ("g", ws.g)),
+            ("gemm", W["fc2"], ws.g.data_ptr(), F, M, h.data_ptr(), d, EPI_RESID, blk.gate2, ("h_fc2", h)),
+        ]
+
+    def _two_pass(self, op) -> bool:
+        return self.overlap and op[0] == "gemm" and self.L.fh3cuda_gemm_launches(op[4]) == 2
+
+    def run(self, ops: list, tap=None) -> None:
+        """Issue `ops` in order; two-pass GEMMs get their expansions one projection ahead.
+        No expansion starts before the main stream reaches this call."""
+        import torch
+        expanded = [i for i, op in enumerate(ops) if self._two_pass(op)]
+        nxt = 0
+        if expanded:
+            start = torch.cuda.Event()
+            start.record(self.stream)
+            self.side.wait_event(start)
+            self._expand(ops[expanded[0]][1], 0)
+        for i, op in enumerate(ops):
+            if op[0] == "norm":
+                self._norm(op)
+            elif nxt < len(expanded) and expanded[nxt] == i:
+                if nxt + 1 < len(expanded):
+                    self._expand(ops[expanded[nxt + 1]][1], (nxt + 1) % 2)
+                self._gemm_expanded(op, nxt % 2)
+                nxt += 1
+            else:
+                self._gemm_fused(op)
+            if tap is not None:
+                tap(*op[-1])
+
+    def block(self, blk: Block, h, text_bf16, tap=None) -> None:
+        """One block on the rows of h.  `tap(stage, tensor)`, when given, sees every
+        intermediate right after the launch that produces it (the parity tests sample
+        rows of each; the launches are the same with or without it)."""
+        self.run(self._block_ops(blk, h, text_bf16), tap)
 
     def step(self, h, text_bf16) -> None:
         """One denoising step of the trunk on the rows of h (fp32, updated in place)."""
+        ops = []
         for blk in self.t.blocks:
-            self.block(blk, h, text_bf16)
+            ops += self._block_ops(blk, h, text_bf16)
+        self.run(ops)

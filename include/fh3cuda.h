@@ -96,6 +96,26 @@ FH3CUDA_API int fh3cuda_device_status(void *stream);
 /* Number of SMs of the current device (0 before fh3cuda_init). */
 FH3CUDA_API int fh3cuda_sm_count(void);
 
+/* Device-memory budget for the library's scratch (0 = unlimited, the default), over
+ * all devices.  A call whose scratch would grow past it fails with FH3_E_NOMEM and
+ * computes nothing (the void drop-in records it as its sticky status).  No counterpart
+ * in the reference, whose nearest equivalent is the host-memory plan preflight of the
+ * trunk streamer (src/io/fh3_trunk.c:101-129). */
+FH3CUDA_API void fh3cuda_set_scratch_limit(uint64_t bytes);
+
+/* Self-test of the bounded device-side wait that every kernel's mbarrier waits use:
+ * launches one thread that waits on an mbarrier nobody arrives at, with a limit of
+ * limit_ns (at most 2 s) instead of the kernels' 4 s.  Nothing else is in flight; the
+ * wait gives up, the kernel returns and fh3cuda_device_status then reports
+ * FH3CUDA_E_TIMEOUT, with the context still usable.  No counterpart in the reference
+ * (its CPU code has no device waits). */
+FH3CUDA_API int fh3cuda_wait_selftest_dev(uint64_t limit_ns, void *stream);
+
+/* Library allocation counters: cudaMalloc calls made so far (scratch growth, context
+ * set-up, weight uploads, trunk and table uploads) and scratch bytes currently held.
+ * No counterpart in the reference (diagnostics). */
+FH3CUDA_API void fh3cuda_alloc_stats(uint64_t *alloc_calls, uint64_t *scratch_bytes);
+
 /* ---- format ------------------------------------------------------------ */
 
 /* Bytes of one weight row: replaces fh3_row_bytes (include/fh3/fh3.h:103,
@@ -133,7 +153,11 @@ FH3CUDA_API int fh3cuda_matmul_dev(const Fh3CudaW *w, const float *x, float *y, 
  * larger calls return FH3_E_INVALID), held by every GPU that loads the library.
  * Set-up: fh3cuda_init(device), then the first call on a device resolves the array's
  * address (make that first call before any stream capture).  All calls share the
- * array: calls that overlap on the GPU race and must be serialised. */
+ * array: calls that overlap on the GPU race and must be serialised.  More than 16
+ * tokens always run the fused GEMM kernels (never the two-pass path with its bf16
+ * weight copy, whatever FH3CUDA_GEMM_KERNEL says), so no row count allocates.  The
+ * library's per-device state, this array's cached address included, does not survive
+ * cudaDeviceReset. */
 FH3CUDA_API int fh3cuda_matmul_noalloc_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
                                            const float *bias_or_null, void *stream);
 
@@ -142,7 +166,9 @@ FH3CUDA_API int fh3cuda_matmul_noalloc_dev(const Fh3CudaW *w, const float *x, fl
  * registered weight ranges (fh3cuda_register_weights); an unregistered
  * pointer is staged to the device for this call.  x is copied in, y copied
  * out; the call returns when y is written.  Failures are recorded for
- * fh3cuda_take_status() and printed to stderr once. */
+ * fh3cuda_take_status() and printed to stderr once.  If the calling thread's
+ * current device has no context yet, the first call sets it up (fh3cuda_init),
+ * so an unmodified fh3 program needs no added call. */
 FH3CUDA_API void fh3cuda_matmul(const Fh3CudaW *w, const float *x, float *y, int n_tok,
                     const float *bias_or_null);
 
@@ -195,6 +221,21 @@ FH3CUDA_API int fh3cuda_gemv_q4k_dev(const Fh3CudaW *w, const float *x, float *y
 FH3CUDA_API int fh3cuda_gemm_q4k_dev(const Fh3CudaW *w, const void *x_bf16, int64_t ldx, void *y,
                                      int64_t ldy, int64_t n_tok, const float *bias_or_null,
                                      const float *gate, int epilogue, void *stream);
+
+/* The two halves of the two-pass path, for callers that schedule them themselves (the
+ * trunk runner expands the next projection's weights on a second stream while the
+ * current GEMM runs).  fh3cuda_q4k_to_bf16_dev writes w's Q4_K rows as bf16 [out][in]
+ * (fh3's fp32 weight, dequant_q4_k of src/core/fh3_quant.c:154-196, rounded once to
+ * bf16: the values the fused GEMM dequantisers feed the tensor cores); w_bf16 holds
+ * out * in elements, 16-byte aligned.  fh3cuda_gemm_bf16w_dev is
+ * fh3cuda_gemm_q4k_dev's GEMM on such a bf16 [out][in] weight matrix (in a multiple of
+ * 64): same epilogues, same results as the Q4_K entry point on the matrix it expands
+ * to.  Together they replace fh3_matmul's large-M regime (src/core/fh3_ops.c:317-404). */
+FH3CUDA_API int fh3cuda_q4k_to_bf16_dev(const Fh3CudaW *w, void *w_bf16, void *stream);
+FH3CUDA_API int fh3cuda_gemm_bf16w_dev(const void *w_bf16, int64_t out, int64_t in, const void *x_bf16,
+                                       int64_t ldx, void *y, int64_t ldy, int64_t n_tok,
+                                       const float *bias_or_null, const float *gate, int epilogue,
+                                       void *stream);
 
 /* Kernel launches one fh3cuda_gemm_q4k_dev call of n_tok rows makes: 1 for the
  * fused kernels, 2 from 2048 rows on, where the weights are first expanded to a

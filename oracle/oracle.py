@@ -22,8 +22,24 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libfh3ref.so")
-# the reference source tree (only where it exists: the container that builds the checker)
-REF_TREE = os.environ.get("FH3_REF_TREE", "/root/reference")
+
+
+def reference_tree() -> str | None:
+    """The reference's source tree, where this machine has it: $FH3_REF_TREE, else the
+    reference_path recorded in the project's BASELINE.json; None when neither exists (GPU
+    boxes use the objects built beforehand into _ref/)."""
+    cand = os.environ.get("FH3_REF_TREE")
+    if not cand:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                cand = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    return cand if cand and os.path.isfile(os.path.join(cand, "src", "core", "fh3_ops.c")) else None
+
+
+REF_TREE = reference_tree()
 
 Q4K = 12
 F32 = 0
@@ -34,9 +50,11 @@ _c_f32p = ctypes.POINTER(ctypes.c_float)
 _c_u8p = ctypes.POINTER(ctypes.c_uint8)
 
 
-def build(quiet: bool = True) -> None:
-    """Compile liboracle.so (and _ref/libfh3ref.so where the reference exists)."""
-    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+def build(quiet: bool = True, relink: bool = False) -> None:
+    """Compile liboracle.so, and where the reference tree exists _ref/libfh3ref.so (and with
+    `relink` the fh3 callers relinked against libfh3cuda.so, which must be built first)."""
+    cmd = ["make", "-C", HERE] + ([f"REF={REF_TREE}"] if REF_TREE else [])
+    out = subprocess.run(cmd + (["all", "relink"] if relink else []), capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
     if not quiet:

@@ -59,8 +59,15 @@ TINY_H3 = ("meta.json", "dit_trunk.bin", "dit_globals.bin", "adaln_table.bin", "
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None, help="the reference source tree (default: $FH3_REF_TREE or "
+                                                 "BASELINE.json's reference_path)")
     args = ap.parse_args()
+    if args.ref is None:
+        sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+        from oracle.oracle import reference_tree
+        args.ref = reference_tree()
+    if not args.ref:
+        raise SystemExit("the reference source tree was not found: pass --ref or set FH3_REF_TREE")
     fx = os.path.join(args.ref, "tests", "fixtures", "quant")
     for name in ("Q4_K.bin", "matmul_ref.bin", "F16.bin", "BF16.bin", "Q8_0.bin", "Q2_K.bin", "Q3_K.bin",
                  "Q5_K.bin", "Q6_K.bin"):
