@@ -64,6 +64,11 @@ def _ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def sm_count() -> int:
+    """SMs of the current device (0 before init)."""
+    return int(load().fh3cuda_sm_count())
+
+
 def row_bytes(type_: int, n: int) -> int:
     """Bytes of one row of `n` weights (fh3_row_bytes)."""
     return int(load().fh3cuda_row_bytes(type_, n))
@@ -166,7 +171,8 @@ def q4k_to_bf16(w: Q4KWeight, out=None, stream=None):
     return out
 
 
-def gemm_bf16w(w_bf16, x_bf16, epi: int = EPI_F32, bias=None, gate=None, out=None, stream=None):
+def gemm_bf16w(w_bf16, x_bf16, epi: int = EPI_F32, bias=None, gate=None, out=None, stream=None,
+               weights_ready: bool = False):
     """The tcgen05 GEMM on a bf16 [out][in] weight matrix (fh3cuda_gemm_bf16w_dev): the
     second half of the two-pass GEMM, same epilogues as gemm()."""
     torch = _torch()
@@ -180,7 +186,8 @@ def gemm_bf16w(w_bf16, x_bf16, epi: int = EPI_F32, bias=None, gate=None, out=Non
     if x_bf16.stride(-1) != 1 or not w_bf16.is_contiguous():
         raise ValueError("x_bf16 rows and the weight matrix must be contiguous")
     check(load().fh3cuda_gemm_bf16w_dev(_ptr(w_bf16), N, K, _ptr(x_bf16), x_bf16.stride(0), _ptr(out),
-                                        out.stride(0), n_tok, _ptr(bias), _ptr(gate), epi, _stream(stream)))
+                                        out.stride(0), n_tok, _ptr(bias), _ptr(gate), epi,
+                                        _lib.GEMM_WEIGHTS_READY if weights_ready else 0, _stream(stream)))
     return out
 
 

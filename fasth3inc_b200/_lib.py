@@ -24,6 +24,7 @@ FH3CUDA_E_TIMEOUT = -21
 FH3CUDA_E_NODEV = -22
 
 EPI_F32, EPI_BF16, EPI_SWIGLU, EPI_RESID = 0, 1, 2, 3
+GEMM_WEIGHTS_READY = 1
 
 EXPORTED = [
     "fh3cuda_init", "fh3cuda_last_error", "fh3cuda_take_status", "fh3cuda_device_status",
@@ -155,7 +156,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         "fh3cuda_set_scratch_limit": (None, [ctypes.c_uint64]),
         "fh3cuda_wait_selftest_dev": (c_int, [ctypes.c_uint64, vp]),
         "fh3cuda_q4k_to_bf16_dev": (c_int, [Wp, vp, vp]),
-        "fh3cuda_gemm_bf16w_dev": (c_int, [vp, i64, i64, vp, i64, vp, i64, i64, vp, vp, c_int, vp]),
+        "fh3cuda_gemm_bf16w_dev": (c_int, [vp, i64, i64, vp, i64, vp, i64, i64, vp, vp, c_int, c_int, vp]),
         "fh3cuda_alloc_stats": (None, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
         "fh3cuda_attention_f32_dev": (c_int, [vp, i64, vp, i64, vp, i64, vp, i64, c_int, c_int, c_int, vp]),
         "fh3cuda_vsa_num_tiles": (c_int, [ctypes.POINTER(Fh3CudaSeq), c_int, ctypes.POINTER(c_int),

@@ -65,7 +65,17 @@ struct Params {
     void* y;
     int epi;
     int* status;
+    // programmatic dependent launch (gemm_bf16_pair_kernel): 0 off; 1 the kernel may start
+    // while the previous kernel on its stream runs, and waits for it (griddepcontrol.wait)
+    // before its first global access; 2 the same, except that the weight tiles of the
+    // first stages are loaded before that wait (the caller guarantees the weights)
+    int pdl = 0;
 };
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 struct Ring {
     int idx = 0;
@@ -181,18 +191,30 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* yr, const float* o)
     }
 }
 
-// Drain one 256-column accumulator (this thread's TMEM lane = one output row) and apply
-// the epilogue.  `nb` is the tile's column block (256 weight rows, or 128 SwiGLU features).
-__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tbase, int64_t m, int64_t nb) {
+// The accumulator row of this thread, 32 columns at a time, straight from TMEM.
+struct TmemAcc {
+    uint32_t tbase;
+    __device__ __forceinline__ void load(int col, uint32_t (&v)[32]) const {
+        fh3::tmem_ld32(tbase + col, v);
+        fh3::tmem_ld_wait();
+        fh3::tmem_regs_ready(v);
+    }
+    __device__ __forceinline__ void load2(int ca, int cb, uint32_t (&a)[32], uint32_t (&b)[32]) const {
+        fh3::tmem_ld32(tbase + ca, a);
+        fh3::tmem_ld32(tbase + cb, b);
+        fh3::tmem_ld_wait();
+        fh3::tmem_regs_ready(a);
+        fh3::tmem_regs_ready(b);
+    }
+};
+
+template <class Acc>
+__device__ __forceinline__ void epilogue_rows(const Params& p, const Acc& acc, int64_t m, int64_t nb) {
     const bool row_ok = m < p.M;
     if (p.epi == FH3CUDA_EPI_SWIGLU) {
         for (int cc = 0; cc < 4; ++cc) {
             uint32_t v[32], g[32];
-            fh3::tmem_ld32(tbase + cc * 32, v);
-            fh3::tmem_ld32(tbase + 128 + cc * 32, g);
-            fh3::tmem_ld_wait();
-            fh3::tmem_regs_ready(v);
-            fh3::tmem_regs_ready(g);
+            acc.load2(cc * 32, 128 + cc * 32, v, g);
             const int64_t f0 = nb * 128 + cc * 32;
             if (!row_ok || f0 >= p.n_out) continue;
             __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy;
@@ -218,9 +240,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tbase, i
     }
     for (int cc = 0; cc < 8; ++cc) {
         uint32_t v[32];
-        fh3::tmem_ld32(tbase + cc * 32, v);
-        fh3::tmem_ld_wait();
-        fh3::tmem_regs_ready(v);
+        acc.load(cc * 32, v);
         const int64_t n0 = nb * 256 + cc * 32;
         if (!row_ok || n0 >= p.N) continue;
         float o[32];
@@ -275,6 +295,12 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tbase, i
             }
         }
     }
+}
+
+// Drain one 256-column accumulator (this thread's TMEM lane = one output row) and apply
+// the epilogue.  `nb` is the tile's column block (256 weight rows, or 128 SwiGLU features).
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tbase, int64_t m, int64_t nb) {
+    epilogue_rows(p, TmemAcc{tbase}, m, nb);
 }
 
 // =============================================================================
@@ -748,8 +774,8 @@ constexpr int64_t kTwoPassRows = 2048;
 // super-blocks a warp are loaded before any is converted, to keep enough reads in
 // flight.  Loads are streaming (evict-first): the weights are read once, and L2 is kept
 // for the GEMM's tiles.
-constexpr int kExpandUnroll = 8;
-constexpr int kExpandThreads = 256;
+constexpr int kExpandUnroll = 4;
+constexpr int kExpandThreads = 128;
 
 __global__ void __launch_bounds__(kExpandThreads)
     dequant_q4k_bf16_kernel(const uint8_t* __restrict__ w, size_t rb, int64_t N, int K,
@@ -827,6 +853,10 @@ __global__ void __launch_bounds__(bfp::kThreads, 1)
     const int ksteps = static_cast<int>(p.K / BK);
     const int64_t pair = blockIdx.x >> 1;
     const int64_t npairs = gridDim.x >> 1;
+    // the next kernel on this stream may be scheduled now: it can only take the SMs this
+    // grid leaves as its CTAs finish, and it waits for the whole grid before it reads or
+    // writes activations (griddepcontrol.wait)
+    if (p.pdl) griddep_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -860,13 +890,39 @@ __global__ void __launch_bounds__(bfp::kThreads, 1)
             Ring r;
             uint32_t filled = 0, par = 0;
             bool ok = true;
+            int ks0 = 0;  // k-steps of the first tile already issued
+            if (p.pdl == 2 && pair < num_tiles) {
+                // weights of the first stages before the previous kernel has finished; the
+                // activations (that kernel's output) only after it
+                int64_t mb, nb;
+                tile_coords(pair, num_m, num_n, mb, nb);
+                const int m0 = static_cast<int>(mb * 256 + cr * 128);
+                const int wrow = swiglu ? static_cast<int>(cr ? p.n_out + nb * 128 : nb * 128)
+                                        : static_cast<int>(nb * BN + cr * 128);
+                ks0 = ksteps < S ? ksteps : S;  // fresh stages: their empty barriers pass at once
+                for (int ks = 0; ks < ks0; ++ks) {
+                    if (leader) fh3::mbar_arrive_expect_tx(&full[ks], 2 * STAGE);
+                    const uint32_t bar = fh3::mapa_shared(fh3::smem_u32(&full[ks]), 0);
+                    fh3::tma_load_2d_pair(smem + ks * STAGE + A_BYTES, &tmB, bar, ks * BK, wrow);
+                }
+                griddep_wait();
+                for (int ks = 0; ks < ks0; ++ks) {
+                    const uint32_t bar = fh3::mapa_shared(fh3::smem_u32(&full[ks]), 0);
+                    fh3::tma_load_2d_pair(smem + ks * STAGE, &tmA, bar, ks * BK, m0);
+                    filled |= 1u << r.idx;
+                    par = (par & ~(1u << r.idx)) | (r.phase << r.idx);
+                    r.next<S>();
+                }
+            } else if (p.pdl) {
+                griddep_wait();
+            }
             for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
                 int64_t mb, nb;
                 tile_coords(tile, num_m, num_n, mb, nb);
                 const int m0 = static_cast<int>(mb * 256 + cr * 128);
                 const int wrow = swiglu ? static_cast<int>(cr ? p.n_out + nb * 128 : nb * 128)
                                         : static_cast<int>(nb * BN + cr * 128);
-                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                for (int ks = ks0; ks < ksteps && ok; ++ks) {
                     if (!(ok = fh3::mbar_wait(&empty[r.idx], r.phase ^ 1u, abort_flag, p.status))) break;
                     // both CTAs' A and B bytes are counted on the leader's full barrier
                     if (leader) fh3::mbar_arrive_expect_tx(&full[r.idx], 2 * STAGE);
@@ -878,6 +934,7 @@ __global__ void __launch_bounds__(bfp::kThreads, 1)
                     par = (par & ~(1u << r.idx)) | (r.phase << r.idx);
                     r.next<S>();
                 }
+                ks0 = 0;
             }
             if (!ok) {
                 volatile int no_abort = 0;
@@ -918,6 +975,7 @@ __global__ void __launch_bounds__(bfp::kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
+        if (p.pdl) griddep_wait();  // y, bias and gate belong to us only once the previous kernel is done
         const int q = warp & 3;
         const uint32_t acc_empty_leader = fh3::mapa_shared(fh3::smem_u32(acc_empty), 0);
         Ring racc;
@@ -1044,18 +1102,23 @@ Params make_params(int64_t n_tok, int64_t N, int64_t K, int64_t ldy, const float
     return p;
 }
 
-cudaLaunchConfig_t pair_config(cudaLaunchAttribute* at, int64_t pairs, int threads, int smem, cudaStream_t s) {
+// `at` holds two attributes: the pair cluster, and programmatic stream serialisation
+// when `pdl` (the kernel may be scheduled while the previous kernel on s still runs)
+cudaLaunchConfig_t pair_config(cudaLaunchAttribute* at, int64_t pairs, int threads, int smem, cudaStream_t s,
+                               bool pdl = false) {
     cudaLaunchConfig_t cfg = {};
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 2;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
     cfg.blockDim = dim3(threads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 2 : 1;
     return cfg;
 }
 
@@ -1077,8 +1140,12 @@ int launch_bf16_pair(const CUtensorMap& tmA, const __nv_bfloat16* wb, const Para
     if (r != CUDA_SUCCESS) return set_error(FH3CUDA_E_CUDA, "cuTensorMapEncodeTiled(B) failed: %d", (int)r);
     const int64_t tiles = gemm_tiles(p, 256);
     const int64_t pairs = tiles < g_bf_clusters ? tiles : g_bf_clusters;
-    cudaLaunchAttribute at[1];
-    cudaLaunchConfig_t cfg = pair_config(at, pairs, bfp::kThreads, bfp::SMEM_BYTES, s);
+    // FH3CUDA_GEMM_PDL=0 launches without the programmatic dependency (the kernel then waits
+    // for the previous kernel before it starts, and its griddepcontrol instructions do nothing)
+    const char* pdl_env = getenv("FH3CUDA_GEMM_PDL");
+    const bool pdl_on = !(pdl_env && strcmp(pdl_env, "0") == 0);
+    cudaLaunchAttribute at[2];
+    cudaLaunchConfig_t cfg = pair_config(at, pairs, bfp::kThreads, bfp::SMEM_BYTES, s, pdl_on && p.pdl != 0);
     return check_cuda(cudaLaunchKernelEx(&cfg, gemm_bf16_pair_kernel, tmA, tmB, p), "gemm_bf16_pair_kernel launch");
 }
 
@@ -1150,12 +1217,14 @@ int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_
         auto* wb = static_cast<__nv_bfloat16*>(scratch(c, 11, static_cast<size_t>(w->out) * w->in * 2, s));
         if (!wb) return FH3_E_NOMEM;
         if ((rc = launch_expand(c, w, wb, s))) return rc;
-        return launch_bf16_pair(tmA, wb, p, s);
+        Params pp = p;
+        pp.pdl = 1;  // the GEMM's prologue overlaps the expansion; every load waits for it
+        return launch_bf16_pair(tmA, wb, pp, s);
     }
     if (pair) {
         const int64_t tiles = gemm_tiles(p, 256);
         const int64_t pairs = tiles < g_pair_clusters ? tiles : g_pair_clusters;
-        cudaLaunchAttribute at[1];
+        cudaLaunchAttribute at[2];
         cudaLaunchConfig_t cfg = pair_config(at, pairs, kThreadsPair, two::SMEM_BYTES, s);
         return check_cuda(cudaLaunchKernelEx(&cfg, gemm_q4k_pair_kernel, tmA, tmW, p), "gemm_q4k_pair_kernel launch");
     }
@@ -1189,7 +1258,7 @@ extern "C" int fh3cuda_q4k_to_bf16_dev(const Fh3CudaW* w, void* w_bf16, void* st
 
 extern "C" int fh3cuda_gemm_bf16w_dev(const void* w_bf16, int64_t out, int64_t in, const void* x_bf16, int64_t ldx,
                                       void* y, int64_t ldy, int64_t n_tok, const float* bias, const float* gate,
-                                      int epi, void* stream) {
+                                      int epi, int flags, void* stream) {
     using namespace fh3host;
     const char* who = "fh3cuda_gemm_bf16w_dev";
     DevCtx* c = ctx();
@@ -1203,6 +1272,7 @@ extern "C" int fh3cuda_gemm_bf16w_dev(const void* w_bf16, int64_t out, int64_t i
     if (g_bf_clusters <= 0) return set_error(FH3CUDA_E_CUDA, "%s: the pair kernel cannot be resident", who);
     CUtensorMap tmA;
     if ((rc = map_activations(&tmA, x_bf16, ldx, n_tok, in))) return rc;
-    const Params p = make_params(n_tok, out, in, ldy, bias, gate, y, epi, ctx_status(c));
+    Params p = make_params(n_tok, out, in, ldy, bias, gate, y, epi, ctx_status(c));
+    p.pdl = (flags & FH3CUDA_GEMM_WEIGHTS_READY) ? 2 : 1;
     return launch_bf16_pair(tmA, static_cast<const __nv_bfloat16*>(w_bf16), p, static_cast<cudaStream_t>(stream));
 }

@@ -197,8 +197,10 @@ class Runner:
         w, x, ldx, rows, y, ldy, epi, gate = op[1:9]
         self.stream.wait_event(self.ev_exp[slot])
         e1 = self._timed("gemm_events", self.stream, 2 * rows * w.in_ * w.out, f"bf16w:{rows}")
+        # the weights were expanded on the side stream and waited for: ready before the previous kernel
         check(self.L.fh3cuda_gemm_bf16w_dev(self.wbuf[slot].data_ptr(), w.out, w.in_, x, ldx, y, ldy, rows, None,
-                                            None if gate is None else gate.data_ptr(), epi, self.s))
+                                            None if gate is None else gate.data_ptr(), epi, _lib.GEMM_WEIGHTS_READY,
+                                            self.s))
         if e1 is not None:
             e1.record(self.stream)
         self.ev_use[slot].record(self.stream)
@@ -236,7 +238,13 @@ class Runner:
         ]
 
     def _two_pass(self, op) -> bool:
-        return self.overlap and op[0] == "gemm" and self.L.fh3cuda_gemm_launches(op[4]) == 2
+        """Expanded-weight GEMM: every projection of the two-pass row range, and with the
+        overlap also the 512-row text K/V projection (its expansion is hidden, and the bf16
+        kernel runs its 80 tiles without dequantiser warps)."""
+        return self.overlap and op[0] == "gemm" and (op[4] >= self.EXPAND_ROWS or
+                                                      self.L.fh3cuda_gemm_launches(op[4]) == 2)
+
+    EXPAND_ROWS = 256
 
     def run(self, ops: list, tap=None) -> None:
         """Issue `ops` in order; two-pass GEMMs get their expansions one projection ahead.

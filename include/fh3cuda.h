@@ -230,12 +230,19 @@ FH3CUDA_API int fh3cuda_gemm_q4k_dev(const Fh3CudaW *w, const void *x_bf16, int6
  * out * in elements, 16-byte aligned.  fh3cuda_gemm_bf16w_dev is
  * fh3cuda_gemm_q4k_dev's GEMM on such a bf16 [out][in] weight matrix (in a multiple of
  * 64): same epilogues, same results as the Q4_K entry point on the matrix it expands
- * to.  Together they replace fh3_matmul's large-M regime (src/core/fh3_ops.c:317-404). */
+ * to.  Together they replace fh3_matmul's large-M regime (src/core/fh3_ops.c:317-404).
+ * The GEMM is launched as a programmatic dependent of the previous kernel on `stream`
+ * (its set-up overlaps that kernel's end; it reads and writes activations only after
+ * that kernel has finished).  flags: FH3CUDA_GEMM_WEIGHTS_READY when w_bf16 was
+ * complete before the previous kernel on `stream` began (written on another stream
+ * and waited for with an event, or earlier on this stream): the GEMM may then load
+ * its first weight tiles while that kernel still runs; 0 otherwise. */
+#define FH3CUDA_GEMM_WEIGHTS_READY 1
 FH3CUDA_API int fh3cuda_q4k_to_bf16_dev(const Fh3CudaW *w, void *w_bf16, void *stream);
 FH3CUDA_API int fh3cuda_gemm_bf16w_dev(const void *w_bf16, int64_t out, int64_t in, const void *x_bf16,
                                        int64_t ldx, void *y, int64_t ldy, int64_t n_tok,
                                        const float *bias_or_null, const float *gate, int epilogue,
-                                       void *stream);
+                                       int flags, void *stream);
 
 /* Kernel launches one fh3cuda_gemm_q4k_dev call of n_tok rows makes: 1 for the
  * fused kernels, 2 from 2048 rows on, where the weights are first expanded to a
