@@ -61,6 +61,59 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_modulate_kernel(
     }
 }
 
+// The same for rows of 4*kNormThreads*V' elements at most (dim a multiple of 4, 16-byte
+// aligned rows): each thread keeps its V float4 of the row in registers, so the row is
+// read from HBM once, and every access is 16 bytes (8 bytes for the bf16 output).  The
+// sum of squares runs in a fixed order (per thread, then the same shuffle tree and warp
+// sums as above), so a row's output does not depend on the others.
+template <int V>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_modulate_vec_kernel(
+    const float4* __restrict__ x, const float4* __restrict__ nw, const float4* __restrict__ shift,
+    const float4* __restrict__ scale, uint2* __restrict__ y, int dim4, float inv_dim, float eps) {
+    __shared__ float red[kNormThreads / 32];
+    const float4* row = x + static_cast<int64_t>(blockIdx.x) * dim4;
+    uint2* out = y + static_cast<int64_t>(blockIdx.x) * dim4;
+    float4 v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int k = threadIdx.x + i * kNormThreads;
+        v[i] = k < dim4 ? row[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        ss = fmaf(v[i].x, v[i].x, ss);
+        ss = fmaf(v[i].y, v[i].y, ss);
+        ss = fmaf(v[i].z, v[i].z, ss);
+        ss = fmaf(v[i].w, v[i].w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; ++w) tot += red[w];
+    const float inv = 1.0f / sqrtf(tot * inv_dim + eps);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int k = threadIdx.x + i * kNormThreads;
+        if (k >= dim4) break;
+        float4 a = make_float4(v[i].x * inv, v[i].y * inv, v[i].z * inv, v[i].w * inv);
+        if (nw) {
+            const float4 w = __ldg(nw + k);
+            a = make_float4(a.x * w.x, a.y * w.y, a.z * w.z, a.w * w.w);
+        }
+        const float4 sc = __ldg(scale + k), sh = __ldg(shift + k);
+        __nv_bfloat162 lo = __floats2bfloat162_rn(fmaf(a.x, 1.0f + sc.x, sh.x), fmaf(a.y, 1.0f + sc.y, sh.y));
+        __nv_bfloat162 hi = __floats2bfloat162_rn(fmaf(a.z, 1.0f + sc.z, sh.z), fmaf(a.w, 1.0f + sc.w, sh.w));
+        uint2 o;
+        o.x = *reinterpret_cast<uint32_t*>(&lo);
+        o.y = *reinterpret_cast<uint32_t*>(&hi);
+        out[k] = o;
+    }
+}
+
 __global__ void swiglu_kernel(const float* __restrict__ in, float* __restrict__ out, int64_t n, int F) {
     const int64_t total = n * F;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -376,8 +429,24 @@ extern "C" int fh3cuda_rmsnorm_modulate_dev(const float* x, const float* norm_w,
     if (!ctx()) return set_error(FH3CUDA_E_NODEV, "fh3cuda_rmsnorm_modulate_dev: call fh3cuda_init first");
     if (!x || !shift || !scale || !y_bf16 || n <= 0 || dim <= 0)
         return set_error(FH3_E_INVALID, "fh3cuda_rmsnorm_modulate_dev: bad arguments");
-    rmsnorm_modulate_kernel<<<n, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        x, norm_w, shift, scale, static_cast<__nv_bfloat16*>(y_bf16), dim, eps);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool vec = (dim % 4) == 0 && al16(x) && al16(shift) && al16(scale) && (!norm_w || al16(norm_w)) &&
+                     (reinterpret_cast<uintptr_t>(y_bf16) & 7) == 0;
+    const int dim4 = dim / 4;
+    const float inv_dim = 1.0f / static_cast<float>(dim);
+#define FH3_NORM_VEC(V)                                                                                         \
+    rmsnorm_modulate_vec_kernel<V><<<n, kNormThreads, 0, s>>>(                                                  \
+        reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(norm_w),                           \
+        reinterpret_cast<const float4*>(shift), reinterpret_cast<const float4*>(scale), static_cast<uint2*>(y_bf16), \
+        dim4, inv_dim, eps)
+    if (vec && dim4 <= 2 * kNormThreads) FH3_NORM_VEC(2);
+    else if (vec && dim4 <= 5 * kNormThreads) FH3_NORM_VEC(5);
+    else if (vec && dim4 <= 8 * kNormThreads) FH3_NORM_VEC(8);
+    else
+        rmsnorm_modulate_kernel<<<n, kNormThreads, 0, s>>>(x, norm_w, shift, scale,
+                                                           static_cast<__nv_bfloat16*>(y_bf16), dim, eps);
+#undef FH3_NORM_VEC
     return check_cuda(cudaGetLastError(), "rmsnorm_modulate launch");
 }
 

@@ -30,6 +30,24 @@ def test_rmsnorm_modulate_vs_oracle(fh3, oracle):
     assert np.abs(got.float().cpu().numpy() - ref).max() <= np.abs(ref).max() * 2 ** -8
 
 
+@pytest.mark.parametrize("n,dim", [(5, 512), (4, 1000), (3, 8192), (3, 10000), (4, 5121), (300, 5120)])
+def test_rmsnorm_modulate_every_row_width(fh3, oracle, n, dim):
+    """Both kernels: rows of up to 8 x 1024 float4 held in registers (one HBM read), and the
+    general one (widths not a multiple of 4, or wider)."""
+    import torch
+    x = oracle.rng_normal(2, 1, n * dim).reshape(n, dim) * 3.0
+    nw = oracle.rng_normal(2, 2, dim)
+    sh = 0.1 * oracle.rng_normal(2, 3, dim)
+    sc = 0.1 * oracle.rng_normal(2, 4, dim)
+    for w in (nw, None):
+        r = oracle.rmsnorm(x, w if w is not None else np.ones(dim, np.float32), 1e-6)
+        ref = oracle.modulate(r, np.tile(sh, (n, 1)), np.tile(sc, (n, 1)))
+        got = fh3.rmsnorm_modulate(torch.from_numpy(x).cuda(), torch.from_numpy(sh).cuda(),
+                                   torch.from_numpy(sc).cuda(), norm_w=None if w is None else torch.from_numpy(w).cuda(),
+                                   eps=1e-6).float().cpu().numpy()
+        assert np.abs(got - ref).max() <= np.abs(ref).max() * 2 ** -8, (n, dim)
+
+
 def test_swiglu_vs_reference_golden(fh3, golden_cases):
     import torch
     h = golden_cases["swiglu/h"]
