@@ -392,9 +392,11 @@ def run_ours(args):
                          f"weights as the GPU"}
 
     peaks, src = load_peaks()
-    gemv = qk = attn = vsa = None
+    gemv = qk = attn = vsa = configs = None
     if rank == 0 and not args.no_gemv:
         hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        configs = measure_configs(fh3, torch, trunk, text_bf,
+                                  float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])), src, cpu_threads)
         gemv = measure_gemv(fh3, torch, hbm, src, cpu_threads=cpu_threads)
         qk = measure_qk_norm_rope(fh3, torch, m_loc, hbm, src)
         attn = measure_attention(fh3, torch, m_loc, float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])),
@@ -443,7 +445,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(float(mx[3])), "clocks": clk, "device_status": status, "parity": parity,
-            "gemv": gemv, "qk_norm_rope": qk, "attention": attn, "vsa_attention": vsa,
+            "configs": configs, "gemv": gemv, "qk_norm_rope": qk, "attention": attn, "vsa_attention": vsa,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -568,6 +570,99 @@ def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100, cpu
             out["shapes"].append(entry)
         del ws
         torch.cuda.synchronize()
+    return out
+
+
+def measure_configs(fh3, torch, trunk, text_bf, peak: float, peak_src: str, cpu_threads) -> dict:
+    """BASELINE configs 1, 3 and 4 on one GPU, each through the path the library takes for it,
+    with weights rotated across the trunk's blocks (more than L2 between repeats):
+      1: fh3_matmul drop-in semantics on device buffers (fh3cuda_matmul_dev), W 5120x5120 Q4_K,
+         x [256][5120] fp32 -> y fp32 (13.42 GFLOP);
+      3: the SwiGLU FFN at M = 4096: x -> bf16, fc1 with the SwiGLU epilogue, fc2 (1.739 TFLOP);
+      4: one block's projection set at M = 16384 latent rows + 512 text rows for cross K/V, through
+         the trunk runner (prologues, epilogues, overlapped expansion; 12.06 TFLOP).
+    The reference's fh3_matmul is timed beside config 1 in full and beside configs 3 and 4 on a row
+    sample (rows are independent; the FLOPs scale with the rows), when cpu_threads is given."""
+    from fasth3inc_b200.trunk import D_MODEL, FFN, Runner, Workspace, block_flops
+    out = {"unit": "TFLOP/s", "peak": peak, "peak_source": f"{peak_src} bf16_tflops", "cpu_threads": cpu_threads}
+    blocks = trunk.blocks
+    nb = len(blocks)
+
+    def timed(fn, reps):
+        fn(0)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i + 1)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def cpu_rate(pairs):
+        """GFLOP/s of the reference's fh3_matmul over [(raw, in, out, x)]"""
+        import numpy as np
+        from oracle import oracle as orc
+        impl = orc.Reference() if orc.Reference.available() else orc.Oracle()
+        flops, t0 = 0, time.perf_counter()
+        for raw, inn, o, x in pairs:
+            impl.matmul(12, raw, inn, o, x)
+            flops += 2 * x.shape[0] * inn * o
+        return flops / (time.perf_counter() - t0) / 1e9, ("reference" if orc.Reference.available() else "port")
+
+    # config 1
+    x1 = torch.randn((256, D_MODEL), device="cuda")
+    y1 = torch.empty((256, D_MODEL), device="cuda")
+    ms = timed(lambda i: fh3.matmul(blocks[i % nb].w["o"], x1, out=y1), 20)
+    f1 = 2 * 256 * D_MODEL * D_MODEL
+    c1 = {"workload": "W 5120x5120 Q4_K, x [256][5120] fp32, y = x W^T (fh3cuda_matmul_dev)", "ms": round(ms, 4),
+          "achieved": round(f1 / ms / 1e9, 1), "frac": round(f1 / ms / 1e9 / peak, 4)}
+    # config 3
+    M3 = 4096
+    x3 = torch.randn((M3, D_MODEL), device="cuda")
+    xb = torch.empty((M3, D_MODEL), dtype=torch.bfloat16, device="cuda")
+    g3 = torch.empty((M3, FFN), dtype=torch.bfloat16, device="cuda")
+    y3 = torch.empty((M3, D_MODEL), device="cuda")
+
+    def ffn(i):
+        b = blocks[i % nb]
+        fh3.to_bf16(x3, out=xb)
+        fh3.gemm(b.w["fc1"], xb, fh3.EPI_SWIGLU, out=g3)
+        fh3.gemm(b.w["fc2"], g3, fh3.EPI_F32, out=y3)
+    ms = timed(ffn, 5)
+    f3 = 3 * 2 * M3 * D_MODEL * FFN
+    c3 = {"workload": "SwiGLU FFN, x [4096][5120] fp32: fc1 [up; gate] 27648x5120 with the SwiGLU epilogue, "
+                      "fc2 5120x13824", "ms": round(ms, 3), "achieved": round(f3 / ms / 1e9, 1),
+          "frac": round(f3 / ms / 1e9 / peak, 4)}
+    del xb, g3, y3
+    # config 4
+    M4, T4 = 16384, text_bf.shape[0]
+    ws = Workspace(M4, T4)
+    h4 = torch.randn((M4, D_MODEL), device="cuda")
+    runner = Runner(trunk, ws)
+    ms = timed(lambda i: runner.block(blocks[i % nb], h4, text_bf), 5)
+    f4 = block_flops(M4, T4)
+    c4 = {"workload": "one block's projection set: QKV/O self-attention and Q/O cross-attention on 16384 latent "
+                      "rows, cross K/V on 512 text rows, SwiGLU FFN 13824, AdaLN rmsnorm+modulate prologues",
+          "ms": round(ms, 3), "achieved": round(f4 / ms / 1e9, 1), "frac": round(f4 / ms / 1e9 / peak, 4)}
+    del ws, h4
+    torch.cuda.synchronize()
+    if cpu_threads:
+        import numpy as np
+        rng = np.random.default_rng(3)
+        b0 = {k: w.data.cpu().numpy() for k, w in blocks[0].w.items()}
+        r, kind = cpu_rate([(b0["o"], D_MODEL, D_MODEL, rng.standard_normal((256, D_MODEL), dtype=np.float32))])
+        c1.update({"cpu_ms": round(2 * 256 * D_MODEL * D_MODEL / r / 1e6, 2), "cpu_kind": kind,
+                   "cpu_sample": "the full config"})
+        s3 = 256
+        xs = rng.standard_normal((s3, D_MODEL), dtype=np.float32)
+        gs = rng.standard_normal((s3, FFN), dtype=np.float32)
+        r, kind = cpu_rate([(b0["fc1"], D_MODEL, 2 * FFN, xs), (b0["fc2"], FFN, D_MODEL, gs)])
+        c3.update({"cpu_ms": round(f3 / r / 1e6, 1), "cpu_kind": kind,
+                   "cpu_sample": f"fc1 and fc2 on {s3} rows, scaled to 4096 rows"})
+        c4.update({"cpu_ms": round(f4 / r / 1e6, 1), "cpu_kind": kind,
+                   "cpu_sample": f"the config-3 sample's rate ({s3} rows of fc1 and fc2), scaled to the config's FLOPs"})
+    out.update({"config1_gemm_m256": c1, "config3_swiglu_ffn_m4096": c3, "config4_block_m16384": c4})
     return out
 
 

@@ -13,8 +13,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libfh3cuda.so")
 SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemv_tc.cu", "gemm.cu", "ops.cu", "attention.cu", "attention_tc.cu", "attention_f32.cu",
-           "vsa.cu", "vsa_tc.cu", "trunk_io.cu", "dit.cu", "gen.cu", "noalloc.cu"]
-HEADERS = ["common.cuh", "flash.cuh"]
+           "vsa.cu", "vsa_tc.cu", "trunk_io.cu", "dit.cu", "gen.cu", "noalloc.cu", "formats.cu"]
+HEADERS = ["common.cuh", "flash.cuh", "formats.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -47,7 +47,6 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         return LIB
     cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), "-I", os.path.join(ROOT, "include"), "-o", LIB + ".tmp"]
     cmd += [os.path.join(CSRC, f) for f in SOURCES]
-    cmd += ["-lcublas"]  # plain fp32 GEMMs of the non-Q4_K weight formats
     if verbose:
         print(" ".join(cmd))
     out = subprocess.run(cmd, capture_output=True, text=True)

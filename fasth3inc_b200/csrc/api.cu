@@ -8,19 +8,18 @@
 #include <mutex>
 #include <vector>
 
-#include <cublas_v2.h>
-
 #include "common.cuh"
 
 namespace fh3host {
 
 // scratch slots: 0 bf16 activations of the GEMM, 1 staged weights, 2-4 the host
 // drop-in's x / y / bias, 5 GEMV fragments, 6 split-tile partials, 7 tile counters,
-// 8 fp32 weight rows of the non-Q4_K formats, 9 video sparse attention's tile data,
+// 8 split-bf16 weight rows of the non-Q4_K formats, 9 video sparse attention's tile data,
 // 10 the DiT forward's activations, 11 bf16 weights of the two-pass large-M GEMM,
 // 12 the transposed V of the tensor-core attention, 13 video sparse attention's tile-order
-// copies of q, k and v, 14 / 15 the tcgen05 GEMV's split-tile partials and counters
-constexpr int kScratchSlots = 16;
+// copies of q, k and v, 14 / 15 the tcgen05 GEMV's split-tile partials and counters,
+// 16 the unit gate that adds the K slices of the non-Q4_K formats' GEMM
+constexpr int kScratchSlots = 17;
 
 struct DevCtx {
     int device = -1;
@@ -29,7 +28,6 @@ struct DevCtx {
     cudaStream_t stream = nullptr; // the drop-in's stream
     void* scratch_ptr[kScratchSlots] = {};
     size_t scratch_size[kScratchSlots] = {};
-    cublasHandle_t blas = nullptr; // fp32 GEMMs of the non-Q4_K formats (created on first use)
 };
 
 namespace {
@@ -265,82 +263,6 @@ extern "C" size_t fh3cuda_row_bytes(int type, int64_t n) {
     }
 }
 
-namespace fh3fmt {
-
-__global__ void add_bias_kernel(float* __restrict__ y, const float* __restrict__ bias, int64_t n_tok, int64_t out) {
-    const int64_t total = n_tok * out;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        y[i] = __fadd_rn(y[i], bias[i % out]);
-}
-
-// fh3_matmul (src/core/fh3_ops.c:317-404) for the formats other than Q4_K (the text
-// encoder's Q5_K / Q6_K, the F16 globals, ...): rows of W are expanded bit-exactly to
-// fp32 (fh3cuda_dequant_dev) in chunks of at most 256 MB of scratch, and each chunk
-// is multiplied by a plain fp32 cuBLAS GEMM (no TF32) into its columns of y; the
-// bias is added afterwards, as the reference adds it to the finished dot product.
-int matmul_other(DevCtx* c, const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias,
-                 cudaStream_t s) {
-    const int64_t K = w->in, N = w->out;
-    int be = 1;
-    switch (w->type) {
-        case FH3CUDA_TYPE_F32: case FH3CUDA_TYPE_F16: case FH3CUDA_TYPE_BF16: be = 1; break;
-        case FH3CUDA_TYPE_Q8_0: be = 32; break;
-        case FH3CUDA_TYPE_Q2_K: case FH3CUDA_TYPE_Q3_K: case FH3CUDA_TYPE_Q5_K: case FH3CUDA_TYPE_Q6_K: be = 256; break;
-        default:
-            return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: weight type %d is not a format fh3_dequant expands",
-                             w->type);
-    }
-    if (K % be)
-        return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: in = %lld is not a multiple of the %d-weight block",
-                         static_cast<long long>(K), be);
-    if (!c->blas) {
-        if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) {
-            c->blas = nullptr;
-            return set_error(FH3CUDA_E_CUDA, "fh3cuda_matmul_dev: cublasCreate failed");
-        }
-        cublasSetMathMode(c->blas, CUBLAS_DEFAULT_MATH);
-    }
-    if (cublasSetStream(c->blas, s) != CUBLAS_STATUS_SUCCESS)
-        return set_error(FH3CUDA_E_CUDA, "fh3cuda_matmul_dev: cublasSetStream failed");
-    const size_t rb = fh3cuda_row_bytes(w->type, K);
-    int64_t chunk = N;
-    float* wf = nullptr;
-    if (w->type != FH3CUDA_TYPE_F32) {
-        const int64_t cap_rows = (int64_t(256) << 20) / (K * 4);
-        chunk = cap_rows < 1 ? 1 : (cap_rows < N ? cap_rows : N);
-        wf = static_cast<float*>(scratch(c, 8, static_cast<size_t>(chunk) * K * 4, s));
-        if (!wf) return FH3_E_NOMEM;
-    }
-    const float one = 1.0f, zero = 0.0f;
-    for (int64_t o0 = 0; o0 < N; o0 += chunk) {
-        const int64_t rows = (o0 + chunk <= N) ? chunk : N - o0;
-        const float* wrows;
-        if (w->type == FH3CUDA_TYPE_F32) {
-            wrows = reinterpret_cast<const float*>(w->data + o0 * rb);
-        } else {
-            const int rc = fh3cuda_dequant_dev(w->type, w->data + o0 * rb, wf, rows, K, s);
-            if (rc != FH3_OK) return rc;
-            wrows = wf;
-        }
-        // column-major view: y^T[N x M] (ld N) = W[rows x K]^T-view x^T[K x M]
-        const cublasStatus_t st = cublasSgemm(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(rows), n_tok,
-                                              static_cast<int>(K), &one, wrows, static_cast<int>(K), x,
-                                              static_cast<int>(K), &zero, y + o0, static_cast<int>(N));
-        if (st != CUBLAS_STATUS_SUCCESS)
-            return set_error(FH3CUDA_E_CUDA, "fh3cuda_matmul_dev: cublasSgemm failed (%d)", static_cast<int>(st));
-    }
-    if (bias) {
-        const int64_t total = static_cast<int64_t>(n_tok) * N;
-        int64_t grid = (total + 255) / 256;
-        if (grid > static_cast<int64_t>(c->sms) * 16) grid = static_cast<int64_t>(c->sms) * 16;
-        add_bias_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(y, bias, n_tok, N);
-        return check_cuda(cudaGetLastError(), "add_bias launch");
-    }
-    return FH3_OK;
-}
-
-}  // namespace fh3fmt
 
 extern "C" int fh3cuda_matmul_dev(const Fh3CudaW* w, const float* x, float* y, int n_tok,
                                   const float* bias, void* stream) {
@@ -349,7 +271,7 @@ extern "C" int fh3cuda_matmul_dev(const Fh3CudaW* w, const float* x, float* y, i
     if (!w || !x || !y || !w->data || n_tok <= 0 || w->in <= 0 || w->out <= 0)
         return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: bad arguments");
     if (w->type != FH3CUDA_TYPE_Q4_K)
-        return fh3fmt::matmul_other(c, w, x, y, n_tok, bias, static_cast<cudaStream_t>(stream));
+        return matmul_formats(c, w, x, y, n_tok, bias, static_cast<cudaStream_t>(stream));
     if ((w->in % fh3::kQ4KBlock) != 0)
         return set_error(FH3_E_INVALID, "fh3cuda_matmul_dev: Q4_K weights need in %% 256 == 0");
     if (n_tok <= 16) return fh3cuda_gemv_q4k_dev(w, x, y, n_tok, bias, stream);

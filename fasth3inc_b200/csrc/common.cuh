@@ -526,6 +526,13 @@ int gemv_args_ok(const Fh3CudaW* w, const float* x, const float* y, int n_tok, c
 // which is the one GEMM path that needs scratch (its bf16 weight copy)
 int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_t ldy, int64_t n_tok,
              const float* bias, const float* gate, int epi, void* stream, bool fused_only);
+// fh3cuda_gemm_bf16w_dev with a weight row stride (ldw elements, >= in, a multiple of 8)
+int gemm_bf16w(const void* w_bf16, int64_t ldw, int64_t out, int64_t in, const void* x_bf16, int64_t ldx, void* y,
+               int64_t ldy, int64_t n_tok, const float* bias, const float* gate, int epi, int flags, cudaStream_t s);
+// fh3_matmul for the formats other than Q4_K (formats.cu): arguments checked by the caller
+// except the format and block rules
+int matmul_formats(DevCtx* c, const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias,
+                   cudaStream_t s);
 // cudaMalloc that the library counts (fh3cuda_alloc_stats) and that honours the scratch
 // limit when `limited` (FH3_E_NOMEM with the message set on failure or refusal)
 int dev_alloc(void** p, size_t bytes, bool limited, const char* who);

@@ -229,7 +229,7 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, const Acc& acc, i
                 }
                 o[j] = vv * silu_ref(gg);
             }
-            if (f0 + 32 <= p.n_out && (p.ldy & 7) == 0) {
+            if (f0 + 32 <= p.n_out && (reinterpret_cast<uintptr_t>(yr + f0) & 15) == 0) {
                 store_bf16x32(yr + f0, o);
             } else {
                 for (int j = 0; j < 32; ++j)
@@ -252,7 +252,7 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, const Acc& acc, i
         const bool full = n0 + 32 <= p.N;
         if (p.epi == FH3CUDA_EPI_BF16) {
             __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n0;
-            if (full && (p.ldy & 7) == 0) {
+            if (full && (reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
                 store_bf16x32(yr, o);
             } else {
                 for (int j = 0; j < 32; ++j)
@@ -261,7 +261,7 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, const Acc& acc, i
         } else {
             float* yr = static_cast<float*>(p.y) + m * p.ldy + n0;
             if (p.epi == FH3CUDA_EPI_RESID) {
-                if (full && (p.ldy & 3) == 0) {
+                if (full && ((reinterpret_cast<uintptr_t>(yr) | reinterpret_cast<uintptr_t>(p.gate + n0)) & 15) == 0) {
                     // issue all 16 loads before the first store: y and gate may not
                     // alias in a valid call, and batching them hides the latency
                     const float4* g4 = reinterpret_cast<const float4*>(p.gate + n0);
@@ -285,7 +285,7 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, const Acc& acc, i
                     for (int j = 0; j < 32; ++j)
                         if (n0 + j < p.N) yr[j] = fmaf(p.gate[n0 + j], o[j], yr[j]);
                 }
-            } else if (full && (p.ldy & 3) == 0) {
+            } else if (full && (reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
                     *reinterpret_cast<float4*>(yr + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
@@ -1128,11 +1128,13 @@ int64_t gemm_tiles(const Params& p, int64_t rows_per_tile) {
 }
 
 // gemm_bf16_pair_kernel on a bf16 [N][K] weight matrix (K a multiple of 64, 16-byte aligned)
-int launch_bf16_pair(const CUtensorMap& tmA, const __nv_bfloat16* wb, const Params& p, cudaStream_t s) {
+// (ldw: elements between weight rows, >= K; 0 means K)
+int launch_bf16_pair(const CUtensorMap& tmA, const __nv_bfloat16* wb, const Params& p, cudaStream_t s,
+                     int64_t ldw = 0) {
     using namespace fh3host;
     CUtensorMap tmB;
     const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.K), static_cast<cuuint64_t>(p.N)};
-    const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(p.K) * 2};
+    const cuuint64_t gstr[1] = {static_cast<cuuint64_t>(ldw > 0 ? ldw : p.K) * 2};
     const cuuint32_t box[2] = {BK, 128};
     const cuuint32_t es[2] = {1, 1};
     CUresult r = encode_tiled(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(wb), gdim, gstr,
@@ -1256,23 +1258,32 @@ extern "C" int fh3cuda_q4k_to_bf16_dev(const Fh3CudaW* w, void* w_bf16, void* st
     return launch_expand(c, w, static_cast<__nv_bfloat16*>(w_bf16), static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int fh3cuda_gemm_bf16w_dev(const void* w_bf16, int64_t out, int64_t in, const void* x_bf16, int64_t ldx,
-                                      void* y, int64_t ldy, int64_t n_tok, const float* bias, const float* gate,
-                                      int epi, int flags, void* stream) {
-    using namespace fh3host;
+namespace fh3host {
+
+int gemm_bf16w(const void* w_bf16, int64_t ldw, int64_t out, int64_t in, const void* x_bf16, int64_t ldx, void* y,
+               int64_t ldy, int64_t n_tok, const float* bias, const float* gate, int epi, int flags, cudaStream_t s) {
     const char* who = "fh3cuda_gemm_bf16w_dev";
     DevCtx* c = ctx();
     if (!c) return set_error(FH3CUDA_E_NODEV, "%s: call fh3cuda_init first", who);
     if (!w_bf16) return set_error(FH3_E_INVALID, "%s: bad arguments", who);
     int rc = check_gemm_args(who, x_bf16, ldx, y, ldy, n_tok, out, in, gate, epi);
     if (rc) return rc;
-    if ((in % BK) != 0 || (reinterpret_cast<uintptr_t>(w_bf16) & 15))
-        return set_error(FH3_E_INVALID, "%s: in must be a multiple of 64 and the weights 16-byte aligned", who);
+    if ((in % BK) != 0 || (reinterpret_cast<uintptr_t>(w_bf16) & 15) || ldw < in || (ldw % 8) != 0)
+        return set_error(FH3_E_INVALID, "%s: in must be a multiple of 64, the weight rows 16-byte aligned", who);
     if ((rc = gemm_setup())) return rc;
     if (g_bf_clusters <= 0) return set_error(FH3CUDA_E_CUDA, "%s: the pair kernel cannot be resident", who);
     CUtensorMap tmA;
     if ((rc = map_activations(&tmA, x_bf16, ldx, n_tok, in))) return rc;
     Params p = make_params(n_tok, out, in, ldy, bias, gate, y, epi, ctx_status(c));
     p.pdl = (flags & FH3CUDA_GEMM_WEIGHTS_READY) ? 2 : 1;
-    return launch_bf16_pair(tmA, static_cast<const __nv_bfloat16*>(w_bf16), p, static_cast<cudaStream_t>(stream));
+    return launch_bf16_pair(tmA, static_cast<const __nv_bfloat16*>(w_bf16), p, s, ldw);
+}
+
+}  // namespace fh3host
+
+extern "C" int fh3cuda_gemm_bf16w_dev(const void* w_bf16, int64_t out, int64_t in, const void* x_bf16, int64_t ldx,
+                                      void* y, int64_t ldy, int64_t n_tok, const float* bias, const float* gate,
+                                      int epi, int flags, void* stream) {
+    return fh3host::gemm_bf16w(w_bf16, in, out, in, x_bf16, ldx, y, ldy, n_tok, bias, gate, epi, flags,
+                               static_cast<cudaStream_t>(stream));
 }

@@ -139,7 +139,9 @@ FH3CUDA_API int fh3cuda_dequant_dev(int type, const void *src, float *dst, int64
  * Frobenius error <= 1e-5 against fh3_matmul); larger n_tok runs the tcgen05
  * GEMM on bf16 operands with fp32 accumulation (<= 5e-3).  Every other format
  * fh3_dequant expands (the text encoder's Q5_K / Q6_K, F16 / F32 globals, ...):
- * rows expanded bit-exactly to fp32, then an fp32 cuBLAS GEMM (<= 1e-5).
+ * weights formed bit-exactly as fh3_dequant's fp32 values, then up to 16 tokens an
+ * fp32 CUDA-core GEMV, above that the tcgen05 GEMM on the four bf16 products of
+ * weights and activations split into high and low bf16 parts (<= 1e-5 both).
  * Internal scratch is cached per device and grows on demand. */
 FH3CUDA_API int fh3cuda_matmul_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
                        const float *bias_or_null, void *stream);

@@ -3,8 +3,10 @@ and every other format fh3_dequant expands) on the GPU.
 
 Dequantisation is bit-exact with the reference (its gguf fixtures and the oracle, which is
 bitwise equal to fh3_dequant; NaN payloads of random fp16 scales compared as NaN).  The
-matmul expands rows to fp32 and runs an fp32 GEMM: relative Frobenius error <= 1e-5 against
-fh3_matmul (the oracle, and the reference's own outputs in tests/golden)."""
+matmul forms fh3_dequant's fp32 weights and contracts them at fp32 accuracy: up to 16
+tokens on the CUDA cores, above that on the tcgen05 tensor cores as four bf16 products of
+split operands.  Relative Frobenius error <= 1e-5 against fh3_matmul (the oracle, and the
+reference's own outputs in tests/golden)."""
 from __future__ import annotations
 
 import os
@@ -99,14 +101,33 @@ def test_matmul_vs_oracle(fh3, oracle, t, M):
     assert rel_fro(got, ref) <= TOL
 
 
-def test_matmul_in_row_chunks(fh3, oracle):
-    """8200 x 8192 Q6_K: 269 MB of fp32 rows, expanded in two chunks."""
+@pytest.mark.parametrize("M", [3, 40])
+def test_matmul_in_row_chunks(fh3, oracle, M):
+    """8200 x 8192 Q6_K: 3 tokens on the GEMV; 40 tokens through the split-bf16 GEMM, whose
+    537 MB of expanded weight rows are processed in three chunks of whole 256-row tiles."""
     import torch
-    t, K, N, M = 14, 8192, 8200, 3
+    t, K, N = 14, 8192, 8200
     raw = _weights(oracle, t, N, K, seed=5)
     x = oracle.rng_normal(5, 1, M * K).reshape(M, K)
     ref = oracle.matmul(t, raw, K, N, x)
     got = fh3.matmul(fh3.Weight.from_bytes(raw, K, N, type_=t), torch.from_numpy(x).cuda()).cpu().numpy()
+    assert rel_fro(got, ref) <= TOL
+
+
+@pytest.mark.parametrize("t", [0, 1, 13])
+def test_matmul_odd_widths_and_many_tokens(fh3, oracle, t):
+    """A width that is not a multiple of 16 (padded with zeros in the split operands) for the
+    element formats, and more tokens than one 256-row tile."""
+    import torch
+    K = 1000 if t in (0, 1) else 1280
+    N, M = 333, 700
+    raw = (np.random.default_rng(t).standard_normal(N * K).astype(np.float32) * 0.05).view(np.uint8) \
+        if t == 0 else _weights(oracle, t, N, K, seed=t + 200)
+    x = oracle.rng_normal(t + 9, M, M * K).reshape(M, K)
+    bias = oracle.rng_normal(t + 9, 98, N)
+    ref = oracle.matmul(t, raw, K, N, x, bias)
+    w = fh3.Weight.from_bytes(raw, K, N, type_=t)
+    got = fh3.matmul(w, torch.from_numpy(x).cuda(), torch.from_numpy(bias).cuda()).cpu().numpy()
     assert rel_fro(got, ref) <= TOL
 
 
