@@ -9,10 +9,12 @@
 // Final layer: rmsnorm(final_norm) -> modulate (final AdaLN rows) -> video / audio
 // heads.  The text refiner has plain residuals and no modulation or rope.
 //
-// Activations are fp32 [rows][width] in one scratch slot.  Projections go through
-// fh3cuda_matmul_dev, so every weight format fh3 packs is served (Q4_K on the
-// tensor-core GEMM / GEMV, F32 and the other formats on their paths).  Attention
-// runs in fp32 (cfg.attn_bf16 = 0: the CPU path's accuracy) or on bf16 tensor cores.
+// Activations are fp32 [rows][width] in one scratch slot.  A trunk block whose projections
+// are all Q4_K, with bf16 tensor-core attention (cfg.attn_bf16 = 1), runs on bf16 operands
+// with the GEMMs' fused prologue and epilogues (fused_block_run, the bench trunk's
+// launches).  Otherwise projections go through fh3cuda_matmul_dev, so every weight format
+// fh3 packs is served (F32 and the other formats on their paths), and attention runs in
+// fp32 (cfg.attn_bf16 = 0: the CPU path's accuracy) or on bf16 tensor cores.
 // Rows are ordered text | audio | video; AdaLN pair of a row: text 1, audio 2,
 // video 0 (fh3_seq_build, src/model/fh3_seq.c:56-72).
 #include <algorithm>
@@ -98,10 +100,11 @@ namespace {
 
 constexpr int kDitSlot = 10;
 
-// activations of one call, [rows][width] fp32 (bf16 copies for tensor-core attention)
+// activations of one call, [rows][width] fp32 (bf16 copies for tensor-core attention,
+// and the bf16 operands of the fused Q4_K block)
 struct DitBufs {
     float *h, *normed, *qkv, *attn, *proj, *fc1, *sw, *gatec;
-    __nv_bfloat16 *qkvb, *gateb;
+    __nv_bfloat16 *qkvb, *gateb, *ab, *attnb, *gb;
 };
 
 size_t dit_layout(int64_t rows, const Fh3CudaDitCfg& c, uint8_t* base, DitBufs* b) {
@@ -124,6 +127,9 @@ size_t dit_layout(int64_t rows, const Fh3CudaDitCfg& c, uint8_t* base, DitBufs* 
     if (c.attn_bf16) {
         x.qkvb = reinterpret_cast<__nv_bfloat16*>(take(3 * inner, 2));
         x.gateb = reinterpret_cast<__nv_bfloat16*>(take(inner, 2));
+        x.ab = reinterpret_cast<__nv_bfloat16*>(take(hid, 2));
+        x.attnb = reinterpret_cast<__nv_bfloat16*>(take(inner, 2));
+        x.gb = reinterpret_cast<__nv_bfloat16*>(take(F, 2));
     }
     if (b) *b = x;
     return off;
@@ -193,6 +199,84 @@ int dit_attention(const Fh3CudaDitCfg& c, const DitBufs& b, int64_t rows, const 
 }
 
 const PairRows kNoPairs = {{nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr}, 0, 0};
+
+// A block whose projections are all Q4_K runs on bf16 operands end to end (with bf16
+// tensor-core attention): the rmsnorm+modulate prologue writes bf16, the QKV and
+// gate_compress GEMMs write bf16, q and k are normalised and rotated in bf16, attention
+// writes bf16, the O and fc2 GEMMs add gate * y into h in their epilogue, and fc1 applies
+// SwiGLU in its epilogue -- the launches the bench's trunk makes.  Otherwise (F32 or other
+// formats, or fp32 attention) the block takes the fp32 chain below.
+bool fused_block(const Fh3CudaDitCfg& c, const Fh3CudaLayerView& v) {
+    auto q4k = [](const Fh3CudaW& w) { return w.type == FH3CUDA_TYPE_Q4_K && (w.in % 256) == 0; };
+    const bool gated = c.attn == 1 && v.gate_compress.data && v.gate_compress.out > 0;
+    return c.attn_bf16 && q4k(v.qkv) && q4k(v.out) && q4k(v.fc1) && q4k(v.fc2) && (!gated || q4k(v.gate_compress));
+}
+
+// the contiguous row ranges of the three modalities (text | audio | video) and their pairs
+struct Ranges {
+    int64_t r0[3], n[3];
+    int pair[3];
+};
+Ranges ranges(int T, int A, int V) {
+    return Ranges{{0, T, static_cast<int64_t>(T) + A}, {T, A, V}, {1, 2, 0}};
+}
+
+// one trunk block on the bf16 path; pr(L, chunk, pair) is the AdaLN row
+template <class RowFn>
+int fused_block_run(const Fh3CudaDitCfg& c, const Fh3CudaLayerView& v, const DitBufs& b, int64_t N, const Ranges& rg,
+                    const Fh3CudaSeq* seq, const float* cos_t, const float* sin_t, RowFn row, cudaStream_t s) {
+    const int hid = c.hidden_size, heads = c.num_heads, hd = c.head_dim, F = c.ffn_dim;
+    const int64_t inner = static_cast<int64_t>(heads) * hd;
+    int rc;
+    auto norm_mod = [&](const Fh3CudaW& nw, int chunk) {
+        for (int m = 0; m < 3; ++m) {
+            if (rg.n[m] <= 0) continue;
+            const int r = fh3cuda_rmsnorm_modulate_dev(b.h + rg.r0[m] * hid, reinterpret_cast<const float*>(nw.data),
+                                                       row(chunk, rg.pair[m]), row(chunk + 1, rg.pair[m]),
+                                                       b.ab + rg.r0[m] * hid, static_cast<int>(rg.n[m]), hid,
+                                                       c.norm_eps, s);
+            if (r) return r;
+        }
+        return static_cast<int>(FH3_OK);
+    };
+    auto resid = [&](const Fh3CudaW& w, const __nv_bfloat16* x, int64_t ldx, int chunk) {
+        for (int m = 0; m < 3; ++m) {
+            if (rg.n[m] <= 0) continue;
+            const int r = fh3cuda_gemm_q4k_dev(&w, x + rg.r0[m] * ldx, ldx, b.h + rg.r0[m] * hid, hid, rg.n[m], nullptr,
+                                               row(chunk, rg.pair[m]), FH3CUDA_EPI_RESID, s);
+            if (r) return r;
+        }
+        return static_cast<int>(FH3_OK);
+    };
+    if ((rc = norm_mod(v.norm1, 0))) return rc;
+    if ((rc = fh3cuda_gemm_q4k_dev(&v.qkv, b.ab, hid, b.qkvb, 3 * inner, N, nullptr, nullptr, FH3CUDA_EPI_BF16, s)))
+        return rc;
+    for (int part = 0; part < 2; ++part) {  // q, k: per-head rmsnorm + rope3 over 96 channels, in bf16
+        __nv_bfloat16* x = b.qkvb + part * inner;
+        rc = fh3cuda_qk_norm_rope_dev(x, 1, 3 * inner, x, 1, 3 * inner,
+                                      reinterpret_cast<const float*>(part ? v.k_norm.data : v.q_norm.data), cos_t,
+                                      sin_t, static_cast<int>(N), heads, hd, 96, c.qk_norm_eps, s);
+        if (rc) return rc;
+    }
+    const __nv_bfloat16* q = b.qkvb;
+    if (c.attn == 1) {
+        const bool gated = v.gate_compress.data && v.gate_compress.out > 0;
+        if (gated && (rc = fh3cuda_gemm_q4k_dev(&v.gate_compress, b.ab, hid, b.gateb, inner, N, nullptr, nullptr,
+                                                FH3CUDA_EPI_BF16, s)))
+            return rc;
+        rc = fh3cuda_vsa_attention_dev(c.vsa_tile, c.vsa_sparsity, seq, q, 3 * inner, q + inner, 3 * inner,
+                                       q + 2 * inner, 3 * inner, 1, gated ? b.gateb : nullptr, inner, b.attnb, 1, inner,
+                                       heads, hd, s);
+    } else {
+        rc = fh3cuda_attention_dev(q, 3 * inner, q + inner, 3 * inner, q + 2 * inner, 3 * inner, b.attnb, 1, inner,
+                                   static_cast<int>(N), heads, hd, s);
+    }
+    if (rc) return rc;
+    if ((rc = resid(v.out, b.attnb, inner, 2))) return rc;
+    if ((rc = norm_mod(v.norm2, 3))) return rc;
+    if ((rc = fh3cuda_gemm_q4k_dev(&v.fc1, b.ab, hid, b.gb, F, N, nullptr, nullptr, FH3CUDA_EPI_SWIGLU, s))) return rc;
+    return resid(v.fc2, b.gb, F, 5);
+}
 
 }  // namespace
 
@@ -289,6 +373,11 @@ extern "C" int fh3cuda_dit_forward_dev(const Fh3CudaDitCfg* cfg, const Fh3CudaDi
             return set_error(FH3_E_INVALID, "%s: layer %d norm weights are not F32", who, L);
         PairRows pr;
         if ((rc = pair_rows(L, 0, pr))) return rc;
+        if (fused_block(c, v)) {
+            auto row = [&](int chunk, int pair) { return fh3cuda_adaln_row(adaln, step, L, pair, chunk); };
+            if ((rc = fused_block_run(c, v, b, N, ranges(T, A, V), seq, cos_t, sin_t, row, s))) return rc;
+            continue;
+        }
         if ((rc = norm(b.h, reinterpret_cast<const float*>(v.norm1.data), b.normed, N, hid, c.norm_eps, pr, s))) return rc;
         if ((rc = mm(v.qkv, b.normed, b.qkv, N, nullptr, s))) return rc;
         for (int part = 0; part < 2; ++part) {  // q, k: per-head rmsnorm + rope3 over 96 channels

@@ -86,3 +86,65 @@ def test_readers_error_codes(tmp_path, fn, name):
         p.write_bytes(good[:12] + struct.pack("<I", 512) + good[16:])
         assert _open_code(fn, str(p)) == -8                                      # FH3_E_INVALID
     assert _open_code(fn, os.path.join(TINY, name)) == -22                      # the file checks out: no device
+
+
+def _tiny_globals():
+    from fasth3inc_b200.dit import read_gguf
+    _, tensors, buf, data = read_gguf(os.path.join(TINY, "dit_globals.bin"))
+    out = {}
+    for name, t in tensors.items():
+        a = np.frombuffer(buf, np.float32, int(np.prod(t.ne)), data + t.offset)
+        out[name] = a.reshape(tuple(reversed(t.ne))) if len(t.ne) > 1 else a
+    return out
+
+
+def _tiny_inputs():
+    from fasth3inc_b200.dit import rope_tables
+    f = lambda n, shape: np.fromfile(os.path.join(TINY, n), np.float32).reshape(shape)
+    cos, sin = rope_tables(np.fromfile(os.path.join(TINY, "pos.bin"), np.float64))
+    return f("text_rows.bin", (6, 256)), f("x_video.bin", (8, 96)), f("x_audio.bin", (4, 32)), cos, sin
+
+
+TINY_CFG = dict(hidden=256, heads=2, head_dim=128, ffn=512, eps=1e-5, qk_eps=1e-5, final_eps=1e-5, vsa_tile=64,
+                vsa_sparsity=0.8)
+TINY_SEQ = (18, 6, 4, 8, 1, 1, 8)
+
+
+@pytest.mark.parametrize("attn,suffix", [(0, ""), (1, "_vsa")])
+@pytest.mark.parametrize("step", [0, 7])
+def test_oracle_dit_composition_matches_reference_tiny(oracle, attn, suffix, step):
+    """The CPU composition used to check the Q4_K DiT forward (tests/q4k_pack.py) reproduces the
+    reference's own tiny-model outputs (computed by torch, tests/unit/test_dit_tiny.c:155-156:
+    relative L2 <= 1e-4) from the F32 trunk, so it is pinned before it judges the GPU."""
+    from conftest import rel_l2
+    from q4k_pack import oracle_forward, read_adaln, read_pack
+    layers = read_pack(os.path.join(TINY, "dit_trunk.bin"))
+    text_rows, xv, xa, cos, sin = _tiny_inputs()
+    vv, va = oracle_forward(oracle, layers, _tiny_globals(), read_adaln(os.path.join(TINY, "adaln_table.bin")),
+                            text_rows, xv, xa, cos, sin, step, dict(TINY_CFG, attn=attn), TINY_SEQ)
+    ref_v = np.fromfile(os.path.join(TINY, f"video_v{suffix}_step{step}.bin"), np.float32).reshape(vv.shape)
+    ref_a = np.fromfile(os.path.join(TINY, f"audio_v{suffix}_step{step}.bin"), np.float32).reshape(va.shape)
+    assert rel_l2(vv, ref_v) <= 1e-4 and rel_l2(va, ref_a) <= 1e-4
+
+
+def test_q4k_pack_rewrite_passes_the_readers_file_checks(tmp_path, oracle):
+    """The synthetic Q4_K pack keeps the FH3P layout: every projection becomes Q4_K rows of the
+    same shape, norms stay F32, and (without a device) fh3cuda_pack_open accepts the file up to
+    the device allocation."""
+    from q4k_pack import read_pack, write_q4k_pack
+    dst = str(tmp_path / "q4k_trunk.bin")
+    src_layers = read_pack(os.path.join(TINY, "dit_trunk.bin"))
+    write_q4k_pack(os.path.join(TINY, "dit_trunk.bin"), dst, oracle)
+    got = read_pack(dst)
+    assert len(got) == len(src_layers) == 3
+    for a, b in zip(got, src_layers):
+        for name in ("qkv", "out", "fc1", "fc2"):
+            assert a[name]["type"] == 12 and (a[name]["in_"], a[name]["out"]) == (b[name]["in_"], b[name]["out"])
+            assert len(a[name]["raw"]) == a[name]["out"] * oracle.row_bytes(12, a[name]["in_"])
+            deq = oracle.dequant(12, a[name]["raw"], a[name]["out"], a[name]["in_"])
+            w = b[name]["raw"].view(np.float32).reshape(deq.shape)
+            assert np.abs(deq - w).max() <= 0.1 * np.abs(w).max()       # a Q4_K rounding of the same weights
+        for name in ("norm1", "norm2", "q_norm", "k_norm"):
+            assert a[name]["type"] == 0 and np.array_equal(a[name]["raw"], b[name]["raw"])
+    if not HAS_GPU:
+        assert _open_code("pack", dst) == -22                  # the file checks out: no device
