@@ -54,7 +54,7 @@ def parse():
                     help="run each projection as one fh3cuda_gemm_q4k_dev call (no second stream)")
     ap.add_argument("--no-gemv", action="store_true",
                     help="skip the GEMV (1..4 token), q/k norm+rope and attention measurements")
-    ap.add_argument("--case", choices=["gemm", "gemv", "qk", "attn", "vsa"], default=None,
+    ap.add_argument("--case", choices=["gemm", "gemv", "qk", "attn", "vsa", "norm"], default=None,
                     help="run one kernel's launches on a small case (for ncu) instead of the bench")
     ap.add_argument("--case-rows", type=int, default=8192, help="--case gemm / qk: activation rows")
     ap.add_argument("--case-kn", type=int, nargs=2, default=(5120, 13824), help="--case gemv: in, out")
@@ -809,6 +809,14 @@ def run_case(args):
             fh3.vsa_attention(qkv[:, :H * Dh], qkv[:, H * Dh:2 * H * Dh], qkv[:, 2 * H * Dh:], gate, seq, H, Dh,
                               out=out)
         shape = {"rows": n, "heads": H, "head_dim": Dh, "grid": list(seq[4:])}
+    elif args.case == "norm":
+        M = args.case_rows
+        h = torch.randn((M, D_MODEL), device="cuda")
+        sh, sc = 0.1 * torch.randn(D_MODEL, device="cuda"), 0.1 * torch.randn(D_MODEL, device="cuda")
+        a = torch.empty((M, D_MODEL), dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.case_reps):
+            fh3.rmsnorm_modulate(h, sh, sc, out=a)
+        shape = {"rows": M, "dim": D_MODEL}
     elif args.case == "qk":
         H, Dh, R = 40, 128, 96
         qkv = torch.randn((args.case_rows, 3 * H * Dh), device="cuda").to(torch.bfloat16)

@@ -770,10 +770,11 @@ constexpr int64_t kTwoPassRows = 2048;
 // Q4_K -> bf16 [N][K], one warp per super-block step: lane l writes output chunk l of
 // the super-block (weights 8l..8l+7, 16 bytes), so a warp's store is 512 contiguous
 // bytes; every lane reads the 16-byte header (one broadcast request) and the 8 nibble
-// bytes its chunk needs (the 32 lanes' reads cover the 128 nibble bytes).  kUnroll
-// super-blocks a warp are loaded before any is converted, to keep enough reads in
-// flight.  Loads are streaming (evict-first): the weights are read once, and L2 is kept
-// for the GEMM's tiles.
+// bytes its chunk needs (the 32 lanes' reads cover the 128 nibble bytes).  A warp owns a
+// contiguous run of super-blocks (row-major over (row, super-block)), walked with an
+// incremental (row, super-block) position -- no division per step -- kExpandUnroll at a
+// time, all their loads issued before any is converted.  Loads are streaming
+// (evict-first): the weights are read once, and L2 is kept for the GEMM's tiles.
 constexpr int kExpandUnroll = 4;
 constexpr int kExpandThreads = 128;
 
@@ -783,32 +784,44 @@ __global__ void __launch_bounds__(kExpandThreads)
     const int lane = threadIdx.x & 31;
     const int nblk = K / fh3::kQ4KBlock;
     const int64_t total = N * nblk;
-    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int64_t begin = warp * total / nwarps, end = (warp + 1) * total / nwarps;
+    if (begin >= end) return;
     const int sub = lane >> 3, j = lane & 7, hh = j >> 2;
     const int qoff = 16 + 32 * sub + 8 * (j & 3);  // this lane's 8 nibble bytes
-    for (int64_t base = warp0 * kExpandUnroll; base < total; base += nwarps * kExpandUnroll) {
+    int64_t n = begin / nblk;
+    int b = static_cast<int>(begin - n * nblk);
+    const uint8_t* src = w + n * rb + static_cast<size_t>(b) * fh3::kQ4KBytes;
+    __nv_bfloat16* dst = out + n * K + static_cast<int64_t>(b) * fh3::kQ4KBlock + lane * 8;
+    for (int64_t idx = begin; idx < end; idx += kExpandUnroll) {
+        const int cnt = end - idx < kExpandUnroll ? static_cast<int>(end - idx) : kExpandUnroll;
         uint4 hdr[kExpandUnroll];
         uint2 q[kExpandUnroll];
+        __nv_bfloat16* d[kExpandUnroll];
 #pragma unroll
         for (int u = 0; u < kExpandUnroll; ++u) {
-            const int64_t idx = base + u;
-            if (idx < total) {
-                const int64_t n = idx / nblk;
-                const uint8_t* blk = w + n * rb + static_cast<size_t>(idx - n * nblk) * fh3::kQ4KBytes;
-                hdr[u] = __ldcs(reinterpret_cast<const uint4*>(blk));
-                q[u] = __ldcs(reinterpret_cast<const uint2*>(blk + qoff));
+            if (u < cnt) {
+                hdr[u] = __ldcs(reinterpret_cast<const uint4*>(src));
+                q[u] = __ldcs(reinterpret_cast<const uint2*>(src + qoff));
+                d[u] = dst;
+                // next super-block of the run (the next row after the last one)
+                if (++b == nblk) {
+                    b = 0;
+                    src += rb - static_cast<size_t>(nblk - 1) * fh3::kQ4KBytes;
+                    dst += fh3::kQ4KBlock;
+                } else {
+                    src += fh3::kQ4KBytes;
+                    dst += fh3::kQ4KBlock;
+                }
             }
         }
 #pragma unroll
         for (int u = 0; u < kExpandUnroll; ++u) {
-            const int64_t idx = base + u;
-            if (idx < total) {
-                const int64_t n = idx / nblk;
+            if (u < cnt) {
                 float sc, nm;
                 q4k_sub_scales(hdr[u], 2 * sub + hh, sc, nm);
-                const uint4 pk = q4k_chunk8_bf16(sc, nm, q[u].x, q[u].y, hh);
-                *reinterpret_cast<uint4*>(out + n * K + (idx - n * nblk) * fh3::kQ4KBlock + lane * 8) = pk;
+                *reinterpret_cast<uint4*>(d[u]) = q4k_chunk8_bf16(sc, nm, q[u].x, q[u].y, hh);
             }
         }
     }

@@ -422,6 +422,9 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, FH3_GV_MIN_BLOCKS) gemv_mma_
 #ifndef FH3_GV_STREAM_WARPS
 #define FH3_GV_STREAM_WARPS 16  // warps of the one CTA per SM
 #endif
+#ifndef FH3_GV_STREAM_MIN_BLOCKS
+#define FH3_GV_STREAM_MIN_BLOCKS 1  // CTAs an SM must hold at once (2: consecutive calls overlap)
+#endif
 constexpr int kStreamWarps = FH3_GV_STREAM_WARPS;
 
 __device__ __forceinline__ int64_t stream_warp_of(int64_t u, int64_t GW, int64_t units) {
@@ -508,7 +511,7 @@ __device__ __forceinline__ void build_fragments(const float* __restrict__ x, int
 }
 
 template <int M>
-__global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_stream_kernel(
+__global__ void __launch_bounds__(kStreamWarps * 32, FH3_GV_STREAM_MIN_BLOCKS) gemv_stream_kernel(
     const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, int64_t units, int seg_max,
     const float* __restrict__ x, const float* __restrict__ bias, float* __restrict__ y, int64_t ldy,
     float* __restrict__ partials, int* __restrict__ counters, int* status) {
