@@ -29,9 +29,9 @@ METRIC = "Q4_K DiT step ms & dequant-GEMM TFLOP/s (GEMV GB/s) at 1/2/4/8 B200 vs
 UNIT = "TFLOP/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum per FLOP of one gemm_bf16_pair_kernel fc1 launch
-# (8192 rows: 1324.5 + 219.5 MB for 2.319 TFLOP, profiles/gemm_bf16_pair_fc1_m8192.md), scaled to
+# (8192 rows: 1164.4 + 219.6 MB for 2.319 TFLOP, profiles/gemm_bf16_pair_fc1_m8192.md), scaled to
 # the bench's fc1 launch at this rank's rows.
-GEMM_TRAFFIC_BYTES_PER_FLOP = (1324.5e6 + 219.5e6) / 2.319e12
+GEMM_TRAFFIC_BYTES_PER_FLOP = (1164.4e6 + 219.6e6) / 2.319e12
 
 
 def parse():
