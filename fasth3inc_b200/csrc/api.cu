@@ -18,8 +18,9 @@ namespace fh3host {
 // 10 the DiT forward's activations, 11 bf16 weights of the two-pass large-M GEMM,
 // 12 the transposed V of the tensor-core attention, 13 video sparse attention's tile-order
 // copies of q, k and v, 14 / 15 the tcgen05 GEMV's split-tile partials and counters,
-// 16 the unit gate that adds the K slices of the non-Q4_K formats' GEMM
-constexpr int kScratchSlots = 17;
+// 16 the fused GEMM's split-K partials, 17 the unit gate that adds the K slices of the
+// non-Q4_K formats' GEMM
+constexpr int kScratchSlots = 18;
 
 struct DevCtx {
     int device = -1;

@@ -263,7 +263,7 @@ int matmul_formats(DevCtx* c, const Fh3CudaW* w, const float* x, float* y, int n
     const int64_t nslices = (Kp + kSliceK - 1) / kSliceK;
     float* ones = nullptr;
     if (nslices > 1) {
-        ones = static_cast<float*>(scratch(c, 16, static_cast<size_t>(wrows) * 4, s));
+        ones = static_cast<float*>(scratch(c, 17, static_cast<size_t>(wrows) * 4, s));
         if (ones) {
             fill_kernel<<<grid_of(c, wrows), 256, 0, s>>>(ones, wrows, 1.0f);
             if (int rc = check_cuda(cudaGetLastError(), "fill_kernel launch")) return rc;

@@ -65,6 +65,11 @@ struct Params {
     void* y;
     int epi;
     int* status;
+    // split-K (gemm_q4k_pair_kernel): each tile's super-blocks cut into ksplit ranges, one
+    // unit of work each; a unit stores its fp32 accumulator in part[split][M][n_out] (no
+    // bias), and splitk_reduce_kernel adds the ranges in order and applies the epilogue
+    int ksplit = 1;
+    float* part = nullptr;
     // programmatic dependent launch (gemm_bf16_pair_kernel): 0 off; 1 the kernel may start
     // while the previous kernel on its stream runs, and waits for it (griddepcontrol.wait)
     // before its first global access; 2 the same, except that the weight tiles of the
@@ -562,6 +567,16 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
     const int ksteps = static_cast<int>(p.K / BK);
     const int64_t pair = blockIdx.x >> 1;
     const int64_t npairs = gridDim.x >> 1;
+    // units of work: (tile, K range of whole super-blocks); ksplit 1 = whole tiles
+    const int ksplit = p.ksplit;
+    const int64_t num_units = num_tiles * ksplit;
+    const int nsb = ksteps / 4;
+    auto unit_of = [&](int64_t u, int64_t& tile, int& split, int& sb0, int& sb1) {
+        tile = u / ksplit;
+        split = static_cast<int>(u - tile * ksplit);
+        sb0 = split * nsb / ksplit;
+        sb1 = (split + 1) * nsb / ksplit;
+    };
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < SA; ++i) { fh3::mbar_init(&a_full[i], 1); fh3::mbar_init(&a_empty[i], 1); }
@@ -594,11 +609,13 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
             Ring ra;
             uint32_t a_filled = 0, a_par = 0;
             bool ok = true;
-            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
-                int64_t mb, nb;
+            for (int64_t u = pair; u < num_units && ok; u += npairs) {
+                int64_t tile, mb, nb;
+                int split, sb0, sb1;
+                unit_of(u, tile, split, sb0, sb1);
                 tile_coords(tile, num_m, num_n, mb, nb);
                 const int m0 = static_cast<int>(mb * 256 + cr * 128);
-                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                for (int ks = 4 * sb0; ks < 4 * sb1 && ok; ++ks) {
                     if (!(ok = fh3::mbar_wait(&a_empty[ra.idx], ra.phase ^ 1u, abort_flag, p.status))) break;
                     // both CTAs' activation bytes are counted on the leader's a_full
                     if (leader) fh3::mbar_arrive_expect_tx(&a_full[ra.idx], 2 * A_BYTES);
@@ -627,12 +644,14 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
             Ring rr;
             uint32_t r_filled = 0, r_par = 0;
             bool ok = true;
-            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
-                int64_t mb, nb;
+            for (int64_t u = pair; u < num_units && ok; u += npairs) {
+                int64_t tile, mb, nb;
+                int split, sb0, sb1;
+                unit_of(u, tile, split, sb0, sb1);
                 tile_coords(tile, num_m, num_n, mb, nb);
                 const int wrow = swiglu ? static_cast<int>(cr ? p.n_out + nb * 128 : nb * 128)
                                         : static_cast<int>(nb * BN + cr * 128);
-                for (int rs = 0; rs < ksteps / 4 && ok; ++rs) {
+                for (int rs = sb0; rs < sb1 && ok; ++rs) {
                     if (!(ok = fh3::mbar_wait(&r_empty[rr.idx], rr.phase ^ 1u, abort_flag, p.status))) break;
                     fh3::mbar_arrive_expect_tx(&r_full[rr.idx], R_BYTES);
                     fh3::tma_load_2d(smem + OFF_R + rr.idx * R_BYTES, &tmW, &r_full[rr.idx],
@@ -654,11 +673,14 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
             constexpr uint32_t idesc = fh3::idesc_bf16_f32(256, BN);
             Ring ra, rb, racc;
             bool ok = true;
-            for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
+            for (int64_t u = pair; u < num_units && ok; u += npairs) {
+                int64_t tile;
+                int split, sb0, sb1;
+                unit_of(u, tile, split, sb0, sb1);
                 if (!(ok = fh3::mbar_wait(&acc_empty[racc.idx], racc.phase ^ 1u, abort_flag, p.status))) break;
                 fh3::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(racc.idx * BN);
-                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                for (int ks = 4 * sb0; ks < 4 * sb1 && ok; ++ks) {
                     if (!(ok = fh3::mbar_wait(&a_full[ra.idx], ra.phase, abort_flag, p.status))) break;
                     if (!(ok = fh3::mbar_wait(&b_full[rb.idx], rb.phase, abort_flag, p.status))) break;
                     fh3::tc_fence_after();
@@ -666,7 +688,8 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
                     const uint64_t bd = fh3::sdesc_sw128(fh3::smem_u32(smem + OFF_B + rb.idx * B_BYTES));
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
-                        fh3::umma_f16_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0 ? 1u : 0u);
+                        fh3::umma_f16_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc,
+                                           (ks != 4 * sb0 || kk != 0) ? 1u : 0u);
                     fh3::umma_commit_pair(&a_empty[ra.idx], 0x3);
                     fh3::umma_commit_pair(&b_empty[rb.idx], 0x3);
                     ra.next<SA>();
@@ -687,8 +710,10 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
         const int q = warp & 3;
         const uint32_t acc_empty_leader = fh3::mapa_shared(fh3::smem_u32(acc_empty), 0);
         Ring racc;
-        for (int64_t tile = pair; tile < num_tiles; tile += npairs) {
-            int64_t mb, nb;
+        for (int64_t u = pair; u < num_units; u += npairs) {
+            int64_t tile, mb, nb;
+            int split, sb0, sb1;
+            unit_of(u, tile, split, sb0, sb1);
             tile_coords(tile, num_m, num_n, mb, nb);
             int ok = 1;
             if (lane == 0) ok = fh3::mbar_wait(&acc_full[racc.idx], racc.phase, abort_flag, p.status);
@@ -696,7 +721,29 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
             fh3::tc_fence_after();
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(racc.idx * BN);
-            epilogue_tile(p, tbase, mb * 256 + cr * 128 + q * 32 + lane, nb);
+            const int64_t m = mb * 256 + cr * 128 + q * 32 + lane;
+            if (ksplit == 1) {
+                epilogue_tile(p, tbase, m, nb);
+            } else {
+                // this K range's fp32 accumulator row, as is
+                float* prow = p.part + (static_cast<int64_t>(split) * p.M + m) * p.n_out;
+                for (int cc = 0; cc < 8; ++cc) {
+                    uint32_t v[32];
+                    TmemAcc{tbase}.load(cc * 32, v);
+                    const int64_t n0 = nb * 256 + cc * 32;
+                    if (m >= p.M || n0 >= p.n_out) continue;
+                    if (n0 + 32 <= p.n_out && (reinterpret_cast<uintptr_t>(prow + n0) & 15) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            __stcg(reinterpret_cast<float4*>(prow + n0 + j),
+                                   make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                               __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])));
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + j < p.n_out) prow[n0 + j] = __uint_as_float(v[j]);
+                    }
+                }
+            }
             fh3::tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -718,8 +765,11 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
         Ring rr;
         uint32_t s_base = 0;  // index of the first K-64 stage of the current raw stage
         bool ok = true;
-        for (int64_t tile = pair; tile < num_tiles && ok; tile += npairs) {
-            for (int rs = 0; rs < ksteps / 4 && ok; ++rs, s_base += 4) {
+        for (int64_t u = pair; u < num_units && ok; u += npairs) {
+            int64_t tile;
+            int split, sb0, sb1;
+            unit_of(u, tile, split, sb0, sb1);
+            for (int rs = sb0; rs < sb1 && ok; ++rs, s_base += 4) {
                 int w = 1;
                 if (lane == 0) w = fh3::mbar_wait(&r_full[rr.idx], rr.phase, abort_flag, p.status);
                 if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
@@ -1021,6 +1071,27 @@ __global__ void __launch_bounds__(bfp::kThreads, 1)
     }
 }
 
+// y = epilogue(sum over s of part[s] (+ bias)), the split-K ranges added in order: F32, BF16
+// or the gated residual h += gate * (sum + bias).  part is [ksplit][M][N] fp32.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int ksplit, int64_t M, int64_t N,
+                                     const float* __restrict__ bias, const float* __restrict__ gate, void* y,
+                                     int64_t ldy, int epi) {
+    const int64_t total = M * N;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float v = __ldcg(part + e);
+        for (int sp = 1; sp < ksplit; ++sp) v += __ldcg(part + sp * total + e);
+        const int64_t m = e / N, n = e - m * N;
+        if (bias) v += bias[n];
+        if (epi == FH3CUDA_EPI_BF16) {
+            static_cast<__nv_bfloat16*>(y)[m * ldy + n] = __float2bfloat16_rn(v);
+        } else {
+            float* yy = static_cast<float*>(y) + m * ldy + n;
+            *yy = epi == FH3CUDA_EPI_RESID ? fmaf(gate[n], v, *yy) : v;
+        }
+    }
+}
+
 std::once_flag g_attr_once;
 cudaError_t g_attr_err = cudaSuccess;
 int g_pair_clusters = 0;  // co-resident CTA pairs on device 0's layout (queried once)
@@ -1206,7 +1277,18 @@ int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_
         return set_error(FH3_E_INVALID, "%s: weights and x must be 16-byte aligned", who);
     if ((rc = gemm_setup())) return rc;
 
-    const bool pair = use_pair_kernel(n_tok) && g_pair_clusters > 0;
+    bool pair = use_pair_kernel(n_tok) && g_pair_clusters > 0;
+    {
+        // up to 128 rows the one-SM kernel takes one CTA per 256 output columns; when that
+        // would leave more than half the SMs idle, the pair kernel's split-K spreads the K
+        // ranges over them instead (unless FH3CUDA_GEMM_KERNEL forces a kernel)
+        const char* gk0 = getenv("FH3CUDA_GEMM_KERNEL");
+        const char* sk0 = getenv("FH3CUDA_GEMM_SPLITK");
+        const int64_t cols = epi == FH3CUDA_EPI_SWIGLU ? 0 : (w->out + 255) / 256;
+        if (!pair && !gk0 && !(sk0 && strcmp(sk0, "0") == 0) && !fused_only && g_pair_clusters > 0 && cols > 0 &&
+            ((n_tok + 127) / 128) * cols * 2 <= ctx_sms(c) && (w->in / fh3::kQ4KBlock) >= 4)
+            pair = true;
+    }
     const size_t rb = fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, w->in);
     CUtensorMap tmA, tmW;
     if ((rc = map_activations(&tmA, x_bf16, ldx, n_tok, w->in))) return rc;
@@ -1238,10 +1320,31 @@ int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_
     }
     if (pair) {
         const int64_t tiles = gemm_tiles(p, 256);
-        const int64_t pairs = tiles < g_pair_clusters ? tiles : g_pair_clusters;
+        // Split-K when the tiles would keep at most half the CTA pairs busy (small M and N):
+        // the tiles' super-blocks are cut into up to four ranges so that more pairs share the
+        // dequantisation and the MMAs, and a reduction adds the ranges in order.  Not with
+        // the SwiGLU epilogue, and not for fused_only callers (the partials are scratch).
+        const char* sk_env = getenv("FH3CUDA_GEMM_SPLITK");
+        const int nsb = static_cast<int>(w->in / fh3::kQ4KBlock);
+        int ksplit = 1;
+        if (!fused_only && epi != FH3CUDA_EPI_SWIGLU && !(sk_env && strcmp(sk_env, "0") == 0) && tiles * 2 <= g_pair_clusters)
+            ksplit = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({g_pair_clusters / tiles, nsb / 2, 4})));
+        Params pk = p;
+        if (ksplit > 1) {
+            pk.ksplit = ksplit;
+            pk.part = static_cast<float*>(scratch(c, 16, static_cast<size_t>(ksplit) * n_tok * p.n_out * 4, s));
+            if (!pk.part) return FH3_E_NOMEM;
+        }
+        const int64_t units = tiles * pk.ksplit;
+        const int64_t pairs = units < g_pair_clusters ? units : g_pair_clusters;
         cudaLaunchAttribute at[2];
         cudaLaunchConfig_t cfg = pair_config(at, pairs, kThreadsPair, two::SMEM_BYTES, s);
-        return check_cuda(cudaLaunchKernelEx(&cfg, gemm_q4k_pair_kernel, tmA, tmW, p), "gemm_q4k_pair_kernel launch");
+        rc = check_cuda(cudaLaunchKernelEx(&cfg, gemm_q4k_pair_kernel, tmA, tmW, pk), "gemm_q4k_pair_kernel launch");
+        if (rc || pk.ksplit == 1) return rc;  // whole tiles: the epilogue wrote y
+        const int64_t total = n_tok * p.n_out;
+        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 8));
+        splitk_reduce_kernel<<<blocks, 256, 0, s>>>(pk.part, ksplit, n_tok, p.n_out, bias, gate, y, ldy, epi);
+        return check_cuda(cudaGetLastError(), "splitk_reduce_kernel launch");
     }
     const int64_t tiles = gemm_tiles(p, 128);
     const int grid = static_cast<int>(tiles < ctx_sms(c) ? tiles : ctx_sms(c));

@@ -250,7 +250,10 @@ FH3CUDA_API int fh3cuda_gemm_bf16w_dev(const void *w_bf16, int64_t out, int64_t 
  * fused kernels, 2 from 2048 rows on, where the weights are first expanded to a
  * bf16 copy (the same bf16 values the fused dequantisers produce) and a TMA-fed
  * bf16 pair kernel runs the tiles.  FH3CUDA_GEMM_KERNEL=2sm / 1sm / two-pass in the
- * environment forces a path. */
+ * environment forces a path.  A call whose tiles would keep at most half of the CTA
+ * pairs busy (small n_tok and out, not SwiGLU) splits each tile's K range on the fused
+ * pair kernel and adds one reduction launch, not counted here
+ * (FH3CUDA_GEMM_SPLITK=0 keeps whole tiles). */
 FH3CUDA_API int fh3cuda_gemm_launches(int64_t n_tok);
 
 /* fp32 -> bf16 (round to nearest even), n elements. */
