@@ -536,9 +536,18 @@ def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100, cpu
 
     A sleep kernel holds the stream while the host queues `reps` calls, so the CUDA events
     bracket GPU time only (each call's launches, chained by programmatic dependent launch).
-    GB/s counts the algorithmic bytes of one call: Q4_K weights + x + y."""
+    GB/s counts the algorithmic bytes of one call: Q4_K weights + x + y.  Each entry also
+    carries the second fraction the hot-path contract asks for at M = 4 and 16, where a GEMV
+    has 3.6 M flop per byte: 2 M K N flop per call against the fp32 CUDA-core FMA rate (the
+    rate an fp32 dequantise-and-FMA GEMV is bound by; the kernels here use exact-operand
+    tensor-core MMAs instead, so it is a comparison, not their own ceiling)."""
     import math
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    sm_mhz = float(load_peaks()[0].get("sm_max_mhz") or 1965.0)
+    fp32_tflops = sms * 128 * 2 * sm_mhz * 1e6 / 1e12
     out = {"unit": "GB/s", "peak": hbm_gbs, "peak_source": f"{peak_src} hbm_gbs", "reps": reps,
+           "fp32_core_peak_tflops": round(fp32_tflops, 1),
+           "fp32_core_peak_source": f"nominal: {sms} SMs x 128 fp32 lanes x 2 flop x {sm_mhz:.0f} MHz max SM clock",
            "method": "sleep-held stream, CUDA events around back-to-back calls, weights rotated > L2",
            "cpu_threads": cpu_threads,
            "cpu_method": "fh3_matmul on the host, best of 5 calls after one warm-up (bench_matmul.c:76-94)",
@@ -562,8 +571,10 @@ def measure_gemv(fh3, torch, hbm_gbs: float, peak_src: str, reps: int = 100, cpu
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1000.0 / reps
             gbs = (wbytes + 4 * M * (K + N)) / us / 1e3
+            tflops = 2.0 * M * K * N / us / 1e6
             entry = {"in": K, "out": N, "tokens": M, "kernel": gemv_kernel_name(K, N, M),
-                     "us_per_call": round(us, 2), "achieved": round(gbs, 1), "frac": round(gbs / hbm_gbs, 4)}
+                     "us_per_call": round(us, 2), "achieved": round(gbs, 1), "frac": round(gbs / hbm_gbs, 4),
+                     "tflops": round(tflops, 2), "fp32_core_frac": round(tflops / fp32_tflops, 4)}
             if cpu_threads:
                 cus, kind = cpu_gemv_us(K, N, M)
                 entry.update({"cpu_us": round(cus, 1), "cpu_kind": kind})
