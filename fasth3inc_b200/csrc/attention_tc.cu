@@ -1,23 +1,26 @@
 // attention_tc.cu -- dense attention (fh3_attention, src/core/fh3_ops.c:587-695) on the
 // 5th-generation tensor cores: head_dim 128, bf16 q/k/v, fp32 softmax and accumulation.
 //
-// A CTA owns 128 query rows of one head and walks the keys in tiles of 128:
+// A CTA owns 256 query rows of one head as two tiles of 128 (A and B) and walks the keys
+// in tiles of 128; for each query tile:
 //   S_j = Q K_j^T      tcgen05.mma (M 128, N 128, K 128) into a TMEM score tile
 //   P_j = exp2(S_j c - m)   softmax warpgroup: thread i owns query row i (TMEM lane i),
-//                      reads its 128 scores with tcgen05.ld, writes P_j as bf16 into
-//                      shared memory in the K-major 128-byte-swizzle layout
-//   O += P_j V_j       tcgen05.mma (M 128, N 128, K 128) accumulating in a TMEM output
-//                      tile across the key walk
+//                      reads its 128 scores with tcgen05.ld and writes P_j back as bf16
+//                      pairs into the first 64 columns of its score tile
+//   O += P_j V_j       tcgen05.mma (M 128, N 128, K 128) with P taken from tensor memory,
+//                      accumulating in a TMEM output tile across the key walk
 // P_j is taken against a reference max that is raised only when a tile's row max exceeds
 // it by more than 2^8 (then the row of O in TMEM and its sum are rescaled once), so O
-// stays in tensor memory.  Score tiles are double-buffered in TMEM, so S_{j+1} and
-// P_{j-1} V_{j-1} run on the tensor cores while the softmax of tile j runs.
+// stays in tensor memory.  TMEM: S_A 0, S_B 128, O_A 256, O_B 384.  MMA issue order per
+// key tile: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): the tensor cores run one group's
+// products while the other group's softmax runs, and every S commit also covers the PV
+// that read the same columns before.
 // V is transposed once per call (vt[h][d][key]) so that both products take K-major
 // operands, the layout TMA's 128-byte swizzle writes.
 //
 // Warps: 0 TMA producer (Q once, then K_j and V_j^T tiles, two stages), 1 TMEM owner and
-// MMA issuer, 2-5 softmax / epilogue.  Every mbarrier wait is bounded (common.cuh); on a
-// timeout the roles stop, the MMAs issued so far retire before TMEM is freed, and the
+// MMA issuer, 2-5 group A, 6-9 group B.  Every mbarrier wait is bounded (common.cuh); on
+// a timeout the roles stop, the MMAs issued so far retire before TMEM is freed, and the
 // producer lets its copies in flight land.  No TMA multicast.
 #include <algorithm>
 #include <cstdlib>
@@ -28,22 +31,11 @@
 namespace {
 
 constexpr int kTcHD = 128;              // head_dim
-constexpr int kTcRows = 128;            // query rows a CTA
+constexpr int kTcRows = 128;            // query rows a tile (two tiles a CTA)
 constexpr int kTcKeys = 128;            // keys a tile
 constexpr int kBlk = 128 * 64 * 2;      // one [128 rows][64 bf16] 128-byte-swizzle block: 16 KB
 constexpr int kTile = 2 * kBlk;         // [128][128] bf16 operand: 32 KB
-constexpr int OFF_Q = 0;
-constexpr int OFF_KV = OFF_Q + kTile;           // 2 stages x (K tile, V^T tile)
-constexpr int OFF_P = OFF_KV + 2 * 2 * kTile;   // 2 P buffers
-constexpr int OFF_BAR = OFF_P + 2 * kTile;
-// q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full[2], o_empty[2], drain
-constexpr int kTcBars = 1 + 2 * 8 + 1;
-constexpr int OFF_MISC = OFF_BAR + kTcBars * 8;
-constexpr int kTcSmem = OFF_MISC + 64 + 1024;
-constexpr int kTcThreads = 6 * 32;
-constexpr uint32_t kTmemCols = 512;    // S0 S1 at 0 and 128, O at 256 (power-of-two allocation)
-constexpr uint32_t kTmemO = 256;
-static_assert(kTcSmem <= 232448, "shared memory budget");
+constexpr uint32_t kTmemCols = 512;    // S_A, S_B, O_A, O_B: 128 columns each
 
 // vt[c][tok] = v[tok][c] (c = h*128 + d) in 64 x 64 tiles of 16-byte accesses (the entry
 // point checks that v is 16-byte aligned and ldv a multiple of 8).  grid (ceil(n/64),
@@ -53,303 +45,6 @@ __global__ void __launch_bounds__(256) vt_transpose_kernel(const __nv_bfloat16* 
     fh3::transpose64_bf16(v, ldv, [](int p) { return p; }, blockIdx.y * 64, blockIdx.x * 64, n, vt, ldt);
 }
 
-struct Bars {
-    uint64_t *q_full, *kv_full, *kv_empty, *s_full, *s_empty, *p_full, *p_empty, *o_full, *o_empty, *drain;
-};
-
-__device__ __forceinline__ Bars tc_bars(uint8_t* smem) {
-    uint64_t* b = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-    Bars x;
-    x.q_full = b;
-    x.kv_full = b + 1;
-    x.kv_empty = b + 3;
-    x.s_full = b + 5;
-    x.s_empty = b + 7;
-    x.p_full = b + 9;
-    x.p_empty = b + 11;
-    x.o_full = b + 13;
-    x.o_empty = b + 15;
-    x.drain = b + 17;
-    return x;
-}
-
-// byte offset of 16-byte chunk `ch` (0..15 over 128 keys) of row r in a [128][128] bf16
-// K-major operand made of two 128-byte-swizzle blocks
-__device__ __forceinline__ uint32_t p_off(int r, int ch) {
-    return static_cast<uint32_t>((ch >> 3) * kBlk + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
-}
-
-}  // namespace
-
-namespace {
-
-template <bool OUT_BF16>
-__global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(
-    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-    const __grid_constant__ CUtensorMap tmVt, void* __restrict__ o, int64_t ldo, int n, float scale_log2,
-    int* status) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const Bars B = tc_bars(smem);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y;
-    const int q0 = blockIdx.x * kTcRows;
-    const int T = (n + kTcKeys - 1) / kTcKeys;
-
-    if (threadIdx.x == 0) {
-        fh3::mbar_init(B.q_full, 1);
-        for (int i = 0; i < 2; ++i) {
-            fh3::mbar_init(&B.kv_full[i], 1);
-            fh3::mbar_init(&B.kv_empty[i], 1);
-            fh3::mbar_init(&B.s_full[i], 1);
-            fh3::mbar_init(&B.s_empty[i], 4);
-            fh3::mbar_init(&B.p_full[i], 4);
-            fh3::mbar_init(&B.p_empty[i], 1);
-            fh3::mbar_init(&B.o_full[i], 1);
-        }
-        fh3::mbar_init(B.drain, 1);
-        *abort_flag = 0;
-        fh3::fence_mbar_init();
-    }
-    if (warp == 1) {
-        fh3::tmem_alloc(tmem_slot, kTmemCols);
-        fh3::tmem_relinquish();
-    }
-    if (warp == 0 && lane == 0) {
-        fh3::tma_prefetch_desc(&tmQ);
-        fh3::tma_prefetch_desc(&tmK);
-        fh3::tma_prefetch_desc(&tmVt);
-    }
-    fh3::tc_fence_before();
-    __syncthreads();
-    fh3::tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            uint32_t filled = 0, par = 0;
-            fh3::mbar_arrive_expect_tx(B.q_full, kTile);
-            for (int c = 0; c < 2; ++c)
-                fh3::tma_load_2d(smem + OFF_Q + c * kBlk, &tmQ, B.q_full, h * kTcHD + c * 64, q0);
-            bool ok = true;
-            for (int j = 0; j < T && ok; ++j) {
-                const int st = j & 1;
-                if (!(ok = fh3::mbar_wait<true>(&B.kv_empty[st], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
-                uint8_t* kvb = smem + OFF_KV + st * 2 * kTile;
-                fh3::mbar_arrive_expect_tx(&B.kv_full[st], 2 * kTile);
-                for (int c = 0; c < 2; ++c) {
-                    fh3::tma_load_2d(kvb + c * kBlk, &tmK, &B.kv_full[st], h * kTcHD + c * 64, j * kTcKeys);
-                    fh3::tma_load_2d(kvb + kTile + c * kBlk, &tmVt, &B.kv_full[st], j * kTcKeys + c * 64, h * kTcHD);
-                }
-                filled |= 1u << st;
-                par = (par & ~(1u << st)) | (static_cast<uint32_t>((j >> 1) & 1) << st);
-            }
-            volatile int no_abort = 0;
-            fh3::mbar_wait<true>(B.q_full, 0, &no_abort, nullptr);  // Q lands before the CTA can leave
-            if (!ok)
-                for (int i = 0; i < 2; ++i)
-                    if (filled & (1u << i)) fh3::mbar_wait<true>(&B.kv_full[i], (par >> i) & 1u, &no_abort, nullptr);
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = fh3::idesc_bf16_f32(128, 128);
-            const uint32_t qa = fh3::smem_u32(smem + OFF_Q);
-            bool ok = fh3::mbar_wait<true>(B.q_full, 0, abort_flag, status);
-            // O += P_i V_i (the output tile accumulates across key tiles)
-            auto pv = [&](int i) {
-                const int bi = i & 1;
-                if (!(ok = fh3::mbar_wait<true>(&B.p_full[bi], (i >> 1) & 1, abort_flag, status))) return;
-                fh3::tc_fence_after();
-                const uint32_t pa = fh3::smem_u32(smem + OFF_P + bi * kTile);
-                const uint32_t va = fh3::smem_u32(smem + OFF_KV + bi * 2 * kTile + kTile);
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        fh3::umma_f16(tmem + kTmemO, fh3::sdesc_sw128(pa + c * kBlk) + 2 * kk,
-                                      fh3::sdesc_sw128(va + c * kBlk) + 2 * kk, idesc, (i | c | kk) != 0 ? 1u : 0u);
-                fh3::umma_commit(B.o_full);
-                fh3::umma_commit(&B.p_empty[bi]);
-                fh3::umma_commit(&B.kv_empty[bi]);  // K_i and V_i are both consumed
-            };
-            for (int j = 0; j < T && ok; ++j) {
-                const int b = j & 1;
-                if (!(ok = fh3::mbar_wait<true>(&B.kv_full[b], (j >> 1) & 1, abort_flag, status))) break;
-                if (!(ok = fh3::mbar_wait<true>(&B.s_empty[b], ((j >> 1) & 1) ^ 1u, abort_flag, status))) break;
-                fh3::tc_fence_after();
-                const uint32_t ka = fh3::smem_u32(smem + OFF_KV + b * 2 * kTile);
-                const uint32_t d = tmem + b * 128;
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        fh3::umma_f16(d, fh3::sdesc_sw128(qa + c * kBlk) + 2 * kk,
-                                      fh3::sdesc_sw128(ka + c * kBlk) + 2 * kk, idesc, (c | kk) != 0 ? 1u : 0u);
-                fh3::umma_commit(&B.s_full[b]);
-                if (j >= 1) pv(j - 1);
-            }
-            if (ok) pv(T - 1);
-            fh3::umma_commit(B.drain);  // every MMA issued retires before TMEM is freed
-            volatile int no_abort = 0;
-            fh3::mbar_wait<true>(B.drain, 0, &no_abort, nullptr);
-        }
-    } else {
-        // ------------------------------------------------------------ softmax and epilogue (warps 2-5)
-        // P_j = 2^(s - m_ref) against a reference max m_ref that is raised only when a tile's
-        // max exceeds it by more than 2^8: then O (in TMEM) and the row sum l are rescaled
-        // once; otherwise P <= 256 and O, l stay consistent with m_ref.
-        const int qw = warp & 3;  // TMEM lanes 32*qw .. 32*qw+31 belong to this warp
-        const int r = qw * 32 + lane;
-        const uint32_t trow = tmem + (static_cast<uint32_t>(qw * 32) << 16);
-        float m_ref = -INFINITY, l = 0.0f;
-        bool ok = true;
-        auto wait_warp = [&](uint64_t* bar, uint32_t parity) {
-            int w = 1;
-            if (lane == 0) w = fh3::mbar_wait<true>(bar, parity, abort_flag, status);
-            return __shfl_sync(0xffffffffu, w, 0) != 0;
-        };
-        for (int j = 0; j < T && ok; ++j) {
-            const int b = j & 1;
-            if (!(ok = wait_warp(&B.s_full[b], (j >> 1) & 1))) break;
-            fh3::tc_fence_after();
-            const int kb = j * kTcKeys;
-            uint32_t v[4][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) fh3::tmem_ld32(trow + b * 128 + c * 32, v[c]);
-            fh3::tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) fh3::tmem_regs_ready(v[c]);
-            // row max of the raw scores (the scale is positive); keys past n only in the last tile
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (kb + kTcKeys <= n) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
-            } else {
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        if (kb + c * 32 + e >= n) v[c][e] = __float_as_uint(-INFINITY);
-                        mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
-                    }
-            }
-            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
-            const bool raise = mx > m_ref + 8.0f;  // always true on the first tile
-            if (j > 0 && __any_sync(0xffffffffu, raise)) {
-                // rescale this warp's rows of O once PV_{j-1} has landed (PV_j waits for our P_j)
-                if (!(ok = wait_warp(B.o_full, (j - 1) & 1))) break;
-                fh3::tc_fence_after();
-                const float a = raise ? exp2f(m_ref - mx) : 1.0f;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t ov[32];
-                    fh3::tmem_ld32(trow + kTmemO + c * 32, ov);
-                    fh3::tmem_ld_wait();
-                    fh3::tmem_regs_ready(ov);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
-                    fh3::tmem_st32(trow + kTmemO + c * 32, ov);
-                }
-                fh3::tmem_st_wait();
-                l *= a;
-            }
-            if (raise) m_ref = mx;
-            if (!(ok = wait_warp(&B.p_empty[b], ((j >> 1) & 1) ^ 1u))) break;  // P_{j-2} consumed
-            uint8_t* pb = smem + OFF_P + b * kTile;
-            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            const float nm = -m_ref;
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int e = 8 * t + 2 * u;
-                        const float p0 = exp2f(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
-                        const float p1 = exp2f(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
-                        rs4[u] += p0 + p1;
-                        const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                        pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
-                    }
-                    *reinterpret_cast<uint4*>(pb + p_off(r, c * 4 + t)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                }
-            fh3::tc_fence_before();         // this warp's TMEM reads and writes are complete
-            fh3::fence_proxy_async_smem();  // P_j visible to the tensor cores
-            __syncwarp();
-            if (lane == 0) {
-                fh3::mbar_arrive(&B.s_empty[b]);
-                fh3::mbar_arrive(&B.p_full[b]);
-            }
-            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-        }
-        if (ok) ok = wait_warp(B.o_full, (T - 1) & 1);  // the last PV has landed
-        const int row = q0 + r;
-        if (ok) {
-            fh3::tc_fence_after();
-            uint32_t ov[4][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) fh3::tmem_ld32(trow + kTmemO + c * 32, ov[c]);
-            fh3::tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) fh3::tmem_regs_ready(ov[c]);
-            if (row < n) {
-                const float inv = 1.0f / l;
-                const int64_t base = static_cast<int64_t>(row) * ldo + static_cast<int64_t>(h) * kTcHD;
-                if (OUT_BF16) {
-                    __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(o) + base;
-#pragma unroll
-                    for (int d = 0; d < kTcHD; d += 8) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int e = d + 2 * u;
-                            const __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(ov[e >> 5][e & 31]) * inv,
-                                                                            __uint_as_float(ov[(e + 1) >> 5][(e + 1) & 31]) * inv);
-                            w[u] = *reinterpret_cast<const uint32_t*>(&pp);
-                        }
-                        *reinterpret_cast<uint4*>(ob + d) = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                } else {
-                    float* of = static_cast<float*>(o) + base;
-#pragma unroll
-                    for (int d = 0; d < kTcHD; d += 4)
-                        *reinterpret_cast<float4*>(of + d) = make_float4(
-                            __uint_as_float(ov[d >> 5][d & 31]) * inv, __uint_as_float(ov[d >> 5][(d & 31) + 1]) * inv,
-                            __uint_as_float(ov[d >> 5][(d & 31) + 2]) * inv, __uint_as_float(ov[d >> 5][(d & 31) + 3]) * inv);
-                }
-            }
-        }
-    }
-
-    fh3::tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        fh3::tc_fence_after();
-        fh3::tmem_dealloc(tmem, kTmemCols);
-    }
-}
-
-}  // namespace
-
-namespace {
-
-// ---------------------------------------------------------------------------
-// Two query tiles a CTA (ping-pong).  A CTA owns 256 query rows of one head: tiles A and
-// B of 128 rows, each with its own softmax warpgroup, TMEM score tile and TMEM output
-// tile (S_A 0, S_B 128, O_A 256, O_B 384).  A group writes P_j as bf16 pairs into the
-// first 64 columns of its score tile, and O += P_j V_j takes P from tensor memory.  MMA
-// issue order per key tile: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): the tensor cores run
-// one group's products while the other group's softmax runs, and every S commit also
-// covers the PV that read the same columns before.
-// Warps: 0 TMA producer, 1 TMEM owner and MMA issuer, 2-5 group A, 6-9 group B.
-// ---------------------------------------------------------------------------
 constexpr int kPpRows = 256;
 constexpr int PP_OFF_QA = 0;
 constexpr int PP_OFF_QB = PP_OFF_QA + kTile;
@@ -687,45 +382,23 @@ int attention_tc(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, in
         enc(&tvt, vt, static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(rows), npad) != CUDA_SUCCESS)
         return set_error(FH3CUDA_E_CUDA, "attention: cuTensorMapEncodeTiled failed");
     const float scale_log2 = (1.0f / sqrtf(static_cast<float>(kTcHD))) * 1.4426950408889634f;
-    const char* kname = getenv("FH3CUDA_ATTN_KERNEL");
-    if (!(kname && strcmp(kname, "tc1") == 0)) {
-        // two query tiles a CTA (ping-pong); FH3CUDA_ATTN_KERNEL=tc1 keeps one tile a CTA
-        static bool attr_pp = false;
-        if (!attr_pp) {
-            rc = check_cuda(cudaFuncSetAttribute(attention_pp_kernel<false>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem),
-                            "attention_pp smem attribute");
-            if (!rc) rc = check_cuda(cudaFuncSetAttribute(attention_pp_kernel<true>,
-                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem),
-                                     "attention_pp smem attribute");
-            if (rc) return rc;
-            attr_pp = true;
-        }
-        const dim3 grid(static_cast<unsigned>((n + kPpRows - 1) / kPpRows), static_cast<unsigned>(heads));
-        if (o_bf16)
-            attention_pp_kernel<true><<<grid, kPpThreads, kPpSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2,
-                                                                       ctx_status(c));
-        else
-            attention_pp_kernel<false><<<grid, kPpThreads, kPpSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2,
-                                                                        ctx_status(c));
-        return check_cuda(cudaGetLastError(), "attention_pp_kernel launch");
-    }
     static bool attr = false;
     if (!attr) {
-        rc = check_cuda(cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kTcSmem), "attention_tc smem attribute");
-        if (!rc) rc = check_cuda(cudaFuncSetAttribute(attention_tc_kernel<true>,
-                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem),
-                                 "attention_tc smem attribute");
+        rc = check_cuda(cudaFuncSetAttribute(attention_pp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kPpSmem),
+                        "attention_pp smem attribute");
+        if (!rc) rc = check_cuda(cudaFuncSetAttribute(attention_pp_kernel<true>,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem),
+                                 "attention_pp smem attribute");
         if (rc) return rc;
         attr = true;
     }
-    const dim3 grid(static_cast<unsigned>((n + kTcRows - 1) / kTcRows), static_cast<unsigned>(heads));
+    const dim3 grid(static_cast<unsigned>((n + kPpRows - 1) / kPpRows), static_cast<unsigned>(heads));
     if (o_bf16)
-        attention_tc_kernel<true><<<grid, kTcThreads, kTcSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2, ctx_status(c));
+        attention_pp_kernel<true><<<grid, kPpThreads, kPpSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2, ctx_status(c));
     else
-        attention_tc_kernel<false><<<grid, kTcThreads, kTcSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2, ctx_status(c));
-    return check_cuda(cudaGetLastError(), "attention_tc_kernel launch");
+        attention_pp_kernel<false><<<grid, kPpThreads, kPpSmem, s>>>(tq, tk, tvt, o, ldo, n, scale_log2, ctx_status(c));
+    return check_cuda(cudaGetLastError(), "attention_pp_kernel launch");
 }
 
 }  // namespace fh3host

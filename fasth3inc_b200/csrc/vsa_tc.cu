@@ -8,23 +8,11 @@
 // (vsa_rows_kernel) and v transposed into VpT[h*128 + d][position] (vsa_vt_kernel).
 // Then a kept tile is one TMA box of K rows and one of V^T columns.
 //
-// vsa_tc64_kernel (the default, below): a CTA owns one query tile of one head in an
-// M = 64 MMA and walks its kept tiles two a step, one softmax warpgroup per tile of the
-// step, each with its own running max, sum and TMEM output, merged at the end.
-//
-// vsa_tc_kernel (FH3CUDA_VSA_KERNEL=tc128): a CTA owns one query tile (<= 64 rows) of one
-// head.  The tile's queries fill both halves of an M = 128 MMA and its kept key tiles are
-// walked two at a time: in chunk c, rows 0..63 take the keys of lst[2c] and rows 64..127
-// those of lst[2c+1]:
-//   S_c = Q K_c^T     (M 128, N 128, K 128) into one of two TMEM score tiles
-//   P_c               four softmax warps, one (query, half) row per thread, against a
-//                     reference max raised only when a chunk's max exceeds it by more
-//                     than 2^8 (that row of O in TMEM and its sum are then rescaled once)
-//   O += P_c V_c      (M 128, N 128, K 128) accumulating in TMEM; the P quadrants that
-//                     pair a row with the other half's keys are zero
-// then the two halves of each query (rows r and r + 64) are merged, coarse * gate is
-// added and rows are scattered back to token order.  The same roles, barrier protocol
-// and bounded waits as attention_tc.cu.
+// vsa_tc64_kernel: a CTA owns one query tile of one head in an M = 64 MMA and walks its
+// kept tiles two a step, one softmax warpgroup per tile of the step, each with its own
+// running max, sum and TMEM output, merged at the end; coarse * gate is added and rows
+// are scattered back to token order.  The roles, barrier protocol and bounded waits
+// follow attention_tc.cu.
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
@@ -105,331 +93,19 @@ __global__ void __launch_bounds__(256) vsa_vt_kernel(const __nv_bfloat16* __rest
 namespace {
 
 constexpr int kVB = 128 * 64 * 2;            // [128][64] bf16 128-byte-swizzle block: 16 KB
-constexpr int kVH = 64 * 64 * 2;             // a 64-row box inside such a block: 8 KB
-constexpr int kVT = 2 * kVB;                 // [128][128] operand: 32 KB
-constexpr int V_OFF_Q = 0;                   // Q: the query tile in rows 0..63 and again in 64..127
-constexpr int V_OFF_KV = V_OFF_Q + kVT;      // 2 stages: K [128 keys][128] + V^T [128][128 keys]
-constexpr int V_OFF_P = V_OFF_KV + 2 * 2 * kVT;
-constexpr int V_OFF_BAR = V_OFF_P + 2 * kVT;
-// q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full, drain
-constexpr int kVBars = 1 + 2 * 6 + 1 + 1;
-constexpr int V_OFF_MISC = V_OFF_BAR + kVBars * 8;
-constexpr int kVSmem = V_OFF_MISC + 64 + 1024;
-constexpr int kVThreads = 6 * 32;
-constexpr uint32_t kVTmemCols = 512;  // S0 at 0, S1 at 128, O at 256
-constexpr uint32_t kVTmemO = 256;
-static_assert(kVSmem <= 232448, "shared memory budget");
 
-// Chunk c pairs kept tiles lst[2c] (keys 0..63 of the chunk, used by query rows 0..63) and
-// lst[2c+1] (keys 64..127, used by the same queries repeated in rows 64..127); the P
-// quadrants that pair rows with the other tile's keys stay zero, so the output rows
-// 0..63 and 64..127 accumulate the two halves of the key walk, merged at the end.
-template <bool OUT_BF16>
-__global__ void __launch_bounds__(kVThreads, 1) vsa_tc_kernel(
-    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-    const __grid_constant__ CUtensorMap tmVt, const int* __restrict__ perm, const int* __restrict__ toff,
-    const int* __restrict__ poff, const int* __restrict__ sel, const int* __restrict__ selcnt, int nt,
-    const __nv_bfloat16* __restrict__ gate, int64_t ldg, const float* __restrict__ outc, int heads,
-    void* __restrict__ o, int64_t ldo, float scale_log2, int* status) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + V_OFF_BAR);
-    uint64_t* q_full = bar;
-    uint64_t* kv_full = bar + 1;
-    uint64_t* kv_empty = bar + 3;
-    uint64_t* s_full = bar + 5;
-    uint64_t* s_empty = bar + 7;
-    uint64_t* p_full = bar + 9;
-    uint64_t* p_empty = bar + 11;
-    uint64_t* o_full = bar + 13;
-    uint64_t* drain = bar + 14;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + V_OFF_MISC);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + V_OFF_MISC + 8);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i = blockIdx.x, h = blockIdx.y;
-    const size_t rowi = static_cast<size_t>(h) * nt + i;
-    const int* lst = sel + rowi * nt;
-    const int L = selcnt[rowi];            // >= 1
-    const int C = (L + 1) / 2;             // chunks
-    const int qrows = toff[i + 1] - toff[i];  // <= 64
-
-    // the P quadrants (rows 0..63, keys 64..127) and (rows 64..127, keys 0..63) of both buffers
-    // stay zero: block 1 rows 0..63 and block 0 rows 64..127
-    for (int e = threadIdx.x; e < 2 * 2 * 512; e += blockDim.x) {
-        const int buf = e >> 10, q = (e >> 9) & 1, off = (e & 511) * 16;
-        *reinterpret_cast<uint4*>(smem + V_OFF_P + buf * kVT + (q ? 0 : kVB) + (q ? 64 * 128 : 0) + off) =
-            make_uint4(0u, 0u, 0u, 0u);
-    }
-    fh3::fence_proxy_async_smem();
-    if (threadIdx.x == 0) {
-        fh3::mbar_init(q_full, 1);
-        for (int s = 0; s < 2; ++s) {
-            fh3::mbar_init(&kv_full[s], 1);
-            fh3::mbar_init(&kv_empty[s], 1);
-            fh3::mbar_init(&s_full[s], 1);
-            fh3::mbar_init(&s_empty[s], 4);
-            fh3::mbar_init(&p_full[s], 4);
-            fh3::mbar_init(&p_empty[s], 1);
-        }
-        fh3::mbar_init(o_full, 1);
-        fh3::mbar_init(drain, 1);
-        *abort_flag = 0;
-        fh3::fence_mbar_init();
-    }
-    if (warp == 1) {
-        fh3::tmem_alloc(tmem_slot, kVTmemCols);
-        fh3::tmem_relinquish();
-    }
-    fh3::tc_fence_before();
-    __syncthreads();
-    fh3::tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            uint32_t filled = 0, par = 0;
-            fh3::mbar_arrive_expect_tx(q_full, 4 * kVH);
-            for (int c = 0; c < 2; ++c)
-                for (int half = 0; half < 2; ++half)
-                    fh3::tma_load_2d(smem + V_OFF_Q + c * kVB + half * kVH, &tmQ, q_full, h * 128 + c * 64, poff[i]);
-            bool ok = true;
-            for (int cc = 0; cc < C && ok; ++cc) {
-                const int st = cc & 1;
-                const uint32_t ph = static_cast<uint32_t>((cc >> 1) & 1);
-                if (!(ok = fh3::mbar_wait<true>(&kv_empty[st], ph ^ 1u, abort_flag, status))) break;
-                // a chunk with one tile loads it twice; the second half is masked out
-                const int ya = poff[lst[2 * cc]], yb = poff[lst[min(2 * cc + 1, L - 1)]];
-                uint8_t* sb = smem + V_OFF_KV + st * 2 * kVT;
-                fh3::mbar_arrive_expect_tx(&kv_full[st], 2 * kVT);
-                for (int c = 0; c < 2; ++c) {
-                    fh3::tma_load_2d(sb + c * kVB, &tmK, &kv_full[st], h * 128 + c * 64, ya);
-                    fh3::tma_load_2d(sb + c * kVB + kVH, &tmK, &kv_full[st], h * 128 + c * 64, yb);
-                }
-                fh3::tma_load_2d(sb + kVT, &tmVt, &kv_full[st], ya, h * 128);
-                fh3::tma_load_2d(sb + kVT + kVB, &tmVt, &kv_full[st], yb, h * 128);
-                filled |= 1u << st;
-                par = (par & ~(1u << st)) | (ph << st);
-            }
-            volatile int no_abort = 0;
-            fh3::mbar_wait<true>(q_full, 0, &no_abort, nullptr);
-            if (!ok)
-                for (int s = 0; s < 2; ++s)
-                    if (filled & (1u << s)) fh3::mbar_wait<true>(&kv_full[s], (par >> s) & 1u, &no_abort, nullptr);
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = fh3::idesc_bf16_f32(128, 128);
-            const uint32_t qa = fh3::smem_u32(smem + V_OFF_Q);
-            bool ok = fh3::mbar_wait<true>(q_full, 0, abort_flag, status);
-            auto pv = [&](int cc) {
-                const int bi = cc & 1;
-                if (!(ok = fh3::mbar_wait<true>(&p_full[bi], (cc >> 1) & 1, abort_flag, status))) return;
-                fh3::tc_fence_after();
-                const uint32_t pa = fh3::smem_u32(smem + V_OFF_P + bi * kVT);
-                const uint32_t va = fh3::smem_u32(smem + V_OFF_KV + bi * 2 * kVT + kVT);
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        fh3::umma_f16(tmem + kVTmemO, fh3::sdesc_sw128(pa + c * kVB) + 2 * kk,
-                                      fh3::sdesc_sw128(va + c * kVB) + 2 * kk, idesc, (cc | c | kk) != 0 ? 1u : 0u);
-                fh3::umma_commit(o_full);
-                fh3::umma_commit(&p_empty[bi]);
-                fh3::umma_commit(&kv_empty[bi]);
-            };
-            for (int cc = 0; cc < C && ok; ++cc) {
-                const int b = cc & 1;
-                if (!(ok = fh3::mbar_wait<true>(&kv_full[b], (cc >> 1) & 1, abort_flag, status))) break;
-                if (!(ok = fh3::mbar_wait<true>(&s_empty[b], ((cc >> 1) & 1) ^ 1u, abort_flag, status))) break;
-                fh3::tc_fence_after();
-                const uint32_t ka = fh3::smem_u32(smem + V_OFF_KV + b * 2 * kVT);
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        fh3::umma_f16(tmem + b * 128, fh3::sdesc_sw128(qa + c * kVB) + 2 * kk,
-                                      fh3::sdesc_sw128(ka + c * kVB) + 2 * kk, idesc, (c | kk) != 0 ? 1u : 0u);
-                fh3::umma_commit(&s_full[b]);
-                if (cc >= 1) pv(cc - 1);
-            }
-            if (ok) pv(C - 1);
-            fh3::umma_commit(drain);
-            volatile int no_abort = 0;
-            fh3::mbar_wait<true>(drain, 0, &no_abort, nullptr);
-        }
-    } else {
-        // ------------------------------------------------------------ softmax, merge and epilogue (warps 2-5)
-        const int qw = warp & 3;          // TMEM lanes 32*qw .. 32*qw+31
-        const int half = qw >> 1;         // rows 0..63: the chunk's first tile; rows 64..127: its second
-        const int r = qw * 32 + lane;
-        const uint32_t trow = tmem + (static_cast<uint32_t>(qw * 32) << 16);
-        float m_ref = -INFINITY, lsum = 0.0f;
-        bool ok = true;
-        auto wait_warp = [&](uint64_t* bw, uint32_t parity) {
-            int w = 1;
-            if (lane == 0) w = fh3::mbar_wait<true>(bw, parity, abort_flag, status);
-            return __shfl_sync(0xffffffffu, w, 0) != 0;
-        };
-        for (int cc = 0; cc < C && ok; ++cc) {
-            const int b = cc & 1;
-            const int li = 2 * cc + half;
-            const int cnt = li < L ? toff[lst[li] + 1] - toff[lst[li]] : 0;  // valid keys of this half
-            if (!(ok = wait_warp(&s_full[b], (cc >> 1) & 1))) break;
-            fh3::tc_fence_after();
-            uint32_t v[2][32];
-            fh3::tmem_ld32(trow + b * 128 + half * 64, v[0]);
-            fh3::tmem_ld32(trow + b * 128 + half * 64 + 32, v[1]);
-            fh3::tmem_ld_wait();
-            fh3::tmem_regs_ready(v[0]);
-            fh3::tmem_regs_ready(v[1]);
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (cnt == 64) {  // a full tile: no masking
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
-            } else {
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        if (c * 32 + e >= cnt) v[c][e] = __float_as_uint(-INFINITY);  // other tiles' keys, padding
-                        mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
-                    }
-            }
-            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
-            const bool raise = mx > m_ref + 8.0f;  // false while a half-row has seen no key
-            if (cc > 0 && __any_sync(0xffffffffu, raise)) {
-                if (!(ok = wait_warp(o_full, (cc - 1) & 1))) break;  // the previous P V has landed
-                fh3::tc_fence_after();
-                const float a = raise ? exp2f(m_ref - mx) : 1.0f;  // 0 while this row's O is still empty
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t ov[32];
-                    fh3::tmem_ld32(trow + kVTmemO + c * 32, ov);
-                    fh3::tmem_ld_wait();
-                    fh3::tmem_regs_ready(ov);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * a);
-                    fh3::tmem_st32(trow + kVTmemO + c * 32, ov);
-                }
-                fh3::tmem_st_wait();
-                lsum *= a;
-            }
-            if (raise) m_ref = mx;
-            if (!(ok = wait_warp(&p_empty[b], ((cc >> 1) & 1) ^ 1u))) break;  // P_{cc-2} consumed
-            uint8_t* pb = smem + V_OFF_P + b * kVT + half * kVB;
-            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;  // no key seen yet: every p is 0
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int e = 8 * t + 2 * u;
-                        const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e]), scale_log2, nm));
-                        const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][e + 1]), scale_log2, nm));
-                        rs4[u] += p0 + p1;
-                        const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                        pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
-                    }
-                    const int ch = c * 4 + t;
-                    *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                }
-            lsum += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-            fh3::tc_fence_before();
-            fh3::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                fh3::mbar_arrive(&s_empty[b]);
-                fh3::mbar_arrive(&p_full[b]);
-            }
-        }
-        if (ok) ok = wait_warp(o_full, (C - 1) & 1);  // the last P V has landed (P buffers free)
-        uint32_t ov[4][32];
-        if (ok) {
-            fh3::tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) fh3::tmem_ld32(trow + kVTmemO + c * 32, ov[c]);
-            fh3::tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) fh3::tmem_regs_ready(ov[c]);
-        }
-        // merge the halves: rows 64..127 hand (m, l, O) to rows 0..63 through the P buffers
-        float* xch = reinterpret_cast<float*>(smem + V_OFF_P);  // [64][130]
-        if (half == 1 && ok) {
-            float* d = xch + (r - 64) * 130;
-            d[0] = m_ref;
-            d[1] = lsum;
-#pragma unroll
-            for (int e = 0; e < 128; ++e) d[2 + e] = __uint_as_float(ov[e >> 5][e & 31]);
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps, on every path
-        if (half == 0 && ok && r < qrows) {
-            const float* x = xch + r * 130;
-            const float mb = x[0], lb = x[1];
-            const float m = fmaxf(m_ref, mb);  // finite: the query's tiles hold keys
-            const float wa = m_ref == -INFINITY ? 0.0f : exp2f(m_ref - m);
-            const float wb = mb == -INFINITY ? 0.0f : exp2f(mb - m);
-            const float inv = 1.0f / (lsum * wa + lb * wb);
-            const int64_t t = perm[toff[i] + r];
-            const float* cb = gate ? outc + (static_cast<size_t>(i) * heads + h) * 128 : nullptr;
-            const int64_t col = static_cast<int64_t>(h) * 128;
-#pragma unroll
-            for (int d = 0; d < 128; d += 8) {
-                float w8[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    w8[u] = (__uint_as_float(ov[(d + u) >> 5][(d + u) & 31]) * wa + x[2 + d + u] * wb) * inv;
-                if (cb) {
-                    const uint4 g4 = *reinterpret_cast<const uint4*>(gate + t * ldg + col + d);
-                    const __nv_bfloat16* g8 = reinterpret_cast<const __nv_bfloat16*>(&g4);
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) w8[u] += cb[d + u] * __bfloat162float(g8[u]);
-                }
-                if (OUT_BF16) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const __nv_bfloat162 pp = __floats2bfloat162_rn(w8[2 * u], w8[2 * u + 1]);
-                        w[u] = *reinterpret_cast<const uint32_t*>(&pp);
-                    }
-                    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o) + t * ldo + col + d) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
-                } else {
-                    float* of = static_cast<float*>(o) + t * ldo + col + d;
-                    *reinterpret_cast<float4*>(of) = make_float4(w8[0], w8[1], w8[2], w8[3]);
-                    *reinterpret_cast<float4*>(of + 4) = make_float4(w8[4], w8[5], w8[6], w8[7]);
-                }
-            }
-        }
-    }
-
-    fh3::tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        fh3::tc_fence_after();
-        fh3::tmem_dealloc(tmem, kVTmemCols);
-    }
-}
-
-
-// M = 64 variant (the default): the query tile fills an M = 64 MMA once, so no tensor or
-// softmax work goes to duplicated rows.  Kept tiles go two a step (chunk c pairs tile
-// a = lst[2c] and tile b = lst[2c+1]; an odd last chunk repeats tile a with every key of
-// the copy masked):
+// The query tile fills an M = 64 MMA once, so no tensor or softmax work goes to
+// duplicated rows.  Kept tiles go two a step (chunk c pairs tile a = lst[2c] and tile
+// b = lst[2c+1]; an odd last chunk repeats tile a with every key of the copy masked):
 //   S_c = Q [K_a; K_b]^T   (M 64, N 128, K 128) into one of two TMEM score tiles
 //   P_a, P_b               two softmax warpgroups, A on the keys of tile a, B on those of
 //                          tile b, each with its own running max, sum and output
 //   O_A += P_a V_a, O_B += P_b V_b   (M 64, N 128, K 64 each) accumulating in TMEM
 // and at the end the two partial outputs of each query are merged (shared memory), with
-// the lazy 2^8 reference max of the other kernels.  Query row m of an M = 64 MMA sits in
-// TMEM lane (m % 16) + 32 (m / 16); the 16x32bx2 load shape gives lanes l and l + 16 of a
-// warp the same row, 32 keys each.  K and V^T have rings of their own (three 32 KB stages
+// the lazy reference max of attention_tc.cu (raised only when a tile's row max exceeds it
+// by more than 2^8, the row of O and its sum then rescaled once).  Query row m of an
+// M = 64 MMA sits in TMEM lane (m % 16) + 32 (m / 16); the 16x32bx2 load shape gives
+// lanes l and l + 16 of a warp the same row, 32 keys each.  K and V^T have rings of their own (three 32 KB stages
 // each): a K stage is released as soon as its S MMAs complete and a V^T stage when its
 // P V MMAs do, and the S and P V MMAs are issued by two threads, so a step's scores never
 // wait behind the previous step's P.  Two tiles a step halve the barrier round trips of a
@@ -852,11 +528,7 @@ int vsa_fine_tc(const int* perm, const int* toff, const int* sel, const int* sel
         return set_error(FH3CUDA_E_CUDA, "vsa: cuTensorMapEncodeTiled failed");
     static bool attr = false;
     if (!attr) {
-        rc = check_cuda(cudaFuncSetAttribute(vsa_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kVSmem),
-                        "vsa_tc smem attribute");
-        if (!rc) rc = check_cuda(cudaFuncSetAttribute(vsa_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                      kVSmem), "vsa_tc smem attribute");
-        if (!rc) rc = check_cuda(cudaFuncSetAttribute(vsa_tc64_kernel<false>,
+        rc = check_cuda(cudaFuncSetAttribute(vsa_tc64_kernel<false>,
                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kV6Smem),
                                  "vsa_tc64 smem attribute");
         if (!rc) rc = check_cuda(cudaFuncSetAttribute(vsa_tc64_kernel<true>,
@@ -867,25 +539,13 @@ int vsa_fine_tc(const int* perm, const int* toff, const int* sel, const int* sel
     }
     const float scale_log2 = (1.0f / sqrtf(128.0f)) * 1.4426950408889634f;
     const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(heads));
-    // FH3CUDA_VSA_KERNEL=tc128 selects the M = 128 kernel with duplicated query rows
-    const char* vk = getenv("FH3CUDA_VSA_KERNEL");
-    if (!(vk && strcmp(vk, "tc128") == 0)) {
-        if (o_bf16)
-            vsa_tc64_kernel<true><<<grid, kV6Threads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate,
-                                                                   ldg, outc, heads, o, ldo, scale_log2, ctx_status(c));
-        else
-            vsa_tc64_kernel<false><<<grid, kV6Threads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt,
-                                                                    gate, ldg, outc, heads, o, ldo, scale_log2,
-                                                                    ctx_status(c));
-        return check_cuda(cudaGetLastError(), "vsa_tc64_kernel launch");
-    }
     if (o_bf16)
-        vsa_tc_kernel<true><<<grid, kVThreads, kVSmem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate, ldg,
-                                                            outc, heads, o, ldo, scale_log2, ctx_status(c));
+        vsa_tc64_kernel<true><<<grid, kV6Threads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate, ldg,
+                                                               outc, heads, o, ldo, scale_log2, ctx_status(c));
     else
-        vsa_tc_kernel<false><<<grid, kVThreads, kVSmem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate, ldg,
-                                                             outc, heads, o, ldo, scale_log2, ctx_status(c));
-    return check_cuda(cudaGetLastError(), "vsa_tc_kernel launch");
+        vsa_tc64_kernel<false><<<grid, kV6Threads, kV6Smem, s>>>(tq, tk, tvt, perm, toff, poff, sel, selcnt, nt, gate,
+                                                                ldg, outc, heads, o, ldo, scale_log2, ctx_status(c));
+    return check_cuda(cudaGetLastError(), "vsa_tc64_kernel launch");
 }
 
 }  // namespace fh3host

@@ -292,8 +292,7 @@ FH3CUDA_API int fh3cuda_qk_norm_rope_dev(const void *src, int src_bf16, int64_t 
  * q[i*ldq + h*128 + d] (likewise k, v; o with ldo), so the thirds of a bf16
  * QKV output can be passed directly.  o is fp32 (o_bf16 = 0) or bf16.  Strides
  * multiples of 8, pointers 16-byte aligned.  Kernel: tcgen05 with two query tiles a
- * CTA by default; FH3CUDA_ATTN_KERNEL=tc1 (one tile a CTA) or mma (mma.sync) in the
- * environment selects another. */
+ * CTA. */
 FH3CUDA_API int fh3cuda_attention_dev(const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v,
                                       int64_t ldv, void *o, int o_bf16, int64_t ldo, int n, int heads,
                                       int head_dim, void *stream);
@@ -331,9 +330,8 @@ FH3CUDA_API int fh3cuda_vsa_num_tiles(const Fh3CudaSeq *seq, int tile, int *num_
  * bit-exact); their strides must be multiples of 8 and the pointers (q, k, v,
  * gate, o) 16-byte aligned.  With fp32 operands it runs in fp32 (the CPU
  * path's accuracy) and o must be fp32.  head_dim 64 or 128.  bf16 fine pass: tcgen05
- * with M = 64 query tiles by default (head_dim 128, tiles of at most 64 tokens);
- * FH3CUDA_VSA_KERNEL=tc128 (the query tile twice in an M = 128 MMA) or mma (mma.sync)
- * in the environment selects another. */
+ * with M = 64 query tiles (head_dim 128, tiles of at most 64 tokens), mma.sync
+ * otherwise; FH3CUDA_VSA_KERNEL=mma in the environment forces mma.sync. */
 FH3CUDA_API int fh3cuda_vsa_attention_dev(int tile, float sparsity, const Fh3CudaSeq *seq, const void *q,
                                           int64_t ldq, const void *k, int64_t ldk, const void *v, int64_t ldv,
                                           int in_bf16, const void *gate, int64_t ldg, void *o, int o_bf16,

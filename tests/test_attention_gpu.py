@@ -3,8 +3,8 @@
 The kernels take bf16 q/k/v (fp32 softmax and accumulation, P rounded to bf16 for the
 second product), so they are compared with fp32 computations on the SAME bf16-rounded inputs:
 the oracle (bitwise equal to the reference, tests/test_oracle.py) and torch's fp32
-attention.  Two kernels serve bf16 operands: tcgen05 (score and output tiles in tensor
-memory, the default) and mma.sync.  Tolerance: relative Frobenius error <= 1e-2 (the bf16
+attention.  The kernel for bf16 operands is tcgen05 (score and output tiles in tensor
+memory, two query tiles a CTA).  Tolerance: relative Frobenius error <= 1e-2 (the bf16
 operand bar of the chained block test); against the reference's own fp32-input case the
 input rounding is included, tolerance 2e-2.  fp32 operands run in fp32 at 1e-5."""
 from __future__ import annotations
@@ -16,18 +16,6 @@ from conftest import rel_fro
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
-
-
-@pytest.fixture(autouse=True, params=["tc", "tc1", "mma"])
-def attn_kernel(request, monkeypatch):
-    """Every bf16 test on every kernel: tcgen05 with two query tiles a CTA (the default),
-    tcgen05 with one query tile a CTA (FH3CUDA_ATTN_KERNEL=tc1) and the mma.sync flash
-    kernel (FH3CUDA_ATTN_KERNEL=mma)."""
-    if request.param == "tc":
-        monkeypatch.delenv("FH3CUDA_ATTN_KERNEL", raising=False)
-    else:
-        monkeypatch.setenv("FH3CUDA_ATTN_KERNEL", request.param)
-    return request.param
 
 
 def _bf16(a):

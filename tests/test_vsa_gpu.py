@@ -21,13 +21,12 @@ TOL = 1e-2      # bf16 operands
 TOL_F32 = 1e-5  # fp32 operands, the reference's bar
 
 
-@pytest.fixture(autouse=True, params=["tc", "tc128", "mma"])
+@pytest.fixture(autouse=True, params=["tc", "mma"])
 def vsa_kernel(request, monkeypatch):
-    """bf16 head_dim-128 cases on every fine pass: tcgen05 with an M = 64 query tile (tile-order
-    operands, TMEM tiles; the default for tiles of at most 64 tokens), tcgen05 with the query
-    tile repeated in an M = 128 MMA (FH3CUDA_VSA_KERNEL=tc128) and mma.sync
-    (FH3CUDA_VSA_KERNEL=mma)."""
-    if request.param in ("mma", "tc128"):
+    """bf16 head_dim-128 cases on both fine passes: tcgen05 with an M = 64 query tile
+    (tile-order operands, TMEM tiles; the default for tiles of at most 64 tokens) and
+    mma.sync (FH3CUDA_VSA_KERNEL=mma; the default for head_dim 64 and for larger tiles)."""
+    if request.param == "mma":
         monkeypatch.setenv("FH3CUDA_VSA_KERNEL", request.param)
     else:
         monkeypatch.delenv("FH3CUDA_VSA_KERNEL", raising=False)
