@@ -267,10 +267,18 @@ __device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int 
     using C = GtCfg<M>;
     const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     float am = 0.0f;
+    bool fin = true;  // false for an Inf or NaN element
 #pragma unroll
-    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(e[i]));
+    for (int i = 0; i < 8; ++i) {
+        am = fmaxf(am, fabsf(e[i]));
+        fin = fin && fabsf(e[i]) <= 3.40282347e38f;
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    // a non-finite x has no integer digits: the super-block's factor becomes NaN, so every
+    // output of the token is NaN (fh3_matmul gives a non-finite value there too: Inf times
+    // a weight, and 0 * Inf for a zero weight)
+    const bool all_fin = __all_sync(0xffffffffu, fin);
     // E with am < 2^E from the exponent field (subnormal am scaled up by 2^64 first)
     int E = 0;
     if (am > 0.0f && am <= 3.0e38f)
@@ -307,7 +315,8 @@ __device__ __forceinline__ void build_b(const float4& v0, const float4& v1, int 
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     float* sx = reinterpret_cast<float*>(smem + C::OFF_X) + (slot * M + t) * 8;
     if ((lane & 3) == 0) sx[lane >> 2] = sum;
-    if (lane == 0) reinterpret_cast<float*>(smem + C::OFF_FS)[slot * M + t] = pow2_exact(-s);
+    if (lane == 0)
+        reinterpret_cast<float*>(smem + C::OFF_FS)[slot * M + t] = all_fin ? pow2_exact(-s) : __int_as_float(0x7FC00000);
 }
 
 // B blocks of 6..16 tokens, once per call: block b (GtCfg<M>::SLOT_BYTES bytes) holds, for

@@ -171,3 +171,22 @@ def test_two_pass_equals_fused_bitwise(fh3, monkeypatch):
         outs[kern] = (y, yb, h, ys)
     for a, b in zip(outs["2sm"], outs["two-pass"]):
         assert torch.equal(a, b)
+
+
+def test_non_finite_activations(fh3, oracle):
+    """An Inf or NaN in a row of x makes every output of that row non-finite, as in
+    fh3_matmul; the other rows are unaffected (also through a split-K reduction)."""
+    import torch
+    K, N, M = 1280, 300, 40
+    raw = oracle.make_weights(seed=14, stream=1, rows=N, n=K)
+    x = oracle.rng_normal(14, 2, M * K).reshape(M, K).astype(np.float32)
+    x[3, 100] = np.inf
+    x[17, 1000] = np.nan
+    with np.errstate(invalid="ignore", over="ignore"):
+        ref = oracle.matmul(Q4K, raw, K, N, x)
+    got = fh3.matmul(_w(fh3, raw, K, N), torch.from_numpy(x).cuda()).cpu().numpy()
+    for r in range(M):
+        if r in (3, 17):
+            assert not np.isfinite(ref[r]).any() and not np.isfinite(got[r]).any(), r
+        else:
+            assert rel_fro(got[r], ref[r]) <= TOL, r

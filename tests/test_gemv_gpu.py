@@ -174,3 +174,27 @@ def test_fresh_weight_buffers_first_call(fh3, oracle):
             keep.append(W)
             got = fh3.gemv(W, torch.from_numpy(x).cuda()).cpu().numpy()
             assert rel_fro(got, ref) <= TOL, (M, trial)
+
+
+def test_non_finite_activations(fh3, oracle):
+    """An Inf or NaN activation makes every output of its token non-finite, as fh3_matmul's
+    fp32 sums do (Inf times a weight, and 0 * Inf = NaN for a zero weight); the other
+    tokens keep the usual accuracy."""
+    K, N = 1280, 70
+    w = oracle.make_weights(seed=13, stream=1, rows=N, n=K)
+    for M in (1, 3, 5, 8, 16):
+        x = oracle.rng_normal(13, M, M * K).reshape(M, K).astype(np.float32)
+        x[0, 300] = np.inf
+        bad = {0}
+        if M > 2:
+            x[2, 17] = np.nan
+            bad.add(2)
+        with np.errstate(invalid="ignore", over="ignore"):
+            ref = oracle.matmul(Q4K, w, K, N, x)
+        got = _run(fh3, w, K, N, x)
+        for t in range(M):
+            if t in bad:
+                assert not np.isfinite(ref[t]).any(), (M, t)  # the reference's own behaviour
+                assert not np.isfinite(got[t]).any(), (M, t)
+            else:
+                assert rel_fro(got[t], ref[t]) <= TOL, (M, t)
