@@ -70,10 +70,14 @@ struct Params {
     // bias), and splitk_reduce_kernel adds the ranges in order and applies the epilogue
     int ksplit = 1;
     float* part = nullptr;
-    // programmatic dependent launch (gemm_bf16_pair_kernel): 0 off; 1 the kernel may start
-    // while the previous kernel on its stream runs, and waits for it (griddepcontrol.wait)
-    // before its first global access; 2 the same, except that the weight tiles of the
-    // first stages are loaded before that wait (the caller guarantees the weights)
+    // programmatic dependent launch: 0 off; 1 the kernel may start while the previous
+    // kernel on its stream runs, and waits for it (griddepcontrol.wait) before its first
+    // access to activations, outputs, bias, gate or partials; 2 (gemm_bf16_pair_kernel)
+    // the same, except that the weight tiles of the first stages are loaded before that
+    // wait (the caller guarantees the weights).  gemm_q4k_pair_kernel with 1 loads and
+    // dequantises its Q4_K weights before the wait: no kernel of this library that lets
+    // its dependents start early writes Q4_K data (weights arrive by copies, and by
+    // kernels that run to completion before any dependent starts)
     int pdl = 0;
 };
 
@@ -577,6 +581,9 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
         sb0 = split * nsb / ksplit;
         sb1 = (split + 1) * nsb / ksplit;
     };
+    // the next kernel on this stream (the split-K reduction, the next call's conversion)
+    // may be scheduled now; it waits for this whole grid before touching its outputs
+    if (p.pdl) griddep_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < SA; ++i) { fh3::mbar_init(&a_full[i], 1); fh3::mbar_init(&a_empty[i], 1); }
@@ -609,6 +616,7 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
             Ring ra;
             uint32_t a_filled = 0, a_par = 0;
             bool ok = true;
+            if (p.pdl) griddep_wait();  // the activations are the previous kernel's output
             for (int64_t u = pair; u < num_units && ok; u += npairs) {
                 int64_t tile, mb, nb;
                 int split, sb0, sb1;
@@ -710,6 +718,7 @@ __global__ void __launch_bounds__(kThreadsPair, 1)
         const int q = warp & 3;
         const uint32_t acc_empty_leader = fh3::mapa_shared(fh3::smem_u32(acc_empty), 0);
         Ring racc;
+        if (p.pdl) griddep_wait();  // y, bias, gate and the partials belong to us after it
         for (int64_t u = pair; u < num_units; u += npairs) {
             int64_t tile, mb, nb;
             int split, sb0, sb1;
@@ -1076,6 +1085,9 @@ __global__ void __launch_bounds__(bfp::kThreads, 1)
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ksplit, int64_t M, int64_t N,
                                      const float* __restrict__ bias, const float* __restrict__ gate, void* y,
                                      int64_t ldy, int epi) {
+    // launched as a programmatic dependent of the GEMM: the partials are read after it
+    griddep_launch_dependents();
+    griddep_wait();
     const int64_t total = M * N;
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
          e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -1330,6 +1342,8 @@ int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_
         if (!fused_only && epi != FH3CUDA_EPI_SWIGLU && !(sk_env && strcmp(sk_env, "0") == 0) && tiles * 2 <= g_pair_clusters)
             ksplit = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({g_pair_clusters / tiles, nsb / 2, 4})));
         Params pk = p;
+        const char* pdl_env = getenv("FH3CUDA_GEMM_PDL");
+        pk.pdl = (pdl_env && strcmp(pdl_env, "0") == 0) ? 0 : 1;
         if (ksplit > 1) {
             pk.ksplit = ksplit;
             pk.part = static_cast<float*>(scratch(c, 16, static_cast<size_t>(ksplit) * n_tok * p.n_out * 4, s));
@@ -1338,13 +1352,24 @@ int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_
         const int64_t units = tiles * pk.ksplit;
         const int64_t pairs = units < g_pair_clusters ? units : g_pair_clusters;
         cudaLaunchAttribute at[2];
-        cudaLaunchConfig_t cfg = pair_config(at, pairs, kThreadsPair, two::SMEM_BYTES, s);
+        cudaLaunchConfig_t cfg = pair_config(at, pairs, kThreadsPair, two::SMEM_BYTES, s, pk.pdl != 0);
         rc = check_cuda(cudaLaunchKernelEx(&cfg, gemm_q4k_pair_kernel, tmA, tmW, pk), "gemm_q4k_pair_kernel launch");
         if (rc || pk.ksplit == 1) return rc;  // whole tiles: the epilogue wrote y
         const int64_t total = n_tok * p.n_out;
         const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 8));
-        splitk_reduce_kernel<<<blocks, 256, 0, s>>>(pk.part, ksplit, n_tok, p.n_out, bias, gate, y, ldy, epi);
-        return check_cuda(cudaGetLastError(), "splitk_reduce_kernel launch");
+        cudaLaunchConfig_t rcfg = {};
+        rcfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+        rcfg.blockDim = dim3(256, 1, 1);
+        rcfg.stream = s;
+        cudaLaunchAttribute ra[1];
+        ra[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        ra[0].val.programmaticStreamSerializationAllowed = 1;
+        rcfg.attrs = ra;
+        rcfg.numAttrs = pk.pdl ? 1 : 0;
+        return check_cuda(cudaLaunchKernelEx(&rcfg, splitk_reduce_kernel, static_cast<const float*>(pk.part), ksplit,
+                                             static_cast<int64_t>(n_tok), p.n_out, bias, gate, static_cast<void*>(y),
+                                             ldy, epi),
+                          "splitk_reduce_kernel launch");
     }
     const int64_t tiles = gemm_tiles(p, 128);
     const int grid = static_cast<int>(tiles < ctx_sms(c) ? tiles : ctx_sms(c));

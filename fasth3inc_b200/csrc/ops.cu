@@ -15,6 +15,9 @@
 namespace {
 
 __global__ void f32_to_bf16_kernel(const float4* __restrict__ x, uint2* __restrict__ y, int64_t n4) {
+    // a GEMM launched next as a programmatic dependent may start its prologue and weight
+    // loads now; it waits for this grid before it reads the converted activations
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const float4 v = x[i];
