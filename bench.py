@@ -54,7 +54,7 @@ def parse():
                     help="run each projection as one fh3cuda_gemm_q4k_dev call (no second stream)")
     ap.add_argument("--no-gemv", action="store_true",
                     help="skip the GEMV (1..4 token), q/k norm+rope and attention measurements")
-    ap.add_argument("--case", choices=["gemm", "gemv", "qk", "attn", "vsa", "norm"], default=None,
+    ap.add_argument("--case", choices=["gemm", "matmul", "gemv", "qk", "attn", "vsa", "norm"], default=None,
                     help="run one kernel's launches on a small case (for ncu) instead of the bench")
     ap.add_argument("--case-rows", type=int, default=8192, help="--case gemm / qk: activation rows")
     ap.add_argument("--case-kn", type=int, nargs=2, default=(5120, 13824), help="--case gemv: in, out")
@@ -802,6 +802,14 @@ def run_case(args):
         for _ in range(args.case_reps):
             fh3.gemm(w, x, fh3.EPI_SWIGLU, out=y)
         shape = {"rows": args.case_rows, "in": D_MODEL, "out": 2 * FFN, "epilogue": "swiglu"}
+    elif args.case == "matmul":
+        # BASELINE config 1's drop-in call: fh3cuda_matmul_dev on fp32 rows, W 5120 x 5120 Q4_K
+        ws = [fh3.make_weights(D_MODEL, D_MODEL, seed=i, stream_id=3) for i in range(args.case_reps)]
+        x = torch.randn((args.case_rows, D_MODEL), device="cuda")
+        y = torch.empty((args.case_rows, D_MODEL), device="cuda")
+        for w in ws:
+            fh3.matmul(w, x, out=y)
+        shape = {"rows": args.case_rows, "in": D_MODEL, "out": D_MODEL}
     elif args.case == "attn":
         H, Dh = 40, 128
         qkv = torch.randn((args.case_rows, 3 * H * Dh), device="cuda").to(torch.bfloat16)
