@@ -1081,7 +1081,10 @@ __global__ void __launch_bounds__(bfp::kThreads, 1)
 }
 
 // y = epilogue(sum over s of part[s] (+ bias)), the split-K ranges added in order: F32, BF16
-// or the gated residual h += gate * (sum + bias).  part is [ksplit][M][N] fp32.
+// or the gated residual h += gate * (sum + bias).  part is [ksplit][M][N] fp32.  VEC: four
+// consecutive elements a thread with 16-byte accesses (N and ldy multiples of 4, y, bias
+// and gate aligned), the same additions in the same order as the scalar form.
+template <bool VEC>
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ksplit, int64_t M, int64_t N,
                                      const float* __restrict__ bias, const float* __restrict__ gate, void* y,
                                      int64_t ldy, int epi) {
@@ -1089,17 +1092,61 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ksplit,
     griddep_launch_dependents();
     griddep_wait();
     const int64_t total = M * N;
-    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
-         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float v = __ldcg(part + e);
-        for (int sp = 1; sp < ksplit; ++sp) v += __ldcg(part + sp * total + e);
-        const int64_t m = e / N, n = e - m * N;
-        if (bias) v += bias[n];
-        if (epi == FH3CUDA_EPI_BF16) {
-            static_cast<__nv_bfloat16*>(y)[m * ldy + n] = __float2bfloat16_rn(v);
-        } else {
-            float* yy = static_cast<float*>(y) + m * ldy + n;
-            *yy = epi == FH3CUDA_EPI_RESID ? fmaf(gate[n], v, *yy) : v;
+    if constexpr (VEC) {
+        const int64_t t4 = total / 4;
+        for (int64_t e4 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e4 < t4;
+             e4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+            const int64_t e = 4 * e4;
+            float4 v = __ldcg(reinterpret_cast<const float4*>(part + e));
+            for (int sp = 1; sp < ksplit; ++sp) {
+                const float4 w = __ldcg(reinterpret_cast<const float4*>(part + sp * total + e));
+                v.x += w.x;
+                v.y += w.y;
+                v.z += w.z;
+                v.w += w.w;
+            }
+            const int64_t m = e / N, n = e - m * N;
+            if (bias) {
+                const float4 b = *reinterpret_cast<const float4*>(bias + n);
+                v.x += b.x;
+                v.y += b.y;
+                v.z += b.z;
+                v.w += b.w;
+            }
+            if (epi == FH3CUDA_EPI_BF16) {
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+                uint2 o;
+                o.x = *reinterpret_cast<const uint32_t*>(&lo);
+                o.y = *reinterpret_cast<const uint32_t*>(&hi);
+                *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(y) + m * ldy + n) = o;
+            } else {
+                float4* yy = reinterpret_cast<float4*>(static_cast<float*>(y) + m * ldy + n);
+                if (epi == FH3CUDA_EPI_RESID) {
+                    const float4 g = *reinterpret_cast<const float4*>(gate + n);
+                    float4 h = *yy;
+                    h.x = fmaf(g.x, v.x, h.x);
+                    h.y = fmaf(g.y, v.y, h.y);
+                    h.z = fmaf(g.z, v.z, h.z);
+                    h.w = fmaf(g.w, v.w, h.w);
+                    *yy = h;
+                } else {
+                    *yy = v;
+                }
+            }
+        }
+    } else {
+        for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+             e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+            float v = __ldcg(part + e);
+            for (int sp = 1; sp < ksplit; ++sp) v += __ldcg(part + sp * total + e);
+            const int64_t m = e / N, n = e - m * N;
+            if (bias) v += bias[n];
+            if (epi == FH3CUDA_EPI_BF16) {
+                static_cast<__nv_bfloat16*>(y)[m * ldy + n] = __float2bfloat16_rn(v);
+            } else {
+                float* yy = static_cast<float*>(y) + m * ldy + n;
+                *yy = epi == FH3CUDA_EPI_RESID ? fmaf(gate[n], v, *yy) : v;
+            }
         }
     }
 }
@@ -1356,7 +1403,12 @@ int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_
         rc = check_cuda(cudaLaunchKernelEx(&cfg, gemm_q4k_pair_kernel, tmA, tmW, pk), "gemm_q4k_pair_kernel launch");
         if (rc || pk.ksplit == 1) return rc;  // whole tiles: the epilogue wrote y
         const int64_t total = n_tok * p.n_out;
-        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 8));
+        auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+        const bool vec = p.n_out % 4 == 0 && ldy % 4 == 0 && al16(pk.part) && (!bias || al16(bias)) &&
+                         (epi != FH3CUDA_EPI_RESID || al16(gate)) &&
+                         (epi == FH3CUDA_EPI_BF16 ? (reinterpret_cast<uintptr_t>(y) & 7) == 0 : al16(y));
+        const int64_t work = vec ? total / 4 : total;
+        const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(ctx_sms(c)) * 8));
         cudaLaunchConfig_t rcfg = {};
         rcfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
         rcfg.blockDim = dim3(256, 1, 1);
@@ -1366,9 +1418,9 @@ int gemm_q4k(const Fh3CudaW* w, const void* x_bf16, int64_t ldx, void* y, int64_
         ra[0].val.programmaticStreamSerializationAllowed = 1;
         rcfg.attrs = ra;
         rcfg.numAttrs = pk.pdl ? 1 : 0;
-        return check_cuda(cudaLaunchKernelEx(&rcfg, splitk_reduce_kernel, static_cast<const float*>(pk.part), ksplit,
-                                             static_cast<int64_t>(n_tok), p.n_out, bias, gate, static_cast<void*>(y),
-                                             ldy, epi),
+        return check_cuda(cudaLaunchKernelEx(&rcfg, vec ? splitk_reduce_kernel<true> : splitk_reduce_kernel<false>,
+                                             static_cast<const float*>(pk.part), ksplit, static_cast<int64_t>(n_tok),
+                                             p.n_out, bias, gate, static_cast<void*>(y), ldy, epi),
                           "splitk_reduce_kernel launch");
     }
     const int64_t tiles = gemm_tiles(p, 128);
