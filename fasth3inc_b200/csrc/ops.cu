@@ -40,10 +40,20 @@ __global__ void f32_to_bf16_tail_kernel(const float* __restrict__ x, __nv_bfloat
 // inv = 1/sqrtf(mean + eps), v = x*inv*w, out = v*(1+scale) + shift -> bf16.
 constexpr int kNormThreads = 256;
 
+// The norms run between the trunk's GEMMs as programmatic dependents: the next GEMM may be
+// scheduled (and load its weights) at once, and this kernel reads x only after the previous
+// kernel has finished.  Writing y then is safe too: the kernel that last read y (the GEMM
+// before the previous one) finished before the previous kernel did.
+__device__ __forceinline__ void norm_griddep() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_modulate_kernel(
     const float* __restrict__ x, const float* __restrict__ nw, const float* __restrict__ shift,
     const float* __restrict__ scale, __nv_bfloat16* __restrict__ y, int dim, float eps) {
     __shared__ float red[kNormThreads / 32];
+    norm_griddep();
     const float* row = x + static_cast<int64_t>(blockIdx.x) * dim;
     __nv_bfloat16* out = y + static_cast<int64_t>(blockIdx.x) * dim;
     float ss = 0.0f;
@@ -74,6 +84,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_modulate_vec_kernel(
     const float4* __restrict__ x, const float4* __restrict__ nw, const float4* __restrict__ shift,
     const float4* __restrict__ scale, uint2* __restrict__ y, int dim4, float inv_dim, float eps) {
     __shared__ float red[kNormThreads / 32];
+    norm_griddep();
     const float4* row = x + static_cast<int64_t>(blockIdx.x) * dim4;
     uint2* out = y + static_cast<int64_t>(blockIdx.x) * dim4;
     float4 v[V];
@@ -438,19 +449,32 @@ extern "C" int fh3cuda_rmsnorm_modulate_dev(const float* x, const float* norm_w,
                      (reinterpret_cast<uintptr_t>(y_bf16) & 7) == 0;
     const int dim4 = dim / 4;
     const float inv_dim = 1.0f / static_cast<float>(dim);
-#define FH3_NORM_VEC(V)                                                                                         \
-    rmsnorm_modulate_vec_kernel<V><<<n, kNormThreads, 0, s>>>(                                                  \
-        reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(norm_w),                           \
-        reinterpret_cast<const float4*>(shift), reinterpret_cast<const float4*>(scale), static_cast<uint2*>(y_bf16), \
-        dim4, inv_dim, eps)
-    if (vec && dim4 <= 2 * kNormThreads) FH3_NORM_VEC(2);
-    else if (vec && dim4 <= 5 * kNormThreads) FH3_NORM_VEC(5);
-    else if (vec && dim4 <= 8 * kNormThreads) FH3_NORM_VEC(8);
+    // a programmatic dependent of the previous kernel (the kernels wait before reading x)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(n), 1, 1);
+    cfg.blockDim = dim3(kNormThreads, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const auto* x4 = reinterpret_cast<const float4*>(x);
+    const auto* w4 = reinterpret_cast<const float4*>(norm_w);
+    const auto* sh4 = reinterpret_cast<const float4*>(shift);
+    const auto* sc4 = reinterpret_cast<const float4*>(scale);
+    auto* y2 = static_cast<uint2*>(y_bf16);
+    cudaError_t e;
+    if (vec && dim4 <= 2 * kNormThreads)
+        e = cudaLaunchKernelEx(&cfg, rmsnorm_modulate_vec_kernel<2>, x4, w4, sh4, sc4, y2, dim4, inv_dim, eps);
+    else if (vec && dim4 <= 5 * kNormThreads)
+        e = cudaLaunchKernelEx(&cfg, rmsnorm_modulate_vec_kernel<5>, x4, w4, sh4, sc4, y2, dim4, inv_dim, eps);
+    else if (vec && dim4 <= 8 * kNormThreads)
+        e = cudaLaunchKernelEx(&cfg, rmsnorm_modulate_vec_kernel<8>, x4, w4, sh4, sc4, y2, dim4, inv_dim, eps);
     else
-        rmsnorm_modulate_kernel<<<n, kNormThreads, 0, s>>>(x, norm_w, shift, scale,
-                                                           static_cast<__nv_bfloat16*>(y_bf16), dim, eps);
-#undef FH3_NORM_VEC
-    return check_cuda(cudaGetLastError(), "rmsnorm_modulate launch");
+        e = cudaLaunchKernelEx(&cfg, rmsnorm_modulate_kernel, x, norm_w, shift, scale,
+                               static_cast<__nv_bfloat16*>(y_bf16), dim, eps);
+    return check_cuda(e, "rmsnorm_modulate launch");
 }
 
 extern "C" int fh3cuda_swiglu_dev(const float* in, float* out, int n, int F, void* stream) {
