@@ -81,27 +81,49 @@ class Clocks:
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
+        self.lines = []
+        self.t_region = 0.0
 
     def start(self):
+        """Start sampling and return once the first sample has arrived (nvidia-smi takes a
+        while to start), so that a short timed region is sampled too; samples that arrive
+        before this returns are not counted."""
+        import threading
+        self.lines = []
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+
+        def read():
+            for line in self.proc.stdout:
+                self.lines.append((time.time(), line))
+
+        self.reader = threading.Thread(target=read, daemon=True)
+        self.reader.start()
+        t0 = time.time()
+        while not self.lines and self.proc.poll() is None and time.time() - t0 < 5.0:
+            time.sleep(0.01)
+        self.t_region = time.time()
 
     def stop(self) -> dict:
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=10)
+            self.proc.wait(timeout=10)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+            self.proc.wait()
+        self.reader.join(timeout=5)
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for t, line in self.lines:
+            if t < self.t_region:
+                continue
             f = [c.strip() for c in line.split(",")]
             if len(f) < 8:
                 continue
@@ -271,10 +293,10 @@ def run_ours(args):
 
     # timed region
     clocks = Clocks(local)
+    clocks.start()  # returns once sampling runs; the barrier then lines the ranks up
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
     runner.gemm_events, runner.expand_events, runner.norm_events = [], [], []
     ag_events = []
     runner.launches = 0
