@@ -248,7 +248,9 @@ class Runner:
 
     def run(self, ops: list, tap=None) -> None:
         """Issue `ops` in order; two-pass GEMMs get their expansions one projection ahead.
-        No expansion starts before the main stream reaches this call."""
+        No expansion starts before the main stream reaches this call.  Besides "norm" and
+        "gemm", an op may be ("call", fn): fn(stream) issues other launches on the main stream
+        at that point of the sequence (for example converting the next input to bf16)."""
         import torch
         expanded = [i for i, op in enumerate(ops) if self._two_pass(op)]
         nxt = 0
@@ -258,6 +260,9 @@ class Runner:
             self.side.wait_event(start)
             self._expand(ops[expanded[0]][1], 0)
         for i, op in enumerate(ops):
+            if op[0] == "call":          # ("call", fn): fn(stream) issues its own launches, in order
+                op[1](self.stream)
+                continue
             if op[0] == "norm":
                 self._norm(op)
             elif nxt < len(expanded) and expanded[nxt] == i:
