@@ -22,6 +22,15 @@
  *   - Device-side waits inside the kernels are bounded; a wait that gives up
  *     records FH3CUDA_E_TIMEOUT in the device status word, read by
  *     fh3cuda_device_status().
+ *   - Stream order: the GEMV and GEMM kernels are launched as programmatic
+ *     dependents of the previous kernel on their stream and start reading
+ *     their Q4_K weights before that kernel has finished (activations, bias,
+ *     gate and outputs only after it).  Weights written by a copy, or by a
+ *     kernel that runs to completion before its dependents start (every
+ *     kernel of this library that writes weights does), are safe; weights
+ *     written by a foreign kernel that signals its dependents early
+ *     (griddepcontrol.launch_dependents) must be ordered with an event or a
+ *     synchronisation before the call.
  */
 #ifndef FH3CUDA_H
 #define FH3CUDA_H
