@@ -16,13 +16,15 @@ SOURCES = ["api.cu", "dequant.cu", "gemv.cu", "gemv_mma.cu", "gemv_tc.cu", "gemm
            "vsa.cu", "vsa_tc.cu", "trunk_io.cu", "dit.cu", "gen.cu", "noalloc.cu", "formats.cu"]
 HEADERS = ["common.cuh", "flash.cuh", "formats.cuh"]
 
-NVCC_FLAGS = [
+BUILD_DIR = os.path.join(PKG, "_build")   # one object per source (git- and gpurun-ignored)
+COMPILE_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-    "-shared", "-cudart", "static",
     "--expt-relaxed-constexpr",
 ]
+LINK_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart", "static"]
+NVCC_FLAGS = COMPILE_FLAGS + ["-shared", "-cudart", "static"]  # the one-command form, for reference
 
 
 def _nvcc() -> str:
@@ -41,19 +43,56 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> str:
-    """Compile every CUDA source into fasth3inc_b200/libfh3cuda.so."""
+def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None, jobs: int | None = None) -> str:
+    """Compile every CUDA source into fasth3inc_b200/libfh3cuda.so: one object per source,
+    compiled in parallel (only the sources, or all of them after a header or flag change,
+    whose objects are out of date), then one link."""
     if not force and not _stale():
         return LIB
-    cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), "-I", os.path.join(ROOT, "include"), "-o", LIB + ".tmp"]
-    cmd += [os.path.join(CSRC, f) for f in SOURCES]
+    from concurrent.futures import ThreadPoolExecutor
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    flags = [*COMPILE_FLAGS, *(extra or []), "-I", os.path.join(ROOT, "include")]
+    stamp = os.path.join(BUILD_DIR, "flags.txt")
+    sig = " ".join(flags)
+    same_flags = os.path.exists(stamp) and open(stamp).read() == sig
+    hdr = max(os.path.getmtime(p) for p in [os.path.join(CSRC, h) for h in HEADERS] +
+              [os.path.join(ROOT, "include", "fh3cuda.h")])
+    objs = [os.path.join(BUILD_DIR, os.path.splitext(f)[0] + ".o") for f in SOURCES]
+
+    def fresh(src, obj):
+        return (not force and same_flags and os.path.exists(obj) and
+                os.path.getmtime(obj) >= max(os.path.getmtime(src), hdr))
+
+    todo = [(os.path.join(CSRC, f), o) for f, o in zip(SOURCES, objs) if not fresh(os.path.join(CSRC, f), o)]
+
+    def compile_one(item):
+        src, obj = item
+        cmd = [_nvcc(), *flags, "-c", "-o", obj + ".tmp", src]
+        if verbose:
+            print(" ".join(cmd))
+        out = subprocess.run(cmd, capture_output=True, text=True)
+        if out.returncode != 0:
+            return src, out.stdout + out.stderr
+        os.replace(obj + ".tmp", obj)
+        return None, out.stdout + out.stderr
+
+    with ThreadPoolExecutor(max_workers=jobs or max(1, min(len(todo), os.cpu_count() or 1))) as ex:
+        results = list(ex.map(compile_one, todo))
+    errors = [(src, log) for src, log in results if src is not None]
+    if errors:
+        raise RuntimeError("nvcc failed:\n" + "\n".join(f"{src}:\n{log}" for src, log in errors))
+    if verbose:
+        for _, log in results:
+            if log:
+                print(log)
+    with open(stamp, "w") as f:
+        f.write(sig)
+    cmd = [_nvcc(), *LINK_FLAGS, "-o", LIB + ".tmp", *objs]
     if verbose:
         print(" ".join(cmd))
     out = subprocess.run(cmd, capture_output=True, text=True)
     if out.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + out.stdout + out.stderr)
-    if verbose and (out.stdout or out.stderr):
-        print(out.stdout + out.stderr)
+        raise RuntimeError("nvcc link failed:\n" + out.stdout + out.stderr)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 
