@@ -46,3 +46,42 @@ def test_split_k_matches_whole_tiles(fh3, oracle, monkeypatch, M, N, K):
     y = fh3.matmul(w, x32, bias)
     assert rel_fro(y.cpu().numpy(), oracle.matmul(12, raw, K, N, x32.cpu().numpy(), bias.cpu().numpy())) <= 5e-3
     assert fh3.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N", [(256, 1024), (96, 1024), (600, 4096), (2100, 1024)])
+def test_dependent_chain_queued_equals_synchronised(fh3, oracle, monkeypatch, M, N):
+    """GEMMs that consume the previous GEMM's output, queued back to back (each launched as a
+    programmatic dependent of the previous kernel, its weights loaded before the wait, the
+    split-K partials reused call after call) give the same bits as the same chain with a
+    synchronisation after every call.  Shapes: split-K (256 and 96 rows), whole tiles on the fused
+    kernel (600 x 4096), the two-pass path (2100 rows)."""
+    import torch
+    monkeypatch.delenv("FH3CUDA_GEMM_KERNEL", raising=False)
+    K = N
+    ws = [fh3.Q4KWeight.from_bytes(oracle.make_weights(seed=200 + i, stream=19, rows=N, n=K), K, N) for i in range(4)]
+    g = torch.Generator(device="cuda").manual_seed(M)
+    x = fh3.to_bf16(torch.randn((M, K), device="cuda", generator=g))
+    gate = torch.randn(N, device="cuda", generator=g)
+    h0 = torch.randn((M, N), device="cuda", generator=g)
+
+    def chain(sync):
+        h = h0.clone()
+        a = fh3.gemm(ws[0], x, fh3.EPI_BF16)
+        if sync:
+            torch.cuda.synchronize()
+        b = fh3.gemm(ws[1], a, fh3.EPI_BF16)            # reads the previous GEMM's output
+        if sync:
+            torch.cuda.synchronize()
+        fh3.gemm(ws[2], b, fh3.EPI_RESID, gate=gate, out=h)  # h += gate * (b W^T), in place
+        if sync:
+            torch.cuda.synchronize()
+        fh3.gemm(ws[3], fh3.to_bf16(h), fh3.EPI_RESID, gate=gate, out=h)
+        torch.cuda.synchronize()
+        return a, b, h
+
+    ref = chain(True)
+    for _ in range(3):
+        got = chain(False)
+        for r, t in zip(ref, got):
+            assert torch.equal(r, t)
+    assert fh3.device_status() == 0
