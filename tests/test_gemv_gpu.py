@@ -198,3 +198,31 @@ def test_non_finite_activations(fh3, oracle):
                 assert not np.isfinite(got[t]).any(), (M, t)
             else:
                 assert rel_fro(got[t], ref[t]) <= TOL, (M, t)
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_dependent_chain_queued_equals_synchronised(fh3, oracle, M):
+    """GEMVs whose x is the previous call's y, queued back to back (each launched as a
+    programmatic dependent of the previous kernel, its weights requested before the wait),
+    give the same bits as the same chain with a synchronisation after every call."""
+    import torch
+    dims = [1024, 2048, 1024, 1280, 1024]
+    ws = [fh3.Q4KWeight.from_bytes(oracle.make_weights(seed=300 + i, stream=1, rows=dims[i + 1], n=dims[i]),
+                                   dims[i], dims[i + 1]) for i in range(len(dims) - 1)]
+    x0 = torch.from_numpy(oracle.rng_normal(301, M, M * dims[0]).reshape(M, dims[0]).astype(np.float32)).cuda()
+    run = fh3.matmul if _PATH["kernel"] == "matmul" else fh3.gemv
+
+    def chain(sync):
+        outs, h = [], x0
+        for w in ws:
+            h = run(w, h)
+            outs.append(h)
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return outs
+
+    ref = chain(True)
+    for _ in range(2):
+        for a, b in zip(ref, chain(False)):
+            assert torch.equal(a, b)
