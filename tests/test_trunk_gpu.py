@@ -74,3 +74,32 @@ def test_rows_for_rank_partitions_rows():
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
             sizes = [b - a for a, b in spans]
             assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("M", [300, 2500])
+def test_queued_step_equals_stage_by_stage(fh3, M):
+    """The step queued as the bench runs it (norms and GEMMs chained by programmatic dependent
+    launch, every expansion on the side stream one projection ahead) gives the same bits as
+    the same launches with a synchronisation after every stage.  2500 rows take the two-pass
+    path with its overlapped expansions; 300 rows the fused kernels."""
+    import torch
+
+    from fasth3inc_b200.trunk import Runner, Trunk, Workspace
+    d, F, T = 512, 1024, 40
+    trunk = Trunk(d=d, F=F, n_blocks=2, seed=9).build()
+    ws = Workspace(M, T, d=d, F=F)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    h0 = torch.randn((M, d), device="cuda", generator=g)
+    text_bf = fh3.to_bf16(torch.randn((T, d), device="cuda", generator=g))
+    runner = Runner(trunk, ws)
+
+    h_sync = h0.clone()
+    for blk in trunk.blocks:
+        runner.block(blk, h_sync, text_bf, tap=lambda stage, t: torch.cuda.synchronize())
+    torch.cuda.synchronize()
+    for _ in range(2):
+        h = h0.clone()
+        runner.step(h, text_bf)
+        torch.cuda.synchronize()
+        assert torch.equal(h, h_sync)
+    assert fh3.device_status() == 0
