@@ -561,6 +561,8 @@ GEMV_SHAPES = ((5120, 13824), (13824, 5120), (5120, 5120))   # (in, out): fc-up,
 
 def gemv_kernel_name(K: int, N: int, M: int) -> str:
     """The kernel the default GEMV dispatch (csrc/gemv_mma.cu, gemv_mma) picks."""
+    if M == 1 and (K // 256) * 2180 <= 227 * 1024:
+        return "gemv_i8_kernel"
     if N <= K or M >= 5:
         return "gemv_tc_kernel (i8 A)" if M <= 5 else "gemv_tc_kernel (f16 A = sc*q) + gemv_xprep_kernel"
     if M <= 2:

@@ -631,6 +631,343 @@ __global__ void __launch_bounds__(kStreamWarps * 32, FH3_GV_STREAM_MIN_BLOCKS) g
 }
 
 // ---------------------------------------------------------------------------
+// 1 token on integer MMAs: the persistent stream-K walk of gemv_stream_kernel with the
+// dot products on mma.sync.m16n8k32 (u8 nibbles x s8 activation digits -> int32).
+//
+// * x of each super-block is rounded to an integer under a power of two 2^s
+//   (max|x| * 2^s < 2^22) and cut into three balanced signed base-256 digits.
+// * The nibbles enter as u8 as they lie in the bytes: low nibbles (w & 0x0F0F0F0F) are
+//   q, high nibbles (w & 0xF0F0F0F0) are 16 q; one AND per four weights.
+// * One MMA (K 32) takes positions 8tq..8tq+3 (a second one 8tq+4..8tq+7) of both
+//   sub-blocks of a 32-byte chunk c: k slots 4tq+r are the low-nibble sub-block 2c, slots
+//   16+4tq+r the high-nibble sub-block 2c+1.  B column g holds digit g of sub-block 2c
+//   (g < 3) or digit g-3 of sub-block 2c+1 (3 <= g < 6), zero in the other half and in
+//   columns 6, 7.  The chunk's accumulator so holds the six digit-plane sums of its two
+//   sub-blocks for rows g, g+8, exact; each is multiplied by its sub-block's 6-bit scale
+//   and summed over the chunks in int32 (|sum| < 2^28), converted once per super-block
+//   and scaled by d * 2^-s in fp32.  A lane's two accumulator columns keep the same digit
+//   and nibble half in every chunk, so their weights 256^p (and 1/16 for high nibbles)
+//   are applied once, when the tile's segment ends.
+// * The min term is one m16n8k16 fp16 MMA of the 6-bit mins (fp16 subnormals m * 2^-24)
+//   against the sub-block sums X_j of x * 2^(s-13) in two fp16 planes.
+// Shared memory (built by every CTA for the whole K after griddepcontrol.wait):
+//   digit fragments [nblk][4 chunks][32 lanes] uint4 | min-term fragments [nblk][32] u32 |
+//   factors 2^-s [nblk] (NaN for a super-block holding a non-finite x).
+// Limits: |x| < 2^112 (the min term's factor 2^(37-s) stays finite).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_i8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_i8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// 2^e as a float for e in [-126, 127] (exact)
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+// the low bytes of four words -> one word
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+}
+
+// x (K fp32, one token) -> this CTA's digit fragments, min-term fragments and factors.
+// A warp takes one super-block at a time (lane l: elements 8l..8l+7, i.e. sub-block
+// l / 4, positions 8(l % 4)..+7), with up to four super-blocks' loads in flight.
+// * max|x| from the largest magnitude bit pattern (a NaN or Inf pattern is larger than
+//   every finite one, which flags the super-block as non-finite); E with max|x| < 2^E.
+// * x * 2^s + 1.5 * 2^23 (one rounding: |x * 2^s| < 2^22 keeps the sum in [2^23, 2^24])
+//   holds xi = round-to-nearest-even(x * 2^s) in its low bits: the bit pattern minus
+//   0x4B400000.  The balanced digits follow with shifts: r1 = (xi + 128) >> 8 and
+//   r2 = (r1 + 128) >> 8 give xi = d0 + 256 d1 + 65536 d2 with d0 = xi - 256 r1,
+//   d1 = r1 - 256 r2, d2 = r2, so each digit's byte is the low byte of xi, r1, r2.
+// * Scalings by 2^s, 2^(s-13) and 2^-s use two power-of-two factors where one would
+//   leave the normal range (s lies in [-106, 170]).
+__device__ __forceinline__ void build_i8(const float* __restrict__ x, int nblk, uint4* sB, uint32_t* sM, float* sF) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int tq = lane & 3, j = lane >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    constexpr int kBatch = 4;
+    for (int b0 = warp; b0 < nblk; b0 += kBatch * nw) {
+        float4 xv[kBatch][2];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int b = b0 + u * nw;
+            if (b < nblk) {
+                xv[u][0] = __ldg(x4 + b * 64 + lane * 2);
+                xv[u][1] = __ldg(x4 + b * 64 + lane * 2 + 1);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int b = b0 + u * nw;
+            if (b >= nblk) break;  // warp-uniform
+            const float e[8] = {xv[u][0].x, xv[u][0].y, xv[u][0].z, xv[u][0].w,
+                                xv[u][1].x, xv[u][1].y, xv[u][1].z, xv[u][1].w};
+            uint32_t mb = 0u;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) mb = max(mb, __float_as_uint(e[v]) & 0x7FFFFFFFu);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+            const bool fin = mb < 0x7F800000u;
+            int E = 0;
+            if (fin && mb != 0u) E = (mb >> 23) ? static_cast<int>(mb >> 23) - 126 : (32 - __clz(mb)) - 149;
+            const int s = 22 - E;  // |x| * 2^s < 2^22
+            uint32_t xb[8];
+            if (s >= -126 && s <= 127) {
+                const float p = pow2f(s);
+#pragma unroll
+                for (int v = 0; v < 8; ++v) xb[v] = __float_as_uint(fmaf(e[v], p, 12582912.0f));
+            } else {
+                const int s1 = s >> 1;
+                const float p1 = pow2f(s1), p2 = pow2f(s - s1);
+#pragma unroll
+                for (int v = 0; v < 8; ++v) xb[v] = __float_as_uint(fmaf(e[v] * p1, p2, 12582912.0f));
+            }
+            uint32_t r1[8], r2[8];
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+                const int a = static_cast<int>(xb[v] - 0x4B3FFF80u) >> 8;  // (xi + 128) >> 8
+                r1[v] = static_cast<uint32_t>(a);
+                r2[v] = static_cast<uint32_t>((a + 128) >> 8);
+            }
+            const uint32_t D[3][2] = {{pack_low_bytes(xb[0], xb[1], xb[2], xb[3]), pack_low_bytes(xb[4], xb[5], xb[6], xb[7])},
+                                      {pack_low_bytes(r1[0], r1[1], r1[2], r1[3]), pack_low_bytes(r1[4], r1[5], r1[6], r1[7])},
+                                      {pack_low_bytes(r2[0], r2[1], r2[2], r2[3]), pack_low_bytes(r2[4], r2[5], r2[6], r2[7])}};
+            // chunk c = j / 2; low-nibble sub-block (j even) -> columns 0..2, words 0 and 2
+            // (k slots of the first and second MMA); high-nibble one -> columns 3..5, words 1, 3
+            const int par = j & 1;
+            uint4* bc = sB + (static_cast<size_t>(b) * 4 + (j >> 1)) * 32;
+#pragma unroll
+            for (int p = 0; p < 3; ++p)
+                bc[(3 * par + p) * 4 + tq] =
+                    par ? make_uint4(0u, D[p][0], 0u, D[p][1]) : make_uint4(D[p][0], 0u, D[p][1], 0u);
+            sB[(static_cast<size_t>(b) * 4 + (lane >> 3)) * 32 + 24 + (lane & 7)] = make_uint4(0u, 0u, 0u, 0u);
+            // sub-block sums (each quad holds its sub-block's), then lane 4g + tq (g < 2) of the
+            // min-term fragment: plane g of (X_2tq, X_2tq+1) * 2^(s-13)  (|X| * 2^(s-13) < 2^14)
+            float sum = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            const float xa = __shfl_sync(0xffffffffu, sum, 8 * tq);
+            const float xc = __shfl_sync(0xffffffffu, sum, 8 * tq + 4);
+            uint32_t mw = 0u;
+            if (lane < 8) {
+                const int t = s - 13, t1 = t >> 1;
+                const float pa = pow2f(t1), pb = pow2f(t - t1);
+                const float va = (xa * pa) * pb, vc = (xc * pa) * pb;
+                const __half ha = __float2half_rn(va), hc = __float2half_rn(vc);
+                mw = lane < 4 ? pack_half2(ha, hc)
+                              : pack_half2(__float2half_rn(va - __half2float(ha)), __float2half_rn(vc - __half2float(hc)));
+            }
+            sM[static_cast<size_t>(b) * 32 + lane] = mw;
+            if (lane == 0) {
+                const int w = -s, w1 = w >> 1;
+                sF[b] = fin ? pow2f(w1) * pow2f(w - w1) : __int_as_float(0x7FC00000);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Per-lane constants of the integer unit.
+struct I8Lane {
+    uint32_t sel_m;       // min bytes 2(tq&1), 2(tq&1)+1 -> fp16 pair of integers
+    bool lo;              // tq < 2: mins of sub-blocks 0..3
+    uint32_t sel[2][2];   // [chunk parity][column]: scale byte of the column's sub-block
+    float cw[2];          // digit weight of the lane's columns 2tq, 2tq+1
+};
+
+__device__ __forceinline__ I8Lane i8_lane(int lane) {
+    I8Lane L;
+    const int tq = lane & 3;
+    const uint32_t k0 = 2u * (lane & 1);
+    L.sel_m = k0 | 0x40u | ((k0 + 1) << 8) | 0x4000u;
+    L.lo = tq < 2;
+    // column 2tq + i belongs to the high-nibble sub-block when it is 3..5
+    const uint32_t par0 = tq >= 2 ? 1u : 0u, par1 = tq >= 1 ? 1u : 0u;
+    L.sel[0][0] = 0x4440u | par0;
+    L.sel[0][1] = 0x4440u | par1;
+    L.sel[1][0] = 0x4440u | (2u + par0);
+    L.sel[1][1] = 0x4440u | (2u + par1);
+    // columns 0..2: 256^p; 3..5: 256^p / 16; 6, 7: unused
+    L.cw[0] = tq == 0 ? 1.0f : tq == 1 ? 65536.0f : tq == 2 ? 16.0f : 0.0f;
+    L.cw[1] = tq == 0 ? 256.0f : tq == 1 ? 0.0625f : tq == 2 ? 4096.0f : 0.0f;
+    return L;
+}
+
+// One unit: rows g, g+8 of a 16-row tile against one super-block.  bq: the super-block's
+// digit fragments ([4][32] uint4), bm: this lane's min-term fragment word, fs = 2^-s.
+__device__ __forceinline__ void i8_unit(const SuperBlock& sbk, const uint4* __restrict__ bq, uint32_t bm, float fs,
+                                        int lane, const I8Lane& L, float (&accd)[2][2], float (&accm)[2]) {
+    uint32_t scl[2], sch[2], am[2];
+    float d[2], dmn[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint4 h = sbk.hd[i];
+        d[i] = fh3::h2f_bits(h.x);
+        dmn[i] = fh3::h2f_bits(h.x >> 16);
+        scl[i] = h.y & 0x3F3F3F3Fu;                                       // sc_0..3
+        sch[i] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);        // sc_4..7
+        const uint32_t mw = L.lo ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+        am[i] = __byte_perm(mw, 0u, L.sel_m);
+    }
+    int S[2][2] = {{0, 0}, {0, 0}};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 bf = bq[c * 32 + lane];
+        const uint2 w0 = sbk.q[0][c], w1 = sbk.q[1][c];
+        int C[4];
+        mma_i8_z(C, w0.x & 0x0F0F0F0Fu, w1.x & 0x0F0F0F0Fu, w0.x & 0xF0F0F0F0u, w1.x & 0xF0F0F0F0u, bf.x, bf.y);
+        mma_i8(C, w0.y & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu, w0.y & 0xF0F0F0F0u, w1.y & 0xF0F0F0F0u, bf.z, bf.w);
+        const uint32_t s0 = c < 2 ? scl[0] : sch[0], s1 = c < 2 ? scl[1] : sch[1];
+        S[0][0] += static_cast<int>(__byte_perm(s0, 0u, L.sel[c & 1][0])) * C[0];
+        S[0][1] += static_cast<int>(__byte_perm(s0, 0u, L.sel[c & 1][1])) * C[1];
+        S[1][0] += static_cast<int>(__byte_perm(s1, 0u, L.sel[c & 1][0])) * C[2];
+        S[1][1] += static_cast<int>(__byte_perm(s1, 0u, L.sel[c & 1][1])) * C[3];
+    }
+    float dm4[4];
+    mma_16816_z(dm4, am[0], am[1], 0u, 0u, bm, 0u);
+    const float f0 = d[0] * fs, f1 = d[1] * fs;
+    accd[0][0] = fmaf(__int2float_rn(S[0][0]), f0, accd[0][0]);
+    accd[0][1] = fmaf(__int2float_rn(S[0][1]), f0, accd[0][1]);
+    accd[1][0] = fmaf(__int2float_rn(S[1][0]), f1, accd[1][0]);
+    accd[1][1] = fmaf(__int2float_rn(S[1][1]), f1, accd[1][1]);
+    const float fm = fs * 137438953472.0f;  // 2^37: back from the mins' 2^-24 and the planes' 2^(s-13)
+    accm[0] = fmaf(dm4[0] + dm4[1], -dmn[0] * fm, accm[0]);
+    accm[1] = fmaf(dm4[2] + dm4[3], -dmn[1] * fm, accm[1]);
+}
+
+__global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_i8_kernel(
+    const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t N, int64_t units, int seg_max,
+    const float* __restrict__ x, const float* __restrict__ bias, float* __restrict__ y,
+    float* __restrict__ partials, int* __restrict__ counters, int* status) {
+    extern __shared__ __align__(128) uint8_t gv_smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nw = blockDim.x >> 5;
+    const int g = lane >> 2, tq = lane & 3;
+
+    uint4* sB = reinterpret_cast<uint4*>(gv_smem);
+    uint32_t* sM = reinterpret_cast<uint32_t*>(sB + static_cast<size_t>(nblk) * 128);
+    float* sF = reinterpret_cast<float*>(sM + static_cast<size_t>(nblk) * 32);
+
+    // the run partition of gemv_stream_kernel: equal contiguous runs, at most one warp per
+    // unit, so the runs meeting a tile are consecutive warps
+    const int64_t GW = min(static_cast<int64_t>(gridDim.x) * nw, units);
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * nw + warp;
+    const int64_t u0 = gw < GW ? gw * units / GW : units;
+    const int64_t u1 = gw < GW ? (gw + 1) * units / GW : units;
+    const int n = static_cast<int>(u1 - u0);
+
+    int lt = static_cast<int>(u0 / nblk), lb = static_cast<int>(u0 % nblk);
+    auto load_next = [&](SuperBlock& dst) {
+        const int64_t r0 = static_cast<int64_t>(lt) * 16 + g, r1 = r0 + 8;
+        load_sb(dst, W + (r0 < N ? r0 : N - 1) * row_bytes, W + (r1 < N ? r1 : N - 1) * row_bytes, lb, tq);
+        if (++lb == nblk) {
+            lb = 0;
+            ++lt;
+        }
+    };
+    SuperBlock sa, sbuf;
+    if (n > 0) load_next(sa);
+    if (n > 1) load_next(sbuf);
+    pdl_launch_dependents();  // the next kernel may start its own weight loads
+
+    pdl_wait();  // x, y and the scratch are ours from here on
+    build_i8(x, nblk, sB, sM, sF);
+
+    const I8Lane L = i8_lane(lane);
+    float accd[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+    float accm[2] = {0.0f, 0.0f};
+    int t = static_cast<int>(u0 / nblk), b = static_cast<int>(u0 % nblk);
+    // end of this warp's segment of tile t: direct store, or partials + last-arriver sum
+    // (the count sits in the run, where its round trip overlaps the run's loads in flight)
+    auto finish_segment = [&]() {
+        // the quad's columns -> row sums (fixed order), held by every lane of the quad
+        float v0 = fmaf(accd[0][0], L.cw[0], fmaf(accd[0][1], L.cw[1], accm[0]));
+        float v1 = fmaf(accd[1][0], L.cw[0], fmaf(accd[1][1], L.cw[1], accm[1]));
+        v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+        v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+        v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+        accd[0][0] = accd[0][1] = accd[1][0] = accd[1][1] = 0.0f;
+        accm[0] = accm[1] = 0.0f;
+        const int64_t wf = stream_warp_of(static_cast<int64_t>(t) * nblk, GW, units);
+        const int64_t wl = stream_warp_of(static_cast<int64_t>(t + 1) * nblk - 1, GW, units);
+        const int nseg = static_cast<int>(wl - wf + 1);
+        const int64_t r0 = static_cast<int64_t>(t) * 16 + g, r1 = r0 + 8;
+        if (nseg == 1) {
+            if (tq == 0) {
+                if (r0 < N) y[r0] = v0 + (bias ? bias[r0] : 0.0f);
+                if (r1 < N) y[r1] = v1 + (bias ? bias[r1] : 0.0f);
+            }
+            return;
+        }
+        if (nseg > seg_max) {
+            if (lane == 0) fh3::record_status(status, FH3_ERR);  // never write past the slots
+            return;
+        }
+        float* pt = partials + static_cast<int64_t>(t) * seg_max * 16;
+        if (tq == 0) {
+            pt[(gw - wf) * 16 + g] = v0;
+            pt[(gw - wf) * 16 + g + 8] = v1;
+        }
+        // the warp's stores, then lane 0's release/acquire count: it publishes them at GPU
+        // scope and, for the last segment, acquires the other segments' stores
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(counters + t) : "memory");
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old != nseg - 1) return;
+        __syncwarp();
+        if (tq == 0) {  // last segment: add all in segment order
+            float s0 = 0.0f, s1 = 0.0f;
+            for (int q0 = 0; q0 < nseg; q0 += 4) {  // four segments' loads in flight, added in order
+                float a0[4], a1[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const bool ok = q0 + u < nseg;
+                    a0[u] = ok ? __ldcg(pt + (q0 + u) * 16 + g) : 0.0f;
+                    a1[u] = ok ? __ldcg(pt + (q0 + u) * 16 + g + 8) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (q0 + u < nseg) {
+                        s0 = q0 + u == 0 ? a0[u] : s0 + a0[u];
+                        s1 = q0 + u == 0 ? a1[u] : s1 + a1[u];
+                    }
+                }
+            }
+            if (r0 < N) y[r0] = s0 + (bias ? bias[r0] : 0.0f);
+            if (r1 < N) y[r1] = s1 + (bias ? bias[r1] : 0.0f);
+        }
+        if (lane == 0) counters[t] = 0;
+    };
+    auto step = [&](const SuperBlock& cur, int i) {
+        i8_unit(cur, sB + static_cast<size_t>(b) * 128, sM[static_cast<size_t>(b) * 32 + lane], sF[b], lane, L, accd,
+                accm);
+        if (b == nblk - 1 || i == n - 1) finish_segment();
+        if (++b == nblk) {
+            b = 0;
+            ++t;
+        }
+    };
+    for (int i = 0; i < n; i += 2) {
+        step(sa, i);
+        if (i + 2 < n) load_next(sa);
+        if (i + 1 >= n) break;
+        step(sbuf, i + 1);
+        if (i + 3 < n) load_next(sbuf);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // 5..16 tokens: a CTA owns a 16-row tile and a K range; the range's B fragments are
 // copied to shared memory once.  When the fragments of the whole K would not fit, a
 // cluster of S CTAs splits K and the partial sums meet over distributed shared memory.
@@ -803,6 +1140,41 @@ int launch_stream(const Fh3CudaW* w, const float* x, float* y, const float* bias
                       "gemv_stream_kernel launch");
 }
 
+// Launch the 1-token integer kernel when its shared memory fits; returns 1 (not launched)
+// otherwise.  It shares the stream kernel's partial and counter slots (same run partition).
+int launch_i8(const Fh3CudaW* w, const float* x, float* y, const float* bias, cudaStream_t s) {
+    using namespace fh3host;
+    DevCtx* c = ctx();
+    const int64_t N = w->out, K = w->in;
+    const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
+    const size_t smem = static_cast<size_t>(nblk) * (128 * 16 + 32 * 4 + 4);
+    if (smem > 227 * 1024) return 1;
+    const int sms = ctx_sms(c);
+    const int64_t ntiles = (N + 15) / 16;
+    const int64_t units = ntiles * nblk;
+    const int64_t GW = std::min<int64_t>(static_cast<int64_t>(sms) * kStreamWarps, units);
+    const int64_t per = units / GW;  // >= 1: each run spans at least `per` units
+    const int seg_max = static_cast<int>(std::min<int64_t>(nblk, (nblk + per - 1) / per + 1));
+    float* partials = static_cast<float*>(scratch(c, 6, static_cast<size_t>(ntiles) * seg_max * 16 * 4, s));
+    int* counters = static_cast<int*>(scratch_zeroed(c, 7, static_cast<size_t>(ntiles) * 4, s));
+    if (!partials || !counters) return FH3_E_NOMEM;
+
+    static int smem_set = 0;
+    int rc = set_smem(reinterpret_cast<const void*>(gemv_i8_kernel), smem, smem_set, "gemv_i8_kernel smem attribute");
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms), 1, 1);
+    cfg.blockDim = dim3(kStreamWarps * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemv_i8_kernel, w->data, fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, K), nblk,
+                                         N, units, seg_max, x, bias, y, partials, counters, ctx_status(c)),
+                      "gemv_i8_kernel launch");
+}
+
 template <int NT>
 int launch_mma(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, const float* fsb, int M,
                float* y, const float* bias, cudaStream_t s) {
@@ -849,16 +1221,22 @@ namespace fh3host {
 int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s) {
     DevCtx* c = ctx();
     if (!c) return set_error(FH3CUDA_E_NODEV, "gemv_mma: call fh3cuda_init first");
-    // 1..2 tokens: the single-launch stream-K kernel; FH3CUDA_GEMV_KERNEL=mma-cta
-    // selects the prep + CTA-per-tile kernels instead
-    // The tcgen05 kernel (gemv_tc.cu) when out <= in or from 5 tokens on (measured faster
-    // there: 5120->5120 and 13824->5120 at every token count, 5120->13824 from 5 tokens; the
-    // warp-MMA kernels stay ahead for 5120->13824 at 1..4 tokens).  FH3CUDA_GEMV_KERNEL=tc
-    // forces it for every shape; mma-stream / mma-cta force the warp-MMA kernels.
+    // 1 token: the stream-K kernel on integer MMAs (gemv_i8_kernel; measured faster than the
+    // others on every BASELINE shape).  2 tokens: the stream-K kernel on fp16 MMAs;
+    // FH3CUDA_GEMV_KERNEL=mma-cta selects the prep + CTA-per-tile kernels instead.
+    // The tcgen05 kernel (gemv_tc.cu) at 2..16 tokens when out <= in, and from 5 tokens on
+    // (measured faster there: 5120->5120 and 13824->5120 at 2..16 tokens, 5120->13824 from
+    // 5 tokens; the warp-MMA kernels stay ahead for 5120->13824 at 2..4 tokens).
+    // FH3CUDA_GEMV_KERNEL=tc forces it for every shape; mma-stream / mma-cta force the
+    // fp16 warp-MMA kernels, mma-i8 the integer one (at 1 token).
     const char* kname = getenv("FH3CUDA_GEMV_KERNEL");
     const bool cta = kname && strcmp(kname, "mma-cta") == 0;
     const bool warp_mma = kname && (cta || strcmp(kname, "mma-stream") == 0);
     const bool tc_forced = kname && strcmp(kname, "tc") == 0;
+    if (n_tok == 1 && !warp_mma && !tc_forced) {
+        const int r = launch_i8(w, x, y, bias, s);
+        if (r != 1) return r;
+    }
     if (!warp_mma && (tc_forced || w->out <= w->in || n_tok >= 5)) {
         const int r = gemv_tc(w, x, y, n_tok, bias, s);
         if (r != 1) return r;

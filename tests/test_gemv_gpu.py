@@ -25,13 +25,14 @@ def gemv_path(request):
     return request.param
 
 
-@pytest.fixture(autouse=True, params=["default", "tc", "mma-stream", "mma-cta", "fp32"])
+@pytest.fixture(autouse=True, params=["default", "tc", "mma-stream", "mma-cta", "mma-i8", "fp32"])
 def gemv_kernel(request, monkeypatch):
     """...and on every GEMV kernel: the default choice (tcgen05 integer MMAs when out <= in
     or from 5 tokens on, warp-level MMAs otherwise), the tcgen05 kernel forced for every
     shape ("tc"), the warp-MMA kernels ("mma-stream": persistent stream-K for 1..2 tokens,
-    CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile) and the fp32 CUDA-core kernel
-    (FH3CUDA_GEMV_KERNEL=fp32)."""
+    CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile; "mma-i8": the 1-token stream-K
+    kernel on integer MMAs of the nibbles against activation digits) and the fp32 CUDA-core
+    kernel (FH3CUDA_GEMV_KERNEL=fp32)."""
     if request.param == "default":
         monkeypatch.delenv("FH3CUDA_GEMV_KERNEL", raising=False)
     else:
