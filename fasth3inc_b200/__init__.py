@@ -129,9 +129,10 @@ def matmul(w: Q4KWeight, x, bias=None, out=None, stream=None):
 
 def gemv(w: Q4KWeight, x, bias=None, out=None, stream=None):
     """Q4_K GEMV for 1..16 tokens (fh3cuda_gemv_q4k_dev): tensor-core kernels by default
-    (tcgen05 MMAs when out <= in or from 5 tokens: integer MMAs up to 5 tokens, f16 MMAs of
-    sc*q from 6; warp-level MMAs otherwise);
-    FH3CUDA_GEMV_KERNEL=tc | mma-stream | mma-cta | fp32 selects one."""
+    (1 token: warp-level integer MMAs of the nibbles against digits of x; from 2 tokens
+    tcgen05 MMAs when out <= in or from 5 tokens: integer MMAs up to 5 tokens, f16 MMAs of
+    sc*q from 6; warp-level f16 MMAs otherwise);
+    FH3CUDA_GEMV_KERNEL=tc | mma-stream | mma-cta | mma-i8 | fp32 selects one."""
     torch = _torch()
     _ensure(x)
     n_tok = x.shape[0]
