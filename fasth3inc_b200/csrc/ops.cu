@@ -231,10 +231,14 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(
 // The same for a compile-time head_dim HD and half rotation HALF (a multiple of 8,
 // or 0).  An 8-lane group takes kQkHeadsPerGroup heads of one token: the norm
 // weights and the token's cos/sin live in registers for all of them, the next
-// head's row is loaded while the current one is computed, and each lane keeps its
+// kQkAhead heads' rows are in flight while the current one is computed, and each lane keeps its
 // HD/8 strided values in registers after one staging pass; both halves of every
 // rotation pair (channels j and j + HALF) are in the same lane.
 constexpr int kQkHeadsPerGroup = 8;
+#ifndef FH3_QK_AHEAD
+#define FH3_QK_AHEAD 2
+#endif
+constexpr int kQkAhead = FH3_QK_AHEAD;  // heads of a group in flight
 
 template <bool SRC_BF16, int HD>
 struct QkRaw {
@@ -289,10 +293,16 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_reg_kernel(
             s1[m] = __ldg(sn + i * ROT + HALF + j);
         }
     }
-    QkRaw<SRC_BF16, HD> cur, nxt;
-    qk_load<SRC_BF16, HD>(cur, src, i * ld_src + static_cast<int64_t>(h0) * HD, l8);
-    for (int h = h0; h < h1; ++h) {
-        if (h + 1 < h1) qk_load<SRC_BF16, HD>(nxt, src, i * ld_src + static_cast<int64_t>(h + 1) * HD, l8);
+    // a ring of kQkAhead heads in flight: a slot is refilled as soon as its head is staged
+    QkRaw<SRC_BF16, HD> buf[kQkAhead];
+#pragma unroll
+    for (int k = 0; k < kQkAhead; ++k)
+        if (h0 + k < h1) qk_load<SRC_BF16, HD>(buf[k], src, i * ld_src + static_cast<int64_t>(h0 + k) * HD, l8);
+#pragma unroll
+    for (int jj = 0; jj < kQkHeadsPerGroup; ++jj) {
+        const int h = h0 + jj;
+        if (h >= h1) break;
+        QkRaw<SRC_BF16, HD>& cur = buf[jj % kQkAhead];
 #pragma unroll
         for (int k = 0; k < HD / 32; ++k) {
             float4 f;
@@ -306,6 +316,8 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_reg_kernel(
             }
             *reinterpret_cast<float4*>(vec + 4 * l8 + 32 * k) = f;
         }
+        if (h + kQkAhead < h1)
+            qk_load<SRC_BF16, HD>(cur, src, i * ld_src + static_cast<int64_t>(h + kQkAhead) * HD, l8);
         __syncwarp(gmask);
         float val[NV];
         float ss = 0.0f;
@@ -348,7 +360,6 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_reg_kernel(
             }
         }
         __syncwarp(gmask);  // the stage is rewritten by the next head
-        if (h + 1 < h1) cur = nxt;
     }
 }
 
