@@ -563,6 +563,8 @@ def gemv_kernel_name(K: int, N: int, M: int) -> str:
     """The kernel the default GEMV dispatch (csrc/gemv_mma.cu, gemv_mma) picks."""
     if M == 1 and (K // 256) * 2180 <= 227 * 1024:
         return "gemv_i8_kernel"
+    if 2 <= M <= 4 and (M == 2 or N > K) and (K // 256) * (768 * M + 128 + 4 * M) <= 227 * 1024:
+        return "gemv_i8m_kernel"
     if N <= K or M >= 5:
         return "gemv_tc_kernel (i8 A)" if M <= 5 else "gemv_tc_kernel (f16 A = sc*q) + gemv_xprep_kernel"
     if M <= 2:

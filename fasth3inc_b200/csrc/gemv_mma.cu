@@ -968,6 +968,309 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_i8_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// 2..4 tokens on integer MMAs: gemv_i8_kernel's walk and activation digits, one MMA per
+// nibble half.  With more than one token the two halves' digit columns no longer fit one
+// MMA's eight, so each sub-block gets its own MMA (K 32: positions 8tq..8tq+3 in slots
+// 4tq+r, 8tq+4..8tq+7 in slots 16+4tq+r) against B columns (token t, digit p) = 3t + p,
+// eight per n-group (one n-group for 2 tokens, two for 3 and 4).  A chunk's low- and
+// high-nibble accumulators are multiplied by 16 sc_2c and sc_2c+1 (the high nibbles enter as
+// 16 q) and summed in int32 (|sum| < 2^29); each token's columns are scaled by d * 2^-s_t
+// once per super-block and by 256^p / 16 when the segment ends.
+// Shared memory: digit pairs [nblk][8 sub-blocks][3M columns][4 tq] uint2 | min-term
+// fragments [nblk][32] u32 (column 2t + plane) | factors 2^-s [nblk][M] (NaN: non-finite x).
+// ---------------------------------------------------------------------------
+template <int M>
+__device__ __forceinline__ void build_i8m(const float* __restrict__ x, int64_t K, int nblk, uint2* sB, uint32_t* sM,
+                                          float* sF) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int tq = lane & 3, j = lane >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const int items = M * nblk;
+    constexpr int kBatch = 4;
+    for (int it0 = warp; it0 < items; it0 += kBatch * nw) {
+        float4 xv[kBatch][2];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int it = it0 + u * nw;
+            if (it < items) {
+                const int t = it / nblk, b = it - t * nblk;
+                const float4* xp = x4 + (static_cast<int64_t>(t) * K >> 2) + b * 64 + lane * 2;
+                xv[u][0] = __ldg(xp);
+                xv[u][1] = __ldg(xp + 1);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int it = it0 + u * nw;
+            if (it >= items) break;  // warp-uniform
+            const int t = it / nblk, b = it - t * nblk;
+            const float e[8] = {xv[u][0].x, xv[u][0].y, xv[u][0].z, xv[u][0].w,
+                                xv[u][1].x, xv[u][1].y, xv[u][1].z, xv[u][1].w};
+            uint32_t mb = 0u;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) mb = max(mb, __float_as_uint(e[v]) & 0x7FFFFFFFu);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+            const bool fin = mb < 0x7F800000u;
+            int E = 0;
+            if (fin && mb != 0u) E = (mb >> 23) ? static_cast<int>(mb >> 23) - 126 : (32 - __clz(mb)) - 149;
+            const int sx = 22 - E;  // |x| * 2^sx < 2^22
+            uint32_t xb[8];
+            if (sx >= -126 && sx <= 127) {
+                const float pw = pow2f(sx);
+#pragma unroll
+                for (int v = 0; v < 8; ++v) xb[v] = __float_as_uint(fmaf(e[v], pw, 12582912.0f));
+            } else {
+                const int s1 = sx >> 1;
+                const float p1 = pow2f(s1), p2 = pow2f(sx - s1);
+#pragma unroll
+                for (int v = 0; v < 8; ++v) xb[v] = __float_as_uint(fmaf(e[v] * p1, p2, 12582912.0f));
+            }
+            uint32_t r1[8], r2[8];
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+                const int a = static_cast<int>(xb[v] - 0x4B3FFF80u) >> 8;  // (xi + 128) >> 8
+                r1[v] = static_cast<uint32_t>(a);
+                r2[v] = static_cast<uint32_t>((a + 128) >> 8);
+            }
+            uint2* bc = sB + ((static_cast<size_t>(b) * 8 + j) * (3 * M) + 3 * t) * 4 + tq;
+            bc[0] = make_uint2(pack_low_bytes(xb[0], xb[1], xb[2], xb[3]), pack_low_bytes(xb[4], xb[5], xb[6], xb[7]));
+            bc[4] = make_uint2(pack_low_bytes(r1[0], r1[1], r1[2], r1[3]), pack_low_bytes(r1[4], r1[5], r1[6], r1[7]));
+            bc[8] = make_uint2(pack_low_bytes(r2[0], r2[1], r2[2], r2[3]), pack_low_bytes(r2[4], r2[5], r2[6], r2[7]));
+            // sub-block sums, then lanes 8t .. 8t+7 of the min-term fragment: column 2t + plane
+            float sum = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            const float xa = __shfl_sync(0xffffffffu, sum, 8 * tq);
+            const float xc = __shfl_sync(0xffffffffu, sum, 8 * tq + 4);
+            if (lane < 8) {
+                const int tt = sx - 13, t1 = tt >> 1;
+                const float pa = pow2f(t1), pb = pow2f(tt - t1);
+                const float va = (xa * pa) * pb, vc = (xc * pa) * pb;
+                const __half ha = __float2half_rn(va), hc = __float2half_rn(vc);
+                sM[static_cast<size_t>(b) * 32 + 8 * t + lane] =
+                    lane < 4 ? pack_half2(ha, hc)
+                             : pack_half2(__float2half_rn(va - __half2float(ha)), __float2half_rn(vc - __half2float(hc)));
+            }
+            if (t == 0 && lane >= 8 * M) sM[static_cast<size_t>(b) * 32 + lane] = 0u;  // columns past 2M
+            if (lane == 0) {
+                const int w = -sx, w1 = w >> 1;
+                sF[static_cast<size_t>(b) * M + t] = fin ? pow2f(w1) * pow2f(w - w1) : __int_as_float(0x7FC00000);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+template <int M>
+__global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_i8m_kernel(
+    const uint8_t* __restrict__ W, size_t row_bytes, int nblk, int64_t K, int64_t N, int64_t units, int seg_max,
+    const float* __restrict__ x, const float* __restrict__ bias, float* __restrict__ y, int64_t ldy,
+    float* __restrict__ partials, int* __restrict__ counters, int* status) {
+    constexpr int NC = 3 * M;         // digit columns
+    constexpr int NG = (NC + 7) / 8;  // MMA n-groups of eight
+    extern __shared__ __align__(128) uint8_t gv_smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nw = blockDim.x >> 5;
+    const int g = lane >> 2, tq = lane & 3;
+
+    uint2* sB = reinterpret_cast<uint2*>(gv_smem);
+    uint32_t* sM = reinterpret_cast<uint32_t*>(sB + static_cast<size_t>(nblk) * 8 * NC * 4);
+    float* sF = reinterpret_cast<float*>(sM + static_cast<size_t>(nblk) * 32);
+
+    // the run partition of gemv_stream_kernel
+    const int64_t GW = min(static_cast<int64_t>(gridDim.x) * nw, units);
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * nw + warp;
+    const int64_t u0 = gw < GW ? gw * units / GW : units;
+    const int64_t u1 = gw < GW ? (gw + 1) * units / GW : units;
+    const int n = static_cast<int>(u1 - u0);
+
+    int lt = static_cast<int>(u0 / nblk), lb = static_cast<int>(u0 % nblk);
+    auto load_next = [&](SuperBlock& dst) {
+        const int64_t r0 = static_cast<int64_t>(lt) * 16 + g, r1 = r0 + 8;
+        load_sb(dst, W + (r0 < N ? r0 : N - 1) * row_bytes, W + (r1 < N ? r1 : N - 1) * row_bytes, lb, tq);
+        if (++lb == nblk) {
+            lb = 0;
+            ++lt;
+        }
+    };
+    SuperBlock sa, sbuf;
+    if (n > 0) load_next(sa);
+    if (n > 1) load_next(sbuf);
+    pdl_launch_dependents();  // the next kernel may start its own weight loads
+
+    pdl_wait();  // x, y and the scratch are ours from here on
+    build_i8m<M>(x, K, nblk, sB, sM, sF);
+
+    // per-lane constants: B column g of each n-group, and the token and digit weight of the
+    // accumulator columns 2tq, 2tq+1 of each n-group (token -1: a column past 3M)
+    const uint32_t k0 = 2u * (lane & 1);
+    const uint32_t sel_m = k0 | 0x40u | ((k0 + 1) << 8) | 0x4000u;
+    const bool lo = tq < 2;
+    int bcol[NG], tok[NG][2];
+    uint32_t bmask[NG];
+    float cw[NG][2];
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng) {
+        const int c = 8 * ng + g;
+        bcol[ng] = min(c, NC - 1);
+        bmask[ng] = c < NC ? 0xFFFFFFFFu : 0u;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int cc = 8 * ng + 2 * tq + i;
+            tok[ng][i] = cc < NC ? cc / 3 : -1;
+            const int pd = cc % 3;
+            cw[ng][i] = cc < NC ? (pd == 0 ? 0.0625f : pd == 1 ? 16.0f : 4096.0f) : 0.0f;  // 256^p / 16
+        }
+    }
+    float accd[NG][2][2], accm[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng) accd[ng][0][0] = accd[ng][0][1] = accd[ng][1][0] = accd[ng][1][1] = 0.0f;
+
+    int t = static_cast<int>(u0 / nblk), b = static_cast<int>(u0 % nblk);
+    auto unit = [&](const SuperBlock& sbk) {
+        const uint2* bq = sB + static_cast<size_t>(b) * 8 * NC * 4;
+        uint32_t scl[2], sch[2], am[2];
+        float d[2], dmn[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const uint4 h = sbk.hd[i];
+            d[i] = fh3::h2f_bits(h.x);
+            dmn[i] = fh3::h2f_bits(h.x >> 16);
+            scl[i] = h.y & 0x3F3F3F3Fu;
+            sch[i] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+            const uint32_t mw = lo ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+            am[i] = __byte_perm(mw, 0u, sel_m);
+        }
+        int S[NG][2][2];
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) S[ng][0][0] = S[ng][0][1] = S[ng][1][0] = S[ng][1][1] = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint2 w0 = sbk.q[0][c], w1 = sbk.q[1][c];
+            const uint32_t s0 = c < 2 ? scl[0] : sch[0], s1 = c < 2 ? scl[1] : sch[1];
+            const uint32_t sl = 0x4440u | (2 * (c & 1)), sh = sl + 1;
+            const int lo0 = static_cast<int>(__byte_perm(s0, 0u, sl)) << 4, hi0 = static_cast<int>(__byte_perm(s0, 0u, sh));
+            const int lo1 = static_cast<int>(__byte_perm(s1, 0u, sl)) << 4, hi1 = static_cast<int>(__byte_perm(s1, 0u, sh));
+#pragma unroll
+            for (int ng = 0; ng < NG; ++ng) {
+                const uint2 bl = bq[((2 * c) * NC + bcol[ng]) * 4 + tq];
+                const uint2 bh = bq[((2 * c + 1) * NC + bcol[ng]) * 4 + tq];
+                int Cl[4], Ch[4];
+                mma_i8_z(Cl, w0.x & 0x0F0F0F0Fu, w1.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu,
+                         bl.x & bmask[ng], bl.y & bmask[ng]);
+                mma_i8_z(Ch, w0.x & 0xF0F0F0F0u, w1.x & 0xF0F0F0F0u, w0.y & 0xF0F0F0F0u, w1.y & 0xF0F0F0F0u,
+                         bh.x & bmask[ng], bh.y & bmask[ng]);
+                S[ng][0][0] += lo0 * Cl[0] + hi0 * Ch[0];
+                S[ng][0][1] += lo0 * Cl[1] + hi0 * Ch[1];
+                S[ng][1][0] += lo1 * Cl[2] + hi1 * Ch[2];
+                S[ng][1][1] += lo1 * Cl[3] + hi1 * Ch[3];
+            }
+        }
+        float dm4[4];
+        mma_16816_z(dm4, am[0], am[1], 0u, 0u, sM[static_cast<size_t>(b) * 32 + lane], 0u);
+        const float* fsb = sF + static_cast<size_t>(b) * M;
+        // columns past 3M hold zeros: a zero factor keeps a non-finite token out of them
+        const float fm = tq < M ? fsb[tq] * 137438953472.0f : 0.0f;  // 2^37, as gemv_i8_kernel
+        accm[0] = fmaf(dm4[0] + dm4[1], -dmn[0] * fm, accm[0]);
+        accm[1] = fmaf(dm4[2] + dm4[3], -dmn[1] * fm, accm[1]);
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const float f = tok[ng][i] >= 0 ? fsb[tok[ng][i]] : 0.0f;
+                accd[ng][0][i] = fmaf(__int2float_rn(S[ng][0][i]), d[0] * f, accd[ng][0][i]);
+                accd[ng][1][i] = fmaf(__int2float_rn(S[ng][1][i]), d[1] * f, accd[ng][1][i]);
+            }
+    };
+    // end of this warp's segment of tile t: direct store, or partials + last-arriver sum
+    auto finish_segment = [&]() {
+        // each token's columns -> its row sums (fixed order), held by every lane of the quad
+        float v[M][2];
+#pragma unroll
+        for (int tt = 0; tt < M; ++tt)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                float a = tq == tt ? accm[r] : 0.0f;
+#pragma unroll
+                for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+                        if (tok[ng][i] == tt) a = fmaf(accd[ng][r][i], cw[ng][i], a);
+                a += __shfl_xor_sync(0xffffffffu, a, 1);
+                a += __shfl_xor_sync(0xffffffffu, a, 2);
+                v[tt][r] = a;
+            }
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) accd[ng][0][0] = accd[ng][0][1] = accd[ng][1][0] = accd[ng][1][1] = 0.0f;
+        accm[0] = accm[1] = 0.0f;
+        // lane tq keeps token tq's sums
+        float v0 = 0.0f, v1 = 0.0f;
+#pragma unroll
+        for (int tt = 0; tt < M; ++tt)
+            if (tq == tt) {
+                v0 = v[tt][0];
+                v1 = v[tt][1];
+            }
+        const int64_t wf = stream_warp_of(static_cast<int64_t>(t) * nblk, GW, units);
+        const int64_t wl = stream_warp_of(static_cast<int64_t>(t + 1) * nblk - 1, GW, units);
+        const int nseg = static_cast<int>(wl - wf + 1);
+        const int64_t r0 = static_cast<int64_t>(t) * 16 + g, r1 = r0 + 8;
+        if (nseg == 1) {
+            if (tq < M) {
+                if (r0 < N) y[tq * ldy + r0] = v0 + (bias ? bias[r0] : 0.0f);
+                if (r1 < N) y[tq * ldy + r1] = v1 + (bias ? bias[r1] : 0.0f);
+            }
+            return;
+        }
+        if (nseg > seg_max) {
+            if (lane == 0) fh3::record_status(status, FH3_ERR);  // never write past the slots
+            return;
+        }
+        float* pt = partials + static_cast<int64_t>(t) * seg_max * 16 * M;
+        if (tq < M) {
+            pt[((gw - wf) * 16 + g) * M + tq] = v0;
+            pt[((gw - wf) * 16 + g + 8) * M + tq] = v1;
+        }
+        // the warp's stores, then lane 0's release/acquire count: it publishes them at GPU
+        // scope and, for the last segment, acquires the other segments' stores
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(counters + t) : "memory");
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old != nseg - 1) return;
+        __syncwarp();
+        if (tq < M) {  // last segment: add all in segment order
+            float s0 = 0.0f, s1 = 0.0f;
+            for (int q = 0; q < nseg; ++q) {
+                const float a0 = __ldcg(pt + (q * 16 + g) * M + tq), a1 = __ldcg(pt + (q * 16 + g + 8) * M + tq);
+                s0 = q == 0 ? a0 : s0 + a0;
+                s1 = q == 0 ? a1 : s1 + a1;
+            }
+            if (r0 < N) y[tq * ldy + r0] = s0 + (bias ? bias[r0] : 0.0f);
+            if (r1 < N) y[tq * ldy + r1] = s1 + (bias ? bias[r1] : 0.0f);
+        }
+        if (lane == 0) counters[t] = 0;
+    };
+    auto step = [&](const SuperBlock& cur, int i) {
+        unit(cur);
+        if (b == nblk - 1 || i == n - 1) finish_segment();
+        if (++b == nblk) {
+            b = 0;
+            ++t;
+        }
+    };
+    for (int i = 0; i < n; i += 2) {
+        step(sa, i);
+        if (i + 2 < n) load_next(sa);
+        if (i + 1 >= n) break;
+        step(sbuf, i + 1);
+        if (i + 3 < n) load_next(sbuf);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // 5..16 tokens: a CTA owns a 16-row tile and a K range; the range's B fragments are
 // copied to shared memory once.  When the fragments of the whole K would not fit, a
 // cluster of S CTAs splits K and the partial sums meet over distributed shared memory.
@@ -1175,6 +1478,43 @@ int launch_i8(const Fh3CudaW* w, const float* x, float* y, const float* bias, cu
                       "gemv_i8_kernel launch");
 }
 
+// Launch the 2..4-token integer kernel when its shared memory fits; returns 1 otherwise.
+template <int M>
+int launch_i8m(const Fh3CudaW* w, const float* x, float* y, const float* bias, cudaStream_t s) {
+    using namespace fh3host;
+    DevCtx* c = ctx();
+    const int64_t N = w->out, K = w->in;
+    const int nblk = static_cast<int>(K / fh3::kQ4KBlock);
+    const size_t smem = static_cast<size_t>(nblk) * (8 * 3 * M * 4 * 8 + 32 * 4 + M * 4);
+    if (smem > 227 * 1024) return 1;
+    const int sms = ctx_sms(c);
+    const int64_t ntiles = (N + 15) / 16;
+    const int64_t units = ntiles * nblk;
+    const int64_t GW = std::min<int64_t>(static_cast<int64_t>(sms) * kStreamWarps, units);
+    const int64_t per = units / GW;  // >= 1: each run spans at least `per` units
+    const int seg_max = static_cast<int>(std::min<int64_t>(nblk, (nblk + per - 1) / per + 1));
+    float* partials = static_cast<float*>(scratch(c, 6, static_cast<size_t>(ntiles) * seg_max * 16 * M * 4, s));
+    int* counters = static_cast<int*>(scratch_zeroed(c, 7, static_cast<size_t>(ntiles) * 4, s));
+    if (!partials || !counters) return FH3_E_NOMEM;
+
+    static int smem_set = 0;
+    int rc = set_smem(reinterpret_cast<const void*>(gemv_i8m_kernel<M>), smem, smem_set,
+                      "gemv_i8m_kernel smem attribute");
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms), 1, 1);
+    cfg.blockDim = dim3(kStreamWarps * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemv_i8m_kernel<M>, static_cast<const uint8_t*>(w->data),
+                                         fh3cuda_row_bytes(FH3CUDA_TYPE_Q4_K, K), nblk, K, N, units, seg_max, x, bias,
+                                         y, N, partials, counters, ctx_status(c)),
+                      "gemv_i8m_kernel launch");
+}
+
 template <int NT>
 int launch_mma(const Fh3CudaW* w, const uint4* frag, const uint32_t* mfrag, const int* expo, const float* fsb, int M,
                float* y, const float* bias, cudaStream_t s) {
@@ -1221,20 +1561,25 @@ namespace fh3host {
 int gemv_mma(const Fh3CudaW* w, const float* x, float* y, int n_tok, const float* bias, cudaStream_t s) {
     DevCtx* c = ctx();
     if (!c) return set_error(FH3CUDA_E_NODEV, "gemv_mma: call fh3cuda_init first");
-    // 1 token: the stream-K kernel on integer MMAs (gemv_i8_kernel; measured faster than the
-    // others on every BASELINE shape).  2 tokens: the stream-K kernel on fp16 MMAs;
-    // FH3CUDA_GEMV_KERNEL=mma-cta selects the prep + CTA-per-tile kernels instead.
-    // The tcgen05 kernel (gemv_tc.cu) at 2..16 tokens when out <= in, and from 5 tokens on
-    // (measured faster there: 5120->5120 and 13824->5120 at 2..16 tokens, 5120->13824 from
-    // 5 tokens; the warp-MMA kernels stay ahead for 5120->13824 at 2..4 tokens).
-    // FH3CUDA_GEMV_KERNEL=tc forces it for every shape; mma-stream / mma-cta force the
-    // fp16 warp-MMA kernels, mma-i8 the integer one (at 1 token).
+    // Measured on the BASELINE shapes (5120->13824, 13824->5120, 5120->5120):
+    // * 1 token: the stream-K kernel on integer MMAs (gemv_i8_kernel), faster on all three;
+    // * 2 tokens, and 3..4 tokens when out > in: its 2..4-token form (gemv_i8m_kernel);
+    // * the tcgen05 kernel (gemv_tc.cu) at 3..4 tokens when out <= in and from 5 tokens on.
+    // FH3CUDA_GEMV_KERNEL=tc forces tcgen05 for every shape; mma-i8 the integer kernels for
+    // 1..4 tokens; mma-stream / mma-cta the fp16 warp-MMA kernels (single-launch stream-K for
+    // 1..2 tokens, prep + CTA-per-tile otherwise; mma-cta always the latter).
     const char* kname = getenv("FH3CUDA_GEMV_KERNEL");
     const bool cta = kname && strcmp(kname, "mma-cta") == 0;
     const bool warp_mma = kname && (cta || strcmp(kname, "mma-stream") == 0);
     const bool tc_forced = kname && strcmp(kname, "tc") == 0;
     if (n_tok == 1 && !warp_mma && !tc_forced) {
         const int r = launch_i8(w, x, y, bias, s);
+        if (r != 1) return r;
+    }
+    const bool i8_forced = kname && strcmp(kname, "mma-i8") == 0;
+    if (n_tok >= 2 && n_tok <= 4 && !warp_mma && !tc_forced && (i8_forced || n_tok == 2 || w->out > w->in)) {
+        const int r = n_tok == 2 ? launch_i8m<2>(w, x, y, bias, s)
+                    : n_tok == 3 ? launch_i8m<3>(w, x, y, bias, s) : launch_i8m<4>(w, x, y, bias, s);
         if (r != 1) return r;
     }
     if (!warp_mma && (tc_forced || w->out <= w->in || n_tok >= 5)) {

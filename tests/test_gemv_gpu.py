@@ -30,9 +30,9 @@ def gemv_kernel(request, monkeypatch):
     """...and on every GEMV kernel: the default choice (tcgen05 integer MMAs when out <= in
     or from 5 tokens on, warp-level MMAs otherwise), the tcgen05 kernel forced for every
     shape ("tc"), the warp-MMA kernels ("mma-stream": persistent stream-K for 1..2 tokens,
-    CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile; "mma-i8": the 1-token stream-K
-    kernel on integer MMAs of the nibbles against activation digits) and the fp32 CUDA-core
-    kernel (FH3CUDA_GEMV_KERNEL=fp32)."""
+    CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile; "mma-i8": the stream-K kernels on
+    integer MMAs of the nibbles against activation digits, for 1..4 tokens) and the fp32
+    CUDA-core kernel (FH3CUDA_GEMV_KERNEL=fp32)."""
     if request.param == "default":
         monkeypatch.delenv("FH3CUDA_GEMV_KERNEL", raising=False)
     else:
@@ -70,7 +70,7 @@ def test_reference_fp64_golden_first_16_tokens(fh3):
 
 
 @pytest.mark.parametrize("K,N", [(5120, 5120), (5120, 13824), (13824, 5120)])
-@pytest.mark.parametrize("M", [1, 4, 16])
+@pytest.mark.parametrize("M", [1, 2, 4, 16])
 def test_baseline_shapes_vs_oracle(fh3, oracle, K, N, M):
     w = oracle.make_weights(seed=K + N, stream=1, rows=N, n=K)
     x = oracle.rng_normal(M, 2, M * K).reshape(M, K)
@@ -183,7 +183,7 @@ def test_non_finite_activations(fh3, oracle):
     tokens keep the usual accuracy."""
     K, N = 1280, 70
     w = oracle.make_weights(seed=13, stream=1, rows=N, n=K)
-    for M in (1, 3, 5, 8, 16):
+    for M in (1, 2, 3, 4, 5, 8, 16):
         x = oracle.rng_normal(13, M, M * K).reshape(M, K).astype(np.float32)
         x[0, 300] = np.inf
         bad = {0}
