@@ -129,9 +129,9 @@ def matmul(w: Q4KWeight, x, bias=None, out=None, stream=None):
 
 def gemv(w: Q4KWeight, x, bias=None, out=None, stream=None):
     """Q4_K GEMV for 1..16 tokens (fh3cuda_gemv_q4k_dev): tensor-core kernels by default
-    (1 token: warp-level integer MMAs of the nibbles against digits of x; from 2 tokens
-    tcgen05 MMAs when out <= in or from 5 tokens: integer MMAs up to 5 tokens, f16 MMAs of
-    sc*q from 6; warp-level f16 MMAs otherwise);
+    (warp-level integer MMAs of the nibbles against digits of x at 1-2 tokens and at 3-4
+    when out > in; otherwise tcgen05 MMAs: integer MMAs up to 5 tokens, f16 MMAs of sc*q
+    from 6);
     FH3CUDA_GEMV_KERNEL=tc | mma-stream | mma-cta | mma-i8 | fp32 selects one."""
     torch = _torch()
     _ensure(x)

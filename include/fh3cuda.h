@@ -205,12 +205,12 @@ FH3CUDA_API int fh3cuda_release_weights(const void *host);
 /* ---- explicit kernels (tests, benchmarks, fused trunk) ----------------- */
 
 /* Q4_K GEMV, 1 <= n_tok <= 16; same contract as fh3cuda_matmul_dev.  Tensor-core
- * kernels: at 1 token warp-level integer MMAs of the nibbles against base-256 digits of
- * x; from 2 tokens tcgen05 MMAs when out <= in or n_tok >= 5 (integer MMAs of the
- * nibbles up to 5 tokens; from 6, f16 MMAs of sc*q against x in two f16 pieces),
- * warp-level f16 MMAs otherwise.  FH3CUDA_GEMV_KERNEL in the environment selects one:
- * tc (tcgen05 for every shape), mma-stream / mma-cta (warp-level f16 MMAs), mma-i8 (the
- * integer warp-level kernel at 1 token), fp32 (the fp32 CUDA-core kernel). */
+ * kernels: warp-level integer MMAs of the nibbles against base-256 digits of x at 1-2
+ * tokens, and at 3-4 when out > in; otherwise tcgen05 MMAs (integer MMAs of the nibbles up
+ * to 5 tokens; from 6, f16 MMAs of sc*q against x in two f16 pieces).
+ * FH3CUDA_GEMV_KERNEL in the environment selects one: tc (tcgen05 for every shape),
+ * mma-i8 (the integer warp-level kernels, 1-4 tokens), mma-stream / mma-cta (warp-level
+ * f16 MMAs), fp32 (the fp32 CUDA-core kernel). */
 FH3CUDA_API int fh3cuda_gemv_q4k_dev(const Fh3CudaW *w, const float *x, float *y, int n_tok,
                          const float *bias_or_null, void *stream);
 
