@@ -27,8 +27,8 @@ def gemv_path(request):
 
 @pytest.fixture(autouse=True, params=["default", "tc", "mma-stream", "mma-cta", "mma-i8", "fp32"])
 def gemv_kernel(request, monkeypatch):
-    """...and on every GEMV kernel: the default choice (tcgen05 integer MMAs when out <= in
-    or from 5 tokens on, warp-level MMAs otherwise), the tcgen05 kernel forced for every
+    """...and on every GEMV kernel: the default choice (warp-level integer MMAs at 1-2 tokens
+    and at 3-4 when out > in, tcgen05 otherwise), the tcgen05 kernel forced for every
     shape ("tc"), the warp-MMA kernels ("mma-stream": persistent stream-K for 1..2 tokens,
     CTA-per-tile otherwise; "mma-cta" forces CTA-per-tile; "mma-i8": the stream-K kernels on
     integer MMAs of the nibbles against activation digits, for 1..4 tokens) and the fp32
@@ -109,6 +109,19 @@ def test_every_token_count_and_row_tail(fh3, oracle):
             assert rel_fro(got, ref) <= TOL, (M, bias is None)
 
 
+@pytest.mark.parametrize("K,Ms", [(27136, (1,)), (27392, (1, 2)), (18432, (3, 4)), (18688, (3, 4))])
+def test_shared_memory_bounds_of_the_integer_kernels(fh3, oracle, K, Ms):
+    """K at and just past the sizes whose activation digits fit the integer kernels' shared
+    memory (1 token: 106 super-blocks; 4 tokens: 72): past them the dispatch falls back to
+    the next kernel with the same accuracy.  1-2 tokens take the integer kernels on every
+    shape; 3-4 tokens do under the "mma-i8" parameter of the kernel fixture."""
+    N = 72
+    w = oracle.make_weights(seed=K, stream=1, rows=N, n=K)
+    for M in Ms:
+        x = oracle.rng_normal(K, M, M * K).reshape(M, K)
+        assert rel_fro(_run(fh3, w, K, N, x), oracle.matmul(Q4K, w, K, N, x)) <= TOL, M
+
+
 def test_single_row_single_block(fh3, oracle):
     w = oracle.make_weights(seed=6, stream=1, rows=1, n=256)
     x = oracle.rng_normal(6, 2, 256).reshape(1, 256)
@@ -147,7 +160,7 @@ def test_split_tiles_repeat_bitwise(fh3, oracle):
     import torch
     K, N = 13824, 1000
     ws = [fh3.Q4KWeight.from_bytes(oracle.make_weights(seed=20 + i, stream=1, rows=N, n=K), K, N) for i in range(2)]
-    for M in (1, 3, 5, 8, 16):
+    for M in (1, 2, 3, 4, 5, 8, 16):
         x = torch.from_numpy(oracle.rng_normal(21, M, M * K).reshape(M, K).astype(np.float32)).cuda()
         runs = []
         for r in range(3):
