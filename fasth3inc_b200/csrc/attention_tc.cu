@@ -30,6 +30,13 @@
 
 namespace {
 
+// max of three floats in one instruction (sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 constexpr int kTcHD = 128;              // head_dim
 constexpr int kTcRows = 128;            // query rows a tile (two tiles a CTA)
 constexpr int kTcKeys = 128;            // keys a tile
@@ -240,7 +247,9 @@ __global__ void __launch_bounds__(kPpThreads, 1) attention_pp_kernel(
 #pragma unroll
                     for (int c = 0; c < 2; ++c)
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[c][e]));
+                        for (int e = 0; e < 32; e += 2)
+                            mx4[(e >> 1) & 3] = max3f(mx4[(e >> 1) & 3], __uint_as_float(v[c][e]),
+                                                      __uint_as_float(v[c][e + 1]));
                 } else {
 #pragma unroll
                     for (int c = 0; c < 2; ++c)
@@ -267,9 +276,11 @@ __global__ void __launch_bounds__(kPpThreads, 1) attention_pp_kernel(
                 l *= a;
             }
             if (raise) m_ref = mx;
-            // pass 2: P as bf16 pairs over the consumed columns (keys 64hf.. -> columns 32hf..)
-            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            // pass 2: P as bf16 pairs over the consumed columns (keys 64hf.. -> columns 32hf..);
+            // the scale-and-shift and the row sum run on packed fp32 pairs
+            uint64_t rs2[2] = {fh3::f2_pack(0.0f, 0.0f), fh3::f2_pack(0.0f, 0.0f)};
             const float nm = -m_ref;
+            const uint64_t sc2 = fh3::f2_pack(scale_log2, scale_log2), nm2 = fh3::f2_pack(nm, nm);
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t v[2][32];
@@ -290,9 +301,10 @@ __global__ void __launch_bounds__(kPpThreads, 1) attention_pp_kernel(
                     uint32_t pk[16];  // keys 64hf + 32c .. +31 -> columns 32hf + 16c ..
 #pragma unroll
                     for (int u = 0; u < 16; ++u) {
-                        const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][2 * u]), scale_log2, nm));
-                        const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[c][2 * u + 1]), scale_log2, nm));
-                        rs4[u & 3] += p0 + p1;
+                        const float2 a = fh3::f2_unpack(fh3::f2_fma(
+                            fh3::f2_pack(__uint_as_float(v[c][2 * u]), __uint_as_float(v[c][2 * u + 1])), sc2, nm2));
+                        const float p0 = fh3::ex2_approx(a.x), p1 = fh3::ex2_approx(a.y);
+                        rs2[u & 1] = fh3::f2_add(rs2[u & 1], fh3::f2_pack(p0, p1));
                         const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                         pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
                     }
@@ -303,7 +315,8 @@ __global__ void __launch_bounds__(kPpThreads, 1) attention_pp_kernel(
             fh3::tc_fence_before();  // this warp's TMEM reads and writes are complete
             __syncwarp();
             if (lane == 0) fh3::mbar_arrive(&B.p_full[g]);
-            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+            const float2 r0 = fh3::f2_unpack(rs2[0]), r1 = fh3::f2_unpack(rs2[1]);
+            l += (r0.x + r0.y) + (r1.x + r1.y);
         }
         if (ok) ok = wait_warp(&B.o_full[g], 0);  // the last PV has landed
         if (ok) {
