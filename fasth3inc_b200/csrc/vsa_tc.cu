@@ -21,6 +21,13 @@
 
 namespace {
 
+// max of three floats in one instruction (sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 // poff[i] = sum over tiles before i of count rounded up to 8; poff[nt] = the total.
 // One CTA of 1024 threads.
 __global__ void __launch_bounds__(1024) vsa_padoff_kernel(const int* __restrict__ toff, int nt,
@@ -344,7 +351,8 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             if (cnt >= 32) {  // a full half: no masking
 #pragma unroll
-                for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
+                for (int e = 0; e < 32; e += 2)
+                    mx4[(e >> 1) & 3] = max3f(mx4[(e >> 1) & 3], __uint_as_float(v[e]), __uint_as_float(v[e + 1]));
             } else {
 #pragma unroll
                 for (int e = 0; e < 32; ++e) {
@@ -375,24 +383,28 @@ __global__ void __launch_bounds__(kV6Threads, 1) vsa_tc64_kernel(
             }
             if (raise) m_ref = mx;
             uint8_t* pb = smem + V6_OFF_P + g * kV6Q;
-            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            // scale-and-shift and the row sum on packed fp32 pairs
+            uint64_t rs2[2] = {fh3::f2_pack(0.0f, 0.0f), fh3::f2_pack(0.0f, 0.0f)};
             const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;  // no key seen yet: every p is 0
+            const uint64_t sc2 = fh3::f2_pack(scale_log2, scale_log2), nm2 = fh3::f2_pack(nm, nm);
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 uint32_t pk[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int e = 8 * t + 2 * u;
-                    const float p0 = fh3::ex2_approx(fmaf(__uint_as_float(v[e]), scale_log2, nm));
-                    const float p1 = fh3::ex2_approx(fmaf(__uint_as_float(v[e + 1]), scale_log2, nm));
-                    rs4[u] += p0 + p1;
+                    const float2 a = fh3::f2_unpack(
+                        fh3::f2_fma(fh3::f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2, nm2));
+                    const float p0 = fh3::ex2_approx(a.x), p1 = fh3::ex2_approx(a.y);
+                    rs2[u & 1] = fh3::f2_add(rs2[u & 1], fh3::f2_pack(p0, p1));
                     const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                     pk[u] = *reinterpret_cast<const uint32_t*>(&pp);
                 }
                 const int ch = hf * 4 + t;
                 *reinterpret_cast<uint4*>(pb + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-            lsum += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+            const float2 r0 = fh3::f2_unpack(rs2[0]), r1 = fh3::f2_unpack(rs2[1]);
+            lsum += (r0.x + r0.y) + (r1.x + r1.y);
             fh3::tc_fence_before();
             fh3::fence_proxy_async_smem();
             __syncwarp();
