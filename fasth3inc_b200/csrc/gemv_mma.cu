@@ -982,6 +982,8 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) gemv_i8_kernel(
 template <int M>
 __device__ __forceinline__ void build_i8m(const float* __restrict__ x, int64_t K, int nblk, uint2* sB, uint32_t* sM,
                                           float* sF) {
+    // the min-term fragment is one m16n8k16 B operand: eight columns, two per token
+    static_assert(M >= 2 && M <= 4, "the integer kernel's min term holds at most 4 tokens");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int tq = lane & 3, j = lane >> 2;
     const float4* x4 = reinterpret_cast<const float4*>(x);
