@@ -9,6 +9,14 @@
 //   X_tj = sum_{k in j} x_tk  (32-weight sub-blocks j; w = dl*q - ml as in
 //   dequant_q4_k, src/core/fh3_quant.c:154-196)
 //
+// Two families of kernels, both exact in their products:
+// * fp16 MMAs (this header's description below): gemv_stream_kernel, and the prep +
+//   CTA-per-tile kernels gemv_mma_small_kernel / gemv_mma_kernel;
+// * integer MMAs (1..4 tokens, the defaults at 1-2 tokens and at 3-4 when out > in):
+//   gemv_i8_kernel and gemv_i8m_kernel, where x enters as base-256 digits and the
+//   nibbles as u8 straight from the bytes (see their own descriptions further down).
+// gemv_mma() at the end of the file picks the kernel.
+//
 // * A operand = the nibbles themselves: (word & 0x000F000F) is a pair of fp16
 //   subnormals q * 2^-24, exact; high nibbles (word & 0x00F000F0) are 16 q * 2^-24.
 //   Eight weights cost one shift and four ANDs.
